@@ -1,0 +1,368 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention stage on BASELINE.json's workloads.
+
+Default (the headline): Qwen2.5-Coder-3B-shaped decode over
+all 36 layers -- 16 q heads, 2 KV heads, head_dim 128, 4096 cached f16 tokens
+(N(0,1)*0.5), fp32 queries, RoPE theta 1e6 -- appending one token per layer
+per step and attending over 4097..4352 tokens across 256 steps.  One step =
+one te_attention_decode call over the 36 layers (RoPE + f16 append + split-K
+flash decode + LSE combine, one kernel launch).
+
+  metric  decode-attn KV GB/s: algorithmic bytes (KV read + append + q/out) per
+          step / device time per step
+  e2e     the same through the C ABI with host buffers (pinned q/k/v in, out
+          back to host every step)
+  prefill BASELINE config 3 (2048-token causal prefill, 36 layers) TFLOP/s
+
+Run under torchrun for N GPUs: each rank decodes its own independent sequence
+(sequence sharding, weak scaling; no collective on the data path); the time is
+the max over ranks.  `--impl reference` times the reference's own CPU attention
+(TinyEngine's c/src/ops.c built into oracle/_ref) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+# Config 2 shapes.
+LAYERS, HEADS, KV_HEADS, HEAD_DIM = 36, 16, 2, 128
+CTX0, DECODE_STEPS, THETA = 4096, 256, 1e6
+# Config 3 shapes.
+PREFILL_TOKENS = 2048
+
+METRIC = "decode-attn KV GB/s (% of HBM peak) @Qwen-3B ctx4K; prefill attn TFLOPS"
+
+
+def step_bytes(n_attended: int, layers: int = LAYERS) -> int:
+    """Algorithmic bytes of one decode step: per layer, read the K and V cache
+    (n_attended tokens x kv_heads x head_dim x f16 each), read q and the new raw
+    k/v (fp32), write the appended f16 k/v row and the fp32 output."""
+    kv_read = 2 * n_attended * KV_HEADS * HEAD_DIM * 2
+    qo = 2 * HEADS * HEAD_DIM * 4
+    new = 2 * KV_HEADS * HEAD_DIM * 4 + 2 * KV_HEADS * HEAD_DIM * 2
+    return layers * (kv_read + qo + new)
+
+
+def prefill_flops(s: int = PREFILL_TOKENS, layers: int = LAYERS) -> int:
+    """Causal-exact FLOPs: QK^T and PV over the lower triangle incl. diagonal."""
+    return layers * 4 * HEADS * HEAD_DIM * s * (s + 1) // 2
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows: list[list[str]] = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = [r for r in self.rows if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# reference / CPU baseline
+# ---------------------------------------------------------------------------
+
+class CpuDecode:
+    """The reference CPU attention (te_attention_decode_f32) on config-2
+    layer-steps: each call rotates q (te_rope_f32) and attends one layer's
+    fp32-widened f16 cache of 4097 tokens; independent layers run on `threads`
+    host threads (ctypes releases the GIL during each C call)."""
+
+    def __init__(self, kind: str, threads: int, n_layers: int = LAYERS):
+        from oracle import oracle as O
+        self.lib = O.ref() if kind == "reference" else O.port()
+        self.threads = threads
+        self.n = CTX0 + 1
+        self.n_layers = n_layers
+        rng = np.random.default_rng(0)
+        shape = self.n * KV_HEADS * HEAD_DIM
+        self.ks = [(rng.standard_normal(shape) * 0.5).astype(np.float16).astype(np.float32) for _ in range(n_layers)]
+        self.vs = [(rng.standard_normal(shape) * 0.5).astype(np.float16).astype(np.float32) for _ in range(n_layers)]
+        self.qs = [rng.standard_normal(HEADS * HEAD_DIM).astype(np.float32) for _ in range(n_layers)]
+        from concurrent.futures import ThreadPoolExecutor
+        self.pool = ThreadPoolExecutor(max_workers=threads)
+
+    def _one(self, i):
+        q = self.qs[i].copy()
+        self.lib.rope_f32(q, HEADS, HEAD_DIM, self.n - 1, THETA)
+        return self.lib.attention_decode_f32(q, self.ks[i], self.vs[i], self.n - 1, HEADS, KV_HEADS, HEAD_DIM)
+
+    def step(self) -> int:
+        """One decode step: every layer once.  Returns the number of layer calls."""
+        list(self.pool.map(self._one, range(self.n_layers)))
+        return self.n_layers
+
+    def sample(self, budget_s: float):
+        """Whole steps until budget_s has passed; returns (GB/s, calls, seconds)."""
+        calls = 0
+        t0 = time.perf_counter()
+        while True:
+            calls += self.step()
+            if time.perf_counter() - t0 >= budget_s:
+                break
+        dt = time.perf_counter() - t0
+        return step_bytes(self.n, layers=1) * calls / dt / 1e9, calls, dt
+
+    def close(self):
+        self.pool.shutdown()
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    kind = "reference" if O.ref_available() else "port"
+    threads = O.host_cores()
+    # one step of the reference arm = one 36-layer decode step of config 2 on all host threads
+    cpu = CpuDecode(kind, threads)
+    for _ in range(max(args.warmup, 0)):
+        cpu.step()
+    t0 = time.perf_counter()
+    calls = 0
+    for _ in range(args.steps):
+        calls += cpu.step()
+    dt = time.perf_counter() - t0
+    cpu.close()
+    value = step_bytes(CTX0 + 1, layers=1) * calls / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "decode3b: Qwen2.5-Coder-3B decode, 36 layers, H16/Hkv2/hd128, ctx 4097",
+                   "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"{LAYERS} layer calls per step at N={CTX0 + 1} (f16 cache widened to fp32)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def run_gpu(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_HOST_BUFFERS, AttnEngine
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    hbm_peak, tc_peak, peak_src = load_peaks()
+    eng = AttnEngine(local)
+    stream = torch.cuda.ExternalStream(eng.stream)
+    cap = CTX0 + DECODE_STEPS
+    cache = eng.kv_cache(layers=LAYERS, max_seqs=1, max_tokens_per_seq=cap, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
+                         rope_theta=THETA)
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    with torch.cuda.stream(stream):
+        for layer in range(LAYERS):
+            k = (torch.randn((CTX0, KV_HEADS, HEAD_DIM), generator=g, device="cuda") * 0.5).half()
+            v = (torch.randn((CTX0, KV_HEADS, HEAD_DIM), generator=g, device="cuda") * 0.5).half()
+            stream.synchronize()
+            cache.write_f16(layer, 0, 0, k, v)
+        q = torch.randn((LAYERS, 1, HEADS, HEAD_DIM), generator=g, device="cuda")
+        kn = torch.randn((LAYERS, 1, KV_HEADS, HEAD_DIM), generator=g, device="cuda") * 0.5
+        vn = torch.randn((LAYERS, 1, KV_HEADS, HEAD_DIM), generator=g, device="cuda") * 0.5
+        out = torch.empty((LAYERS, 1, HEADS, HEAD_DIM), device="cuda")
+    stream.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step(flags=0, host=None):
+        if cache.length(0) >= cap:
+            cache.truncate(0, CTX0)
+        if host is None:
+            cache.decode(0, LAYERS, [0], q, out, HEADS, k_new=kn, v_new=vn, flags=TE_ATTN_ADVANCE | flags)
+        else:
+            hq, hk, hv, ho = host
+            cache.decode(0, LAYERS, [0], hq, ho, HEADS, k_new=hk, v_new=hv,
+                         flags=TE_ATTN_ADVANCE | TE_ATTN_HOST_BUFFERS)
+
+    # ---- device-timed decode -------------------------------------------
+    for _ in range(max(args.warmup, 3)):
+        step()
+    eng.synchronize()
+    cache.truncate(0, CTX0)
+    # step i attends CTX0 + (i mod 256) + 1 tokens (the cache wraps back to CTX0 every 256 steps)
+    lens = [CTX0 + (i % DECODE_STEPS) + 1 for i in range(args.steps)]
+    launches0 = eng.launch_count
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        ev1.synchronize()
+    launches = eng.launch_count - launches0
+    eng.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    bytes_rank = sum(step_bytes(n) for n in lens)
+    value = bytes_rank * world / (ms_max / 1e3) / 1e9
+    kernel_gbs = bytes_rank / (ms / 1e3) / 1e9
+
+    # ---- e2e through the C ABI with host buffers -------------------------
+    hq = torch.empty(q.shape, dtype=torch.float32, pin_memory=True).copy_(q)
+    hk = torch.empty(kn.shape, dtype=torch.float32, pin_memory=True).copy_(kn)
+    hv = torch.empty(vn.shape, dtype=torch.float32, pin_memory=True).copy_(vn)
+    ho = torch.empty(out.shape, dtype=torch.float32, pin_memory=True)
+    host = (hq, hk, hv, ho)
+    cache.truncate(0, CTX0)
+    for _ in range(max(args.warmup, 3)):
+        step(host=host)
+    cache.truncate(0, CTX0)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    t_wall = time.perf_counter()
+    for _ in range(args.steps):
+        step(host=host)
+    e1.record(stream)
+    e1.synchronize()
+    wall_ms = (time.perf_counter() - t_wall) * 1e3
+    e2e_ms = max(e0.elapsed_time(e1), wall_ms)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = bytes_rank * world / (e2e_ms / 1e3) / 1e9
+    h2d = (hq.numel() + hk.numel() + hv.numel()) * 4
+    d2h = ho.numel() * 4
+
+    # ---- CPU baseline (rank 0, N=1 only) ---------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import oracle as O
+        kind = "reference" if O.ref_available() else "port"
+        threads = O.host_cores()
+        cd = CpuDecode(kind, threads)
+        gbs, calls, dt = cd.sample(args.cpu_seconds)
+        cd.close()
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+               "sample": f"{calls} config-2 layer calls (N={CTX0 + 1}, 16 heads) in {dt:.1f} s on {threads} threads"}
+
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.is_file():
+        traffic = json.loads(tfile.read_text()).get("decode_f16_kernel_decode3b_bytes_per_launch")
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 KV, fp32 q/accumulate", "data": "synthetic",
+            "config": {"workload": "decode3b: BASELINE config 2 -- Qwen2.5-Coder-3B decode, 36 layers, H16/Hkv2/"
+                                   "hd128, f16 KV, 4097..4352 tokens over 256 steps, 1 token appended per layer-step",
+                       "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+                       "l2": "per-step KV (151 MB) exceeds the 126 MB L2",
+                       "kernel": "decode_f16_kernel<128,3>: fused RoPE-append + split-K decode + LSE combine"},
+            "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(kernel_gbs / hbm_peak, 4), "traffic": traffic,
+                         "peak_source": f"{peak_src} (burst copy)"},
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    cache.close()
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=DECODE_STEPS)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,182 @@
+/*
+ * TinyEngine attention engine for NVIDIA B200 (sm_100a): device-resident
+ * f16 paged KV cache, fused RoPE + append, split-K GQA flash decode and
+ * causal flash prefill on tcgen05 tensor cores.
+ *
+ * These entry points replace the attention slice of TinyEngine's internal
+ * Metal boundary (c/src/metal_backend.h:206-343: te_metal_decode_layer_f32,
+ * te_metal_decode_all_layers_f32, te_metal_prefill_layer_f32,
+ * te_metal_prefill_all_layers_f32) and of the resident-KV manager
+ * (c/src/metal/metal_backend_layers.mm.inc:1116-1173, 2029-2181).  The
+ * reference passes host fp32 caches into each call and copies them in and
+ * out; here the cache lives in HBM for its whole life and only queries,
+ * new K/V rows and outputs cross the boundary.
+ *
+ * Conventions
+ * - All functions return te_status (tinyengine.h); te_attn_engine_last_error
+ *   gives the detailed message of the engine's last failure.
+ * - Pointers named q, k, v, out are DEVICE pointers (cudaMalloc, torch
+ *   tensors' data_ptr(), ...) unless TE_ATTN_HOST_BUFFERS is set, in which
+ *   case they are host pointers (pinned memory recommended) and the call
+ *   copies them in and out and returns only when `out` is filled.
+ * - Host arrays (seq_ids, q_positions) are read during the call only.
+ * - Work is queued on the engine's stream; device-pointer calls return
+ *   without synchronising.
+ * - An engine and its caches are used from one host thread at a time;
+ *   distinct engines are independent (no global lock).
+ * - Nothing falls back to the CPU: without a CUDA device, engine creation
+ *   returns TE_STATUS_UNSUPPORTED.
+ *
+ * Layouts (fp32 unless stated)
+ *   decode  q, out:   [n_layers][n_seqs][heads][head_dim]
+ *           k/v_new:  [n_layers][n_seqs][kv_heads][head_dim]   (pre-RoPE)
+ *           partial:  [n_layers][n_seqs][heads][head_dim + 2]
+ *                     = { acc[head_dim], m, l }: m = max of q.k*log2(e)/sqrt(head_dim),
+ *                     l = sum 2^(s - m), acc = sum 2^(s - m) * v.
+ *   prefill q, out:   [n_layers][n_tokens][heads][head_dim]
+ *           k, v:     [n_layers][n_tokens][kv_heads][head_dim] (pre-RoPE)
+ *   cache rows read/written by te_kv_cache_read_f16 / te_kv_cache_write_f16:
+ *                     [n_tokens][kv_heads][head_dim] IEEE binary16 bits.
+ */
+#ifndef TINYENGINE_ATTN_H
+#define TINYENGINE_ATTN_H
+
+#include "tinyengine.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TE_ATTN_ABI_VERSION 1u
+
+/* Flags for the compute entry points. */
+#define TE_ATTN_ADVANCE       (1u << 0) /* after the call, each sequence's length += tokens appended */
+#define TE_ATTN_PARTIAL       (1u << 1) /* decode writes partial records instead of normalised output */
+#define TE_ATTN_NO_ROPE       (1u << 2) /* q (and k) are used as given, without rotation */
+#define TE_ATTN_INPUT_F16     (1u << 3) /* q/k/v inputs are binary16 instead of fp32 */
+#define TE_ATTN_HOST_BUFFERS  (1u << 4) /* q/k/v/out are host pointers; call is synchronous */
+
+typedef struct te_attn_engine te_attn_engine;
+typedef struct te_kv_cache te_kv_cache;
+
+typedef struct te_attn_options {
+    uint32_t abi_version;      /* TE_ATTN_ABI_VERSION */
+    int32_t device;            /* CUDA device ordinal */
+    void *stream;              /* cudaStream_t to launch on; NULL = engine-owned non-blocking stream */
+    uint32_t decode_chunk_tokens; /* split-K chunk length (multiple of 64); 0 = chosen per call */
+    uint32_t flags;            /* reserved, 0 */
+} te_attn_options;
+
+typedef struct te_kv_cache_desc {
+    uint32_t abi_version;      /* TE_ATTN_ABI_VERSION */
+    uint32_t layers;
+    uint32_t max_seqs;         /* sequence slots 0 .. max_seqs-1 */
+    uint32_t max_tokens_per_seq;
+    uint32_t kv_heads;
+    uint32_t head_dim;         /* 64 or 128 */
+    uint32_t page_tokens;      /* tokens per page, multiple of 64; 0 = 128 */
+    uint32_t total_pages;      /* pages per layer in the pool; 0 = max_seqs * pages per full sequence */
+    uint32_t max_position;     /* RoPE table length (global positions); 0 = max_tokens_per_seq */
+    float rope_theta;          /* RoPE base, > 0 (Qwen2: 1e6) */
+} te_kv_cache_desc;
+
+/* Engine ------------------------------------------------------------------ */
+
+TE_API te_attn_options te_attn_default_options(void);
+TE_API te_status te_attn_engine_create(const te_attn_options *options, te_attn_engine **out_engine);
+TE_API void te_attn_engine_free(te_attn_engine *engine);
+TE_API te_status te_attn_engine_set_stream(te_attn_engine *engine, void *stream);
+TE_API void *te_attn_engine_stream(const te_attn_engine *engine);
+/* Waits for queued work; reports (and clears) a device-side error such as an
+ * expired bounded wait as TE_STATUS_RUNTIME_ERROR. */
+TE_API te_status te_attn_engine_synchronize(te_attn_engine *engine);
+TE_API const char *te_attn_engine_last_error(const te_attn_engine *engine);
+/* Number of this library's kernels launched by the engine so far. */
+TE_API uint64_t te_attn_engine_launch_count(const te_attn_engine *engine);
+
+/* KV cache ---------------------------------------------------------------- */
+
+TE_API te_kv_cache_desc te_kv_cache_default_desc(void);
+TE_API te_status te_kv_cache_create(te_attn_engine *engine, const te_kv_cache_desc *desc,
+                                    te_kv_cache **out_cache);
+TE_API void te_kv_cache_free(te_kv_cache *cache);
+/* Empties sequence `seq` (its pages return to the pool) and sets the global
+ * RoPE position of its first token (0 for a whole sequence; the start of the
+ * shard for a KV-split shard). */
+TE_API te_status te_kv_cache_seq_reset(te_kv_cache *cache, size_t seq, size_t position_offset);
+/* Drops the tokens at index >= length (length <= current length); the pages
+ * stay mapped and are overwritten by later appends.  No reference counterpart
+ * (the reference's generation state only grows, c/src/qwen.c:376-392). */
+TE_API te_status te_kv_cache_seq_truncate(te_kv_cache *cache, size_t seq, size_t length);
+TE_API te_status te_kv_cache_seq_length(const te_kv_cache *cache, size_t seq, size_t *out_length);
+/* Raw f16 rows (already rotated) into / out of tokens [token_begin, +n_tokens)
+ * of one layer; `k`/`v` may be host or device pointers.  A write grows the
+ * sequence's length to token_begin + n_tokens when that is larger. */
+TE_API te_status te_kv_cache_write_f16(te_kv_cache *cache, size_t layer, size_t seq,
+                                       size_t token_begin, size_t n_tokens,
+                                       const uint16_t *k, const uint16_t *v);
+TE_API te_status te_kv_cache_read_f16(te_kv_cache *cache, size_t layer, size_t seq,
+                                      size_t token_begin, size_t n_tokens,
+                                      uint16_t *k, uint16_t *v);
+
+/* Compute ----------------------------------------------------------------- */
+
+/*
+ * Fused RoPE(k) + binary16 round-to-nearest-even append of n_tokens new rows
+ * per layer for layers [layer_begin, +n_layers) of sequence `seq`, at local
+ * token indices length .. length+n_tokens-1 (global RoPE positions offset +
+ * index).  Replaces the k/v half of te_qkv_bias_rope_cache_batch_h_f32
+ * (c/src/metal/metal_kernels.metal.inc:2344-2429) and the CPU append
+ * (c/src/qwen.c:805-807).  Flags: TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16,
+ * TE_ATTN_NO_ROPE.
+ */
+TE_API te_status te_kv_append_rope(te_kv_cache *cache, size_t layer_begin, size_t n_layers,
+                                   size_t seq, const void *k, const void *v, size_t n_tokens,
+                                   uint32_t flags);
+
+/*
+ * One decode step for n_seqs sequences over layers [layer_begin, +n_layers).
+ * When k_new/v_new are non-NULL, each sequence first appends one token per
+ * layer (RoPE + f16 append at index `length`), then every query attends over
+ * all cached tokens including the new one; q is rotated at the sequence's
+ * last global position, or at q_positions[i] when q_positions is non-NULL
+ * (KV-split shards that do not own the newest token).  Output is normalised
+ * attention, or partial records with TE_ATTN_PARTIAL.  Replaces
+ * te_attention_decode_f32 as called from c/src/qwen.c:1038-1046 and the
+ * attention kernels of te_metal_decode_all_layers_f32
+ * (c/src/metal/metal_backend_layers.mm.inc:1273-1296).
+ */
+TE_API te_status te_attention_decode(te_kv_cache *cache, size_t layer_begin, size_t n_layers,
+                                     const uint32_t *seq_ids, size_t n_seqs,
+                                     const int64_t *q_positions,
+                                     const float *q, const float *k_new, const float *v_new,
+                                     size_t heads, float *out, uint32_t flags);
+
+/*
+ * Log-sum-exp merge of partial records from n_parts shards:
+ * partials[n_parts][rows][head_dim + 2] -> out[rows][head_dim].  No reference
+ * counterpart (the reference runs on one device); the rescale is that of
+ * c/src/metal/metal_kernels.metal.inc:2650-2681.
+ */
+TE_API te_status te_attention_merge_partials(te_attn_engine *engine, const float *partials,
+                                             size_t n_parts, size_t rows, size_t head_dim,
+                                             float *out, uint32_t flags);
+
+/*
+ * Causal prefill of n_tokens new tokens of sequence `seq` over layers
+ * [layer_begin, +n_layers): RoPE + f16 append of k/v, RoPE of q, then every
+ * new token t attends to cached tokens 0 .. length+t (length = tokens cached
+ * before the call).  Replaces the CPU prefill loop (c/src/qwen.c:774-824) and
+ * te_metal_prefill_all_layers_f32's attention
+ * (c/src/metal/metal_backend_layers.mm.inc:2406-2456).  Flags:
+ * TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16, TE_ATTN_HOST_BUFFERS.
+ */
+TE_API te_status te_attention_prefill(te_kv_cache *cache, size_t layer_begin, size_t n_layers,
+                                      size_t seq, const void *q, const void *k, const void *v,
+                                      size_t n_tokens, size_t heads, float *out, uint32_t flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,19 @@
+"""B200-native attention stage for TinyEngine (Qwen2-style GQA).
+
+The product is ``libtinyengine.so`` (built from ``csrc/``) behind the C ABI in
+``include/tinyengine.h`` and ``include/tinyengine_attn.h``; this package holds
+its ctypes binding and the multi-GPU host orchestration.
+"""
+from .runtime import (  # noqa: F401
+    TE_ATTN_ADVANCE,
+    TE_ATTN_HOST_BUFFERS,
+    TE_ATTN_INPUT_F16,
+    TE_ATTN_NO_ROPE,
+    TE_ATTN_PARTIAL,
+    AttnEngine,
+    KVCache,
+    TinyEngineError,
+    attention_decode_f32,
+    load_library,
+    rope_f32,
+)

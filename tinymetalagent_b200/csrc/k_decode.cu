@@ -1,0 +1,583 @@
+// Split-K GQA flash decode over the paged f16 KV cache (sm_100a).
+//
+// One CTA = one (layer, sequence, kv head, chunk of chunk_tokens tokens).  It
+// serves the whole GQA group of that kv head (up to 16 query heads), so every
+// K/V byte is read from HBM exactly once per step.  Reference semantics:
+// te_attention_decode_f32 (c/src/ops.c:323-395) with f16 K/V widened exactly,
+// as in te_attention_flash_h_f32_kernel
+// (c/src/metal/metal_kernels.metal.inc:3374-3495); the group-shared KV read
+// follows te_attention_flash_gqa_f32_kernel (:3209-3372).
+//
+// Pipeline: warp 4 lane 0 streams 64-token stages (K and V, 128B-swizzled
+// 64x64 TMA boxes) into a ring of `R` shared-memory slots; warps 0-3 each take
+// 16 tokens of every stage.  Scores S = Q K^T and O += P V run on
+// mma.sync.m16n8k16 (f16 in, f32 accumulate) with the query heads as the M
+// rows.  The head dimension is permuted per thread so that every operand
+// fragment is one 16-byte shared-memory load (conflict-free under the swizzle)
+// and the query fragments stay in registers for the whole chunk; the
+// permutation is applied identically to q and k, so q.k is unchanged.
+//
+// Split-K partials (acc, m, l) go to scratch; the last CTA of a
+// (layer, seq, kv head) to finish (atomic ticket, no waiting) merges them.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cmath>
+
+#include "te_internal.h"
+#include "te_ptx.cuh"
+
+namespace te {
+namespace {
+
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kBoxBytes = kStageTokens * 64 * 2;  // 64 tokens x 64 dims x f16
+
+template <int HD>
+struct DecodeCfg {
+  static constexpr int kBoxes = HD / 64;                   // TMA boxes per K (or V) stage
+  static constexpr int kStageBytes = 2 * kBoxes * kBoxBytes;
+  static constexpr int kKSteps = HD / 16;                  // mma k-steps for q.k
+  static constexpr int kChunksPerThread = HD / 32;         // 16-byte chunks of a K row per thread
+  static constexpr int kThreadsPerBox = 8 / kChunksPerThread;
+  static constexpr int kNTiles = HD / 8;                   // mma n-tiles for P.V
+};
+
+__device__ __forceinline__ float rope_lo(float a, float b, float c, float s) {
+  return __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+}
+__device__ __forceinline__ float rope_hi(float a, float b, float c, float s) {
+  return __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+}
+
+// Physical head-dim offset (in halves) of the 16-byte chunk a thread with
+// quad index c reads for k-step pair j.
+template <int HD>
+__device__ __forceinline__ int k_chunk_of(int c, int j, int* box) {
+  using C = DecodeCfg<HD>;
+  *box = c / C::kThreadsPerBox;
+  return C::kChunksPerThread * (c % C::kThreadsPerBox) + ((j + c) % C::kChunksPerThread);
+}
+
+template <int HD, int R>
+__global__ void __launch_bounds__(kThreads, 2) decode_f16_kernel(const __grid_constant__ DecodeParams p) {
+  using C = DecodeCfg<HD>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + R * C::kStageBytes);
+  uint64_t* empty = full + R;
+  int* flags = reinterpret_cast<int*>(empty + R);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  // ---- work item -------------------------------------------------------
+  const int cx = blockIdx.x;
+  const int layer_local = blockIdx.y / p.kv_heads;
+  const int kvh = blockIdx.y % p.kv_heads;
+  int si = 0;
+  for (int i = 1; i < p.n_seqs; ++i) {
+    if (cx >= p.seqs[i].chunk_begin) si = i;
+  }
+  const SeqEntry se = p.seqs[si];
+  const int chunk = cx - se.chunk_begin;
+  if (chunk < 0 || chunk >= se.n_chunks) return;  // uniform per CTA
+  const int t0 = chunk * p.chunk_tokens;
+  const int t1 = min(se.len, t0 + p.chunk_tokens);
+  const int n_st = (t1 - t0 + kStageTokens - 1) / kStageTokens;
+  const int layer = p.layer_begin + layer_local;
+  const int G = p.group;
+  const int H = p.group * p.kv_heads;
+
+  if (tid == 0) {
+    for (int i = 0; i < R; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kConsumerWarps);
+    }
+    fence_mbarrier_init();
+    flags[0] = 0;
+  }
+
+  // ---- fused RoPE(k) + f16 append of the new token (tail chunk only) ----
+  const int new_idx = se.len - 1;
+  if (se.new_pos >= 0 && p.k_new != nullptr && new_idx >= t0 && new_idx < t1 && tid < HD) {
+    const int page = p.page_table[se.slot * p.max_pages_per_seq + new_idx / p.page_tokens];
+    const size_t row = ((size_t)(layer * p.num_pages + page) * p.kv_heads + kvh) * p.page_tokens +
+                       (new_idx % p.page_tokens);
+    const float* kn = p.k_new + ((size_t)(layer_local * p.seq_total + p.seq_base + si) * p.kv_heads + kvh) * HD;
+    const float* vn = p.v_new + ((size_t)(layer_local * p.seq_total + p.seq_base + si) * p.kv_heads + kvh) * HD;
+    constexpr int half = HD / 2;
+    if (tid < half) {
+      float a = kn[tid], b = kn[tid + half];
+      float lo = a, hi = b;
+      if (p.rope) {
+        const float c = p.rope_cos[(size_t)se.new_pos * half + tid];
+        const float s = p.rope_sin[(size_t)se.new_pos * half + tid];
+        lo = rope_lo(a, b, c, s);
+        hi = rope_hi(a, b, c, s);
+      }
+      p.k_pool[row * HD + tid] = __half_as_ushort(__float2half_rn(lo));
+      p.k_pool[row * HD + tid + half] = __half_as_ushort(__float2half_rn(hi));
+    }
+    p.v_pool[row * HD + tid] = __half_as_ushort(__float2half_rn(vn[tid]));
+    fence_proxy_async();  // generic-proxy stores above -> visible to this CTA's TMA reads
+  }
+  __syncthreads();
+
+  // Consumer state, declared at CTA scope so it survives the role split.
+  float acc[C::kNTiles][4];
+  float m_lo = -INFINITY, m_hi = -INFINITY;
+  float l_lo = 0.f, l_hi = 0.f;
+  const int g = lane >> 2;  // mma group id: head row g (and g + 8), token row
+  const int c = lane & 3;   // thread in group
+
+  // ---- producer: TMA ring ----------------------------------------------
+  if (warp == kConsumerWarps) {
+    if (lane == 0) {
+      const uint64_t policy = policy_evict_first();
+      bool ok = true;
+      for (int s = 0; s < n_st && ok; ++s) {
+        const int slot = s % R;
+        if (s >= R) {
+          if (!mbar_wait(&empty[slot], ((s / R) - 1) & 1)) {
+            set_error(p.error, 1);
+            ok = false;
+            break;
+          }
+        }
+        const int tok = t0 + s * kStageTokens;
+        const int page = p.page_table[se.slot * p.max_pages_per_seq + tok / p.page_tokens];
+        const int row = ((layer * p.num_pages + page) * p.kv_heads + kvh) * p.page_tokens + (tok % p.page_tokens);
+        unsigned char* st = smem + slot * C::kStageBytes;
+        mbar_arrive_expect_tx(&full[slot], C::kStageBytes);
+#pragma unroll
+        for (int b = 0; b < C::kBoxes; ++b) {
+          tma_load_2d_hint(st + b * kBoxBytes, &p.tmap_k, &full[slot], b * 64, row, policy);
+          tma_load_2d_hint(st + (C::kBoxes + b) * kBoxBytes, &p.tmap_v, &full[slot], b * 64, row, policy);
+        }
+      }
+      // Never leave the CTA with copies in flight: wait for the last stages.
+      for (int s = max(0, n_st - R); s < n_st; ++s) {
+        if (!mbar_wait(&full[s % R], (s / R) & 1)) set_error(p.error, 2);
+      }
+    }
+  } else {
+    // ---- consumers ------------------------------------------------------
+    const bool row_lo_valid = g < G;
+    const bool row_hi_valid = g + 8 < G;
+
+    // Query fragments: a[ks][0..3] for k-step ks (rows g / g+8).
+    uint32_t qa[C::kKSteps][4];
+    {
+      const float* qbase = p.q + ((size_t)(layer_local * p.seq_total + p.seq_base + si) * H + kvh * G) * HD;
+      constexpr int half = HD / 2;
+      const float* crow = p.rope_cos + (size_t)se.q_pos * half;
+      const float* srow = p.rope_sin + (size_t)se.q_pos * half;
+#pragma unroll
+      for (int j = 0; j < C::kChunksPerThread; ++j) {
+        int box;
+        const int ch = k_chunk_of<HD>(c, j, &box);
+        const int d0 = box * 64 + ch * 8;
+        float v[2][8];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int row = g + 8 * r;
+          const bool valid = r == 0 ? row_lo_valid : row_hi_valid;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int d = d0 + e;
+            float x = 0.f;
+            if (valid) {
+              const float* qr = qbase + (size_t)row * HD;
+              if (p.rope) {
+                if (d < half) {
+                  x = rope_lo(qr[d], qr[d + half], crow[d], srow[d]);
+                } else {
+                  x = rope_hi(qr[d - half], qr[d], crow[d - half], srow[d - half]);
+                }
+              } else {
+                x = qr[d];
+              }
+            }
+            v[r][e] = x;
+          }
+        }
+        // k-step 2j uses dims d0+0..3, k-step 2j+1 uses d0+4..7
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          qa[2 * j + h][0] = pack_half2(v[0][4 * h + 0], v[0][4 * h + 1]);
+          qa[2 * j + h][1] = pack_half2(v[1][4 * h + 0], v[1][4 * h + 1]);
+          qa[2 * j + h][2] = pack_half2(v[0][4 * h + 2], v[0][4 * h + 3]);
+          qa[2 * j + h][3] = pack_half2(v[1][4 * h + 2], v[1][4 * h + 3]);
+        }
+      }
+    }
+
+#pragma unroll
+    for (int i = 0; i < C::kNTiles; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    const float sl = p.scale_log2;
+    bool failed = false;
+
+    for (int s = 0; s < n_st; ++s) {
+      const int slot = s % R;
+      if (!mbar_wait(&full[slot], (s / R) & 1)) {
+        set_error(p.error, 3);
+        failed = true;
+        break;
+      }
+      const int tok_base = t0 + s * kStageTokens + 16 * warp;
+      if (tok_base < t1) {
+        const uint32_t st = smem_u32(smem + slot * C::kStageBytes);
+        // ---- S = Q K^T (rows: heads, cols: 8 tokens per mma) ----
+        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int r = 16 * warp + g + 8 * t;  // token row in the stage
+#pragma unroll
+          for (int j = 0; j < C::kChunksPerThread; ++j) {
+            int box;
+            const int ch = k_chunk_of<HD>(c, j, &box);
+            const uint4 kv = lds128(st + box * kBoxBytes + r * 128 + ((ch ^ (r & 7)) << 4));
+            mma_16816(sacc[t], qa[2 * j], kv.x, kv.y);
+            mma_16816(sacc[t], qa[2 * j + 1], kv.z, kv.w);
+          }
+        }
+        // ---- online softmax (log2 domain) ----
+        float sc[2][4];
+        float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int tok = tok_base + 8 * t + 2 * c + (e & 1);
+            const float v = tok < t1 ? sacc[t][e] * sl : -INFINITY;
+            sc[t][e] = v;
+            if (e < 2) mx_lo = fmaxf(mx_lo, v); else mx_hi = fmaxf(mx_hi, v);
+          }
+        }
+        mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+        mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+        mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+        mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+        const float nm_lo = fmaxf(m_lo, mx_lo);
+        const float nm_hi = fmaxf(m_hi, mx_hi);
+        const float base_lo = nm_lo == -INFINITY ? 0.f : nm_lo;
+        const float base_hi = nm_hi == -INFINITY ? 0.f : nm_hi;
+        const float al_lo = ex2(m_lo - base_lo);
+        const float al_hi = ex2(m_hi - base_hi);
+        m_lo = nm_lo;
+        m_hi = nm_hi;
+        float ps_lo = 0.f, ps_hi = 0.f;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float pv = ex2(sc[t][e] - (e < 2 ? base_lo : base_hi));
+            sc[t][e] = pv;
+            if (e < 2) ps_lo += pv; else ps_hi += pv;
+          }
+        }
+        l_lo = l_lo * al_lo + ps_lo;
+        l_hi = l_hi * al_hi + ps_hi;
+#pragma unroll
+        for (int i = 0; i < C::kNTiles; ++i) {
+          acc[i][0] *= al_lo;
+          acc[i][1] *= al_lo;
+          acc[i][2] *= al_hi;
+          acc[i][3] *= al_hi;
+        }
+        uint32_t pa[4];
+        pa[0] = pack_half2(sc[0][0], sc[0][1]);
+        pa[1] = pack_half2(sc[0][2], sc[0][3]);
+        pa[2] = pack_half2(sc[1][0], sc[1][1]);
+        pa[3] = pack_half2(sc[1][2], sc[1][3]);
+        // ---- O += P V ----
+        const int rv0 = 16 * warp + 2 * c;
+#pragma unroll
+        for (int b = 0; b < C::kBoxes; ++b) {
+          const uint32_t vb = st + (C::kBoxes + b) * kBoxBytes;
+          const uint4 v0 = lds128(vb + (rv0 + 0) * 128 + ((g ^ ((rv0 + 0) & 7)) << 4));
+          const uint4 v1 = lds128(vb + (rv0 + 1) * 128 + ((g ^ ((rv0 + 1) & 7)) << 4));
+          const uint4 v8 = lds128(vb + (rv0 + 8) * 128 + ((g ^ ((rv0 + 8) & 7)) << 4));
+          const uint4 v9 = lds128(vb + (rv0 + 9) * 128 + ((g ^ ((rv0 + 9) & 7)) << 4));
+          const uint32_t w0[4] = {v0.x, v0.y, v0.z, v0.w};
+          const uint32_t w1[4] = {v1.x, v1.y, v1.z, v1.w};
+          const uint32_t w8[4] = {v8.x, v8.y, v8.z, v8.w};
+          const uint32_t w9[4] = {v9.x, v9.y, v9.z, v9.w};
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const uint32_t sel = (jj & 1) ? 0x7632u : 0x5410u;
+            const uint32_t b0 = prmt(w0[jj >> 1], w1[jj >> 1], sel);
+            const uint32_t b1 = prmt(w8[jj >> 1], w9[jj >> 1], sel);
+            mma_16816(acc[b * 8 + jj], pa, b0, b1);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    (void)failed;
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+
+  }
+  __syncthreads();  // all stages consumed and every TMA copy complete: the ring is free
+  if (warp < kConsumerWarps) {
+    float* sm_m = reinterpret_cast<float*>(smem);             // [4][16]
+    float* sm_l = sm_m + kConsumerWarps * 16;                  // [4][16]
+    float* sm_o = sm_l + kConsumerWarps * 16;                  // [4][16][HD]
+    if (c == 0) {
+      sm_m[warp * 16 + g] = m_lo;
+      sm_m[warp * 16 + g + 8] = m_hi;
+      sm_l[warp * 16 + g] = l_lo;
+      sm_l[warp * 16 + g + 8] = l_hi;
+    }
+#pragma unroll
+    for (int i = 0; i < C::kNTiles; ++i) {
+      const int b = i >> 3, jj = i & 7;
+      const int d0 = 64 * b + 8 * (2 * c) + jj;
+      const int d1 = 64 * b + 8 * (2 * c + 1) + jj;
+      float* o_lo = sm_o + ((size_t)warp * 16 + g) * HD;
+      float* o_hi = sm_o + ((size_t)warp * 16 + g + 8) * HD;
+      o_lo[d0] = acc[i][0];
+      o_lo[d1] = acc[i][1];
+      o_hi[d0] = acc[i][2];
+      o_hi[d1] = acc[i][3];
+    }
+  }
+  __syncthreads();  // per-warp states in shared memory
+
+  // ---- merge the 4 warps: one record per query head of the group ----------
+  const float* sm_m = reinterpret_cast<const float*>(smem);
+  const float* sm_l = sm_m + kConsumerWarps * 16;
+  const float* sm_o = sm_l + kConsumerWarps * 16;
+  const bool single = se.n_chunks == 1;
+  const size_t out_row0 = (size_t)(layer_local * p.seq_total + p.seq_base + si) * H + kvh * G;
+  const int rec = HD + 2;
+  float* part_base = p.partials + ((size_t)(layer_local * p.kv_heads + kvh) * p.total_chunks + cx) * G * rec;
+  for (int it = tid; it < G * HD; it += kThreads) {
+    const int row = it / HD, d = it % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm_m[w * 16 + row]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float mw = sm_m[w * 16 + row];
+      const float wt = mw == -INFINITY ? 0.f : ex2(mw - M);
+      L += sm_l[w * 16 + row] * wt;
+      O += sm_o[((size_t)w * 16 + row) * HD + d] * wt;
+    }
+    if (single) {
+      if (p.partial_out) {
+        float* r = p.out + (out_row0 + row) * rec;
+        r[d] = O;
+        if (d == 0) { r[HD] = M; r[HD + 1] = L; }
+      } else {
+        p.out[(out_row0 + row) * HD + d] = O / L;
+      }
+    } else {
+      float* r = part_base + (size_t)row * rec;
+      r[d] = O;
+      if (d == 0) { r[HD] = M; r[HD + 1] = L; }
+    }
+  }
+  if (single) return;
+
+  // ---- split-K: the last CTA of this (layer, seq, kv head) merges ---------
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t* ctr = p.counters + (size_t)(layer_local * p.kv_heads + kvh) * p.n_seqs + si;
+    const uint32_t ticket = atomicAdd(ctr, 1u);
+    const int last = ticket == (uint32_t)(se.n_chunks - 1);
+    if (last) *ctr = 0u;  // every other CTA of the group has already taken its ticket
+    flags[0] = last;
+  }
+  __syncthreads();
+  if (!flags[0]) return;
+  __threadfence();
+  const float* grp = p.partials + ((size_t)(layer_local * p.kv_heads + kvh) * p.total_chunks + se.chunk_begin) * G * rec;
+  // The warp-merge area is dead here (its results are in `partials`); reuse the ring.
+  if (4096 + 2 * se.n_chunks * G + 32 > R * C::kStageBytes / 4) {
+    set_error(p.error, 4);  // host caps n_chunks so this cannot happen
+    return;
+  }
+  float* sm_cm = reinterpret_cast<float*>(smem) + 4096;   // [n_chunks][G] maxima
+  float* sm_cl = sm_cm + se.n_chunks * G;
+  float* sm_M = sm_cl + se.n_chunks * G;                  // [G]
+  float* sm_L = sm_M + 16;                                // [G]
+  for (int i = tid; i < se.n_chunks * G; i += kThreads) {
+    sm_cm[i] = __ldcg(grp + (size_t)i * rec + HD);
+    sm_cl[i] = __ldcg(grp + (size_t)i * rec + HD + 1);
+  }
+  __syncthreads();
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int k = 0; k < se.n_chunks; ++k) M = fmaxf(M, sm_cm[k * G + tid]);
+    float L = 0.f;
+    for (int k = 0; k < se.n_chunks; ++k) L += sm_cl[k * G + tid] * ex2(sm_cm[k * G + tid] - M);
+    sm_M[tid] = M;
+    sm_L[tid] = L;
+  }
+  __syncthreads();
+  for (int it = tid; it < G * HD; it += kThreads) {
+    const int row = it / HD, d = it % HD;
+    const float M = sm_M[row];
+    float O = 0.f;
+    for (int k = 0; k < se.n_chunks; ++k) {
+      O += __ldcg(grp + ((size_t)k * G + row) * rec + d) * ex2(sm_cm[k * G + row] - M);
+    }
+    if (p.partial_out) {
+      float* r = p.out + (out_row0 + row) * rec;
+      r[d] = O;
+      if (d == 0) { r[HD] = M; r[HD + 1] = sm_L[row]; }
+    } else {
+      p.out[(out_row0 + row) * HD + d] = O / sm_L[row];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Generic fp32 decode used by the drop-in te_attention_decode_f32: any
+// head_dim, any group size, fp32 K/V in the reference's token-major layout.
+// Mirrors the reference's three passes (scores, softmax, weighted V sum) and
+// its per-dot accumulation order; only expf and the sum's order differ.
+__global__ void decode_f32_generic_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                          const float* __restrict__ v, float* __restrict__ scores,
+                                          float* __restrict__ out, int n, int kv_heads, int head_dim, int group,
+                                          float scale) {
+  const int h = blockIdx.x;
+  const int kvh = h / group;
+  const float* qh = q + (size_t)h * head_dim;
+  float* sc = scores + (size_t)h * n;
+  __shared__ float red[32];
+  __shared__ float bcast;
+  float mx = -FLT_MAX;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float* kt = k + ((size_t)t * kv_heads + kvh) * head_dim;
+    float dot = 0.f;
+    for (int d = 0; d < head_dim; ++d) dot = __fadd_rn(dot, __fmul_rn(qh[d], kt[d]));
+    const float s = __fmul_rn(dot, scale);
+    sc[t] = s;
+    mx = fmaxf(mx, s);
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = -FLT_MAX;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+    bcast = m;
+  }
+  __syncthreads();
+  mx = bcast;
+  float sum = 0.f;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float e = expf(sc[t] - mx);
+    sc[t] = e;
+    sum += e;
+  }
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i];
+    bcast = s;
+  }
+  __syncthreads();
+  const float total = bcast;
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    float acc = 0.f;
+    for (int t = 0; t < n; ++t) {
+      const float pt = total > 0.f ? __fdiv_rn(sc[t], total) : sc[t];
+      acc = __fadd_rn(acc, __fmul_rn(pt, v[((size_t)t * kv_heads + kvh) * head_dim + d]));
+    }
+    out[(size_t)h * head_dim + d] = acc;
+  }
+}
+
+// Log-sum-exp merge of partial records [n_parts][rows][hd + 2].
+__global__ void merge_partials_kernel(const float* __restrict__ partials, int n_parts, int rows, int head_dim,
+                                      float* __restrict__ out, int partial_out) {
+  const int row = blockIdx.x;
+  const int rec = head_dim + 2;
+  __shared__ float sM, sL;
+  if (threadIdx.x == 0) {
+    float M = -INFINITY;
+    for (int k = 0; k < n_parts; ++k) {
+      const float* r = partials + ((size_t)k * rows + row) * rec;
+      if (r[head_dim + 1] > 0.f) M = fmaxf(M, r[head_dim]);
+    }
+    float L = 0.f;
+    for (int k = 0; k < n_parts; ++k) {
+      const float* r = partials + ((size_t)k * rows + row) * rec;
+      if (r[head_dim + 1] > 0.f) L += r[head_dim + 1] * ex2(r[head_dim] - M);
+    }
+    sM = M;
+    sL = L;
+  }
+  __syncthreads();
+  const float M = sM, L = sL;
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    float O = 0.f;
+    for (int k = 0; k < n_parts; ++k) {
+      const float* r = partials + ((size_t)k * rows + row) * rec;
+      if (r[head_dim + 1] > 0.f) O += r[d] * ex2(r[head_dim] - M);
+    }
+    if (partial_out) {
+      float* r = out + (size_t)row * rec;
+      r[d] = O;
+      if (d == 0) { r[head_dim] = M; r[head_dim + 1] = L; }
+    } else {
+      out[(size_t)row * head_dim + d] = L > 0.f ? O / L : 0.f;
+    }
+  }
+}
+
+template <int HD, int R>
+cudaError_t launch_decode_impl(const DecodeParams& p, cudaStream_t s) {
+  using C = DecodeCfg<HD>;
+  const size_t smem = 1024 + (size_t)R * C::kStageBytes + 2 * R * sizeof(uint64_t) + 16;
+  static bool configured = false;  // per-process attribute; set once per instantiation
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(decode_f16_kernel<HD, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  dim3 grid(p.total_chunks, p.n_layers * p.kv_heads);
+  decode_f16_kernel<HD, R><<<grid, kThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_decode_f16(const DecodeParams& p, int head_dim, int stages, cudaStream_t s) {
+  (void)stages;
+  if (head_dim == 128) return launch_decode_impl<128, 3>(p, s);
+  if (head_dim == 64) return launch_decode_impl<64, 4>(p, s);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_decode_f32_generic(const float* q, const float* k, const float* v, float* scores, float* out,
+                                      size_t n_tokens, int heads, int kv_heads, int head_dim, cudaStream_t s) {
+  const float scale = 1.0f / sqrtf((float)head_dim);
+  decode_f32_generic_kernel<<<heads, 256, 0, s>>>(q, k, v, scores, out, (int)n_tokens, kv_heads, head_dim,
+                                                   heads / kv_heads, scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_merge_partials(const float* partials, int n_parts, int rows, int head_dim, float* out,
+                                  int partial_out, cudaStream_t s) {
+  merge_partials_kernel<<<rows, 128, 0, s>>>(partials, n_parts, rows, head_dim, out, partial_out);
+  return cudaGetLastError();
+}
+
+}  // namespace te

@@ -1,0 +1,757 @@
+// C-ABI layer of libtinyengine.so: argument validation with the reference's
+// status codes, the device-resident engine and paged f16 KV cache, work
+// decomposition for the kernels, and the two drop-in CPU-API functions.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tinyengine.h"
+#include "../../include/tinyengine_attn.h"
+#include "te_internal.h"
+
+extern "C" void te_host_rope_table(float* cos_table, float* sin_table, size_t first_position, size_t positions,
+                                   size_t head_dim, float theta);
+
+using namespace te;
+
+struct te_attn_engine {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  int sm_count = 148;
+  uint32_t decode_chunk = 0;
+  float* partials = nullptr;
+  size_t partials_bytes = 0;
+  uint32_t* counters = nullptr;
+  size_t counters_count = 0;
+  int* d_error = nullptr;
+  void* io = nullptr;  // device staging for TE_ATTN_HOST_BUFFERS
+  size_t io_bytes = 0;
+  void* qh = nullptr;  // prefill: rotated f16 queries
+  size_t qh_bytes = 0;
+  uint32_t* tile_counter = nullptr;
+  uint64_t launches = 0;
+  std::string last_error;
+};
+
+struct te_kv_cache {
+  te_attn_engine* eng = nullptr;
+  te_kv_cache_desc d{};
+  uint32_t pages_per_seq = 0;
+  uint16_t* k_pool = nullptr;
+  uint16_t* v_pool = nullptr;
+  int32_t* d_page_table = nullptr;
+  std::vector<int32_t> h_page_table;  // [max_seqs][pages_per_seq], -1 = unmapped
+  std::vector<int64_t> len, offset;
+  std::vector<int32_t> free_pages;
+  float* d_cos = nullptr;
+  float* d_sin = nullptr;
+  CUtensorMap tmap_k{}, tmap_v{};
+};
+
+namespace {
+
+// Switches to a device for the duration of a call and restores the caller's.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+te_status fail(te_attn_engine* e, te_status st, const std::string& msg) {
+  if (e) e->last_error = msg;
+  return st;
+}
+
+te_status cuda_fail(te_attn_engine* e, cudaError_t err, const char* what) {
+  std::string m = std::string(what) + ": " + cudaGetErrorString(err);
+  if (e) e->last_error = m;
+  return err == cudaErrorMemoryAllocation ? TE_STATUS_OUT_OF_MEMORY : TE_STATUS_RUNTIME_ERROR;
+}
+
+bool cuda_device_available() {
+  int n = 0;
+  return cudaGetDeviceCount(&n) == cudaSuccess && n > 0;
+}
+
+// Grows a device buffer; the stream is drained first so no queued kernel uses the old one.
+cudaError_t grow(te_attn_engine* e, void** buf, size_t* cap, size_t need, bool zero) {
+  if (need <= *cap) return cudaSuccess;
+  cudaError_t err = cudaStreamSynchronize(e->stream);
+  if (err != cudaSuccess) return err;
+  if (*buf) cudaFree(*buf);
+  *buf = nullptr;
+  *cap = 0;
+  size_t sz = std::max(need, (size_t)1 << 20);
+  err = cudaMalloc(buf, sz);
+  if (err != cudaSuccess) return err;
+  if (zero) {
+    err = cudaMemset(*buf, 0, sz);
+    if (err != cudaSuccess) return err;
+  }
+  *cap = sz;
+  return cudaSuccess;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  return fn;
+}
+
+// 2-D f16 tensor map over [rows][cols] with a box of box_rows x 64 columns, 128B swizzle.
+bool make_tmap_f16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+size_t pool_row(const te_kv_cache* c, size_t layer, int32_t page, size_t kvh, size_t tok_in_page) {
+  return ((layer * c->d.total_pages + (size_t)page) * c->d.kv_heads + kvh) * c->d.page_tokens + tok_in_page;
+}
+
+// Maps pages so that sequence `seq` can hold `tokens` tokens.
+te_status ensure_pages(te_kv_cache* c, size_t seq, size_t tokens) {
+  if (tokens > c->d.max_tokens_per_seq) {
+    return fail(c->eng, TE_STATUS_INVALID_ARGUMENT, "sequence would exceed max_tokens_per_seq");
+  }
+  const size_t need = (tokens + c->d.page_tokens - 1) / c->d.page_tokens;
+  int32_t* row = c->h_page_table.data() + seq * c->pages_per_seq;
+  size_t first_new = need, last_new = 0;
+  for (size_t i = 0; i < need; ++i) {
+    if (row[i] >= 0) continue;
+    if (c->free_pages.empty()) return fail(c->eng, TE_STATUS_OUT_OF_MEMORY, "KV page pool exhausted");
+    row[i] = c->free_pages.back();
+    c->free_pages.pop_back();
+    first_new = std::min(first_new, i);
+    last_new = i;
+  }
+  if (first_new < need) {
+    cudaError_t err = cudaMemcpyAsync(c->d_page_table + seq * c->pages_per_seq + first_new, row + first_new,
+                                      (last_new - first_new + 1) * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                      c->eng->stream);
+    if (err != cudaSuccess) return cuda_fail(c->eng, err, "page table upload");
+  }
+  return TE_STATUS_OK;
+}
+
+// Copies rows [n][kv_heads][hd] between a flat buffer and the paged pool.
+te_status copy_rows(te_kv_cache* c, size_t layer, size_t seq, size_t t0, size_t n, uint16_t* pool, void* flat,
+                    bool to_pool) {
+  const size_t hd = c->d.head_dim, hkv = c->d.kv_heads, P = c->d.page_tokens;
+  const int32_t* row = c->h_page_table.data() + seq * c->pages_per_seq;
+  size_t t = t0;
+  while (t < t0 + n) {
+    const size_t pg = t / P, in_pg = t % P;
+    const size_t m = std::min(P - in_pg, t0 + n - t);
+    if (row[pg] < 0) return fail(c->eng, TE_STATUS_INVALID_ARGUMENT, "tokens outside the sequence's pages");
+    for (size_t h = 0; h < hkv; ++h) {
+      uint16_t* dev = pool + pool_row(c, layer, row[pg], h, in_pg) * hd;
+      uint16_t* fl = reinterpret_cast<uint16_t*>(flat) + ((t - t0) * hkv + h) * hd;
+      cudaError_t err = to_pool ? cudaMemcpy2DAsync(dev, hd * 2, fl, hkv * hd * 2, hd * 2, m, cudaMemcpyDefault,
+                                                    c->eng->stream)
+                                : cudaMemcpy2DAsync(fl, hkv * hd * 2, dev, hd * 2, hd * 2, m, cudaMemcpyDefault,
+                                                    c->eng->stream);
+      if (err != cudaSuccess) return cuda_fail(c->eng, err, "KV row copy");
+    }
+    t += m;
+  }
+  return TE_STATUS_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// tinyengine.h: version, status strings, drop-in CPU-API functions
+// ===========================================================================
+
+extern "C" {
+
+TE_API const char* te_version(void) { return "0.1.0-b200-attn"; }
+
+TE_API const char* te_strerror(te_status status) {
+  switch (status) {
+    case TE_STATUS_OK: return "ok";
+    case TE_STATUS_INVALID_ARGUMENT: return "invalid argument";
+    case TE_STATUS_IO_ERROR: return "I/O error";
+    case TE_STATUS_UNSUPPORTED: return "unsupported";
+    case TE_STATUS_OUT_OF_MEMORY: return "out of memory";
+    case TE_STATUS_RUNTIME_ERROR: return "runtime error";
+    default: return "unknown error";
+  }
+}
+
+TE_API te_status te_rope_f32(float* values, size_t heads, size_t head_dim, size_t position, float theta) {
+  // Validation order and codes: c/src/ops.c:302-304.
+  if (values == NULL || heads == 0u || head_dim == 0u || (head_dim % 2u) != 0u || !(theta > 0.0f)) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  if (!cuda_device_available()) return TE_STATUS_UNSUPPORTED;
+  const size_t half = head_dim / 2;
+  std::vector<float> tab(2 * half);
+  te_host_rope_table(tab.data(), tab.data() + half, position, 1, head_dim, theta);
+  cudaStream_t s = cudaStreamPerThread;
+  const size_t vbytes = heads * head_dim * sizeof(float);
+  float* d = nullptr;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&d), vbytes + 2 * half * sizeof(float), s) != cudaSuccess) {
+    return TE_STATUS_OUT_OF_MEMORY;
+  }
+  float* dtab = d + heads * head_dim;
+  te_status st = TE_STATUS_OK;
+  if (cudaMemcpyAsync(d, values, vbytes, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaMemcpyAsync(dtab, tab.data(), 2 * half * sizeof(float), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      launch_rope_rows(d, dtab, dtab + half, (int)heads, (int)head_dim, s) != cudaSuccess ||
+      cudaMemcpyAsync(values, d, vbytes, cudaMemcpyDeviceToHost, s) != cudaSuccess) {
+    st = TE_STATUS_RUNTIME_ERROR;
+  }
+  cudaFreeAsync(d, s);
+  if (cudaStreamSynchronize(s) != cudaSuccess) st = TE_STATUS_RUNTIME_ERROR;
+  return st;
+}
+
+TE_API te_status te_attention_decode_f32(const float* query, const float* key_cache, const float* value_cache,
+                                         size_t position, size_t heads, size_t kv_heads, size_t head_dim,
+                                         float* out) {
+  // Validation order and codes: c/src/ops.c:333-339.
+  if (query == NULL || key_cache == NULL || value_cache == NULL || out == NULL || heads == 0u || kv_heads == 0u ||
+      head_dim == 0u || (heads % kv_heads) != 0u) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  if (position == SIZE_MAX) return TE_STATUS_UNSUPPORTED;
+  if (!cuda_device_available()) return TE_STATUS_UNSUPPORTED;
+  const size_t n = position + 1;
+  if (n > (size_t)INT32_MAX || heads > 65535u) return TE_STATUS_UNSUPPORTED;
+  cudaStream_t s = cudaStreamPerThread;
+  const size_t qb = heads * head_dim * sizeof(float);
+  const size_t kvb = n * kv_heads * head_dim * sizeof(float);
+  const size_t scb = heads * n * sizeof(float);
+  char* d = nullptr;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&d), 2 * qb + 2 * kvb + scb, s) != cudaSuccess) {
+    return TE_STATUS_OUT_OF_MEMORY;
+  }
+  float* dq = reinterpret_cast<float*>(d);
+  float* dout = reinterpret_cast<float*>(d + qb);
+  float* dk = reinterpret_cast<float*>(d + 2 * qb);
+  float* dv = reinterpret_cast<float*>(d + 2 * qb + kvb);
+  float* dsc = reinterpret_cast<float*>(d + 2 * qb + 2 * kvb);
+  te_status st = TE_STATUS_OK;
+  if (cudaMemcpyAsync(dq, query, qb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaMemcpyAsync(dk, key_cache, kvb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaMemcpyAsync(dv, value_cache, kvb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      launch_decode_f32_generic(dq, dk, dv, dsc, dout, n, (int)heads, (int)kv_heads, (int)head_dim, s) !=
+          cudaSuccess ||
+      cudaMemcpyAsync(out, dout, qb, cudaMemcpyDeviceToHost, s) != cudaSuccess) {
+    st = TE_STATUS_RUNTIME_ERROR;
+  }
+  cudaFreeAsync(d, s);
+  if (cudaStreamSynchronize(s) != cudaSuccess) st = TE_STATUS_RUNTIME_ERROR;
+  return st;
+}
+
+// ===========================================================================
+// tinyengine_attn.h: engine
+// ===========================================================================
+
+TE_API te_attn_options te_attn_default_options(void) {
+  te_attn_options o;
+  std::memset(&o, 0, sizeof(o));
+  o.abi_version = TE_ATTN_ABI_VERSION;
+  return o;
+}
+
+TE_API te_status te_attn_engine_create(const te_attn_options* options, te_attn_engine** out_engine) {
+  if (options == NULL || out_engine == NULL) return TE_STATUS_INVALID_ARGUMENT;
+  *out_engine = nullptr;
+  if (options->abi_version != TE_ATTN_ABI_VERSION) return TE_STATUS_UNSUPPORTED;
+  if (options->decode_chunk_tokens % kStageTokens != 0) return TE_STATUS_INVALID_ARGUMENT;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return TE_STATUS_UNSUPPORTED;
+  if (options->device < 0 || options->device >= n) return TE_STATUS_INVALID_ARGUMENT;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, options->device) != cudaSuccess) return TE_STATUS_RUNTIME_ERROR;
+  if (prop.major != 10) return TE_STATUS_UNSUPPORTED;  // built for sm_100a only
+  DeviceGuard dg(options->device);
+  te_attn_engine* e = new te_attn_engine();
+  e->device = options->device;
+  e->sm_count = prop.multiProcessorCount;
+  e->decode_chunk = options->decode_chunk_tokens;
+  if (options->stream) {
+    e->stream = reinterpret_cast<cudaStream_t>(options->stream);
+  } else {
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) {
+      delete e;
+      return TE_STATUS_RUNTIME_ERROR;
+    }
+    e->own_stream = true;
+  }
+  if (cudaMalloc(reinterpret_cast<void**>(&e->d_error), 64) != cudaSuccess ||
+      cudaMemset(e->d_error, 0, 64) != cudaSuccess) {
+    te_attn_engine_free(e);
+    return TE_STATUS_OUT_OF_MEMORY;
+  }
+  e->tile_counter = reinterpret_cast<uint32_t*>(e->d_error + 4);
+  *out_engine = e;
+  return TE_STATUS_OK;
+}
+
+TE_API void te_attn_engine_free(te_attn_engine* e) {
+  if (!e) return;
+  {
+    DeviceGuard dg(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    cudaFree(e->partials);
+    cudaFree(e->counters);
+    cudaFree(e->d_error);
+    cudaFree(e->io);
+    cudaFree(e->qh);
+    if (e->own_stream && e->stream) cudaStreamDestroy(e->stream);
+  }
+  delete e;
+}
+
+TE_API te_status te_attn_engine_set_stream(te_attn_engine* e, void* stream) {
+  if (!e) return TE_STATUS_INVALID_ARGUMENT;
+  DeviceGuard dg(e->device);
+  cudaStreamSynchronize(e->stream);
+  if (e->own_stream) cudaStreamDestroy(e->stream);
+  e->own_stream = false;
+  e->stream = reinterpret_cast<cudaStream_t>(stream);
+  if (!stream) {
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) return TE_STATUS_RUNTIME_ERROR;
+    e->own_stream = true;
+  }
+  return TE_STATUS_OK;
+}
+
+TE_API void* te_attn_engine_stream(const te_attn_engine* e) { return e ? reinterpret_cast<void*>(e->stream) : nullptr; }
+
+TE_API te_status te_attn_engine_synchronize(te_attn_engine* e) {
+  if (!e) return TE_STATUS_INVALID_ARGUMENT;
+  DeviceGuard dg(e->device);
+  cudaError_t err = cudaStreamSynchronize(e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "stream synchronize");
+  int code = 0;
+  err = cudaMemcpy(&code, e->d_error, sizeof(int), cudaMemcpyDeviceToHost);
+  if (err != cudaSuccess) return cuda_fail(e, err, "error word read");
+  if (code != 0) {
+    cudaMemset(e->d_error, 0, sizeof(int));
+    char buf[128];
+    std::snprintf(buf, sizeof(buf), "device-side error %d (a bounded wait expired or a capacity check failed)", code);
+    return fail(e, TE_STATUS_RUNTIME_ERROR, buf);
+  }
+  return TE_STATUS_OK;
+}
+
+TE_API const char* te_attn_engine_last_error(const te_attn_engine* e) {
+  return e ? e->last_error.c_str() : "no engine";
+}
+
+TE_API uint64_t te_attn_engine_launch_count(const te_attn_engine* e) { return e ? e->launches : 0; }
+
+// ===========================================================================
+// KV cache
+// ===========================================================================
+
+TE_API te_kv_cache_desc te_kv_cache_default_desc(void) {
+  te_kv_cache_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.abi_version = TE_ATTN_ABI_VERSION;
+  d.layers = 1;
+  d.max_seqs = 1;
+  d.max_tokens_per_seq = 4096;
+  d.kv_heads = 2;
+  d.head_dim = 128;
+  d.page_tokens = 128;
+  d.rope_theta = 1000000.0f;
+  return d;
+}
+
+TE_API te_status te_kv_cache_create(te_attn_engine* e, const te_kv_cache_desc* desc, te_kv_cache** out_cache) {
+  if (!e || !desc || !out_cache) return TE_STATUS_INVALID_ARGUMENT;
+  *out_cache = nullptr;
+  if (desc->abi_version != TE_ATTN_ABI_VERSION) return fail(e, TE_STATUS_UNSUPPORTED, "cache desc ABI version");
+  te_kv_cache_desc d = *desc;
+  if (d.page_tokens == 0) d.page_tokens = 128;
+  if (d.layers == 0 || d.max_seqs == 0 || d.max_tokens_per_seq == 0 || d.kv_heads == 0 ||
+      !(d.rope_theta > 0.0f) || d.page_tokens % kStageTokens != 0) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "invalid cache description");
+  }
+  if (d.head_dim != 64 && d.head_dim != 128) return fail(e, TE_STATUS_UNSUPPORTED, "head_dim must be 64 or 128");
+  const uint32_t pps = (d.max_tokens_per_seq + d.page_tokens - 1) / d.page_tokens;
+  if (d.total_pages == 0) d.total_pages = d.max_seqs * pps;
+  if (d.max_position == 0) d.max_position = d.max_tokens_per_seq;
+  const uint64_t rows = (uint64_t)d.layers * d.total_pages * d.kv_heads * d.page_tokens;
+  if (rows >= (1ull << 31)) return fail(e, TE_STATUS_UNSUPPORTED, "pool too large for 32-bit row coordinates");
+  DeviceGuard dg(e->device);
+  te_kv_cache* c = new te_kv_cache();
+  c->eng = e;
+  c->d = d;
+  c->pages_per_seq = pps;
+  const size_t pool_bytes = rows * d.head_dim * sizeof(uint16_t);
+  const size_t half = d.head_dim / 2;
+  cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&c->k_pool), pool_bytes);
+  if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void**>(&c->v_pool), pool_bytes);
+  if (err == cudaSuccess) err = cudaMemsetAsync(c->k_pool, 0, pool_bytes, e->stream);
+  if (err == cudaSuccess) err = cudaMemsetAsync(c->v_pool, 0, pool_bytes, e->stream);
+  if (err == cudaSuccess)
+    err = cudaMalloc(reinterpret_cast<void**>(&c->d_page_table), (size_t)d.max_seqs * pps * sizeof(int32_t));
+  if (err == cudaSuccess)
+    err = cudaMalloc(reinterpret_cast<void**>(&c->d_cos), 2 * (size_t)d.max_position * half * sizeof(float));
+  if (err != cudaSuccess) {
+    te_kv_cache_free(c);
+    return cuda_fail(e, err, "KV cache allocation");
+  }
+  c->d_sin = c->d_cos + (size_t)d.max_position * half;
+  c->h_page_table.assign((size_t)d.max_seqs * pps, -1);
+  c->len.assign(d.max_seqs, 0);
+  c->offset.assign(d.max_seqs, 0);
+  c->free_pages.resize(d.total_pages);
+  for (uint32_t i = 0; i < d.total_pages; ++i) c->free_pages[i] = (int32_t)(d.total_pages - 1 - i);
+  std::vector<float> tab(2 * (size_t)d.max_position * half);
+  te_host_rope_table(tab.data(), tab.data() + (size_t)d.max_position * half, 0, d.max_position, d.head_dim,
+                     d.rope_theta);
+  err = cudaMemcpy(c->d_cos, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice);
+  if (err == cudaSuccess)
+    err = cudaMemcpy(c->d_page_table, c->h_page_table.data(), c->h_page_table.size() * sizeof(int32_t),
+                     cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  if (err != cudaSuccess) {
+    te_kv_cache_free(c);
+    return cuda_fail(e, err, "KV cache initialisation");
+  }
+  if (!make_tmap_f16(&c->tmap_k, c->k_pool, rows, d.head_dim, kStageTokens) ||
+      !make_tmap_f16(&c->tmap_v, c->v_pool, rows, d.head_dim, kStageTokens)) {
+    te_kv_cache_free(c);
+    return fail(e, TE_STATUS_RUNTIME_ERROR, "cuTensorMapEncodeTiled failed");
+  }
+  *out_cache = c;
+  return TE_STATUS_OK;
+}
+
+TE_API void te_kv_cache_free(te_kv_cache* c) {
+  if (!c) return;
+  {
+    DeviceGuard dg(c->eng->device);
+    cudaStreamSynchronize(c->eng->stream);
+    cudaFree(c->k_pool);
+    cudaFree(c->v_pool);
+    cudaFree(c->d_page_table);
+    cudaFree(c->d_cos);
+  }
+  delete c;
+}
+
+TE_API te_status te_kv_cache_seq_reset(te_kv_cache* c, size_t seq, size_t position_offset) {
+  if (!c || seq >= c->d.max_seqs) return TE_STATUS_INVALID_ARGUMENT;
+  int32_t* row = c->h_page_table.data() + seq * c->pages_per_seq;
+  for (uint32_t i = 0; i < c->pages_per_seq; ++i) {
+    if (row[i] >= 0) c->free_pages.push_back(row[i]);
+    row[i] = -1;
+  }
+  c->len[seq] = 0;
+  c->offset[seq] = (int64_t)position_offset;
+  // Device rows of unmapped entries are never read (reads stop at the length).
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_kv_cache_seq_truncate(te_kv_cache* c, size_t seq, size_t length) {
+  if (!c || seq >= c->d.max_seqs || length > (size_t)c->len[seq]) return TE_STATUS_INVALID_ARGUMENT;
+  c->len[seq] = (int64_t)length;  // pages stay mapped; later appends overwrite the dropped tokens
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_kv_cache_seq_length(const te_kv_cache* c, size_t seq, size_t* out_length) {
+  if (!c || !out_length || seq >= c->d.max_seqs) return TE_STATUS_INVALID_ARGUMENT;
+  *out_length = (size_t)c->len[seq];
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_kv_cache_write_f16(te_kv_cache* c, size_t layer, size_t seq, size_t token_begin,
+                                       size_t n_tokens, const uint16_t* k, const uint16_t* v) {
+  if (!c || !k || !v || layer >= c->d.layers || seq >= c->d.max_seqs || n_tokens == 0) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  DeviceGuard dg(c->eng->device);
+  te_status st = ensure_pages(c, seq, token_begin + n_tokens);
+  if (st != TE_STATUS_OK) return st;
+  st = copy_rows(c, layer, seq, token_begin, n_tokens, c->k_pool, const_cast<uint16_t*>(k), true);
+  if (st == TE_STATUS_OK) st = copy_rows(c, layer, seq, token_begin, n_tokens, c->v_pool, const_cast<uint16_t*>(v), true);
+  if (st != TE_STATUS_OK) return st;
+  c->len[seq] = std::max<int64_t>(c->len[seq], (int64_t)(token_begin + n_tokens));
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_kv_cache_read_f16(te_kv_cache* c, size_t layer, size_t seq, size_t token_begin,
+                                      size_t n_tokens, uint16_t* k, uint16_t* v) {
+  if (!c || !k || !v || layer >= c->d.layers || seq >= c->d.max_seqs || n_tokens == 0) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  if (token_begin + n_tokens > (size_t)c->len[seq]) return fail(c->eng, TE_STATUS_INVALID_ARGUMENT, "read past length");
+  DeviceGuard dg(c->eng->device);
+  te_status st = copy_rows(c, layer, seq, token_begin, n_tokens, c->k_pool, k, false);
+  if (st == TE_STATUS_OK) st = copy_rows(c, layer, seq, token_begin, n_tokens, c->v_pool, v, false);
+  if (st != TE_STATUS_OK) return st;
+  cudaError_t err = cudaStreamSynchronize(c->eng->stream);
+  return err == cudaSuccess ? TE_STATUS_OK : cuda_fail(c->eng, err, "KV read");
+}
+
+// ===========================================================================
+// Compute
+// ===========================================================================
+
+TE_API te_status te_kv_append_rope(te_kv_cache* c, size_t layer_begin, size_t n_layers, size_t seq, const void* k,
+                                   const void* v, size_t n_tokens, uint32_t flags) {
+  if (!c || !k || !v || n_layers == 0 || n_tokens == 0 || layer_begin + n_layers > c->d.layers ||
+      seq >= c->d.max_seqs) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | TE_ATTN_NO_ROPE)) {
+    return fail(c->eng, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for te_kv_append_rope");
+  }
+  te_attn_engine* e = c->eng;
+  DeviceGuard dg(e->device);
+  const int64_t first = c->len[seq];
+  if ((uint64_t)(c->offset[seq] + first + n_tokens) > c->d.max_position) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "RoPE position beyond max_position");
+  }
+  te_status st = ensure_pages(c, seq, (size_t)first + n_tokens);
+  if (st != TE_STATUS_OK) return st;
+  AppendParams p{};
+  p.k = k;
+  p.v = v;
+  p.k_pool = c->k_pool;
+  p.v_pool = c->v_pool;
+  p.page_row = c->d_page_table + seq * c->pages_per_seq;
+  p.rope_cos = c->d_cos;
+  p.rope_sin = c->d_sin;
+  p.input_f16 = (flags & TE_ATTN_INPUT_F16) ? 1 : 0;
+  p.rope = (flags & TE_ATTN_NO_ROPE) ? 0 : 1;
+  p.n_layers = (int32_t)n_layers;
+  p.layer_begin = (int32_t)layer_begin;
+  p.n_tokens = (int32_t)n_tokens;
+  p.first_index = (int32_t)first;
+  p.first_pos = (int32_t)(c->offset[seq] + first);
+  p.kv_heads = (int32_t)c->d.kv_heads;
+  p.head_dim = (int32_t)c->d.head_dim;
+  p.num_pages = (int32_t)c->d.total_pages;
+  p.page_tokens = (int32_t)c->d.page_tokens;
+  cudaError_t err = launch_append_rope(p, e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "append kernel launch");
+  e->launches++;
+  if (flags & TE_ATTN_ADVANCE) c->len[seq] = first + (int64_t)n_tokens;
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t n_layers, const uint32_t* seq_ids,
+                                     size_t n_seqs, const int64_t* q_positions, const float* q, const float* k_new,
+                                     const float* v_new, size_t heads, float* out, uint32_t flags) {
+  if (!c || !seq_ids || !q || !out || n_layers == 0 || n_seqs == 0 || heads == 0 ||
+      layer_begin + n_layers > c->d.layers || (k_new == NULL) != (v_new == NULL)) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  te_attn_engine* e = c->eng;
+  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_PARTIAL | TE_ATTN_NO_ROPE | TE_ATTN_HOST_BUFFERS)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for te_attention_decode");
+  }
+  const size_t hkv = c->d.kv_heads, hd = c->d.head_dim;
+  if (heads % hkv != 0) return fail(e, TE_STATUS_INVALID_ARGUMENT, "heads must be a multiple of kv_heads");
+  const size_t G = heads / hkv;
+  if (G > 16) return fail(e, TE_STATUS_UNSUPPORTED, "more than 16 query heads per kv head");
+  if (n_seqs > c->d.max_seqs) return TE_STATUS_INVALID_ARGUMENT;
+  const bool append = k_new != NULL;
+  DeviceGuard dg(e->device);
+
+  // Per-sequence work, validated before anything is queued.
+  std::vector<SeqEntry> ent(n_seqs);
+  std::vector<char> seen(c->d.max_seqs, 0);
+  size_t max_len = 0;
+  for (size_t i = 0; i < n_seqs; ++i) {
+    const uint32_t s = seq_ids[i];
+    if (s >= c->d.max_seqs || seen[s]) return fail(e, TE_STATUS_INVALID_ARGUMENT, "bad or repeated sequence id");
+    seen[s] = 1;
+    const int64_t len = c->len[s] + (append ? 1 : 0);
+    if (len <= 0) return fail(e, TE_STATUS_INVALID_ARGUMENT, "decode over an empty sequence");
+    if ((uint64_t)len > c->d.max_tokens_per_seq) return fail(e, TE_STATUS_INVALID_ARGUMENT, "sequence full");
+    const int64_t qpos = q_positions ? q_positions[i] : c->offset[s] + len - 1;
+    const int64_t npos = append ? c->offset[s] + len - 1 : -1;
+    if (qpos < 0 || (uint64_t)qpos >= c->d.max_position || (uint64_t)(npos + 1) > c->d.max_position) {
+      return fail(e, TE_STATUS_INVALID_ARGUMENT, "RoPE position beyond max_position");
+    }
+    ent[i].slot = (int32_t)s;
+    ent[i].len = (int32_t)len;
+    ent[i].q_pos = (int32_t)qpos;
+    ent[i].new_pos = (int32_t)npos;
+    max_len = std::max(max_len, (size_t)len);
+  }
+  if (append) {
+    for (size_t i = 0; i < n_seqs; ++i) {
+      te_status st = ensure_pages(c, seq_ids[i], (size_t)ent[i].len);
+      if (st != TE_STATUS_OK) return st;
+    }
+  }
+
+  // Split-K chunk: a multiple of the 64-token stage, sized for ~8 CTAs per SM
+  // over the whole call, and large enough that one sequence's chunk count
+  // fits the in-kernel combine's shared-memory table.
+  size_t total_tok = 0;
+  for (auto& x : ent) total_tok += (size_t)x.len;
+  total_tok *= hkv * n_layers;
+  size_t chunk = e->decode_chunk;
+  if (chunk == 0) {
+    chunk = total_tok / ((size_t)8 * e->sm_count);
+    chunk = std::min<size_t>(std::max<size_t>(chunk, 64), 4096);
+  }
+  const size_t stage_floats = (hd == 128 ? 3 * 32768 : 4 * 16384) / 4;
+  const size_t max_chunks = (stage_floats - 4096 - 32) / (2 * G);
+  chunk = std::max(chunk, (max_len + max_chunks - 1) / max_chunks);
+  chunk = (chunk + kStageTokens - 1) / kStageTokens * kStageTokens;
+
+  // Device staging for host buffers.
+  const size_t q_elems = n_layers * n_seqs * heads * hd;
+  const size_t kv_elems = n_layers * n_seqs * hkv * hd;
+  const size_t out_elems = n_layers * n_seqs * heads * (hd + ((flags & TE_ATTN_PARTIAL) ? 2 : 0));
+  const float* dq = q;
+  const float* dk = k_new;
+  const float* dv = v_new;
+  float* dout = out;
+  if (flags & TE_ATTN_HOST_BUFFERS) {
+    const size_t need = (q_elems + 2 * kv_elems + out_elems) * sizeof(float);
+    cudaError_t err = grow(e, &e->io, &e->io_bytes, need, false);
+    if (err != cudaSuccess) return cuda_fail(e, err, "staging allocation");
+    float* base = reinterpret_cast<float*>(e->io);
+    float* sq = base;
+    float* sk = sq + q_elems;
+    float* sv = sk + kv_elems;
+    dout = sv + kv_elems;
+    err = cudaMemcpyAsync(sq, q, q_elems * sizeof(float), cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess && append) err = cudaMemcpyAsync(sk, k_new, kv_elems * sizeof(float), cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess && append) err = cudaMemcpyAsync(sv, v_new, kv_elems * sizeof(float), cudaMemcpyHostToDevice, e->stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "input upload");
+    dq = sq;
+    dk = append ? sk : nullptr;
+    dv = append ? sv : nullptr;
+  }
+
+  DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.tmap_k = c->tmap_k;
+  p.tmap_v = c->tmap_v;
+  p.page_table = c->d_page_table;
+  p.q = dq;
+  p.k_new = dk;
+  p.v_new = dv;
+  p.out = dout;
+  p.k_pool = c->k_pool;
+  p.v_pool = c->v_pool;
+  p.rope_cos = c->d_cos;
+  p.rope_sin = c->d_sin;
+  p.error = e->d_error;
+  p.seq_total = (int32_t)n_seqs;
+  p.layer_begin = (int32_t)layer_begin;
+  p.n_layers = (int32_t)n_layers;
+  p.kv_heads = (int32_t)hkv;
+  p.group = (int32_t)G;
+  p.chunk_tokens = (int32_t)chunk;
+  p.num_pages = (int32_t)c->d.total_pages;
+  p.page_tokens = (int32_t)c->d.page_tokens;
+  p.max_pages_per_seq = (int32_t)c->pages_per_seq;
+  p.rope = (flags & TE_ATTN_NO_ROPE) ? 0 : 1;
+  p.partial_out = (flags & TE_ATTN_PARTIAL) ? 1 : 0;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hd));
+
+  for (size_t base = 0; base < n_seqs; base += kMaxParamSeqs) {
+    const size_t nb = std::min<size_t>(kMaxParamSeqs, n_seqs - base);
+    int32_t chunks = 0;
+    for (size_t i = 0; i < nb; ++i) {
+      SeqEntry x = ent[base + i];
+      x.chunk_begin = chunks;
+      x.n_chunks = (int32_t)((x.len + chunk - 1) / chunk);
+      chunks += x.n_chunks;
+      p.seqs[i] = x;
+    }
+    p.n_seqs = (int32_t)nb;
+    p.seq_base = (int32_t)base;
+    p.total_chunks = chunks;
+    const size_t part_bytes = n_layers * hkv * (size_t)chunks * G * (hd + 2) * sizeof(float);
+    cudaError_t err = grow(e, reinterpret_cast<void**>(&e->partials), &e->partials_bytes, part_bytes, false);
+    if (err == cudaSuccess) {
+      size_t bytes = e->counters_count * sizeof(uint32_t);
+      err = grow(e, reinterpret_cast<void**>(&e->counters), &bytes, n_layers * hkv * nb * sizeof(uint32_t), true);
+      e->counters_count = bytes / sizeof(uint32_t);
+    }
+    if (err != cudaSuccess) return cuda_fail(e, err, "decode scratch allocation");
+    p.partials = e->partials;
+    p.counters = e->counters;
+    if (n_layers * hkv > 65535u) return fail(e, TE_STATUS_UNSUPPORTED, "too many layers x kv heads in one call");
+    err = launch_decode_f16(p, (int)hd, 0, e->stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "decode kernel launch");
+    e->launches++;
+  }
+
+  if (flags & TE_ATTN_HOST_BUFFERS) {
+    cudaError_t err = cudaMemcpyAsync(out, dout, out_elems * sizeof(float), cudaMemcpyDeviceToHost, e->stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "output download");
+  }
+  if (append && (flags & TE_ATTN_ADVANCE)) {
+    for (size_t i = 0; i < n_seqs; ++i) c->len[seq_ids[i]] += 1;
+  }
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_attention_merge_partials(te_attn_engine* e, const float* partials, size_t n_parts, size_t rows,
+                                             size_t head_dim, float* out, uint32_t flags) {
+  if (!e || !partials || !out || n_parts == 0 || rows == 0 || head_dim == 0) return TE_STATUS_INVALID_ARGUMENT;
+  if (flags & ~TE_ATTN_PARTIAL) return fail(e, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for merge");
+  if (rows > (size_t)INT32_MAX) return TE_STATUS_UNSUPPORTED;
+  DeviceGuard dg(e->device);
+  cudaError_t err = launch_merge_partials(partials, (int)n_parts, (int)rows, (int)head_dim, out,
+                                          (flags & TE_ATTN_PARTIAL) ? 1 : 0, e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "merge kernel launch");
+  e->launches++;
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t n_layers, size_t seq,
+                                      const void* q, const void* k, const void* v, size_t n_tokens, size_t heads,
+                                      float* out, uint32_t flags) {
+  if (!c || !q || !k || !v || !out || n_layers == 0 || n_tokens == 0 || heads == 0 ||
+      layer_begin + n_layers > c->d.layers || seq >= c->d.max_seqs) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  (void)flags;
+  return fail(c->eng, TE_STATUS_UNSUPPORTED, "prefill kernel not built yet");
+}
+
+}  // extern "C"

@@ -1,0 +1,138 @@
+// Internal declarations shared by the C-ABI layer (te_api.cpp) and the
+// kernel translation units (*.cu).  Not installed; not part of the ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/tinyengine_attn.h"
+
+namespace te {
+
+// Decode work description for one sequence, passed to the decode kernel by
+// value (kernel parameter space), so a launch needs no host->device copy.
+struct SeqEntry {
+  int32_t slot;         // cache sequence slot (row of the page table)
+  int32_t len;          // tokens attended (after the optional append)
+  int32_t q_pos;        // RoPE position of the query
+  int32_t new_pos;      // RoPE position of the appended token, or -1 (no append)
+  int32_t chunk_begin;  // first split-K chunk index of this sequence in the grid
+  int32_t n_chunks;     // number of split-K chunks
+};
+
+constexpr int kMaxParamSeqs = 64;  // sequences per decode launch
+constexpr int kStageTokens = 64;   // tokens per TMA stage
+
+struct DecodeParams {
+  CUtensorMap tmap_k;  // 2-D view [rows][head_dim] of the K pool, box 64x64, 128B swizzle
+  CUtensorMap tmap_v;
+  const int32_t* page_table;  // [max_seqs][max_pages_per_seq]
+  const float* q;             // [n_layers][n_seqs][heads][hd]
+  const float* k_new;         // [n_layers][n_seqs][kv_heads][hd] or null
+  const float* v_new;
+  float* out;                 // normalised [..][heads][hd] or partial [..][heads][hd+2]
+  float* partials;            // split-K scratch
+  uint32_t* counters;         // [n_layers][kv_heads][n_seqs], zero between launches
+  uint16_t* k_pool;           // for the fused append (generic stores)
+  uint16_t* v_pool;
+  const float* rope_cos;      // [max_position][hd/2]
+  const float* rope_sin;
+  int* error;
+  int32_t n_seqs;             // sequences in this launch (<= kMaxParamSeqs)
+  int32_t seq_total;          // sequences in the caller's arrays (row stride of q/out)
+  int32_t seq_base;           // index of this launch's first sequence in those arrays
+  int32_t layer_begin;
+  int32_t n_layers;
+  int32_t kv_heads;
+  int32_t group;              // heads per kv head (<= 16)
+  int32_t chunk_tokens;       // multiple of kStageTokens
+  int32_t total_chunks;
+  int32_t num_pages;          // pages per layer
+  int32_t page_tokens;
+  int32_t max_pages_per_seq;
+  int32_t rope;               // 1: rotate q (and appended k)
+  int32_t partial_out;        // 1: write partial records
+  float scale_log2;           // log2(e) / sqrt(hd)
+  SeqEntry seqs[kMaxParamSeqs];
+};
+
+// Launchers (kernels live in the .cu files).  All return cudaError_t of the launch.
+cudaError_t launch_decode_f16(const DecodeParams& p, int head_dim, int stages, cudaStream_t s);
+cudaError_t launch_decode_f32_generic(const float* q, const float* k, const float* v, float* scores, float* out,
+                                      size_t n_tokens, int heads, int kv_heads, int head_dim, cudaStream_t s);
+cudaError_t launch_rope_rows(float* values, const float* cos_row, const float* sin_row, int heads, int head_dim,
+                             cudaStream_t s);
+cudaError_t launch_merge_partials(const float* partials, int n_parts, int rows, int head_dim, float* out,
+                                  int partial_out, cudaStream_t s);
+
+struct AppendParams {
+  const void* k;            // [n_layers][n_tokens][kv_heads][hd], fp32 or f16
+  const void* v;
+  uint16_t* k_pool;
+  uint16_t* v_pool;
+  const int32_t* page_row;  // page table row of the sequence
+  const float* rope_cos;
+  const float* rope_sin;
+  int32_t input_f16;
+  int32_t rope;
+  int32_t n_layers;
+  int32_t layer_begin;
+  int32_t n_tokens;
+  int32_t first_index;      // local token index of the first new token
+  int32_t first_pos;        // global RoPE position of the first new token
+  int32_t kv_heads;
+  int32_t head_dim;
+  int32_t num_pages;
+  int32_t page_tokens;
+};
+cudaError_t launch_append_rope(const AppendParams& p, cudaStream_t s);
+
+// Rotates (optionally) and converts prefill queries to a head-major f16 buffer
+// qh[n_layers][heads][n_tokens_padded][hd] for the prefill kernel's TMA loads.
+struct QPrepParams {
+  const void* q;            // [n_layers][n_tokens][heads][hd]
+  __half* qh;
+  const float* rope_cos;
+  const float* rope_sin;
+  int32_t input_f16;
+  int32_t rope;
+  int32_t n_layers;
+  int32_t n_tokens;
+  int32_t n_tokens_padded;
+  int32_t heads;
+  int32_t head_dim;
+  int32_t first_pos;
+};
+cudaError_t launch_q_prep(const QPrepParams& p, cudaStream_t s);
+
+struct PrefillParams {
+  CUtensorMap tmap_q;   // [n_layers*heads*n_tokens_padded][hd] f16
+  CUtensorMap tmap_k;   // K pool view
+  CUtensorMap tmap_v;
+  const int32_t* page_table_row;
+  float* out;           // [n_layers][n_tokens][heads][hd]
+  int* error;
+  int32_t n_layers;
+  int32_t layer_begin;
+  int32_t heads;
+  int32_t kv_heads;
+  int32_t n_tokens;
+  int32_t n_tokens_padded;
+  int32_t q_offset;     // cached tokens before the first new token
+  int32_t num_pages;
+  int32_t page_tokens;
+  int32_t n_items;      // work items (layer, head, q tile)
+  uint32_t* tile_counter;
+  float scale_log2;
+};
+cudaError_t launch_prefill_tc(const PrefillParams& p, cudaStream_t s);
+cudaError_t launch_prefill_simt(const PrefillParams& p, const __half* qh, const uint16_t* k_pool,
+                                const uint16_t* v_pool, cudaStream_t s);
+
+}  // namespace te

@@ -1,0 +1,313 @@
+"""ctypes binding of libtinyengine.so (include/tinyengine.h + include/tinyengine_attn.h).
+
+Follows the shape of TinyEngine's own binding (python/tinyengine/runtime.py:
+library discovery through ``TINYENGINE_LIBRARY`` (:244-268),
+``_configure_library`` setting argtypes/restype (:271-378) and ``_check``
+raising ``TinyEngineError`` with ``te_strerror`` text (:381-384)).
+
+Compute entry points take device pointers; the helpers below accept torch CUDA
+tensors (``data_ptr()``) or raw integer addresses.  Host-buffer calls
+(``TE_ATTN_HOST_BUFFERS``) accept numpy arrays or pinned CPU tensors.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Optional, Sequence
+
+TE_ABI_VERSION = 3
+TE_ATTN_ABI_VERSION = 1
+
+TE_STATUS_OK = 0
+TE_STATUS_INVALID_ARGUMENT = 1
+TE_STATUS_IO_ERROR = 2
+TE_STATUS_UNSUPPORTED = 3
+TE_STATUS_OUT_OF_MEMORY = 4
+TE_STATUS_RUNTIME_ERROR = 5
+
+TE_ATTN_ADVANCE = 1 << 0
+TE_ATTN_PARTIAL = 1 << 1
+TE_ATTN_NO_ROPE = 1 << 2
+TE_ATTN_INPUT_F16 = 1 << 3
+TE_ATTN_HOST_BUFFERS = 1 << 4
+
+
+class TinyEngineError(RuntimeError):
+    def __init__(self, message: str, status: int = TE_STATUS_RUNTIME_ERROR):
+        super().__init__(message)
+        self.status = status
+
+
+class AttnOptions(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", ctypes.c_uint32),
+        ("device", ctypes.c_int32),
+        ("stream", ctypes.c_void_p),
+        ("decode_chunk_tokens", ctypes.c_uint32),
+        ("flags", ctypes.c_uint32),
+    ]
+
+
+class KVCacheDesc(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", ctypes.c_uint32),
+        ("layers", ctypes.c_uint32),
+        ("max_seqs", ctypes.c_uint32),
+        ("max_tokens_per_seq", ctypes.c_uint32),
+        ("kv_heads", ctypes.c_uint32),
+        ("head_dim", ctypes.c_uint32),
+        ("page_tokens", ctypes.c_uint32),
+        ("total_pages", ctypes.c_uint32),
+        ("max_position", ctypes.c_uint32),
+        ("rope_theta", ctypes.c_float),
+    ]
+
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_i64p = ctypes.POINTER(ctypes.c_int64)
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+_int = ctypes.c_int
+
+
+def _candidate_libraries() -> list[Path]:
+    env = os.environ.get("TINYENGINE_LIBRARY")
+    here = Path(__file__).resolve()
+    out: list[Path] = []
+    if env:
+        out.append(Path(env))
+    out.append(here.parent / "libtinyengine.so")
+    return out
+
+
+# Every entry point of include/*.h with its ctypes signature (restype, argtypes).
+SIGNATURES: dict[str, tuple] = {
+    "te_version": (ctypes.c_char_p, []),
+    "te_strerror": (ctypes.c_char_p, [_int]),
+    "te_rope_f32": (_int, [_f32p, _sz, _sz, _sz, ctypes.c_float]),
+    "te_attention_decode_f32": (_int, [_f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, _f32p]),
+    "te_attn_default_options": (AttnOptions, []),
+    "te_attn_engine_create": (_int, [ctypes.POINTER(AttnOptions), ctypes.POINTER(_vp)]),
+    "te_attn_engine_free": (None, [_vp]),
+    "te_attn_engine_set_stream": (_int, [_vp, _vp]),
+    "te_attn_engine_stream": (_vp, [_vp]),
+    "te_attn_engine_synchronize": (_int, [_vp]),
+    "te_attn_engine_last_error": (ctypes.c_char_p, [_vp]),
+    "te_attn_engine_launch_count": (ctypes.c_uint64, [_vp]),
+    "te_kv_cache_default_desc": (KVCacheDesc, []),
+    "te_kv_cache_create": (_int, [_vp, ctypes.POINTER(KVCacheDesc), ctypes.POINTER(_vp)]),
+    "te_kv_cache_free": (None, [_vp]),
+    "te_kv_cache_seq_reset": (_int, [_vp, _sz, _sz]),
+    "te_kv_cache_seq_truncate": (_int, [_vp, _sz, _sz]),
+    "te_kv_cache_seq_length": (_int, [_vp, _sz, ctypes.POINTER(_sz)]),
+    "te_kv_cache_write_f16": (_int, [_vp, _sz, _sz, _sz, _sz, _vp, _vp]),
+    "te_kv_cache_read_f16": (_int, [_vp, _sz, _sz, _sz, _sz, _vp, _vp]),
+    "te_kv_append_rope": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _sz, ctypes.c_uint32]),
+    "te_attention_decode": (_int, [_vp, _sz, _sz, _u32p, _sz, _i64p, _vp, _vp, _vp, _sz, _vp, ctypes.c_uint32]),
+    "te_attention_merge_partials": (_int, [_vp, _vp, _sz, _sz, _sz, _vp, ctypes.c_uint32]),
+    "te_attention_prefill": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _vp, _sz, _sz, _vp, ctypes.c_uint32]),
+}
+
+
+def _configure_library(lib: ctypes.CDLL) -> None:
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+
+
+_LIB: Optional[ctypes.CDLL] = None
+
+
+def load_library() -> ctypes.CDLL:
+    """Loads libtinyengine.so; raises TinyEngineError when it has not been built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    for cand in _candidate_libraries():
+        if cand.is_file():
+            lib = ctypes.CDLL(str(cand))
+            _configure_library(lib)
+            _LIB = lib
+            return lib
+    searched = "\n".join(str(p) for p in _candidate_libraries())
+    raise TinyEngineError(
+        "libtinyengine.so not found (build it with `python -m tinymetalagent_b200.build`). Searched:\n" + searched,
+        TE_STATUS_UNSUPPORTED,
+    )
+
+
+def _check(lib: ctypes.CDLL, status: int, engine=None) -> None:
+    if status != TE_STATUS_OK:
+        message = lib.te_strerror(status).decode()
+        if engine is not None:
+            detail = lib.te_attn_engine_last_error(engine)
+            if detail:
+                message = f"{message}: {detail.decode()}"
+        raise TinyEngineError(message, status)
+
+
+def _addr(x) -> Optional[int]:
+    """Device/host address of a torch tensor, numpy array, int or None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):
+        return x.ctypes.data
+    raise TypeError(f"cannot take the address of {type(x)!r}")
+
+
+# ---------------------------------------------------------------------------
+# Drop-in CPU-API functions (host fp32 buffers, same contract as the reference)
+# ---------------------------------------------------------------------------
+
+def rope_f32(values, heads: int, head_dim: int, position: int, theta: float) -> None:
+    """In-place te_rope_f32 on a float32 numpy array (runs on the current CUDA device)."""
+    lib = load_library()
+    _check(lib, lib.te_rope_f32(values.ctypes.data_as(_f32p), heads, head_dim, position, theta))
+
+
+def attention_decode_f32(query, key_cache, value_cache, position: int, heads: int, kv_heads: int,
+                         head_dim: int, out) -> None:
+    """te_attention_decode_f32 on float32 numpy arrays."""
+    lib = load_library()
+    _check(lib, lib.te_attention_decode_f32(
+        query.ctypes.data_as(_f32p), key_cache.ctypes.data_as(_f32p), value_cache.ctypes.data_as(_f32p),
+        position, heads, kv_heads, head_dim, out.ctypes.data_as(_f32p)))
+
+
+# ---------------------------------------------------------------------------
+# Device-resident engine
+# ---------------------------------------------------------------------------
+
+class AttnEngine:
+    """One engine per GPU: owns a stream (or uses the given one) and decode scratch."""
+
+    def __init__(self, device: int = 0, stream: Optional[int] = None, decode_chunk_tokens: int = 0):
+        self.lib = load_library()
+        opts = self.lib.te_attn_default_options()
+        opts.device = device
+        opts.stream = stream
+        opts.decode_chunk_tokens = decode_chunk_tokens
+        handle = _vp()
+        _check(self.lib, self.lib.te_attn_engine_create(ctypes.byref(opts), ctypes.byref(handle)))
+        self.handle = handle
+        self.device = device
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.te_attn_engine_free(self.handle)
+            self.handle = None
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, status: int) -> None:
+        _check(self.lib, status, self.handle)
+
+    @property
+    def stream(self) -> int:
+        return self.lib.te_attn_engine_stream(self.handle) or 0
+
+    def set_stream(self, stream: Optional[int]) -> None:
+        self.check(self.lib.te_attn_engine_set_stream(self.handle, stream))
+
+    def synchronize(self) -> None:
+        self.check(self.lib.te_attn_engine_synchronize(self.handle))
+
+    @property
+    def launch_count(self) -> int:
+        return int(self.lib.te_attn_engine_launch_count(self.handle))
+
+    def merge_partials(self, partials, n_parts: int, rows: int, head_dim: int, out, partial_out: bool = False):
+        self.check(self.lib.te_attention_merge_partials(
+            self.handle, _addr(partials), n_parts, rows, head_dim, _addr(out),
+            TE_ATTN_PARTIAL if partial_out else 0))
+
+    def kv_cache(self, **kw) -> "KVCache":
+        return KVCache(self, **kw)
+
+
+class KVCache:
+    """Paged f16 KV cache in HBM: [layers][pages][kv_heads][page_tokens][head_dim] per K and V."""
+
+    def __init__(self, engine: AttnEngine, layers: int, max_seqs: int, max_tokens_per_seq: int, kv_heads: int,
+                 head_dim: int, page_tokens: int = 128, total_pages: int = 0, max_position: int = 0,
+                 rope_theta: float = 1e6):
+        self.engine = engine
+        self.lib = engine.lib
+        d = self.lib.te_kv_cache_default_desc()
+        d.layers, d.max_seqs, d.max_tokens_per_seq = layers, max_seqs, max_tokens_per_seq
+        d.kv_heads, d.head_dim, d.page_tokens = kv_heads, head_dim, page_tokens
+        d.total_pages, d.max_position, d.rope_theta = total_pages, max_position, rope_theta
+        handle = _vp()
+        engine.check(self.lib.te_kv_cache_create(engine.handle, ctypes.byref(d), ctypes.byref(handle)))
+        self.handle = handle
+        self.layers, self.max_seqs, self.kv_heads, self.head_dim = layers, max_seqs, kv_heads, head_dim
+        self.page_tokens = page_tokens
+        self.max_tokens_per_seq = max_tokens_per_seq
+        self.rope_theta = rope_theta
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.te_kv_cache_free(self.handle)
+            self.handle = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _c(self, status: int) -> None:
+        self.engine.check(status)
+
+    def reset(self, seq: int, position_offset: int = 0) -> None:
+        self._c(self.lib.te_kv_cache_seq_reset(self.handle, seq, position_offset))
+
+    def truncate(self, seq: int, length: int) -> None:
+        self._c(self.lib.te_kv_cache_seq_truncate(self.handle, seq, length))
+
+    def length(self, seq: int) -> int:
+        n = _sz()
+        self._c(self.lib.te_kv_cache_seq_length(self.handle, seq, ctypes.byref(n)))
+        return n.value
+
+    def write_f16(self, layer: int, seq: int, token_begin: int, k, v) -> None:
+        """k, v: [n][kv_heads][head_dim] binary16 (torch f16 tensor, numpy float16/uint16)."""
+        n = int(k.shape[0])
+        self._c(self.lib.te_kv_cache_write_f16(self.handle, layer, seq, token_begin, n, _addr(k), _addr(v)))
+
+    def read_f16(self, layer: int, seq: int, token_begin: int, n_tokens: int):
+        import numpy as np
+        k = np.zeros((n_tokens, self.kv_heads, self.head_dim), dtype=np.uint16)
+        v = np.zeros_like(k)
+        self._c(self.lib.te_kv_cache_read_f16(self.handle, layer, seq, token_begin, n_tokens, k.ctypes.data,
+                                              v.ctypes.data))
+        return k, v
+
+    def append_rope(self, layer_begin: int, n_layers: int, seq: int, k, v, n_tokens: int, flags: int = 0) -> None:
+        self._c(self.lib.te_kv_append_rope(self.handle, layer_begin, n_layers, seq, _addr(k), _addr(v), n_tokens,
+                                           flags))
+
+    def decode(self, layer_begin: int, n_layers: int, seq_ids: Sequence[int], q, out, heads: int,
+               k_new=None, v_new=None, q_positions: Optional[Sequence[int]] = None, flags: int = 0) -> None:
+        n = len(seq_ids)
+        ids = (ctypes.c_uint32 * n)(*seq_ids)
+        qp = (ctypes.c_int64 * n)(*q_positions) if q_positions is not None else None
+        self._c(self.lib.te_attention_decode(self.handle, layer_begin, n_layers, ids, n, qp, _addr(q),
+                                             _addr(k_new), _addr(v_new), heads, _addr(out), flags))
+
+    def prefill(self, layer_begin: int, n_layers: int, seq: int, q, k, v, n_tokens: int, heads: int, out,
+                flags: int = 0) -> None:
+        self._c(self.lib.te_attention_prefill(self.handle, layer_begin, n_layers, seq, _addr(q), _addr(k), _addr(v),
+                                              n_tokens, heads, _addr(out), flags))
