@@ -216,7 +216,7 @@ def run_gpu(args) -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
 
     hbm_peak, tc_peak, peak_src = load_peaks()
-    eng = AttnEngine(local)
+    eng = AttnEngine(local, decode_chunk_tokens=args.chunk)
     stream = torch.cuda.ExternalStream(eng.stream)
     cap = CTX0 + DECODE_STEPS
     cache = eng.kv_cache(layers=LAYERS, max_seqs=1, max_tokens_per_seq=cap, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
@@ -356,7 +356,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--chunk", type=int, default=0, help="split-K chunk tokens (multiple of 64; 0 = auto)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
