@@ -175,6 +175,46 @@ TE_API te_status te_attention_prefill(te_kv_cache *cache, size_t layer_begin, si
                                       size_t seq, const void *q, const void *k, const void *v,
                                       size_t n_tokens, size_t heads, float *out, uint32_t flags);
 
+/*
+ * Allocation-free decode for callers that cannot allocate device memory:
+ * code that runs where cudaMalloc is not allowed or would break its memory
+ * plan (a host framework or plugin host that owns every device allocation, a
+ * fixed-budget serving runtime, work issued from a context that must not
+ * synchronise the device).  Such callers cannot create an engine, whose
+ * decode scratch grows with cudaMalloc.  No counterpart in the reference
+ * (TinyEngine's CPU and Metal paths allocate freely).
+ *
+ * One layer, one sequence: q[heads][head_dim] fp32 (used as given, already
+ * rotated) attends the first n_tokens tokens of a caller-owned paged f16
+ * cache laid out like one layer of the engine's pool,
+ * k_pool/v_pool[num_pages][kv_heads][page_tokens][head_dim], with
+ * page_table[i] = page holding tokens [i*page_tokens, (i+1)*page_tokens).
+ * All pointers are device pointers; out[heads][head_dim] fp32.  Work is
+ * queued on `stream` (cudaStream_t, NULL = legacy default stream) on the
+ * current device; the call does not synchronise.
+ *
+ * The split-K scratch is a fixed 4 MiB + 1.25 KiB file-scope device array
+ * that every GPU which loads this library holds until the process exits.
+ * Limits: head_dim 64 or 128; heads / kv_heads <= 16; kv_heads <= 256;
+ * kv_heads * (heads / kv_heads) * (head_dim + 2) * 4 bytes must fit the
+ * 4 MiB scratch (chunking adapts to n_tokens); larger shapes return
+ * TE_STATUS_UNSUPPORTED.  The call allocates nothing: no cudaMalloc or
+ * cudaFree and no allocating library routine.
+ *
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current), so make that first call
+ * before any stream capture.  Every call shares the one array: calls whose
+ * kernels overlap on the GPU (different streams, or different host threads)
+ * race on it and must be serialised by the caller.  Counters are cleared at
+ * the start of each call; a device-side wait that expires is not reported by
+ * this asynchronous call.
+ */
+TE_API te_status te_attention_decode_paged_noalloc(
+    const uint16_t *k_pool, const uint16_t *v_pool, const int32_t *page_table,
+    size_t num_pages, size_t page_tokens, size_t n_tokens,
+    const float *q, size_t heads, size_t kv_heads, size_t head_dim,
+    float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -22,8 +22,11 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
+#include <cstring>
+#include <mutex>
 
 #include "te_internal.h"
 #include "te_ptx.cuh"
@@ -581,3 +584,124 @@ cudaError_t launch_merge_partials(const float* partials, int n_parts, int rows, 
 }
 
 }  // namespace te
+
+// ===========================================================================
+// Allocation-free decode entry point.
+//
+// Callers that cannot allocate device memory -- code running where
+// cudaMalloc is not permitted or not wanted (inside a host callback or a
+// stream-ordered region that must not synchronise, a runtime with its own
+// fixed memory plan, a plugin whose host framework owns every allocation) --
+// cannot create an engine, whose decode scratch grows with cudaMalloc.  This
+// entry point runs the same decode kernel with its split-K scratch (partial
+// records, completion counters, error word) in one fixed file-scope device
+// array instead.  Every GPU that loads this library holds that array until
+// the process exits.
+// ===========================================================================
+
+namespace {
+
+constexpr size_t kNoAllocPartialBytes = size_t(4) << 20;  // split-K partial records (4 MiB)
+constexpr size_t kNoAllocCounterBytes = 1024;             // 256 completion counters
+constexpr size_t kNoAllocScratchBytes = kNoAllocPartialBytes + kNoAllocCounterBytes + 256;  // + error word
+constexpr int kNoAllocMaxKvHeads = 256;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch per device, resolved once per device
+// with that device current.  In host code the symbol itself is only a
+// host-side stand-in, never a device address.
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) te_status te_attention_decode_paged_noalloc(
+    const uint16_t* k_pool, const uint16_t* v_pool, const int32_t* page_table, size_t num_pages,
+    size_t page_tokens, size_t n_tokens, const float* q, size_t heads, size_t kv_heads, size_t head_dim,
+    float* out, void* stream) {
+  using namespace te;
+  if (!k_pool || !v_pool || !page_table || !q || !out || num_pages == 0 || n_tokens == 0 || heads == 0 ||
+      kv_heads == 0 || heads % kv_heads != 0 || page_tokens == 0 || page_tokens % kStageTokens != 0) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  if (head_dim != 64 && head_dim != 128) return TE_STATUS_UNSUPPORTED;
+  const size_t G = heads / kv_heads;
+  if (G > 16 || kv_heads > (size_t)kNoAllocMaxKvHeads) return TE_STATUS_UNSUPPORTED;
+  const size_t pages_needed = (n_tokens + page_tokens - 1) / page_tokens;
+  const uint64_t rows = (uint64_t)num_pages * kv_heads * page_tokens;
+  if (pages_needed > num_pages || rows >= (1ull << 31) || n_tokens > (size_t)INT32_MAX) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  // Chunking: the partial records of all chunks must fit the fixed scratch and
+  // the kernel's in-shared-memory combine table.
+  const size_t rec_bytes = kv_heads * G * (head_dim + 2) * sizeof(float);
+  const size_t fit_chunks = kNoAllocPartialBytes / rec_bytes;
+  if (fit_chunks == 0) return TE_STATUS_UNSUPPORTED;
+  const size_t stage_floats = (head_dim == 128 ? 3 * 32768 : 4 * 16384) / 4;
+  const size_t smem_chunks = (stage_floats - 4096 - 32) / (2 * G);
+  const size_t max_chunks = std::min(fit_chunks, smem_chunks);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return TE_STATUS_RUNTIME_ERROR;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  size_t chunk = n_tokens * kv_heads / ((size_t)8 * sms);
+  chunk = std::min<size_t>(std::max<size_t>(chunk, 64), 4096);
+  chunk = std::max(chunk, (n_tokens + max_chunks - 1) / max_chunks);
+  chunk = (chunk + kStageTokens - 1) / kStageTokens * kStageTokens;
+  const size_t n_chunks = (n_tokens + chunk - 1) / chunk;
+
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+        return TE_STATUS_RUNTIME_ERROR;
+      }
+      g_noalloc_addr[dev] = p;
+    }
+    base = g_noalloc_addr[dev];
+  }
+  unsigned char* scratch = static_cast<unsigned char*>(base);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // Counters and the error word must start at zero; partial records need no clearing.
+  if (cudaMemsetAsync(scratch + kNoAllocPartialBytes, 0, kNoAllocCounterBytes + 256, s) != cudaSuccess) {
+    return TE_STATUS_RUNTIME_ERROR;
+  }
+
+  DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  if (!encode_tmap_f16(&p.tmap_k, k_pool, rows, head_dim, kStageTokens) ||
+      !encode_tmap_f16(&p.tmap_v, v_pool, rows, head_dim, kStageTokens)) {
+    return TE_STATUS_RUNTIME_ERROR;
+  }
+  p.page_table = page_table;
+  p.q = q;
+  p.out = out;
+  p.partials = reinterpret_cast<float*>(scratch);
+  p.counters = reinterpret_cast<uint32_t*>(scratch + kNoAllocPartialBytes);
+  p.error = reinterpret_cast<int*>(scratch + kNoAllocPartialBytes + kNoAllocCounterBytes);
+  p.n_seqs = 1;
+  p.seq_total = 1;
+  p.layer_begin = 0;
+  p.n_layers = 1;
+  p.kv_heads = (int32_t)kv_heads;
+  p.group = (int32_t)G;
+  p.chunk_tokens = (int32_t)chunk;
+  p.total_chunks = (int32_t)n_chunks;
+  p.num_pages = (int32_t)num_pages;
+  p.page_tokens = (int32_t)page_tokens;
+  p.max_pages_per_seq = (int32_t)pages_needed;
+  p.rope = 0;
+  p.partial_out = 0;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+  p.seqs[0].slot = 0;
+  p.seqs[0].len = (int32_t)n_tokens;
+  p.seqs[0].q_pos = 0;
+  p.seqs[0].new_pos = -1;
+  p.seqs[0].chunk_begin = 0;
+  p.seqs[0].n_chunks = (int32_t)n_chunks;
+  return launch_decode_f16(p, (int)head_dim, 0, s) == cudaSuccess ? TE_STATUS_OK : TE_STATUS_RUNTIME_ERROR;
+}

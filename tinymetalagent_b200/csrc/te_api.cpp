@@ -192,6 +192,12 @@ te_status copy_rows(te_kv_cache* c, size_t layer, size_t seq, size_t t0, size_t 
 
 }  // namespace
 
+namespace te {
+bool encode_tmap_f16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  return make_tmap_f16(m, base, rows, cols, box_rows);
+}
+}  // namespace te
+
 // ===========================================================================
 // tinyengine.h: version, status strings, drop-in CPU-API functions
 // ===========================================================================

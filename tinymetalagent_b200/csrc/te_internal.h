@@ -62,6 +62,9 @@ struct DecodeParams {
   SeqEntry seqs[kMaxParamSeqs];
 };
 
+// 2-D f16 tensor map over [rows][cols] (box box_rows x 64, 128B swizzle); false on failure.
+bool encode_tmap_f16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+
 // Launchers (kernels live in the .cu files).  All return cudaError_t of the launch.
 cudaError_t launch_decode_f16(const DecodeParams& p, int head_dim, int stages, cudaStream_t s);
 cudaError_t launch_decode_f32_generic(const float* q, const float* k, const float* v, float* scores, float* out,

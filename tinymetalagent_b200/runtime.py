@@ -109,6 +109,7 @@ SIGNATURES: dict[str, tuple] = {
     "te_attention_decode": (_int, [_vp, _sz, _sz, _u32p, _sz, _i64p, _vp, _vp, _vp, _sz, _vp, ctypes.c_uint32]),
     "te_attention_merge_partials": (_int, [_vp, _vp, _sz, _sz, _sz, _vp, ctypes.c_uint32]),
     "te_attention_prefill": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _vp, _sz, _sz, _vp, ctypes.c_uint32]),
+    "te_attention_decode_paged_noalloc": (_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _sz, _sz, _sz, _vp, _vp]),
 }
 
 
