@@ -318,6 +318,11 @@ def run_gpu(args) -> None:
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
                "sample": f"{calls} config-2 layer calls (N={CTX0 + 1}, 16 heads) in {dt:.1f} s on {threads} threads"}
 
+    # ---- prefill: 2048-token causal prefill over 36 layers ----
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill(eng, stream, tc_peak, peak_src, args, world, rank, local)
+
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.is_file():
@@ -341,12 +346,63 @@ def run_gpu(args) -> None:
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     cache.close()
     eng.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_prefill(eng, stream, tc_peak, peak_src, args, world, rank, local):
+    """Config 3: f16 Q/K/V for 2048 tokens x 36 layers; one te_attention_prefill call
+    (RoPE + f16 append, query prep, tcgen05 flash prefill) per step, device-timed."""
+    import torch
+    import torch.distributed as dist
+
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16
+    s = PREFILL_TOKENS
+    cache = eng.kv_cache(layers=LAYERS, max_seqs=1, max_tokens_per_seq=s, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
+                         rope_theta=THETA)
+    g = torch.Generator(device="cuda").manual_seed(99 + rank)
+    with torch.cuda.stream(stream):
+        q = torch.randn((LAYERS, s, HEADS, HEAD_DIM), generator=g, device="cuda").half()
+        k = torch.randn((LAYERS, s, KV_HEADS, HEAD_DIM), generator=g, device="cuda").half()
+        v = torch.randn((LAYERS, s, KV_HEADS, HEAD_DIM), generator=g, device="cuda").half()
+        out = torch.empty((LAYERS, s, HEADS, HEAD_DIM), device="cuda")
+    stream.synchronize()
+
+    def step():
+        cache.truncate(0, 0)
+        cache.prefill(0, LAYERS, 0, q, k, v, s, HEADS, out, TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16)
+
+    for _ in range(3):
+        step()
+    eng.synchronize()
+    steps = max(3, min(args.prefill_steps, 50))
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = eng.launch_count
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    ev1.synchronize()
+    eng.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = prefill_flops(s, LAYERS)
+    tflops = flops / (ms / 1e3) / 1e12
+    cache.close()
+    return {"metric": "causal prefill attention TFLOP/s (BASELINE config 3)", "value": round(tflops * world, 2),
+            "unit": "TFLOP/s", "ms_per_step": round(ms, 4), "steps": steps,
+            "workload": "S=2048, H16/Hkv2/hd128, 36 layers, f16 Q/K/V, RoPE+append+tcgen05 prefill per step",
+            "flops_per_step": flops, "gpu_launches": int(eng.launch_count - launches0),
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                         "frac": round(tflops / tc_peak, 4), "peak_source": f"{peak_src} (bf16 dense burst)"}}
 
 
 def main() -> None:
@@ -358,6 +414,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--chunk", type=int, default=0, help="split-K chunk tokens (multiple of 64; 0 = auto)")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
+    ap.add_argument("--prefill-steps", type=int, default=10)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

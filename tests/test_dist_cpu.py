@@ -1,0 +1,112 @@
+"""Multi-GPU host logic on CPU: the sequence-sharding planner, the KV-split
+ranges, and the KV-split decode protocol (partial records, all-gather, LSE
+merge) run as world-size-2 gloo ranks with the CPU oracle standing in for the
+per-rank GPU compute."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from tinymetalagent_b200.dist import KVSplitDecoder, ShardSpec, kv_split_ranges, merge_partials_numpy, shard_sequences
+
+
+def test_shard_sequences_balanced_and_complete():
+    rng = np.random.default_rng(0)
+    lengths = rng.integers(256, 8193, size=64)
+    for world in (1, 2, 4, 8):
+        shards = shard_sequences(lengths, world)
+        flat = sorted(i for s in shards for i in s)
+        assert flat == list(range(64))
+        loads = [int(sum(lengths[i] for i in s)) for s in shards]
+        assert max(loads) - min(loads) <= int(lengths.max())
+        assert shards == shard_sequences(lengths, world)
+
+
+def test_kv_split_ranges_cover_contiguously():
+    for n, w in [(32768, 1), (32768, 2), (32768, 8), (10, 3), (7, 7)]:
+        r = kv_split_ranges(n, w)
+        assert r[0][0] == 0 and r[-1][1] == n
+        assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
+        assert max(e - b for b, e in r) - min(e - b for b, e in r) <= 1
+        assert (r[-1][1] - r[-1][0]) == min(e - b for b, e in r)
+    with pytest.raises(ValueError):
+        kv_split_ranges(3, 4)
+
+
+H, HKV, HD, N, STEPS, THETA = 8, 2, 64, 301, 3, 1e6
+
+
+def _data():
+    rng = np.random.default_rng(42)
+    k = rng.standard_normal((N + STEPS, HKV, HD)).astype(np.float32)
+    v = rng.standard_normal((N + STEPS, HKV, HD)).astype(np.float32)
+    q = rng.standard_normal((STEPS, H, HD)).astype(np.float32)
+    return k, v, q
+
+
+def _worker(rank, world, port_no, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port_no)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import oracle as O
+        port = O.port()
+        kraw, vraw, qraw = _data()
+        spec = ShardSpec.plan(rank, world, N)
+        kb, vb = port.append_rope_f16(kraw[spec.begin:spec.end], vraw[spec.begin:spec.end], spec.begin, HKV, HD, THETA)
+        local = {"k": port.f16_bits_to_f32(kb), "v": port.f16_bits_to_f32(vb)}
+
+        def partial_fn(q, k_new, v_new, q_pos):
+            if spec.is_tail:
+                nk, nv = port.append_rope_f16(k_new.numpy()[0, 0][None], v_new.numpy()[0, 0][None], q_pos, HKV, HD, THETA)
+                local["k"] = np.concatenate([local["k"], port.f16_bits_to_f32(nk)])
+                local["v"] = np.concatenate([local["v"], port.f16_bits_to_f32(nv)])
+            qr = q.numpy()[0, 0].copy().ravel()
+            port.rope_f32(qr, H, HD, q_pos, THETA)
+            n_local = local["k"].shape[0]
+            return torch.from_numpy(port.decode_partial_f32(qr, local["k"].ravel(), local["v"].ravel(), 0, n_local,
+                                                            H, HKV, HD))
+
+        dec = KVSplitDecoder(spec, 1, H, HD, partial_fn=partial_fn,
+                             merge_fn=lambda g: torch.from_numpy(merge_partials_numpy(g.numpy())), device="cpu")
+        worst = 0.0
+        for s in range(STEPS):
+            out = dec.step(torch.from_numpy(qraw[s][None, None]), torch.from_numpy(kraw[N + s][None, None]),
+                           torch.from_numpy(vraw[N + s][None, None])).numpy()
+            # full-sequence oracle over positions 0..N+s
+            kb_all, vb_all = port.append_rope_f16(kraw[:N + s + 1], vraw[:N + s + 1], 0, HKV, HD, THETA)
+            qr = qraw[s].copy().ravel()
+            port.rope_f32(qr, H, HD, N + s, THETA)
+            exp = port.attention_decode_f32(qr, port.f16_bits_to_f32(kb_all).ravel(),
+                                            port.f16_bits_to_f32(vb_all).ravel(), N + s, H, HKV, HD)
+            worst = max(worst, float(np.max(np.abs(out.ravel() - exp) - (1e-5 + 1e-4 * np.abs(exp)))))
+        results.put((rank, worst))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_kv_split_protocol_gloo(world):
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, _free_port() if False else 29611 + world, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    codes = [p.exitcode for p in procs]
+    assert codes == [0] * world, codes
+    got = sorted(results.get(timeout=5) for _ in range(world))
+    assert [r for r, _ in got] == list(range(world))
+    assert all(w <= 0 for _, w in got), got

@@ -46,6 +46,16 @@ struct DecodeCfg {
   static constexpr int kChunksPerThread = HD / 32;         // 16-byte chunks of a K row per thread
   static constexpr int kThreadsPerBox = 8 / kChunksPerThread;
   static constexpr int kNTiles = HD / 8;                   // mma n-tiles for P.V
+  static constexpr int kRing = HD == 128 ? 5 : 8;          // stages in flight per CTA
+  static constexpr int kMergeBytes = kConsumerWarps * 16 * HD * 4;
+  static constexpr int kQBytes = 16 * HD * 4;              // rotated q rows of the group, fp32
+  static constexpr int kOffMerge = kRing * kStageBytes;
+  static constexpr int kOffQ = kOffMerge + kMergeBytes;
+  static constexpr int kOffML = kOffQ + kQBytes;           // m[4][16], l[4][16]
+  static constexpr int kOffBar = kOffML + 2 * kConsumerWarps * 16 * 4;
+  static constexpr int kSmemBytes = kOffBar + 2 * kRing * 8 + 64 + 1024;
+  // combine table (per-chunk m and l of one group) lives in the merge area
+  static constexpr int kMaxCombineFloats = kMergeBytes / 4 - 32;
 };
 
 __device__ __forceinline__ float rope_lo(float a, float b, float c, float s) {
@@ -55,8 +65,8 @@ __device__ __forceinline__ float rope_hi(float a, float b, float c, float s) {
   return __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
 }
 
-// Physical head-dim offset (in halves) of the 16-byte chunk a thread with
-// quad index c reads for k-step pair j.
+// Physical head-dim offset (in 16-byte chunks within a 64-column box) that a
+// thread with quad index c reads for k-step pair j, and the box it lies in.
 template <int HD>
 __device__ __forceinline__ int k_chunk_of(int c, int j, int* box) {
   using C = DecodeCfg<HD>;
@@ -64,36 +74,55 @@ __device__ __forceinline__ int k_chunk_of(int c, int j, int* box) {
   return C::kChunksPerThread * (c % C::kThreadsPerBox) + ((j + c) % C::kChunksPerThread);
 }
 
-template <int HD, int R>
-__global__ void __launch_bounds__(kThreads, 2) decode_f16_kernel(const __grid_constant__ DecodeParams p) {
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+}
+
+// One work item: a chunk of one (layer, sequence, kv head).
+struct Work {
+  int layer_local, kvh, si, cx, t0, t1, n_st;
+};
+
+__device__ __forceinline__ Work work_of(const DecodeParams& p, int it) {
+  Work w;
+  const int grp = it / p.total_chunks;  // layer_local * kv_heads + kvh
+  w.cx = it - grp * p.total_chunks;
+  w.layer_local = grp / p.kv_heads;
+  w.kvh = grp - w.layer_local * p.kv_heads;
+  int lo = 0, hi = p.n_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.seqs[mid].chunk_begin <= w.cx) lo = mid; else hi = mid - 1;
+  }
+  w.si = lo;
+  w.t0 = (w.cx - p.seqs[lo].chunk_begin) * p.chunk_tokens;
+  w.t1 = min(p.seqs[lo].len, w.t0 + p.chunk_tokens);
+  w.n_st = (w.t1 - w.t0 + kStageTokens - 1) / kStageTokens;
+  return w;
+}
+
+// Persistent: one CTA per SM loops over work items (round-robin), the TMA
+// ring streams continuously across items.
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_constant__ DecodeParams p) {
   using C = DecodeCfg<HD>;
+  constexpr int R = C::kRing;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + R * C::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* empty = full + R;
   int* flags = reinterpret_cast<int*>(empty + R);
+  float* sm_o = reinterpret_cast<float*>(smem + C::kOffMerge);  // [4][16][HD]
+  float* sm_q = reinterpret_cast<float*>(smem + C::kOffQ);      // [16][HD] rotated q
+  float* sm_m = reinterpret_cast<float*>(smem + C::kOffML);     // [4][16]
+  float* sm_l = sm_m + kConsumerWarps * 16;                     // [4][16]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-
-  // ---- work item -------------------------------------------------------
-  const int cx = blockIdx.x;
-  const int layer_local = blockIdx.y / p.kv_heads;
-  const int kvh = blockIdx.y % p.kv_heads;
-  int si = 0;
-  for (int i = 1; i < p.n_seqs; ++i) {
-    if (cx >= p.seqs[i].chunk_begin) si = i;
-  }
-  const SeqEntry se = p.seqs[si];
-  const int chunk = cx - se.chunk_begin;
-  if (chunk < 0 || chunk >= se.n_chunks) return;  // uniform per CTA
-  const int t0 = chunk * p.chunk_tokens;
-  const int t1 = min(se.len, t0 + p.chunk_tokens);
-  const int n_st = (t1 - t0 + kStageTokens - 1) / kStageTokens;
-  const int layer = p.layer_begin + layer_local;
   const int G = p.group;
   const int H = p.group * p.kv_heads;
+  const int n_items = p.n_layers * p.kv_heads * p.total_chunks;
 
   if (tid == 0) {
     for (int i = 0; i < R; ++i) {
@@ -101,144 +130,156 @@ __global__ void __launch_bounds__(kThreads, 2) decode_f16_kernel(const __grid_co
       mbar_init(&empty[i], kConsumerWarps);
     }
     fence_mbarrier_init();
-    flags[0] = 0;
-  }
-
-  // ---- fused RoPE(k) + f16 append of the new token (tail chunk only) ----
-  const int new_idx = se.len - 1;
-  if (se.new_pos >= 0 && p.k_new != nullptr && new_idx >= t0 && new_idx < t1 && tid < HD) {
-    const int page = p.page_table[se.slot * p.max_pages_per_seq + new_idx / p.page_tokens];
-    const size_t row = ((size_t)(layer * p.num_pages + page) * p.kv_heads + kvh) * p.page_tokens +
-                       (new_idx % p.page_tokens);
-    const float* kn = p.k_new + ((size_t)(layer_local * p.seq_total + p.seq_base + si) * p.kv_heads + kvh) * HD;
-    const float* vn = p.v_new + ((size_t)(layer_local * p.seq_total + p.seq_base + si) * p.kv_heads + kvh) * HD;
-    constexpr int half = HD / 2;
-    if (tid < half) {
-      float a = kn[tid], b = kn[tid + half];
-      float lo = a, hi = b;
-      if (p.rope) {
-        const float c = p.rope_cos[(size_t)se.new_pos * half + tid];
-        const float s = p.rope_sin[(size_t)se.new_pos * half + tid];
-        lo = rope_lo(a, b, c, s);
-        hi = rope_hi(a, b, c, s);
-      }
-      p.k_pool[row * HD + tid] = __half_as_ushort(__float2half_rn(lo));
-      p.k_pool[row * HD + tid + half] = __half_as_ushort(__float2half_rn(hi));
-    }
-    p.v_pool[row * HD + tid] = __half_as_ushort(__float2half_rn(vn[tid]));
-    fence_proxy_async();  // generic-proxy stores above -> visible to this CTA's TMA reads
   }
   __syncthreads();
 
-  // Consumer state, declared at CTA scope so it survives the role split.
-  float acc[C::kNTiles][4];
-  float m_lo = -INFINITY, m_hi = -INFINITY;
-  float l_lo = 0.f, l_hi = 0.f;
-  const int g = lane >> 2;  // mma group id: head row g (and g + 8), token row
-  const int c = lane & 3;   // thread in group
-
-  // ---- producer: TMA ring ----------------------------------------------
   if (warp == kConsumerWarps) {
+    // ---- producer warp: fused append (all lanes) + TMA ring (lane 0) --------
     if (lane == 0) {
-      const uint64_t policy = policy_evict_first();
-      bool ok = true;
-      for (int s = 0; s < n_st && ok; ++s) {
-        const int slot = s % R;
-        if (s >= R) {
-          if (!mbar_wait(&empty[slot], ((s / R) - 1) & 1)) {
+      prefetch_tmap(&p.tmap_k);
+      prefetch_tmap(&p.tmap_v);
+    }
+    const uint64_t policy = policy_evict_first();
+    uint32_t sidx = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const Work w = work_of(p, it);
+      const SeqEntry se = p.seqs[w.si];
+      const int layer = p.layer_begin + w.layer_local;
+      const int new_idx = se.len - 1;
+      if (se.new_pos >= 0 && p.k_new != nullptr && new_idx >= w.t0 && new_idx < w.t1) {
+        // RoPE(k) + f16 round-to-nearest-even append of the new token, written
+        // before the TMA that reads it (proxy fence below).
+        const int page = p.page_table[se.slot * p.max_pages_per_seq + new_idx / p.page_tokens];
+        const size_t row = ((size_t)(layer * p.num_pages + page) * p.kv_heads + w.kvh) * p.page_tokens +
+                           (new_idx % p.page_tokens);
+        const size_t src = ((size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * p.kv_heads + w.kvh) * HD;
+        const float* kn = p.k_new + src;
+        const float* vn = p.v_new + src;
+        constexpr int half = HD / 2;
+        for (int i = lane; i < half; i += 32) {
+          const float a = kn[i], b = kn[i + half];
+          float lo = a, hi = b;
+          if (p.rope) {
+            const float c = p.rope_cos[(size_t)se.new_pos * half + i];
+            const float s = p.rope_sin[(size_t)se.new_pos * half + i];
+            lo = rope_lo(a, b, c, s);
+            hi = rope_hi(a, b, c, s);
+          }
+          p.k_pool[row * HD + i] = __half_as_ushort(__float2half_rn(lo));
+          p.k_pool[row * HD + i + half] = __half_as_ushort(__float2half_rn(hi));
+        }
+        for (int i = lane; i < HD; i += 32) p.v_pool[row * HD + i] = __half_as_ushort(__float2half_rn(vn[i]));
+        fence_proxy_async();
+        __syncwarp();
+      }
+      for (int s = 0; s < w.n_st; ++s, ++sidx) {
+        const int slot = sidx % R;
+        if (lane == 0) {
+          if (sidx >= (uint32_t)R && !mbar_wait(&empty[slot], ((sidx / R) - 1) & 1)) {
             set_error(p.error, 1);
             ok = false;
-            break;
+          }
+          if (ok) {
+            const int tok = w.t0 + s * kStageTokens;
+            const int page = p.page_table[se.slot * p.max_pages_per_seq + tok / p.page_tokens];
+            const int row = ((layer * p.num_pages + page) * p.kv_heads + w.kvh) * p.page_tokens + (tok % p.page_tokens);
+            unsigned char* st = smem + slot * C::kStageBytes;
+            mbar_arrive_expect_tx(&full[slot], C::kStageBytes);
+#pragma unroll
+            for (int b = 0; b < C::kBoxes; ++b) {
+              tma_load_2d_hint(st + b * kBoxBytes, &p.tmap_k, &full[slot], b * 64, row, policy);
+              tma_load_2d_hint(st + (C::kBoxes + b) * kBoxBytes, &p.tmap_v, &full[slot], b * 64, row, policy);
+            }
           }
         }
-        const int tok = t0 + s * kStageTokens;
-        const int page = p.page_table[se.slot * p.max_pages_per_seq + tok / p.page_tokens];
-        const int row = ((layer * p.num_pages + page) * p.kv_heads + kvh) * p.page_tokens + (tok % p.page_tokens);
-        unsigned char* st = smem + slot * C::kStageBytes;
-        mbar_arrive_expect_tx(&full[slot], C::kStageBytes);
-#pragma unroll
-        for (int b = 0; b < C::kBoxes; ++b) {
-          tma_load_2d_hint(st + b * kBoxBytes, &p.tmap_k, &full[slot], b * 64, row, policy);
-          tma_load_2d_hint(st + (C::kBoxes + b) * kBoxBytes, &p.tmap_v, &full[slot], b * 64, row, policy);
-        }
-      }
-      // Never leave the CTA with copies in flight: wait for the last stages.
-      for (int s = max(0, n_st - R); s < n_st; ++s) {
-        if (!mbar_wait(&full[s % R], (s / R) & 1)) set_error(p.error, 2);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
       }
     }
-  } else {
-    // ---- consumers ------------------------------------------------------
-    const bool row_lo_valid = g < G;
-    const bool row_hi_valid = g + 8 < G;
+    // Never leave the CTA with copies in flight: the last stages have landed.
+    if (lane == 0) {
+      for (uint32_t k = sidx > (uint32_t)R ? sidx - R : 0; k < sidx; ++k) {
+        if (!mbar_wait(&full[k % R], (k / R) & 1)) set_error(p.error, 2);
+      }
+    }
+    return;
+  }
 
-    // Query fragments: a[ks][0..3] for k-step ks (rows g / g+8).
-    uint32_t qa[C::kKSteps][4];
+  // ---- consumer warps 0-3 ------------------------------------------------
+  const int g = lane >> 2;  // mma group id: head rows g and g+8, token rows
+  const int c = lane & 3;   // thread in group
+  const float sl = p.scale_log2;
+  constexpr int half = HD / 2;
+  uint32_t sidx = 0;
+  bool failed = false;
+  for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+    const Work w = work_of(p, it);
+    const SeqEntry se = p.seqs[w.si];
+    const size_t qrow0 = (size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * H + w.kvh * G;
+
+    // 1) rotated q rows of the group -> shared memory (coalesced loads)
     {
-      const float* qbase = p.q + ((size_t)(layer_local * p.seq_total + p.seq_base + si) * H + kvh * G) * HD;
-      constexpr int half = HD / 2;
+      const float* qg = p.q + qrow0 * HD;
       const float* crow = p.rope_cos + (size_t)se.q_pos * half;
       const float* srow = p.rope_sin + (size_t)se.q_pos * half;
-#pragma unroll
-      for (int j = 0; j < C::kChunksPerThread; ++j) {
-        int box;
-        const int ch = k_chunk_of<HD>(c, j, &box);
-        const int d0 = box * 64 + ch * 8;
-        float v[2][8];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const int row = g + 8 * r;
-          const bool valid = r == 0 ? row_lo_valid : row_hi_valid;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int d = d0 + e;
-            float x = 0.f;
-            if (valid) {
-              const float* qr = qbase + (size_t)row * HD;
-              if (p.rope) {
-                if (d < half) {
-                  x = rope_lo(qr[d], qr[d + half], crow[d], srow[d]);
-                } else {
-                  x = rope_hi(qr[d - half], qr[d], crow[d - half], srow[d - half]);
-                }
-              } else {
-                x = qr[d];
-              }
-            }
-            v[r][e] = x;
+      for (int i = tid; i < 16 * half; i += kConsumerWarps * 32) {
+        const int r = i / half, d = i - r * half;
+        float lo = 0.f, hi = 0.f;
+        if (r < G) {
+          const float a = qg[r * HD + d], b = qg[r * HD + d + half];
+          if (p.rope) {
+            lo = rope_lo(a, b, crow[d], srow[d]);
+            hi = rope_hi(a, b, crow[d], srow[d]);
+          } else {
+            lo = a;
+            hi = b;
           }
         }
-        // k-step 2j uses dims d0+0..3, k-step 2j+1 uses d0+4..7
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          qa[2 * j + h][0] = pack_half2(v[0][4 * h + 0], v[0][4 * h + 1]);
-          qa[2 * j + h][1] = pack_half2(v[1][4 * h + 0], v[1][4 * h + 1]);
-          qa[2 * j + h][2] = pack_half2(v[0][4 * h + 2], v[0][4 * h + 3]);
-          qa[2 * j + h][3] = pack_half2(v[1][4 * h + 2], v[1][4 * h + 3]);
-        }
+        sm_q[r * HD + d] = lo;
+        sm_q[r * HD + d + half] = hi;
       }
     }
+    consumer_sync();
+    uint32_t qa[C::kKSteps][4];
+#pragma unroll
+    for (int j = 0; j < C::kChunksPerThread; ++j) {
+      int box;
+      const int ch = k_chunk_of<HD>(c, j, &box);
+      const int d0 = box * 64 + ch * 8;
+      const float4 lo0 = *reinterpret_cast<const float4*>(sm_q + g * HD + d0);
+      const float4 lo1 = *reinterpret_cast<const float4*>(sm_q + g * HD + d0 + 4);
+      const float4 hi0 = *reinterpret_cast<const float4*>(sm_q + (g + 8) * HD + d0);
+      const float4 hi1 = *reinterpret_cast<const float4*>(sm_q + (g + 8) * HD + d0 + 4);
+      // k-step 2j uses dims d0+0..3, k-step 2j+1 uses d0+4..7
+      qa[2 * j][0] = pack_half2(lo0.x, lo0.y);
+      qa[2 * j][1] = pack_half2(hi0.x, hi0.y);
+      qa[2 * j][2] = pack_half2(lo0.z, lo0.w);
+      qa[2 * j][3] = pack_half2(hi0.z, hi0.w);
+      qa[2 * j + 1][0] = pack_half2(lo1.x, lo1.y);
+      qa[2 * j + 1][1] = pack_half2(hi1.x, hi1.y);
+      qa[2 * j + 1][2] = pack_half2(lo1.z, lo1.w);
+      qa[2 * j + 1][3] = pack_half2(hi1.z, hi1.w);
+    }
 
+    // 2) stream the chunk's stages
+    float acc[C::kNTiles][4];
 #pragma unroll
     for (int i = 0; i < C::kNTiles; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-    const float sl = p.scale_log2;
-    bool failed = false;
-
-    for (int s = 0; s < n_st; ++s) {
-      const int slot = s % R;
-      if (!mbar_wait(&full[slot], (s / R) & 1)) {
+    float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+    for (int s = 0; s < w.n_st; ++s, ++sidx) {
+      const int slot = sidx % R;
+      if (!failed && !mbar_wait(&full[slot], (sidx / R) & 1)) {
         set_error(p.error, 3);
         failed = true;
-        break;
       }
-      const int tok_base = t0 + s * kStageTokens + 16 * warp;
-      if (tok_base < t1) {
+      const int tok_base = w.t0 + s * kStageTokens + 16 * warp;
+      if (!failed && tok_base < w.t1) {
         const uint32_t st = smem_u32(smem + slot * C::kStageBytes);
-        // ---- S = Q K^T (rows: heads, cols: 8 tokens per mma) ----
         float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
-          const int r = 16 * warp + g + 8 * t;  // token row in the stage
+          const int r = 16 * warp + g + 8 * t;
 #pragma unroll
           for (int j = 0; j < C::kChunksPerThread; ++j) {
             int box;
@@ -248,7 +289,6 @@ __global__ void __launch_bounds__(kThreads, 2) decode_f16_kernel(const __grid_co
             mma_16816(sacc[t], qa[2 * j + 1], kv.z, kv.w);
           }
         }
-        // ---- online softmax (log2 domain) ----
         float sc[2][4];
         float mx_lo = -INFINITY, mx_hi = -INFINITY;
 #pragma unroll
@@ -256,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_f16_kernel(const __grid_co
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int tok = tok_base + 8 * t + 2 * c + (e & 1);
-            const float v = tok < t1 ? sacc[t][e] * sl : -INFINITY;
+            const float v = tok < w.t1 ? sacc[t][e] * sl : -INFINITY;
             sc[t][e] = v;
             if (e < 2) mx_lo = fmaxf(mx_lo, v); else mx_hi = fmaxf(mx_hi, v);
           }
@@ -285,19 +325,20 @@ __global__ void __launch_bounds__(kThreads, 2) decode_f16_kernel(const __grid_co
         }
         l_lo = l_lo * al_lo + ps_lo;
         l_hi = l_hi * al_hi + ps_hi;
+        if (__any_sync(0xffffffffu, al_lo != 1.f || al_hi != 1.f)) {
 #pragma unroll
-        for (int i = 0; i < C::kNTiles; ++i) {
-          acc[i][0] *= al_lo;
-          acc[i][1] *= al_lo;
-          acc[i][2] *= al_hi;
-          acc[i][3] *= al_hi;
+          for (int i = 0; i < C::kNTiles; ++i) {
+            acc[i][0] *= al_lo;
+            acc[i][1] *= al_lo;
+            acc[i][2] *= al_hi;
+            acc[i][3] *= al_hi;
+          }
         }
         uint32_t pa[4];
         pa[0] = pack_half2(sc[0][0], sc[0][1]);
         pa[1] = pack_half2(sc[0][2], sc[0][3]);
         pa[2] = pack_half2(sc[1][0], sc[1][1]);
         pa[3] = pack_half2(sc[1][2], sc[1][3]);
-        // ---- O += P V ----
         const int rv0 = 16 * warp + 2 * c;
 #pragma unroll
         for (int b = 0; b < C::kBoxes; ++b) {
@@ -322,18 +363,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_f16_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    (void)failed;
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
 
-  }
-  __syncthreads();  // all stages consumed and every TMA copy complete: the ring is free
-  if (warp < kConsumerWarps) {
-    float* sm_m = reinterpret_cast<float*>(smem);             // [4][16]
-    float* sm_l = sm_m + kConsumerWarps * 16;                  // [4][16]
-    float* sm_o = sm_l + kConsumerWarps * 16;                  // [4][16][HD]
+    // 3) merge the 4 warps' states: one record per query head of the group
     if (c == 0) {
       sm_m[warp * 16 + g] = m_lo;
       sm_m[warp * 16 + g + 8] = m_hi;
@@ -352,97 +387,93 @@ __global__ void __launch_bounds__(kThreads, 2) decode_f16_kernel(const __grid_co
       o_hi[d0] = acc[i][2];
       o_hi[d1] = acc[i][3];
     }
-  }
-  __syncthreads();  // per-warp states in shared memory
-
-  // ---- merge the 4 warps: one record per query head of the group ----------
-  const float* sm_m = reinterpret_cast<const float*>(smem);
-  const float* sm_l = sm_m + kConsumerWarps * 16;
-  const float* sm_o = sm_l + kConsumerWarps * 16;
-  const bool single = se.n_chunks == 1;
-  const size_t out_row0 = (size_t)(layer_local * p.seq_total + p.seq_base + si) * H + kvh * G;
-  const int rec = HD + 2;
-  float* part_base = p.partials + ((size_t)(layer_local * p.kv_heads + kvh) * p.total_chunks + cx) * G * rec;
-  for (int it = tid; it < G * HD; it += kThreads) {
-    const int row = it / HD, d = it % HD;
-    float M = -INFINITY;
+    consumer_sync();
+    const bool single = se.n_chunks == 1;
+    const int rec = HD + 2;
+    float* part = p.partials + ((size_t)(w.layer_local * p.kv_heads + w.kvh) * p.total_chunks + w.cx) * G * rec;
+    for (int i = tid; i < G * HD; i += kConsumerWarps * 32) {
+      const int row = i / HD, d = i - row * HD;
+      float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm_m[w * 16 + row]);
-    float L = 0.f, O = 0.f;
+      for (int ww = 0; ww < kConsumerWarps; ++ww) M = fmaxf(M, sm_m[ww * 16 + row]);
+      float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) {
-      const float mw = sm_m[w * 16 + row];
-      const float wt = mw == -INFINITY ? 0.f : ex2(mw - M);
-      L += sm_l[w * 16 + row] * wt;
-      O += sm_o[((size_t)w * 16 + row) * HD + d] * wt;
-    }
-    if (single) {
-      if (p.partial_out) {
-        float* r = p.out + (out_row0 + row) * rec;
+      for (int ww = 0; ww < kConsumerWarps; ++ww) {
+        const float mw = sm_m[ww * 16 + row];
+        const float wt = mw == -INFINITY ? 0.f : ex2(mw - M);
+        L += sm_l[ww * 16 + row] * wt;
+        O += sm_o[((size_t)ww * 16 + row) * HD + d] * wt;
+      }
+      if (single) {
+        if (p.partial_out) {
+          float* r = p.out + (qrow0 + row) * rec;
+          r[d] = O;
+          if (d == 0) { r[HD] = M; r[HD + 1] = L; }
+        } else {
+          p.out[(qrow0 + row) * HD + d] = O / L;
+        }
+      } else {
+        float* r = part + (size_t)row * rec;
         r[d] = O;
         if (d == 0) { r[HD] = M; r[HD + 1] = L; }
-      } else {
-        p.out[(out_row0 + row) * HD + d] = O / L;
       }
-    } else {
-      float* r = part_base + (size_t)row * rec;
-      r[d] = O;
-      if (d == 0) { r[HD] = M; r[HD + 1] = L; }
     }
-  }
-  if (single) return;
-
-  // ---- split-K: the last CTA of this (layer, seq, kv head) merges ---------
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    uint32_t* ctr = p.counters + (size_t)(layer_local * p.kv_heads + kvh) * p.n_seqs + si;
-    const uint32_t ticket = atomicAdd(ctr, 1u);
-    const int last = ticket == (uint32_t)(se.n_chunks - 1);
-    if (last) *ctr = 0u;  // every other CTA of the group has already taken its ticket
-    flags[0] = last;
-  }
-  __syncthreads();
-  if (!flags[0]) return;
-  __threadfence();
-  const float* grp = p.partials + ((size_t)(layer_local * p.kv_heads + kvh) * p.total_chunks + se.chunk_begin) * G * rec;
-  // The warp-merge area is dead here (its results are in `partials`); reuse the ring.
-  if (4096 + 2 * se.n_chunks * G + 32 > R * C::kStageBytes / 4) {
-    set_error(p.error, 4);  // host caps n_chunks so this cannot happen
-    return;
-  }
-  float* sm_cm = reinterpret_cast<float*>(smem) + 4096;   // [n_chunks][G] maxima
-  float* sm_cl = sm_cm + se.n_chunks * G;
-  float* sm_M = sm_cl + se.n_chunks * G;                  // [G]
-  float* sm_L = sm_M + 16;                                // [G]
-  for (int i = tid; i < se.n_chunks * G; i += kThreads) {
-    sm_cm[i] = __ldcg(grp + (size_t)i * rec + HD);
-    sm_cl[i] = __ldcg(grp + (size_t)i * rec + HD + 1);
-  }
-  __syncthreads();
-  if (tid < G) {
-    float M = -INFINITY;
-    for (int k = 0; k < se.n_chunks; ++k) M = fmaxf(M, sm_cm[k * G + tid]);
-    float L = 0.f;
-    for (int k = 0; k < se.n_chunks; ++k) L += sm_cl[k * G + tid] * ex2(sm_cm[k * G + tid] - M);
-    sm_M[tid] = M;
-    sm_L[tid] = L;
-  }
-  __syncthreads();
-  for (int it = tid; it < G * HD; it += kThreads) {
-    const int row = it / HD, d = it % HD;
-    const float M = sm_M[row];
-    float O = 0.f;
-    for (int k = 0; k < se.n_chunks; ++k) {
-      O += __ldcg(grp + ((size_t)k * G + row) * rec + d) * ex2(sm_cm[k * G + row] - M);
+    if (!single) {
+      // 4) split-K: the last CTA to finish a (layer, seq, kv head) merges its chunks
+      __threadfence();
+      consumer_sync();
+      if (tid == 0) {
+        uint32_t* ctr = p.counters + (size_t)(w.layer_local * p.kv_heads + w.kvh) * p.n_seqs + w.si;
+        const uint32_t ticket = atomicAdd(ctr, 1u);
+        const int last = ticket == (uint32_t)(se.n_chunks - 1);
+        if (last) *ctr = 0u;  // every chunk of the group has taken its ticket
+        flags[0] = last;
+      }
+      consumer_sync();
+      if (flags[0]) {
+        __threadfence();
+        const float* grp =
+            p.partials + ((size_t)(w.layer_local * p.kv_heads + w.kvh) * p.total_chunks + se.chunk_begin) * G * rec;
+        float* sm_cm = sm_o;                     // [n_chunks][G] maxima (merge area is free now)
+        float* sm_cl = sm_cm + se.n_chunks * G;  // [n_chunks][G] sums
+        float* sm_M = sm_cl + se.n_chunks * G;   // [16]
+        float* sm_L = sm_M + 16;                 // [16]
+        if (2 * se.n_chunks * G > C::kMaxCombineFloats) {
+          set_error(p.error, 4);  // the host caps n_chunks so this cannot happen
+        } else {
+          for (int i = tid; i < se.n_chunks * G; i += kConsumerWarps * 32) {
+            sm_cm[i] = __ldcg(grp + (size_t)i * rec + HD);
+            sm_cl[i] = __ldcg(grp + (size_t)i * rec + HD + 1);
+          }
+          consumer_sync();
+          if (tid < G) {
+            float M = -INFINITY;
+            for (int k = 0; k < se.n_chunks; ++k) M = fmaxf(M, sm_cm[k * G + tid]);
+            float L = 0.f;
+            for (int k = 0; k < se.n_chunks; ++k) L += sm_cl[k * G + tid] * ex2(sm_cm[k * G + tid] - M);
+            sm_M[tid] = M;
+            sm_L[tid] = L;
+          }
+          consumer_sync();
+          for (int i = tid; i < G * HD; i += kConsumerWarps * 32) {
+            const int row = i / HD, d = i - row * HD;
+            const float M = sm_M[row];
+            float O = 0.f;
+            for (int k = 0; k < se.n_chunks; ++k) {
+              O += __ldcg(grp + ((size_t)k * G + row) * rec + d) * ex2(sm_cm[k * G + row] - M);
+            }
+            if (p.partial_out) {
+              float* r = p.out + (qrow0 + row) * rec;
+              r[d] = O;
+              if (d == 0) { r[HD] = M; r[HD + 1] = sm_L[row]; }
+            } else {
+              p.out[(qrow0 + row) * HD + d] = O / sm_L[row];
+            }
+          }
+        }
+      }
     }
-    if (p.partial_out) {
-      float* r = p.out + (out_row0 + row) * rec;
-      r[d] = O;
-      if (d == 0) { r[HD] = M; r[HD + 1] = sm_L[row]; }
-    } else {
-      p.out[(out_row0 + row) * HD + d] = O / sm_L[row];
-    }
+    consumer_sync();  // merge / q areas are reused by the next item
   }
 }
 
@@ -545,18 +576,23 @@ __global__ void merge_partials_kernel(const float* __restrict__ partials, int n_
   }
 }
 
-template <int HD, int R>
+template <int HD>
 cudaError_t launch_decode_impl(const DecodeParams& p, cudaStream_t s) {
   using C = DecodeCfg<HD>;
-  const size_t smem = 1024 + (size_t)R * C::kStageBytes + 2 * R * sizeof(uint64_t) + 16;
-  static bool configured = false;  // per-process attribute; set once per instantiation
+  static int sms = 0;  // per-process; one device type
+  static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_f16_kernel<HD, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(decode_f16_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
     if (e != cudaSuccess) return e;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     configured = true;
   }
-  dim3 grid(p.total_chunks, p.n_layers * p.kv_heads);
-  decode_f16_kernel<HD, R><<<grid, kThreads, smem, s>>>(p);
+  const long long items = (long long)p.n_layers * p.kv_heads * p.total_chunks;
+  const int grid = (int)(items < sms ? items : sms);
+  decode_f16_kernel<HD><<<grid, kThreads, C::kSmemBytes, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -564,8 +600,8 @@ cudaError_t launch_decode_impl(const DecodeParams& p, cudaStream_t s) {
 
 cudaError_t launch_decode_f16(const DecodeParams& p, int head_dim, int stages, cudaStream_t s) {
   (void)stages;
-  if (head_dim == 128) return launch_decode_impl<128, 3>(p, s);
-  if (head_dim == 64) return launch_decode_impl<64, 4>(p, s);
+  if (head_dim == 128) return launch_decode_impl<128>(p, s);
+  if (head_dim == 64) return launch_decode_impl<64>(p, s);
   return cudaErrorInvalidValue;
 }
 
@@ -639,8 +675,7 @@ extern "C" __attribute__((visibility("default"))) te_status te_attention_decode_
   const size_t rec_bytes = kv_heads * G * (head_dim + 2) * sizeof(float);
   const size_t fit_chunks = kNoAllocPartialBytes / rec_bytes;
   if (fit_chunks == 0) return TE_STATUS_UNSUPPORTED;
-  const size_t stage_floats = (head_dim == 128 ? 3 * 32768 : 4 * 16384) / 4;
-  const size_t smem_chunks = (stage_floats - 4096 - 32) / (2 * G);
+  const size_t smem_chunks = decode_max_chunks((int)head_dim, (int)G);
   const size_t max_chunks = std::min(fit_chunks, smem_chunks);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return TE_STATUS_RUNTIME_ERROR;

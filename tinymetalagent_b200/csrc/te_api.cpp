@@ -2,6 +2,7 @@
 // status codes, the device-resident engine and paged f16 KV cache, work
 // decomposition for the kernels, and the two drop-in CPU-API functions.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -638,8 +639,7 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
     chunk = total_tok / ((size_t)8 * e->sm_count);
     chunk = std::min<size_t>(std::max<size_t>(chunk, 64), 4096);
   }
-  const size_t stage_floats = (hd == 128 ? 3 * 32768 : 4 * 16384) / 4;
-  const size_t max_chunks = (stage_floats - 4096 - 32) / (2 * G);
+  const size_t max_chunks = decode_max_chunks((int)hd, (int)G);
   chunk = std::max(chunk, (max_len + max_chunks - 1) / max_chunks);
   chunk = (chunk + kStageTokens - 1) / kStageTokens * kStageTokens;
 
@@ -756,8 +756,129 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
       layer_begin + n_layers > c->d.layers || seq >= c->d.max_seqs) {
     return TE_STATUS_INVALID_ARGUMENT;
   }
-  (void)flags;
-  return fail(c->eng, TE_STATUS_UNSUPPORTED, "prefill kernel not built yet");
+  te_attn_engine* e = c->eng;
+  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | TE_ATTN_HOST_BUFFERS | TE_ATTN_NO_ROPE)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for te_attention_prefill");
+  }
+  const size_t hkv = c->d.kv_heads, hd = c->d.head_dim;
+  if (heads % hkv != 0) return fail(e, TE_STATUS_INVALID_ARGUMENT, "heads must be a multiple of kv_heads");
+  if (hd != 128) return fail(e, TE_STATUS_UNSUPPORTED, "prefill kernel is built for head_dim 128");
+  const size_t q_offset = (size_t)c->len[seq];
+  const size_t total = q_offset + n_tokens;
+  if (total > c->d.max_tokens_per_seq) return fail(e, TE_STATUS_INVALID_ARGUMENT, "sequence would exceed max_tokens_per_seq");
+  if ((uint64_t)(c->offset[seq] + total) > c->d.max_position) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "RoPE position beyond max_position");
+  }
+  const size_t n_pad = (n_tokens + 127) / 128 * 128;
+  const size_t items = n_layers * heads * (n_pad / 128);
+  const size_t qh_rows = n_layers * heads * n_pad;
+  if (items > (size_t)INT32_MAX || qh_rows >= (1ull << 31)) return fail(e, TE_STATUS_UNSUPPORTED, "prefill too large");
+  DeviceGuard dg(e->device);
+  te_status st = ensure_pages(c, seq, total);
+  if (st != TE_STATUS_OK) return st;
+
+  const size_t in_el = (flags & TE_ATTN_INPUT_F16) ? 2 : 4;
+  const size_t q_bytes = n_layers * n_tokens * heads * hd * in_el;
+  const size_t kv_bytes = n_layers * n_tokens * hkv * hd * in_el;
+  const size_t out_bytes = n_layers * n_tokens * heads * hd * sizeof(float);
+  const void* dq = q;
+  const void* dk = k;
+  const void* dv = v;
+  float* dout = out;
+  cudaError_t err;
+  if (flags & TE_ATTN_HOST_BUFFERS) {
+    err = grow(e, &e->io, &e->io_bytes, q_bytes + 2 * kv_bytes + out_bytes + 256, false);
+    if (err != cudaSuccess) return cuda_fail(e, err, "staging allocation");
+    char* base = reinterpret_cast<char*>(e->io);
+    char* sq = base;
+    char* sk = sq + q_bytes;
+    char* sv = sk + kv_bytes;
+    dout = reinterpret_cast<float*>(sv + kv_bytes);
+    err = cudaMemcpyAsync(sq, q, q_bytes, cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(sk, k, kv_bytes, cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(sv, v, kv_bytes, cudaMemcpyHostToDevice, e->stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "input upload");
+    dq = sq;
+    dk = sk;
+    dv = sv;
+  }
+
+  // 1) RoPE(k) + f16 append of the new tokens for every layer
+  AppendParams a{};
+  a.k = dk;
+  a.v = dv;
+  a.k_pool = c->k_pool;
+  a.v_pool = c->v_pool;
+  a.page_row = c->d_page_table + seq * c->pages_per_seq;
+  a.rope_cos = c->d_cos;
+  a.rope_sin = c->d_sin;
+  a.input_f16 = (flags & TE_ATTN_INPUT_F16) ? 1 : 0;
+  a.rope = (flags & TE_ATTN_NO_ROPE) ? 0 : 1;
+  a.n_layers = (int32_t)n_layers;
+  a.layer_begin = (int32_t)layer_begin;
+  a.n_tokens = (int32_t)n_tokens;
+  a.first_index = (int32_t)q_offset;
+  a.first_pos = (int32_t)(c->offset[seq] + q_offset);
+  a.kv_heads = (int32_t)hkv;
+  a.head_dim = (int32_t)hd;
+  a.num_pages = (int32_t)c->d.total_pages;
+  a.page_tokens = (int32_t)c->d.page_tokens;
+  err = launch_append_rope(a, e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "append kernel launch");
+  e->launches++;
+
+  // 2) rotated f16 queries, head-major and padded to 128-row tiles
+  err = grow(e, &e->qh, &e->qh_bytes, qh_rows * hd * sizeof(__half), false);
+  if (err != cudaSuccess) return cuda_fail(e, err, "prefill query scratch allocation");
+  QPrepParams qp{};
+  qp.q = dq;
+  qp.qh = reinterpret_cast<__half*>(e->qh);
+  qp.rope_cos = c->d_cos;
+  qp.rope_sin = c->d_sin;
+  qp.input_f16 = a.input_f16;
+  qp.rope = a.rope;
+  qp.n_layers = (int32_t)n_layers;
+  qp.n_tokens = (int32_t)n_tokens;
+  qp.n_tokens_padded = (int32_t)n_pad;
+  qp.heads = (int32_t)heads;
+  qp.head_dim = (int32_t)hd;
+  qp.first_pos = a.first_pos;
+  err = launch_q_prep(qp, e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "query preparation launch");
+  e->launches++;
+
+  // 3) causal flash attention on tcgen05
+  PrefillParams p;
+  std::memset(&p, 0, sizeof(p));
+  if (!make_tmap_f16(&p.tmap_q, e->qh, qh_rows, hd, 64)) return fail(e, TE_STATUS_RUNTIME_ERROR, "query tensor map");
+  p.tmap_k = c->tmap_k;
+  p.tmap_v = c->tmap_v;
+  p.page_table_row = c->d_page_table + seq * c->pages_per_seq;
+  p.out = dout;
+  p.error = e->d_error;
+  p.n_layers = (int32_t)n_layers;
+  p.layer_begin = (int32_t)layer_begin;
+  p.heads = (int32_t)heads;
+  p.kv_heads = (int32_t)hkv;
+  p.n_tokens = (int32_t)n_tokens;
+  p.n_tokens_padded = (int32_t)n_pad;
+  p.q_offset = (int32_t)q_offset;
+  p.num_pages = (int32_t)c->d.total_pages;
+  p.page_tokens = (int32_t)c->d.page_tokens;
+  p.n_pages_mapped = (int32_t)((total + c->d.page_tokens - 1) / c->d.page_tokens);
+  p.n_items = (int32_t)items;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hd));
+  err = launch_prefill_tc(p, e->sm_count, e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "prefill kernel launch");
+  e->launches++;
+
+  if (flags & TE_ATTN_HOST_BUFFERS) {
+    err = cudaMemcpyAsync(out, dout, out_bytes, cudaMemcpyDeviceToHost, e->stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "output download");
+  }
+  if (flags & TE_ATTN_ADVANCE) c->len[seq] = (int64_t)total;
+  return TE_STATUS_OK;
 }
 
 }  // extern "C"

@@ -27,6 +27,13 @@ struct SeqEntry {
 };
 
 constexpr int kMaxParamSeqs = 64;  // sequences per decode launch
+
+// Largest split-K chunk count per (layer, sequence, kv head) that the decode
+// kernel's in-shared-memory combine table holds (per-chunk m and l of every
+// query head of the group, inside the 4-warp merge area).
+inline size_t decode_max_chunks(int head_dim, int group) {
+  return ((size_t)4 * 16 * head_dim - 32) / (2 * (size_t)group);
+}
 constexpr int kStageTokens = 64;   // tokens per TMA stage
 
 struct DecodeParams {
@@ -115,10 +122,10 @@ struct QPrepParams {
 cudaError_t launch_q_prep(const QPrepParams& p, cudaStream_t s);
 
 struct PrefillParams {
-  CUtensorMap tmap_q;   // [n_layers*heads*n_tokens_padded][hd] f16
-  CUtensorMap tmap_k;   // K pool view
+  CUtensorMap tmap_q;   // [n_layers*heads*n_tokens_padded][hd] f16, box 64x64, 128B swizzle
+  CUtensorMap tmap_k;   // K pool view (as for decode)
   CUtensorMap tmap_v;
-  const int32_t* page_table_row;
+  const int32_t* page_table_row;  // page table row of the sequence
   float* out;           // [n_layers][n_tokens][heads][hd]
   int* error;
   int32_t n_layers;
@@ -126,16 +133,14 @@ struct PrefillParams {
   int32_t heads;
   int32_t kv_heads;
   int32_t n_tokens;
-  int32_t n_tokens_padded;
-  int32_t q_offset;     // cached tokens before the first new token
-  int32_t num_pages;
+  int32_t n_tokens_padded;  // multiple of 128
+  int32_t q_offset;     // tokens cached before the first new token
+  int32_t num_pages;    // pages per layer in the pool
   int32_t page_tokens;
-  int32_t n_items;      // work items (layer, head, q tile)
-  uint32_t* tile_counter;
+  int32_t n_pages_mapped;  // mapped pages of the sequence (covers q_offset + n_tokens)
+  int32_t n_items;      // work items: n_layers * heads * (n_tokens_padded / 128)
   float scale_log2;
 };
-cudaError_t launch_prefill_tc(const PrefillParams& p, cudaStream_t s);
-cudaError_t launch_prefill_simt(const PrefillParams& p, const __half* qh, const uint16_t* k_pool,
-                                const uint16_t* v_pool, cudaStream_t s);
+cudaError_t launch_prefill_tc(const PrefillParams& p, int sm_count, cudaStream_t s);
 
 }  // namespace te

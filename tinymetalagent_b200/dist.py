@@ -1,0 +1,143 @@
+"""Multi-GPU orchestration of the attention stage: one process per GPU.
+
+Two partitionings, chosen where the work shards naturally (the reference runs
+on a single device; there is no counterpart):
+
+* Sequence sharding (batched decode of independent sequences): each rank owns
+  whole sequences and runs ``te_attention_decode`` on them; no collective on
+  the data path.  ``shard_sequences`` balances total cached tokens per rank.
+* KV-sequence split (one long context): rank r owns a contiguous token range of
+  the sequence; the last rank owns the tail and appends new tokens.  Each rank
+  computes partial softmax records (acc, m, l) over its range with the query
+  rotated at the global position; the records are all-gathered over NCCL and
+  merged by ``te_attention_merge_partials`` (log-sum-exp).
+
+The per-rank compute of ``KVSplitDecoder`` is the engine; tests replace it with
+a CPU stand-in to check the partition/gather/merge protocol on gloo ranks.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional, Sequence
+
+import numpy as np
+
+
+def shard_sequences(lengths: Sequence[int], world: int) -> list[list[int]]:
+    """Greedy longest-first assignment of sequences to ranks, balancing the sum
+    of lengths (the decode work is proportional to cached tokens).  Returns, per
+    rank, the sequence indices in ascending order; deterministic for equal input."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
+    loads = [0] * world
+    out: list[list[int]] = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda k: (loads[k], k))
+        out[r].append(i)
+        loads[r] += int(lengths[i])
+    return [sorted(x) for x in out]
+
+
+def kv_split_ranges(n_tokens: int, world: int) -> list[tuple[int, int]]:
+    """Contiguous [begin, end) token ranges per rank; the remainder goes to the
+    first ranks so the tail rank (which grows by appends) is never the largest."""
+    if n_tokens < world:
+        raise ValueError("fewer tokens than ranks")
+    base, rem = divmod(n_tokens, world)
+    out, b = [], 0
+    for r in range(world):
+        e = b + base + (1 if r < rem else 0)
+        out.append((b, e))
+        b = e
+    return out
+
+
+@dataclass
+class ShardSpec:
+    rank: int
+    world: int
+    begin: int          # global position of this rank's first cached token
+    end: int            # one past its last cached token (before appends)
+    global_len: int     # tokens cached over all ranks (before appends)
+
+    @property
+    def is_tail(self) -> bool:
+        return self.rank == self.world - 1
+
+    @staticmethod
+    def plan(rank: int, world: int, n_tokens: int) -> "ShardSpec":
+        b, e = kv_split_ranges(n_tokens, world)[rank]
+        return ShardSpec(rank, world, b, e, n_tokens)
+
+
+class KVSplitDecoder:
+    """Decode steps of one long sequence split over `world` ranks.
+
+    cache      this rank's KVCache (one sequence slot), holding tokens [begin, end)
+    group      torch.distributed process group (NCCL for GPUs)
+    partial_fn optional stand-in for the engine: (q, k_new, v_new, q_position) -> partial
+               records [n_layers][heads][head_dim + 2] as a torch tensor
+    merge_fn   optional stand-in for te_attention_merge_partials: (gathered [world][rows][hd+2]) -> out
+    """
+
+    def __init__(self, spec: ShardSpec, n_layers: int, heads: int, head_dim: int, cache=None, engine=None,
+                 group=None, partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None,
+                 device=None):
+        self.spec = spec
+        self.n_layers, self.heads, self.head_dim = n_layers, heads, head_dim
+        self.cache, self.engine, self.group = cache, engine, group
+        self.partial_fn = partial_fn
+        self.merge_fn = merge_fn
+        self.device = device
+        self.length = spec.global_len  # global length of the sequence (all ranks agree)
+        import torch
+        rows = n_layers * heads
+        self._part = torch.empty((rows, head_dim + 2), dtype=torch.float32, device=device)
+        # concatenated along dim 0 (the form every backend's all_gather_into_tensor accepts)
+        self._gather_flat = torch.empty((spec.world * rows, head_dim + 2), dtype=torch.float32, device=device)
+        self._gather = self._gather_flat.view(spec.world, rows, head_dim + 2)
+        self._out = torch.empty((n_layers, 1, heads, head_dim), dtype=torch.float32, device=device)
+
+    def _local_partial(self, q, k_new, v_new, q_pos: int):
+        from .runtime import TE_ATTN_ADVANCE, TE_ATTN_PARTIAL
+        if self.partial_fn is not None:
+            self._part.copy_(self.partial_fn(q, k_new, v_new, q_pos).reshape(self._part.shape))
+            return
+        if self.spec.is_tail:
+            self.cache.decode(0, self.n_layers, [0], q, self._part, self.heads, k_new=k_new, v_new=v_new,
+                              flags=TE_ATTN_PARTIAL | TE_ATTN_ADVANCE)
+        else:
+            self.cache.decode(0, self.n_layers, [0], q, self._part, self.heads, q_positions=[q_pos],
+                              flags=TE_ATTN_PARTIAL)
+
+    def step(self, q, k_new, v_new):
+        """One decode step: q [n_layers][1][heads][hd] raw fp32 (every rank gets the
+        same q), k_new/v_new [n_layers][1][kv_heads][hd] (used by the tail rank).
+        Returns the merged attention output [n_layers][1][heads][hd] on every rank."""
+        import torch.distributed as dist
+        q_pos = self.length  # global position of the new token
+        self._local_partial(q, k_new, v_new, q_pos)
+        if self.spec.world > 1:
+            dist.all_gather_into_tensor(self._gather_flat, self._part, group=self.group)
+        else:
+            self._gather[0].copy_(self._part)
+        if self.merge_fn is not None:
+            self._out.copy_(self.merge_fn(self._gather).reshape(self._out.shape))
+        else:
+            self.engine.merge_partials(self._gather, self.spec.world, self.n_layers * self.heads, self.head_dim,
+                                       self._out)
+        self.length += 1
+        return self._out
+
+
+def merge_partials_numpy(parts: np.ndarray) -> np.ndarray:
+    """Log-sum-exp merge of partial records [parts][rows][hd+2] (m, l in log2 units);
+    used by the host-side tests of the split protocol."""
+    m = parts[..., -2]
+    l = parts[..., -1]
+    acc = parts[..., :-2]
+    mx = np.max(np.where(l > 0, m, -np.inf), axis=0)
+    w = np.where(l > 0, np.exp2(m - mx), 0.0)
+    L = np.sum(l * w, axis=0)
+    return np.sum(acc * w[..., None], axis=0) / L[..., None]
