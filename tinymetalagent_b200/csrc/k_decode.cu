@@ -35,28 +35,41 @@ namespace te {
 namespace {
 
 constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kThreads = (kConsumerWarps + 2) * 32;  // + producer warp + helper warp
 constexpr int kBoxBytes = kStageTokens * 64 * 2;  // 64 tokens x 64 dims x f16
 
-template <int HD>
+// Shared-memory plan for head dim HD and GP = 8 or 16 padded query rows per
+// group: a ring of 64-token K/V stages, and double-buffered query, RoPE,
+// fragment and merge areas so one item's prologue/epilogue overlaps the next
+// item's streaming.
+template <int HD, int GP>
 struct DecodeCfg {
   static constexpr int kBoxes = HD / 64;                   // TMA boxes per K (or V) stage
   static constexpr int kStageBytes = 2 * kBoxes * kBoxBytes;
   static constexpr int kKSteps = HD / 16;                  // mma k-steps for q.k
   static constexpr int kChunksPerThread = HD / 32;         // 16-byte chunks of a K row per thread
-  static constexpr int kThreadsPerBox = 8 / kChunksPerThread;
   static constexpr int kNTiles = HD / 8;                   // mma n-tiles for P.V
-  static constexpr int kRing = HD == 128 ? 5 : 8;          // stages in flight per CTA
-  static constexpr int kMergeBytes = kConsumerWarps * 16 * HD * 4;
-  static constexpr int kQBytes = 16 * HD * 4;              // rotated q rows of the group, fp32
+  static constexpr int kRing = HD == 128 ? (GP == 8 ? 5 : 4) : 8;  // K/V stages in flight
+  static constexpr int kRowF = HD + 4;                     // padded row stride (floats): rows 4 banks apart
+  static constexpr int kMergeBytes = kConsumerWarps * GP * kRowF * 4;  // one buffer: per-warp O
+  static constexpr int kQBytes = GP * kRowF * 4;           // one buffer: raw q rows of the group
+  static constexpr int kCSBytes = HD * 4;                  // one buffer: cos row + sin row
+  static constexpr int kFragBytes = kKSteps * 4 * 4 * 32;  // one buffer: f16 query fragments of a warp
+  static constexpr int kMLFloats = 2 * kConsumerWarps * 16;  // one buffer: m[4][16], l[4][16]
   static constexpr int kOffMerge = kRing * kStageBytes;
-  static constexpr int kOffQ = kOffMerge + kMergeBytes;
-  static constexpr int kOffML = kOffQ + kQBytes;           // m[4][16], l[4][16]
-  static constexpr int kOffBar = kOffML + 2 * kConsumerWarps * 16 * 4;
-  static constexpr int kSmemBytes = kOffBar + 2 * kRing * 8 + 64 + 1024;
-  // combine table (per-chunk m and l of one group) lives in the merge area
-  static constexpr int kMaxCombineFloats = kMergeBytes / 4 - 32;
+  static constexpr int kOffQ = kOffMerge + 2 * kMergeBytes;
+  static constexpr int kOffCS = kOffQ + 2 * kQBytes;
+  static constexpr int kOffFrag = kOffCS + 2 * kCSBytes;
+  static constexpr int kOffML = kOffFrag + 2 * kFragBytes;
+  static constexpr int kOffBar = kOffML + 2 * kMLFloats * 4;
+  static constexpr int kNumBars = 2 * kRing + 12;  // full, empty, then [2] each: qfull qempty fready fempty mready mfree
+  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 1024;
 };
+
+// Split-K partial records in scratch: { acc[HD], m, l, pad, pad } so every
+// record starts on a 16-byte boundary.
+template <int HD>
+constexpr int kScratchRec = HD + 4;
 
 __device__ __forceinline__ float rope_lo(float a, float b, float c, float s) {
   return __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
@@ -69,13 +82,10 @@ __device__ __forceinline__ float rope_hi(float a, float b, float c, float s) {
 // thread with quad index c reads for k-step pair j, and the box it lies in.
 template <int HD>
 __device__ __forceinline__ int k_chunk_of(int c, int j, int* box) {
-  using C = DecodeCfg<HD>;
-  *box = c / C::kThreadsPerBox;
-  return C::kChunksPerThread * (c % C::kThreadsPerBox) + ((j + c) % C::kChunksPerThread);
-}
-
-__device__ __forceinline__ void consumer_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+  constexpr int per_thread = HD / 32;
+  constexpr int threads_per_box = 8 / per_thread;
+  *box = c / threads_per_box;
+  return per_thread * (c % threads_per_box) + ((j + c) % per_thread);
 }
 
 // One work item: a chunk of one (layer, sequence, kv head).
@@ -101,21 +111,32 @@ __device__ __forceinline__ Work work_of(const DecodeParams& p, int it) {
   return w;
 }
 
-// Persistent: one CTA per SM loops over work items (round-robin), the TMA
-// ring streams continuously across items.
-template <int HD>
+// Persistent: one CTA per SM loops over work items (round-robin over the grid).
+//   warps 0-3  consumers: each takes 16 tokens of every K/V stage (mma.sync
+//              S = Q K^T, online softmax, O += P V) and parks its state
+//   warp 4     producer: query/RoPE row prefetch, fused append, K/V TMA ring
+//   warp 5     helper: rotates each item's query into f16 fragments ahead of
+//              the consumers, and merges the four consumer states of each
+//              finished item into the output (or a split-K partial record)
+template <int HD, int GP>
 __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_constant__ DecodeParams p) {
-  using C = DecodeCfg<HD>;
+  using C = DecodeCfg<HD, GP>;
   constexpr int R = C::kRing;
+  constexpr int REC = kScratchRec<HD>;
+  constexpr int half = HD / 2;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* empty = full + R;
-  int* flags = reinterpret_cast<int*>(empty + R);
-  float* sm_o = reinterpret_cast<float*>(smem + C::kOffMerge);  // [4][16][HD]
-  float* sm_q = reinterpret_cast<float*>(smem + C::kOffQ);      // [16][HD] rotated q
-  float* sm_m = reinterpret_cast<float*>(smem + C::kOffML);     // [4][16]
-  float* sm_l = sm_m + kConsumerWarps * 16;                     // [4][16]
+  uint64_t* qfull = empty + R;   // [2] producer -> helper
+  uint64_t* qempty = qfull + 2;  // [2] helper -> producer
+  uint64_t* fready = qempty + 2; // [2] helper -> consumers
+  uint64_t* fempty = fready + 2; // [2] consumers -> helper
+  uint64_t* mready = fempty + 2; // [2] consumers -> helper
+  uint64_t* mfree = mready + 2;  // [2] helper -> consumers
+
+  // The split-K combine (a dependent launch) may be scheduled now; it waits for this grid to finish.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -129,23 +150,53 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kConsumerWarps);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&qfull[b], 1);
+      mbar_init(&qempty[b], 1);
+      mbar_init(&fready[b], 1);
+      mbar_init(&fempty[b], kConsumerWarps);
+      mbar_init(&mready[b], kConsumerWarps);
+      mbar_init(&mfree[b], 1);
+    }
     fence_mbarrier_init();
   }
   __syncthreads();
 
   if (warp == kConsumerWarps) {
-    // ---- producer warp: fused append (all lanes) + TMA ring (lane 0) --------
+    // ---- producer warp: q prefetch + fused append + K/V TMA ring -------------
     if (lane == 0) {
       prefetch_tmap(&p.tmap_k);
       prefetch_tmap(&p.tmap_v);
     }
     const uint64_t policy = policy_evict_first();
-    uint32_t sidx = 0;
+    uint32_t sidx = 0, k = 0;
     bool ok = true;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
       const Work w = work_of(p, it);
       const SeqEntry se = p.seqs[w.si];
       const int layer = p.layer_begin + w.layer_local;
+      if (lane == 0) {
+        const int b = k & 1;
+        if (k >= 2 && !mbar_wait(&qempty[b], ((k >> 1) - 1) & 1)) {
+          set_error(p.error, 5);
+          ok = false;
+        }
+        if (ok) {
+          const size_t qrow0 = (size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * H + w.kvh * G;
+          const uint32_t qbytes = (uint32_t)(G * HD * 4);
+          const uint32_t csbytes = p.rope ? (uint32_t)(2 * half * 4) : 0u;
+          mbar_arrive_expect_tx(&qfull[b], qbytes + csbytes);
+          float* qdst = reinterpret_cast<float*>(smem + C::kOffQ + b * C::kQBytes);
+          for (int r = 0; r < G; ++r) bulk_load(qdst + r * C::kRowF, p.q + (qrow0 + r) * HD, HD * 4, &qfull[b]);
+          if (p.rope) {
+            float* cs = reinterpret_cast<float*>(smem + C::kOffCS + b * C::kCSBytes);
+            bulk_load(cs, p.rope_cos + (size_t)se.q_pos * half, half * 4, &qfull[b]);
+            bulk_load(cs + half, p.rope_sin + (size_t)se.q_pos * half, half * 4, &qfull[b]);
+          }
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
       const int new_idx = se.len - 1;
       if (se.new_pos >= 0 && p.k_new != nullptr && new_idx >= w.t0 && new_idx < w.t1) {
         // RoPE(k) + f16 round-to-nearest-even append of the new token, written
@@ -156,15 +207,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         const size_t src = ((size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * p.kv_heads + w.kvh) * HD;
         const float* kn = p.k_new + src;
         const float* vn = p.v_new + src;
-        constexpr int half = HD / 2;
         for (int i = lane; i < half; i += 32) {
-          const float a = kn[i], b = kn[i + half];
-          float lo = a, hi = b;
+          const float a = kn[i], bb = kn[i + half];
+          float lo = a, hi = bb;
           if (p.rope) {
             const float c = p.rope_cos[(size_t)se.new_pos * half + i];
             const float s = p.rope_sin[(size_t)se.new_pos * half + i];
-            lo = rope_lo(a, b, c, s);
-            hi = rope_hi(a, b, c, s);
+            lo = rope_lo(a, bb, c, s);
+            hi = rope_hi(a, bb, c, s);
           }
           p.k_pool[row * HD + i] = __half_as_ushort(__float2half_rn(lo));
           p.k_pool[row * HD + i + half] = __half_as_ushort(__float2half_rn(hi));
@@ -173,23 +223,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         fence_proxy_async();
         __syncwarp();
       }
+      // Page-table entries of this chunk, one per lane, read together up front
+      // (the loop refreshes the batch every 32 pages).
+      const int pg0 = w.t0 / p.page_tokens;
+      int pg_batch = -1;
+      int pg_reg = 0;
       for (int s = 0; s < w.n_st; ++s, ++sidx) {
         const int slot = sidx % R;
+        const int tok = w.t0 + s * kStageTokens;
+        const int rel = tok / p.page_tokens - pg0;
+        if ((rel >> 5) != pg_batch) {
+          pg_batch = rel >> 5;
+          const int idx = pg0 + pg_batch * 32 + lane;
+          pg_reg = idx < p.max_pages_per_seq ? p.page_table[se.slot * p.max_pages_per_seq + idx] : 0;
+        }
+        const int page = __shfl_sync(0xffffffffu, pg_reg, rel & 31);
         if (lane == 0) {
           if (sidx >= (uint32_t)R && !mbar_wait(&empty[slot], ((sidx / R) - 1) & 1)) {
             set_error(p.error, 1);
             ok = false;
           }
           if (ok) {
-            const int tok = w.t0 + s * kStageTokens;
-            const int page = p.page_table[se.slot * p.max_pages_per_seq + tok / p.page_tokens];
             const int row = ((layer * p.num_pages + page) * p.kv_heads + w.kvh) * p.page_tokens + (tok % p.page_tokens);
             unsigned char* st = smem + slot * C::kStageBytes;
             mbar_arrive_expect_tx(&full[slot], C::kStageBytes);
 #pragma unroll
-            for (int b = 0; b < C::kBoxes; ++b) {
-              tma_load_2d_hint(st + b * kBoxBytes, &p.tmap_k, &full[slot], b * 64, row, policy);
-              tma_load_2d_hint(st + (C::kBoxes + b) * kBoxBytes, &p.tmap_v, &full[slot], b * 64, row, policy);
+            for (int bx = 0; bx < C::kBoxes; ++bx) {
+              tma_load_2d_hint(st + bx * kBoxBytes, &p.tmap_k, &full[slot], bx * 64, row, policy);
+              tma_load_2d_hint(st + (C::kBoxes + bx) * kBoxBytes, &p.tmap_v, &full[slot], bx * 64, row, policy);
             }
           }
         }
@@ -197,12 +258,156 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         if (!ok) break;
       }
     }
-    // Never leave the CTA with copies in flight: the last stages have landed.
+    // Never leave the CTA with copies in flight: the last stages and q buffers have landed.
     if (lane == 0) {
-      for (uint32_t k = sidx > (uint32_t)R ? sidx - R : 0; k < sidx; ++k) {
-        if (!mbar_wait(&full[k % R], (k / R) & 1)) set_error(p.error, 2);
+      for (uint32_t j = sidx > (uint32_t)R ? sidx - R : 0; j < sidx; ++j) {
+        if (!mbar_wait(&full[j % R], (j / R) & 1)) set_error(p.error, 2);
+      }
+      for (uint32_t j = k > 2u ? k - 2 : 0; j < k; ++j) {
+        if (!mbar_wait(&qfull[j & 1], (j >> 1) & 1)) set_error(p.error, 6);
       }
     }
+    return;
+  }
+
+  if (warp == kConsumerWarps + 1) {
+    // ---- helper warp: query fragments ahead of the consumers; merges behind them ----
+    const int g = lane >> 2, c = lane & 3;  // the fragment owner this lane prepares for
+    uint32_t k = 0;
+    bool ok = true;
+    // fragments for the CTA's item number kk (all 32 lanes; warp-uniform waits)
+    auto prepare = [&](uint32_t kk, int it_k) -> bool {
+      const int b = kk & 1;
+      const Work w = work_of(p, it_k);
+      (void)w;
+      if (!mbar_wait_warp(&qfull[b], (kk >> 1) & 1)) return false;
+      if (kk >= 2 && !mbar_wait_warp(&fempty[b], ((kk >> 1) - 1) & 1)) return false;
+      const float* sq = reinterpret_cast<const float*>(smem + C::kOffQ + b * C::kQBytes);
+      const float* cs = reinterpret_cast<const float*>(smem + C::kOffCS + b * C::kCSBytes);
+      uint4* frag = reinterpret_cast<uint4*>(smem + C::kOffFrag + b * C::kFragBytes);
+#pragma unroll
+      for (int j = 0; j < C::kChunksPerThread; ++j) {
+        int box;
+        const int ch = k_chunk_of<HD>(c, j, &box);
+        const int d0 = box * 64 + ch * 8;                  // 8 consecutive dims, all on one side of half
+        const int dp = d0 < half ? d0 + half : d0 - half;  // their rotation partners
+        const int di = d0 < half ? d0 : d0 - half;         // cos/sin index
+        float cv[8], sv[8];
+        if (p.rope) {
+          const float4 c0 = *reinterpret_cast<const float4*>(cs + di);
+          const float4 c1 = *reinterpret_cast<const float4*>(cs + di + 4);
+          const float4 s0 = *reinterpret_cast<const float4*>(cs + half + di);
+          const float4 s1 = *reinterpret_cast<const float4*>(cs + half + di + 4);
+          cv[0] = c0.x; cv[1] = c0.y; cv[2] = c0.z; cv[3] = c0.w; cv[4] = c1.x; cv[5] = c1.y; cv[6] = c1.z; cv[7] = c1.w;
+          sv[0] = s0.x; sv[1] = s0.y; sv[2] = s0.z; sv[3] = s0.w; sv[4] = s1.x; sv[5] = s1.y; sv[6] = s1.z; sv[7] = s1.w;
+        }
+        float v[2][8];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int row = g + 8 * r;
+          if (row >= G || row >= GP) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[r][e] = 0.f;
+            continue;
+          }
+          const float* qr = sq + row * C::kRowF;
+          const float4 x0 = *reinterpret_cast<const float4*>(qr + d0);
+          const float4 x1 = *reinterpret_cast<const float4*>(qr + d0 + 4);
+          const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          if (p.rope) {
+            const float4 y0 = *reinterpret_cast<const float4*>(qr + dp);
+            const float4 y1 = *reinterpret_cast<const float4*>(qr + dp + 4);
+            const float y[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              v[r][e] = d0 < half ? rope_lo(x[e], y[e], cv[e], sv[e]) : rope_hi(y[e], x[e], cv[e], sv[e]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[r][e] = x[e];
+          }
+        }
+        // k-step 2j uses dims d0+0..3, k-step 2j+1 uses d0+4..7; stored as [k-step][lane] uint4
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint4 f;
+          f.x = pack_half2(v[0][4 * h + 0], v[0][4 * h + 1]);
+          f.y = pack_half2(v[1][4 * h + 0], v[1][4 * h + 1]);
+          f.z = pack_half2(v[0][4 * h + 2], v[0][4 * h + 3]);
+          f.w = pack_half2(v[1][4 * h + 2], v[1][4 * h + 3]);
+          frag[(2 * j + h) * 32 + lane] = f;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&qempty[b]);  // raw rows consumed: the producer may refill this buffer
+        mbar_arrive(&fready[b]);
+      }
+      return true;
+    };
+    if (blockIdx.x < n_items) ok = prepare(0, blockIdx.x);
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+      if (it + (int)gridDim.x < n_items && !prepare(k + 1, it + gridDim.x)) {
+        ok = false;
+        break;
+      }
+      // merge item k: the four consumer warps' (m, l, O) -> output or split-K record
+      const int b = k & 1;
+      if (!mbar_wait_warp(&mready[b], (k >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const Work w = work_of(p, it);
+      const SeqEntry se = p.seqs[w.si];
+      const size_t qrow0 = (size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * H + w.kvh * G;
+      const float* sm_o = reinterpret_cast<const float*>(smem + C::kOffMerge + b * C::kMergeBytes);
+      const float* sm_m = reinterpret_cast<const float*>(smem + C::kOffML) + b * C::kMLFloats;
+      const float* sm_l = sm_m + kConsumerWarps * 16;
+      const bool single = se.n_chunks == 1;
+      float* part = p.partials + ((size_t)(w.layer_local * p.kv_heads + w.kvh) * p.total_chunks + w.cx) * G * REC;
+      constexpr int kLanesPerRow = HD / 4;        // float4 per lane
+      constexpr int kRowStep = 32 / kLanesPerRow; // rows handled per pass
+      const int d = 4 * (lane % kLanesPerRow);
+      const int r0 = lane / kLanesPerRow;
+#pragma unroll
+      for (int u = 0; u < GP / kRowStep; ++u) {
+        const int row = r0 + u * kRowStep;
+        if (row >= G) continue;
+        float M = -INFINITY;
+#pragma unroll
+        for (int ww = 0; ww < kConsumerWarps; ++ww) M = fmaxf(M, sm_m[ww * 16 + row]);
+        float L = 0.f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int ww = 0; ww < kConsumerWarps; ++ww) {
+          const float mw = sm_m[ww * 16 + row];
+          const float wt = mw == -INFINITY ? 0.f : ex2(mw - M);
+          const float4 o = *reinterpret_cast<const float4*>(sm_o + ((size_t)ww * GP + row) * C::kRowF + d);
+          L += sm_l[ww * 16 + row] * wt;
+          O.x += o.x * wt;
+          O.y += o.y * wt;
+          O.z += o.z * wt;
+          O.w += o.w * wt;
+        }
+        if (single && !p.partial_out) {
+          const float inv = 1.f / L;
+          *reinterpret_cast<float4*>(p.out + (qrow0 + row) * HD + d) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+        } else if (single) {
+          // public partial records are {acc[HD], m, l}
+          float* r = p.out + (qrow0 + row) * (HD + 2);
+          *reinterpret_cast<float2*>(r + d) = make_float2(O.x, O.y);
+          *reinterpret_cast<float2*>(r + d + 2) = make_float2(O.z, O.w);
+          if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
+        } else {
+          float* r = part + (size_t)row * REC;
+          *reinterpret_cast<float4*>(r + d) = O;
+          if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&mfree[b]);
+    }
+    if (!ok) set_error(p.error, 9);
     return;
   }
 
@@ -210,57 +415,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
   const int g = lane >> 2;  // mma group id: head rows g and g+8, token rows
   const int c = lane & 3;   // thread in group
   const float sl = p.scale_log2;
-  constexpr int half = HD / 2;
-  uint32_t sidx = 0;
+  uint32_t sidx = 0, k = 0;
   bool failed = false;
-  for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+  for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++k) {
     const Work w = work_of(p, it);
-    const SeqEntry se = p.seqs[w.si];
-    const size_t qrow0 = (size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * H + w.kvh * G;
 
-    // 1) rotated q rows of the group -> shared memory (coalesced loads)
+    // 1) query fragments prepared by the helper warp
+    const int fb = k & 1;
+    if (!failed && !mbar_wait_warp(&fready[fb], (k >> 1) & 1)) {
+      set_error(p.error, 7);
+      failed = true;
+    }
+    uint32_t qa[C::kKSteps][4];
     {
-      const float* qg = p.q + qrow0 * HD;
-      const float* crow = p.rope_cos + (size_t)se.q_pos * half;
-      const float* srow = p.rope_sin + (size_t)se.q_pos * half;
-      for (int i = tid; i < 16 * half; i += kConsumerWarps * 32) {
-        const int r = i / half, d = i - r * half;
-        float lo = 0.f, hi = 0.f;
-        if (r < G) {
-          const float a = qg[r * HD + d], b = qg[r * HD + d + half];
-          if (p.rope) {
-            lo = rope_lo(a, b, crow[d], srow[d]);
-            hi = rope_hi(a, b, crow[d], srow[d]);
-          } else {
-            lo = a;
-            hi = b;
-          }
-        }
-        sm_q[r * HD + d] = lo;
-        sm_q[r * HD + d + half] = hi;
+      const uint4* frag = reinterpret_cast<const uint4*>(smem + C::kOffFrag + fb * C::kFragBytes);
+#pragma unroll
+      for (int ks = 0; ks < C::kKSteps; ++ks) {
+        const uint4 f = frag[ks * 32 + lane];
+        qa[ks][0] = f.x;
+        qa[ks][1] = f.y;
+        qa[ks][2] = f.z;
+        qa[ks][3] = f.w;
       }
     }
-    consumer_sync();
-    uint32_t qa[C::kKSteps][4];
-#pragma unroll
-    for (int j = 0; j < C::kChunksPerThread; ++j) {
-      int box;
-      const int ch = k_chunk_of<HD>(c, j, &box);
-      const int d0 = box * 64 + ch * 8;
-      const float4 lo0 = *reinterpret_cast<const float4*>(sm_q + g * HD + d0);
-      const float4 lo1 = *reinterpret_cast<const float4*>(sm_q + g * HD + d0 + 4);
-      const float4 hi0 = *reinterpret_cast<const float4*>(sm_q + (g + 8) * HD + d0);
-      const float4 hi1 = *reinterpret_cast<const float4*>(sm_q + (g + 8) * HD + d0 + 4);
-      // k-step 2j uses dims d0+0..3, k-step 2j+1 uses d0+4..7
-      qa[2 * j][0] = pack_half2(lo0.x, lo0.y);
-      qa[2 * j][1] = pack_half2(hi0.x, hi0.y);
-      qa[2 * j][2] = pack_half2(lo0.z, lo0.w);
-      qa[2 * j][3] = pack_half2(hi0.z, hi0.w);
-      qa[2 * j + 1][0] = pack_half2(lo1.x, lo1.y);
-      qa[2 * j + 1][1] = pack_half2(hi1.x, hi1.y);
-      qa[2 * j + 1][2] = pack_half2(lo1.z, lo1.w);
-      qa[2 * j + 1][3] = pack_half2(hi1.z, hi1.w);
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&fempty[fb]);
 
     // 2) stream the chunk's stages
     float acc[C::kNTiles][4];
@@ -269,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
     for (int s = 0; s < w.n_st; ++s, ++sidx) {
       const int slot = sidx % R;
-      if (!failed && !mbar_wait(&full[slot], (sidx / R) & 1)) {
+      if (!failed && !mbar_wait_warp(&full[slot], (sidx / R) & 1)) {
         set_error(p.error, 3);
         failed = true;
       }
@@ -341,8 +520,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         pa[3] = pack_half2(sc[1][2], sc[1][3]);
         const int rv0 = 16 * warp + 2 * c;
 #pragma unroll
-        for (int b = 0; b < C::kBoxes; ++b) {
-          const uint32_t vb = st + (C::kBoxes + b) * kBoxBytes;
+        for (int bx = 0; bx < C::kBoxes; ++bx) {
+          const uint32_t vb = st + (C::kBoxes + bx) * kBoxBytes;
           const uint4 v0 = lds128(vb + (rv0 + 0) * 128 + ((g ^ ((rv0 + 0) & 7)) << 4));
           const uint4 v1 = lds128(vb + (rv0 + 1) * 128 + ((g ^ ((rv0 + 1) & 7)) << 4));
           const uint4 v8 = lds128(vb + (rv0 + 8) * 128 + ((g ^ ((rv0 + 8) & 7)) << 4));
@@ -356,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
             const uint32_t sel = (jj & 1) ? 0x7632u : 0x5410u;
             const uint32_t b0 = prmt(w0[jj >> 1], w1[jj >> 1], sel);
             const uint32_t b1 = prmt(w8[jj >> 1], w9[jj >> 1], sel);
-            mma_16816(acc[b * 8 + jj], pa, b0, b1);
+            mma_16816(acc[bx * 8 + jj], pa, b0, b1);
           }
         }
       }
@@ -368,7 +547,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
 
-    // 3) merge the 4 warps' states: one record per query head of the group
+    // 3) park this warp's state for the helper's merge
+    const int mb = k & 1;
+    if (k >= 2 && !failed && !mbar_wait_warp(&mfree[mb], ((k >> 1) - 1) & 1)) {
+      set_error(p.error, 8);
+      failed = true;
+    }
+    float* sm_o = reinterpret_cast<float*>(smem + C::kOffMerge + mb * C::kMergeBytes);  // [4][GP][kRowF]
+    float* sm_m = reinterpret_cast<float*>(smem + C::kOffML) + mb * C::kMLFloats;       // [4][16]
+    float* sm_l = sm_m + kConsumerWarps * 16;                                          // [4][16]
     if (c == 0) {
       sm_m[warp * 16 + g] = m_lo;
       sm_m[warp * 16 + g + 8] = m_hi;
@@ -377,103 +564,74 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     }
 #pragma unroll
     for (int i = 0; i < C::kNTiles; ++i) {
-      const int b = i >> 3, jj = i & 7;
-      const int d0 = 64 * b + 8 * (2 * c) + jj;
-      const int d1 = 64 * b + 8 * (2 * c + 1) + jj;
-      float* o_lo = sm_o + ((size_t)warp * 16 + g) * HD;
-      float* o_hi = sm_o + ((size_t)warp * 16 + g + 8) * HD;
+      const int bx = i >> 3, jj = i & 7;
+      const int d0 = 64 * bx + 8 * (2 * c) + jj;
+      const int d1 = 64 * bx + 8 * (2 * c + 1) + jj;
+      float* o_lo = sm_o + ((size_t)warp * GP + g) * C::kRowF;
       o_lo[d0] = acc[i][0];
       o_lo[d1] = acc[i][1];
-      o_hi[d0] = acc[i][2];
-      o_hi[d1] = acc[i][3];
-    }
-    consumer_sync();
-    const bool single = se.n_chunks == 1;
-    const int rec = HD + 2;
-    float* part = p.partials + ((size_t)(w.layer_local * p.kv_heads + w.kvh) * p.total_chunks + w.cx) * G * rec;
-    for (int i = tid; i < G * HD; i += kConsumerWarps * 32) {
-      const int row = i / HD, d = i - row * HD;
-      float M = -INFINITY;
-#pragma unroll
-      for (int ww = 0; ww < kConsumerWarps; ++ww) M = fmaxf(M, sm_m[ww * 16 + row]);
-      float L = 0.f, O = 0.f;
-#pragma unroll
-      for (int ww = 0; ww < kConsumerWarps; ++ww) {
-        const float mw = sm_m[ww * 16 + row];
-        const float wt = mw == -INFINITY ? 0.f : ex2(mw - M);
-        L += sm_l[ww * 16 + row] * wt;
-        O += sm_o[((size_t)ww * 16 + row) * HD + d] * wt;
-      }
-      if (single) {
-        if (p.partial_out) {
-          float* r = p.out + (qrow0 + row) * rec;
-          r[d] = O;
-          if (d == 0) { r[HD] = M; r[HD + 1] = L; }
-        } else {
-          p.out[(qrow0 + row) * HD + d] = O / L;
-        }
-      } else {
-        float* r = part + (size_t)row * rec;
-        r[d] = O;
-        if (d == 0) { r[HD] = M; r[HD + 1] = L; }
+      if (GP > 8) {
+        float* o_hi = sm_o + ((size_t)warp * GP + g + 8) * C::kRowF;
+        o_hi[d0] = acc[i][2];
+        o_hi[d1] = acc[i][3];
       }
     }
-    if (!single) {
-      // 4) split-K: the last CTA to finish a (layer, seq, kv head) merges its chunks
-      __threadfence();
-      consumer_sync();
-      if (tid == 0) {
-        uint32_t* ctr = p.counters + (size_t)(w.layer_local * p.kv_heads + w.kvh) * p.n_seqs + w.si;
-        const uint32_t ticket = atomicAdd(ctr, 1u);
-        const int last = ticket == (uint32_t)(se.n_chunks - 1);
-        if (last) *ctr = 0u;  // every chunk of the group has taken its ticket
-        flags[0] = last;
-      }
-      consumer_sync();
-      if (flags[0]) {
-        __threadfence();
-        const float* grp =
-            p.partials + ((size_t)(w.layer_local * p.kv_heads + w.kvh) * p.total_chunks + se.chunk_begin) * G * rec;
-        float* sm_cm = sm_o;                     // [n_chunks][G] maxima (merge area is free now)
-        float* sm_cl = sm_cm + se.n_chunks * G;  // [n_chunks][G] sums
-        float* sm_M = sm_cl + se.n_chunks * G;   // [16]
-        float* sm_L = sm_M + 16;                 // [16]
-        if (2 * se.n_chunks * G > C::kMaxCombineFloats) {
-          set_error(p.error, 4);  // the host caps n_chunks so this cannot happen
-        } else {
-          for (int i = tid; i < se.n_chunks * G; i += kConsumerWarps * 32) {
-            sm_cm[i] = __ldcg(grp + (size_t)i * rec + HD);
-            sm_cl[i] = __ldcg(grp + (size_t)i * rec + HD + 1);
-          }
-          consumer_sync();
-          if (tid < G) {
-            float M = -INFINITY;
-            for (int k = 0; k < se.n_chunks; ++k) M = fmaxf(M, sm_cm[k * G + tid]);
-            float L = 0.f;
-            for (int k = 0; k < se.n_chunks; ++k) L += sm_cl[k * G + tid] * ex2(sm_cm[k * G + tid] - M);
-            sm_M[tid] = M;
-            sm_L[tid] = L;
-          }
-          consumer_sync();
-          for (int i = tid; i < G * HD; i += kConsumerWarps * 32) {
-            const int row = i / HD, d = i - row * HD;
-            const float M = sm_M[row];
-            float O = 0.f;
-            for (int k = 0; k < se.n_chunks; ++k) {
-              O += __ldcg(grp + ((size_t)k * G + row) * rec + d) * ex2(sm_cm[k * G + row] - M);
-            }
-            if (p.partial_out) {
-              float* r = p.out + (qrow0 + row) * rec;
-              r[d] = O;
-              if (d == 0) { r[HD] = M; r[HD + 1] = sm_L[row]; }
-            } else {
-              p.out[(qrow0 + row) * HD + d] = O / sm_L[row];
-            }
-          }
-        }
-      }
-    }
-    consumer_sync();  // merge / q areas are reused by the next item
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&mready[mb]);
+  }
+}
+
+// Split-K combine: one CTA per (layer, sequence, kv head, group of rows).
+// Runs as a programmatic dependent launch: its CTAs may be resident early and
+// wait here until the decode grid has finished and its writes are visible.
+template <int HD>
+__global__ void __launch_bounds__(128) decode_combine_kernel(const __grid_constant__ DecodeParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  constexpr int REC = kScratchRec<HD>;
+  constexpr int kLanesPerRow = HD / 4;                 // float4 per lane
+  constexpr int kRowsPerCta = 128 / kLanesPerRow;
+  const int G = p.group;
+  const int row_groups = (G + kRowsPerCta - 1) / kRowsPerCta;
+  int b = blockIdx.x;
+  const int rg = b % row_groups;
+  b /= row_groups;
+  const int si = b % p.n_seqs;
+  b /= p.n_seqs;
+  const int kvh = b % p.kv_heads;
+  const int layer_local = b / p.kv_heads;
+  const SeqEntry se = p.seqs[si];
+  if (se.n_chunks <= 1) return;
+  const int row = rg * kRowsPerCta + threadIdx.x / kLanesPerRow;
+  if (row >= G) return;
+  const int d = 4 * (threadIdx.x % kLanesPerRow);
+  const int nc = se.n_chunks;
+  const float* grp = p.partials + ((size_t)(layer_local * p.kv_heads + kvh) * p.total_chunks + se.chunk_begin) * G * REC;
+  float M = -INFINITY;
+#pragma unroll 8
+  for (int kk = 0; kk < nc; ++kk) M = fmaxf(M, grp[((size_t)kk * G + row) * REC + HD]);
+  float L = 0.f;
+  float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+  for (int kk = 0; kk < nc; ++kk) {
+    const float* r = grp + ((size_t)kk * G + row) * REC;
+    const float2 ml = *reinterpret_cast<const float2*>(r + HD);
+    const float wt = ex2(ml.x - M);
+    const float4 o = *reinterpret_cast<const float4*>(r + d);
+    L += ml.y * wt;
+    O.x += o.x * wt;
+    O.y += o.y * wt;
+    O.z += o.z * wt;
+    O.w += o.w * wt;
+  }
+  const size_t orow = (size_t)(layer_local * p.seq_total + p.seq_base + si) * (G * p.kv_heads) + kvh * G + row;
+  if (p.partial_out) {
+    float* r = p.out + orow * (HD + 2);
+    *reinterpret_cast<float2*>(r + d) = make_float2(O.x, O.y);
+    *reinterpret_cast<float2*>(r + d + 2) = make_float2(O.z, O.w);
+    if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
+  } else {
+    const float inv = 1.f / L;
+    *reinterpret_cast<float4*>(p.out + orow * HD + d) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
   }
 }
 
@@ -576,13 +734,13 @@ __global__ void merge_partials_kernel(const float* __restrict__ partials, int n_
   }
 }
 
-template <int HD>
+template <int HD, int GP>
 cudaError_t launch_decode_impl(const DecodeParams& p, cudaStream_t s) {
-  using C = DecodeCfg<HD>;
-  static int sms = 0;  // per-process; one device type
+  using C = DecodeCfg<HD, GP>;
+  static int sms = 0;  // per process (one device model)
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_f16_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(decode_f16_kernel<HD, GP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
     if (e != cudaSuccess) return e;
     int dev = 0;
@@ -592,16 +750,34 @@ cudaError_t launch_decode_impl(const DecodeParams& p, cudaStream_t s) {
   }
   const long long items = (long long)p.n_layers * p.kv_heads * p.total_chunks;
   const int grid = (int)(items < sms ? items : sms);
-  decode_f16_kernel<HD><<<grid, kThreads, C::kSmemBytes, s>>>(p);
-  return cudaGetLastError();
+  decode_f16_kernel<HD, GP><<<grid, kThreads, C::kSmemBytes, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  bool any_split = false;
+  for (int i = 0; i < p.n_seqs; ++i) any_split |= p.seqs[i].n_chunks > 1;
+  if (!any_split) return cudaSuccess;
+  // split-K combine as a programmatic dependent launch (its CTAs wait for the decode grid)
+  constexpr int kRowsPerCta = 128 / (HD / 4);
+  const int row_groups = (p.group + kRowsPerCta - 1) / kRowsPerCta;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.n_layers * p.kv_heads * p.n_seqs * row_groups));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_combine_kernel<HD>, p);
 }
 
 }  // namespace
 
 cudaError_t launch_decode_f16(const DecodeParams& p, int head_dim, int stages, cudaStream_t s) {
   (void)stages;
-  if (head_dim == 128) return launch_decode_impl<128>(p, s);
-  if (head_dim == 64) return launch_decode_impl<64>(p, s);
+  if (head_dim == 128) return p.group <= 8 ? launch_decode_impl<128, 8>(p, s) : launch_decode_impl<128, 16>(p, s);
+  if (head_dim == 64) return p.group <= 8 ? launch_decode_impl<64, 8>(p, s) : launch_decode_impl<64, 16>(p, s);
   return cudaErrorInvalidValue;
 }
 
@@ -672,7 +848,7 @@ extern "C" __attribute__((visibility("default"))) te_status te_attention_decode_
   }
   // Chunking: the partial records of all chunks must fit the fixed scratch and
   // the kernel's in-shared-memory combine table.
-  const size_t rec_bytes = kv_heads * G * (head_dim + 2) * sizeof(float);
+  const size_t rec_bytes = kv_heads * G * decode_scratch_rec((int)head_dim) * sizeof(float);
   const size_t fit_chunks = kNoAllocPartialBytes / rec_bytes;
   if (fit_chunks == 0) return TE_STATUS_UNSUPPORTED;
   const size_t smem_chunks = decode_max_chunks((int)head_dim, (int)G);

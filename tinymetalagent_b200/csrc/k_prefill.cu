@@ -11,7 +11,8 @@
 // One work item = (layer, query head, 128-query tile); items are ordered by
 // decreasing causal length and dealt round-robin to a persistent grid of one
 // CTA per SM.  Warp roles (192 threads):
-//   warp 0     TMA producer: Q tile, then K/V tiles (128 keys) into a 2-stage ring
+//   warp 0     TMA producer: Q tiles (double-buffered, so the next item's Q
+//              is prefetched), K/V tiles (128 keys) into a 2-stage ring
 //   warp 1     TMEM owner; lane 0 issues tcgen05.mma:
 //                S[sb] = Q K^T   (M=128 queries, N=128 keys, K=128 dims, f16 -> f32 in TMEM)
 //                O    += P V     (M=128 queries, N=128 dims,  K=128 keys)
@@ -42,14 +43,14 @@ constexpr int kHalf = kTile / 2;            // 16 KiB: 128 rows x 128 B
 constexpr int kBox = 64 * 128;              // 8 KiB TMA box: 64 rows x 64 f16
 constexpr int kThreads = 192;
 
-constexpr int OFF_Q = 0;
-constexpr int OFF_KV = OFF_Q + kTile;       // stage s: K at OFF_KV + s*2*kTile, V at + kTile
+constexpr int OFF_Q = 0;                    // two Q buffers (the next item's Q is prefetched)
+constexpr int OFF_KV = OFF_Q + 2 * kTile;   // stage s: K at OFF_KV + s*2*kTile, V at + kTile
 constexpr int OFF_P = OFF_KV + 4 * kTile;
-constexpr int OFF_BAR = OFF_P + kTile;      // 196608
+constexpr int OFF_BAR = OFF_P + kTile;      // 229376
 constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
 
 enum Bar {
-  Q_FULL = 0, Q_EMPTY, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1,
+  Q_FULL0 = 0, Q_FULL1, Q_EMPTY0, Q_EMPTY1, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1,
   S_FULL0, S_FULL1, S_EMPTY0, S_EMPTY1, P_FULL, PV_DONE, O_EMPTY, DRAIN, kNumBars
 };
 
@@ -87,9 +88,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar[Q_FULL], 1);
-    mbar_init(&bar[Q_EMPTY], 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar[Q_FULL0 + s], 1);
+      mbar_init(&bar[Q_EMPTY0 + s], 1);
       mbar_init(&bar[K_FULL0 + s], 1);
       mbar_init(&bar[V_FULL0 + s], 1);
       mbar_init(&bar[KV_EMPTY0 + s], 1);
@@ -116,47 +117,85 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // The whole warp walks the items (page-table entries are read one per lane
+    // and shuffled); lane 0 issues every TMA copy.
     if (lane == 0) {
       prefetch_tmap(&p.tmap_q);
       prefetch_tmap(&p.tmap_k);
       prefetch_tmap(&p.tmap_v);
-      uint32_t qc = 0, kc = 0;
-      for (int it = blockIdx.x; it < p.n_items && !aborted(abort_flag); it += gridDim.x) {
-        const Item I = item_of(p, it);
-        if (!mbar_wait(&bar[Q_EMPTY], (qc & 1) ^ 1)) { set_error(p.error, 11); *abort_flag = 1; break; }
-        mbar_arrive_expect_tx(&bar[Q_FULL], kTile);
-        const int qrow = (I.layer_local * p.heads + I.head) * p.n_tokens_padded + I.qt * BM;
+    }
+    uint32_t qc = 0, kc = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      // one lane reads the abort flag so the whole warp takes the same branch
+      if (__shfl_sync(0xffffffffu, lane == 0 && aborted(abort_flag) ? 1 : 0, 0)) break;
+      const Item I = item_of(p, it);
+      const int qs = qc & 1;
+      if (lane == 0) {
+        if (!mbar_wait(&bar[Q_EMPTY0 + qs], ((qc >> 1) & 1) ^ 1)) {
+          set_error(p.error, 11);
+          ok = false;
+        } else {
+          mbar_arrive_expect_tx(&bar[Q_FULL0 + qs], kTile);
+          const int qrow = (I.layer_local * p.heads + I.head) * p.n_tokens_padded + I.qt * BM;
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+          for (int h = 0; h < 2; ++h)
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-            tma_load_2d(smem + OFF_Q + c * kHalf + h * kBox, &p.tmap_q, &bar[Q_FULL], c * 64, qrow + h * 64);
-        ++qc;
-        const int layer = p.layer_begin + I.layer_local;
-        const int kvh = I.head / G;
-        for (int j = 0; j < I.n_kv; ++j, ++kc) {
-          const int s = kc & 1;
-          if (!mbar_wait(&bar[KV_EMPTY0 + s], ((kc >> 1) & 1) ^ 1)) { set_error(p.error, 12); *abort_flag = 1; break; }
-          unsigned char* ks = smem + OFF_KV + s * 2 * kTile;
-          unsigned char* vs = ks + kTile;
-          mbar_arrive_expect_tx(&bar[K_FULL0 + s], kTile);
-          mbar_arrive_expect_tx(&bar[V_FULL0 + s], kTile);
+            for (int c = 0; c < 2; ++c)
+              tma_load_2d(smem + OFF_Q + qs * kTile + c * kHalf + h * kBox, &p.tmap_q, &bar[Q_FULL0 + qs], c * 64,
+                          qrow + h * 64);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      ++qc;
+      const int layer = p.layer_begin + I.layer_local;
+      const int kvh = I.head / G;
+      int pg_batch = -1, pg_reg = 0;
+      for (int j = 0; j < I.n_kv; ++j, ++kc) {
+        const int s = kc & 1;
+        int pages[2];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int tok = j * BN + h * 64;
-            const int pg_idx = min(tok / p.page_tokens, p.n_pages_mapped - 1);  // rows past the end are masked
-            const int pg = p.page_table_row[pg_idx];
-            const int row = ((layer * p.num_pages + pg) * p.kv_heads + kvh) * p.page_tokens + (tok % p.page_tokens);
+        for (int h = 0; h < 2; ++h) {
+          const int idx = min((j * BN + h * 64) / p.page_tokens, p.n_pages_mapped - 1);  // rows past the end are masked
+          if ((idx >> 5) != pg_batch) {
+            pg_batch = idx >> 5;
+            const int e = pg_batch * 32 + lane;
+            pg_reg = e < p.n_pages_mapped ? p.page_table_row[e] : 0;
+          }
+          pages[h] = __shfl_sync(0xffffffffu, pg_reg, idx & 31);
+        }
+        if (lane == 0) {
+          if (!mbar_wait(&bar[KV_EMPTY0 + s], ((kc >> 1) & 1) ^ 1)) {
+            set_error(p.error, 12);
+            ok = false;
+          } else {
+            unsigned char* ks = smem + OFF_KV + s * 2 * kTile;
+            unsigned char* vs = ks + kTile;
+            mbar_arrive_expect_tx(&bar[K_FULL0 + s], kTile);
+            mbar_arrive_expect_tx(&bar[V_FULL0 + s], kTile);
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              tma_load_2d(ks + c * kHalf + h * kBox, &p.tmap_k, &bar[K_FULL0 + s], c * 64, row);
-              tma_load_2d(vs + c * kHalf + h * kBox, &p.tmap_v, &bar[V_FULL0 + s], c * 64, row);
+            for (int h = 0; h < 2; ++h) {
+              const int tok = j * BN + h * 64;
+              const int row = ((layer * p.num_pages + pages[h]) * p.kv_heads + kvh) * p.page_tokens + (tok % p.page_tokens);
+#pragma unroll
+              for (int c = 0; c < 2; ++c) {
+                tma_load_2d(ks + c * kHalf + h * kBox, &p.tmap_k, &bar[K_FULL0 + s], c * 64, row);
+                tma_load_2d(vs + c * kHalf + h * kBox, &p.tmap_v, &bar[V_FULL0 + s], c * 64, row);
+              }
             }
           }
         }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
       }
-      // Leave no copy in flight: the last Q and K/V stages have landed (immediate when consumed).
-      if (qc > 0 && !mbar_wait(&bar[Q_FULL], (qc - 1) & 1)) set_error(p.error, 13);
+    }
+    if (!ok) *abort_flag = 1;
+    // Leave no copy in flight: the last Q and K/V stages have landed (immediate when consumed).
+    if (lane == 0) {
+      for (uint32_t j = qc >= 2 ? qc - 2 : 0; j < qc; ++j) {
+        if (!mbar_wait(&bar[Q_FULL0 + (j & 1)], (j >> 1) & 1)) set_error(p.error, 13);
+      }
       for (uint32_t k = (kc >= 2 ? kc - 2 : 0); k < kc; ++k) {
         if (!mbar_wait(&bar[K_FULL0 + (k & 1)], (k >> 1) & 1)) set_error(p.error, 14);
         if (!mbar_wait(&bar[V_FULL0 + (k & 1)], (k >> 1) & 1)) set_error(p.error, 14);
@@ -167,14 +206,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16_f32(BM, BN, false, false);
       constexpr uint32_t idesc_pv = idesc_f16_f32(BM, HD, false, true);
-      const uint32_t sq = smem_u32(smem + OFF_Q);
       const uint32_t sp = smem_u32(smem + OFF_P);
       uint32_t qc = 0, kc = 0, sc = 0, pc = 0, oc = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < p.n_items && ok && !aborted(abort_flag); it += gridDim.x) {
         const Item I = item_of(p, it);
-        if (!mbar_wait(&bar[Q_FULL], qc & 1)) { ok = false; break; }
+        const int qs = qc & 1;
+        if (!mbar_wait(&bar[Q_FULL0 + qs], (qc >> 1) & 1)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t sq = smem_u32(smem + OFF_Q + qs * kTile);
         const uint32_t kc0 = kc;
         auto do_pv = [&](int jj) -> bool {
           const uint32_t k_idx = kc0 + jj;
@@ -214,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           }
           umma_commit(&bar[S_FULL0 + sb]);
           ++sc;
-          if (j == I.n_kv - 1) umma_commit(&bar[Q_EMPTY]);
+          if (j == I.n_kv - 1) umma_commit(&bar[Q_EMPTY0 + qs]);
           if (j >= 1 && !do_pv(j - 1)) ok = false;
         }
         if (ok && !do_pv(I.n_kv - 1)) ok = false;
@@ -236,7 +276,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const float sl = p.scale_log2;
     uint32_t sc = 0, pc = 0;
     bool ok = true;
-    for (int it = blockIdx.x; it < p.n_items && ok && !aborted(abort_flag); it += gridDim.x) {
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
+      if (__any_sync(0xffffffffu, aborted(abort_flag))) break;
       const Item I = item_of(p, it);
       const int q_pos = p.q_offset + I.qt * BM + row;
       const int key_limit = min(q_pos, total - 1);
@@ -244,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < I.n_kv; ++j) {
         const int sb = sc & 1;
-        if (!mbar_wait(&bar[S_FULL0 + sb], (sc >> 1) & 1)) { ok = false; break; }
+        if (!mbar_wait_warp(&bar[S_FULL0 + sb], (sc >> 1) & 1)) { ok = false; break; }
         tc_fence_after();
         float s[BN];
 #pragma unroll
@@ -257,17 +298,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         if (lane == 0) mbar_arrive(&bar[S_EMPTY0 + sb]);
         ++sc;
         const bool need_mask = (j + 1) * BN - 1 > first_row_limit;
-        float tmax = -INFINITY;
+        if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          float v = s[c] * sl;
-          if (need_mask && j * BN + c > key_limit) v = -INFINITY;
-          s[c] = v;
-          tmax = fmaxf(tmax, v);
+          for (int c = 0; c < BN; ++c) {
+            if (j * BN + c > key_limit) s[c] = -INFINITY;
+          }
         }
-        const float m_new = fmaxf(m, tmax);
+        // row max of the raw scores: 8 independent partial maxima, then a tree
+        float pm[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) pm[u] = s[u];
+#pragma unroll
+        for (int c = 8; c < BN; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
+        const float tmax_raw = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                                     fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        const float m_new = fmaxf(m, tmax_raw * sl);  // scaling by sl > 0 preserves the max
         if (pc > 0) {  // P buffer free and O stable: the previous P V finished
-          if (!mbar_wait(&bar[PV_DONE], (pc - 1) & 1)) { ok = false; break; }
+          if (!mbar_wait_warp(&bar[PV_DONE], (pc - 1) & 1)) { ok = false; break; }
           tc_fence_after();
         }
         if (j == 0) {
@@ -287,13 +334,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           tmem_wait_st();
           m = m_new;
         }
-        float rs = 0.f;
+        // p = 2^(s*scale - m): one FFMA + one SFU op per score; 8 partial sums
+        const float neg_m = -m;
+        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < BN; ++c) {
-          const float e = ex2(s[c] - m);
+          const float e = ex2(fmaf(s[c], sl, neg_m));
           s[c] = e;
-          rs += e;
+          ps[c & 7] += e;
         }
+        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         l += rs;
         // P row -> shared memory, 128B-swizzled K-major (two 64-key halves).
 #pragma unroll
@@ -310,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       }
       if (!ok) break;
       // epilogue: O / l -> out[layer][token][head][:]
-      if (!mbar_wait(&bar[PV_DONE], (pc - 1) & 1)) { ok = false; break; }
+      if (!mbar_wait_warp(&bar[PV_DONE], (pc - 1) & 1)) { ok = false; break; }
       tc_fence_after();
       const int tok = I.qt * BM + row;
       const float inv = 1.f / l;

@@ -23,10 +23,6 @@ __device__ __forceinline__ float rope_hi(float a, float b, float c, float s) {
   return __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
 }
 
-__device__ __forceinline__ float load_in(const void* base, size_t idx, int f16) {
-  return f16 ? __half2float(reinterpret_cast<const __half*>(base)[idx]) : reinterpret_cast<const float*>(base)[idx];
-}
-
 __global__ void rope_rows_kernel(float* values, const float* cos_row, const float* sin_row, int heads,
                                  int head_dim) {
   const int half = head_dim / 2;
@@ -40,28 +36,71 @@ __global__ void rope_rows_kernel(float* values, const float* cos_row, const floa
   row[d + half] = rope_hi(a, b, c, s);
 }
 
-// One thread per (layer, token, kv head, rotation pair).
+// 8 consecutive values of an fp32 or f16 row as fp32.
+__device__ __forceinline__ void load8(const void* base, size_t idx, int f16, float (&v)[8]) {
+  if (f16) {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(base) + idx);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  return u;
+}
+
+// Rotates 8 pairs (d..d+7, d+half..d+half+7) in place with the reference expressions.
+__device__ __forceinline__ void rope8(float (&lo)[8], float (&hi)[8], const float* cos_row, const float* sin_row, int d) {
+  const float4 c0 = *reinterpret_cast<const float4*>(cos_row + d);
+  const float4 c1 = *reinterpret_cast<const float4*>(cos_row + d + 4);
+  const float4 s0 = *reinterpret_cast<const float4*>(sin_row + d);
+  const float4 s1 = *reinterpret_cast<const float4*>(sin_row + d + 4);
+  const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a = lo[i], b = hi[i];
+    lo[i] = rope_lo(a, b, c[i], s[i]);
+    hi[i] = rope_hi(a, b, c[i], s[i]);
+  }
+}
+
+// One thread per (layer, token, kv head, group of 8 rotation pairs).
 __global__ void append_rope_kernel(const AppendParams p) {
   const int half = p.head_dim / 2;
-  const long long total = (long long)p.n_layers * p.n_tokens * p.kv_heads * half;
+  const int groups = half / 8;
+  const long long total = (long long)p.n_layers * p.n_tokens * p.kv_heads * groups;
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
-  const int d = (int)(i % half);
-  long long r = i / half;
+  const int d = (int)(i % groups) * 8;
+  long long r = i / groups;
   const int kvh = (int)(r % p.kv_heads);
   r /= p.kv_heads;
   const int t = (int)(r % p.n_tokens);
   const int ll = (int)(r / p.n_tokens);
   const size_t in_row = (((size_t)ll * p.n_tokens + t) * p.kv_heads + kvh) * p.head_dim;
-  const float a = load_in(p.k, in_row + d, p.input_f16);
-  const float b = load_in(p.k, in_row + d + half, p.input_f16);
-  float lo = a, hi = b;
+  float klo[8], khi[8], vlo[8], vhi[8];
+  load8(p.k, in_row + d, p.input_f16, klo);
+  load8(p.k, in_row + d + half, p.input_f16, khi);
+  load8(p.v, in_row + d, p.input_f16, vlo);
+  load8(p.v, in_row + d + half, p.input_f16, vhi);
   if (p.rope) {
     const int pos = p.first_pos + t;
-    const float c = p.rope_cos[(size_t)pos * half + d];
-    const float s = p.rope_sin[(size_t)pos * half + d];
-    lo = rope_lo(a, b, c, s);
-    hi = rope_hi(a, b, c, s);
+    rope8(klo, khi, p.rope_cos + (size_t)pos * half, p.rope_sin + (size_t)pos * half, d);
   }
   const int idx = p.first_index + t;
   const int page = p.page_row[idx / p.page_tokens];
@@ -69,43 +108,40 @@ __global__ void append_rope_kernel(const AppendParams p) {
   const size_t row = ((size_t)(layer * p.num_pages + page) * p.kv_heads + kvh) * p.page_tokens + (idx % p.page_tokens);
   uint16_t* kd = p.k_pool + row * p.head_dim;
   uint16_t* vd = p.v_pool + row * p.head_dim;
-  kd[d] = __half_as_ushort(__float2half_rn(lo));
-  kd[d + half] = __half_as_ushort(__float2half_rn(hi));
-  vd[d] = __half_as_ushort(__float2half_rn(load_in(p.v, in_row + d, p.input_f16)));
-  vd[d + half] = __half_as_ushort(__float2half_rn(load_in(p.v, in_row + d + half, p.input_f16)));
+  *reinterpret_cast<uint4*>(kd + d) = pack8(klo);
+  *reinterpret_cast<uint4*>(kd + d + half) = pack8(khi);
+  *reinterpret_cast<uint4*>(vd + d) = pack8(vlo);
+  *reinterpret_cast<uint4*>(vd + d + half) = pack8(vhi);
 }
 
 // q[n_layers][n_tokens][heads][hd] -> qh[n_layers][heads][n_tokens_padded][hd] (f16, rotated).
 // Padding rows (t >= n_tokens) are written as zeros.
 __global__ void q_prep_kernel(const QPrepParams p) {
   const int half = p.head_dim / 2;
-  const long long total = (long long)p.n_layers * p.n_tokens_padded * p.heads * half;
+  const int groups = half / 8;
+  const long long total = (long long)p.n_layers * p.n_tokens_padded * p.heads * groups;
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
-  const int d = (int)(i % half);
-  long long r = i / half;
+  const int d = (int)(i % groups) * 8;
+  long long r = i / groups;
   const int h = (int)(r % p.heads);
   r /= p.heads;
   const int t = (int)(r % p.n_tokens_padded);
   const int ll = (int)(r / p.n_tokens_padded);
-  float lo = 0.f, hi = 0.f;
+  float lo[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float hi[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (t < p.n_tokens) {
     const size_t in_row = (((size_t)ll * p.n_tokens + t) * p.heads + h) * p.head_dim;
-    const float a = load_in(p.q, in_row + d, p.input_f16);
-    const float b = load_in(p.q, in_row + d + half, p.input_f16);
-    lo = a;
-    hi = b;
+    load8(p.q, in_row + d, p.input_f16, lo);
+    load8(p.q, in_row + d + half, p.input_f16, hi);
     if (p.rope) {
       const int pos = p.first_pos + t;
-      const float c = p.rope_cos[(size_t)pos * half + d];
-      const float s = p.rope_sin[(size_t)pos * half + d];
-      lo = rope_lo(a, b, c, s);
-      hi = rope_hi(a, b, c, s);
+      rope8(lo, hi, p.rope_cos + (size_t)pos * half, p.rope_sin + (size_t)pos * half, d);
     }
   }
   __half* o = p.qh + (((size_t)ll * p.heads + h) * p.n_tokens_padded + t) * p.head_dim;
-  o[d] = __float2half_rn(lo);
-  o[d + half] = __float2half_rn(hi);
+  *reinterpret_cast<uint4*>(o + d) = pack8(lo);
+  *reinterpret_cast<uint4*>(o + d + half) = pack8(hi);
 }
 
 }  // namespace
@@ -118,14 +154,14 @@ cudaError_t launch_rope_rows(float* values, const float* cos_row, const float* s
 }
 
 cudaError_t launch_append_rope(const AppendParams& p, cudaStream_t s) {
-  const long long total = (long long)p.n_layers * p.n_tokens * p.kv_heads * (p.head_dim / 2);
+  const long long total = (long long)p.n_layers * p.n_tokens * p.kv_heads * (p.head_dim / 16);
   if (total == 0) return cudaSuccess;
   append_rope_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_q_prep(const QPrepParams& p, cudaStream_t s) {
-  const long long total = (long long)p.n_layers * p.n_tokens_padded * p.heads * (p.head_dim / 2);
+  const long long total = (long long)p.n_layers * p.n_tokens_padded * p.heads * (p.head_dim / 16);
   if (total == 0) return cudaSuccess;
   q_prep_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(p);
   return cudaGetLastError();

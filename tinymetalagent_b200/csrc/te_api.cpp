@@ -547,6 +547,9 @@ TE_API te_status te_kv_append_rope(te_kv_cache* c, size_t layer_begin, size_t n_
     return fail(c->eng, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for te_kv_append_rope");
   }
   te_attn_engine* e = c->eng;
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "k and v must be 16-byte aligned");
+  }
   DeviceGuard dg(e->device);
   const int64_t first = c->len[seq];
   if ((uint64_t)(c->offset[seq] + first + n_tokens) > c->d.max_position) {
@@ -709,7 +712,7 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
     p.n_seqs = (int32_t)nb;
     p.seq_base = (int32_t)base;
     p.total_chunks = chunks;
-    const size_t part_bytes = n_layers * hkv * (size_t)chunks * G * (hd + 2) * sizeof(float);
+    const size_t part_bytes = n_layers * hkv * (size_t)chunks * G * decode_scratch_rec((int)hd) * sizeof(float);
     cudaError_t err = grow(e, reinterpret_cast<void**>(&e->partials), &e->partials_bytes, part_bytes, false);
     if (err == cudaSuccess) {
       size_t bytes = e->counters_count * sizeof(uint32_t);
@@ -723,6 +726,12 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
     err = launch_decode_f16(p, (int)hd, 0, e->stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "decode kernel launch");
     e->launches++;
+    for (size_t i = 0; i < nb; ++i) {
+      if (p.seqs[i].n_chunks > 1) {
+        e->launches++;  // the split-K combine kernel
+        break;
+      }
+    }
   }
 
   if (flags & TE_ATTN_HOST_BUFFERS) {
@@ -763,6 +772,10 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   const size_t hkv = c->d.kv_heads, hd = c->d.head_dim;
   if (heads % hkv != 0) return fail(e, TE_STATUS_INVALID_ARGUMENT, "heads must be a multiple of kv_heads");
   if (hd != 128) return fail(e, TE_STATUS_UNSUPPORTED, "prefill kernel is built for head_dim 128");
+  if (!(flags & TE_ATTN_HOST_BUFFERS) &&
+      ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "q, k and v must be 16-byte aligned");
+  }
   const size_t q_offset = (size_t)c->len[seq];
   const size_t total = q_offset + n_tokens;
   if (total > c->d.max_tokens_per_seq) return fail(e, TE_STATUS_INVALID_ARGUMENT, "sequence would exceed max_tokens_per_seq");

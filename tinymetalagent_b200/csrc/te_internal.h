@@ -28,12 +28,16 @@ struct SeqEntry {
 
 constexpr int kMaxParamSeqs = 64;  // sequences per decode launch
 
-// Largest split-K chunk count per (layer, sequence, kv head) that the decode
-// kernel's in-shared-memory combine table holds (per-chunk m and l of every
-// query head of the group, inside the 4-warp merge area).
+// Split-K bound per (layer, sequence, kv head): the combine kernel reads one
+// partial record per chunk; beyond this many chunks the host grows the chunk.
 inline size_t decode_max_chunks(int head_dim, int group) {
-  return ((size_t)4 * 16 * head_dim - 32) / (2 * (size_t)group);
+  (void)head_dim;
+  (void)group;
+  return 4096;
 }
+// Floats per split-K scratch record: acc[head_dim], m, l, two pad (16-byte aligned records).
+inline size_t decode_scratch_rec(int head_dim) { return (size_t)head_dim + 4; }
+
 constexpr int kStageTokens = 64;   // tokens per TMA stage
 
 struct DecodeParams {

@@ -73,6 +73,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Bounded wait whose outcome is the same in every lane of the (converged,
+// full) warp, for warps that go on to execute warp-collective instructions.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
+}
+
 // 2-D TMA tile load global -> shared, completion counted on `bar`.
 // x (innermost coordinate) must be a multiple of 16 bytes / element size.
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int32_t x, int32_t y) {
@@ -91,6 +97,13 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const void* tmap, ui
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
       "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
+}
+
+// 1-D bulk copy global -> shared (no multicast); addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {
