@@ -109,6 +109,12 @@ TE_API te_status te_kv_cache_seq_reset(te_kv_cache *cache, size_t seq, size_t po
  * (the reference's generation state only grows, c/src/qwen.c:376-392). */
 TE_API te_status te_kv_cache_seq_truncate(te_kv_cache *cache, size_t seq, size_t length);
 TE_API te_status te_kv_cache_seq_length(const te_kv_cache *cache, size_t seq, size_t *out_length);
+/* Maps pages so that sequence `seq` can grow to `tokens` tokens without any
+ * page-table upload later: a decode/append that stays within reserved pages
+ * issues only kernel launches and can be captured into a CUDA graph.  No
+ * reference counterpart (the reference allocates the whole context up front,
+ * c/src/qwen.c:458-486). */
+TE_API te_status te_kv_cache_reserve(te_kv_cache *cache, size_t seq, size_t tokens);
 /* Raw f16 rows (already rotated) into / out of tokens [token_begin, +n_tokens)
  * of one layer; `k`/`v` may be host or device pointers.  A write grows the
  * sequence's length to token_begin + n_tokens when that is larger. */

@@ -333,3 +333,54 @@ def test_decode_rejects_bad_arguments(engine):
     with pytest.raises(TinyEngineError):
         cache.decode(0, 2, [0], q, out, 8)          # layer range
     cache.close()
+
+
+def test_decode_steps_in_cuda_graph_match_eager():
+    """Decode steps captured in a CUDA graph (pages reserved first) give the eager results."""
+    import torch
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, AttnEngine
+    h, hkv, hd, L, n0, steps = 16, 2, 128, 3, 1000, 4
+    g = torch.Generator(device="cuda").manual_seed(3)
+    k0 = [(torch.randn((n0, hkv, hd), generator=g, device="cuda") * 0.5).half() for _ in range(L)]
+    v0 = [(torch.randn((n0, hkv, hd), generator=g, device="cuda") * 0.5).half() for _ in range(L)]
+    qs = [torch.randn((L, 1, h, hd), generator=g, device="cuda") for _ in range(steps)]
+    ks = [torch.randn((L, 1, hkv, hd), generator=g, device="cuda") for _ in range(steps)]
+    vs = [torch.randn((L, 1, hkv, hd), generator=g, device="cuda") for _ in range(steps)]
+    outs = {}
+    for mode in ("eager", "graph"):
+        eng = AttnEngine(0)
+        st = torch.cuda.ExternalStream(eng.stream)
+        cache = eng.kv_cache(layers=L, max_seqs=1, max_tokens_per_seq=n0 + steps, kv_heads=hkv, head_dim=hd)
+        torch.cuda.synchronize()
+        for layer in range(L):
+            cache.write_f16(layer, 0, 0, k0[layer], v0[layer])
+        cache.reserve(0, n0 + steps)
+        out = [torch.zeros((L, 1, h, hd), device="cuda") for _ in range(steps)]
+
+        def run():
+            for i in range(steps):
+                cache.decode(0, L, [0], qs[i], out[i], h, k_new=ks[i], v_new=vs[i], flags=TE_ATTN_ADVANCE)
+
+        if mode == "eager":
+            run()
+        else:
+            # warm the engine's scratch at the same shapes, then capture from the same start
+            run()
+            eng.synchronize()
+            cache.truncate(0, n0)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=st):
+                run()
+            for o in out:
+                o.zero_()
+            torch.cuda.synchronize()
+            with torch.cuda.stream(st):
+                graph.replay()
+            st.synchronize()
+            del graph
+        eng.synchronize()
+        outs[mode] = [o.clone() for o in out]
+        cache.close()
+        eng.close()
+    for a, b in zip(outs["eager"], outs["graph"]):
+        assert torch.equal(a, b)

@@ -88,27 +88,57 @@ __device__ __forceinline__ int k_chunk_of(int c, int j, int* box) {
   return per_thread * (c % threads_per_box) + ((j + c) % per_thread);
 }
 
-// One work item: a chunk of one (layer, sequence, kv head).
-struct Work {
-  int layer_local, kvh, si, cx, t0, t1, n_st;
+// Stream-K work: the stages of all (layer, kv head, sequence) groups are laid
+// end to end and CTA b owns the contiguous range [start(b), start(b+1)); a
+// segment is the part of that range inside one group.
+struct Seg {
+  int layer_local, kvh, si, gidx;  // gidx = (layer_local * kv_heads + kvh) * n_seqs + si
+  int t0, t1, n_st;                // tokens [t0, t1) of the group, in n_st stages
+  long long s_next;                // first stage after this segment
+  long long gs0, gs1;              // the group's stage range
 };
 
-__device__ __forceinline__ Work work_of(const DecodeParams& p, int it) {
-  Work w;
-  const int grp = it / p.total_chunks;  // layer_local * kv_heads + kvh
-  w.cx = it - grp * p.total_chunks;
-  w.layer_local = grp / p.kv_heads;
-  w.kvh = grp - w.layer_local * p.kv_heads;
+__device__ __forceinline__ Seg seg_at(const DecodeParams& p, long long s, long long s_end) {
+  Seg g;
+  const int blk = (int)(s / p.block_stages);
+  const int rem = (int)(s - (long long)blk * p.block_stages);
   int lo = 0, hi = p.n_seqs - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (p.seqs[mid].chunk_begin <= w.cx) lo = mid; else hi = mid - 1;
+    if (p.seqs[mid].stage_begin <= rem) lo = mid; else hi = mid - 1;
   }
-  w.si = lo;
-  w.t0 = (w.cx - p.seqs[lo].chunk_begin) * p.chunk_tokens;
-  w.t1 = min(p.seqs[lo].len, w.t0 + p.chunk_tokens);
-  w.n_st = (w.t1 - w.t0 + kStageTokens - 1) / kStageTokens;
-  return w;
+  g.si = lo;
+  g.layer_local = blk / p.kv_heads;
+  g.kvh = blk - g.layer_local * p.kv_heads;
+  g.gidx = blk * p.n_seqs + lo;
+  g.gs0 = (long long)blk * p.block_stages + p.seqs[lo].stage_begin;
+  g.gs1 = g.gs0 + p.seqs[lo].n_stages;
+  g.s_next = min(s_end, g.gs1);
+  g.t0 = (int)(s - g.gs0) * kStageTokens;
+  g.t1 = min(p.seqs[lo].len, (int)(g.s_next - g.gs0) * kStageTokens);
+  g.n_st = (int)(g.s_next - s);
+  return g;
+}
+
+// Final result of one query-head row, 4 dims at d: normalised output, or the
+// public partial record {acc[HD], m, l} when the caller asked for partials.
+template <int HD>
+__device__ __forceinline__ void store_result(const DecodeParams& p, size_t orow, int d, const float4& O, float M,
+                                             float L) {
+  if (!p.partial_out) {
+    const float inv = 1.f / L;
+    *reinterpret_cast<float4*>(p.out + orow * HD + d) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+  } else {
+    float* r = p.out + orow * (HD + 2);
+    *reinterpret_cast<float2*>(r + d) = make_float2(O.x, O.y);
+    *reinterpret_cast<float2*>(r + d + 2) = make_float2(O.z, O.w);
+    if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
+  }
+}
+
+// CTA owning stage s: the b with start(b) <= s < start(b + 1).
+__device__ __forceinline__ int cta_of(const DecodeParams& p, long long s) {
+  return (int)(((s + 1) * p.grid + p.total_stages - 1) / p.total_stages - 1);
 }
 
 // Persistent: one CTA per SM loops over work items (round-robin over the grid).
@@ -135,15 +165,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
   uint64_t* mready = fempty + 2; // [2] consumers -> helper
   uint64_t* mfree = mready + 2;  // [2] helper -> consumers
 
-  // The split-K combine (a dependent launch) may be scheduled now; it waits for this grid to finish.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int G = p.group;
   const int H = p.group * p.kv_heads;
-  const int n_items = p.n_layers * p.kv_heads * p.total_chunks;
+  const long long s_beg = stage_start(blockIdx.x, p.total_stages, p.grid);
+  const long long s_end = stage_start(blockIdx.x + 1, p.total_stages, p.grid);
 
   if (tid == 0) {
     for (int i = 0; i < R; ++i) {
@@ -171,8 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     const uint64_t policy = policy_evict_first();
     uint32_t sidx = 0, k = 0;
     bool ok = true;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
-      const Work w = work_of(p, it);
+    for (long long sg = s_beg; sg < s_end && ok; ++k) {
+      const Seg w = seg_at(p, sg, s_end);
+      sg = w.s_next;
       const SeqEntry se = p.seqs[w.si];
       const int layer = p.layer_begin + w.layer_local;
       if (lane == 0) {
@@ -275,11 +304,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     const int g = lane >> 2, c = lane & 3;  // the fragment owner this lane prepares for
     uint32_t k = 0;
     bool ok = true;
-    // fragments for the CTA's item number kk (all 32 lanes; warp-uniform waits)
-    auto prepare = [&](uint32_t kk, int it_k) -> bool {
+    // fragments for the CTA's segment number kk (all 32 lanes; warp-uniform waits)
+    auto prepare = [&](uint32_t kk) -> bool {
       const int b = kk & 1;
-      const Work w = work_of(p, it_k);
-      (void)w;
       if (!mbar_wait_warp(&qfull[b], (kk >> 1) & 1)) return false;
       if (kk >= 2 && !mbar_wait_warp(&fempty[b], ((kk >> 1) - 1) & 1)) return false;
       const float* sq = reinterpret_cast<const float*>(smem + C::kOffQ + b * C::kQBytes);
@@ -345,9 +372,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
       }
       return true;
     };
-    if (blockIdx.x < n_items) ok = prepare(0, blockIdx.x);
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
-      if (it + (int)gridDim.x < n_items && !prepare(k + 1, it + gridDim.x)) {
+    if (s_beg < s_end) ok = prepare(0);
+    for (long long sg = s_beg; sg < s_end && ok; ++k) {
+      const Seg w = seg_at(p, sg, s_end);
+      sg = w.s_next;
+      if (sg < s_end && !prepare(k + 1)) {
         ok = false;
         break;
       }
@@ -357,14 +386,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         ok = false;
         break;
       }
-      const Work w = work_of(p, it);
-      const SeqEntry se = p.seqs[w.si];
       const size_t qrow0 = (size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * H + w.kvh * G;
       const float* sm_o = reinterpret_cast<const float*>(smem + C::kOffMerge + b * C::kMergeBytes);
       const float* sm_m = reinterpret_cast<const float*>(smem + C::kOffML) + b * C::kMLFloats;
       const float* sm_l = sm_m + kConsumerWarps * 16;
-      const bool single = se.n_chunks == 1;
-      float* part = p.partials + ((size_t)(w.layer_local * p.kv_heads + w.kvh) * p.total_chunks + w.cx) * G * REC;
+      const int b_first = cta_of(p, w.gs0);
+      const int parts = cta_of(p, w.gs1 - 1) - b_first + 1;
+      const bool single = parts == 1;
+      float* part = p.partials + ((size_t)blockIdx.x * p.max_segs + k) * G * REC;
       constexpr int kLanesPerRow = HD / 4;        // float4 per lane
       constexpr int kRowStep = 32 / kLanesPerRow; // rows handled per pass
       const int d = 4 * (lane % kLanesPerRow);
@@ -389,19 +418,88 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
           O.z += o.z * wt;
           O.w += o.w * wt;
         }
-        if (single && !p.partial_out) {
-          const float inv = 1.f / L;
-          *reinterpret_cast<float4*>(p.out + (qrow0 + row) * HD + d) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
-        } else if (single) {
-          // public partial records are {acc[HD], m, l}
-          float* r = p.out + (qrow0 + row) * (HD + 2);
-          *reinterpret_cast<float2*>(r + d) = make_float2(O.x, O.y);
-          *reinterpret_cast<float2*>(r + d + 2) = make_float2(O.z, O.w);
-          if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
+        if (single) {
+          store_result<HD>(p, qrow0 + row, d, O, M, L);
         } else {
           float* r = part + (size_t)row * REC;
           *reinterpret_cast<float4*>(r + d) = O;
           if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
+        }
+      }
+      if (!single) {
+        // the last CTA of the group to finish merges the group's records
+        __syncwarp();
+        __threadfence();
+        int last = 0;
+        if (lane == 0) {
+          const uint32_t ticket = atomicAdd(&p.counters[w.gidx], 1u);
+          last = ticket == (uint32_t)(parts - 1);
+          if (last) p.counters[w.gidx] = 0u;  // every part has taken its ticket
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          // Part records of this group: CTA b_first + pp holds it as its segment
+          // jp = gidx - (group of its first stage).  Record offsets go to shared
+          // memory (the just-merged buffer b is still ours), then every load of
+          // all parts and rows is issued before any result is needed.
+          long long* off = reinterpret_cast<long long*>(smem + C::kOffMerge + b * C::kMergeBytes);
+          const int max_parts = C::kMergeBytes / (int)sizeof(long long);
+          if (parts > max_parts) {
+            set_error(p.error, 10);  // the host bounds the split so this cannot happen
+          } else {
+            for (int pp = lane; pp < parts; pp += 32) {
+              const int bp = b_first + pp;
+              const int jp = w.gidx - seg_at(p, stage_start(bp, p.total_stages, p.grid), p.total_stages).gidx;
+              off[pp] = ((long long)bp * p.max_segs + jp) * G * REC;
+            }
+            __syncwarp();
+            float M[GP / kRowStep], L[GP / kRowStep];
+            float4 O[GP / kRowStep];
+#pragma unroll
+            for (int u = 0; u < GP / kRowStep; ++u) {
+              M[u] = -INFINITY;
+              L[u] = 0.f;
+              O[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            for (int pp = 0; pp < parts; ++pp) {
+              const float* rec = p.partials + off[pp];
+#pragma unroll
+              for (int u = 0; u < GP / kRowStep; ++u) {
+                const int row = r0 + u * kRowStep;
+                if (row < G) M[u] = fmaxf(M[u], __ldcg(rec + (size_t)row * REC + HD));
+              }
+            }
+            for (int pp = 0; pp < parts; ++pp) {
+              const float* rec = p.partials + off[pp];
+              float2 ml[GP / kRowStep];
+              float4 o[GP / kRowStep];
+#pragma unroll
+              for (int u = 0; u < GP / kRowStep; ++u) {
+                const int row = r0 + u * kRowStep;
+                if (row < G) {
+                  ml[u] = __ldcg(reinterpret_cast<const float2*>(rec + (size_t)row * REC + HD));
+                  o[u] = __ldcg(reinterpret_cast<const float4*>(rec + (size_t)row * REC + d));
+                }
+              }
+#pragma unroll
+              for (int u = 0; u < GP / kRowStep; ++u) {
+                const int row = r0 + u * kRowStep;
+                if (row >= G) continue;
+                const float wt = ex2(ml[u].x - M[u]);
+                L[u] += ml[u].y * wt;
+                O[u].x += o[u].x * wt;
+                O[u].y += o[u].y * wt;
+                O[u].z += o[u].z * wt;
+                O[u].w += o[u].w * wt;
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < GP / kRowStep; ++u) {
+              const int row = r0 + u * kRowStep;
+              if (row < G) store_result<HD>(p, qrow0 + row, d, O[u], M[u], L[u]);
+            }
+          }
         }
       }
       __syncwarp();
@@ -417,8 +515,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
   const float sl = p.scale_log2;
   uint32_t sidx = 0, k = 0;
   bool failed = false;
-  for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++k) {
-    const Work w = work_of(p, it);
+  for (long long sg = s_beg; sg < s_end; ++k) {
+    const Seg w = seg_at(p, sg, s_end);
+    sg = w.s_next;
 
     // 1) query fragments prepared by the helper warp
     const int fb = k & 1;
@@ -581,60 +680,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
   }
 }
 
-// Split-K combine: one CTA per (layer, sequence, kv head, group of rows).
-// Runs as a programmatic dependent launch: its CTAs may be resident early and
-// wait here until the decode grid has finished and its writes are visible.
-template <int HD>
-__global__ void __launch_bounds__(128) decode_combine_kernel(const __grid_constant__ DecodeParams p) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  constexpr int REC = kScratchRec<HD>;
-  constexpr int kLanesPerRow = HD / 4;                 // float4 per lane
-  constexpr int kRowsPerCta = 128 / kLanesPerRow;
-  const int G = p.group;
-  const int row_groups = (G + kRowsPerCta - 1) / kRowsPerCta;
-  int b = blockIdx.x;
-  const int rg = b % row_groups;
-  b /= row_groups;
-  const int si = b % p.n_seqs;
-  b /= p.n_seqs;
-  const int kvh = b % p.kv_heads;
-  const int layer_local = b / p.kv_heads;
-  const SeqEntry se = p.seqs[si];
-  if (se.n_chunks <= 1) return;
-  const int row = rg * kRowsPerCta + threadIdx.x / kLanesPerRow;
-  if (row >= G) return;
-  const int d = 4 * (threadIdx.x % kLanesPerRow);
-  const int nc = se.n_chunks;
-  const float* grp = p.partials + ((size_t)(layer_local * p.kv_heads + kvh) * p.total_chunks + se.chunk_begin) * G * REC;
-  float M = -INFINITY;
-#pragma unroll 8
-  for (int kk = 0; kk < nc; ++kk) M = fmaxf(M, grp[((size_t)kk * G + row) * REC + HD]);
-  float L = 0.f;
-  float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-  for (int kk = 0; kk < nc; ++kk) {
-    const float* r = grp + ((size_t)kk * G + row) * REC;
-    const float2 ml = *reinterpret_cast<const float2*>(r + HD);
-    const float wt = ex2(ml.x - M);
-    const float4 o = *reinterpret_cast<const float4*>(r + d);
-    L += ml.y * wt;
-    O.x += o.x * wt;
-    O.y += o.y * wt;
-    O.z += o.z * wt;
-    O.w += o.w * wt;
-  }
-  const size_t orow = (size_t)(layer_local * p.seq_total + p.seq_base + si) * (G * p.kv_heads) + kvh * G + row;
-  if (p.partial_out) {
-    float* r = p.out + orow * (HD + 2);
-    *reinterpret_cast<float2*>(r + d) = make_float2(O.x, O.y);
-    *reinterpret_cast<float2*>(r + d + 2) = make_float2(O.z, O.w);
-    if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
-  } else {
-    const float inv = 1.f / L;
-    *reinterpret_cast<float4*>(p.out + orow * HD + d) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Generic fp32 decode used by the drop-in te_attention_decode_f32: any
 // head_dim, any group size, fp32 K/V in the reference's token-major layout.
@@ -737,39 +782,15 @@ __global__ void merge_partials_kernel(const float* __restrict__ partials, int n_
 template <int HD, int GP>
 cudaError_t launch_decode_impl(const DecodeParams& p, cudaStream_t s) {
   using C = DecodeCfg<HD, GP>;
-  static int sms = 0;  // per process (one device model)
-  static bool configured = false;
+  static bool configured = false;  // per process
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(decode_f16_kernel<HD, GP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
     if (e != cudaSuccess) return e;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     configured = true;
   }
-  const long long items = (long long)p.n_layers * p.kv_heads * p.total_chunks;
-  const int grid = (int)(items < sms ? items : sms);
-  decode_f16_kernel<HD, GP><<<grid, kThreads, C::kSmemBytes, s>>>(p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  bool any_split = false;
-  for (int i = 0; i < p.n_seqs; ++i) any_split |= p.seqs[i].n_chunks > 1;
-  if (!any_split) return cudaSuccess;
-  // split-K combine as a programmatic dependent launch (its CTAs wait for the decode grid)
-  constexpr int kRowsPerCta = 128 / (HD / 4);
-  const int row_groups = (p.group + kRowsPerCta - 1) / kRowsPerCta;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.n_layers * p.kv_heads * p.n_seqs * row_groups));
-  cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_combine_kernel<HD>, p);
+  decode_f16_kernel<HD, GP><<<p.grid, kThreads, C::kSmemBytes, s>>>(p);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -846,22 +867,10 @@ extern "C" __attribute__((visibility("default"))) te_status te_attention_decode_
   if (pages_needed > num_pages || rows >= (1ull << 31) || n_tokens > (size_t)INT32_MAX) {
     return TE_STATUS_INVALID_ARGUMENT;
   }
-  // Chunking: the partial records of all chunks must fit the fixed scratch and
-  // the kernel's in-shared-memory combine table.
-  const size_t rec_bytes = kv_heads * G * decode_scratch_rec((int)head_dim) * sizeof(float);
-  const size_t fit_chunks = kNoAllocPartialBytes / rec_bytes;
-  if (fit_chunks == 0) return TE_STATUS_UNSUPPORTED;
-  const size_t smem_chunks = decode_max_chunks((int)head_dim, (int)G);
-  const size_t max_chunks = std::min(fit_chunks, smem_chunks);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return TE_STATUS_RUNTIME_ERROR;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  size_t chunk = n_tokens * kv_heads / ((size_t)8 * sms);
-  chunk = std::min<size_t>(std::max<size_t>(chunk, 64), 4096);
-  chunk = std::max(chunk, (n_tokens + max_chunks - 1) / max_chunks);
-  chunk = (chunk + kStageTokens - 1) / kStageTokens * kStageTokens;
-  const size_t n_chunks = (n_tokens + chunk - 1) / chunk;
 
   void* base = nullptr;
   {
@@ -900,8 +909,6 @@ extern "C" __attribute__((visibility("default"))) te_status te_attention_decode_
   p.n_layers = 1;
   p.kv_heads = (int32_t)kv_heads;
   p.group = (int32_t)G;
-  p.chunk_tokens = (int32_t)chunk;
-  p.total_chunks = (int32_t)n_chunks;
   p.num_pages = (int32_t)num_pages;
   p.page_tokens = (int32_t)page_tokens;
   p.max_pages_per_seq = (int32_t)pages_needed;
@@ -912,7 +919,14 @@ extern "C" __attribute__((visibility("default"))) te_status te_attention_decode_
   p.seqs[0].len = (int32_t)n_tokens;
   p.seqs[0].q_pos = 0;
   p.seqs[0].new_pos = -1;
-  p.seqs[0].chunk_begin = 0;
-  p.seqs[0].n_chunks = (int32_t)n_chunks;
+  // Stream-K split whose partial records fit the fixed scratch.
+  const size_t rec_bytes = G * decode_scratch_rec((int)head_dim) * sizeof(float);
+  long long max_grid = sms;
+  plan_stream_k(p, max_grid);
+  while ((size_t)p.grid * p.max_segs * rec_bytes > kNoAllocPartialBytes && max_grid > 1) {
+    max_grid /= 2;
+    plan_stream_k(p, max_grid);
+  }
+  if ((size_t)p.grid * p.max_segs * rec_bytes > kNoAllocPartialBytes) return TE_STATUS_UNSUPPORTED;
   return launch_decode_f16(p, (int)head_dim, 0, s) == cudaSuccess ? TE_STATUS_OK : TE_STATUS_RUNTIME_ERROR;
 }

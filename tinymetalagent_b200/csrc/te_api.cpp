@@ -95,7 +95,8 @@ cudaError_t grow(te_attn_engine* e, void** buf, size_t* cap, size_t need, bool z
   if (*buf) cudaFree(*buf);
   *buf = nullptr;
   *cap = 0;
-  size_t sz = std::max(need, (size_t)1 << 20);
+  // geometric growth: a call that needs slightly more never reallocates each time
+  size_t sz = std::max(std::max(2 * need, 2 * *cap), (size_t)1 << 20);
   err = cudaMalloc(buf, sz);
   if (err != cudaSuccess) return err;
   if (zero) {
@@ -498,6 +499,12 @@ TE_API te_status te_kv_cache_seq_truncate(te_kv_cache* c, size_t seq, size_t len
   return TE_STATUS_OK;
 }
 
+TE_API te_status te_kv_cache_reserve(te_kv_cache* c, size_t seq, size_t tokens) {
+  if (!c || seq >= c->d.max_seqs) return TE_STATUS_INVALID_ARGUMENT;
+  DeviceGuard dg(c->eng->device);
+  return ensure_pages(c, seq, tokens);
+}
+
 TE_API te_status te_kv_cache_seq_length(const te_kv_cache* c, size_t seq, size_t* out_length) {
   if (!c || !out_length || seq >= c->d.max_seqs) return TE_STATUS_INVALID_ARGUMENT;
   *out_length = (size_t)c->len[seq];
@@ -631,21 +638,6 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
     }
   }
 
-  // Split-K chunk: a multiple of the 64-token stage, sized for ~8 CTAs per SM
-  // over the whole call, and large enough that one sequence's chunk count
-  // fits the in-kernel combine's shared-memory table.
-  size_t total_tok = 0;
-  for (auto& x : ent) total_tok += (size_t)x.len;
-  total_tok *= hkv * n_layers;
-  size_t chunk = e->decode_chunk;
-  if (chunk == 0) {
-    chunk = total_tok / ((size_t)8 * e->sm_count);
-    chunk = std::min<size_t>(std::max<size_t>(chunk, 64), 4096);
-  }
-  const size_t max_chunks = decode_max_chunks((int)hd, (int)G);
-  chunk = std::max(chunk, (max_len + max_chunks - 1) / max_chunks);
-  chunk = (chunk + kStageTokens - 1) / kStageTokens * kStageTokens;
-
   // Device staging for host buffers.
   const size_t q_elems = n_layers * n_seqs * heads * hd;
   const size_t kv_elems = n_layers * n_seqs * hkv * hd;
@@ -691,7 +683,6 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
   p.n_layers = (int32_t)n_layers;
   p.kv_heads = (int32_t)hkv;
   p.group = (int32_t)G;
-  p.chunk_tokens = (int32_t)chunk;
   p.num_pages = (int32_t)c->d.total_pages;
   p.page_tokens = (int32_t)c->d.page_tokens;
   p.max_pages_per_seq = (int32_t)c->pages_per_seq;
@@ -699,20 +690,22 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
   p.partial_out = (flags & TE_ATTN_PARTIAL) ? 1 : 0;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hd));
 
+  // Stream-K split over at most one CTA per SM, or over ranges of about
+  // decode_chunk_tokens tokens when the engine was given that hint.
   for (size_t base = 0; base < n_seqs; base += kMaxParamSeqs) {
     const size_t nb = std::min<size_t>(kMaxParamSeqs, n_seqs - base);
-    int32_t chunks = 0;
-    for (size_t i = 0; i < nb; ++i) {
-      SeqEntry x = ent[base + i];
-      x.chunk_begin = chunks;
-      x.n_chunks = (int32_t)((x.len + chunk - 1) / chunk);
-      chunks += x.n_chunks;
-      p.seqs[i] = x;
-    }
+    for (size_t i = 0; i < nb; ++i) p.seqs[i] = ent[base + i];
     p.n_seqs = (int32_t)nb;
     p.seq_base = (int32_t)base;
-    p.total_chunks = chunks;
-    const size_t part_bytes = n_layers * hkv * (size_t)chunks * G * decode_scratch_rec((int)hd) * sizeof(float);
+    long long max_grid = e->sm_count;
+    if (e->decode_chunk) {
+      long long tokens = 0;
+      for (size_t i = 0; i < nb; ++i) tokens += p.seqs[i].len;
+      tokens *= (long long)(n_layers * hkv);
+      max_grid = std::min<long long>(max_grid, std::max<long long>(1, (tokens + e->decode_chunk - 1) / e->decode_chunk));
+    }
+    plan_stream_k(p, max_grid);
+    const size_t part_bytes = (size_t)p.grid * p.max_segs * G * decode_scratch_rec((int)hd) * sizeof(float);
     cudaError_t err = grow(e, reinterpret_cast<void**>(&e->partials), &e->partials_bytes, part_bytes, false);
     if (err == cudaSuccess) {
       size_t bytes = e->counters_count * sizeof(uint32_t);
@@ -722,16 +715,9 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
     if (err != cudaSuccess) return cuda_fail(e, err, "decode scratch allocation");
     p.partials = e->partials;
     p.counters = e->counters;
-    if (n_layers * hkv > 65535u) return fail(e, TE_STATUS_UNSUPPORTED, "too many layers x kv heads in one call");
     err = launch_decode_f16(p, (int)hd, 0, e->stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "decode kernel launch");
     e->launches++;
-    for (size_t i = 0; i < nb; ++i) {
-      if (p.seqs[i].n_chunks > 1) {
-        e->launches++;  // the split-K combine kernel
-        break;
-      }
-    }
   }
 
   if (flags & TE_ATTN_HOST_BUFFERS) {

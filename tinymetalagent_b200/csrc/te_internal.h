@@ -22,19 +22,14 @@ struct SeqEntry {
   int32_t len;          // tokens attended (after the optional append)
   int32_t q_pos;        // RoPE position of the query
   int32_t new_pos;      // RoPE position of the appended token, or -1 (no append)
-  int32_t chunk_begin;  // first split-K chunk index of this sequence in the grid
-  int32_t n_chunks;     // number of split-K chunks
+  int32_t stage_begin;  // first 64-token stage of this sequence within a (layer, kv head) block
+  int32_t n_stages;     // ceil(len / 64)
 };
 
 constexpr int kMaxParamSeqs = 64;  // sequences per decode launch
 
-// Split-K bound per (layer, sequence, kv head): the combine kernel reads one
-// partial record per chunk; beyond this many chunks the host grows the chunk.
-inline size_t decode_max_chunks(int head_dim, int group) {
-  (void)head_dim;
-  (void)group;
-  return 4096;
-}
+// Stream-K split: CTA b of `grid` owns stages [stage_start(b), stage_start(b+1)).
+__host__ __device__ inline long long stage_start(long long b, long long total, long long grid) { return b * total / grid; }
 // Floats per split-K scratch record: acc[head_dim], m, l, two pad (16-byte aligned records).
 inline size_t decode_scratch_rec(int head_dim) { return (size_t)head_dim + 4; }
 
@@ -62,8 +57,10 @@ struct DecodeParams {
   int32_t n_layers;
   int32_t kv_heads;
   int32_t group;              // heads per kv head (<= 16)
-  int32_t chunk_tokens;       // multiple of kStageTokens
-  int32_t total_chunks;
+  int32_t block_stages;       // stages of one (layer, kv head) block: sum of n_stages
+  int32_t grid;               // CTAs sharing the stages (stream-K split)
+  int32_t max_segs;           // partial-record slots per CTA
+  long long total_stages;     // n_layers * kv_heads * block_stages
   int32_t num_pages;          // pages per layer
   int32_t page_tokens;
   int32_t max_pages_per_seq;
@@ -75,6 +72,41 @@ struct DecodeParams {
 
 // 2-D f16 tensor map over [rows][cols] (box box_rows x 64, 128B swizzle); false on failure.
 bool encode_tmap_f16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+
+// Plans the stream-K split of a decode launch: fills each sequence's stage
+// range (from its len), block_stages, total_stages, grid (<= max_grid CTAs,
+// at least one stage each) and max_segs (groups any one CTA touches).
+inline void plan_stream_k(DecodeParams& p, long long max_grid) {
+  int acc = 0;
+  for (int i = 0; i < p.n_seqs; ++i) {
+    p.seqs[i].n_stages = (p.seqs[i].len + kStageTokens - 1) / kStageTokens;
+    p.seqs[i].stage_begin = acc;
+    acc += p.seqs[i].n_stages;
+  }
+  p.block_stages = acc;
+  p.total_stages = (long long)p.n_layers * p.kv_heads * acc;
+  long long grid = max_grid < p.total_stages ? max_grid : p.total_stages;
+  if (grid < 1) grid = 1;
+  p.grid = (int32_t)grid;
+  auto gidx = [&](long long st) {
+    const long long blk = st / acc;
+    const int rem = (int)(st - blk * acc);
+    int lo = 0, hi = p.n_seqs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.seqs[mid].stage_begin <= rem) lo = mid; else hi = mid - 1;
+    }
+    return blk * p.n_seqs + lo;
+  };
+  long long segs = 1;
+  for (long long b = 0; b < grid; ++b) {
+    const long long s0 = stage_start(b, p.total_stages, grid);
+    const long long s1 = stage_start(b + 1, p.total_stages, grid) - 1;
+    const long long n = gidx(s1) - gidx(s0) + 1;
+    if (n > segs) segs = n;
+  }
+  p.max_segs = (int32_t)segs;
+}
 
 // Launchers (kernels live in the .cu files).  All return cudaError_t of the launch.
 cudaError_t launch_decode_f16(const DecodeParams& p, int head_dim, int stages, cudaStream_t s);

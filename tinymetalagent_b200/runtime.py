@@ -103,6 +103,7 @@ SIGNATURES: dict[str, tuple] = {
     "te_kv_cache_seq_reset": (_int, [_vp, _sz, _sz]),
     "te_kv_cache_seq_truncate": (_int, [_vp, _sz, _sz]),
     "te_kv_cache_seq_length": (_int, [_vp, _sz, ctypes.POINTER(_sz)]),
+    "te_kv_cache_reserve": (_int, [_vp, _sz, _sz]),
     "te_kv_cache_write_f16": (_int, [_vp, _sz, _sz, _sz, _sz, _vp, _vp]),
     "te_kv_cache_read_f16": (_int, [_vp, _sz, _sz, _sz, _sz, _vp, _vp]),
     "te_kv_append_rope": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _sz, ctypes.c_uint32]),
@@ -277,6 +278,10 @@ class KVCache:
 
     def truncate(self, seq: int, length: int) -> None:
         self._c(self.lib.te_kv_cache_seq_truncate(self.handle, seq, length))
+
+    def reserve(self, seq: int, tokens: int) -> None:
+        """Map pages for `tokens` tokens now (graph-capturable decode steps afterwards)."""
+        self._c(self.lib.te_kv_cache_reserve(self.handle, seq, tokens))
 
     def length(self, seq: int) -> int:
         n = _sz()
