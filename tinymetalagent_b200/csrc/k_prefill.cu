@@ -8,22 +8,26 @@
 // (c/src/metal/metal_kernels.metal.inc:2693-2836, causal test
 // c/tests/kernel_ops.c:678-741).
 //
-// One work item = (layer, query head, 128-query tile); items are ordered by
-// decreasing causal length and dealt round-robin to a persistent grid of one
-// CTA per SM.  Warp roles (192 threads):
-//   warp 0     TMA producer: Q tiles (double-buffered, so the next item's Q
-//              is prefetched), K/V tiles (128 keys) into a 2-stage ring
-//   warp 1     TMEM owner; lane 0 issues tcgen05.mma:
-//                S[sb] = Q K^T   (M=128 queries, N=128 keys, K=128 dims, f16 -> f32 in TMEM)
-//                O    += P V     (M=128 queries, N=128 dims,  K=128 keys)
-//   warps 2-5  softmax + epilogue, one query row per thread (TMEM lane): read S
-//              with tcgen05.ld, causal mask, online softmax in exp2 domain, P
-//              (f16) to shared memory in the 128B-swizzled K-major layout the
-//              MMA reads; O is rescaled in TMEM only when the running max grows
-//              by more than 2^8 (exact: l uses the same reference max).
-// S is double-buffered in TMEM so Q K^T of tile j+1 overlaps the softmax of
-// tile j, and P V of tile j overlaps the softmax of tile j+1.
-// Operands are staged by TMA with 128-byte swizzle (no multicast).
+// One work item = (layer, kv head, pair of query heads of that GQA group,
+// 128-query tile).  Both heads attend exactly the same keys, so every K/V tile
+// staged by TMA feeds four MMAs (an odd group's last head is a single-head
+// item).  Items are ordered by decreasing causal length and dealt round-robin
+// to a persistent grid of one CTA per SM.
+//
+// Warp roles (320 threads):
+//   warp 0      TMA producer: the Q tiles, then K/V tiles (128 keys) into a 2-stage ring
+//   warp 1      TMEM owner; lane 0 issues tcgen05.mma in the order
+//                 QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) | ...
+//               (S = Q K^T: M=128 queries, N=128 keys, K=128 dims, A/B from shared
+//                memory; O += P V: A = P from tensor memory, B = V from shared memory)
+//   warps 2-5   softmax + epilogue of head A, one query row per thread (TMEM lane)
+//   warps 6-9   softmax + epilogue of head B
+// Tensor memory: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512) columns;
+// P (f16, two per 32-bit column) overwrites the first 64 columns of its S once
+// S has been read.  tcgen05.mma operations of one thread execute in issue
+// order, so the next Q K^T into S starts only after the P V that reads P
+// there.  O is rescaled in TMEM only when a row's running max grows by more
+// than 2^8 (exact: l uses the same reference max).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -41,34 +45,41 @@ constexpr int HD = 128;                     // head dim
 constexpr int kTile = BM * HD * 2;          // 32 KiB: 128 rows x 128 f16, as two 64-column halves
 constexpr int kHalf = kTile / 2;            // 16 KiB: 128 rows x 128 B
 constexpr int kBox = 64 * 128;              // 8 KiB TMA box: 64 rows x 64 f16
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 
-constexpr int OFF_Q = 0;                    // two Q buffers (the next item's Q is prefetched)
-constexpr int OFF_KV = OFF_Q + 2 * kTile;   // stage s: K at OFF_KV + s*2*kTile, V at + kTile
-constexpr int OFF_P = OFF_KV + 4 * kTile;
-constexpr int OFF_BAR = OFF_P + kTile;      // 229376
+constexpr int OFF_QA = 0;
+constexpr int OFF_QB = kTile;
+constexpr int OFF_KV = 2 * kTile;           // stage s: K at OFF_KV + s*2*kTile, V at + kTile
+constexpr int OFF_BAR = OFF_KV + 4 * kTile; // 196608
 constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
 
 enum Bar {
-  Q_FULL0 = 0, Q_FULL1, Q_EMPTY0, Q_EMPTY1, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1,
-  S_FULL0, S_FULL1, S_EMPTY0, S_EMPTY1, P_FULL, PV_DONE, O_EMPTY, DRAIN, kNumBars
+  Q_FULL = 0, Q_EMPTY, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1,
+  S_FULL_A, S_FULL_B, P_FULL_A, P_FULL_B, O_FULL_A, O_FULL_B, O_EMPTY_A, O_EMPTY_B, DRAIN, kNumBars
 };
 
-constexpr uint32_t kTmemCols = 512;         // S0 [0,128), S1 [128,256), O [256,384)
-constexpr uint32_t kColO = 256;
+constexpr uint32_t kTmemCols = 512;
+__device__ __forceinline__ uint32_t col_s(int t) { return t ? 128u : 0u; }
+__device__ __forceinline__ uint32_t col_o(int t) { return t ? 384u : 256u; }
 
 struct Item {
-  int layer_local, head, qt, n_kv;
+  int layer_local, kvh, head_a, has_b, qt, n_kv;
 };
 
 __device__ __forceinline__ Item item_of(const PrefillParams& p, int it) {
-  const int per_qt = p.n_layers * p.heads;
+  const int G = p.heads / p.kv_heads;
+  const int pairs = (G + 1) / 2;
+  const int per_qt = p.n_layers * p.kv_heads * pairs;
   const int n_qt = p.n_tokens_padded / BM;
   Item I;
-  I.qt = n_qt - 1 - it / per_qt;            // longest causal rows first
-  const int r = it % per_qt;
-  I.layer_local = r / p.heads;
-  I.head = r % p.heads;
+  I.qt = n_qt - 1 - it / per_qt;  // longest causal rows first
+  int r = it % per_qt;
+  const int pr = r % pairs;
+  r /= pairs;
+  I.kvh = r % p.kv_heads;
+  I.layer_local = r / p.kv_heads;
+  I.head_a = I.kvh * G + 2 * pr;
+  I.has_b = 2 * pr + 1 < G;
   const int total = p.q_offset + p.n_tokens;
   const int last_key = min(p.q_offset + (I.qt + 1) * BM, total);  // keys [0, last_key)
   I.n_kv = (last_key + BN - 1) / BN;
@@ -76,6 +87,27 @@ __device__ __forceinline__ Item item_of(const PrefillParams& p, int it) {
 }
 
 __device__ __forceinline__ bool aborted(volatile int* flag) { return *flag != 0; }
+
+// tcgen05.st of 16 packed f16 pairs to this thread's lane.
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&u)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7]),
+        "r"(u[8]), "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15])
+      : "memory");
+}
+
+// O (+)= P V with P (f16) in tensor memory as the A operand.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -88,18 +120,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
+    mbar_init(&bar[Q_FULL], 1);
+    mbar_init(&bar[Q_EMPTY], 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&bar[Q_FULL0 + s], 1);
-      mbar_init(&bar[Q_EMPTY0 + s], 1);
       mbar_init(&bar[K_FULL0 + s], 1);
       mbar_init(&bar[V_FULL0 + s], 1);
       mbar_init(&bar[KV_EMPTY0 + s], 1);
-      mbar_init(&bar[S_FULL0 + s], 1);
-      mbar_init(&bar[S_EMPTY0 + s], 4);
+      mbar_init(&bar[S_FULL_A + s], 1);
+      mbar_init(&bar[P_FULL_A + s], 4);
+      mbar_init(&bar[O_FULL_A + s], 1);
+      mbar_init(&bar[O_EMPTY_A + s], 4);
     }
-    mbar_init(&bar[P_FULL], 4);
-    mbar_init(&bar[PV_DONE], 1);
-    mbar_init(&bar[O_EMPTY], 4);
     mbar_init(&bar[DRAIN], 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -113,7 +144,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int total = p.q_offset + p.n_tokens;
-  const int G = p.heads / p.kv_heads;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -124,33 +154,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       prefetch_tmap(&p.tmap_k);
       prefetch_tmap(&p.tmap_v);
     }
-    uint32_t qc = 0, kc = 0;
+    uint32_t ic = 0, kc = 0;
     bool ok = true;
-    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
-      // one lane reads the abort flag so the whole warp takes the same branch
+    for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x, ++ic) {
       if (__shfl_sync(0xffffffffu, lane == 0 && aborted(abort_flag) ? 1 : 0, 0)) break;
       const Item I = item_of(p, it);
-      const int qs = qc & 1;
       if (lane == 0) {
-        if (!mbar_wait(&bar[Q_EMPTY0 + qs], ((qc >> 1) & 1) ^ 1)) {
+        if (!mbar_wait(&bar[Q_EMPTY], (ic & 1) ^ 1)) {
           set_error(p.error, 11);
           ok = false;
         } else {
-          mbar_arrive_expect_tx(&bar[Q_FULL0 + qs], kTile);
-          const int qrow = (I.layer_local * p.heads + I.head) * p.n_tokens_padded + I.qt * BM;
+          mbar_arrive_expect_tx(&bar[Q_FULL], I.has_b ? 2 * kTile : kTile);
+          for (int t = 0; t < 1 + I.has_b; ++t) {
+            const int qrow = (I.layer_local * p.heads + I.head_a + t) * p.n_tokens_padded + I.qt * BM;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
+            for (int h = 0; h < 2; ++h)
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
-              tma_load_2d(smem + OFF_Q + qs * kTile + c * kHalf + h * kBox, &p.tmap_q, &bar[Q_FULL0 + qs], c * 64,
-                          qrow + h * 64);
+              for (int c = 0; c < 2; ++c)
+                tma_load_2d(smem + (t ? OFF_QB : OFF_QA) + c * kHalf + h * kBox, &p.tmap_q, &bar[Q_FULL], c * 64,
+                            qrow + h * 64);
+          }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
-      ++qc;
       const int layer = p.layer_begin + I.layer_local;
-      const int kvh = I.head / G;
       int pg_batch = -1, pg_reg = 0;
       for (int j = 0; j < I.n_kv; ++j, ++kc) {
         const int s = kc & 1;
@@ -177,7 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int tok = j * BN + h * 64;
-              const int row = ((layer * p.num_pages + pages[h]) * p.kv_heads + kvh) * p.page_tokens + (tok % p.page_tokens);
+              const int row = ((layer * p.num_pages + pages[h]) * p.kv_heads + I.kvh) * p.page_tokens +
+                              (tok % p.page_tokens);
 #pragma unroll
               for (int c = 0; c < 2; ++c) {
                 tma_load_2d(ks + c * kHalf + h * kBox, &p.tmap_k, &bar[K_FULL0 + s], c * 64, row);
@@ -193,9 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     if (!ok) *abort_flag = 1;
     // Leave no copy in flight: the last Q and K/V stages have landed (immediate when consumed).
     if (lane == 0) {
-      for (uint32_t j = qc >= 2 ? qc - 2 : 0; j < qc; ++j) {
-        if (!mbar_wait(&bar[Q_FULL0 + (j & 1)], (j >> 1) & 1)) set_error(p.error, 13);
-      }
+      if (ic > 0 && !mbar_wait(&bar[Q_FULL], (ic - 1) & 1)) set_error(p.error, 13);
       for (uint32_t k = (kc >= 2 ? kc - 2 : 0); k < kc; ++k) {
         if (!mbar_wait(&bar[K_FULL0 + (k & 1)], (k >> 1) & 1)) set_error(p.error, 14);
         if (!mbar_wait(&bar[V_FULL0 + (k & 1)], (k >> 1) & 1)) set_error(p.error, 14);
@@ -206,61 +233,64 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16_f32(BM, BN, false, false);
       constexpr uint32_t idesc_pv = idesc_f16_f32(BM, HD, false, true);
-      const uint32_t sp = smem_u32(smem + OFF_P);
-      uint32_t qc = 0, kc = 0, sc = 0, pc = 0, oc = 0;
+      const uint32_t sq[2] = {smem_u32(smem + OFF_QA), smem_u32(smem + OFF_QB)};
+      uint32_t ic = 0, kc = 0;
+      uint32_t pc[2] = {0, 0};  // P tiles consumed per head slot
+      uint32_t oc[2] = {0, 0};  // items (with that head slot) started
       bool ok = true;
-      for (int it = blockIdx.x; it < p.n_items && ok && !aborted(abort_flag); it += gridDim.x) {
-        const Item I = item_of(p, it);
-        const int qs = qc & 1;
-        if (!mbar_wait(&bar[Q_FULL0 + qs], (qc >> 1) & 1)) { ok = false; break; }
+      auto wait = [&](int b, uint32_t parity) -> bool {
+        if (!mbar_wait(&bar[b], parity)) return false;
         tc_fence_after();
-        const uint32_t sq = smem_u32(smem + OFF_Q + qs * kTile);
-        const uint32_t kc0 = kc;
-        auto do_pv = [&](int jj) -> bool {
-          const uint32_t k_idx = kc0 + jj;
-          const int s = k_idx & 1;
-          if (!mbar_wait(&bar[P_FULL], pc & 1)) return false;
-          if (jj == 0 && !mbar_wait(&bar[O_EMPTY], (oc & 1) ^ 1)) return false;
-          if (!mbar_wait(&bar[V_FULL0 + s], (k_idx >> 1) & 1)) return false;
-          tc_fence_after();
-          const uint32_t sv = smem_u32(smem + OFF_KV + s * 2 * kTile + kTile);
+        return true;
+      };
+      auto qk = [&](int t, uint32_t k_idx) {
+        const uint32_t sk = smem_u32(smem + OFF_KV + (k_idx & 1) * 2 * kTile);
 #pragma unroll
-          for (int k = 0; k < BN / 16; ++k) {
-            const uint64_t a = smem_desc_sw128(sp + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
-            const uint64_t b = smem_desc_sw128(sv + k * 2048, kHalf, 1024);
-            umma_f16(tmem + kColO, a, b, idesc_pv, (jj > 0 || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&bar[PV_DONE]);
-          umma_commit(&bar[KV_EMPTY0 + s]);
-          ++pc;
-          return true;
-        };
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint64_t a = smem_desc_sw128(sq[t] + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
+          const uint64_t b = smem_desc_sw128(sk + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
+          umma_f16(tmem + col_s(t), a, b, idesc_qk, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar[S_FULL_A + t]);
+      };
+      auto pv = [&](int t, uint32_t k_idx, int j) {
+        const uint32_t sv = smem_u32(smem + OFF_KV + (k_idx & 1) * 2 * kTile + kTile);
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k) {
+          const uint64_t b = smem_desc_sw128(sv + k * 2048, kHalf, 1024);
+          umma_f16_ts(tmem + col_o(t), tmem + col_s(t) + k * 8, b, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        }
+      };
+      for (int it = blockIdx.x; it < p.n_items && ok && !aborted(abort_flag); it += gridDim.x, ++ic) {
+        const Item I = item_of(p, it);
+        const int nt = 1 + I.has_b;
+        const uint32_t kc0 = kc;
+        if (!wait(Q_FULL, ic & 1) || !wait(K_FULL0 + (kc0 & 1), (kc0 >> 1) & 1)) { ok = false; break; }
+        for (int t = 0; t < nt; ++t) qk(t, kc0);
+        if (I.n_kv == 1) umma_commit(&bar[Q_EMPTY]);
         for (int j = 0; j < I.n_kv && ok; ++j) {
           const uint32_t k_idx = kc0 + j;
           const int s = k_idx & 1;
-          const int sb = sc & 1;
-          if (!mbar_wait(&bar[K_FULL0 + s], (k_idx >> 1) & 1) ||
-              !mbar_wait(&bar[S_EMPTY0 + sb], ((sc >> 1) & 1) ^ 1)) {
-            ok = false;
-            break;
+          for (int t = 0; t < nt; ++t) {
+            if (!wait(P_FULL_A + t, pc[t] & 1) || (j == 0 && !wait(O_EMPTY_A + t, (oc[t] & 1) ^ 1)) ||
+                !wait(V_FULL0 + s, (k_idx >> 1) & 1)) {
+              ok = false;
+              break;
+            }
+            ++pc[t];
+            pv(t, k_idx, j);
+            if (t == nt - 1) umma_commit(&bar[KV_EMPTY0 + s]);  // every P V of tile j issued: stage free on completion
+            if (j + 1 < I.n_kv) {
+              if (t == 0 && !wait(K_FULL0 + ((k_idx + 1) & 1), ((k_idx + 1) >> 1) & 1)) { ok = false; break; }
+              qk(t, k_idx + 1);
+              if (j + 2 == I.n_kv && t == nt - 1) umma_commit(&bar[Q_EMPTY]);
+            } else {
+              umma_commit(&bar[O_FULL_A + t]);
+              ++oc[t];
+            }
           }
-          tc_fence_after();
-          const uint32_t sk = smem_u32(smem + OFF_KV + s * 2 * kTile);
-#pragma unroll
-          for (int k = 0; k < HD / 16; ++k) {
-            const uint64_t a = smem_desc_sw128(sq + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
-            const uint64_t b = smem_desc_sw128(sk + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
-            umma_f16(tmem + sb * BN, a, b, idesc_qk, k > 0 ? 1u : 0u);
-          }
-          umma_commit(&bar[S_FULL0 + sb]);
-          ++sc;
-          if (j == I.n_kv - 1) umma_commit(&bar[Q_EMPTY0 + qs]);
-          if (j >= 1 && !do_pv(j - 1)) ok = false;
         }
-        if (ok && !do_pv(I.n_kv - 1)) ok = false;
         kc = kc0 + I.n_kv;
-        ++qc;
-        ++oc;
       }
       if (!ok) { set_error(p.error, 15); *abort_flag = 1; }
       // Every MMA this thread issued has completed before TMEM is released.
@@ -269,106 +299,99 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
+    const int t = warp >= 6 ? 1 : 0;  // which head of the pair
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-    const uint32_t sp = smem_u32(smem + OFF_P);
+    const uint32_t s_addr = tmem + lane_addr + col_s(t);
+    const uint32_t o_addr = tmem + lane_addr + col_o(t);
     const float sl = p.scale_log2;
-    uint32_t sc = 0, pc = 0;
+    uint32_t sc = 0, oc = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
       if (__any_sync(0xffffffffu, aborted(abort_flag))) break;
       const Item I = item_of(p, it);
+      if (t == 1 && !I.has_b) continue;
       const int q_pos = p.q_offset + I.qt * BM + row;
       const int key_limit = min(q_pos, total - 1);
       const int first_row_limit = min(p.q_offset + I.qt * BM, total - 1);
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < I.n_kv; ++j) {
-        const int sb = sc & 1;
-        if (!mbar_wait_warp(&bar[S_FULL0 + sb], (sc >> 1) & 1)) { ok = false; break; }
-        tc_fence_after();
-        float s[BN];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(tmem + lane_addr + sb * BN + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
-        }
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar[S_EMPTY0 + sb]);
+        if (!mbar_wait_warp(&bar[S_FULL_A + t], sc & 1)) { ok = false; break; }
         ++sc;
+        tc_fence_after();
         const bool need_mask = (j + 1) * BN - 1 > first_row_limit;
+        // the row's 128 scores: four loads in flight, one wait
+        float x[BN];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<float(*)[32]>(&x[c * 32]));
+        tmem_wait_ld();
         if (need_mask) {
 #pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            if (j * BN + c > key_limit) s[c] = -INFINITY;
+          for (int e = 0; e < BN; ++e) {
+            if (j * BN + e > key_limit) x[e] = -INFINITY;
           }
         }
-        // row max of the raw scores: 8 independent partial maxima, then a tree
+        // row max of the raw scores (8 independent partial maxima)
         float pm[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) pm[u] = s[u];
+        for (int u = 0; u < 8; ++u) pm[u] = x[u];
 #pragma unroll
-        for (int c = 8; c < BN; ++c) pm[c & 7] = fmaxf(pm[c & 7], s[c]);
+        for (int e = 8; e < BN; ++e) pm[e & 7] = fmaxf(pm[e & 7], x[e]);
         const float tmax_raw = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                                      fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
         const float m_new = fmaxf(m, tmax_raw * sl);  // scaling by sl > 0 preserves the max
-        if (pc > 0) {  // P buffer free and O stable: the previous P V finished
-          if (!mbar_wait_warp(&bar[PV_DONE], (pc - 1) & 1)) { ok = false; break; }
-          tc_fence_after();
-        }
-        if (j == 0) {
-          m = m_new;
-        } else if (m_new > m + 8.f) {
-          const float alpha = ex2(m - m_new);
-          l *= alpha;
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            float o[32];
-            tmem_ld32(tmem + lane_addr + kColO + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] *= alpha;
-            tmem_st32(tmem + lane_addr + kColO + c * 32, o);
-          }
-          tmem_wait_st();
-          m = m_new;
-        }
-        // p = 2^(s*scale - m): one FFMA + one SFU op per score; 8 partial sums
+        // lazy rescale: keep the old reference max unless the row max grew by > 2^8
+        const bool rescale = j > 0 && m_new > m + 8.f;
+        const float alpha = rescale ? ex2(m - m_new) : 1.f;
+        if (j == 0 || rescale) m = m_new;
+        // p = 2^(s*scale - m) -> f16 pairs over the first half of S's columns
+        // (S is entirely in registers, so overwriting its columns is safe)
         const float neg_m = -m;
         float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const float e = ex2(fmaf(s[c], sl, neg_m));
-          s[c] = e;
-          ps[c & 7] += e;
-        }
-        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-        l += rs;
-        // P row -> shared memory, 128B-swizzled K-major (two 64-key halves).
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int ch = 0; ch < BN / 8; ++ch) {
-          const uint32_t addr = sp + (ch >> 3) * kHalf + row * 128 + ((((ch & 7) ^ (row & 7))) << 4);
-          sts128(addr, pack_half2(s[ch * 8 + 0], s[ch * 8 + 1]), pack_half2(s[ch * 8 + 2], s[ch * 8 + 3]),
-                 pack_half2(s[ch * 8 + 4], s[ch * 8 + 5]), pack_half2(s[ch * 8 + 6], s[ch * 8 + 7]));
+          for (int e = 0; e < 32; e += 2) {
+            const float e0 = ex2(fmaf(x[c * 32 + e], sl, neg_m));
+            const float e1 = ex2(fmaf(x[c * 32 + e + 1], sl, neg_m));
+            ps[e & 7] += e0;
+            ps[(e + 1) & 7] += e1;
+            pk[e >> 1] = pack_half2(e0, e1);
+          }
+          tmem_st16u(s_addr + c * 16, pk);
         }
-        fence_proxy_async_shared();
+        l = l * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
+        if (rescale) {
+          // O is stable: the commit that signalled this S tracks the previous P V too
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            float o[32];
+            tmem_ld32(o_addr + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(o_addr + c * 32, o);
+          }
+        }
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bar[P_FULL]);
-        ++pc;
+        if (lane == 0) mbar_arrive(&bar[P_FULL_A + t]);
       }
       if (!ok) break;
       // epilogue: O / l -> out[layer][token][head][:]
-      if (!mbar_wait_warp(&bar[PV_DONE], (pc - 1) & 1)) { ok = false; break; }
+      if (!mbar_wait_warp(&bar[O_FULL_A + t], oc & 1)) { ok = false; break; }
+      ++oc;
       tc_fence_after();
       const int tok = I.qt * BM + row;
       const float inv = 1.f / l;
-      float* dst = p.out + (((size_t)I.layer_local * p.n_tokens + tok) * p.heads + I.head) * HD;
+      float* dst = p.out + (((size_t)I.layer_local * p.n_tokens + tok) * p.heads + I.head_a + t) * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         float o[32];
-        tmem_ld32(tmem + lane_addr + kColO + c * 32, o);
+        tmem_ld32(o_addr + c * 32, o);
         tmem_wait_ld();
         if (tok < p.n_tokens) {
 #pragma unroll
@@ -380,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[O_EMPTY]);
+      if (lane == 0) mbar_arrive(&bar[O_EMPTY_A + t]);
     }
     if (!ok) { set_error(p.error, 17); *abort_flag = 1; }
   }
@@ -392,6 +415,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 }
 
 }  // namespace
+
+int prefill_items(int n_layers, int heads, int kv_heads, int n_tokens_padded) {
+  const int G = heads / kv_heads;
+  return n_layers * kv_heads * ((G + 1) / 2) * (n_tokens_padded / BM);
+}
 
 cudaError_t launch_prefill_tc(const PrefillParams& p, int sm_count, cudaStream_t s) {
   static bool configured = false;

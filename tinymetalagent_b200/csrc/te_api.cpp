@@ -769,7 +769,7 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
     return fail(e, TE_STATUS_INVALID_ARGUMENT, "RoPE position beyond max_position");
   }
   const size_t n_pad = (n_tokens + 127) / 128 * 128;
-  const size_t items = n_layers * heads * (n_pad / 128);
+  const size_t items = (size_t)prefill_items((int)n_layers, (int)heads, (int)hkv, (int)n_pad);
   const size_t qh_rows = n_layers * heads * n_pad;
   if (items > (size_t)INT32_MAX || qh_rows >= (1ull << 31)) return fail(e, TE_STATUS_UNSUPPORTED, "prefill too large");
   DeviceGuard dg(e->device);

@@ -178,5 +178,7 @@ struct PrefillParams {
   float scale_log2;
 };
 cudaError_t launch_prefill_tc(const PrefillParams& p, int sm_count, cudaStream_t s);
+// Work items of the prefill kernel: (layer, kv head, query-head pair, 128-query tile).
+int prefill_items(int n_layers, int heads, int kv_heads, int n_tokens_padded);
 
 }  // namespace te
