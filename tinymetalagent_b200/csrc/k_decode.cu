@@ -35,7 +35,7 @@ namespace te {
 namespace {
 
 constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 2) * 32;  // + producer warp + helper warp
+constexpr int kThreads = (kConsumerWarps + 3) * 32;  // + producer, helper and appender warps
 constexpr int kBoxBytes = kStageTokens * 64 * 2;  // 64 tokens x 64 dims x f16
 
 // Shared-memory plan for head dim HD and GP = 8 or 16 padded query rows per
@@ -56,14 +56,19 @@ struct DecodeCfg {
   static constexpr int kCSBytes = HD * 4;                  // one buffer: cos row + sin row
   static constexpr int kFragBytes = kKSteps * 4 * 4 * 32;  // one buffer: f16 query fragments of a warp
   static constexpr int kMLFloats = 2 * kConsumerWarps * 16;  // one buffer: m[4][16], l[4][16]
+  static constexpr int kNewBytes = 3 * HD * 4;             // one buffer: new token's raw k, v, and cos/sin row
+  static constexpr int kResBytes = (16 + HD) * 4;          // one buffer: new token's scores[16], v[HD] (as cached)
   static constexpr int kOffMerge = kRing * kStageBytes;
   static constexpr int kOffQ = kOffMerge + 2 * kMergeBytes;
   static constexpr int kOffCS = kOffQ + 2 * kQBytes;
   static constexpr int kOffFrag = kOffCS + 2 * kCSBytes;
   static constexpr int kOffML = kOffFrag + 2 * kFragBytes;
-  static constexpr int kOffBar = kOffML + 2 * kMLFloats * 4;
-  static constexpr int kNumBars = 2 * kRing + 12;  // full, empty, then [2] each: qfull qempty fready fempty mready mfree
+  static constexpr int kOffNew = kOffML + 2 * kMLFloats * 4;
+  static constexpr int kOffRes = kOffNew + 2 * kNewBytes;
+  static constexpr int kOffBar = kOffRes + 2 * kResBytes;
+  static constexpr int kNumBars = 2 * kRing + 14;  // full, empty, then [2] each: qfull qempty fready fempty mready mfree nready
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
 };
 
 // Split-K partial records in scratch: { acc[HD], m, l, pad, pad } so every
@@ -90,17 +95,21 @@ __device__ __forceinline__ int k_chunk_of(int c, int j, int* box) {
 
 // Stream-K work: the stages of all (layer, kv head, sequence) groups are laid
 // end to end and CTA b owns the contiguous range [start(b), start(b+1)); a
-// segment is the part of that range inside one group.
+// segment is the part of that range inside one group.  A CTA walks its range
+// from the end: a group's newest stage (the one the fused append writes) sits
+// at the start of a range, so the append's small loads, which would wait
+// behind the kernel's initial K/V burst, come after the CTA's other segments.
 struct Seg {
   int layer_local, kvh, si, gidx;  // gidx = (layer_local * kv_heads + kvh) * n_seqs + si
   int t0, t1, n_st;                // tokens [t0, t1) of the group, in n_st stages
-  long long s_next;                // first stage after this segment
+  long long s_begin;               // first stage of this segment (where the next one processed ends)
   long long gs0, gs1;              // the group's stage range
 };
 
-__device__ __forceinline__ Seg seg_at(const DecodeParams& p, long long s, long long s_end) {
+// The group holding stage s (fills si, layer_local, kvh, gidx, gs0, gs1).
+__device__ __forceinline__ Seg group_at(const DecodeParams& p, long long s) {
   Seg g;
-  const int blk = (int)(s / p.block_stages);
+  const int blk = (int)div_nonneg(s, p.block_stages);
   const int rem = (int)(s - (long long)blk * p.block_stages);
   int lo = 0, hi = p.n_seqs - 1;
   while (lo < hi) {
@@ -113,11 +122,24 @@ __device__ __forceinline__ Seg seg_at(const DecodeParams& p, long long s, long l
   g.gidx = blk * p.n_seqs + lo;
   g.gs0 = (long long)blk * p.block_stages + p.seqs[lo].stage_begin;
   g.gs1 = g.gs0 + p.seqs[lo].n_stages;
-  g.s_next = min(s_end, g.gs1);
-  g.t0 = (int)(s - g.gs0) * kStageTokens;
-  g.t1 = min(p.seqs[lo].len, (int)(g.s_next - g.gs0) * kStageTokens);
-  g.n_st = (int)(g.s_next - s);
   return g;
+}
+
+// The segment of [s_lo, s_hi) that ends at s_hi.
+__device__ __forceinline__ Seg seg_ending(const DecodeParams& p, long long s_hi, long long s_lo) {
+  Seg g = group_at(p, s_hi - 1);
+  g.s_begin = max(s_lo, g.gs0);
+  g.t0 = (int)(g.s_begin - g.gs0) * kStageTokens;
+  g.t1 = min(old_tokens(p, g.si), (int)(s_hi - g.gs0) * kStageTokens);
+  g.n_st = (int)(s_hi - g.s_begin);
+  return g;
+}
+
+// A segment that ends at its group's last stage carries the group's new token
+// (when the call appends one): the helper appends it and folds its score into
+// the segment's merge; K/V stages cover only the tokens cached before.
+__device__ __forceinline__ bool seg_has_new(const DecodeParams& p, const Seg& w) {
+  return p.seqs[w.si].new_pos >= 0 && p.k_new != nullptr && w.s_begin + w.n_st == w.gs1;
 }
 
 // Final result of one query-head row, 4 dims at d: normalised output, or the
@@ -138,15 +160,24 @@ __device__ __forceinline__ void store_result(const DecodeParams& p, size_t orow,
 
 // CTA owning stage s: the b with start(b) <= s < start(b + 1).
 __device__ __forceinline__ int cta_of(const DecodeParams& p, long long s) {
-  return (int)(((s + 1) * p.grid + p.total_stages - 1) / p.total_stages - 1);
+  return (int)(div_nonneg((s + 1) * p.grid + p.total_stages - 1, p.total_stages) - 1);
+}
+
+// Scratch offset (floats) of the split-K record CTA bp wrote for group gidx:
+// its segment jp = gidx - (group of bp's first stage).
+template <int HD>
+__device__ __forceinline__ long long record_offset(const DecodeParams& p, int bp, int gidx) {
+  const int jp = gidx - group_at(p, stage_start(bp, p.total_stages, p.grid)).gidx;
+  return ((long long)bp * p.max_segs + jp) * p.group * kScratchRec<HD>;
 }
 
 // Persistent: one CTA per SM loops over work items (round-robin over the grid).
 //   warps 0-3  consumers: each takes 16 tokens of every K/V stage (mma.sync
 //              S = Q K^T, online softmax, O += P V) and parks its state
-//   warp 4     producer: query/RoPE row prefetch, fused append, K/V TMA ring
+//   warp 4     producer: query/RoPE (and new k/v) row prefetch, K/V TMA ring
 //   warp 5     helper: rotates each item's query into f16 fragments ahead of
-//              the consumers, and merges the four consumer states of each
+//              the consumers; appends the new token (RoPE, f16) and scores
+//              it; merges the four consumer states and the new token of each
 //              finished item into the output (or a split-K partial record)
 template <int HD, int GP>
 __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_constant__ DecodeParams p) {
@@ -163,7 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
   uint64_t* fready = qempty + 2; // [2] helper -> consumers
   uint64_t* fempty = fready + 2; // [2] consumers -> helper
   uint64_t* mready = fempty + 2; // [2] consumers -> helper
-  uint64_t* mfree = mready + 2;  // [2] helper -> consumers
+  uint64_t* mfree = mready + 2;  // [2] helper -> consumers, appender
+  uint64_t* nready = mfree + 2;  // [2] appender -> helper
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -180,11 +212,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&qfull[b], 1);
-      mbar_init(&qempty[b], 1);
+      mbar_init(&qempty[b], 2);  // helper and appender
       mbar_init(&fready[b], 1);
       mbar_init(&fempty[b], kConsumerWarps);
       mbar_init(&mready[b], kConsumerWarps);
       mbar_init(&mfree[b], 1);
+      mbar_init(&nready[b], 1);
     }
     fence_mbarrier_init();
   }
@@ -199,11 +232,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     const uint64_t policy = policy_evict_first();
     uint32_t sidx = 0, k = 0;
     bool ok = true;
-    for (long long sg = s_beg; sg < s_end && ok; ++k) {
-      const Seg w = seg_at(p, sg, s_end);
-      sg = w.s_next;
+    for (long long sg = s_end; sg > s_beg && ok; ++k) {
+      const Seg w = seg_ending(p, sg, s_beg);
+      sg = w.s_begin;
       const SeqEntry se = p.seqs[w.si];
       const int layer = p.layer_begin + w.layer_local;
+      const bool has_new = seg_has_new(p, w);
       if (lane == 0) {
         const int b = k & 1;
         if (k >= 2 && !mbar_wait(&qempty[b], ((k >> 1) - 1) & 1)) {
@@ -211,10 +245,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
           ok = false;
         }
         if (ok) {
+          // the group's query rows and RoPE row; with a new token also its raw
+          // k and v rows (and its own RoPE row when its position differs)
           const size_t qrow0 = (size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * H + w.kvh * G;
-          const uint32_t qbytes = (uint32_t)(G * HD * 4);
-          const uint32_t csbytes = p.rope ? (uint32_t)(2 * half * 4) : 0u;
-          mbar_arrive_expect_tx(&qfull[b], qbytes + csbytes);
+          const bool new_cs = has_new && p.rope && se.new_pos != se.q_pos;
+          uint32_t bytes = (uint32_t)(G * HD * 4) + (p.rope ? (uint32_t)(2 * half * 4) : 0u);
+          if (has_new) bytes += (uint32_t)(2 * HD * 4) + (new_cs ? (uint32_t)(2 * half * 4) : 0u);
+          mbar_arrive_expect_tx(&qfull[b], bytes);
           float* qdst = reinterpret_cast<float*>(smem + C::kOffQ + b * C::kQBytes);
           for (int r = 0; r < G; ++r) bulk_load(qdst + r * C::kRowF, p.q + (qrow0 + r) * HD, HD * 4, &qfull[b]);
           if (p.rope) {
@@ -222,36 +259,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
             bulk_load(cs, p.rope_cos + (size_t)se.q_pos * half, half * 4, &qfull[b]);
             bulk_load(cs + half, p.rope_sin + (size_t)se.q_pos * half, half * 4, &qfull[b]);
           }
+          if (has_new) {
+            float* nb = reinterpret_cast<float*>(smem + C::kOffNew + b * C::kNewBytes);
+            const size_t src = ((size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * p.kv_heads + w.kvh) * HD;
+            bulk_load(nb, p.k_new + src, HD * 4, &qfull[b]);
+            bulk_load(nb + HD, p.v_new + src, HD * 4, &qfull[b]);
+            if (new_cs) {
+              bulk_load(nb + 2 * HD, p.rope_cos + (size_t)se.new_pos * half, half * 4, &qfull[b]);
+              bulk_load(nb + 2 * HD + half, p.rope_sin + (size_t)se.new_pos * half, half * 4, &qfull[b]);
+            }
+          }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
-      const int new_idx = se.len - 1;
-      if (se.new_pos >= 0 && p.k_new != nullptr && new_idx >= w.t0 && new_idx < w.t1) {
-        // RoPE(k) + f16 round-to-nearest-even append of the new token, written
-        // before the TMA that reads it (proxy fence below).
-        const int page = p.page_table[se.slot * p.max_pages_per_seq + new_idx / p.page_tokens];
-        const size_t row = ((size_t)(layer * p.num_pages + page) * p.kv_heads + w.kvh) * p.page_tokens +
-                           (new_idx % p.page_tokens);
-        const size_t src = ((size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * p.kv_heads + w.kvh) * HD;
-        const float* kn = p.k_new + src;
-        const float* vn = p.v_new + src;
-        for (int i = lane; i < half; i += 32) {
-          const float a = kn[i], bb = kn[i + half];
-          float lo = a, hi = bb;
-          if (p.rope) {
-            const float c = p.rope_cos[(size_t)se.new_pos * half + i];
-            const float s = p.rope_sin[(size_t)se.new_pos * half + i];
-            lo = rope_lo(a, bb, c, s);
-            hi = rope_hi(a, bb, c, s);
-          }
-          p.k_pool[row * HD + i] = __half_as_ushort(__float2half_rn(lo));
-          p.k_pool[row * HD + i + half] = __half_as_ushort(__float2half_rn(hi));
-        }
-        for (int i = lane; i < HD; i += 32) p.v_pool[row * HD + i] = __half_as_ushort(__float2half_rn(vn[i]));
-        fence_proxy_async();
-        __syncwarp();
-      }
       // Page-table entries of this chunk, one per lane, read together up front
       // (the loop refreshes the batch every 32 pages).
       const int pg0 = w.t0 / p.page_tokens;
@@ -304,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     const int g = lane >> 2, c = lane & 3;  // the fragment owner this lane prepares for
     uint32_t k = 0;
     bool ok = true;
-    // fragments for the CTA's segment number kk (all 32 lanes; warp-uniform waits)
+    // query fragments for the CTA's segment number kk (all 32 lanes; warp-uniform waits)
     auto prepare = [&](uint32_t kk) -> bool {
       const int b = kk & 1;
       if (!mbar_wait_warp(&qfull[b], (kk >> 1) & 1)) return false;
@@ -367,137 +388,209 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
       }
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&qempty[b]);  // raw rows consumed: the producer may refill this buffer
+        mbar_arrive(&qempty[b]);  // raw rows consumed (with the appender's arrival the producer may refill)
         mbar_arrive(&fready[b]);
       }
       return true;
     };
+    const int gidx_first = s_beg < s_end ? group_at(p, s_beg).gidx : 0;  // record j of this CTA: group gidx_first + j
     if (s_beg < s_end) ok = prepare(0);
-    for (long long sg = s_beg; sg < s_end && ok; ++k) {
-      const Seg w = seg_at(p, sg, s_end);
-      sg = w.s_next;
-      if (sg < s_end && !prepare(k + 1)) {
+    for (long long sg = s_end; sg > s_beg && ok; ++k) {
+      const Seg w = seg_ending(p, sg, s_beg);
+      sg = w.s_begin;
+      if (sg > s_beg && !prepare(k + 1)) {
         ok = false;
         break;
       }
       // merge item k: the four consumer warps' (m, l, O) -> output or split-K record
       const int b = k & 1;
+      // The group's parts and (lanes < kSlots) the record offsets of the first
+      // combine batch, worked out (64-bit divisions) while the consumers stream.
+      const size_t qrow0 = (size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * H + w.kvh * G;
+      const int b_first = cta_of(p, w.gs0);
+      const int parts = cta_of(p, w.gs1 - 1) - b_first + 1;
+      const bool single = parts == 1;
+      constexpr int kRecFloats = GP * REC;                       // one staged record
+      constexpr int kSlots = C::kMergeBytes / (kRecFloats * 4);  // records staged per combine batch
+      static_assert(kSlots >= 2 && kSlots <= 8, "combine staging");
+      long long first_off = 0;
+      if (!single && lane < min(kSlots, parts)) first_off = record_offset<HD>(p, b_first + lane, w.gidx);
       if (!mbar_wait_warp(&mready[b], (k >> 1) & 1)) {
         ok = false;
         break;
       }
-      const size_t qrow0 = (size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * H + w.kvh * G;
       const float* sm_o = reinterpret_cast<const float*>(smem + C::kOffMerge + b * C::kMergeBytes);
       const float* sm_m = reinterpret_cast<const float*>(smem + C::kOffML) + b * C::kMLFloats;
       const float* sm_l = sm_m + kConsumerWarps * 16;
-      const int b_first = cta_of(p, w.gs0);
-      const int parts = cta_of(p, w.gs1 - 1) - b_first + 1;
-      const bool single = parts == 1;
-      float* part = p.partials + ((size_t)blockIdx.x * p.max_segs + k) * G * REC;
+      float* part = p.partials + ((size_t)blockIdx.x * p.max_segs + (w.gidx - gidx_first)) * G * REC;
       constexpr int kLanesPerRow = HD / 4;        // float4 per lane
       constexpr int kRowStep = 32 / kLanesPerRow; // rows handled per pass
+      constexpr int NR = GP / kRowStep;           // rows per lane
       const int d = 4 * (lane % kLanesPerRow);
       const int r0 = lane / kLanesPerRow;
-#pragma unroll
-      for (int u = 0; u < GP / kRowStep; ++u) {
-        const int row = r0 + u * kRowStep;
-        if (row >= G) continue;
-        float M = -INFINITY;
-#pragma unroll
-        for (int ww = 0; ww < kConsumerWarps; ++ww) M = fmaxf(M, sm_m[ww * 16 + row]);
-        float L = 0.f;
-        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+      // Two phases keep the dependency chains short: lane r < G computes row
+      // r's max, weights and sum; then every lane weights its 4-column slices
+      // of all rows (weights by shuffle from the row's lane), loads first and
+      // stores last.
+      // A segment with the group's new token adds it as a fifth state
+      // (m = its score, l = 1, O = its v row).
+      const bool has_new = seg_has_new(p, w);
+      if (has_new && !mbar_wait_warp(&nready[b], (k >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const float* res = reinterpret_cast<const float*>(smem + C::kOffRes + b * C::kResBytes);
+      float mw[kConsumerWarps] = {}, mn = 0.f, Mr = -INFINITY, Lr = 0.f;
+      if (lane < G) {
 #pragma unroll
         for (int ww = 0; ww < kConsumerWarps; ++ww) {
-          const float mw = sm_m[ww * 16 + row];
-          const float wt = mw == -INFINITY ? 0.f : ex2(mw - M);
-          const float4 o = *reinterpret_cast<const float4*>(sm_o + ((size_t)ww * GP + row) * C::kRowF + d);
-          L += sm_l[ww * 16 + row] * wt;
-          O.x += o.x * wt;
-          O.y += o.y * wt;
-          O.z += o.z * wt;
-          O.w += o.w * wt;
+          mw[ww] = sm_m[ww * 16 + lane];
+          Mr = fmaxf(Mr, mw[ww]);
         }
+        if (has_new) {
+          mn = res[lane];
+          Mr = fmaxf(Mr, mn);
+        }
+#pragma unroll
+        for (int ww = 0; ww < kConsumerWarps; ++ww) {
+          mw[ww] = mw[ww] == -INFINITY ? 0.f : ex2(mw[ww] - Mr);
+          Lr += sm_l[ww * 16 + lane] * mw[ww];
+        }
+        if (has_new) {
+          mn = ex2(mn - Mr);
+          Lr += mn;
+        }
+      }
+      const float4 vn = has_new ? *reinterpret_cast<const float4*>(res + 16 + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 O[NR];
+#pragma unroll
+      for (int u = 0; u < NR; ++u) {
+        const int row = r0 + u * kRowStep;  // < GP <= 16: the shuffle source is a valid lane
+        const float wn = __shfl_sync(0xffffffffu, mn, row);
+        O[u] = make_float4(vn.x * wn, vn.y * wn, vn.z * wn, vn.w * wn);
+#pragma unroll
+        for (int ww = 0; ww < kConsumerWarps; ++ww) {
+          const float wt = __shfl_sync(0xffffffffu, mw[ww], row);
+          const float4 o = *reinterpret_cast<const float4*>(sm_o + ((size_t)ww * GP + row) * C::kRowF + d);
+          O[u].x += o.x * wt;
+          O[u].y += o.y * wt;
+          O[u].z += o.z * wt;
+          O[u].w += o.w * wt;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < NR; ++u) {
+        const int row = r0 + u * kRowStep;
+        const float M = __shfl_sync(0xffffffffu, Mr, row);
+        const float L = __shfl_sync(0xffffffffu, Lr, row);
+        if (row >= G) continue;
         if (single) {
-          store_result<HD>(p, qrow0 + row, d, O, M, L);
+          store_result<HD>(p, qrow0 + row, d, O[u], M, L);
         } else {
           float* r = part + (size_t)row * REC;
-          *reinterpret_cast<float4*>(r + d) = O;
+          *reinterpret_cast<float4*>(r + d) = O[u];
           if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
         }
       }
       if (!single) {
-        // the last CTA of the group to finish merges the group's records
+        // The last CTA of the group to finish folds all the parts' records, in
+        // part order (so the result does not depend on which CTA came last).
+        // Release: the warp's record stores (ordered by __syncwarp) before the
+        // ticket; acquire: the ticket before the record loads.
         __syncwarp();
-        __threadfence();
         int last = 0;
         if (lane == 0) {
+          fence_acq_rel_gpu();
           const uint32_t ticket = atomicAdd(&p.counters[w.gidx], 1u);
           last = ticket == (uint32_t)(parts - 1);
-          if (last) p.counters[w.gidx] = 0u;  // every part has taken its ticket
+          if (last) {
+            fence_acq_rel_gpu();
+            p.counters[w.gidx] = 0u;  // every part has taken its ticket
+          }
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-          __threadfence();
-          // Part records of this group: CTA b_first + pp holds it as its segment
-          // jp = gidx - (group of its first stage).  Record offsets go to shared
-          // memory (the just-merged buffer b is still ours), then every load of
-          // all parts and rows is issued before any result is needed.
-          long long* off = reinterpret_cast<long long*>(smem + C::kOffMerge + b * C::kMergeBytes);
-          const int max_parts = C::kMergeBytes / (int)sizeof(long long);
-          if (parts > max_parts) {
-            set_error(p.error, 10);  // the host bounds the split so this cannot happen
-          } else {
-            for (int pp = lane; pp < parts; pp += 32) {
-              const int bp = b_first + pp;
-              const int jp = w.gidx - seg_at(p, stage_start(bp, p.total_stages, p.grid), p.total_stages).gidx;
-              off[pp] = ((long long)bp * p.max_segs + jp) * G * REC;
-            }
-            __syncwarp();
-            float M[GP / kRowStep], L[GP / kRowStep];
-            float4 O[GP / kRowStep];
+          // Records are copied into the just-merged buffer b (still ours), all
+          // copies of a batch in flight at once.  Slot 0 holds the running fold,
+          // seeded with part 0; the other slots take the next parts.  Each
+          // batch: lane r < G forms row r's new max, slot weights and sum (and
+          // is the only reader and writer of row r's running (m, l)); then all
+          // lanes weight their column slices.  CTA b_first + pp holds part pp
+          // as its segment jp = gidx - (group of its first stage).
+          float* stage = reinterpret_cast<float*>(smem + C::kOffMerge + b * C::kMergeBytes);
+          const uint32_t stage_s = smem_u32(stage);
+#pragma unroll 1
+          for (int pp0 = 0; pp0 < parts;) {
+            const int first_slot = pp0 == 0 ? 0 : 1;
+            const int nb = min(kSlots - first_slot, parts - pp0);
+            long long my_off = first_off;
+            if (pp0 > 0 && lane < nb) my_off = record_offset<HD>(p, b_first + pp0 + lane, w.gidx);
+            __syncwarp();  // the previous batch's reads of the staging slots are done
+#pragma unroll 1
+            for (int j = 0; j < nb; ++j) {
+              const float* rec = p.partials + __shfl_sync(0xffffffffu, my_off, j);
+              const uint32_t dst0 = stage_s + (uint32_t)((first_slot + j) * kRecFloats) * 4u;
 #pragma unroll
-            for (int u = 0; u < GP / kRowStep; ++u) {
-              M[u] = -INFINITY;
-              L[u] = 0.f;
-              O[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            for (int pp = 0; pp < parts; ++pp) {
-              const float* rec = p.partials + off[pp];
-#pragma unroll
-              for (int u = 0; u < GP / kRowStep; ++u) {
-                const int row = r0 + u * kRowStep;
-                if (row < G) M[u] = fmaxf(M[u], __ldcg(rec + (size_t)row * REC + HD));
-              }
-            }
-            for (int pp = 0; pp < parts; ++pp) {
-              const float* rec = p.partials + off[pp];
-              float2 ml[GP / kRowStep];
-              float4 o[GP / kRowStep];
-#pragma unroll
-              for (int u = 0; u < GP / kRowStep; ++u) {
-                const int row = r0 + u * kRowStep;
-                if (row < G) {
-                  ml[u] = __ldcg(reinterpret_cast<const float2*>(rec + (size_t)row * REC + HD));
-                  o[u] = __ldcg(reinterpret_cast<const float4*>(rec + (size_t)row * REC + d));
-                }
-              }
-#pragma unroll
-              for (int u = 0; u < GP / kRowStep; ++u) {
+              for (int u = 0; u < NR; ++u) {
                 const int row = r0 + u * kRowStep;
                 if (row >= G) continue;
-                const float wt = ex2(ml[u].x - M[u]);
-                L[u] += ml[u].y * wt;
-                O[u].x += o[u].x * wt;
-                O[u].y += o[u].y * wt;
-                O[u].z += o[u].z * wt;
-                O[u].w += o[u].w * wt;
+                const uint32_t dst = dst0 + (uint32_t)(row * REC) * 4u;
+                cp_async_cg16(dst + (uint32_t)d * 4u, rec + (size_t)row * REC + d);
+                if (d == 0) cp_async_cg16(dst + HD * 4u, rec + (size_t)row * REC + HD);  // (m, l, pad, pad)
+              }
+            }
+            cp_async_wait_all();
+            __syncwarp();
+            const int hi = first_slot + nb;
+            pp0 += nb;
+            const bool final_batch = pp0 >= parts;
+            float ws[kSlots];
+            float Mn = -INFINITY, Ln = 0.f;
+            if (lane < G) {
+              float2 ml[kSlots];
+#pragma unroll
+              for (int s = 0; s < kSlots; ++s) {
+                ml[s] = s < hi ? *reinterpret_cast<const float2*>(stage + s * kRecFloats + lane * REC + HD)
+                               : make_float2(-INFINITY, 0.f);
+                Mn = fmaxf(Mn, ml[s].x);
+              }
+#pragma unroll
+              for (int s = 0; s < kSlots; ++s) {
+                ws[s] = ml[s].x == -INFINITY ? 0.f : ex2(ml[s].x - Mn);
+                Ln += ml[s].y * ws[s];
+              }
+              if (!final_batch) *reinterpret_cast<float2*>(stage + lane * REC + HD) = make_float2(Mn, Ln);
+            } else {
+#pragma unroll
+              for (int s = 0; s < kSlots; ++s) ws[s] = 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < NR; ++u) {
+              const int row = r0 + u * kRowStep;
+              O[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+              for (int s = 0; s < kSlots; ++s) {
+                const float wt = __shfl_sync(0xffffffffu, ws[s], row);
+                if (s < hi) {
+                  const float4 o = *reinterpret_cast<const float4*>(stage + s * kRecFloats + row * REC + d);
+                  O[u].x += o.x * wt;
+                  O[u].y += o.y * wt;
+                  O[u].z += o.z * wt;
+                  O[u].w += o.w * wt;
+                }
               }
             }
 #pragma unroll
-            for (int u = 0; u < GP / kRowStep; ++u) {
+            for (int u = 0; u < NR; ++u) {
               const int row = r0 + u * kRowStep;
-              if (row < G) store_result<HD>(p, qrow0 + row, d, O[u], M[u], L[u]);
+              const float M = __shfl_sync(0xffffffffu, Mn, row);
+              const float L = __shfl_sync(0xffffffffu, Ln, row);
+              if (row >= G) continue;
+              if (final_batch) {
+                store_result<HD>(p, qrow0 + row, d, O[u], M, L);
+              } else {
+                *reinterpret_cast<float4*>(stage + row * REC + d) = O[u];
+              }
             }
           }
         }
@@ -509,15 +602,88 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     return;
   }
 
+  if (warp == kConsumerWarps + 2) {
+    // ---- appender warp: the new token of a segment that carries one --------
+    // RoPE + f16 append to the cache (fire and forget: no K/V stage of this
+    // launch reads it) and its scores q.k in log2 units for the helper's merge.
+    // Every segment arrives on qempty and nready, so the phases stay in step
+    // with the segment count; result buffer b is rewritten only after the
+    // merge two segments back has released it (mfree).
+    uint32_t k = 0;
+    for (long long sg = s_end; sg > s_beg; ++k) {
+      const Seg w = seg_ending(p, sg, s_beg);
+      sg = w.s_begin;
+      const int b = k & 1;
+      if (!mbar_wait_warp(&qfull[b], (k >> 1) & 1) ||
+          (k >= 2 && !mbar_wait_warp(&mfree[b], ((k >> 1) - 1) & 1))) {
+        set_error(p.error, 11);
+        break;
+      }
+      if (seg_has_new(p, w)) {
+        const SeqEntry se = p.seqs[w.si];
+        const float* sq = reinterpret_cast<const float*>(smem + C::kOffQ + b * C::kQBytes);
+        const float* cs = reinterpret_cast<const float*>(smem + C::kOffCS + b * C::kCSBytes);
+        float* nb = reinterpret_cast<float*>(smem + C::kOffNew + b * C::kNewBytes);  // raw k, v (, cos, sin)
+        const float* csk = se.new_pos != se.q_pos ? nb + 2 * HD : cs;
+        float* res = reinterpret_cast<float*>(smem + C::kOffRes + b * C::kResBytes);  // scores[16], v[HD]
+        const int new_idx = se.len - 1;
+        const int page = p.page_table[se.slot * p.max_pages_per_seq + new_idx / p.page_tokens];
+        const size_t row = ((size_t)((p.layer_begin + w.layer_local) * p.num_pages + page) * p.kv_heads + w.kvh) *
+                               p.page_tokens + (new_idx % p.page_tokens);
+        for (int i = lane; i < half; i += 32) {
+          const float a = nb[i], bb = nb[i + half];
+          float lo = a, hi = bb;
+          if (p.rope) {
+            lo = rope_lo(a, bb, csk[i], csk[half + i]);
+            hi = rope_hi(a, bb, csk[i], csk[half + i]);
+          }
+          const __half hl = __float2half_rn(lo), hh = __float2half_rn(hi);
+          p.k_pool[row * HD + i] = __half_as_ushort(hl);
+          p.k_pool[row * HD + i + half] = __half_as_ushort(hh);
+          nb[i] = __half2float(hl);  // in place: k as the cache holds it (only this lane reads i, i + half)
+          nb[i + half] = __half2float(hh);
+        }
+        for (int i = lane; i < HD; i += 32) {
+          const __half hv = __float2half_rn(nb[HD + i]);
+          p.v_pool[row * HD + i] = __half_as_ushort(hv);
+          res[16 + i] = __half2float(hv);
+        }
+        __syncwarp();
+        for (int h = 0; h < G; ++h) {
+          const float* qr = sq + h * C::kRowF;
+          float dot = 0.f;
+          for (int i = lane; i < half; i += 32) {
+            float ql = qr[i], qh = qr[i + half];
+            if (p.rope) {
+              const float x = ql, y = qh;
+              ql = rope_lo(x, y, cs[i], cs[half + i]);
+              qh = rope_hi(x, y, cs[i], cs[half + i]);
+            }
+            dot = fmaf(ql, nb[i], fmaf(qh, nb[i + half], dot));
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+          if (lane == 0) res[h] = dot * p.scale_log2;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&qempty[b]);
+        mbar_arrive(&nready[b]);
+      }
+    }
+    return;
+  }
+
   // ---- consumer warps 0-3 ------------------------------------------------
   const int g = lane >> 2;  // mma group id: head rows g and g+8, token rows
   const int c = lane & 3;   // thread in group
   const float sl = p.scale_log2;
   uint32_t sidx = 0, k = 0;
   bool failed = false;
-  for (long long sg = s_beg; sg < s_end; ++k) {
-    const Seg w = seg_at(p, sg, s_end);
-    sg = w.s_next;
+  for (long long sg = s_end; sg > s_beg; ++k) {
+    const Seg w = seg_ending(p, sg, s_beg);
+    sg = w.s_begin;
 
     // 1) query fragments prepared by the helper warp
     const int fb = k & 1;

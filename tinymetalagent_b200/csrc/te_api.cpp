@@ -607,6 +607,12 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
   if (G > 16) return fail(e, TE_STATUS_UNSUPPORTED, "more than 16 query heads per kv head");
   if (n_seqs > c->d.max_seqs) return TE_STATUS_INVALID_ARGUMENT;
   const bool append = k_new != NULL;
+  if (!(flags & TE_ATTN_HOST_BUFFERS) &&
+      ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) &
+       15u)) {
+    // the kernel copies query and new k/v rows with 16-byte bulk copies
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "q, k_new and v_new must be 16-byte aligned");
+  }
   DeviceGuard dg(e->device);
 
   // Per-sequence work, validated before anything is queued.

@@ -23,13 +23,23 @@ struct SeqEntry {
   int32_t q_pos;        // RoPE position of the query
   int32_t new_pos;      // RoPE position of the appended token, or -1 (no append)
   int32_t stage_begin;  // first 64-token stage of this sequence within a (layer, kv head) block
-  int32_t n_stages;     // ceil(len / 64)
+  int32_t n_stages;     // max(1, ceil(old tokens / 64)): the stages of tokens cached before the call
 };
 
 constexpr int kMaxParamSeqs = 64;  // sequences per decode launch
 
 // Stream-K split: CTA b of `grid` owns stages [stage_start(b), stage_start(b+1)).
-__host__ __device__ inline long long stage_start(long long b, long long total, long long grid) { return b * total / grid; }
+// Quotient of non-negative a / b; on the device a 32-bit divide when both fit
+// (the 64-bit one is a long software sequence).
+__host__ __device__ inline long long div_nonneg(long long a, long long b) {
+#ifdef __CUDA_ARCH__
+  if ((((unsigned long long)a | (unsigned long long)b) >> 32) == 0) return (long long)((unsigned)a / (unsigned)b);
+#endif
+  return a / b;
+}
+__host__ __device__ inline long long stage_start(long long b, long long total, long long grid) {
+  return div_nonneg(b * total, grid);
+}
 // Floats per split-K scratch record: acc[head_dim], m, l, two pad (16-byte aligned records).
 inline size_t decode_scratch_rec(int head_dim) { return (size_t)head_dim + 4; }
 
@@ -73,13 +83,20 @@ struct DecodeParams {
 // 2-D f16 tensor map over [rows][cols] (box box_rows x 64, 128B swizzle); false on failure.
 bool encode_tmap_f16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
 
+// Tokens of sequence entry i cached before the call: the appended token (if
+// any) is not streamed from the cache but scored from its k/v rows.
+__host__ __device__ inline int old_tokens(const DecodeParams& p, int i) {
+  return p.seqs[i].len - ((p.seqs[i].new_pos >= 0 && p.k_new != nullptr) ? 1 : 0);
+}
+
 // Plans the stream-K split of a decode launch: fills each sequence's stage
-// range (from its len), block_stages, total_stages, grid (<= max_grid CTAs,
+// range (from its old tokens), block_stages, total_stages, grid (<= max_grid CTAs,
 // at least one stage each) and max_segs (groups any one CTA touches).
 inline void plan_stream_k(DecodeParams& p, long long max_grid) {
   int acc = 0;
   for (int i = 0; i < p.n_seqs; ++i) {
-    p.seqs[i].n_stages = (p.seqs[i].len + kStageTokens - 1) / kStageTokens;
+    const int n_old = old_tokens(p, i);
+    p.seqs[i].n_stages = n_old > 0 ? (n_old + kStageTokens - 1) / kStageTokens : 1;
     p.seqs[i].stage_begin = acc;
     acc += p.seqs[i].n_stages;
   }

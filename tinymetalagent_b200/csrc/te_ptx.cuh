@@ -242,6 +242,20 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, ui
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
+// 16-byte global -> shared copy through L2 only (LDGSTS, generic proxy), and
+// the wait for all of this thread's outstanding copies.
+__device__ __forceinline__ void cp_async_cg16(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// GPU-scope acquire-release fence: orders this thread's earlier memory
+// operations (and those it has observed, e.g. through __syncwarp) before its
+// later ones, without the full sequential-consistency fence of __threadfence.
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 __device__ __forceinline__ void set_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
