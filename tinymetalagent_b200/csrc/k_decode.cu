@@ -163,6 +163,26 @@ __device__ __forceinline__ int cta_of(const DecodeParams& p, long long s) {
   return (int)(div_nonneg((s + 1) * p.grid + p.total_stages - 1, p.total_stages) - 1);
 }
 
+// One step of the split-K combine, taken in part order: (M, L, O) absorbs
+// the record (m, l, o).  Explicit roundings, so every code path that combines
+// a group (helper or consumer warps, whichever CTA finishes last) computes
+// bit-identical results.
+__device__ __forceinline__ void fold_part(float& M, float& L, float4& O, float m, float l, const float4& o) {
+  if (m == -INFINITY) return;
+  const float mn = fmaxf(M, m);
+  const float a = M == -INFINITY ? 0.f : ex2(__fsub_rn(M, mn));
+  const float bw = ex2(__fsub_rn(m, mn));
+  L = __fmaf_rn(L, a, __fmul_rn(l, bw));
+  O.x = __fmaf_rn(O.x, a, __fmul_rn(o.x, bw));
+  O.y = __fmaf_rn(O.y, a, __fmul_rn(o.y, bw));
+  O.z = __fmaf_rn(O.z, a, __fmul_rn(o.z, bw));
+  O.w = __fmaf_rn(O.w, a, __fmul_rn(o.w, bw));
+  M = mn;
+}
+
+// Named barrier of the four consumer warps (barrier 0 is __syncthreads).
+__device__ __forceinline__ void consumer_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
 // Scratch offset (floats) of the split-K record CTA bp wrote for group gidx:
 // its segment jp = gidx - (group of bp's first stage).
 template <int HD>
@@ -402,6 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         ok = false;
         break;
       }
+      if (sg == s_beg) break;  // the CTA's last segment: the consumer warps merge it
       // merge item k: the four consumer warps' (m, l, O) -> output or split-K record
       const int b = k & 1;
       // The group's parts and (lanes < kSlots) the record offsets of the first
@@ -511,25 +532,29 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
           // Records are copied into the just-merged buffer b (still ours), all
-          // copies of a batch in flight at once.  Slot 0 holds the running fold,
-          // seeded with part 0; the other slots take the next parts.  Each
-          // batch: lane r < G forms row r's new max, slot weights and sum (and
-          // is the only reader and writer of row r's running (m, l)); then all
-          // lanes weight their column slices.  CTA b_first + pp holds part pp
-          // as its segment jp = gidx - (group of its first stage).
+          // copies of a batch in flight at once, then folded in part order by
+          // fold_part, as the consumer warps' combine does.  CTA b_first + pp
+          // holds part pp as its segment jp = gidx - (group of its first stage).
           float* stage = reinterpret_cast<float*>(smem + C::kOffMerge + b * C::kMergeBytes);
           const uint32_t stage_s = smem_u32(stage);
+          float M[NR], L[NR];
+          float4 O[NR];
+#pragma unroll
+          for (int u = 0; u < NR; ++u) {
+            M[u] = -INFINITY;
+            L[u] = 0.f;
+            O[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
 #pragma unroll 1
-          for (int pp0 = 0; pp0 < parts;) {
-            const int first_slot = pp0 == 0 ? 0 : 1;
-            const int nb = min(kSlots - first_slot, parts - pp0);
+          for (int pp0 = 0; pp0 < parts; pp0 += kSlots) {
+            const int nb = min(kSlots, parts - pp0);
             long long my_off = first_off;
             if (pp0 > 0 && lane < nb) my_off = record_offset<HD>(p, b_first + pp0 + lane, w.gidx);
             __syncwarp();  // the previous batch's reads of the staging slots are done
 #pragma unroll 1
             for (int j = 0; j < nb; ++j) {
               const float* rec = p.partials + __shfl_sync(0xffffffffu, my_off, j);
-              const uint32_t dst0 = stage_s + (uint32_t)((first_slot + j) * kRecFloats) * 4u;
+              const uint32_t dst0 = stage_s + (uint32_t)(j * kRecFloats) * 4u;
 #pragma unroll
               for (int u = 0; u < NR; ++u) {
                 const int row = r0 + u * kRowStep;
@@ -541,57 +566,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
             }
             cp_async_wait_all();
             __syncwarp();
-            const int hi = first_slot + nb;
-            pp0 += nb;
-            const bool final_batch = pp0 >= parts;
-            float ws[kSlots];
-            float Mn = -INFINITY, Ln = 0.f;
-            if (lane < G) {
-              float2 ml[kSlots];
+#pragma unroll 1
+            for (int j = 0; j < nb; ++j) {
 #pragma unroll
-              for (int s = 0; s < kSlots; ++s) {
-                ml[s] = s < hi ? *reinterpret_cast<const float2*>(stage + s * kRecFloats + lane * REC + HD)
-                               : make_float2(-INFINITY, 0.f);
-                Mn = fmaxf(Mn, ml[s].x);
-              }
-#pragma unroll
-              for (int s = 0; s < kSlots; ++s) {
-                ws[s] = ml[s].x == -INFINITY ? 0.f : ex2(ml[s].x - Mn);
-                Ln += ml[s].y * ws[s];
-              }
-              if (!final_batch) *reinterpret_cast<float2*>(stage + lane * REC + HD) = make_float2(Mn, Ln);
-            } else {
-#pragma unroll
-              for (int s = 0; s < kSlots; ++s) ws[s] = 0.f;
-            }
-#pragma unroll
-            for (int u = 0; u < NR; ++u) {
-              const int row = r0 + u * kRowStep;
-              O[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-              for (int s = 0; s < kSlots; ++s) {
-                const float wt = __shfl_sync(0xffffffffu, ws[s], row);
-                if (s < hi) {
-                  const float4 o = *reinterpret_cast<const float4*>(stage + s * kRecFloats + row * REC + d);
-                  O[u].x += o.x * wt;
-                  O[u].y += o.y * wt;
-                  O[u].z += o.z * wt;
-                  O[u].w += o.w * wt;
-                }
+              for (int u = 0; u < NR; ++u) {
+                const int row = r0 + u * kRowStep;
+                if (row >= G) continue;
+                const float* r = stage + j * kRecFloats + row * REC;
+                const float2 ml = *reinterpret_cast<const float2*>(r + HD);
+                fold_part(M[u], L[u], O[u], ml.x, ml.y, *reinterpret_cast<const float4*>(r + d));
               }
             }
+          }
 #pragma unroll
-            for (int u = 0; u < NR; ++u) {
-              const int row = r0 + u * kRowStep;
-              const float M = __shfl_sync(0xffffffffu, Mn, row);
-              const float L = __shfl_sync(0xffffffffu, Ln, row);
-              if (row >= G) continue;
-              if (final_batch) {
-                store_result<HD>(p, qrow0 + row, d, O[u], M, L);
-              } else {
-                *reinterpret_cast<float4*>(stage + row * REC + d) = O[u];
-              }
-            }
+          for (int u = 0; u < NR; ++u) {
+            const int row = r0 + u * kRowStep;
+            if (row < G) store_result<HD>(p, qrow0 + row, d, O[u], M[u], L[u]);
           }
         }
       }
@@ -812,7 +802,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
 
-    // 3) park this warp's state for the helper's merge
+    // 3) park this warp's state for the merge
     const int mb = k & 1;
     if (k >= 2 && !failed && !mbar_wait_warp(&mfree[mb], ((k >> 1) - 1) & 1)) {
       set_error(p.error, 8);
@@ -842,7 +832,150 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&mready[mb]);
+    if (sg > s_beg) {
+      // more segments follow: the helper merges this one while the stages of the next stream
+      if (lane == 0) mbar_arrive(&mready[mb]);
+      continue;
+    }
+    // 4) the CTA's last segment is merged by the four consumer warps together
+    // (nothing else is left to overlap with): thread t owns row t / kTPR and
+    // the float4 columns 4 * (t % kTPR + f * kTPR).
+    constexpr int kTPR = 128 / GP;        // threads per row
+    constexpr int kF = HD / (4 * kTPR);   // float4 columns per thread
+    const int t = tid;                    // 0..127
+    const int row = t / kTPR;
+    const int cl = t % kTPR;
+    consumer_bar_sync();
+    const bool has_new = seg_has_new(p, w);
+    if (has_new && !failed && !mbar_wait_warp(&nready[mb], (k >> 1) & 1)) {
+      set_error(p.error, 12);
+      failed = true;
+    }
+    const float* res = reinterpret_cast<const float*>(smem + C::kOffRes + mb * C::kResBytes);
+    float M = -INFINITY, L = 0.f, wt[kConsumerWarps], wn = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < kConsumerWarps; ++ww) {
+      wt[ww] = sm_m[ww * 16 + row];
+      M = fmaxf(M, wt[ww]);
+    }
+    if (has_new) {
+      wn = res[row];
+      M = fmaxf(M, wn);
+    }
+#pragma unroll
+    for (int ww = 0; ww < kConsumerWarps; ++ww) {
+      wt[ww] = wt[ww] == -INFINITY ? 0.f : ex2(wt[ww] - M);
+      L += sm_l[ww * 16 + row] * wt[ww];
+    }
+    if (has_new) {
+      wn = ex2(wn - M);
+      L += wn;
+    }
+    float4 O[kF];
+#pragma unroll
+    for (int f = 0; f < kF; ++f) {
+      const int d = 4 * (cl + f * kTPR);
+      const float4 vn = has_new ? *reinterpret_cast<const float4*>(res + 16 + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+      O[f] = make_float4(vn.x * wn, vn.y * wn, vn.z * wn, vn.w * wn);
+#pragma unroll
+      for (int ww = 0; ww < kConsumerWarps; ++ww) {
+        const float4 o = *reinterpret_cast<const float4*>(sm_o + ((size_t)ww * GP + row) * C::kRowF + d);
+        O[f].x += o.x * wt[ww];
+        O[f].y += o.y * wt[ww];
+        O[f].z += o.z * wt[ww];
+        O[f].w += o.w * wt[ww];
+      }
+    }
+    const size_t qrow0 = (size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * H + w.kvh * G;
+    const int b_first = cta_of(p, w.gs0);
+    const int parts = cta_of(p, w.gs1 - 1) - b_first + 1;
+    if (parts == 1) {
+      if (row < G) {
+#pragma unroll
+        for (int f = 0; f < kF; ++f) store_result<HD>(p, qrow0 + row, 4 * (cl + f * kTPR), O[f], M, L);
+      }
+      continue;
+    }
+    // Split group: publish this part's record, take a ticket; the last part
+    // folds all records in part order (the result does not depend on which
+    // CTA came last).  Release: the 128 threads' record stores (ordered by
+    // the barrier) before the ticket; acquire: the ticket before the loads.
+    constexpr int REC = kScratchRec<HD>;
+    const int gidx_first = group_at(p, s_beg).gidx;
+    float* part = p.partials + ((size_t)blockIdx.x * p.max_segs + (w.gidx - gidx_first)) * G * REC;
+    if (row < G) {
+#pragma unroll
+      for (int f = 0; f < kF; ++f) *reinterpret_cast<float4*>(part + (size_t)row * REC + 4 * (cl + f * kTPR)) = O[f];
+      if (cl == 0) *reinterpret_cast<float2*>(part + (size_t)row * REC + HD) = make_float2(M, L);
+    }
+    // record offsets of all parts, one thread each, in the merge buffer (its
+    // reads above are complete once every thread has passed the barrier)
+    long long* off = reinterpret_cast<long long*>(sm_o);
+    static_assert(C::kMergeBytes >= 1024 * (int)sizeof(long long), "offsets of up to 1024 parts");
+    consumer_bar_sync();
+    uint32_t* flag = reinterpret_cast<uint32_t*>(sm_m);
+    if (t == 0) {
+      fence_acq_rel_gpu();
+      const uint32_t ticket = atomicAdd(&p.counters[w.gidx], 1u);
+      const uint32_t last = ticket == (uint32_t)(parts - 1);
+      if (last) {
+        fence_acq_rel_gpu();
+        p.counters[w.gidx] = 0u;  // every part has taken its ticket
+      }
+      *flag = last;
+    }
+    for (int pp = t; pp < parts && pp < 1024; pp += 128) off[pp] = record_offset<HD>(p, b_first + pp, w.gidx);
+    consumer_bar_sync();
+    if (*flag == 0u) continue;
+    if (parts > 1024) {
+      set_error(p.error, 10);  // the grid is at most one CTA per SM
+      continue;
+    }
+    const int own = (int)blockIdx.x - b_first;  // this CTA's part: its state is still in registers
+    float M2 = -INFINITY, L2 = 0.f;
+    float4 O2[kF];
+#pragma unroll
+    for (int f = 0; f < kF; ++f) O2[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+    constexpr int kB = 4;  // parts' loads in flight per round trip
+    for (int pp0 = 0; pp0 < parts; pp0 += kB) {
+      float2 ml[kB];
+      float4 o[kB][kF];
+#pragma unroll
+      for (int j = 0; j < kB; ++j) {
+        const int pp = pp0 + j;
+        if (pp < parts && pp != own && row < G) {
+          const float* rec = p.partials + off[pp] + (size_t)row * REC;
+          ml[j] = __ldcg(reinterpret_cast<const float2*>(rec + HD));
+#pragma unroll
+          for (int f = 0; f < kF; ++f) o[j][f] = __ldcg(reinterpret_cast<const float4*>(rec + 4 * (cl + f * kTPR)));
+        } else if (pp == own) {
+          ml[j] = make_float2(M, L);
+#pragma unroll
+          for (int f = 0; f < kF; ++f) o[j][f] = O[f];
+        } else {
+          ml[j] = make_float2(-INFINITY, 0.f);
+#pragma unroll
+          for (int f = 0; f < kF; ++f) o[j][f] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kB; ++j) {
+#pragma unroll
+        for (int f = 0; f < kF; ++f) {
+          // every column slice folds the same (m, l); only the f == kF - 1 fold keeps its (M, L)
+          float Mf = M2, Lf = L2;
+          fold_part(Mf, Lf, O2[f], ml[j].x, ml[j].y, o[j][f]);
+          if (f == kF - 1) {
+            M2 = Mf;
+            L2 = Lf;
+          }
+        }
+      }
+    }
+    if (row < G) {
+#pragma unroll
+      for (int f = 0; f < kF; ++f) store_result<HD>(p, qrow0 + row, 4 * (cl + f * kTPR), O2[f], M2, L2);
+    }
   }
 }
 
