@@ -190,6 +190,49 @@ def test_decode_append_rope_step(port, shape, chunk):
     eng.close()
 
 
+@pytest.mark.parametrize("page_tokens", [64, 128])
+def test_decode_interleaved_pages(port, page_tokens):
+    """Sequences filled in alternating chunks own interleaved (non-consecutive)
+    pages, so the kernel reads the page table; a third sequence filled in one
+    go owns consecutive pages (page ids computed).  One fused append+decode step."""
+    import torch
+    from tinymetalagent_b200 import AttnEngine, TE_ATTN_ADVANCE
+    h, hkv, hd = 16, 2, 128
+    lens = {0: 5 * page_tokens + 17, 1: 3 * page_tokens + 1, 2: 4 * page_tokens - 3}
+    rng = np.random.default_rng(page_tokens)
+    raw = {s: (rng.standard_normal((n, hkv, hd)).astype(np.float32),
+               rng.standard_normal((n, hkv, hd)).astype(np.float32)) for s, n in lens.items()}
+    eng = AttnEngine(0)
+    cache = eng.kv_cache(layers=1, max_seqs=3, max_tokens_per_seq=8 * page_tokens, kv_heads=hkv, head_dim=hd,
+                         page_tokens=page_tokens)
+    filled = {0: 0, 1: 0}
+    while any(filled[s] < lens[s] - 1 for s in (0, 1)):
+        for s in (0, 1):  # one page at a time, alternating: interleaved page ids
+            n = min(page_tokens, lens[s] - 1 - filled[s])
+            if n > 0:
+                k, v = raw[s]
+                cache.append_rope(0, 1, s, torch_dev(k[filled[s]:filled[s] + n]), torch_dev(v[filled[s]:filled[s] + n]),
+                                  n, TE_ATTN_ADVANCE)
+                filled[s] += n
+    k, v = raw[2]
+    cache.append_rope(0, 1, 2, torch_dev(k[:-1]), torch_dev(v[:-1]), lens[2] - 1, TE_ATTN_ADVANCE)
+    q = rng.standard_normal((1, 3, h, hd)).astype(np.float32)
+    kn = np.stack([raw[s][0][-1] for s in (0, 1, 2)])[None]
+    vn = np.stack([raw[s][1][-1] for s in (0, 1, 2)])[None]
+    out = torch.zeros((1, 3, h, hd), dtype=torch.float32, device="cuda")
+    cache.decode(0, 1, [0, 1, 2], torch_dev(q), out, h, k_new=torch_dev(kn), v_new=torch_dev(vn),
+                 flags=TE_ATTN_ADVANCE)
+    eng.synchronize()
+    got = out.cpu().numpy()
+    for i, s in enumerate((0, 1, 2)):
+        expect, kb, vb = _oracle_decode(port, raw[s][0], raw[s][1], q[0, i], 0, hkv, hd, h)
+        close(got[0, i], expect)
+        kg, vg = cache.read_f16(0, s, 0, lens[s])
+        assert np.array_equal(kg, kb) and np.array_equal(vg, vb)
+    cache.close()
+    eng.close()
+
+
 def test_decode_ragged_multi_layer_multi_seq(port):
     """Ragged batch (several sequences, several layers) in one launch, small chunks."""
     import torch

@@ -241,14 +241,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     }
     fence_mbarrier_init();
   }
+  if (tid == 32 * kConsumerWarps) {
+    prefetch_tmap(&p.tmap_k);
+    prefetch_tmap(&p.tmap_v);
+  }
   __syncthreads();
+  // Launched as a programmatic dependent: everything above overlaps the
+  // previous kernel's tail; all global reads and writes come after this wait.
+  // The next kernel may be scheduled as soon as every CTA has started.
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == kConsumerWarps) {
-    // ---- producer warp: q prefetch + fused append + K/V TMA ring -------------
-    if (lane == 0) {
-      prefetch_tmap(&p.tmap_k);
-      prefetch_tmap(&p.tmap_v);
-    }
+    // ---- producer warp: q prefetch + K/V TMA ring -----------------------------
     const uint64_t policy = policy_evict_first();
     uint32_t sidx = 0, k = 0;
     bool ok = true;
@@ -293,8 +298,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
-      // Page-table entries of this chunk, one per lane, read together up front
-      // (the loop refreshes the batch every 32 pages).
+      // Page ids: computed for a sequence whose pages are consecutive in the
+      // pool; otherwise table entries of this chunk, one per lane, read
+      // together up front (the loop refreshes the batch every 32 pages).
       const int pg0 = w.t0 / p.page_tokens;
       int pg_batch = -1;
       int pg_reg = 0;
@@ -302,12 +308,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         const int slot = sidx % R;
         const int tok = w.t0 + s * kStageTokens;
         const int rel = tok / p.page_tokens - pg0;
-        if ((rel >> 5) != pg_batch) {
+        if (se.page_base < 0 && (rel >> 5) != pg_batch) {
           pg_batch = rel >> 5;
           const int idx = pg0 + pg_batch * 32 + lane;
           pg_reg = idx < p.max_pages_per_seq ? p.page_table[se.slot * p.max_pages_per_seq + idx] : 0;
         }
-        const int page = __shfl_sync(0xffffffffu, pg_reg, rel & 31);
+        const int page = se.page_base >= 0 ? se.page_base + pg0 + rel : __shfl_sync(0xffffffffu, pg_reg, rel & 31);
         if (lane == 0) {
           if (sidx >= (uint32_t)R && !mbar_wait(&empty[slot], ((sidx / R) - 1) & 1)) {
             set_error(p.error, 1);
@@ -617,7 +623,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         const float* csk = se.new_pos != se.q_pos ? nb + 2 * HD : cs;
         float* res = reinterpret_cast<float*>(smem + C::kOffRes + b * C::kResBytes);  // scores[16], v[HD]
         const int new_idx = se.len - 1;
-        const int page = p.page_table[se.slot * p.max_pages_per_seq + new_idx / p.page_tokens];
+        const int page = se.page_base >= 0 ? se.page_base + new_idx / p.page_tokens
+                                           : p.page_table[se.slot * p.max_pages_per_seq + new_idx / p.page_tokens];
         const size_t row = ((size_t)((p.layer_begin + w.layer_local) * p.num_pages + page) * p.kv_heads + w.kvh) *
                                p.page_tokens + (new_idx % p.page_tokens);
         for (int i = lane; i < half; i += 32) {
@@ -1088,8 +1095,20 @@ cudaError_t launch_decode_impl(const DecodeParams& p, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  decode_f16_kernel<HD, GP><<<p.grid, kThreads, C::kSmemBytes, s>>>(p);
-  return cudaGetLastError();
+  // Programmatic dependent launch: the CTAs may become resident (on SMs the
+  // previous kernel has left) and set up their barriers before it completes;
+  // they wait for it (griddepcontrol.wait) before touching global memory.
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3((unsigned)p.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_f16_kernel<HD, GP>, p);
 }
 
 }  // namespace
@@ -1218,6 +1237,7 @@ extern "C" __attribute__((visibility("default"))) te_status te_attention_decode_
   p.seqs[0].len = (int32_t)n_tokens;
   p.seqs[0].q_pos = 0;
   p.seqs[0].new_pos = -1;
+  p.seqs[0].page_base = -1;  // the caller's table is read
   // Stream-K split whose partial records fit the fixed scratch.
   const size_t rec_bytes = G * decode_scratch_rec((int)head_dim) * sizeof(float);
   long long max_grid = sms;

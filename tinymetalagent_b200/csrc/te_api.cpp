@@ -50,6 +50,7 @@ struct te_kv_cache {
   uint16_t* v_pool = nullptr;
   int32_t* d_page_table = nullptr;
   std::vector<int32_t> h_page_table;  // [max_seqs][pages_per_seq], -1 = unmapped
+  std::vector<uint32_t> contig;       // per sequence: leading pages that are consecutive in the pool
   std::vector<int64_t> len, offset;
   std::vector<int32_t> free_pages;
   float* d_cos = nullptr;
@@ -165,7 +166,16 @@ te_status ensure_pages(te_kv_cache* c, size_t seq, size_t tokens) {
                                       c->eng->stream);
     if (err != cudaSuccess) return cuda_fail(c->eng, err, "page table upload");
   }
+  uint32_t& run = c->contig[seq];
+  while (run < need && row[run] == row[0] + (int32_t)run) ++run;
   return TE_STATUS_OK;
+}
+
+// First page of `seq` when its pages covering `tokens` are consecutive in the
+// pool (the kernel then computes page ids instead of reading the table), or -1.
+int32_t contiguous_base(const te_kv_cache* c, size_t seq, size_t tokens) {
+  const size_t need = (tokens + c->d.page_tokens - 1) / c->d.page_tokens;
+  return need > 0 && c->contig[seq] >= need ? c->h_page_table[seq * c->pages_per_seq] : -1;
 }
 
 // Copies rows [n][kv_heads][hd] between a flat buffer and the paged pool.
@@ -442,6 +452,7 @@ TE_API te_status te_kv_cache_create(te_attn_engine* e, const te_kv_cache_desc* d
   }
   c->d_sin = c->d_cos + (size_t)d.max_position * half;
   c->h_page_table.assign((size_t)d.max_seqs * pps, -1);
+  c->contig.assign(d.max_seqs, 0);
   c->len.assign(d.max_seqs, 0);
   c->offset.assign(d.max_seqs, 0);
   c->free_pages.resize(d.total_pages);
@@ -487,6 +498,7 @@ TE_API te_status te_kv_cache_seq_reset(te_kv_cache* c, size_t seq, size_t positi
     if (row[i] >= 0) c->free_pages.push_back(row[i]);
     row[i] = -1;
   }
+  c->contig[seq] = 0;
   c->len[seq] = 0;
   c->offset[seq] = (int64_t)position_offset;
   // Device rows of unmapped entries are never read (reads stop at the length).
@@ -643,6 +655,7 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
       if (st != TE_STATUS_OK) return st;
     }
   }
+  for (size_t i = 0; i < n_seqs; ++i) ent[i].page_base = contiguous_base(c, seq_ids[i], (size_t)ent[i].len);
 
   // Device staging for host buffers.
   const size_t q_elems = n_layers * n_seqs * heads * hd;

@@ -24,6 +24,7 @@ struct SeqEntry {
   int32_t new_pos;      // RoPE position of the appended token, or -1 (no append)
   int32_t stage_begin;  // first 64-token stage of this sequence within a (layer, kv head) block
   int32_t n_stages;     // max(1, ceil(old tokens / 64)): the stages of tokens cached before the call
+  int32_t page_base;    // >= 0: the sequence's pages are page_base, page_base + 1, ... (no table read); -1: read the table
 };
 
 constexpr int kMaxParamSeqs = 64;  // sequences per decode launch

@@ -251,6 +251,12 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
+// Programmatic dependent launch: wait until the grids this one depends on
+// have completed and their memory is visible; allow the dependent grid to be
+// scheduled.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // GPU-scope acquire-release fence: orders this thread's earlier memory
 // operations (and those it has observed, e.g. through __syncwarp) before its
 // later ones, without the full sequential-consistency fence of __threadfence.
