@@ -97,6 +97,34 @@ def test_prefill_f16_inputs_multi_layer(port):
     eng.close()
 
 
+def test_prefill_f16_no_rope(port):
+    """f16 inputs with RoPE off: the kernel reads the queries as they are (no rotation)."""
+    import torch
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16, TE_ATTN_NO_ROPE, AttnEngine
+    h, hkv, hd, s = 16, 2, 128, 300
+    rng = np.random.default_rng(21)
+    q16 = rng.standard_normal((1, s, h, hd)).astype(np.float16)
+    k16 = rng.standard_normal((1, s, hkv, hd)).astype(np.float16)
+    v16 = rng.standard_normal((1, s, hkv, hd)).astype(np.float16)
+    eng = AttnEngine(0)
+    cache = eng.kv_cache(layers=1, max_seqs=1, max_tokens_per_seq=s, kv_heads=hkv, head_dim=hd)
+    out = torch.zeros((1, s, h, hd), dtype=torch.float32, device="cuda")
+    t16 = lambda a: dev(a.view(np.uint16)).view(torch.float16)  # noqa: E731
+    cache.prefill(0, 1, 0, t16(q16), t16(k16), t16(v16), s, h, out,
+                  TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | TE_ATTN_NO_ROPE)
+    eng.synchronize()
+    got = out.cpu().numpy()[0]
+    k = k16[0].astype(np.float32).ravel()
+    v = v16[0].astype(np.float32).ravel()
+    for t in (0, 1, 127, 128, 299):
+        exp = port.attention_decode_f32(q16[0, t].astype(np.float32).ravel(), k, v, t, h, hkv, hd)
+        close(got[t], exp.reshape(h, hd))
+    kg, vg = cache.read_f16(0, 0, 0, s)
+    assert np.array_equal(kg, k16[0].view(np.uint16)) and np.array_equal(vg, v16[0].view(np.uint16))
+    cache.close()
+    eng.close()
+
+
 @pytest.mark.parametrize("split", [(100, 60), (128, 128), (70, 200)])
 def test_chunked_prefill_then_decode(port, split):
     """Prefill in two calls (the second attends to the cached first part), then one decode step."""

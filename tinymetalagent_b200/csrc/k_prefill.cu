@@ -50,8 +50,10 @@ constexpr int kThreads = 320;
 constexpr int OFF_QA = 0;
 constexpr int OFF_QB = kTile;
 constexpr int OFF_KV = 2 * kTile;           // stage s: K at OFF_KV + s*2*kTile, V at + kTile
-constexpr int OFF_BAR = OFF_KV + 4 * kTile; // 196608
+constexpr int OFF_OST = OFF_KV + 4 * kTile; // output staging: 4 KiB (32 rows x 128 B) per softmax warp
+constexpr int OFF_BAR = OFF_OST + 8 * 4096;  // 229376
 constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
 
 enum Bar {
   Q_FULL = 0, Q_EMPTY, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1,
@@ -166,13 +168,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         } else {
           mbar_arrive_expect_tx(&bar[Q_FULL], I.has_b ? 2 * kTile : kTile);
           for (int t = 0; t < 1 + I.has_b; ++t) {
-            const int qrow = (I.layer_local * p.heads + I.head_a + t) * p.n_tokens_padded + I.qt * BM;
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
               for (int c = 0; c < 2; ++c)
-                tma_load_2d(smem + (t ? OFF_QB : OFF_QA) + c * kHalf + h * kBox, &p.tmap_q, &bar[Q_FULL], c * 64,
-                            qrow + h * 64);
+                tma_load_4d(smem + (t ? OFF_QB : OFF_QA) + c * kHalf + h * kBox, &p.tmap_q, &bar[Q_FULL], c * 64,
+                            I.head_a + t, I.qt * BM + h * 64, I.layer_local);
           }
         }
       }
@@ -381,24 +382,33 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         if (lane == 0) mbar_arrive(&bar[P_FULL_A + t]);
       }
       if (!ok) break;
-      // epilogue: O / l -> out[layer][token][head][:]
+      // epilogue: O / l -> out[layer][token][head][:].  Each warp writes its 32
+      // rows in four 32-column blocks: registers -> 128B-swizzled staging ->
+      // one TMA store of 32 full 128-byte row segments (rows past n_tokens are
+      // clipped by the tensor map).
       if (!mbar_wait_warp(&bar[O_FULL_A + t], oc & 1)) { ok = false; break; }
       ++oc;
       tc_fence_after();
-      const int tok = I.qt * BM + row;
       const float inv = 1.f / l;
-      float* dst = p.out + (((size_t)I.layer_local * p.n_tokens + tok) * p.heads + I.head_a + t) * HD;
+      const uint32_t stg = smem_u32(smem + OFF_OST + (warp - 2) * 4096);
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         float o[32];
         tmem_ld32(o_addr + c * 32, o);
         tmem_wait_ld();
-        if (tok < p.n_tokens) {
+        if (lane == 0) bulk_wait_read0();  // the previous block's store has read the staging
+        __syncwarp();
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            *reinterpret_cast<float4*>(dst + c * 32 + e) =
-                make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
-          }
+        for (int k = 0; k < 8; ++k) {
+          sts128(stg + lane * 128 + ((k ^ (lane & 7)) << 4), __float_as_uint(o[4 * k] * inv),
+                 __float_as_uint(o[4 * k + 1] * inv), __float_as_uint(o[4 * k + 2] * inv),
+                 __float_as_uint(o[4 * k + 3] * inv));
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_4d(&p.tmap_o, stg, c * 32, I.head_a + t, I.qt * BM + quad * 32, I.layer_local);
+          bulk_commit();
         }
       }
       tc_fence_before();
@@ -406,6 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       if (lane == 0) mbar_arrive(&bar[O_EMPTY_A + t]);
     }
     if (!ok) { set_error(p.error, 17); *abort_flag = 1; }
+    if (lane == 0) bulk_wait0();  // this warp's output stores are complete before the CTA exits
   }
 
   tc_fence_before();

@@ -140,6 +140,36 @@ bool make_tmap_f16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t col
   return r == CUDA_SUCCESS;
 }
 
+// Prefill queries [layers][tokens][heads][hd] f16 as a 4-D tensor map: one box
+// is 64 tokens x 64 dims of one head (128B swizzle); tokens past the end read
+// as zeros.
+bool make_tmap_q_f16(CUtensorMap* m, const void* base, uint64_t hd, uint64_t heads, uint64_t tokens, uint64_t layers) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {hd, heads, tokens, layers};
+  cuuint64_t strides[3] = {hd * 2, heads * hd * 2, tokens * heads * hd * 2};
+  cuuint32_t box[4] = {64, 1, 64, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Prefill output [layers][tokens][heads][hd] f32 as a 4-D tensor map; one TMA
+// store writes 32 tokens x 32 floats of one head (128B swizzle).
+bool make_tmap_out_f32(CUtensorMap* m, void* base, uint64_t hd, uint64_t heads, uint64_t tokens, uint64_t layers) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {hd, heads, tokens, layers};
+  cuuint64_t strides[3] = {hd * 4, heads * hd * 4, tokens * heads * hd * 4};
+  cuuint32_t box[4] = {32, 1, 32, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 size_t pool_row(const te_kv_cache* c, size_t layer, int32_t page, size_t kvh, size_t tok_in_page) {
   return ((layer * c->d.total_pages + (size_t)page) * c->d.kv_heads + kvh) * c->d.page_tokens + tok_in_page;
 }
@@ -778,8 +808,9 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   if (heads % hkv != 0) return fail(e, TE_STATUS_INVALID_ARGUMENT, "heads must be a multiple of kv_heads");
   if (hd != 128) return fail(e, TE_STATUS_UNSUPPORTED, "prefill kernel is built for head_dim 128");
   if (!(flags & TE_ATTN_HOST_BUFFERS) &&
-      ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u)) {
-    return fail(e, TE_STATUS_INVALID_ARGUMENT, "q, k and v must be 16-byte aligned");
+      ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+        reinterpret_cast<uintptr_t>(out)) & 15u)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "q, k, v and out must be 16-byte aligned");
   }
   const size_t q_offset = (size_t)c->len[seq];
   const size_t total = q_offset + n_tokens;
@@ -821,7 +852,7 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
     dv = sv;
   }
 
-  // 1) RoPE(k) + f16 append of the new tokens for every layer
+  // 1) RoPE(k) + f16 append of the new tokens for every layer (launched with 2)
   AppendParams a{};
   a.k = dk;
   a.v = dv;
@@ -841,36 +872,44 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   a.head_dim = (int32_t)hd;
   a.num_pages = (int32_t)c->d.total_pages;
   a.page_tokens = (int32_t)c->d.page_tokens;
-  err = launch_append_rope(a, e->stream);
-  if (err != cudaSuccess) return cuda_fail(e, err, "append kernel launch");
-  e->launches++;
-
-  // 2) rotated f16 queries, head-major and padded to 128-row tiles
-  err = grow(e, &e->qh, &e->qh_bytes, qh_rows * hd * sizeof(__half), false);
-  if (err != cudaSuccess) return cuda_fail(e, err, "prefill query scratch allocation");
+  // 2) f16 queries for the kernel: f16 inputs without RoPE are read as they
+  // are; otherwise they are rotated (and converted) into scratch in the same
+  // layout, in one pass with the append.
+  const bool with_q = !(a.input_f16 && !a.rope);
+  const void* qf16 = dq;
   QPrepParams qp{};
-  qp.q = dq;
-  qp.qh = reinterpret_cast<__half*>(e->qh);
-  qp.rope_cos = c->d_cos;
-  qp.rope_sin = c->d_sin;
-  qp.input_f16 = a.input_f16;
-  qp.rope = a.rope;
-  qp.n_layers = (int32_t)n_layers;
-  qp.n_tokens = (int32_t)n_tokens;
-  qp.n_tokens_padded = (int32_t)n_pad;
-  qp.heads = (int32_t)heads;
-  qp.head_dim = (int32_t)hd;
-  qp.first_pos = a.first_pos;
-  err = launch_q_prep(qp, e->stream);
-  if (err != cudaSuccess) return cuda_fail(e, err, "query preparation launch");
+  if (with_q) {
+    err = grow(e, &e->qh, &e->qh_bytes, n_layers * n_tokens * heads * hd * sizeof(__half), false);
+    if (err != cudaSuccess) return cuda_fail(e, err, "prefill query scratch allocation");
+    qp.q = dq;
+    qp.qh = reinterpret_cast<__half*>(e->qh);
+    qp.rope_cos = c->d_cos;
+    qp.rope_sin = c->d_sin;
+    qp.input_f16 = a.input_f16;
+    qp.rope = a.rope;
+    qp.n_layers = (int32_t)n_layers;
+    qp.n_tokens = (int32_t)n_tokens;
+    qp.heads = (int32_t)heads;
+    qp.head_dim = (int32_t)hd;
+    qp.first_pos = a.first_pos;
+    qf16 = e->qh;
+  }
+  a.error = e->d_error;
+  err = launch_prefill_prep(a, qp, with_q, e->sm_count, e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "append / query preparation launch");
   e->launches++;
 
   // 3) causal flash attention on tcgen05
   PrefillParams p;
   std::memset(&p, 0, sizeof(p));
-  if (!make_tmap_f16(&p.tmap_q, e->qh, qh_rows, hd, 64)) return fail(e, TE_STATUS_RUNTIME_ERROR, "query tensor map");
+  if (!make_tmap_q_f16(&p.tmap_q, qf16, hd, heads, n_tokens, n_layers)) {
+    return fail(e, TE_STATUS_RUNTIME_ERROR, "query tensor map");
+  }
   p.tmap_k = c->tmap_k;
   p.tmap_v = c->tmap_v;
+  if (!make_tmap_out_f32(&p.tmap_o, dout, hd, heads, n_tokens, n_layers)) {
+    return fail(e, TE_STATUS_RUNTIME_ERROR, "output tensor map");
+  }
   p.page_table_row = c->d_page_table + seq * c->pages_per_seq;
   p.out = dout;
   p.error = e->d_error;

@@ -154,31 +154,37 @@ struct AppendParams {
   int32_t head_dim;
   int32_t num_pages;
   int32_t page_tokens;
+  int* error;               // engine error word (bounded waits of the streamed variant)
 };
 cudaError_t launch_append_rope(const AppendParams& p, cudaStream_t s);
 
-// Rotates (optionally) and converts prefill queries to a head-major f16 buffer
-// qh[n_layers][heads][n_tokens_padded][hd] for the prefill kernel's TMA loads.
+// Rotates (optionally) and converts prefill queries to f16 in the same
+// [n_layers][n_tokens][heads][hd] layout (the prefill kernel reads f16 queries)
 struct QPrepParams {
-  const void* q;            // [n_layers][n_tokens][heads][hd]
-  __half* qh;
+  const void* q;            // [n_layers][n_tokens][heads][hd], fp32 or f16
+  __half* qh;               // same layout, f16
   const float* rope_cos;
   const float* rope_sin;
   int32_t input_f16;
   int32_t rope;
   int32_t n_layers;
   int32_t n_tokens;
-  int32_t n_tokens_padded;
   int32_t heads;
   int32_t head_dim;
   int32_t first_pos;
 };
 cudaError_t launch_q_prep(const QPrepParams& p, cudaStream_t s);
+// One pass over a prefill call's inputs: the K/V append of `a` and, when
+// with_q, the query preparation of `q` (same layers and tokens).
+cudaError_t launch_prefill_prep(const AppendParams& a, const QPrepParams& q, bool with_q, int sm_count,
+                                cudaStream_t s);
 
 struct PrefillParams {
-  CUtensorMap tmap_q;   // [n_layers*heads*n_tokens_padded][hd] f16, box 64x64, 128B swizzle
+  CUtensorMap tmap_q;   // f16 queries [n_layers][n_tokens][heads][hd], box 64 x 1 x 64 x 1, 128B swizzle
+                        // (rows past n_tokens read as zeros)
   CUtensorMap tmap_k;   // K pool view (as for decode)
   CUtensorMap tmap_v;
+  CUtensorMap tmap_o;   // out as [n_layers][n_tokens][heads][hd] f32, box 32 x 1 x 32 x 1, 128B swizzle
   const int32_t* page_table_row;  // page table row of the sequence
   float* out;           // [n_layers][n_tokens][heads][hd]
   int* error;
