@@ -14,14 +14,15 @@
 // item).  Items are ordered by decreasing causal length and dealt round-robin
 // to a persistent grid of one CTA per SM.
 //
-// Warp roles (320 threads):
+// Warp roles (384 threads):
 //   warp 0      TMA producer: the Q tiles, then K/V tiles (128 keys) into a 2-stage ring
 //   warp 1      TMEM owner; lane 0 issues tcgen05.mma in the order
 //                 QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) | ...
 //               (S = Q K^T: M=128 queries, N=128 keys, K=128 dims, A/B from shared
 //                memory; O += P V: A = P from tensor memory, B = V from shared memory)
-//   warps 2-5   softmax + epilogue of head A, one query row per thread (TMEM lane)
-//   warps 6-9   softmax + epilogue of head B
+//   warps 2-3   idle (they complete warpgroup 0, whose registers go to the softmax)
+//   warps 4-7   softmax + epilogue of head A, one query row per thread (TMEM lane)
+//   warps 8-11  softmax + epilogue of head B
 // Tensor memory: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512) columns;
 // P (f16, two per 32-bit column) overwrites the first 64 columns of its S once
 // S has been read.  tcgen05.mma operations of one thread execute in issue
@@ -45,7 +46,10 @@ constexpr int HD = 128;                     // head dim
 constexpr int kTile = BM * HD * 2;          // 32 KiB: 128 rows x 128 f16, as two 64-column halves
 constexpr int kHalf = kTile / 2;            // 16 KiB: 128 rows x 128 B
 constexpr int kBox = 64 * 128;              // 8 KiB TMA box: 64 rows x 64 f16
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;               // three warpgroups
+constexpr int kRegsLow = 120;                // per thread, warpgroup 0 (producer, MMA issuer)
+constexpr int kRegsHigh = 184;              // per thread, the two softmax warpgroups
+static_assert(128 * (kRegsLow + 2 * kRegsHigh) <= 65536, "register split exceeds the launch's registers");
 
 constexpr int OFF_QA = 0;
 constexpr int OFF_QB = kTile;
@@ -146,7 +150,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int total = p.q_offset + p.n_tokens;
-
+  // Register split: warpgroup 0 (producer, MMA issuer, two idle warps) gives
+  // registers to the softmax warpgroups, which hold a 128-score row each.
+  // 128 x (kRegsLow + 2 * kRegsHigh) <= 65536 registers of the launch.
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow) : "memory");
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     // The whole warp walks the items (page-table entries are read one per lane
@@ -298,9 +306,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       umma_commit(&bar[DRAIN]);
       if (!mbar_wait(&bar[DRAIN], 0)) set_error(p.error, 16);
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh) : "memory");
     // ------------------------------------------------------------ softmax + epilogue
-    const int t = warp >= 6 ? 1 : 0;  // which head of the pair
+    const int t = warp >= 8 ? 1 : 0;  // which head of the pair
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
@@ -333,36 +343,46 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             if (j * BN + e > key_limit) x[e] = -INFINITY;
           }
         }
-        // row max of the raw scores (8 independent partial maxima)
+        // row max of the raw scores (8 independent partial maxima, 3-input max)
         float pm[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) pm[u] = x[u];
+        for (int u = 0; u < 8; ++u) pm[u] = fmax3(x[u], x[u + 8], x[u + 16]);
 #pragma unroll
-        for (int e = 8; e < BN; ++e) pm[e & 7] = fmaxf(pm[e & 7], x[e]);
-        const float tmax_raw = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                                     fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        for (int e = 24; e < BN; e += 16) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) pm[u] = fmax3(pm[u], x[e + u], e + 8 + u < BN ? x[e + 8 + u] : x[e + u]);
+        }
+        const float tmax_raw = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
         const float m_new = fmaxf(m, tmax_raw * sl);  // scaling by sl > 0 preserves the max
         // lazy rescale: keep the old reference max unless the row max grew by > 2^8
         const bool rescale = j > 0 && m_new > m + 8.f;
         const float alpha = rescale ? ex2(m - m_new) : 1.f;
         if (j == 0 || rescale) m = m_new;
         // p = 2^(s*scale - m) -> f16 pairs over the first half of S's columns
-        // (S is entirely in registers, so overwriting its columns is safe)
-        const float neg_m = -m;
-        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // (S is entirely in registers, so overwriting its columns is safe).
+        // Scale, bias and row sum take two elements per f32x2 instruction.
+        const uint64_t sl2 = f2_pack(sl, sl);
+        const uint64_t nm2 = f2_pack(-m, -m);
+        uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float e0 = ex2(fmaf(x[c * 32 + e], sl, neg_m));
-            const float e1 = ex2(fmaf(x[c * 32 + e + 1], sl, neg_m));
-            ps[e & 7] += e0;
-            ps[(e + 1) & 7] += e1;
+            const uint64_t y = f2_fma(f2_pack(x[c * 32 + e], x[c * 32 + e + 1]), sl2, nm2);
+            float y0, y1;
+            f2_unpack(y, y0, y1);
+            const uint64_t ev = f2_pack(ex2(y0), ex2(y1));
+            ps2[(e >> 1) & 3] = f2_add(ps2[(e >> 1) & 3], ev);
+            float e0, e1;
+            f2_unpack(ev, e0, e1);
             pk[e >> 1] = pack_half2(e0, e1);
           }
           tmem_st16u(s_addr + c * 16, pk);
         }
+        float ps[8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) f2_unpack(ps2[u], ps[2 * u], ps[2 * u + 1]);
         l = l * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
         if (rescale) {
           // O is stable: the commit that signalled this S tracks the previous P V too
@@ -390,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       ++oc;
       tc_fence_after();
       const float inv = 1.f / l;
-      const uint32_t stg = smem_u32(smem + OFF_OST + (warp - 2) * 4096);
+      const uint32_t stg = smem_u32(smem + OFF_OST + (warp - 4) * 4096);
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         float o[32];
