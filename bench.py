@@ -45,13 +45,15 @@ PREFILL_TOKENS = 2048
 METRIC = "decode-attn KV GB/s (% of HBM peak) @Qwen-3B ctx4K; prefill attn TFLOPS"
 
 
-def step_bytes(n_attended: int, layers: int = LAYERS) -> int:
-    """Algorithmic bytes of one decode step: per layer, read the K and V cache
-    (n_attended tokens x kv_heads x head_dim x f16 each), read q and the new raw
-    k/v (fp32), write the appended f16 k/v row and the fp32 output."""
-    kv_read = 2 * n_attended * KV_HEADS * HEAD_DIM * 2
-    qo = 2 * HEADS * HEAD_DIM * 4
-    new = 2 * KV_HEADS * HEAD_DIM * 4 + 2 * KV_HEADS * HEAD_DIM * 2
+def step_bytes(n_attended: int, layers: int = LAYERS, heads: int = HEADS, kv_heads: int = KV_HEADS,
+               head_dim: int = HEAD_DIM, appended: bool = True) -> int:
+    """Algorithmic bytes of one decode step of one sequence: per layer, read the
+    K and V cache of the tokens cached before the step (f16), read q and the
+    new raw k/v (fp32), write the appended f16 k/v row and the fp32 output."""
+    cached = n_attended - 1 if appended else n_attended
+    kv_read = 2 * cached * kv_heads * head_dim * 2
+    qo = 2 * heads * head_dim * 4
+    new = (2 * kv_heads * head_dim * 4 + 2 * kv_heads * head_dim * 2) if appended else 0
     return layers * (kv_read + qo + new)
 
 
@@ -355,6 +357,14 @@ def run_gpu(args) -> None:
     if not args.no_prefill:
         prefill = run_prefill(eng, stream, tc_peak, peak_src, args, world, rank, local)
 
+    # ---- BASELINE configs 4 (sequence-sharded batch) and 5 (KV split + NCCL merge) ----
+    ragged = long = None
+    if not args.no_configs:
+        cache.close()
+        cache = None
+        ragged = run_ragged7b(eng, stream, hbm_peak, peak_src, args, world, rank)
+        long = run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank)
+
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.is_file():
@@ -381,9 +391,12 @@ def run_gpu(args) -> None:
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "ragged7b": ragged,
+            "long7b": long,
         }
         print(json.dumps(line), flush=True)
-    cache.close()
+    if cache is not None:
+        cache.close()
     eng.close()
     if world > 1:
         dist.destroy_process_group()
@@ -439,6 +452,171 @@ def run_prefill(eng, stream, tc_peak, peak_src, args, world, rank, local):
                          "frac": round(tflops / tc_peak, 4), "peak_source": f"{peak_src} (bf16 dense burst)"}}
 
 
+# Config 4 / 5 shapes (Qwen2.5-7B: 28 layers, 28 query heads, 4 KV heads).
+L7, H7, KV7 = 28, 28, 4
+
+
+def _time_steps(stream, fn, steps, world, dist):
+    """Device time of `steps` calls of fn() on `stream` (barrier + sync both
+    sides), max over ranks, in ms."""
+    import torch
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_ragged7b(eng, stream, hbm_peak, peak_src, args, world, rank):
+    """Qwen2.5-7B-shaped batched decode -- 28 layers,
+    H28/Hkv4/hd128, 64 independent sequences of seeded uniform-random length in
+    [256, 8192], f16 KV N(0,1).  Sequences are sharded across ranks (longest
+    first onto the least-loaded rank); each rank runs one te_attention_decode
+    per step over all its sequences and layers (RoPE + append + stream-K split
+    decode), captured in a CUDA graph.  Strong scaling: 64 sequences in total."""
+    import torch
+    import torch.distributed as dist
+
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16, TE_ATTN_NO_ROPE
+    from tinymetalagent_b200.dist import shard_sequences
+    lens = np.random.default_rng(7).integers(256, 8193, size=64)
+    mine = shard_sequences(lens.tolist(), world)[rank]
+    steps = args.cfg_steps
+    n_my = len(mine)
+    cap = int(lens[mine].max()) + steps + 1
+    cache = eng.kv_cache(layers=L7, max_seqs=n_my, max_tokens_per_seq=cap, kv_heads=KV7, head_dim=HEAD_DIM,
+                         rope_theta=THETA)
+    g = torch.Generator(device="cuda").manual_seed(4000 + rank)
+    with torch.cuda.stream(stream):
+        blk_k = torch.randn((8192, KV7, HEAD_DIM), generator=g, device="cuda").half()
+        blk_v = torch.randn((8192, KV7, HEAD_DIM), generator=g, device="cuda").half()
+        q = torch.randn((L7, n_my, H7, HEAD_DIM), generator=g, device="cuda")
+        kn = torch.randn((L7, n_my, KV7, HEAD_DIM), generator=g, device="cuda")
+        vn = torch.randn((L7, n_my, KV7, HEAD_DIM), generator=g, device="cuda")
+        out = torch.empty((L7, n_my, H7, HEAD_DIM), device="cuda")
+    stream.synchronize()
+    for j, sid in enumerate(mine):
+        n = int(lens[sid])
+        for layer in range(L7):
+            off = (layer * 977 + int(sid) * 131) % (8192 - n + 1)  # a different window of the random block per layer
+            flags = TE_ATTN_INPUT_F16 | TE_ATTN_NO_ROPE | (TE_ATTN_ADVANCE if layer == L7 - 1 else 0)
+            cache.append_rope(layer, 1, j, blk_k[off:off + n], blk_v[off:off + n], n, flags)
+        cache.reserve(j, n + steps + 1)
+    eng.synchronize()
+    slots = list(range(n_my))
+
+    def rewind():
+        for j, sid in enumerate(mine):
+            cache.truncate(j, int(lens[sid]))
+
+    def step():
+        cache.decode(0, L7, slots, q, out, H7, k_new=kn, v_new=vn, flags=TE_ATTN_ADVANCE)
+
+    for _ in range(3):
+        step()
+    eng.synchronize()
+    rewind()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(steps):
+            step()
+    rewind()
+    with torch.cuda.stream(stream):
+        graph.replay()  # warm
+    stream.synchronize()
+
+    def replay():
+        with torch.cuda.stream(stream):
+            graph.replay()
+
+    ms = _time_steps(stream, replay, 1, world, dist)
+    del graph
+    bytes_rank = sum(step_bytes(int(lens[sid]) + i + 1, L7, H7, KV7) for sid in mine for i in range(steps))
+    t = torch.tensor([float(bytes_rank)], device="cuda")
+    if world > 1:
+        dist.all_reduce(t)
+    bytes_all = float(t.item())
+    gbs = bytes_all / (ms / 1e3) / 1e9
+    cache.close()
+    return {"metric": "batched decode tokens/s (BASELINE config 4)", "value": round(64 * steps / (ms / 1e3), 1),
+            "unit": "tokens/s", "scaling": "strong", "steps": steps, "ms_per_step": round(ms / steps, 4),
+            "workload": "ragged7b: 64 sequences, lengths U[256, 8192] (seed 7), 28 layers, H28/Hkv4/hd128, "
+                        "f16 KV N(0,1), one token appended per sequence and layer per step",
+            "sequences_per_rank": n_my, "kv_gbs": round(gbs, 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(gbs / world / hbm_peak, 4), "per": "GPU (max-over-ranks time)",
+                         "peak_source": f"{peak_src} (burst copy)"}}
+
+
+def run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank):
+    """one 32768-token sequence, 28 layers, H28/Hkv4/hd128,
+    f16 KV N(0,1), RoPE theta 1e6.  The KV sequence is split across ranks
+    (contiguous token ranges); per step every rank computes partial (acc, m, l)
+    records over its range (the tail rank also appends the new token), the
+    records are all-gathered over NCCL and merged by log-sum-exp
+    (te_attention_merge_partials).  Strong scaling: one sequence in total."""
+    import torch
+    import torch.distributed as dist
+
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16, TE_ATTN_NO_ROPE
+    from tinymetalagent_b200.dist import KVSplitDecoder, ShardSpec
+    n_ctx = 32768
+    steps = args.long_steps
+    spec = ShardSpec.plan(rank, world, n_ctx)
+    n_local = spec.end - spec.begin
+    extra = steps + 8 if spec.is_tail else 0
+    cache = eng.kv_cache(layers=L7, max_seqs=1, max_tokens_per_seq=n_local + extra, kv_heads=KV7, head_dim=HEAD_DIM,
+                         max_position=n_ctx + steps + 16, rope_theta=THETA)
+    cache.reset(0, spec.begin)
+    g = torch.Generator(device="cuda").manual_seed(5000 + rank)
+    for layer in range(L7):
+        with torch.cuda.stream(stream):
+            k = torch.randn((n_local, KV7, HEAD_DIM), generator=g, device="cuda").half()
+            v = torch.randn((n_local, KV7, HEAD_DIM), generator=g, device="cuda").half()
+        stream.synchronize()
+        cache.append_rope(layer, 1, 0, k, v, n_local, TE_ATTN_INPUT_F16 | TE_ATTN_NO_ROPE |
+                          (TE_ATTN_ADVANCE if layer == L7 - 1 else 0))
+        del k, v
+    if spec.is_tail:
+        cache.reserve(0, n_local + extra)
+    eng.synchronize()
+    with torch.cuda.stream(stream):
+        q = torch.randn((L7, 1, H7, HEAD_DIM), generator=g, device="cuda")
+        kn = torch.randn((L7, 1, KV7, HEAD_DIM), generator=g, device="cuda")
+        vn = torch.randn((L7, 1, KV7, HEAD_DIM), generator=g, device="cuda")
+    stream.synchronize()
+    dec = KVSplitDecoder(spec, L7, H7, HEAD_DIM, cache=cache, engine=eng, device="cuda")
+
+    def step():
+        with torch.cuda.stream(stream):  # NCCL and the engine share the engine's stream
+            dec.step(q, kn, vn)
+
+    for _ in range(4):
+        step()
+    ms = _time_steps(stream, step, steps, world, dist)
+    bytes_all = sum(step_bytes(n_ctx + 4 + i + 1, L7, H7, KV7) for i in range(steps))
+    gbs = bytes_all / (ms / 1e3) / 1e9
+    cache.close()
+    return {"metric": "long-context decode tokens/s (BASELINE config 5)", "value": round(steps / (ms / 1e3), 1),
+            "unit": "tokens/s", "scaling": "strong", "steps": steps, "ms_per_step": round(ms / steps, 4),
+            "workload": "long7b: one sequence of 32768 cached tokens, 28 layers, H28/Hkv4/hd128, f16 KV N(0,1), "
+                        f"KV split over {world} rank(s), NCCL all-gather of (acc, m, l) + LSE merge per step",
+            "tokens_per_rank": n_local, "kv_gbs": round(gbs, 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(gbs / world / hbm_peak, 4), "per": "GPU (max-over-ranks time)",
+                         "peak_source": f"{peak_src} (burst copy)"}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -451,6 +629,9 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
     ap.add_argument("--no-graph", action="store_true", help="time the decode steps as eager launches")
     ap.add_argument("--prefill-steps", type=int, default=10)
+    ap.add_argument("--no-configs", action="store_true", help="skip the config-4 / config-5 measurements")
+    ap.add_argument("--cfg-steps", type=int, default=16, help="decode steps timed for config 4")
+    ap.add_argument("--long-steps", type=int, default=128, help="decode steps timed for config 5")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
