@@ -54,7 +54,7 @@ static_assert(128 * (kRegsLow + 2 * kRegsHigh) <= 65536, "register split exceeds
 constexpr int OFF_QA = 0;
 constexpr int OFF_QB = kTile;
 constexpr int OFF_KV = 2 * kTile;           // stage s: K at OFF_KV + s*2*kTile, V at + kTile
-constexpr int OFF_OST = OFF_KV + 4 * kTile; // output staging: 4 KiB (32 rows x 128 B) per softmax warp
+constexpr int OFF_OST = OFF_KV + 4 * kTile; // output staging: 2 x 2 KiB (32 rows x 64 B) per softmax warp
 constexpr int OFF_BAR = OFF_OST + 8 * 4096;  // 229376
 constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
@@ -403,9 +403,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       }
       if (!ok) break;
       // epilogue: O / l -> out[layer][token][head][:].  Each warp writes its 32
-      // rows in four 32-column blocks: registers -> 128B-swizzled staging ->
-      // one TMA store of 32 full 128-byte row segments (rows past n_tokens are
-      // clipped by the tensor map).
+      // rows in eight 16-column blocks: registers -> one of two 2 KiB 64B-
+      // swizzled staging buffers (alternating, so a block's store overlaps
+      // the next block's staging) -> one TMA store of 32 row segments (rows
+      // past n_tokens are clipped by the tensor map).
       if (!mbar_wait_warp(&bar[O_FULL_A + t], oc & 1)) { ok = false; break; }
       ++oc;
       tc_fence_after();
@@ -416,19 +417,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         float o[32];
         tmem_ld32(o_addr + c * 32, o);
         tmem_wait_ld();
-        if (lane == 0) bulk_wait_read0();  // the previous block's store has read the staging
-        __syncwarp();
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          sts128(stg + lane * 128 + ((k ^ (lane & 7)) << 4), __float_as_uint(o[4 * k] * inv),
-                 __float_as_uint(o[4 * k + 1] * inv), __float_as_uint(o[4 * k + 2] * inv),
-                 __float_as_uint(o[4 * k + 3] * inv));
-        }
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_4d(&p.tmap_o, stg, c * 32, I.head_a + t, I.qt * BM + quad * 32, I.layer_local);
-          bulk_commit();
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t buf = stg + h * 2048;
+          if (lane == 0) bulk_wait_read1();  // the store issued from this buffer two blocks ago has read it
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float* v = o + 16 * h + 4 * k;
+            sts128(buf + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4), __float_as_uint(v[0] * inv),
+                   __float_as_uint(v[1] * inv), __float_as_uint(v[2] * inv), __float_as_uint(v[3] * inv));
+          }
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_4d(&p.tmap_o, buf, c * 32 + h * 16, I.head_a + t, I.qt * BM + quad * 32, I.layer_local);
+            bulk_commit();
+          }
         }
       }
       tc_fence_before();

@@ -157,16 +157,16 @@ bool make_tmap_q_f16(CUtensorMap* m, const void* base, uint64_t hd, uint64_t hea
 }
 
 // Prefill output [layers][tokens][heads][hd] f32 as a 4-D tensor map; one TMA
-// store writes 32 tokens x 32 floats of one head (128B swizzle).
+// store writes 32 tokens x 16 floats of one head (64B swizzle).
 bool make_tmap_out_f32(CUtensorMap* m, void* base, uint64_t hd, uint64_t heads, uint64_t tokens, uint64_t layers) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[4] = {hd, heads, tokens, layers};
   cuuint64_t strides[3] = {hd * 4, heads * hd * 4, tokens * heads * hd * 4};
-  cuuint32_t box[4] = {32, 1, 32, 1};
+  cuuint32_t box[4] = {16, 1, 32, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
