@@ -124,29 +124,37 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 class CpuDecode:
-    """The reference CPU attention (te_attention_decode_f32) on config-2
-    layer-steps: each call rotates q (te_rope_f32) and attends one layer's
-    fp32-widened f16 cache of 4097 tokens; independent layers run on `threads`
-    host threads (ctypes releases the GIL during each C call)."""
+    """The reference CPU attention (te_attention_decode_f32) on decode
+    layer-steps (config 2 by default): each call rotates q (te_rope_f32) and
+    attends one layer's fp32-widened f16 cache of n tokens; independent layers
+    run on `threads` host threads (ctypes releases the GIL during each C call)."""
 
-    def __init__(self, kind: str, threads: int, n_layers: int = LAYERS):
+    def __init__(self, kind: str, threads: int, n_layers: int = LAYERS, n: int = CTX0 + 1, heads: int = HEADS,
+                 kv_heads: int = KV_HEADS, scale: float = 0.5, shared_kv: bool = False):
         from oracle import oracle as O
         self.lib = O.ref() if kind == "reference" else O.port()
         self.threads = threads
-        self.n = CTX0 + 1
+        self.n, self.heads, self.kv_heads = n, heads, kv_heads
         self.n_layers = n_layers
         rng = np.random.default_rng(0)
-        shape = self.n * KV_HEADS * HEAD_DIM
-        self.ks = [(rng.standard_normal(shape) * 0.5).astype(np.float16).astype(np.float32) for _ in range(n_layers)]
-        self.vs = [(rng.standard_normal(shape) * 0.5).astype(np.float16).astype(np.float32) for _ in range(n_layers)]
-        self.qs = [rng.standard_normal(HEADS * HEAD_DIM).astype(np.float32) for _ in range(n_layers)]
+        shape = self.n * kv_heads * HEAD_DIM
+        def cache():
+            return (rng.standard_normal(shape, dtype=np.float32) * scale).astype(np.float16).astype(np.float32)
+        if shared_kv:  # one K and one V shared by the layer calls (large caches: bounded set-up time)
+            k, v = cache(), cache()
+            self.ks, self.vs = [k] * n_layers, [v] * n_layers
+        else:
+            self.ks = [cache() for _ in range(n_layers)]
+            self.vs = [cache() for _ in range(n_layers)]
+        self.qs = [rng.standard_normal(heads * HEAD_DIM).astype(np.float32) for _ in range(n_layers)]
         from concurrent.futures import ThreadPoolExecutor
         self.pool = ThreadPoolExecutor(max_workers=threads)
 
     def _one(self, i):
         q = self.qs[i].copy()
-        self.lib.rope_f32(q, HEADS, HEAD_DIM, self.n - 1, THETA)
-        return self.lib.attention_decode_f32(q, self.ks[i], self.vs[i], self.n - 1, HEADS, KV_HEADS, HEAD_DIM)
+        self.lib.rope_f32(q, self.heads, HEAD_DIM, self.n - 1, THETA)
+        return self.lib.attention_decode_f32(q, self.ks[i], self.vs[i], self.n - 1, self.heads, self.kv_heads,
+                                             HEAD_DIM)
 
     def step(self) -> int:
         """One decode step: every layer once.  Returns the number of layer calls."""
@@ -162,7 +170,7 @@ class CpuDecode:
             if time.perf_counter() - t0 >= budget_s:
                 break
         dt = time.perf_counter() - t0
-        return step_bytes(self.n, layers=1) * calls / dt / 1e9, calls, dt
+        return step_bytes(self.n, 1, self.heads, self.kv_heads, appended=False) * calls / dt / 1e9, calls, dt
 
     def close(self):
         self.pool.shutdown()
@@ -185,7 +193,7 @@ def run_reference(args) -> None:
         calls += cpu.step()
     dt = time.perf_counter() - t0
     cpu.close()
-    value = step_bytes(CTX0 + 1, layers=1) * calls / dt / 1e9
+    value = step_bytes(CTX0 + 1, 1, appended=False) * calls / dt / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
@@ -477,6 +485,20 @@ def _time_steps(stream, fn, steps, world, dist):
     return ms
 
 
+def cpu_sample_7b(n: int, budget_s: float):
+    """Bounded sample of the reference CPU attention on 7B-shaped layer calls
+    (H28/Hkv4/hd128, n cached tokens, N(0,1) f16 cache) on all host threads."""
+    from oracle import oracle as O
+    kind = "reference" if O.ref_available() else "port"
+    threads = O.host_cores()
+    cd = CpuDecode(kind, threads, n_layers=min(L7, threads), n=n, heads=H7, kv_heads=KV7, scale=1.0,
+                   shared_kv=n > 16384)
+    gbs, calls, dt = cd.sample(budget_s)
+    cd.close()
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"{calls} layer calls (N={n}, H28/Hkv4) in {dt:.1f} s on {threads} threads"}
+
+
 def run_ragged7b(eng, stream, hbm_peak, peak_src, args, world, rank):
     """Qwen2.5-7B-shaped batched decode -- 28 layers,
     H28/Hkv4/hd128, 64 independent sequences of seeded uniform-random length in
@@ -548,7 +570,10 @@ def run_ragged7b(eng, stream, hbm_peak, peak_src, args, world, rank):
     bytes_all = float(t.item())
     gbs = bytes_all / (ms / 1e3) / 1e9
     cache.close()
-    return {"metric": "batched decode tokens/s (BASELINE config 4)", "value": round(64 * steps / (ms / 1e3), 1),
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample_7b(int(np.median(lens)), args.cpu_seconds / 2)
+    return {"metric": "batched decode tokens/s (BASELINE config 4)", "cpu_baseline": cpu, "value": round(64 * steps / (ms / 1e3), 1),
             "unit": "tokens/s", "scaling": "strong", "steps": steps, "ms_per_step": round(ms / steps, 4),
             "workload": "ragged7b: 64 sequences, lengths U[256, 8192] (seed 7), 28 layers, H28/Hkv4/hd128, "
                         "f16 KV N(0,1), one token appended per sequence and layer per step",
@@ -607,7 +632,10 @@ def run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank):
     bytes_all = sum(step_bytes(n_ctx + 4 + i + 1, L7, H7, KV7) for i in range(steps))
     gbs = bytes_all / (ms / 1e3) / 1e9
     cache.close()
-    return {"metric": "long-context decode tokens/s (BASELINE config 5)", "value": round(steps / (ms / 1e3), 1),
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample_7b(n_ctx + 1, args.cpu_seconds / 2)
+    return {"metric": "long-context decode tokens/s (BASELINE config 5)", "cpu_baseline": cpu, "value": round(steps / (ms / 1e3), 1),
             "unit": "tokens/s", "scaling": "strong", "steps": steps, "ms_per_step": round(ms / steps, 4),
             "workload": "long7b: one sequence of 32768 cached tokens, 28 layers, H28/Hkv4/hd128, f16 KV N(0,1), "
                         f"KV split over {world} rank(s), NCCL all-gather of (acc, m, l) + LSE merge per step",
