@@ -98,6 +98,8 @@ class KVSplitDecoder:
         self._gather_flat = torch.empty((spec.world * rows, head_dim + 2), dtype=torch.float32, device=device)
         self._gather = self._gather_flat.view(spec.world, rows, head_dim + 2)
         self._out = torch.empty((n_layers, 1, heads, head_dim), dtype=torch.float32, device=device)
+        # the engine's kernels and the collective run on one stream (the engine's)
+        self._stream = torch.cuda.ExternalStream(engine.stream) if engine is not None else None
 
     def _local_partial(self, q, k_new, v_new, q_pos: int):
         from .runtime import TE_ATTN_ADVANCE, TE_ATTN_PARTIAL
@@ -114,7 +116,15 @@ class KVSplitDecoder:
     def step(self, q, k_new, v_new):
         """One decode step: q [n_layers][1][heads][hd] raw fp32 (every rank gets the
         same q), k_new/v_new [n_layers][1][kv_heads][hd] (used by the tail rank).
-        Returns the merged attention output [n_layers][1][heads][hd] on every rank."""
+        Returns the merged attention output [n_layers][1][heads][hd] on every rank
+        (ready in stream order on the engine's stream)."""
+        if self._stream is None:
+            return self._step(q, k_new, v_new)
+        import torch
+        with torch.cuda.stream(self._stream):
+            return self._step(q, k_new, v_new)
+
+    def _step(self, q, k_new, v_new):
         import torch.distributed as dist
         q_pos = self.length  # global position of the new token
         self._local_partial(q, k_new, v_new, q_pos)
