@@ -164,6 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       prefetch_tmap(&p.tmap_k);
       prefetch_tmap(&p.tmap_v);
     }
+    // L2 priorities: K/V tiles are re-read by every item of their (layer, kv
+    // head) -- keep them; query tiles are read once -- stream them.
+    const uint64_t keep = policy_evict_last();
+    const uint64_t stream_once = policy_evict_first();
     uint32_t ic = 0, kc = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x, ++ic) {
@@ -180,8 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             for (int h = 0; h < 2; ++h)
 #pragma unroll
               for (int c = 0; c < 2; ++c)
-                tma_load_4d(smem + (t ? OFF_QB : OFF_QA) + c * kHalf + h * kBox, &p.tmap_q, &bar[Q_FULL], c * 64,
-                            I.head_a + t, I.qt * BM + h * 64, I.layer_local);
+                tma_load_4d_hint(smem + (t ? OFF_QB : OFF_QA) + c * kHalf + h * kBox, &p.tmap_q, &bar[Q_FULL],
+                                 c * 64, I.head_a + t, I.qt * BM + h * 64, I.layer_local, stream_once);
           }
         }
       }
@@ -218,8 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
                               (tok % p.page_tokens);
 #pragma unroll
               for (int c = 0; c < 2; ++c) {
-                tma_load_2d(ks + c * kHalf + h * kBox, &p.tmap_k, &bar[K_FULL0 + s], c * 64, row);
-                tma_load_2d(vs + c * kHalf + h * kBox, &p.tmap_v, &bar[V_FULL0 + s], c * 64, row);
+                tma_load_2d_hint(ks + c * kHalf + h * kBox, &p.tmap_k, &bar[K_FULL0 + s], c * 64, row, keep);
+                tma_load_2d_hint(vs + c * kHalf + h * kBox, &p.tmap_v, &bar[V_FULL0 + s], c * 64, row, keep);
               }
             }
           }
@@ -412,6 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       tc_fence_after();
       const float inv = 1.f / l;
       const uint32_t stg = smem_u32(smem + OFF_OST + (warp - 4) * 4096);
+      const uint64_t out_policy = policy_evict_first();  // written once, never read here
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         float o[32];
@@ -431,7 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           fence_proxy_async_shared();
           __syncwarp();
           if (lane == 0) {
-            tma_store_4d(&p.tmap_o, buf, c * 32 + h * 16, I.head_a + t, I.qt * BM + quad * 32, I.layer_local);
+            tma_store_4d_hint(&p.tmap_o, buf, c * 32 + h * 16, I.head_a + t, I.qt * BM + quad * 32, I.layer_local,
+                              out_policy);
             bulk_commit();
           }
         }

@@ -100,6 +100,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
 }
 
 // Same with an L2 eviction-priority hint (createpolicy result).
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const void* tmap, uint64_t* bar, int32_t x, int32_t y,
+                                                 int32_t z, int32_t w, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d_hint(void* dst, const void* tmap, uint64_t* bar, int32_t x, int32_t y,
                                                  uint64_t policy) {
   asm volatile(
@@ -117,6 +126,12 @@ __device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src_smem
                ::"l"(tmap), "r"(src_smem), "r"(x), "r"(y), "r"(z), "r"(w)
                : "memory");
 }
+__device__ __forceinline__ void tma_store_4d_hint(const void* tmap, uint32_t src_smem, int32_t x, int32_t y, int32_t z,
+                                                  int32_t w, uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3, %4, %5}], [%1], %6;"
+               ::"l"(tmap), "r"(src_smem), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // This thread's committed bulk stores have finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -130,6 +145,12 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {
