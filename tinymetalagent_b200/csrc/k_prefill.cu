@@ -54,7 +54,7 @@ static_assert(128 * (kRegsLow + 2 * kRegsHigh) <= 65536, "register split exceeds
 constexpr int OFF_QA = 0;
 constexpr int OFF_QB = kTile;
 constexpr int OFF_KV = 2 * kTile;           // stage s: K at OFF_KV + s*2*kTile, V at + kTile
-constexpr int OFF_OST = OFF_KV + 4 * kTile; // output staging: 2 x 2 KiB (32 rows x 64 B) per softmax warp
+constexpr int OFF_OST = OFF_KV + 4 * kTile; // output staging: 4 KiB (32 rows x 128 B) per softmax warp
 constexpr int OFF_BAR = OFF_OST + 8 * 4096;  // 229376
 constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
@@ -406,39 +406,38 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         if (lane == 0) mbar_arrive(&bar[P_FULL_A + t]);
       }
       if (!ok) break;
-      // epilogue: O / l -> out[layer][token][head][:].  Each warp writes its 32
-      // rows in eight 16-column blocks: registers -> one of two 2 KiB 64B-
-      // swizzled staging buffers (alternating, so a block's store overlaps
-      // the next block's staging) -> one TMA store of 32 row segments (rows
-      // past n_tokens are clipped by the tensor map).
+      // epilogue: O / l -> out[layer][token][head][:].  Each warp moves its 32
+      // rows in four 32-column blocks: TMEM -> registers (one row per lane)
+      // -> a 128B-swizzled 4 KiB staging block -> read back four rows per
+      // instruction -> coalesced 128-byte row segments to global memory.
       if (!mbar_wait_warp(&bar[O_FULL_A + t], oc & 1)) { ok = false; break; }
       ++oc;
       tc_fence_after();
       const float inv = 1.f / l;
       const uint32_t stg = smem_u32(smem + OFF_OST + (warp - 4) * 4096);
-      const uint64_t out_policy = policy_evict_first();  // written once, never read here
+      const int tok0 = I.qt * BM + quad * 32;
+      float* out_base = p.out + (((size_t)I.layer_local * p.n_tokens + tok0) * p.heads + I.head_a + t) * HD;
+      const size_t row_stride = (size_t)p.heads * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         float o[32];
         tmem_ld32(o_addr + c * 32, o);
         tmem_wait_ld();
+        __syncwarp();  // the previous block's read-back is done
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t buf = stg + h * 2048;
-          if (lane == 0) bulk_wait_read1();  // the store issued from this buffer two blocks ago has read it
-          __syncwarp();
+        for (int k = 0; k < 8; ++k) {
+          sts128(stg + lane * 128 + ((k ^ (lane & 7)) << 4), __float_as_uint(o[4 * k] * inv),
+                 __float_as_uint(o[4 * k + 1] * inv), __float_as_uint(o[4 * k + 2] * inv),
+                 __float_as_uint(o[4 * k + 3] * inv));
+        }
+        __syncwarp();
+        const int k = lane & 7;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float* v = o + 16 * h + 4 * k;
-            sts128(buf + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4), __float_as_uint(v[0] * inv),
-                   __float_as_uint(v[1] * inv), __float_as_uint(v[2] * inv), __float_as_uint(v[3] * inv));
-          }
-          fence_proxy_async_shared();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_4d_hint(&p.tmap_o, buf, c * 32 + h * 16, I.head_a + t, I.qt * BM + quad * 32, I.layer_local,
-                              out_policy);
-            bulk_commit();
+        for (int i = 0; i < 8; ++i) {
+          const int r = 4 * i + (lane >> 3);
+          const uint4 v = lds128(stg + r * 128 + ((k ^ (r & 7)) << 4));
+          if (tok0 + r < p.n_tokens) {
+            *reinterpret_cast<uint4*>(out_base + (size_t)r * row_stride + c * 32 + 4 * k) = v;
           }
         }
       }
@@ -447,7 +446,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       if (lane == 0) mbar_arrive(&bar[O_EMPTY_A + t]);
     }
     if (!ok) { set_error(p.error, 17); *abort_flag = 1; }
-    if (lane == 0) bulk_wait0();  // this warp's output stores are complete before the CTA exits
   }
 
   tc_fence_before();

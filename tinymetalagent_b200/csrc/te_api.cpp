@@ -156,20 +156,6 @@ bool make_tmap_q_f16(CUtensorMap* m, const void* base, uint64_t hd, uint64_t hea
   return r == CUDA_SUCCESS;
 }
 
-// Prefill output [layers][tokens][heads][hd] f32 as a 4-D tensor map; one TMA
-// store writes 32 tokens x 16 floats of one head (64B swizzle).
-bool make_tmap_out_f32(CUtensorMap* m, void* base, uint64_t hd, uint64_t heads, uint64_t tokens, uint64_t layers) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[4] = {hd, heads, tokens, layers};
-  cuuint64_t strides[3] = {hd * 4, heads * hd * 4, tokens * heads * hd * 4};
-  cuuint32_t box[4] = {16, 1, 32, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
 size_t pool_row(const te_kv_cache* c, size_t layer, int32_t page, size_t kvh, size_t tok_in_page) {
   return ((layer * c->d.total_pages + (size_t)page) * c->d.kv_heads + kvh) * c->d.page_tokens + tok_in_page;
 }
@@ -907,9 +893,6 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   }
   p.tmap_k = c->tmap_k;
   p.tmap_v = c->tmap_v;
-  if (!make_tmap_out_f32(&p.tmap_o, dout, hd, heads, n_tokens, n_layers)) {
-    return fail(e, TE_STATUS_RUNTIME_ERROR, "output tensor map");
-  }
   p.page_table_row = c->d_page_table + seq * c->pages_per_seq;
   p.out = dout;
   p.error = e->d_error;

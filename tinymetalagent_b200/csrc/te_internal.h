@@ -184,7 +184,6 @@ struct PrefillParams {
                         // (rows past n_tokens read as zeros)
   CUtensorMap tmap_k;   // K pool view (as for decode)
   CUtensorMap tmap_v;
-  CUtensorMap tmap_o;   // out as [n_layers][n_tokens][heads][hd] f32, box 16 x 1 x 32 x 1, 64B swizzle
   const int32_t* page_table_row;  // page table row of the sequence
   float* out;           // [n_layers][n_tokens][heads][hd]
   int* error;

@@ -118,28 +118,6 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const void* tmap, ui
       : "memory");
 }
 
-// 4-D TMA tile store shared -> global (bulk-group completion); rows outside
-// the tensor are not written.
-__device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src_smem, int32_t x, int32_t y, int32_t z,
-                                             int32_t w) {
-  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
-               ::"l"(tmap), "r"(src_smem), "r"(x), "r"(y), "r"(z), "r"(w)
-               : "memory");
-}
-__device__ __forceinline__ void tma_store_4d_hint(const void* tmap, uint32_t src_smem, int32_t x, int32_t y, int32_t z,
-                                                  int32_t w, uint64_t policy) {
-  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3, %4, %5}], [%1], %6;"
-               ::"l"(tmap), "r"(src_smem), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// This thread's committed bulk stores have finished reading shared memory.
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-// ... all but the most recent one.
-__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-// ... and have completed their writes.
-__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
 // 1-D bulk copy global -> shared (no multicast); addresses 16-byte aligned, size a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
