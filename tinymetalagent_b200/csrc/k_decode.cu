@@ -66,7 +66,7 @@ struct DecodeCfg {
   static constexpr int kOffNew = kOffML + 2 * kMLFloats * 4;
   static constexpr int kOffRes = kOffNew + 2 * kNewBytes;
   static constexpr int kOffBar = kOffRes + 2 * kResBytes;
-  static constexpr int kNumBars = 2 * kRing + 14;  // full, empty, then [2] each: qfull qempty fready fempty mready mfree nready
+  static constexpr int kNumBars = 2 * kRing + 15;  // full, empty, [2] each: qfull qempty fready fempty mready mfree nready; cbar
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
 };
@@ -216,14 +216,27 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
   uint64_t* mready = fempty + 2; // [2] consumers -> helper
   uint64_t* mfree = mready + 2;  // [2] helper -> consumers, appender
   uint64_t* nready = mfree + 2;  // [2] appender -> helper
+  uint64_t* cbar = nready + 2;   // cluster mode, rank 0: one arrival per CTA of the cluster (records placed)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int G = p.group;
   const int H = p.group * p.kv_heads;
-  const long long s_beg = stage_start(blockIdx.x, p.total_stages, p.grid);
-  const long long s_end = stage_start(blockIdx.x + 1, p.total_stages, p.grid);
+  // This CTA's stage range: a stream-K slice of all groups' stages or, in
+  // cluster mode, part (b % k) of group (b / k).
+  long long s_beg, s_end;
+  if (p.cluster_k > 1) {
+    const int g = blockIdx.x / p.cluster_k, part = blockIdx.x % p.cluster_k;
+    const int blk = g / p.n_seqs, si = g - blk * p.n_seqs;
+    const long long gs0 = (long long)blk * p.block_stages + p.seqs[si].stage_begin;
+    const int n = p.seqs[si].n_stages;
+    s_beg = gs0 + (long long)part * n / p.cluster_k;
+    s_end = gs0 + (long long)(part + 1) * n / p.cluster_k;
+  } else {
+    s_beg = stage_start(blockIdx.x, p.total_stages, p.grid);
+    s_end = stage_start(blockIdx.x + 1, p.total_stages, p.grid);
+  }
 
   if (tid == 0) {
     for (int i = 0; i < R; ++i) {
@@ -239,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
       mbar_init(&mfree[b], 1);
       mbar_init(&nready[b], 1);
     }
+    mbar_init(cbar, p.cluster_k > 1 ? p.cluster_k : 1);
     fence_mbarrier_init();
   }
   if (tid == 32 * kConsumerWarps) {
@@ -246,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     prefetch_tmap(&p.tmap_v);
   }
   __syncthreads();
+  if (p.cluster_k > 1) cluster_sync_all();  // every CTA's barriers exist before any remote arrival
   // Launched as a programmatic dependent: everything above overlaps the
   // previous kernel's tail; all global reads and writes come after this wait.
   // The next kernel may be scheduled as soon as every CTA has started.
@@ -894,6 +909,51 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
       }
     }
     const size_t qrow0 = (size_t)(w.layer_local * p.seq_total + p.seq_base + w.si) * H + w.kvh * G;
+    constexpr int REC = kScratchRec<HD>;
+    if (p.cluster_k > 1) {
+      // Cluster mode: every part writes its record {acc[hd], m, l} into slot
+      // (its rank) of rank 0's unused second merge buffer (one segment per
+      // CTA) and arrives on rank 0's cbar (release, cluster scope); rank 0
+      // folds the slots in rank order.
+      const uint32_t rank = cluster_ctarank();
+      float* slots = reinterpret_cast<float*>(smem + C::kOffMerge + (mb ^ 1) * C::kMergeBytes);
+      static_assert(C::kMergeBytes >= 4 * GP * REC * 4, "four cluster slots per merge buffer");
+      const uint32_t slot0 = mapa_shared(smem_u32(slots + (size_t)rank * GP * REC), 0);
+      if (row < G) {
+#pragma unroll
+        for (int f = 0; f < kF; ++f) st_cluster_v4(slot0 + (uint32_t)(row * REC + 4 * (cl + f * kTPR)) * 4u, O[f]);
+        if (cl == 0) st_cluster_v2(slot0 + (uint32_t)(row * REC + HD) * 4u, make_float2(M, L));
+      }
+      consumer_bar_sync();
+      if (t == 0) mbar_arrive_cluster(mapa_shared(smem_u32(cbar), 0));
+      if (rank != 0) continue;
+      if (!mbar_wait_cluster(cbar, 0)) {
+        if (t == 0) set_error(p.error, 13);
+        continue;
+      }
+      float M2 = -INFINITY, L2 = 0.f;
+      float4 O2[kF];
+#pragma unroll
+      for (int f = 0; f < kF; ++f) O2[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < p.cluster_k; ++j) {
+        const float* r = slots + (size_t)j * GP * REC + (size_t)row * REC;
+        const float2 ml = *reinterpret_cast<const float2*>(r + HD);
+#pragma unroll
+        for (int f = 0; f < kF; ++f) {
+          float Mf = M2, Lf = L2;
+          fold_part(Mf, Lf, O2[f], ml.x, ml.y, *reinterpret_cast<const float4*>(r + 4 * (cl + f * kTPR)));
+          if (f == kF - 1) {
+            M2 = Mf;
+            L2 = Lf;
+          }
+        }
+      }
+      if (row < G) {
+#pragma unroll
+        for (int f = 0; f < kF; ++f) store_result<HD>(p, qrow0 + row, 4 * (cl + f * kTPR), O2[f], M2, L2);
+      }
+      continue;
+    }
     const int b_first = cta_of(p, w.gs0);
     const int parts = cta_of(p, w.gs1 - 1) - b_first + 1;
     if (parts == 1) {
@@ -907,7 +967,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     // folds all records in part order (the result does not depend on which
     // CTA came last).  Release: the 128 threads' record stores (ordered by
     // the barrier) before the ticket; acquire: the ticket before the loads.
-    constexpr int REC = kScratchRec<HD>;
     const int gidx_first = group_at(p, s_beg).gidx;
     float* part = p.partials + ((size_t)blockIdx.x * p.max_segs + (w.gidx - gidx_first)) * G * REC;
     if (row < G) {
@@ -1098,16 +1157,21 @@ cudaError_t launch_decode_impl(const DecodeParams& p, cudaStream_t s) {
   // Programmatic dependent launch: the CTAs may become resident (on SMs the
   // previous kernel has left) and set up their barriers before it completes;
   // they wait for it (griddepcontrol.wait) before touching global memory.
+  // In cluster mode the k CTAs of a group form one thread-block cluster.
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = p.cluster_k > 1 ? (unsigned)p.cluster_k : 1u;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.gridDim = dim3((unsigned)p.grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, decode_f16_kernel<HD, GP>, p);
 }
 

@@ -740,6 +740,7 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
       max_grid = std::min<long long>(max_grid, std::max<long long>(1, (tokens + e->decode_chunk - 1) / e->decode_chunk));
     }
     plan_stream_k(p, max_grid);
+    if (!e->decode_chunk) plan_cluster(p, e->sm_count);
     const size_t part_bytes = (size_t)p.grid * p.max_segs * G * decode_scratch_rec((int)hd) * sizeof(float);
     cudaError_t err = grow(e, reinterpret_cast<void**>(&e->partials), &e->partials_bytes, part_bytes, false);
     if (err == cudaSuccess) {

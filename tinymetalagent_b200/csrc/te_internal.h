@@ -70,6 +70,8 @@ struct DecodeParams {
   int32_t group;              // heads per kv head (<= 16)
   int32_t block_stages;       // stages of one (layer, kv head) block: sum of n_stages
   int32_t grid;               // CTAs sharing the stages (stream-K split)
+  int32_t cluster_k;          // > 1: clusters of cluster_k CTAs, CTA b takes part b % k of group b / k
+                              // and the parts combine in distributed shared memory; else stream-K
   int32_t max_segs;           // partial-record slots per CTA
   long long total_stages;     // n_layers * kv_heads * block_stages
   int32_t num_pages;          // pages per layer
@@ -124,6 +126,25 @@ inline void plan_stream_k(DecodeParams& p, long long max_grid) {
     if (n > segs) segs = n;
   }
   p.max_segs = (int32_t)segs;
+}
+
+// Cluster split, when every (layer, kv head, sequence) group can take k >= 2
+// whole SMs (k = 2 or 4, at most one CTA per SM, each part >= 1 stage): the
+// split-K combine then stays in distributed shared memory.  Otherwise keeps
+// the stream-K plan.
+inline void plan_cluster(DecodeParams& p, int sm_count) {
+  p.cluster_k = 0;
+  const long long groups = (long long)p.n_layers * p.kv_heads * p.n_seqs;
+  if (groups <= 0) return;
+  long long k = sm_count / groups;
+  if (k < 2) return;
+  k = k >= 4 ? 4 : 2;
+  for (int i = 0; i < p.n_seqs; ++i) {
+    if (p.seqs[i].n_stages < k) return;
+  }
+  p.cluster_k = (int32_t)k;
+  p.grid = (int32_t)(groups * k);
+  p.max_segs = 1;
 }
 
 // Launchers (kernels live in the .cu files).  All return cudaError_t of the launch.
