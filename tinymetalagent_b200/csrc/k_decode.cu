@@ -262,13 +262,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
   __syncthreads();
   if (p.cluster_k > 1) cluster_sync_all();  // every CTA's barriers exist before any remote arrival
   // Launched as a programmatic dependent: everything above overlaps the
-  // previous kernel's tail; all global reads and writes come after this wait.
-  // The next kernel may be scheduled as soon as every CTA has started.
-  griddep_wait();
+  // previous kernel's tail.  Every warp waits for that kernel (griddep_wait)
+  // before its first global read or write; the producer first asks L2 for
+  // its first stages (prefetch hints touch no memory state the previous
+  // kernel could race with: L2 stays coherent with its writes).  The next
+  // kernel may be scheduled as soon as every CTA has started.
   griddep_launch_dependents();
+  if (warp != kConsumerWarps) griddep_wait();
 
   if (warp == kConsumerWarps) {
     // ---- producer warp: q prefetch + K/V TMA ring -----------------------------
+    if (lane == 0 && s_end > s_beg) {
+      const Seg w0 = seg_ending(p, s_end, s_beg);
+      const SeqEntry se0 = p.seqs[w0.si];
+      if (se0.page_base >= 0) {  // page ids without reading the table
+        const int layer0 = p.layer_begin + w0.layer_local;
+        for (int s = 0; s < w0.n_st && s < R; ++s) {
+          const int tok = w0.t0 + s * kStageTokens;
+          const int row = ((layer0 * p.num_pages + se0.page_base + tok / p.page_tokens) * p.kv_heads + w0.kvh) *
+                              p.page_tokens + (tok % p.page_tokens);
+#pragma unroll
+          for (int bx = 0; bx < C::kBoxes; ++bx) {
+            prefetch_tile_2d_l2(&p.tmap_k, bx * 64, row);
+            prefetch_tile_2d_l2(&p.tmap_v, bx * 64, row);
+          }
+        }
+      }
+    }
+    griddep_wait();
     const uint64_t policy = policy_evict_first();
     uint32_t sidx = 0, k = 0;
     bool ok = true;

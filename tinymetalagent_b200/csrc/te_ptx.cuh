@@ -137,6 +137,12 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+// L2 prefetch of one 2-D tensor-map tile (a hint: no shared memory, no completion).
+__device__ __forceinline__ void prefetch_tile_2d_l2(const void* tmap, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
