@@ -1198,8 +1198,7 @@ cudaError_t launch_decode_impl(const DecodeParams& p, cudaStream_t s) {
 
 }  // namespace
 
-cudaError_t launch_decode_f16(const DecodeParams& p, int head_dim, int stages, cudaStream_t s) {
-  (void)stages;
+cudaError_t launch_decode_f16(const DecodeParams& p, int head_dim, cudaStream_t s) {
   if (head_dim == 128) return p.group <= 8 ? launch_decode_impl<128, 8>(p, s) : launch_decode_impl<128, 16>(p, s);
   if (head_dim == 64) return p.group <= 8 ? launch_decode_impl<64, 8>(p, s) : launch_decode_impl<64, 16>(p, s);
   return cudaErrorInvalidValue;
@@ -1332,5 +1331,5 @@ extern "C" __attribute__((visibility("default"))) te_status te_attention_decode_
     plan_stream_k(p, max_grid);
   }
   if ((size_t)p.grid * p.max_segs * rec_bytes > kNoAllocPartialBytes) return TE_STATUS_UNSUPPORTED;
-  return launch_decode_f16(p, (int)head_dim, 0, s) == cudaSuccess ? TE_STATUS_OK : TE_STATUS_RUNTIME_ERROR;
+  return launch_decode_f16(p, (int)head_dim, s) == cudaSuccess ? TE_STATUS_OK : TE_STATUS_RUNTIME_ERROR;
 }

@@ -751,7 +751,7 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
     if (err != cudaSuccess) return cuda_fail(e, err, "decode scratch allocation");
     p.partials = e->partials;
     p.counters = e->counters;
-    err = launch_decode_f16(p, (int)hd, 0, e->stream);
+    err = launch_decode_f16(p, (int)hd, e->stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "decode kernel launch");
     e->launches++;
   }

@@ -148,7 +148,7 @@ inline void plan_cluster(DecodeParams& p, int sm_count) {
 }
 
 // Launchers (kernels live in the .cu files).  All return cudaError_t of the launch.
-cudaError_t launch_decode_f16(const DecodeParams& p, int head_dim, int stages, cudaStream_t s);
+cudaError_t launch_decode_f16(const DecodeParams& p, int head_dim, cudaStream_t s);
 cudaError_t launch_decode_f32_generic(const float* q, const float* k, const float* v, float* scores, float* out,
                                       size_t n_tokens, int heads, int kv_heads, int head_dim, cudaStream_t s);
 cudaError_t launch_rope_rows(float* values, const float* cos_row, const float* sin_row, int heads, int head_dim,
