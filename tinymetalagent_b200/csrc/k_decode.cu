@@ -1,24 +1,28 @@
 // Split-K GQA flash decode over the paged f16 KV cache (sm_100a).
 //
-// One CTA = one (layer, sequence, kv head, chunk of chunk_tokens tokens).  It
-// serves the whole GQA group of that kv head (up to 16 query heads), so every
-// K/V byte is read from HBM exactly once per step.  Reference semantics:
-// te_attention_decode_f32 (c/src/ops.c:323-395) with f16 K/V widened exactly,
-// as in te_attention_flash_h_f32_kernel
+// One launch covers every (layer, kv head, sequence) group of a decode call.
+// A CTA serves the whole GQA group of its kv head (up to 16 query heads), so
+// every cached K/V byte is read from HBM exactly once per step.  Reference
+// semantics: te_attention_decode_f32 (c/src/ops.c:323-395) with f16 K/V
+// widened exactly, as in te_attention_flash_h_f32_kernel
 // (c/src/metal/metal_kernels.metal.inc:3374-3495); the group-shared KV read
 // follows te_attention_flash_gqa_f32_kernel (:3209-3372).
 //
-// Pipeline: warp 4 lane 0 streams 64-token stages (K and V, 128B-swizzled
+// Work split: stream-K (equal stage ranges per persistent CTA over all groups'
+// 64-token stages) or, when every group can take k = 2 or 4 SMs, one
+// thread-block cluster of k CTAs per group.  Parts of a split group combine by
+// log-sum-exp: through distributed shared memory inside a cluster, otherwise
+// through per-part records in scratch, folded by the last part to finish
+// (atomic ticket, no waiting) in part order.
+//
+// Pipeline: the producer warp streams 64-token stages (K and V, 128B-swizzled
 // 64x64 TMA boxes) into a ring of `R` shared-memory slots; warps 0-3 each take
 // 16 tokens of every stage.  Scores S = Q K^T and O += P V run on
 // mma.sync.m16n8k16 (f16 in, f32 accumulate) with the query heads as the M
 // rows.  The head dimension is permuted per thread so that every operand
 // fragment is one 16-byte shared-memory load (conflict-free under the swizzle)
-// and the query fragments stay in registers for the whole chunk; the
+// and the query fragments stay in registers for a whole segment; the
 // permutation is applied identically to q and k, so q.k is unchanged.
-//
-// Split-K partials (acc, m, l) go to scratch; the last CTA of a
-// (layer, seq, kv head) to finish (atomic ticket, no waiting) merges them.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
