@@ -741,18 +741,31 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
     }
     plan_stream_k(p, max_grid);
     if (!e->decode_chunk) plan_cluster(p, e->sm_count);
-    const size_t part_bytes = (size_t)p.grid * p.max_segs * G * decode_scratch_rec((int)hd) * sizeof(float);
-    cudaError_t err = grow(e, reinterpret_cast<void**>(&e->partials), &e->partials_bytes, part_bytes, false);
-    if (err == cudaSuccess) {
-      size_t bytes = e->counters_count * sizeof(uint32_t);
-      err = grow(e, reinterpret_cast<void**>(&e->counters), &bytes, n_layers * hkv * nb * sizeof(uint32_t), true);
-      e->counters_count = bytes / sizeof(uint32_t);
+    auto launch = [&]() -> te_status {
+      const size_t part_bytes = (size_t)p.grid * p.max_segs * G * decode_scratch_rec((int)hd) * sizeof(float);
+      cudaError_t err = grow(e, reinterpret_cast<void**>(&e->partials), &e->partials_bytes, part_bytes, false);
+      if (err == cudaSuccess) {
+        size_t bytes = e->counters_count * sizeof(uint32_t);
+        err = grow(e, reinterpret_cast<void**>(&e->counters), &bytes, n_layers * hkv * nb * sizeof(uint32_t), true);
+        e->counters_count = bytes / sizeof(uint32_t);
+      }
+      if (err != cudaSuccess) return cuda_fail(e, err, "decode scratch allocation");
+      p.partials = e->partials;
+      p.counters = e->counters;
+      err = launch_decode_f16(p, (int)hd, e->stream);
+      if (err != cudaSuccess) return cuda_fail(e, err, "decode kernel launch");
+      return TE_STATUS_OK;
+    };
+    te_status st = launch();
+    if (st != TE_STATUS_OK && p.cluster_k > 1) {
+      // The device could not schedule the clusters (a launch-time, non-sticky
+      // error): the stream-K split instead.
+      (void)cudaGetLastError();
+      plan_stream_k(p, max_grid);
+      p.cluster_k = 0;
+      st = launch();
     }
-    if (err != cudaSuccess) return cuda_fail(e, err, "decode scratch allocation");
-    p.partials = e->partials;
-    p.counters = e->counters;
-    err = launch_decode_f16(p, (int)hd, e->stream);
-    if (err != cudaSuccess) return cuda_fail(e, err, "decode kernel launch");
+    if (st != TE_STATUS_OK) return st;
     e->launches++;
   }
 
