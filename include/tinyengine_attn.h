@@ -93,6 +93,13 @@ TE_API te_status te_attn_engine_synchronize(te_attn_engine *engine);
 TE_API const char *te_attn_engine_last_error(const te_attn_engine *engine);
 /* Number of this library's kernels launched by the engine so far. */
 TE_API uint64_t te_attn_engine_launch_count(const te_attn_engine *engine);
+/* Measurement: while enabled, te_attention_prefill records a pair of CUDA
+ * events around its tensor-core attention kernel on the engine's stream;
+ * te_attn_engine_last_kernel_ms waits for the last recorded pair and returns
+ * that kernel's duration in milliseconds (TE_STATUS_INVALID_ARGUMENT when
+ * nothing was recorded). */
+TE_API te_status te_attn_engine_time_kernels(te_attn_engine *engine, int enable);
+TE_API te_status te_attn_engine_last_kernel_ms(te_attn_engine *engine, float *ms);
 
 /* KV cache ---------------------------------------------------------------- */
 

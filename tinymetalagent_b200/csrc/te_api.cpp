@@ -40,6 +40,9 @@ struct te_attn_engine {
   uint32_t* tile_counter = nullptr;
   uint64_t launches = 0;
   std::string last_error;
+  bool time_kernels = false;  // te_attn_engine_time_kernels
+  bool kernel_timed = false;
+  cudaEvent_t ev_k0 = nullptr, ev_k1 = nullptr;
 };
 
 struct te_kv_cache {
@@ -369,6 +372,8 @@ TE_API void te_attn_engine_free(te_attn_engine* e) {
     cudaFree(e->d_error);
     cudaFree(e->io);
     cudaFree(e->qh);
+    if (e->ev_k0) cudaEventDestroy(e->ev_k0);
+    if (e->ev_k1) cudaEventDestroy(e->ev_k1);
     if (e->own_stream && e->stream) cudaStreamDestroy(e->stream);
   }
   delete e;
@@ -412,6 +417,27 @@ TE_API const char* te_attn_engine_last_error(const te_attn_engine* e) {
 }
 
 TE_API uint64_t te_attn_engine_launch_count(const te_attn_engine* e) { return e ? e->launches : 0; }
+
+TE_API te_status te_attn_engine_time_kernels(te_attn_engine* e, int enable) {
+  if (!e) return TE_STATUS_INVALID_ARGUMENT;
+  if (enable && !e->ev_k0) {
+    DeviceGuard dg(e->device);
+    if (cudaEventCreate(&e->ev_k0) != cudaSuccess || cudaEventCreate(&e->ev_k1) != cudaSuccess) {
+      return fail(e, TE_STATUS_RUNTIME_ERROR, "event creation");
+    }
+  }
+  e->time_kernels = enable != 0;
+  e->kernel_timed = false;
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_attn_engine_last_kernel_ms(te_attn_engine* e, float* ms) {
+  if (!e || !ms || !e->kernel_timed) return TE_STATUS_INVALID_ARGUMENT;
+  DeviceGuard dg(e->device);
+  cudaError_t err = cudaEventSynchronize(e->ev_k1);
+  if (err == cudaSuccess) err = cudaEventElapsedTime(ms, e->ev_k0, e->ev_k1);
+  return err == cudaSuccess ? TE_STATUS_OK : cuda_fail(e, err, "kernel timing");
+}
 
 // ===========================================================================
 // KV cache
@@ -922,8 +948,13 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   p.n_pages_mapped = (int32_t)((total + c->d.page_tokens - 1) / c->d.page_tokens);
   p.n_items = (int32_t)items;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hd));
+  if (e->time_kernels) cudaEventRecord(e->ev_k0, e->stream);
   err = launch_prefill_tc(p, e->sm_count, e->stream);
   if (err != cudaSuccess) return cuda_fail(e, err, "prefill kernel launch");
+  if (e->time_kernels) {
+    cudaEventRecord(e->ev_k1, e->stream);
+    e->kernel_timed = true;
+  }
   e->launches++;
 
   if (flags & TE_ATTN_HOST_BUFFERS) {

@@ -97,6 +97,8 @@ SIGNATURES: dict[str, tuple] = {
     "te_attn_engine_synchronize": (_int, [_vp]),
     "te_attn_engine_last_error": (ctypes.c_char_p, [_vp]),
     "te_attn_engine_launch_count": (ctypes.c_uint64, [_vp]),
+    "te_attn_engine_time_kernels": (_int, [_vp, _int]),
+    "te_attn_engine_last_kernel_ms": (_int, [_vp, ctypes.POINTER(ctypes.c_float)]),
     "te_kv_cache_default_desc": (KVCacheDesc, []),
     "te_kv_cache_create": (_int, [_vp, ctypes.POINTER(KVCacheDesc), ctypes.POINTER(_vp)]),
     "te_kv_cache_free": (None, [_vp]),
@@ -229,6 +231,15 @@ class AttnEngine:
     @property
     def launch_count(self) -> int:
         return int(self.lib.te_attn_engine_launch_count(self.handle))
+
+    def time_kernels(self, enable: bool = True) -> None:
+        """Record CUDA events around te_attention_prefill's attention kernel."""
+        self.check(self.lib.te_attn_engine_time_kernels(self.handle, 1 if enable else 0))
+
+    def last_kernel_ms(self) -> float:
+        ms = ctypes.c_float(0.0)
+        self.check(self.lib.te_attn_engine_last_kernel_ms(self.handle, ctypes.byref(ms)))
+        return float(ms.value)
 
     def merge_partials(self, partials, n_parts: int, rows: int, head_dim: int, out, partial_out: bool = False):
         self.check(self.lib.te_attention_merge_partials(
