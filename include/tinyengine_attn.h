@@ -84,6 +84,8 @@ typedef struct te_kv_cache_desc {
 
 TE_API te_attn_options te_attn_default_options(void);
 TE_API te_status te_attn_engine_create(const te_attn_options *options, te_attn_engine **out_engine);
+/* Frees the engine's stream (when it owns it) and scratch.  Free every cache
+ * created from the engine (te_kv_cache_free) before the engine itself. */
 TE_API void te_attn_engine_free(te_attn_engine *engine);
 TE_API te_status te_attn_engine_set_stream(te_attn_engine *engine, void *stream);
 TE_API void *te_attn_engine_stream(const te_attn_engine *engine);

@@ -204,3 +204,40 @@ def test_prefill_host_buffers(port):
         close(out[0, t], e)
     cache.close()
     eng.close()
+
+
+@pytest.mark.parametrize("shape", [(16, 2), (28, 4)])
+def test_prefill_growing_scores(port, shape):
+    """Keys grow with position (16x over 600 tokens), so a row's running max
+    rises by far more than 2^8 between key tiles and the accumulated O is
+    rescaled many times (paired and single-head items).  f16 inputs with RoPE
+    off: the kernel multiplies exactly the oracle's query values, which keeps
+    this check on the online softmax.  (With a rotated fp32 query, its f16
+    rounding alone moves attention weights at these score magnitudes by a few
+    tenths of a percent, beyond the output tolerance.)"""
+    import torch
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16, TE_ATTN_NO_ROPE, AttnEngine
+    h, hkv = shape
+    hd, s = 128, 600
+    rng = np.random.default_rng(77 + h)
+    q16 = rng.standard_normal((s, h, hd)).astype(np.float16)
+    k16 = (rng.standard_normal((s, hkv, hd)) * (1.0 + np.arange(s) / 40.0)[:, None, None]).astype(np.float16)
+    v16 = rng.standard_normal((s, hkv, hd)).astype(np.float16)
+    eng = AttnEngine(0)
+    try:
+        cache = eng.kv_cache(layers=1, max_seqs=1, max_tokens_per_seq=s, kv_heads=hkv, head_dim=hd)
+        out = torch.zeros((1, s, h, hd), dtype=torch.float32, device="cuda")
+        t16 = lambda a: dev(a.view(np.uint16)).view(torch.float16)  # noqa: E731
+        cache.prefill(0, 1, 0, t16(q16[None]), t16(k16[None]), t16(v16[None]), s, h, out,
+                      TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | TE_ATTN_NO_ROPE)
+        eng.synchronize()
+        got = out.cpu().numpy()[0]
+        k = k16.astype(np.float32).ravel()
+        v = v16.astype(np.float32).ravel()
+        for t in (0, 1, 63, 64, 127, 128, 129, 255, 256, 383, 384, 511, 512, 599):
+            exp = port.attention_decode_f32(q16[t].astype(np.float32).ravel(), k, v, t, h, hkv, hd)
+            close(got[t], exp.reshape(h, hd))
+        kg, vg = cache.read_f16(0, 0, 0, s)
+        assert np.array_equal(kg, k16.view(np.uint16)) and np.array_equal(vg, v16.view(np.uint16))
+    finally:
+        eng.close()

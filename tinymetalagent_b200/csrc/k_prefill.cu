@@ -358,8 +358,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         }
         const float tmax_raw = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
         const float m_new = fmaxf(m, tmax_raw * sl);  // scaling by sl > 0 preserves the max
-        // lazy rescale: keep the old reference max unless the row max grew by > 2^8
+        // lazy rescale: keep the old reference max unless the row max grew by > 2^8.
+        // The decision is per row; the TMEM rescale of O below is
+        // warp-collective, so a warp runs it when any of its rows needs it
+        // (alpha = 1 for the others).
         const bool rescale = j > 0 && m_new > m + 8.f;
+        const bool warp_rescale = __any_sync(0xffffffffu, rescale);
         const float alpha = rescale ? ex2(m - m_new) : 1.f;
         if (j == 0 || rescale) m = m_new;
         // p = 2^(s*scale - m) -> f16 pairs over the first half of S's columns
@@ -388,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
         for (int u = 0; u < 4; ++u) f2_unpack(ps2[u], ps[2 * u], ps[2 * u + 1]);
         l = l * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
-        if (rescale) {
+        if (warp_rescale) {
           // O is stable: the commit that signalled this S tracks the previous P V too
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import weakref
 from pathlib import Path
 from typing import Optional, Sequence
 
@@ -203,9 +204,14 @@ class AttnEngine:
         _check(self.lib, self.lib.te_attn_engine_create(ctypes.byref(opts), ctypes.byref(handle)))
         self.handle = handle
         self.device = device
+        self._caches = weakref.WeakSet()
 
     def close(self) -> None:
+        """Frees the engine; caches created from it are freed first (the C
+        library frees a cache through its engine)."""
         if getattr(self, "handle", None):
+            for cache in list(getattr(self, "_caches", ())):
+                cache.close()
             self.lib.te_attn_engine_free(self.handle)
             self.handle = None
 
@@ -265,15 +271,17 @@ class KVCache:
         handle = _vp()
         engine.check(self.lib.te_kv_cache_create(engine.handle, ctypes.byref(d), ctypes.byref(handle)))
         self.handle = handle
+        engine._caches.add(self)
         self.layers, self.max_seqs, self.kv_heads, self.head_dim = layers, max_seqs, kv_heads, head_dim
         self.page_tokens = page_tokens
         self.max_tokens_per_seq = max_tokens_per_seq
         self.rope_theta = rope_theta
 
     def close(self) -> None:
-        if getattr(self, "handle", None):
+        # An engine that is already gone has freed this cache with itself.
+        if getattr(self, "handle", None) and getattr(self.engine, "handle", None):
             self.lib.te_kv_cache_free(self.handle)
-            self.handle = None
+        self.handle = None
 
     def __del__(self):  # pragma: no cover
         try:
