@@ -15,7 +15,9 @@
 // to a persistent grid of one CTA per SM.
 //
 // Warp roles (384 threads):
-//   warp 0      TMA producer: the Q tiles, then K/V tiles (128 keys) into a 2-stage ring
+//   warp 0      TMA producer: the Q tiles, then K and V tiles (128 keys) into
+//               two 2-stage rings (K released after its tile's last Q K^T, V
+//               after its last P V)
 //   warp 1      TMEM owner; lane 0 issues tcgen05.mma in the order
 //                 QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) | ...
 //               (S = Q K^T: M=128 queries, N=128 keys, K=128 dims, A/B from shared
@@ -60,7 +62,7 @@ constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
 
 enum Bar {
-  Q_FULL = 0, Q_EMPTY, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1,
+  Q_FULL = 0, Q_EMPTY, K_FULL0, K_FULL1, V_FULL0, V_FULL1, K_EMPTY0, K_EMPTY1, V_EMPTY0, V_EMPTY1,
   S_FULL_A, S_FULL_B, P_FULL_A, P_FULL_B, O_FULL_A, O_FULL_B, O_EMPTY_A, O_EMPTY_B, DRAIN, kNumBars
 };
 
@@ -131,7 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar[K_FULL0 + s], 1);
       mbar_init(&bar[V_FULL0 + s], 1);
-      mbar_init(&bar[KV_EMPTY0 + s], 1);
+      mbar_init(&bar[K_EMPTY0 + s], 1);
+      mbar_init(&bar[V_EMPTY0 + s], 1);
       mbar_init(&bar[S_FULL_A + s], 1);
       mbar_init(&bar[P_FULL_A + s], 4);
       mbar_init(&bar[O_FULL_A + s], 1);
@@ -206,26 +209,41 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           }
           pages[h] = __shfl_sync(0xffffffffu, pg_reg, idx & 31);
         }
+        // K and V of a stage are released separately: K after the tile's last
+        // Q K^T, V after its last P V.  V(j) needs the stage of V(j-2), whose
+        // last P V completes before the last Q K^T of K(j-1) that K(j+1)
+        // waits for, so loading K(j) then V(j) never holds a K load behind a
+        // V load.
         if (lane == 0) {
-          if (!mbar_wait(&bar[KV_EMPTY0 + s], ((kc >> 1) & 1) ^ 1)) {
+          int rows[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int tok = j * BN + h * 64;
+            rows[h] = ((layer * p.num_pages + pages[h]) * p.kv_heads + I.kvh) * p.page_tokens + (tok % p.page_tokens);
+          }
+          unsigned char* ks = smem + OFF_KV + s * 2 * kTile;
+          unsigned char* vs = ks + kTile;
+          if (!mbar_wait(&bar[K_EMPTY0 + s], ((kc >> 1) & 1) ^ 1)) {
             set_error(p.error, 12);
             ok = false;
           } else {
-            unsigned char* ks = smem + OFF_KV + s * 2 * kTile;
-            unsigned char* vs = ks + kTile;
             mbar_arrive_expect_tx(&bar[K_FULL0 + s], kTile);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int c = 0; c < 2; ++c)
+                tma_load_2d_hint(ks + c * kHalf + h * kBox, &p.tmap_k, &bar[K_FULL0 + s], c * 64, rows[h], keep);
+          }
+          if (ok && !mbar_wait(&bar[V_EMPTY0 + s], ((kc >> 1) & 1) ^ 1)) {
+            set_error(p.error, 12);
+            ok = false;
+          } else if (ok) {
             mbar_arrive_expect_tx(&bar[V_FULL0 + s], kTile);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int tok = j * BN + h * 64;
-              const int row = ((layer * p.num_pages + pages[h]) * p.kv_heads + I.kvh) * p.page_tokens +
-                              (tok % p.page_tokens);
+            for (int h = 0; h < 2; ++h)
 #pragma unroll
-              for (int c = 0; c < 2; ++c) {
-                tma_load_2d_hint(ks + c * kHalf + h * kBox, &p.tmap_k, &bar[K_FULL0 + s], c * 64, row, keep);
-                tma_load_2d_hint(vs + c * kHalf + h * kBox, &p.tmap_v, &bar[V_FULL0 + s], c * 64, row, keep);
-              }
-            }
+              for (int c = 0; c < 2; ++c)
+                tma_load_2d_hint(vs + c * kHalf + h * kBox, &p.tmap_v, &bar[V_FULL0 + s], c * 64, rows[h], keep);
           }
         }
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -280,22 +298,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         const uint32_t kc0 = kc;
         if (!wait(Q_FULL, ic & 1) || !wait(K_FULL0 + (kc0 & 1), (kc0 >> 1) & 1)) { ok = false; break; }
         for (int t = 0; t < nt; ++t) qk(t, kc0);
+        umma_commit(&bar[K_EMPTY0 + (kc0 & 1)]);  // every Q K^T of tile 0 issued: K stage free on completion
         if (I.n_kv == 1) umma_commit(&bar[Q_EMPTY]);
         for (int j = 0; j < I.n_kv && ok; ++j) {
           const uint32_t k_idx = kc0 + j;
           const int s = k_idx & 1;
           for (int t = 0; t < nt; ++t) {
-            if (!wait(P_FULL_A + t, pc[t] & 1) || (j == 0 && !wait(O_EMPTY_A + t, (oc[t] & 1) ^ 1)) ||
-                !wait(V_FULL0 + s, (k_idx >> 1) & 1)) {
+            // Waits that are normally complete come first (V of this tile, K
+            // of the next), so that the unit's P is the last wait before its
+            // MMAs are issued.
+            if ((t == 0 && !wait(V_FULL0 + s, (k_idx >> 1) & 1)) ||
+                (t == 0 && j + 1 < I.n_kv && !wait(K_FULL0 + ((k_idx + 1) & 1), ((k_idx + 1) >> 1) & 1)) ||
+                (j == 0 && !wait(O_EMPTY_A + t, (oc[t] & 1) ^ 1)) || !wait(P_FULL_A + t, pc[t] & 1)) {
               ok = false;
               break;
             }
             ++pc[t];
             pv(t, k_idx, j);
-            if (t == nt - 1) umma_commit(&bar[KV_EMPTY0 + s]);  // every P V of tile j issued: stage free on completion
+            if (t == nt - 1) umma_commit(&bar[V_EMPTY0 + s]);  // every P V of tile j issued: V stage free on completion
             if (j + 1 < I.n_kv) {
-              if (t == 0 && !wait(K_FULL0 + ((k_idx + 1) & 1), ((k_idx + 1) >> 1) & 1)) { ok = false; break; }
               qk(t, k_idx + 1);
+              if (t == nt - 1) umma_commit(&bar[K_EMPTY0 + ((k_idx + 1) & 1)]);  // K stage of tile j+1 free on completion
               if (j + 2 == I.n_kv && t == nt - 1) umma_commit(&bar[Q_EMPTY]);
             } else {
               umma_commit(&bar[O_FULL_A + t]);
