@@ -427,3 +427,31 @@ def test_decode_steps_in_cuda_graph_match_eager():
         eng.close()
     for a, b in zip(outs["eager"], outs["graph"]):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("chunk", [0, 128])
+def test_decode_growing_scores(port, chunk):
+    """Cached keys grow with position (16x over 3000 tokens), so every split's
+    running max rises by far more than 2^8 between stages and the accumulators
+    are rescaled many times before the split-K combine (cluster and stream-K
+    splits).  The queries are f16 values given as fp32 without RoPE, so the
+    kernel multiplies exactly the oracle's query."""
+    import torch
+    from tinymetalagent_b200 import AttnEngine, TE_ATTN_NO_ROPE
+    h, hkv, hd, n = 16, 2, 128, 3000
+    rng = np.random.default_rng(91)
+    k = (rng.standard_normal((n, hkv, hd)) * (1.0 + np.arange(n) / 200.0)[:, None, None]).astype(np.float16)
+    v = rng.standard_normal((n, hkv, hd)).astype(np.float16)
+    q = rng.standard_normal((1, 1, h, hd)).astype(np.float16).astype(np.float32)
+    eng = AttnEngine(0, decode_chunk_tokens=chunk)
+    try:
+        cache = eng.kv_cache(layers=1, max_seqs=1, max_tokens_per_seq=n, kv_heads=hkv, head_dim=hd)
+        cache.write_f16(0, 0, 0, k.view(np.uint16), v.view(np.uint16))
+        out = torch.zeros((1, 1, h, hd), dtype=torch.float32, device="cuda")
+        cache.decode(0, 1, [0], torch_dev(q), out, h, flags=TE_ATTN_NO_ROPE)
+        eng.synchronize()
+        exp = port.attention_decode_f32(q.ravel(), k.astype(np.float32).ravel(), v.astype(np.float32).ravel(),
+                                        n - 1, h, hkv, hd)
+        close(out.cpu().numpy()[0, 0], exp.reshape(h, hd))
+    finally:
+        eng.close()
