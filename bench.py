@@ -215,7 +215,7 @@ def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
 
-    from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_HOST_BUFFERS, AttnEngine
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_HOST_BUFFERS, TE_ATTN_QKV_BIAS, AttnEngine
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -319,6 +319,42 @@ def run_gpu(args) -> None:
     value = bytes_rank * world / (ms_max / 1e3) / 1e9
     kernel_gbs = bytes_rank / (ms / 1e3) / 1e9
 
+    # ---- the same decode with the fused projection-bias prologue -----------
+    # (TE_ATTN_QKV_BIAS: the layer's q/k/v biases added inside the decode
+    # launch before RoPE and the f16 append), graph-captured and timed alike.
+    qkv_bias = None
+    if not args.no_graph:
+        gb = torch.Generator(device="cuda").manual_seed(4321 + rank)
+        cache.set_qkv_bias(0, HEADS, torch.randn((LAYERS, HEADS * HEAD_DIM), generator=gb, device="cuda") * 0.1,
+                           torch.randn((LAYERS, KV_HEADS * HEAD_DIM), generator=gb, device="cuda") * 0.1,
+                           torch.randn((LAYERS, KV_HEADS * HEAD_DIM), generator=gb, device="cuda") * 0.1)
+        cache.truncate(0, CTX0)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(args.steps):
+                step(flags=TE_ATTN_QKV_BIAS)
+        with torch.cuda.stream(stream):
+            graph.replay()  # warm
+        stream.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        with torch.cuda.stream(stream):
+            graph.replay()
+        ev1.record(stream)
+        ev1.synchronize()
+        ms_b = ev0.elapsed_time(ev1)
+        del graph
+        cache.truncate(0, CTX0)
+        if world > 1:
+            t = torch.tensor([ms_b], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_b = float(t.item())
+        value_b = bytes_rank * world / (ms_b / 1e3) / 1e9
+        qkv_bias = {"metric": "config 2 decode with the fused QKV-bias prologue (TE_ATTN_QKV_BIAS)",
+                    "value": round(value_b, 3), "unit": "GB/s", "ms_per_step": round(ms_b / args.steps, 5),
+                    "relative_to_plain": round(value_b / value, 4)}
+
     # ---- e2e through the C ABI with host buffers -------------------------
     hq = torch.empty(q.shape, dtype=torch.float32, pin_memory=True).copy_(q)
     hk = torch.empty(kn.shape, dtype=torch.float32, pin_memory=True).copy_(kn)
@@ -399,6 +435,7 @@ def run_gpu(args) -> None:
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "decode3b_qkv_bias": qkv_bias,
             "ragged7b": ragged,
             "long7b": long,
         }

@@ -55,6 +55,8 @@ extern "C" {
 #define TE_ATTN_NO_ROPE       (1u << 2) /* q (and k) are used as given, without rotation */
 #define TE_ATTN_INPUT_F16     (1u << 3) /* q/k/v inputs are binary16 instead of fp32 */
 #define TE_ATTN_HOST_BUFFERS  (1u << 4) /* q/k/v/out are host pointers; call is synchronous */
+#define TE_ATTN_QKV_BIAS      (1u << 5) /* add the cache's per-layer q/k/v biases (te_kv_cache_set_qkv_bias)
+                                           to the raw inputs first, in fp32, before RoPE and rounding */
 
 typedef struct te_attn_engine te_attn_engine;
 typedef struct te_kv_cache te_kv_cache;
@@ -133,6 +135,20 @@ TE_API te_status te_kv_cache_write_f16(te_kv_cache *cache, size_t layer, size_t 
 TE_API te_status te_kv_cache_read_f16(te_kv_cache *cache, size_t layer, size_t seq,
                                       size_t token_begin, size_t n_tokens,
                                       uint16_t *k, uint16_t *v);
+/* Stores the fp32 projection biases of layers [layer_begin, +n_layers):
+ * q_bias [n_layers][heads * head_dim], k_bias and v_bias
+ * [n_layers][kv_heads * head_dim] (host or device pointers; NULL = zeros).
+ * Calls with TE_ATTN_QKV_BIAS add them to the raw q/k/v inputs, element by
+ * element in fp32, before RoPE and before the binary16 rounding of the
+ * cache: the reference's te_add_f32 of q/k/v and their biases
+ * (c/src/qwen.c:998-1011 decode, :771-783 prefill; c/src/ops.c:408-416),
+ * fused into the RoPE + append pass as the Metal
+ * te_qkv_bias_rope_cache_batch_h_f32 fuses it
+ * (c/src/metal/metal_kernels.metal.inc:2344-2429).  `heads` is fixed by the
+ * first call (later calls and the compute calls must use the same value). */
+TE_API te_status te_kv_cache_set_qkv_bias(te_kv_cache *cache, size_t layer_begin, size_t n_layers,
+                                          size_t heads, const float *q_bias, const float *k_bias,
+                                          const float *v_bias);
 
 /* Compute ----------------------------------------------------------------- */
 
@@ -143,7 +159,7 @@ TE_API te_status te_kv_cache_read_f16(te_kv_cache *cache, size_t layer, size_t s
  * index).  Replaces the k/v half of te_qkv_bias_rope_cache_batch_h_f32
  * (c/src/metal/metal_kernels.metal.inc:2344-2429) and the CPU append
  * (c/src/qwen.c:805-807).  Flags: TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16,
- * TE_ATTN_NO_ROPE.
+ * TE_ATTN_NO_ROPE, TE_ATTN_QKV_BIAS (k and v biases).
  */
 TE_API te_status te_kv_append_rope(te_kv_cache *cache, size_t layer_begin, size_t n_layers,
                                    size_t seq, const void *k, const void *v, size_t n_tokens,
@@ -156,7 +172,9 @@ TE_API te_status te_kv_append_rope(te_kv_cache *cache, size_t layer_begin, size_
  * all cached tokens including the new one; q is rotated at the sequence's
  * last global position, or at q_positions[i] when q_positions is non-NULL
  * (KV-split shards that do not own the newest token).  Output is normalised
- * attention, or partial records with TE_ATTN_PARTIAL.  Replaces
+ * attention, or partial records with TE_ATTN_PARTIAL.  Flags:
+ * TE_ATTN_ADVANCE, TE_ATTN_PARTIAL, TE_ATTN_NO_ROPE, TE_ATTN_HOST_BUFFERS,
+ * TE_ATTN_QKV_BIAS (q, k_new and v_new get the layer's biases).  Replaces
  * te_attention_decode_f32 as called from c/src/qwen.c:1038-1046 and the
  * attention kernels of te_metal_decode_all_layers_f32
  * (c/src/metal/metal_backend_layers.mm.inc:1273-1296).
@@ -184,7 +202,8 @@ TE_API te_status te_attention_merge_partials(te_attn_engine *engine, const float
  * before the call).  Replaces the CPU prefill loop (c/src/qwen.c:774-824) and
  * te_metal_prefill_all_layers_f32's attention
  * (c/src/metal/metal_backend_layers.mm.inc:2406-2456).  Flags:
- * TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16, TE_ATTN_HOST_BUFFERS.
+ * TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16, TE_ATTN_HOST_BUFFERS, TE_ATTN_NO_ROPE,
+ * TE_ATTN_QKV_BIAS.
  */
 TE_API te_status te_attention_prefill(te_kv_cache *cache, size_t layer_begin, size_t n_layers,
                                       size_t seq, const void *q, const void *k, const void *v,

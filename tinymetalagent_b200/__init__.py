@@ -10,6 +10,7 @@ from .runtime import (  # noqa: F401
     TE_ATTN_INPUT_F16,
     TE_ATTN_NO_ROPE,
     TE_ATTN_PARTIAL,
+    TE_ATTN_QKV_BIAS,
     AttnEngine,
     KVCache,
     TinyEngineError,

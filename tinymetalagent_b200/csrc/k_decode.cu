@@ -80,6 +80,15 @@ struct DecodeCfg {
 template <int HD>
 constexpr int kScratchRec = HD + 4;
 
+// v[i] += b[i] for 8 consecutive fp32 bias values (c/src/ops.c:408-416: one
+// fp32 addition per element, rounded to nearest).
+__device__ __forceinline__ void add_bias8(float (&v)[8], const float* b) {
+  const float4 b0 = *reinterpret_cast<const float4*>(b);
+  const float4 b1 = *reinterpret_cast<const float4*>(b + 4);
+  v[0] = __fadd_rn(v[0], b0.x); v[1] = __fadd_rn(v[1], b0.y); v[2] = __fadd_rn(v[2], b0.z); v[3] = __fadd_rn(v[3], b0.w);
+  v[4] = __fadd_rn(v[4], b1.x); v[5] = __fadd_rn(v[5], b1.y); v[6] = __fadd_rn(v[6], b1.z); v[7] = __fadd_rn(v[7], b1.w);
+}
+
 __device__ __forceinline__ float rope_lo(float a, float b, float c, float s) {
   return __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
 }
@@ -391,9 +400,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
     const int g = lane >> 2, c = lane & 3;  // the fragment owner this lane prepares for
     uint32_t k = 0;
     bool ok = true;
-    // query fragments for the CTA's segment number kk (all 32 lanes; warp-uniform waits)
-    auto prepare = [&](uint32_t kk) -> bool {
+    // query fragments for the CTA's segment number kk (all 32 lanes; warp-uniform
+    // waits); layer_local / kvh locate the segment's query bias rows
+    auto prepare = [&](uint32_t kk, int layer_local, int kvh) -> bool {
       const int b = kk & 1;
+      const float* qbg = p.q_bias ? p.q_bias + ((size_t)(p.layer_begin + layer_local) * H + kvh * G) * HD : nullptr;
       if (!mbar_wait_warp(&qfull[b], (kk >> 1) & 1)) return false;
       if (kk >= 2 && !mbar_wait_warp(&fempty[b], ((kk >> 1) - 1) & 1)) return false;
       const float* sq = reinterpret_cast<const float*>(smem + C::kOffQ + b * C::kQBytes);
@@ -427,11 +438,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
           const float* qr = sq + row * C::kRowF;
           const float4 x0 = *reinterpret_cast<const float4*>(qr + d0);
           const float4 x1 = *reinterpret_cast<const float4*>(qr + d0 + 4);
-          const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          if (qbg) add_bias8(x, qbg + row * HD + d0);
           if (p.rope) {
             const float4 y0 = *reinterpret_cast<const float4*>(qr + dp);
             const float4 y1 = *reinterpret_cast<const float4*>(qr + dp + 4);
-            const float y[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+            float y[8] = {y0.x, y0.y, y0.z, y0.w, y1.x, y1.y, y1.z, y1.w};
+            if (qbg) add_bias8(y, qbg + row * HD + dp);
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               v[r][e] = d0 < half ? rope_lo(x[e], y[e], cv[e], sv[e]) : rope_hi(y[e], x[e], cv[e], sv[e]);
@@ -460,13 +473,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
       return true;
     };
     const int gidx_first = s_beg < s_end ? group_at(p, s_beg).gidx : 0;  // record j of this CTA: group gidx_first + j
-    if (s_beg < s_end) ok = prepare(0);
+    if (s_beg < s_end) {
+      const Seg w0 = p.q_bias ? seg_ending(p, s_end, s_beg) : Seg{};
+      ok = prepare(0, w0.layer_local, w0.kvh);
+    }
     for (long long sg = s_end; sg > s_beg && ok; ++k) {
       const Seg w = seg_ending(p, sg, s_beg);
       sg = w.s_begin;
-      if (sg > s_beg && !prepare(k + 1)) {
-        ok = false;
-        break;
+      if (sg > s_beg) {
+        const Seg wn = p.q_bias ? seg_ending(p, sg, s_beg) : Seg{};
+        if (!prepare(k + 1, wn.layer_local, wn.kvh)) {
+          ok = false;
+          break;
+        }
       }
       if (sg == s_beg) break;  // the CTA's last segment: the consumer warps merge it
       // merge item k: the four consumer warps' (m, l, O) -> output or split-K record
@@ -667,8 +686,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
                                            : p.page_table[se.slot * p.max_pages_per_seq + new_idx / p.page_tokens];
         const size_t row = ((size_t)((p.layer_begin + w.layer_local) * p.num_pages + page) * p.kv_heads + w.kvh) *
                                p.page_tokens + (new_idx % p.page_tokens);
+        // projection biases of this layer (fp32 adds before RoPE and rounding)
+        const size_t kvb = ((size_t)(p.layer_begin + w.layer_local) * p.kv_heads + w.kvh) * HD;
+        const float* kb = p.k_bias ? p.k_bias + kvb : nullptr;
+        const float* vb = p.v_bias ? p.v_bias + kvb : nullptr;
+        const float* qbg = p.q_bias ? p.q_bias + ((size_t)(p.layer_begin + w.layer_local) * H + w.kvh * G) * HD : nullptr;
         for (int i = lane; i < half; i += 32) {
-          const float a = nb[i], bb = nb[i + half];
+          float a = nb[i], bb = nb[i + half];
+          if (kb) {
+            a = __fadd_rn(a, kb[i]);
+            bb = __fadd_rn(bb, kb[i + half]);
+          }
           float lo = a, hi = bb;
           if (p.rope) {
             lo = rope_lo(a, bb, csk[i], csk[half + i]);
@@ -681,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
           nb[i + half] = __half2float(hh);
         }
         for (int i = lane; i < HD; i += 32) {
-          const __half hv = __float2half_rn(nb[HD + i]);
+          const __half hv = __float2half_rn(vb ? __fadd_rn(nb[HD + i], vb[i]) : nb[HD + i]);
           p.v_pool[row * HD + i] = __half_as_ushort(hv);
           res[16 + i] = __half2float(hv);
         }
@@ -691,6 +719,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
           float dot = 0.f;
           for (int i = lane; i < half; i += 32) {
             float ql = qr[i], qh = qr[i + half];
+            if (qbg) {
+              ql = __fadd_rn(ql, qbg[h * HD + i]);
+              qh = __fadd_rn(qh, qbg[h * HD + i + half]);
+            }
             if (p.rope) {
               const float x = ql, y = qh;
               ql = rope_lo(x, y, cs[i], cs[half + i]);

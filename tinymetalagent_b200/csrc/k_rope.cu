@@ -58,6 +58,15 @@ __device__ __forceinline__ void load8(const void* base, size_t idx, int f16, flo
   }
 }
 
+// v[i] += b[i] for 8 consecutive fp32 bias values (the reference's te_add_f32,
+// c/src/ops.c:408-416: one fp32 addition per element, rounded to nearest).
+__device__ __forceinline__ void add_bias8(float (&v)[8], const float* b) {
+  const float4 b0 = *reinterpret_cast<const float4*>(b);
+  const float4 b1 = *reinterpret_cast<const float4*>(b + 4);
+  v[0] = __fadd_rn(v[0], b0.x); v[1] = __fadd_rn(v[1], b0.y); v[2] = __fadd_rn(v[2], b0.z); v[3] = __fadd_rn(v[3], b0.w);
+  v[4] = __fadd_rn(v[4], b1.x); v[5] = __fadd_rn(v[5], b1.y); v[6] = __fadd_rn(v[6], b1.z); v[7] = __fadd_rn(v[7], b1.w);
+}
+
 __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   uint4 u;
   __half2* h = reinterpret_cast<__half2*>(&u);
@@ -101,6 +110,13 @@ __global__ void append_rope_kernel(const AppendParams p) {
   load8(p.k, in_row + d + half, p.input_f16, khi);
   load8(p.v, in_row + d, p.input_f16, vlo);
   load8(p.v, in_row + d + half, p.input_f16, vhi);
+  if (p.k_bias) {
+    const size_t brow = ((size_t)(p.layer_begin + ll) * p.kv_heads + kvh) * HD;
+    add_bias8(klo, p.k_bias + brow + d);
+    add_bias8(khi, p.k_bias + brow + d + half);
+    add_bias8(vlo, p.v_bias + brow + d);
+    add_bias8(vhi, p.v_bias + brow + d + half);
+  }
   if (p.rope) {
     const int pos = p.first_pos + t;
     rope8(klo, khi, p.rope_cos + (size_t)pos * half, p.rope_sin + (size_t)pos * half, d);
@@ -120,11 +136,15 @@ __global__ void append_rope_kernel(const AppendParams p) {
 // Query rows of one token and head: f16 in the same layout, rotated unless
 // RoPE is off.
 template <int HD>
-__device__ __forceinline__ void q_prep_row(const QPrepParams& p, size_t row, int t, int d) {
+__device__ __forceinline__ void q_prep_row(const QPrepParams& p, size_t row, int t, int d, const float* bias_row) {
   constexpr int half = HD / 2;
   float lo[8], hi[8];
   load8(p.q, row + d, p.input_f16, lo);
   load8(p.q, row + d + half, p.input_f16, hi);
+  if (bias_row) {
+    add_bias8(lo, bias_row + d);
+    add_bias8(hi, bias_row + d + half);
+  }
   if (p.rope) {
     const int pos = p.first_pos + t;
     rope8(lo, hi, p.rope_cos + (size_t)pos * half, p.rope_sin + (size_t)pos * half, d);
@@ -142,7 +162,10 @@ __global__ void q_prep_kernel(const QPrepParams p) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (uint32_t)p.n_tokens * (uint32_t)p.heads * groups) return;
   const uint32_t r = i / groups;
-  q_prep_row<HD>(p, ((size_t)ll * p.n_tokens * p.heads + r) * HD, (int)(r / (uint32_t)p.heads), (int)(i % groups) * 8);
+  const float* bias_row =
+      p.q_bias ? p.q_bias + ((size_t)(p.layer_begin + ll) * p.heads + (r % (uint32_t)p.heads)) * HD : nullptr;
+  q_prep_row<HD>(p, ((size_t)ll * p.n_tokens * p.heads + r) * HD, (int)(r / (uint32_t)p.heads), (int)(i % groups) * 8,
+                 bias_row);
 }
 
 // A prefill call's inputs in one pass, streamed through shared memory: each
@@ -268,6 +291,11 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prefill_prep_kernel(const App
         for (int k = 0; k < kQB; ++k) {
           const int r = rb + k * kRowLanes;
           if (r < qrows) {
+            if (q.q_bias) {
+              const float* br = q.q_bias + ((size_t)(q.layer_begin + ll) * qrows + r) * HD;
+              add_bias8(lo[k], br + d);
+              add_bias8(hi[k], br + d + half);
+            }
             if (q.rope) {
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
@@ -288,6 +316,13 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prefill_prep_kernel(const App
         load8s(sk + (size_t)(kvh * HD + d + half) * P::kEl, khi);
         load8s(sv + (size_t)(kvh * HD + d) * P::kEl, vlo);
         load8s(sv + (size_t)(kvh * HD + d + half) * P::kEl, vhi);
+        if (a.k_bias) {
+          const size_t brow = ((size_t)layer * a.kv_heads + kvh) * HD;
+          add_bias8(klo, a.k_bias + brow + d);
+          add_bias8(khi, a.k_bias + brow + d + half);
+          add_bias8(vlo, a.v_bias + brow + d);
+          add_bias8(vhi, a.v_bias + brow + d + half);
+        }
         if (a.rope) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) {

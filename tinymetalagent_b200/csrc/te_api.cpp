@@ -59,6 +59,12 @@ struct te_kv_cache {
   float* d_cos = nullptr;
   float* d_sin = nullptr;
   CUtensorMap tmap_k{}, tmap_v{};
+  // projection biases (te_kv_cache_set_qkv_bias): [layers][bias_heads * hd] for q,
+  // [layers][kv_heads * hd] for k and v; null until set
+  float* d_qb = nullptr;
+  float* d_kb = nullptr;
+  float* d_vb = nullptr;
+  uint32_t bias_heads = 0;
 };
 
 namespace {
@@ -529,6 +535,7 @@ TE_API void te_kv_cache_free(te_kv_cache* c) {
     cudaFree(c->v_pool);
     cudaFree(c->d_page_table);
     cudaFree(c->d_cos);
+    cudaFree(c->d_kb);  // the bias allocation (d_vb and d_qb point into it)
   }
   delete c;
 }
@@ -594,6 +601,47 @@ TE_API te_status te_kv_cache_read_f16(te_kv_cache* c, size_t layer, size_t seq, 
   return err == cudaSuccess ? TE_STATUS_OK : cuda_fail(c->eng, err, "KV read");
 }
 
+TE_API te_status te_kv_cache_set_qkv_bias(te_kv_cache* c, size_t layer_begin, size_t n_layers, size_t heads,
+                                          const float* q_bias, const float* k_bias, const float* v_bias) {
+  if (!c || n_layers == 0 || heads == 0 || layer_begin + n_layers > c->d.layers) return TE_STATUS_INVALID_ARGUMENT;
+  te_attn_engine* e = c->eng;
+  const size_t hkv = c->d.kv_heads, hd = c->d.head_dim;
+  if (heads % hkv != 0) return fail(e, TE_STATUS_INVALID_ARGUMENT, "heads must be a multiple of kv_heads");
+  if (c->bias_heads != 0 && c->bias_heads != heads) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "heads differs from the first te_kv_cache_set_qkv_bias call");
+  }
+  DeviceGuard dg(e->device);
+  const size_t L = c->d.layers;
+  if (!c->d_qb) {
+    // one allocation: q biases, then k, then v; zeros until set
+    const size_t bytes = L * (heads + 2 * hkv) * hd * sizeof(float);
+    cudaError_t err = cudaMalloc(&c->d_kb, bytes);
+    if (err == cudaSuccess) err = cudaMemsetAsync(c->d_kb, 0, bytes, e->stream);
+    if (err != cudaSuccess) {
+      cudaFree(c->d_kb);
+      c->d_kb = nullptr;
+      return cuda_fail(e, err, "bias allocation");
+    }
+    c->d_vb = c->d_kb + L * hkv * hd;
+    c->d_qb = c->d_vb + L * hkv * hd;
+    c->bias_heads = (uint32_t)heads;
+  }
+  struct Part {
+    float* dst;
+    const float* src;
+    size_t row;
+  } parts[3] = {{c->d_qb, q_bias, heads * hd}, {c->d_kb, k_bias, hkv * hd}, {c->d_vb, v_bias, hkv * hd}};
+  for (const Part& pt : parts) {
+    float* dst = pt.dst + layer_begin * pt.row;
+    const size_t bytes = n_layers * pt.row * sizeof(float);
+    const cudaError_t err = pt.src ? cudaMemcpyAsync(dst, pt.src, bytes, cudaMemcpyDefault, e->stream)
+                                   : cudaMemsetAsync(dst, 0, bytes, e->stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "bias upload");
+  }
+  const cudaError_t err = cudaStreamSynchronize(e->stream);
+  return err == cudaSuccess ? TE_STATUS_OK : cuda_fail(e, err, "bias upload");
+}
+
 // ===========================================================================
 // Compute
 // ===========================================================================
@@ -604,8 +652,11 @@ TE_API te_status te_kv_append_rope(te_kv_cache* c, size_t layer_begin, size_t n_
       seq >= c->d.max_seqs) {
     return TE_STATUS_INVALID_ARGUMENT;
   }
-  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | TE_ATTN_NO_ROPE)) {
+  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | TE_ATTN_NO_ROPE | TE_ATTN_QKV_BIAS)) {
     return fail(c->eng, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for te_kv_append_rope");
+  }
+  if ((flags & TE_ATTN_QKV_BIAS) && !c->d_kb) {
+    return fail(c->eng, TE_STATUS_INVALID_ARGUMENT, "TE_ATTN_QKV_BIAS before te_kv_cache_set_qkv_bias");
   }
   te_attn_engine* e = c->eng;
   if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u) {
@@ -626,6 +677,10 @@ TE_API te_status te_kv_append_rope(te_kv_cache* c, size_t layer_begin, size_t n_
   p.page_row = c->d_page_table + seq * c->pages_per_seq;
   p.rope_cos = c->d_cos;
   p.rope_sin = c->d_sin;
+  if (flags & TE_ATTN_QKV_BIAS) {
+    p.k_bias = c->d_kb;
+    p.v_bias = c->d_vb;
+  }
   p.input_f16 = (flags & TE_ATTN_INPUT_F16) ? 1 : 0;
   p.rope = (flags & TE_ATTN_NO_ROPE) ? 0 : 1;
   p.n_layers = (int32_t)n_layers;
@@ -652,11 +707,14 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
     return TE_STATUS_INVALID_ARGUMENT;
   }
   te_attn_engine* e = c->eng;
-  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_PARTIAL | TE_ATTN_NO_ROPE | TE_ATTN_HOST_BUFFERS)) {
+  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_PARTIAL | TE_ATTN_NO_ROPE | TE_ATTN_HOST_BUFFERS | TE_ATTN_QKV_BIAS)) {
     return fail(e, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for te_attention_decode");
   }
   const size_t hkv = c->d.kv_heads, hd = c->d.head_dim;
   if (heads % hkv != 0) return fail(e, TE_STATUS_INVALID_ARGUMENT, "heads must be a multiple of kv_heads");
+  if ((flags & TE_ATTN_QKV_BIAS) && (!c->d_qb || c->bias_heads != heads)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "TE_ATTN_QKV_BIAS needs te_kv_cache_set_qkv_bias with these heads");
+  }
   const size_t G = heads / hkv;
   if (G > 16) return fail(e, TE_STATUS_UNSUPPORTED, "more than 16 query heads per kv head");
   if (n_seqs > c->d.max_seqs) return TE_STATUS_INVALID_ARGUMENT;
@@ -738,6 +796,11 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
   p.v_pool = c->v_pool;
   p.rope_cos = c->d_cos;
   p.rope_sin = c->d_sin;
+  if (flags & TE_ATTN_QKV_BIAS) {
+    p.q_bias = c->d_qb;
+    p.k_bias = c->d_kb;
+    p.v_bias = c->d_vb;
+  }
   p.error = e->d_error;
   p.seq_total = (int32_t)n_seqs;
   p.layer_begin = (int32_t)layer_begin;
@@ -827,11 +890,15 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
     return TE_STATUS_INVALID_ARGUMENT;
   }
   te_attn_engine* e = c->eng;
-  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | TE_ATTN_HOST_BUFFERS | TE_ATTN_NO_ROPE)) {
+  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | TE_ATTN_HOST_BUFFERS | TE_ATTN_NO_ROPE | TE_ATTN_QKV_BIAS)) {
     return fail(e, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for te_attention_prefill");
   }
   const size_t hkv = c->d.kv_heads, hd = c->d.head_dim;
   if (heads % hkv != 0) return fail(e, TE_STATUS_INVALID_ARGUMENT, "heads must be a multiple of kv_heads");
+  const bool bias = (flags & TE_ATTN_QKV_BIAS) != 0;
+  if (bias && (!c->d_qb || c->bias_heads != heads)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "TE_ATTN_QKV_BIAS needs te_kv_cache_set_qkv_bias with these heads");
+  }
   if (hd != 128) return fail(e, TE_STATUS_UNSUPPORTED, "prefill kernel is built for head_dim 128");
   if (!(flags & TE_ATTN_HOST_BUFFERS) &&
       ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
@@ -887,6 +954,10 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   a.page_row = c->d_page_table + seq * c->pages_per_seq;
   a.rope_cos = c->d_cos;
   a.rope_sin = c->d_sin;
+  if (bias) {
+    a.k_bias = c->d_kb;
+    a.v_bias = c->d_vb;
+  }
   a.input_f16 = (flags & TE_ATTN_INPUT_F16) ? 1 : 0;
   a.rope = (flags & TE_ATTN_NO_ROPE) ? 0 : 1;
   a.n_layers = (int32_t)n_layers;
@@ -898,10 +969,10 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   a.head_dim = (int32_t)hd;
   a.num_pages = (int32_t)c->d.total_pages;
   a.page_tokens = (int32_t)c->d.page_tokens;
-  // 2) f16 queries for the kernel: f16 inputs without RoPE are read as they
-  // are; otherwise they are rotated (and converted) into scratch in the same
-  // layout, in one pass with the append.
-  const bool with_q = !(a.input_f16 && !a.rope);
+  // 2) f16 queries for the kernel: f16 inputs without RoPE or bias are read
+  // as they are; otherwise they are biased, rotated and converted into
+  // scratch in the same layout, in one pass with the append.
+  const bool with_q = !(a.input_f16 && !a.rope && !bias);
   const void* qf16 = dq;
   QPrepParams qp{};
   if (with_q) {
@@ -911,9 +982,11 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
     qp.qh = reinterpret_cast<__half*>(e->qh);
     qp.rope_cos = c->d_cos;
     qp.rope_sin = c->d_sin;
+    qp.q_bias = bias ? c->d_qb : nullptr;
     qp.input_f16 = a.input_f16;
     qp.rope = a.rope;
     qp.n_layers = (int32_t)n_layers;
+    qp.layer_begin = (int32_t)layer_begin;
     qp.n_tokens = (int32_t)n_tokens;
     qp.heads = (int32_t)heads;
     qp.head_dim = (int32_t)hd;

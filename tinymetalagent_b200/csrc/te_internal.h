@@ -60,6 +60,9 @@ struct DecodeParams {
   uint16_t* v_pool;
   const float* rope_cos;      // [max_position][hd/2]
   const float* rope_sin;
+  const float* q_bias;        // null, or [cache layers][heads * hd] added to q before RoPE
+  const float* k_bias;        // null, or [cache layers][kv_heads * hd] added to k_new / v_new
+  const float* v_bias;
   int* error;
   int32_t n_seqs;             // sequences in this launch (<= kMaxParamSeqs)
   int32_t seq_total;          // sequences in the caller's arrays (row stride of q/out)
@@ -164,6 +167,8 @@ struct AppendParams {
   const int32_t* page_row;  // page table row of the sequence
   const float* rope_cos;
   const float* rope_sin;
+  const float* k_bias;      // null, or [cache layers][kv_heads * hd] added before RoPE / rounding
+  const float* v_bias;
   int32_t input_f16;
   int32_t rope;
   int32_t n_layers;
@@ -186,9 +191,11 @@ struct QPrepParams {
   __half* qh;               // same layout, f16
   const float* rope_cos;
   const float* rope_sin;
+  const float* q_bias;      // null, or [cache layers][heads * hd] added before RoPE / rounding
   int32_t input_f16;
   int32_t rope;
   int32_t n_layers;
+  int32_t layer_begin;      // cache layer of local layer 0 (bias rows)
   int32_t n_tokens;
   int32_t heads;
   int32_t head_dim;

@@ -32,6 +32,7 @@ TE_ATTN_PARTIAL = 1 << 1
 TE_ATTN_NO_ROPE = 1 << 2
 TE_ATTN_INPUT_F16 = 1 << 3
 TE_ATTN_HOST_BUFFERS = 1 << 4
+TE_ATTN_QKV_BIAS = 1 << 5
 
 
 class TinyEngineError(RuntimeError):
@@ -109,6 +110,7 @@ SIGNATURES: dict[str, tuple] = {
     "te_kv_cache_reserve": (_int, [_vp, _sz, _sz]),
     "te_kv_cache_write_f16": (_int, [_vp, _sz, _sz, _sz, _sz, _vp, _vp]),
     "te_kv_cache_read_f16": (_int, [_vp, _sz, _sz, _sz, _sz, _vp, _vp]),
+    "te_kv_cache_set_qkv_bias": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _vp]),
     "te_kv_append_rope": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _sz, ctypes.c_uint32]),
     "te_attention_decode": (_int, [_vp, _sz, _sz, _u32p, _sz, _i64p, _vp, _vp, _vp, _sz, _vp, ctypes.c_uint32]),
     "te_attention_merge_partials": (_int, [_vp, _vp, _sz, _sz, _sz, _vp, ctypes.c_uint32]),
@@ -311,6 +313,33 @@ class KVCache:
         """k, v: [n][kv_heads][head_dim] binary16 (torch f16 tensor, numpy float16/uint16)."""
         n = int(k.shape[0])
         self._c(self.lib.te_kv_cache_write_f16(self.handle, layer, seq, token_begin, n, _addr(k), _addr(v)))
+
+    def set_qkv_bias(self, layer_begin: int, heads: int, q_bias=None, k_bias=None, v_bias=None) -> None:
+        """fp32 projection biases of layers [layer_begin, +n): q_bias [n][heads * head_dim], k_bias and
+        v_bias [n][kv_heads * head_dim] (numpy or torch; None = zeros).  Calls with TE_ATTN_QKV_BIAS add
+        them to the raw q/k/v inputs before RoPE and rounding."""
+        import numpy as np
+        arrs = []
+        n = None
+        for b, width in ((q_bias, heads * self.head_dim), (k_bias, self.kv_heads * self.head_dim),
+                         (v_bias, self.kv_heads * self.head_dim)):
+            if b is None:
+                arrs.append(None)
+                continue
+            if hasattr(b, "detach"):
+                b = b.detach().float().contiguous()
+            else:
+                b = np.ascontiguousarray(np.asarray(b, dtype=np.float32))
+            rows = int(b.numel() if hasattr(b, "numel") else b.size) // width
+            n = rows if n is None else n
+            if rows * width != (b.numel() if hasattr(b, "numel") else b.size) or rows != n:
+                raise ValueError("bias shapes disagree with heads / kv_heads * head_dim")
+            arrs.append(b)
+        if n is None:
+            raise ValueError("no bias given")
+        ptr = lambda b: None if b is None else _addr(b)  # noqa: E731
+        self._c(self.lib.te_kv_cache_set_qkv_bias(self.handle, layer_begin, n, heads, ptr(arrs[0]), ptr(arrs[1]),
+                                                  ptr(arrs[2])))
 
     def read_f16(self, layer: int, seq: int, token_begin: int, n_tokens: int):
         import numpy as np
