@@ -75,6 +75,7 @@ def test_engine_api_null_guards(lib):
     assert lib.te_attention_prefill(None, 0, 1, 0, None, None, None, 1, 8, None, 0) == R.TE_STATUS_INVALID_ARGUMENT
     assert lib.te_attention_merge_partials(None, None, 1, 1, 64, None, 0) == R.TE_STATUS_INVALID_ARGUMENT
     assert lib.te_kv_cache_seq_reset(None, 0, 0) == R.TE_STATUS_INVALID_ARGUMENT
+    assert lib.te_kv_cache_set_qkv_bias(None, 0, 1, 8, None, None, None) == R.TE_STATUS_INVALID_ARGUMENT
     lib.te_attn_engine_free(None)
     lib.te_kv_cache_free(None)
     assert lib.te_attn_engine_launch_count(None) == 0
@@ -103,3 +104,16 @@ def test_no_cpu_fallback_without_gpu(lib):
     with pytest.raises(R.TinyEngineError) as ei:
         R.AttnEngine(0)
     assert ei.value.status == R.TE_STATUS_UNSUPPORTED
+
+
+def test_set_qkv_bias_checks_shapes_before_the_library():
+    # The binding validates the bias widths (heads * head_dim, kv_heads * head_dim)
+    # and row counts before calling the C function.
+    cache = object.__new__(R.KVCache)
+    cache.head_dim, cache.kv_heads = 128, 2
+    with pytest.raises(ValueError):
+        cache.set_qkv_bias(0, 16, np.zeros((2, 16 * 128 + 1), np.float32))
+    with pytest.raises(ValueError):
+        cache.set_qkv_bias(0, 16, np.zeros((2, 16 * 128), np.float32), np.zeros((3, 2 * 128), np.float32))
+    with pytest.raises(ValueError):
+        cache.set_qkv_bias(0, 16)
