@@ -676,7 +676,8 @@ def run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank):
         kn = torch.randn((L7, 1, KV7, HEAD_DIM), generator=g, device="cuda")
         vn = torch.randn((L7, 1, KV7, HEAD_DIM), generator=g, device="cuda")
     stream.synchronize()
-    dec = KVSplitDecoder(spec, L7, H7, HEAD_DIM, cache=cache, engine=eng, device="cuda")
+    exchange = args.long_exchange if world > 1 else "nccl"
+    dec = KVSplitDecoder(spec, L7, H7, HEAD_DIM, cache=cache, engine=eng, device="cuda", exchange=exchange)
 
     def step():
         with torch.cuda.stream(stream):  # NCCL and the engine share the engine's stream
@@ -709,6 +710,9 @@ def run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank):
     ms = _time_steps(stream, replay, 1, world, dist)
     eng.synchronize()
     del graph
+    if world > 1:
+        dist.barrier()  # every rank's last step is done before the exchange areas go away
+    dec.close()
     bytes_all = sum(step_bytes(n_ctx + i + 1, L7, H7, KV7) for i in range(steps))
     gbs = bytes_all / (ms / 1e3) / 1e9
     cache.close()
@@ -718,8 +722,11 @@ def run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank):
     return {"metric": "long-context decode tokens/s (BASELINE config 5)", "cpu_baseline": cpu, "value": round(steps / (ms / 1e3), 1),
             "unit": "tokens/s", "scaling": "strong", "steps": steps, "ms_per_step": round(ms / steps, 4),
             "workload": "long7b: one sequence of 32768 cached tokens, 28 layers, H28/Hkv4/hd128, f16 KV N(0,1), "
-                        f"KV split over {world} rank(s), NCCL all-gather of (acc, m, l) + LSE merge per step; "
-                        "steps captured in one CUDA graph",
+                        f"KV split over {world} rank(s), "
+                        + ("NVLink push of (acc, m, l) into the peers + LSE merge in one kernel per step; "
+                           if exchange == "p2p" else "NCCL all-gather of (acc, m, l) + LSE merge per step; ")
+                        + "steps captured in one CUDA graph",
+            "exchange": exchange,
             "tokens_per_rank": n_local, "kv_gbs": round(gbs, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(gbs / world / hbm_peak, 4), "per": "GPU (max-over-ranks time)",
@@ -741,6 +748,8 @@ def main() -> None:
     ap.add_argument("--no-configs", action="store_true", help="skip the config-4 / config-5 measurements")
     ap.add_argument("--cfg-steps", type=int, default=16, help="decode steps timed for config 4")
     ap.add_argument("--long-steps", type=int, default=128, help="decode steps timed for config 5")
+    ap.add_argument("--long-exchange", choices=["nccl", "p2p"], default="nccl",
+                    help="config 5 at N>1: NCCL all-gather + merge, or the NVLink exchange kernel")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

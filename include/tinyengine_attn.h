@@ -195,6 +195,38 @@ TE_API te_status te_attention_merge_partials(te_attn_engine *engine, const float
                                              size_t n_parts, size_t rows, size_t head_dim,
                                              float *out, uint32_t flags);
 
+/* KV-split exchange over NVLink --------------------------------------------
+ *
+ * For one sequence whose cached tokens are split over `world` GPUs (one
+ * process per GPU, each rank on its own device with its own engine), one
+ * kernel per decode step replaces the all-gather of the partial records and
+ * te_attention_merge_partials: every rank pushes its records
+ * [rows][head_dim + 2] (from te_attention_decode with TE_ATTN_PARTIAL) into
+ * the other ranks' exchange areas over NVLink (CUDA IPC mappings), then
+ * merges [rows][head_dim] from what has arrived.  No reference counterpart
+ * (the reference runs on one device); the merge is
+ * te_attention_merge_partials'.
+ *
+ * Setup: te_attn_exchange_create on every rank (same world, rows, head_dim),
+ * exchange the TE_ATTN_IPC_HANDLE_BYTES-byte handles among the ranks (any
+ * host channel), te_attn_exchange_connect with all of them in rank order.
+ * Every rank then calls te_attn_exchange_merge once per step, in the same
+ * order; the call is asynchronous on the engine's stream and can be captured
+ * in a CUDA graph.  A rank waits at most 2 s for its peers (then the engine
+ * reports TE_STATUS_RUNTIME_ERROR at its next synchronisation).  Free only
+ * after every rank has finished its last step (a host barrier), since the
+ * peers write into this rank's area.  world <= 8.
+ */
+typedef struct te_attn_exchange te_attn_exchange;
+#define TE_ATTN_IPC_HANDLE_BYTES 64
+
+TE_API te_status te_attn_exchange_create(te_attn_engine *engine, size_t world, size_t rank, size_t rows,
+                                         size_t head_dim, te_attn_exchange **out_exchange,
+                                         unsigned char *ipc_handle);
+TE_API te_status te_attn_exchange_connect(te_attn_exchange *exchange, const unsigned char *ipc_handles);
+TE_API te_status te_attn_exchange_merge(te_attn_exchange *exchange, const float *partial, float *out);
+TE_API void te_attn_exchange_free(te_attn_exchange *exchange);
+
 /*
  * Causal prefill of n_tokens new tokens of sequence `seq` over layers
  * [layer_begin, +n_layers): RoPE + f16 append of k/v, RoPE of q, then every

@@ -76,6 +76,10 @@ def test_engine_api_null_guards(lib):
     assert lib.te_attention_merge_partials(None, None, 1, 1, 64, None, 0) == R.TE_STATUS_INVALID_ARGUMENT
     assert lib.te_kv_cache_seq_reset(None, 0, 0) == R.TE_STATUS_INVALID_ARGUMENT
     assert lib.te_kv_cache_set_qkv_bias(None, 0, 1, 8, None, None, None) == R.TE_STATUS_INVALID_ARGUMENT
+    assert lib.te_attn_exchange_create(None, 2, 0, 8, 128, None, None) == R.TE_STATUS_INVALID_ARGUMENT
+    assert lib.te_attn_exchange_connect(None, None) == R.TE_STATUS_INVALID_ARGUMENT
+    assert lib.te_attn_exchange_merge(None, None, None) == R.TE_STATUS_INVALID_ARGUMENT
+    lib.te_attn_exchange_free(None)
     lib.te_attn_engine_free(None)
     lib.te_kv_cache_free(None)
     assert lib.te_attn_engine_launch_count(None) == 0

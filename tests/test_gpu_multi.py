@@ -1,7 +1,8 @@
 """KV-sequence split on two GPUs (BASELINE config 5's partitioning): each rank
 holds half of one sequence's cache, computes partial (acc, m, l) records, the
-records are all-gathered over NCCL and merged by log-sum-exp; the tail rank
-appends the new token.  Checked against the CPU oracle over the whole
+records are exchanged -- all-gathered over NCCL, or pushed into the peer's
+memory over NVLink by the p2p exchange kernel -- and merged by log-sum-exp;
+the tail rank appends the new token.  Checked against the CPU oracle over the whole
 sequence (outputs within 1e-3 + 2e-3 |ref|; appended rows bit-exact).
 Skipped on fewer than two GPUs."""
 import os
@@ -12,7 +13,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-L, H, HKV, HD, N, STEPS, THETA = 2, 16, 2, 128, 3000, 2, 1e6
+L, H, HKV, HD, N, STEPS, THETA = 2, 16, 2, 128, 3000, 5, 1e6
 
 
 def _data():
@@ -23,7 +24,7 @@ def _data():
     return k, v, q
 
 
-def _worker(rank, world, port_no, out_dir):
+def _worker(rank, world, port_no, out_dir, exchange):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -48,7 +49,7 @@ def _worker(rank, world, port_no, out_dir):
             v = torch.from_numpy(np.ascontiguousarray(vraw[layer, spec.begin:spec.end])).cuda()
             cache.append_rope(layer, 1, 0, k, v, n_local, TE_ATTN_ADVANCE if layer == L - 1 else 0)
         eng.synchronize()
-        dec = KVSplitDecoder(spec, L, H, HD, cache=cache, engine=eng, device="cuda")
+        dec = KVSplitDecoder(spec, L, H, HD, cache=cache, engine=eng, device="cuda", exchange=exchange)
         outs = []
         for s in range(STEPS):
             q = torch.from_numpy(np.ascontiguousarray(qraw[s])).cuda()
@@ -58,6 +59,8 @@ def _worker(rank, world, port_no, out_dir):
             eng.synchronize()
             outs.append(o.cpu().numpy().copy())
         np.save(os.path.join(out_dir, f"out{rank}.npy"), np.stack(outs))
+        dist.barrier()  # every rank's last step is done before the exchange areas go away
+        dec.close()
         if spec.is_tail:
             kg, vg = cache.read_f16(0, 0, n_local, STEPS)
             np.save(os.path.join(out_dir, "tail_k.npy"), kg)
@@ -74,12 +77,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_kv_split_two_gpus_matches_oracle(port, tmp_path):
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+def test_kv_split_two_gpus_matches_oracle(port, tmp_path, exchange):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path), exchange), nprocs=2, join=True,
+                       start_method="spawn")
     kraw, vraw, qraw = _data()
     outs = [np.load(tmp_path / f"out{r}.npy") for r in range(2)]
     assert np.array_equal(outs[0], outs[1])  # every rank holds the same merged output

@@ -67,6 +67,14 @@ struct te_kv_cache {
   uint32_t bias_heads = 0;
 };
 
+struct te_attn_exchange {
+  te_attn_engine* eng = nullptr;
+  int world = 0, rank = 0, rows = 0, hd = 0, grid = 0;
+  float* local = nullptr;                  // this rank's exchange area
+  float* base[kMaxExchangeRanks] = {};     // every rank's area as mapped in this process
+  bool connected = false;
+};
+
 namespace {
 
 // Switches to a device for the duration of a call and restores the caller's.
@@ -880,6 +888,100 @@ TE_API te_status te_attention_merge_partials(te_attn_engine* e, const float* par
   if (err != cudaSuccess) return cuda_fail(e, err, "merge kernel launch");
   e->launches++;
   return TE_STATUS_OK;
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == TE_ATTN_IPC_HANDLE_BYTES, "IPC handle size");
+
+TE_API te_status te_attn_exchange_create(te_attn_engine* e, size_t world, size_t rank, size_t rows, size_t head_dim,
+                                         te_attn_exchange** out, unsigned char* ipc_handle) {
+  if (!e || !out || !ipc_handle || world < 2 || world > (size_t)kMaxExchangeRanks || rank >= world || rows == 0 ||
+      rows > (1u << 20) || (head_dim != 64 && head_dim != 128)) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  DeviceGuard dg(e->device);
+  te_attn_exchange* x = new te_attn_exchange();
+  x->eng = e;
+  x->world = (int)world;
+  x->rank = (int)rank;
+  x->rows = (int)rows;
+  x->hd = (int)head_dim;
+  x->grid = exchange_grid((int)rows);
+  const size_t bytes = exchange_area_bytes(x->world, x->rows, x->hd, x->grid);
+  cudaError_t err = cudaMalloc(&x->local, bytes);
+  if (err == cudaSuccess) err = cudaMemset(x->local, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (err == cudaSuccess) err = cudaIpcGetMemHandle(&h, x->local);
+  if (err != cudaSuccess) {
+    cudaFree(x->local);
+    delete x;
+    return cuda_fail(e, err, "exchange area");
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  x->base[x->rank] = x->local;
+  *out = x;
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_attn_exchange_connect(te_attn_exchange* x, const unsigned char* handles) {
+  if (!x || !handles || x->connected) return TE_STATUS_INVALID_ARGUMENT;
+  DeviceGuard dg(x->eng->device);
+  for (int w = 0; w < x->world; ++w) {
+    if (w == x->rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handles + (size_t)w * TE_ATTN_IPC_HANDLE_BYTES, sizeof(h));
+    void* ptr = nullptr;
+    const cudaError_t err = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) {
+      for (int v = 0; v < w; ++v) {
+        if (v != x->rank && x->base[v]) cudaIpcCloseMemHandle(x->base[v]);
+        if (v != x->rank) x->base[v] = nullptr;
+      }
+      return cuda_fail(x->eng, err, "exchange peer mapping");
+    }
+    x->base[w] = static_cast<float*>(ptr);
+  }
+  x->connected = true;
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_attn_exchange_merge(te_attn_exchange* x, const float* partial, float* out) {
+  if (!x || !partial || !out) return TE_STATUS_INVALID_ARGUMENT;
+  if (!x->connected) return fail(x->eng, TE_STATUS_INVALID_ARGUMENT, "exchange not connected");
+  if ((reinterpret_cast<uintptr_t>(partial) | reinterpret_cast<uintptr_t>(out)) & 7u) {
+    return fail(x->eng, TE_STATUS_INVALID_ARGUMENT, "partial and out must be 8-byte aligned");
+  }
+  te_attn_engine* e = x->eng;
+  DeviceGuard dg(e->device);
+  ExchangeParams p{};
+  p.partial = partial;
+  p.out = out;
+  for (int w = 0; w < x->world; ++w) p.base[w] = x->base[w];
+  const size_t data_floats = 2ull * x->world * x->rows * (x->hd + 2);
+  p.steps = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned long long*>(x->local + data_floats) + 2 * x->grid);
+  p.error = e->d_error;
+  p.world = x->world;
+  p.rank = x->rank;
+  p.rows = x->rows;
+  p.head_dim = x->hd;
+  p.grid = x->grid;
+  p.rows_per_cta = (x->rows + x->grid - 1) / x->grid;
+  const cudaError_t err = launch_exchange_merge(p, e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "exchange kernel launch");
+  e->launches++;
+  return TE_STATUS_OK;
+}
+
+TE_API void te_attn_exchange_free(te_attn_exchange* x) {
+  if (!x) return;
+  {
+    DeviceGuard dg(x->eng->device);
+    cudaStreamSynchronize(x->eng->stream);
+    for (int w = 0; w < x->world; ++w) {
+      if (w != x->rank && x->base[w]) cudaIpcCloseMemHandle(x->base[w]);
+    }
+    cudaFree(x->local);
+  }
+  delete x;
 }
 
 TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t n_layers, size_t seq,

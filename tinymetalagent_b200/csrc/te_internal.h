@@ -232,4 +232,20 @@ cudaError_t launch_prefill_tc(const PrefillParams& p, int sm_count, cudaStream_t
 // Work items of the prefill kernel: (layer, kv head, query-head pair, 128-query tile).
 int prefill_items(int n_layers, int heads, int kv_heads, int n_tokens_padded);
 
+// KV-split exchange over NVLink (k_exchange.cu): one kernel per decode step
+// pushes this rank's partial records into every rank's exchange area and
+// merges the rows once the peers' pushes have arrived.
+constexpr int kMaxExchangeRanks = 8;
+struct ExchangeParams {
+  const float* partial;                 // this rank's records [rows][head_dim + 2]
+  float* out;                           // merged [rows][head_dim]
+  float* base[kMaxExchangeRanks];       // every rank's exchange area (this process's mapping)
+  uint32_t* steps;                      // this rank's per-CTA step counts
+  int* error;
+  int32_t world, rank, rows, head_dim, rows_per_cta, grid;
+};
+size_t exchange_area_bytes(int world, int rows, int head_dim, int grid);
+int exchange_grid(int rows);
+cudaError_t launch_exchange_merge(const ExchangeParams& p, cudaStream_t s);
+
 }  // namespace te

@@ -79,11 +79,15 @@ class KVSplitDecoder:
     partial_fn optional stand-in for the engine: (q, k_new, v_new, q_position) -> partial
                records [n_layers][heads][head_dim + 2] as a torch tensor
     merge_fn   optional stand-in for te_attention_merge_partials: (gathered [world][rows][hd+2]) -> out
+    exchange   "nccl": all-gather the records over the process group, then
+               te_attention_merge_partials; "p2p": one kernel pushes them into
+               the peers' memory over NVLink and merges what arrived
+               (te_attn_exchange_*; needs one GPU per rank, world <= 8)
     """
 
     def __init__(self, spec: ShardSpec, n_layers: int, heads: int, head_dim: int, cache=None, engine=None,
                  group=None, partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None,
-                 device=None):
+                 device=None, exchange: str = "nccl"):
         self.spec = spec
         self.n_layers, self.heads, self.head_dim = n_layers, heads, head_dim
         self.cache, self.engine, self.group = cache, engine, group
@@ -100,6 +104,33 @@ class KVSplitDecoder:
         self._out = torch.empty((n_layers, 1, heads, head_dim), dtype=torch.float32, device=device)
         # the engine's kernels and the collective run on one stream (the engine's)
         self._stream = torch.cuda.ExternalStream(engine.stream) if engine is not None else None
+        self._exchange = None
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange is 'nccl' or 'p2p'")
+        if exchange == "p2p" and spec.world > 1:
+            self._exchange = self._connect_p2p(engine, group, rows, head_dim)
+
+    def _connect_p2p(self, engine, group, rows: int, head_dim: int):
+        import torch
+        import torch.distributed as dist
+        from .runtime import Exchange
+        if engine is None or self.partial_fn is not None or self.merge_fn is not None:
+            raise ValueError("the p2p exchange runs the engine's kernels")
+        if torch.cuda.device_count() < self.spec.world:
+            # the exchange kernel waits for the other ranks: never two ranks on one GPU
+            raise RuntimeError("the p2p exchange needs one GPU per rank")
+        ex = Exchange(engine, self.spec.world, self.spec.rank, rows, head_dim)
+        handles = [None] * self.spec.world
+        dist.all_gather_object(handles, ex.ipc_handle, group=group)
+        ex.connect(handles)
+        dist.barrier(group=group)  # every rank mapped before any rank pushes
+        return ex
+
+    def close(self) -> None:
+        """Frees the p2p exchange; call on every rank after a barrier that follows the last step."""
+        if self._exchange is not None:
+            self._exchange.close()
+            self._exchange = None
 
     def _local_partial(self, q, k_new, v_new, q_pos: int):
         from .runtime import TE_ATTN_ADVANCE, TE_ATTN_PARTIAL
@@ -128,6 +159,10 @@ class KVSplitDecoder:
         import torch.distributed as dist
         q_pos = self.length  # global position of the new token
         self._local_partial(q, k_new, v_new, q_pos)
+        if self._exchange is not None:
+            self._exchange.merge(self._part, self._out)
+            self.length += 1
+            return self._out
         if self.spec.world > 1:
             dist.all_gather_into_tensor(self._gather_flat, self._part, group=self.group)
         else:

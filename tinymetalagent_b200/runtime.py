@@ -114,6 +114,10 @@ SIGNATURES: dict[str, tuple] = {
     "te_kv_append_rope": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _sz, ctypes.c_uint32]),
     "te_attention_decode": (_int, [_vp, _sz, _sz, _u32p, _sz, _i64p, _vp, _vp, _vp, _sz, _vp, ctypes.c_uint32]),
     "te_attention_merge_partials": (_int, [_vp, _vp, _sz, _sz, _sz, _vp, ctypes.c_uint32]),
+    "te_attn_exchange_create": (_int, [_vp, _sz, _sz, _sz, _sz, ctypes.POINTER(_vp), _vp]),
+    "te_attn_exchange_connect": (_int, [_vp, _vp]),
+    "te_attn_exchange_merge": (_int, [_vp, _vp, _vp]),
+    "te_attn_exchange_free": (None, [_vp]),
     "te_attention_prefill": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _vp, _sz, _sz, _vp, ctypes.c_uint32]),
     "te_attention_decode_paged_noalloc": (_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _sz, _sz, _sz, _vp, _vp]),
 }
@@ -256,6 +260,41 @@ class AttnEngine:
 
     def kv_cache(self, **kw) -> "KVCache":
         return KVCache(self, **kw)
+
+
+IPC_HANDLE_BYTES = 64
+
+
+class Exchange:
+    """NVLink exchange + merge of KV-split partial records (te_attn_exchange_*): one
+    per rank, all ranks with the same world, rows and head_dim, each on its own GPU."""
+
+    def __init__(self, engine: "AttnEngine", world: int, rank: int, rows: int, head_dim: int):
+        self.engine = engine
+        self.lib = engine.lib
+        handle = _vp()
+        buf = (ctypes.c_ubyte * IPC_HANDLE_BYTES)()
+        engine.check(self.lib.te_attn_exchange_create(engine.handle, world, rank, rows, head_dim,
+                                                      ctypes.byref(handle), ctypes.addressof(buf)))
+        self.handle = handle
+        self.ipc_handle = bytes(buf)
+        self.world, self.rank = world, rank
+
+    def connect(self, handles: Sequence[bytes]) -> None:
+        """handles: every rank's ipc_handle, in rank order."""
+        blob = b"".join(handles)
+        if len(blob) != self.world * IPC_HANDLE_BYTES:
+            raise ValueError("need one 64-byte handle per rank")
+        buf = (ctypes.c_ubyte * len(blob)).from_buffer_copy(blob)
+        self.engine.check(self.lib.te_attn_exchange_connect(self.handle, ctypes.addressof(buf)))
+
+    def merge(self, partial, out) -> None:
+        self.engine.check(self.lib.te_attn_exchange_merge(self.handle, _addr(partial), _addr(out)))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.te_attn_exchange_free(self.handle)
+            self.handle = None
 
 
 class KVCache:
