@@ -83,6 +83,8 @@ class Port(_Lib):
         L.or_causal_prefill_f32.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, _f32p]
         L.or_decode_partial_f32.argtypes = [_f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, _sz, _f32p]
         L.or_merge_partials_f32.argtypes = [_f32p, _sz, _sz, _sz, _f32p]
+        L.or_matvec_q4_0_f32.argtypes = [ctypes.c_void_p, _sz, _sz, _f32p, _f32p]
+        L.or_matvec_q8_0_f32.argtypes = [ctypes.c_void_p, _sz, _sz, _f32p, _f32p]
         for name in ("or_rope_table", "or_append_rope_f16", "or_causal_prefill_f32",
                      "or_decode_partial_f32", "or_merge_partials_f32"):
             getattr(L, name).restype = ctypes.c_int
@@ -139,6 +141,20 @@ class Port(_Lib):
         assert st == 0
         return out
 
+    def matvec_q4_0_f32(self, w, rows, cols, x):
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(rows, dtype=np.float32)
+        assert self.lib.or_matvec_q4_0_f32(w.ctypes.data, rows, cols, _ptr(x), _ptr(out)) == 0
+        return out
+
+    def matvec_q8_0_f32(self, w, rows, cols, x):
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(rows, dtype=np.float32)
+        assert self.lib.or_matvec_q8_0_f32(w.ctypes.data, rows, cols, _ptr(x), _ptr(out)) == 0
+        return out
+
     def merge_partials_f32(self, partials, heads, head_dim):
         partials = np.ascontiguousarray(partials, dtype=np.float32)
         n_parts = partials.size // (heads * (head_dim + 2))
@@ -153,6 +169,27 @@ class Ref(_Lib):
 
     def __init__(self):
         super().__init__(REF_LIB, "te_")
+        self.lib.ref_stub_model.restype = ctypes.c_void_p
+        self.lib.ref_stub_register_tensor.argtypes = [ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint64,
+                                                     ctypes.c_void_p, ctypes.c_size_t]
+        self.lib.te_model_matvec_f32.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float),
+                                                 ctypes.c_size_t, ctypes.POINTER(ctypes.c_float), ctypes.c_size_t,
+                                                 ctypes.POINTER(ctypes.c_size_t)]
+        self.lib.te_model_matvec_f32.restype = ctypes.c_int
+
+    def model_matvec_f32(self, ggml_type: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+        """te_model_matvec_f32 of the reference on a GGUF-typed matrix given as raw bytes
+        (ggml type 2 = Q4_0, 8 = Q8_0); its Metal path is stubbed out, so this is its CPU row loop."""
+        w = np.ascontiguousarray(w, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(rows, dtype=np.float32)
+        written = ctypes.c_size_t(0)
+        self.lib.ref_stub_register_tensor(ggml_type, cols, rows, w.ctypes.data, w.size)
+        st = self.lib.te_model_matvec_f32(self.lib.ref_stub_model(), b"w", _ptr(x), cols, _ptr(out), rows,
+                                          ctypes.byref(written))
+        self.lib.ref_stub_register_tensor(0, 0, 0, None, 0)
+        assert st == 0 and written.value == rows, st
+        return out
 
 
 _port = None

@@ -17,6 +17,9 @@
  *   or_append_rope_f16      c/src/metal/metal_kernels.metal.inc:2344-2429
  *                           (k/v part of te_qkv_bias_rope_cache_batch_h_f32)
  *   or_causal_prefill_f32   c/src/qwen.c:810-824         (decode call per prompt token)
+ *   or_matvec_q4_0_f32      c/src/ops.c:584-602, 824-845  (te_q4_0_dot_row, scalar path,
+ *                           per row as te_matvec_worker calls it)
+ *   or_matvec_q8_0_f32      c/src/ops.c:604-620, 824-845  (te_q8_0_dot_row, scalar path)
  * Not in the reference (the multi-GPU KV split is new); restated from the
  * (m, l, acc) rescale of c/src/metal/metal_kernels.metal.inc:2650-2681:
  *   or_decode_partial_f32, or_merge_partials_f32
@@ -348,6 +351,56 @@ int or_merge_partials_f32(const float *partials, size_t n_parts, size_t heads, s
         for (size_t d = 0; d < head_dim; ++d) {
             out[h * head_dim + d] = total > 0.0f ? out[h * head_dim + d] / total : 0.0f;
         }
+    }
+    return OR_OK;
+}
+
+/* GGUF Q4_0 / Q8_0 row-major matrices [rows][cols], 32-weight blocks:
+ * Q4_0 block = f16 scale (little-endian) + 16 bytes, byte j holding weight j
+ * in its low nibble and weight j + 16 in its high nibble, both offset by 8;
+ * Q8_0 block = f16 scale + 32 int8.  One sequential fp32 sum per row, in the
+ * reference's element order (c/src/ops.c:584-620). */
+int or_matvec_q4_0_f32(const uint8_t *w, size_t rows, size_t cols, const float *x, float *out) {
+    if (w == NULL || x == NULL || out == NULL || rows == 0u || cols == 0u || (cols % 32u) != 0u) {
+        return OR_INVALID_ARGUMENT;
+    }
+    const size_t blocks = cols / 32u;
+    for (size_t r = 0; r < rows; ++r) {
+        const uint8_t *row = w + r * blocks * 18u;
+        float sum = 0.0f;
+        for (size_t b = 0; b < blocks; ++b) {
+            const uint8_t *src = row + b * 18u;
+            const float scale = or_f16_to_f32((uint16_t)(src[0] | ((uint16_t)src[1] << 8)));
+            const uint8_t *qs = src + 2u;
+            const float *xb = x + b * 32u;
+            for (size_t j = 0; j < 16u; ++j) {
+                sum += (((float)(qs[j] & 0x0fu) - 8.0f) * scale) * xb[j];
+                sum += (((float)(qs[j] >> 4u) - 8.0f) * scale) * xb[j + 16u];
+            }
+        }
+        out[r] = sum;
+    }
+    return OR_OK;
+}
+
+int or_matvec_q8_0_f32(const uint8_t *w, size_t rows, size_t cols, const float *x, float *out) {
+    if (w == NULL || x == NULL || out == NULL || rows == 0u || cols == 0u || (cols % 32u) != 0u) {
+        return OR_INVALID_ARGUMENT;
+    }
+    const size_t blocks = cols / 32u;
+    for (size_t r = 0; r < rows; ++r) {
+        const uint8_t *row = w + r * blocks * 34u;
+        float sum = 0.0f;
+        for (size_t b = 0; b < blocks; ++b) {
+            const uint8_t *src = row + b * 34u;
+            const float scale = or_f16_to_f32((uint16_t)(src[0] | ((uint16_t)src[1] << 8)));
+            const int8_t *qs = (const int8_t *)(src + 2u);
+            const float *xb = x + b * 32u;
+            for (size_t j = 0; j < 32u; ++j) {
+                sum += ((float)qs[j] * scale) * xb[j];
+            }
+        }
+        out[r] = sum;
     }
     return OR_OK;
 }

@@ -55,6 +55,9 @@ int or_decode_partial_f32(const float *query, const float *key_cache, const floa
 int or_merge_partials_f32(const float *partials, size_t n_parts, size_t heads, size_t head_dim,
                           float *out);
 
+int or_matvec_q4_0_f32(const uint8_t *w, size_t rows, size_t cols, const float *x, float *out);
+int or_matvec_q8_0_f32(const uint8_t *w, size_t rows, size_t cols, const float *x, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,6 +20,33 @@ from oracle import oracle as O  # noqa: E402
 THETA = 1e6
 
 
+def quant_matrix(rng, ggml_type: int, rows: int, cols: int) -> np.ndarray:
+    """Random GGUF Q4_0 (type 2: f16 scale + 16 nibble bytes) or Q8_0 (type 8: f16 scale + 32 int8)
+    blocks of 32 weights, row-major [rows][cols / 32 blocks] as raw bytes."""
+    blocks = cols // 32
+    width = 18 if ggml_type == 2 else 34
+    w = np.zeros((rows, blocks, width), np.uint8)
+    scales = (rng.standard_normal((rows, blocks)) * 0.02).astype(np.float16)
+    w[:, :, 0:2] = scales.view(np.uint8).reshape(rows, blocks, 2)
+    w[:, :, 2:] = rng.integers(0, 256, (rows, blocks, width - 2), dtype=np.uint8)
+    return w.reshape(-1)
+
+
+def make_matvec(ref, dst: Path) -> None:
+    """te_model_matvec_f32 of the reference (its CPU row loop) on seeded GGUF matrices."""
+    rng = np.random.default_rng(20261202)
+    g: dict[str, np.ndarray] = {}
+    for i, (ggml_type, rows, cols) in enumerate([(2, 32, 896), (2, 48, 1024), (8, 32, 896), (8, 48, 1024)]):
+        w = quant_matrix(rng, ggml_type, rows, cols)
+        x = rng.standard_normal(cols).astype(np.float32)
+        g[f"mv{i}_meta"] = np.array([ggml_type, rows, cols], np.int64)
+        g[f"mv{i}_w"] = w
+        g[f"mv{i}_x"] = x
+        g[f"mv{i}_out"] = ref.model_matvec_f32(ggml_type, w, rows, cols, x)
+    np.savez_compressed(dst, **g)
+    print("wrote", dst)
+
+
 def main() -> None:
     ref = O.ref()
     rng = np.random.default_rng(20261201)
@@ -82,6 +109,7 @@ def main() -> None:
     dst = Path(__file__).resolve().parent / "golden.npz"
     np.savez_compressed(dst, **g)
     print(f"wrote {dst} ({dst.stat().st_size} bytes, {len(g)} arrays)")
+    make_matvec(ref, Path(__file__).resolve().parent / "golden_matvec.npz")
 
 
 if __name__ == "__main__":

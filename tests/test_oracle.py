@@ -1,6 +1,7 @@
 """The CPU oracle restatement against the reference: KATs, golden vectors and,
 where the reference build exists, the reference's compiled ops.c directly."""
 import math
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -135,3 +136,27 @@ def test_oracle_rejects_like_reference(port):
     assert port.rope_f32(z, 1, 4, 0, 0.0) == 1      # theta <= 0
     with pytest.raises(RuntimeError):
         port.attention_decode_f32(z, z, z, 0, 3, 2, 1)  # heads % kv_heads != 0
+
+
+def test_golden_matvec_bit_exact(port):
+    """The restated Q4_0 / Q8_0 row dot products equal the reference's te_model_matvec_f32
+    (its CPU row loop, c/src/ops.c:216-262 and :584-620) on the committed fixture."""
+    g = dict(np.load(Path(__file__).resolve().parent / "golden" / "golden_matvec.npz"))
+    for i in range(4):
+        ggml_type, rows, cols = (int(v) for v in g[f"mv{i}_meta"])
+        fn = port.matvec_q4_0_f32 if ggml_type == 2 else port.matvec_q8_0_f32
+        assert np.array_equal(fn(g[f"mv{i}_w"], rows, cols, g[f"mv{i}_x"]), g[f"mv{i}_out"])
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference build (oracle/_ref) absent")
+def test_matvec_port_equals_reference_random(port):
+    import sys
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+    from make_golden import quant_matrix
+    ref = O.ref()
+    rng = np.random.default_rng(77)
+    for ggml_type, rows, cols in [(2, 1, 32), (2, 600, 2048), (8, 5, 3584), (8, 520, 512)]:
+        w = quant_matrix(rng, ggml_type, rows, cols)
+        x = rng.standard_normal(cols).astype(np.float32)
+        fn = port.matvec_q4_0_f32 if ggml_type == 2 else port.matvec_q8_0_f32
+        assert np.array_equal(fn(w, rows, cols, x), ref.model_matvec_f32(ggml_type, w, rows, cols, x))
