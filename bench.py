@@ -401,6 +401,11 @@ def run_gpu(args) -> None:
     if not args.no_prefill:
         prefill = run_prefill(eng, stream, tc_peak, peak_src, args, world, rank, local)
 
+    # ---- quantized matrix-vector products (the projections' building block) ----
+    gemv = None
+    if not args.no_gemv:
+        gemv = run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank)
+
     # ---- BASELINE configs 4 (sequence-sharded batch) and 5 (KV split + NCCL merge) ----
     ragged = long = None
     if not args.no_configs:
@@ -436,6 +441,7 @@ def run_gpu(args) -> None:
             "cpu_baseline": cpu,
             "prefill": prefill,
             "decode3b_qkv_bias": qkv_bias,
+            "gemv_gguf": gemv,
             "ragged7b": ragged,
             "long7b": long,
         }
@@ -539,6 +545,62 @@ def _time_steps(stream, fn, steps, world, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     return ms
+
+
+def run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank):
+    """te_matvec_gguf on a 32768 x 8192 GGUF matrix (Q4_0 151 MB, Q8_0 285 MB -- both beyond the
+    126 MB L2, so every call streams the weights from HBM), one fp32 input vector; weight bytes
+    per second against the measured copy peak."""
+    import torch
+    import torch.distributed as dist
+    rows, cols = 32768, 8192
+    res = {"metric": "GGUF matrix-vector weight bandwidth (te_matvec_gguf)", "unit": "GB/s",
+           "shape": f"{rows}x{cols}, 1 vector", "peak": hbm_peak, "peak_source": f"{peak_src} (burst copy)"}
+    g = torch.Generator(device="cuda").manual_seed(77 + rank)
+    x = torch.randn((1, cols), generator=g, device="cuda")
+    y = torch.empty((1, rows), device="cuda")
+    for name, quant, width in (("q4_0", 4, 18), ("q8_0", 8, 34)):
+        with torch.cuda.stream(stream):
+            w = torch.randint(0, 256, (rows, cols // 32, width), generator=g, device="cuda", dtype=torch.uint8)
+            w[:, :, 0:2] = (torch.randn((rows, cols // 32), generator=g, device="cuda") * 0.02).half() \
+                .view(torch.uint8).view(rows, cols // 32, 2)
+        stream.synchronize()
+        calls = 20
+
+        def run():
+            for _ in range(calls):
+                eng.matvec_gguf(quant, w, rows, cols, x, y, 1)
+
+        for _ in range(3):
+            eng.matvec_gguf(quant, w, rows, cols, x, y, 1)
+        ms = _time_steps(stream, run, 1, world, dist)
+        nbytes = w.numel() + x.numel() * 4 + y.numel() * 4
+        gbs = nbytes * calls / (ms / 1e3) / 1e9
+        res[name] = {"value": round(gbs * world, 1), "per_gpu_gbs": round(gbs, 1), "us_per_call": round(ms * 1e3 / calls, 2),
+                     "weight_bytes": int(w.numel()), "frac": round(gbs / hbm_peak, 4)}
+        del w
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import oracle as O
+        if O.ref_available():
+            import numpy as np
+            sys.path.insert(0, str(ROOT / "tests" / "golden"))
+            from make_golden import quant_matrix
+            r_cpu = 8192
+            wq = quant_matrix(np.random.default_rng(5), 2, r_cpu, cols)
+            xc = np.random.default_rng(6).standard_normal(cols).astype(np.float32)
+            ref = O.ref()
+            ref.model_matvec_f32(2, wq, r_cpu, cols, xc)
+            t0 = time.perf_counter()
+            n = 0
+            while time.perf_counter() - t0 < 2.0:
+                ref.model_matvec_f32(2, wq, r_cpu, cols, xc)
+                n += 1
+            dt = time.perf_counter() - t0
+            res["cpu_baseline"] = {"value": round(wq.size * n / dt / 1e9, 3), "unit": "GB/s", "kind": "reference",
+                                   "cores": O.host_cores(),
+                                   "sample": f"{n} calls of te_model_matvec_f32 (Q4_0 {r_cpu}x{cols}, its pthread "
+                                             f"row split) in {dt:.1f} s"}
+    return res
 
 
 def cpu_sample_7b(n: int, budget_s: float):
@@ -746,6 +808,7 @@ def main() -> None:
     ap.add_argument("--no-graph", action="store_true", help="time the decode steps as eager launches")
     ap.add_argument("--prefill-steps", type=int, default=10)
     ap.add_argument("--no-configs", action="store_true", help="skip the config-4 / config-5 measurements")
+    ap.add_argument("--no-gemv", action="store_true", help="skip the GGUF matrix-vector measurement")
     ap.add_argument("--cfg-steps", type=int, default=16, help="decode steps timed for config 4")
     ap.add_argument("--long-steps", type=int, default=128, help="decode steps timed for config 5")
     ap.add_argument("--long-exchange", choices=["nccl", "p2p"], default="nccl",

@@ -195,6 +195,26 @@ TE_API te_status te_attention_merge_partials(te_attn_engine *engine, const float
                                              size_t n_parts, size_t rows, size_t head_dim,
                                              float *out, uint32_t flags);
 
+/* Quantized matrix-vector products ------------------------------------------
+ *
+ * y[v][r] = sum_c W[r][c] * x[v][c] for v < n_vectors (1..8), where W is a
+ * row-major GGUF matrix [rows][cols] of 32-weight blocks -- Q4_0: f16 scale
+ * + 16 bytes of 4-bit quants (weight j in the low nibble of byte j, weight
+ * j+16 in its high nibble, both offset by 8); Q8_0: f16 scale + 32 int8 --
+ * x [n_vectors][cols] and y [n_vectors][rows] fp32.  Device pointers, w and x
+ * 16-byte aligned, cols a multiple of 32; asynchronous on the engine's
+ * stream.  Replaces the quantized row loop of te_model_matvec_f32
+ * (c/src/ops.c:216-262, dot products :584-620) and te_metal_matvec_f32; the
+ * products are the reference's, the sums run in another order (results agree
+ * to fp32 rounding).  quant: TE_ATTN_QUANT_GGUF_Q4_0 or _Q8_0 (the values of
+ * the reference's te_quant_kind, c/include/tinyengine.h:51,55).
+ * TE_STATUS_UNSUPPORTED for rows too long to stage (more than about 200k
+ * Q4_0 or 106k Q8_0 columns). */
+#define TE_ATTN_QUANT_GGUF_Q4_0 4u
+#define TE_ATTN_QUANT_GGUF_Q8_0 8u
+TE_API te_status te_matvec_gguf(te_attn_engine *engine, uint32_t quant, const void *w, size_t rows,
+                                size_t cols, const float *x, size_t n_vectors, float *y);
+
 /* KV-split exchange over NVLink --------------------------------------------
  *
  * For one sequence whose cached tokens are split over `world` GPUs (one

@@ -1,0 +1,109 @@
+"""GPU parity of the GGUF Q4_0 / Q8_0 matrix-vector kernel (te_matvec_gguf).
+
+Reference: te_model_matvec_f32's CPU row loop (c/src/ops.c:216-262, dot
+products :584-620), restated in the oracle (pinned bit-for-bit to the
+reference in tests/test_oracle.py).  The kernel forms the same products and
+sums them in another order, so the bar is fp32 summation error:
+|y - ref| <= 1e-5 * sum_c |w_rc x_c| + 1e-6.
+"""
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+from make_golden import quant_matrix  # noqa: E402
+
+Q4, Q8 = 4, 8          # TE_ATTN_QUANT_GGUF_Q4_0 / _Q8_0
+GGML = {Q4: 2, Q8: 8}  # ggml type ids of the fixture generator
+
+
+def dequant(quant, w, rows, cols):
+    blocks = cols // 32
+    width = 18 if quant == Q4 else 34
+    b = w.reshape(rows, blocks, width)
+    scale = b[:, :, 0:2].copy().view(np.float16).astype(np.float32)[..., 0]
+    if quant == Q4:
+        qs = b[:, :, 2:]
+        q = np.concatenate([(qs & 0x0F), (qs >> 4)], axis=2).astype(np.float32) - 8.0
+    else:
+        q = b[:, :, 2:].view(np.int8).astype(np.float32)
+    return (q * scale[..., None]).reshape(rows, cols)
+
+
+def check(port, quant, w, rows, cols, x, y):
+    ref_fn = port.matvec_q4_0_f32 if quant == Q4 else port.matvec_q8_0_f32
+    wd = np.abs(dequant(quant, w, rows, cols))
+    for v in range(x.shape[0]):
+        ref = ref_fn(w, rows, cols, x[v])
+        bound = 1e-5 * (wd @ np.abs(x[v])) + 1e-6
+        err = np.abs(y[v] - ref)
+        assert (err <= bound).all(), (v, float(err.max()), float((err - bound).max()))
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("quant", [Q4, Q8])
+@pytest.mark.parametrize("shape", [(1, 32, 1), (37, 896, 1), (300, 2048, 3), (4096, 2048, 1), (2048, 11008, 2),
+                                   (5, 3584, 8), (129, 160, 5)])
+def test_matvec_matches_oracle(port, quant, shape):
+    import torch
+    from tinymetalagent_b200 import AttnEngine
+    rows, cols, nv = shape
+    rng = np.random.default_rng(rows * 7 + cols + quant)
+    w = quant_matrix(rng, GGML[quant], rows, cols)
+    x = rng.standard_normal((nv, cols)).astype(np.float32)
+    eng = AttnEngine(0)
+    try:
+        y = torch.full((nv, rows), float("nan"), dtype=torch.float32, device="cuda")
+        eng.matvec_gguf(quant, dev(w), rows, cols, dev(x), y, nv)
+        eng.synchronize()
+        check(port, quant, w, rows, cols, x, y.cpu().numpy())
+    finally:
+        eng.close()
+
+
+def test_matvec_golden_fixture(port):
+    """The committed outputs of the reference's te_model_matvec_f32."""
+    import torch
+    from tinymetalagent_b200 import AttnEngine
+    g = dict(np.load(Path(__file__).resolve().parent / "golden" / "golden_matvec.npz"))
+    eng = AttnEngine(0)
+    try:
+        for i in range(4):
+            ggml_type, rows, cols = (int(v) for v in g[f"mv{i}_meta"])
+            quant = Q4 if ggml_type == 2 else Q8
+            y = torch.zeros((1, rows), dtype=torch.float32, device="cuda")
+            eng.matvec_gguf(quant, dev(g[f"mv{i}_w"]), rows, cols, dev(g[f"mv{i}_x"][None]), y, 1)
+            eng.synchronize()
+            wd = np.abs(dequant(quant, g[f"mv{i}_w"], rows, cols))
+            bound = 1e-5 * (wd @ np.abs(g[f"mv{i}_x"])) + 1e-6
+            assert (np.abs(y.cpu().numpy()[0] - g[f"mv{i}_out"]) <= bound).all()
+    finally:
+        eng.close()
+
+
+def test_matvec_rejects_bad_arguments():
+    import torch
+    from tinymetalagent_b200 import AttnEngine, TinyEngineError
+    eng = AttnEngine(0)
+    try:
+        w = torch.zeros(18 * 4 + 16, dtype=torch.uint8, device="cuda")
+        x = torch.zeros((1, 64), dtype=torch.float32, device="cuda")
+        y = torch.zeros((1, 2), dtype=torch.float32, device="cuda")
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf(Q4, w[2:], 2, 64, x, y)      # w not 16-byte aligned
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf(Q4, w, 2, 48, x, y)          # cols not a multiple of 32
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf(3, w, 2, 64, x, y)           # not Q4_0 / Q8_0
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf(Q4, w, 2, 64, x, y, 9)       # more than 8 vectors
+    finally:
+        eng.close()

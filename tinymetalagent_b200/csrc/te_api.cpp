@@ -890,6 +890,33 @@ TE_API te_status te_attention_merge_partials(te_attn_engine* e, const float* par
   return TE_STATUS_OK;
 }
 
+TE_API te_status te_matvec_gguf(te_attn_engine* e, uint32_t quant, const void* w, size_t rows, size_t cols,
+                                const float* x, size_t n_vectors, float* y) {
+  if (!e || !w || !x || !y || rows == 0 || cols == 0 || cols % 32 != 0 || n_vectors == 0 || n_vectors > 8 ||
+      (quant != TE_ATTN_QUANT_GGUF_Q4_0 && quant != TE_ATTN_QUANT_GGUF_Q8_0)) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15u) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "w and x must be 16-byte aligned");
+  }
+  const int block_bytes = quant == TE_ATTN_QUANT_GGUF_Q4_0 ? 18 : 34;
+  const size_t rb = cols / 32 * block_bytes;
+  if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX || 2 * (rb + 32) > 227 * 1024) {
+    return fail(e, TE_STATUS_UNSUPPORTED, "matrix rows too long to stage");
+  }
+  DeviceGuard dg(e->device);
+  GemvParams p{};
+  p.w = w;
+  p.x = x;
+  p.y = y;
+  p.rows = (int32_t)rows;
+  p.cols = (int32_t)cols;
+  const cudaError_t err = launch_gemv_gguf(p, block_bytes, (int)n_vectors, e->sm_count, e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "matvec kernel launch");
+  e->launches++;
+  return TE_STATUS_OK;
+}
+
 static_assert(sizeof(cudaIpcMemHandle_t) == TE_ATTN_IPC_HANDLE_BYTES, "IPC handle size");
 
 TE_API te_status te_attn_exchange_create(te_attn_engine* e, size_t world, size_t rank, size_t rows, size_t head_dim,

@@ -248,4 +248,16 @@ size_t exchange_area_bytes(int world, int rows, int head_dim, int grid);
 int exchange_grid(int rows);
 cudaError_t launch_exchange_merge(const ExchangeParams& p, cudaStream_t s);
 
+// GGUF Q4_0 / Q8_0 matrix-vector products (k_gemv.cu).
+struct GemvParams {
+  const void* w;            // [rows][cols / 32 blocks], 16-byte aligned base
+  const float* x;           // [n_vectors][cols]
+  float* y;                 // [n_vectors][rows]
+  int32_t rows, cols;
+  int32_t rows_per_group;   // set by the launcher
+  int32_t stage_bytes;      // set by the launcher
+};
+// block_bytes 18 (Q4_0) or 34 (Q8_0); 1 <= n_vectors <= 8.
+cudaError_t launch_gemv_gguf(GemvParams p, int block_bytes, int n_vectors, int sm_count, cudaStream_t s);
+
 }  // namespace te
