@@ -140,10 +140,12 @@ __global__ void __launch_bounds__(kGemvThreads, V <= 2 ? 2 : 1) gemv_gguf_kernel
 
 template <int BLOCK_BYTES, int V>
 cudaError_t launch_v(const GemvParams& p, int grid, int smem, cudaStream_t s) {
+  // the largest staging any accepted shape needs (the host rejects longer rows);
+  // each launch still asks for its own size
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(gemv_gguf_kernel<BLOCK_BYTES, V>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
     configured = true;
   }
