@@ -57,6 +57,7 @@ extern "C" {
 #define TE_ATTN_HOST_BUFFERS  (1u << 4) /* q/k/v/out are host pointers; call is synchronous */
 #define TE_ATTN_QKV_BIAS      (1u << 5) /* add the cache's per-layer q/k/v biases (te_kv_cache_set_qkv_bias)
                                            to the raw inputs first, in fp32, before RoPE and rounding */
+#define TE_ATTN_ACCUMULATE    (1u << 6) /* te_matvec_gguf: y += W x (the residual add of a projection) */
 
 typedef struct te_attn_engine te_attn_engine;
 typedef struct te_kv_cache te_kv_cache;
@@ -207,13 +208,17 @@ TE_API te_status te_attention_merge_partials(te_attn_engine *engine, const float
  * (c/src/ops.c:216-262, dot products :584-620) and te_metal_matvec_f32; the
  * products are the reference's, the sums run in another order (results agree
  * to fp32 rounding).  quant: TE_ATTN_QUANT_GGUF_Q4_0 or _Q8_0 (the values of
- * the reference's te_quant_kind, c/include/tinyengine.h:51,55).
+ * the reference's te_quant_kind, c/include/tinyengine.h:51,55).  With
+ * TE_ATTN_ACCUMULATE each finished dot product is added to y in fp32 (y is
+ * read first): the output projection and its residual add in one pass, as
+ * c/src/qwen.c:1072-1079 does with te_qwen_matvec_exact then te_add_f32 (and
+ * the MLP down projection at :1105-1108).
  * TE_STATUS_UNSUPPORTED for rows too long to stage (more than about 200k
  * Q4_0 or 106k Q8_0 columns). */
 #define TE_ATTN_QUANT_GGUF_Q4_0 4u
 #define TE_ATTN_QUANT_GGUF_Q8_0 8u
 TE_API te_status te_matvec_gguf(te_attn_engine *engine, uint32_t quant, const void *w, size_t rows,
-                                size_t cols, const float *x, size_t n_vectors, float *y);
+                                size_t cols, const float *x, size_t n_vectors, float *y, uint32_t flags);
 
 /* KV-split exchange over NVLink --------------------------------------------
  *

@@ -105,5 +105,34 @@ def test_matvec_rejects_bad_arguments():
             eng.matvec_gguf(3, w, 2, 64, x, y)           # not Q4_0 / Q8_0
         with pytest.raises(TinyEngineError):
             eng.matvec_gguf(Q4, w, 2, 64, x, y, 9)       # more than 8 vectors
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf(Q4, w, 2, 64, x, y, 1, 1 << 3)  # a flag other than TE_ATTN_ACCUMULATE
+    finally:
+        eng.close()
+
+
+@pytest.mark.parametrize("quant", [Q4, Q8])
+def test_matvec_residual_accumulate(port, quant):
+    """Output projection + residual (c/src/qwen.c:1072-1079): y = residual + (W x), the add in fp32
+    after the dot product."""
+    import torch
+    from tinymetalagent_b200 import TE_ATTN_ACCUMULATE, AttnEngine
+    rows, cols, nv = 2048, 2048, 2
+    rng = np.random.default_rng(99 + quant)
+    w = quant_matrix(rng, GGML[quant], rows, cols)
+    x = rng.standard_normal((nv, cols)).astype(np.float32)
+    res = rng.standard_normal((nv, rows)).astype(np.float32)
+    eng = AttnEngine(0)
+    try:
+        y = dev(res)
+        eng.matvec_gguf(quant, dev(w), rows, cols, dev(x), y, nv, TE_ATTN_ACCUMULATE)
+        eng.synchronize()
+        got = y.cpu().numpy()
+        ref_fn = port.matvec_q4_0_f32 if quant == Q4 else port.matvec_q8_0_f32
+        wd = np.abs(dequant(quant, w, rows, cols))
+        for v in range(nv):
+            exp = (res[v] + ref_fn(w, rows, cols, x[v])).astype(np.float32)
+            bound = 1e-5 * (wd @ np.abs(x[v])) + 1e-6 + 1e-7 * np.abs(exp)
+            assert (np.abs(got[v] - exp) <= bound).all()
     finally:
         eng.close()

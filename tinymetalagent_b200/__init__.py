@@ -5,6 +5,7 @@ The product is ``libtinyengine.so`` (built from ``csrc/``) behind the C ABI in
 its ctypes binding and the multi-GPU host orchestration.
 """
 from .runtime import (  # noqa: F401
+    TE_ATTN_ACCUMULATE,
     TE_ATTN_ADVANCE,
     TE_ATTN_HOST_BUFFERS,
     TE_ATTN_INPUT_F16,

@@ -131,7 +131,10 @@ __global__ void __launch_bounds__(kGemvThreads, V <= 2 ? 2 : 1) gemv_gguf_kernel
         float s = acc[v];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) p.y[(size_t)v * p.rows + row] = s;
+        if (lane == 0) {
+          float* yp = p.y + (size_t)v * p.rows + row;
+          *yp = p.accumulate ? __fadd_rn(*yp, s) : s;  // the residual add after the projection
+        }
       }
     }
     __syncthreads();  // the stage is rewritten by the copy issued two groups later

@@ -891,9 +891,9 @@ TE_API te_status te_attention_merge_partials(te_attn_engine* e, const float* par
 }
 
 TE_API te_status te_matvec_gguf(te_attn_engine* e, uint32_t quant, const void* w, size_t rows, size_t cols,
-                                const float* x, size_t n_vectors, float* y) {
+                                const float* x, size_t n_vectors, float* y, uint32_t flags) {
   if (!e || !w || !x || !y || rows == 0 || cols == 0 || cols % 32 != 0 || n_vectors == 0 || n_vectors > 8 ||
-      (quant != TE_ATTN_QUANT_GGUF_Q4_0 && quant != TE_ATTN_QUANT_GGUF_Q8_0)) {
+      (quant != TE_ATTN_QUANT_GGUF_Q4_0 && quant != TE_ATTN_QUANT_GGUF_Q8_0) || (flags & ~TE_ATTN_ACCUMULATE)) {
     return TE_STATUS_INVALID_ARGUMENT;
   }
   if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15u) {
@@ -911,6 +911,7 @@ TE_API te_status te_matvec_gguf(te_attn_engine* e, uint32_t quant, const void* w
   p.y = y;
   p.rows = (int32_t)rows;
   p.cols = (int32_t)cols;
+  p.accumulate = (flags & TE_ATTN_ACCUMULATE) ? 1 : 0;
   const cudaError_t err = launch_gemv_gguf(p, block_bytes, (int)n_vectors, e->sm_count, e->stream);
   if (err != cudaSuccess) return cuda_fail(e, err, "matvec kernel launch");
   e->launches++;
