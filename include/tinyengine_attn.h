@@ -213,8 +213,9 @@ TE_API te_status te_attention_merge_partials(te_attn_engine *engine, const float
  * read first): the output projection and its residual add in one pass, as
  * c/src/qwen.c:1072-1079 does with te_qwen_matvec_exact then te_add_f32 (and
  * the MLP down projection at :1105-1108).
- * TE_STATUS_UNSUPPORTED for rows too long to stage (more than about 200k
- * Q4_0 or 106k Q8_0 columns). */
+ * TE_STATUS_UNSUPPORTED for rows too long to stage (more than about 205k
+ * Q4_0 or 108k Q8_0 columns).  A staging wait that runs out (2 s) sets the
+ * engine's error word. */
 #define TE_ATTN_QUANT_GGUF_Q4_0 4u
 #define TE_ATTN_QUANT_GGUF_Q8_0 8u
 TE_API te_status te_matvec_gguf(te_attn_engine *engine, uint32_t quant, const void *w, size_t rows,

@@ -51,7 +51,10 @@ def dev(a):
 
 @pytest.mark.parametrize("quant", [Q4, Q8])
 @pytest.mark.parametrize("shape", [(1, 32, 1), (37, 896, 1), (300, 2048, 3), (4096, 2048, 1), (2048, 11008, 2),
-                                   (5, 3584, 8), (129, 160, 5)])
+                                   (5, 3584, 8), (129, 160, 5),
+                                   # long rows: fewer rows per staged group, and (99 968 columns of
+                                   # Q8_0) stages so large that one CTA per SM holds them
+                                   (40, 29568, 3), (4, 99968, 1)])
 def test_matvec_matches_oracle(port, quant, shape):
     import torch
     from tinymetalagent_b200 import AttnEngine
@@ -107,6 +110,8 @@ def test_matvec_rejects_bad_arguments():
             eng.matvec_gguf(Q4, w, 2, 64, x, y, 9)       # more than 8 vectors
         with pytest.raises(TinyEngineError):
             eng.matvec_gguf(Q4, w, 2, 64, x, y, 1, 1 << 3)  # a flag other than TE_ATTN_ACCUMULATE
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf(Q8, w, 2, 110016, x, y)      # a row too long for two shared-memory stages
     finally:
         eng.close()
 

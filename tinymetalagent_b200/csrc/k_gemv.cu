@@ -9,15 +9,22 @@
 // weight = quant * scale.  The Metal version is te_metal_matvec_f32
 // (c/src/metal/metal_kernels.metal.inc:75-1927).  Here the products are the
 // reference's ((q - 8) * scale) * x in fp32; the sums run in another order
-// (per-lane partial sums, then a warp tree), so results agree to fp32
-// rounding, not bit for bit.
+// (per-lane partial sums, a warp tree, then the 8 warps in order), so results
+// agree to fp32 rounding, not bit for bit.
 //
-// A CTA takes groups of whole rows, a contiguous byte range of W, and copies
-// each group into shared memory with 16-byte asynchronous copies (two stages,
-// the next group in flight while the current one is reduced); the ragged
-// ends of a range (row starts are only 2-byte aligned: 18- and 34-byte
-// blocks) are fetched with 2-byte loads.  Warps then take rows, lanes take
-// blocks, and a warp reduction produces y[v][row] for up to 8 input vectors.
+// A persistent CTA walks groups of up to R whole rows (a contiguous byte range
+// of W).  One thread stages each group into shared memory with a single bulk
+// copy (cp.async.bulk, completion on the stage's mbarrier), keeping the next
+// stages - 1 groups in flight in a ring; the copy is widened to 16-byte
+// boundaries (rows start only 2-byte aligned: 18- and 34-byte blocks), and the
+// few bytes past the matrix's last 16-byte boundary are read with plain loads.
+// The 8 warps split the columns: a warp step covers 8 blocks (256 weights),
+// lane l taking block l / 4 and 8 of its weights (4 or 8 quant bytes), and
+// warp w takes steps w, w + 8, ... of every row of the group, so each input
+// value a lane loads serves all R rows.  Quant codes become exact floats
+// through the 2^23 bit pattern (one byte permute per weight), scales and
+// products run two per f32x2 instruction, and each warp's per-row sums meet
+// in shared memory, where y[v][row] is formed.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -28,159 +35,263 @@ namespace te {
 namespace {
 
 constexpr int kGemvThreads = 256;
-constexpr int kGemvStageBytes = 24 * 1024;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvMaxStages = 4;
+constexpr int kGemvHeader = 64;                          // the stages' mbarriers
+constexpr int kGemvPartialFloats = 2 * kGemvWarps * 16;  // [2 parities][warps][R * V <= 16]
+constexpr int kGemvStageOffset = kGemvHeader + kGemvPartialFloats * 4;
+static_assert(kGemvStageOffset % 16 == 0, "bulk copies land on 16-byte boundaries");
 
-template <int BLOCK_BYTES, int V>
-__global__ void __launch_bounds__(kGemvThreads, V <= 2 ? 2 : 1) gemv_gguf_kernel(const GemvParams p) {
-  extern __shared__ __align__(16) unsigned char gsm[];
-  const int rb = (p.cols / 32) * BLOCK_BYTES;  // bytes per row
-  const int rows_per_group = p.rows_per_group;
-  const int n_groups = (p.rows + rows_per_group - 1) / rows_per_group;
-  const int stage_bytes = p.stage_bytes;
-  const unsigned char* w = static_cast<const unsigned char*>(p.w);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// rows per group for V input vectors: R * V <= 16 accumulator pairs per lane
+__host__ __device__ constexpr int gemv_rows(int v) { return v <= 2 ? 8 : (v <= 4 ? 4 : 2); }
 
-  // group g covers bytes [lo, hi) of W; its copy starts at lo rounded down to 16
-  auto span = [&](int g, long long& lo16, long long& hi) {
-    const long long r0 = (long long)g * rows_per_group;
-    const long long r1 = min((long long)p.rows, r0 + rows_per_group);
-    lo16 = (r0 * rb) & ~15ll;
-    hi = r1 * rb;
-  };
-  auto issue = [&](int g, int stage) {
-    long long lo16, hi;
-    span(g, lo16, hi);
-    unsigned char* dst = gsm + stage * stage_bytes;
-    const long long hi16 = hi & ~15ll;
-    const int n16 = (int)((hi16 - lo16) >> 4);
-    for (int i = threadIdx.x; i < n16; i += blockDim.x) {
-      cp_async_cg16(smem_u32(dst + i * 16), w + lo16 + (long long)i * 16);
-    }
-    // tail: [max(hi16, lo16), hi) in 2-byte words (row ranges and offsets are even)
-    const long long t0 = hi16 > lo16 ? hi16 : lo16;
-    const int nt = (int)((hi - t0) >> 1);
-    for (int i = threadIdx.x; i < nt; i += blockDim.x) {
-      *reinterpret_cast<uint16_t*>(dst + (t0 - lo16) + 2 * i) =
-          __ldg(reinterpret_cast<const uint16_t*>(w + t0) + i);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-
-  int g = blockIdx.x;
-  if (g < n_groups) issue(g, 0);
-  for (int it = 0; g < n_groups; g += gridDim.x, ++it) {
-    const int stage = it & 1;
-    const int gn = g + gridDim.x;
-    if (gn < n_groups) {
-      issue(gn, stage ^ 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");  // this group's copies have landed
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
-    __syncthreads();
-    long long lo16, hi;
-    span(g, lo16, hi);
-    const unsigned char* base = gsm + stage * stage_bytes;
-    const int r0 = g * rows_per_group;
-    const int r1 = min(p.rows, r0 + rows_per_group);
-    for (int row = r0 + warp; row < r1; row += kGemvThreads / 32) {
-      const unsigned char* rp = base + ((long long)row * rb - lo16);
-      float acc[V];
+// One group's dot products, accumulated per lane: a warp step covers 8
+// blocks (256 weights) and lane l takes block l / 4 of it and 8 of its
+// weights -- Q4_0: quant bytes 4 (l % 4) .. +3, i.e. weights 4 (l % 4) .. +3
+// (low nibbles) and 16 + 4 (l % 4) .. +3 (high nibbles); Q8_0: weights
+// 8 (l % 4) .. +7 -- for every row of the group (FULL: all R rows present, no
+// per-row guard).  A lane past the row's end (cols / 32 not a multiple of 8)
+// reads the row's last block with scale 0 and input 0.
+template <int BLOCK_BYTES, int V, int R, bool FULL>
+__device__ __forceinline__ void gemv_pass(const unsigned char* base, int rb, int nb, int nr, const float* x, int cols,
+                                          int warp, int lane, uint64_t (&acc)[R][V]) {
+  constexpr float kOff = BLOCK_BYTES == 18 ? 8388616.0f : 8388736.0f;  // 2^23 + the quant offset (8 or 128)
+  const uint64_t off2 = f2_pack(kOff, kOff);
+  const int j = lane & 3;
+  const int xo0 = BLOCK_BYTES == 18 ? 4 * j : 8 * j;       // input offsets of the lane's two weight quads
+  const int xo1 = BLOCK_BYTES == 18 ? 16 + 4 * j : 8 * j + 4;
+  const int qo = BLOCK_BYTES == 18 ? 2 + 4 * j : 2 + 8 * j;  // the lane's quant bytes within a block
+  for (int b0 = 8 * warp; b0 < nb; b0 += 8 * kGemvWarps) {
+    const int b = b0 + (lane >> 2);
+    const bool in = b < nb;
+    const int bc = in ? b : nb - 1;
+    uint64_t xs[V][4];
 #pragma unroll
-      for (int v = 0; v < V; ++v) acc[v] = 0.f;
-      for (int b = lane; b < p.cols / 32; b += 32) {
-        const unsigned char* blk = rp + b * BLOCK_BYTES;
-        const float scale = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
-        constexpr int kWords = (BLOCK_BYTES - 2) / 2;  // 2-byte words of quants: 8 (Q4_0) or 16 (Q8_0)
-        uint32_t qw[kWords];
-#pragma unroll
-        for (int j = 0; j < kWords; ++j) qw[j] = *reinterpret_cast<const uint16_t*>(blk + 2 + 2 * j);
-        // weights 16h .. 16h+15 (Q4_0: low nibbles of the 16 bytes, then high
-        // nibbles; Q8_0: bytes 16h .. 16h+15)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float wq[16];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            if (BLOCK_BYTES == 18) {
-              const uint32_t q0 = qw[j] & 0xffu, q1 = qw[j] >> 8;
-              wq[2 * j] = ((float)(h ? q0 >> 4 : q0 & 0x0fu) - 8.0f) * scale;
-              wq[2 * j + 1] = ((float)(h ? q1 >> 4 : q1 & 0x0fu) - 8.0f) * scale;
-            } else {
-              const uint32_t two = qw[8 * h + j];
-              wq[2 * j] = (float)(int8_t)(two & 0xffu) * scale;
-              wq[2 * j + 1] = (float)(int8_t)(two >> 8) * scale;
-            }
-          }
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            const float4* xv = reinterpret_cast<const float4*>(p.x + (size_t)v * p.cols + (size_t)b * 32 + 16 * h);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float4 xx = __ldg(xv + k);
-              acc[v] = fmaf(wq[4 * k], xx.x, acc[v]);
-              acc[v] = fmaf(wq[4 * k + 1], xx.y, acc[v]);
-              acc[v] = fmaf(wq[4 * k + 2], xx.z, acc[v]);
-              acc[v] = fmaf(wq[4 * k + 3], xx.w, acc[v]);
-            }
-          }
-        }
+    for (int v = 0; v < V; ++v) {
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
+      if (in) {
+        const float* xr = x + (size_t)v * cols + (size_t)b * 32;
+        a = __ldg(reinterpret_cast<const float4*>(xr + xo0));
+        c = __ldg(reinterpret_cast<const float4*>(xr + xo1));
       }
+      xs[v][0] = f2_pack(a.x, a.y);
+      xs[v][1] = f2_pack(a.z, a.w);
+      xs[v][2] = f2_pack(c.x, c.y);
+      xs[v][3] = f2_pack(c.z, c.w);
+    }
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        float s = acc[v];
+    for (int r = 0; r < R; ++r) {
+      if (FULL || r < nr) {
+        const unsigned char* blk = base + r * rb + bc * BLOCK_BYTES;
+        float sc = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
+        sc = in ? sc : 0.f;
+        const uint16_t* qp = reinterpret_cast<const uint16_t*>(blk + qo);
+        uint32_t lo, hi;  // the lane's 8 codes, one per byte (Q8_0: int8 + 128)
+        if (BLOCK_BYTES == 18) {
+          const uint32_t q = prmt(qp[0], qp[1], 0x5410u);
+          lo = q & 0x0f0f0f0fu;
+          hi = (q >> 4) & 0x0f0f0f0fu;
+        } else {
+          lo = prmt(qp[0], qp[1], 0x5410u) ^ 0x80808080u;
+          hi = prmt(qp[2], qp[3], 0x5410u) ^ 0x80808080u;
+        }
+        // code byte i under the exponent bits of 2^23: the float 2^23 + code,
+        // exact; minus the offset, times the scale, both exact in fp32
+        const uint64_t s2 = f2_pack(sc, sc);
+        uint64_t wq[4];
+        wq[0] = f2_pack(__uint_as_float(prmt(lo, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(lo, 0x4B000000u, 0x7441u)));
+        wq[1] = f2_pack(__uint_as_float(prmt(lo, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(lo, 0x4B000000u, 0x7443u)));
+        wq[2] = f2_pack(__uint_as_float(prmt(hi, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(hi, 0x4B000000u, 0x7441u)));
+        wq[3] = f2_pack(__uint_as_float(prmt(hi, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(hi, 0x4B000000u, 0x7443u)));
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) {
-          float* yp = p.y + (size_t)v * p.rows + row;
-          *yp = p.accumulate ? __fadd_rn(*yp, s) : s;  // the residual add after the projection
+        for (int k = 0; k < 4; ++k) wq[k] = f2_mul(f2_sub(wq[k], off2), s2);
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) acc[r][v] = f2_fma(wq[k], xs[v][k], acc[r][v]);
         }
       }
     }
-    __syncthreads();  // the stage is rewritten by the copy issued two groups later
   }
 }
 
 template <int BLOCK_BYTES, int V>
-cudaError_t launch_v(const GemvParams& p, int grid, int smem, cudaStream_t s) {
-  // the largest staging any accepted shape needs (the host rejects longer rows);
-  // each launch still asks for its own size
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_gguf_kernel(const GemvParams p) {
+  constexpr int R = gemv_rows(V);
+  extern __shared__ __align__(128) unsigned char gsm[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
+  float* partial = reinterpret_cast<float*>(gsm + kGemvHeader);
+  unsigned char* stages = gsm + kGemvStageOffset;
+  __shared__ int s_abort;
+
+  const int nb = p.cols / 32;
+  const long long rb = (long long)nb * BLOCK_BYTES;  // bytes per row
+  const long long total = (long long)p.rows * rb;
+  const long long total16 = total & ~15ll;
+  const int rows_per_group = p.rows_per_group;
+  const int n_groups = (p.rows + rows_per_group - 1) / rows_per_group;
+  const int n_stages = p.stages;
+  const unsigned char* w = static_cast<const unsigned char*>(p.w);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < n_stages; ++s) mbar_init(&full[s], 1);
+    fence_mbarrier_init();
+    s_abort = 0;
+  }
+  __syncthreads();
+
+  // one thread: stage group g; the copy covers [lo rounded down to 16, hi
+  // rounded up to 16) clipped to the matrix's last 16-byte boundary, and the
+  // bytes past that boundary (last group only) arrive by plain loads before
+  // the mbarrier arrival that publishes them
+  auto issue = [&](int g, int stage) {
+    const long long lo = (long long)g * rows_per_group * rb;
+    const long long hi = min((long long)p.rows, (long long)(g + 1) * rows_per_group) * rb;
+    const long long lo16 = lo & ~15ll;
+    const long long hi16 = min((hi + 15) & ~15ll, total16);
+    unsigned char* dst = stages + (size_t)stage * p.stage_bytes;
+    for (long long t = hi16 > lo16 ? hi16 : lo16; t < hi; t += 2) {
+      *reinterpret_cast<uint16_t*>(dst + (t - lo16)) = __ldg(reinterpret_cast<const uint16_t*>(w + t));
+    }
+    if (hi16 > lo16) {
+      mbar_arrive_expect_tx(&full[stage], (uint32_t)(hi16 - lo16));
+      bulk_load(dst, w + lo16, (uint32_t)(hi16 - lo16), &full[stage]);
+    } else {
+      mbar_arrive(&full[stage]);
+    }
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s + 1 < n_stages; ++s) {
+      const int g = blockIdx.x + s * gridDim.x;
+      if (g < n_groups) issue(g, s);
+    }
+  }
+
+  int it = 0;
+  for (int g = blockIdx.x; g < n_groups; g += gridDim.x, ++it) {
+    // the stage of iteration it - 1 was released by the barrier that ended it
+    if (threadIdx.x == 0) {
+      const int gi = g + (n_stages - 1) * gridDim.x;
+      if (gi < n_groups) issue(gi, (it + n_stages - 1) % n_stages);
+    }
+    const int stage = it % n_stages;
+    if (!mbar_wait(&full[stage], (uint32_t)(it / n_stages) & 1u)) {
+      set_error(p.error, 50);
+      s_abort = 1;  // every thread leaves after this iteration's barrier
+    }
+    const int r0 = g * rows_per_group;
+    const int nr = min(p.rows - r0, rows_per_group);
+    const long long lo16 = ((long long)r0 * rb) & ~15ll;
+    const unsigned char* base = stages + (size_t)stage * p.stage_bytes + (int)((long long)r0 * rb - lo16);
+
+    uint64_t acc[R][V];  // f32x2 partial sums
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+#pragma unroll
+      for (int v = 0; v < V; ++v) acc[r][v] = 0ull;
+    }
+    if (nr == R) {
+      gemv_pass<BLOCK_BYTES, V, R, true>(base, (int)rb, nb, nr, p.x, p.cols, warp, lane, acc);
+    } else {
+      gemv_pass<BLOCK_BYTES, V, R, false>(base, (int)rb, nb, nr, p.x, p.cols, warp, lane, acc);
+    }
+    float* part = partial + (it & 1) * (kGemvWarps * 16);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (r < nr) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          float a0, a1;
+          f2_unpack(acc[r][v], a0, a1);
+          float s = a0 + a1;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+          if (lane == 0) part[(warp * R + r) * V + v] = s;
+        }
+      }
+    }
+    __syncthreads();  // partial sums complete; this iteration's stage is free again
+    if (threadIdx.x < nr * V) {
+      const int r = threadIdx.x / V, v = threadIdx.x % V;
+      float s = part[r * V + v];
+#pragma unroll
+      for (int k = 1; k < kGemvWarps; ++k) s += part[(k * R + r) * V + v];
+      float* yp = p.y + (size_t)v * p.rows + r0 + r;
+      *yp = p.accumulate ? __fadd_rn(*yp, s) : s;  // the residual add after the projection
+    }
+    if (s_abort) {  // read after the barrier: the same decision in every thread
+      // before leaving, let the copies this CTA still has in flight land (bounded)
+      if (threadIdx.x == 0) {
+        for (int j = it; j < it + n_stages; ++j) {
+          if (blockIdx.x + j * gridDim.x < n_groups) mbar_wait(&full[j % n_stages], (uint32_t)(j / n_stages) & 1u);
+        }
+      }
+      break;
+    }
+  }
+}
+
+template <int BLOCK_BYTES, int V>
+cudaError_t launch_v(const GemvParams& p, int ctas_per_sm, int sm_count, int smem, cudaStream_t s) {
+  // the largest staging any accepted shape needs (the host rejects longer
+  // rows); each launch still asks for its own size
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(gemv_gguf_kernel<BLOCK_BYTES, V>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 128);
     if (e != cudaSuccess) return e;
     configured = true;
   }
+  const int n_groups = (p.rows + p.rows_per_group - 1) / p.rows_per_group;
+  const int slots = ctas_per_sm * sm_count;
+  const int grid = n_groups < slots ? n_groups : slots;
   gemv_gguf_kernel<BLOCK_BYTES, V><<<grid, kGemvThreads, smem, s>>>(p);
   return cudaGetLastError();
 }
 
 template <int BLOCK_BYTES>
-cudaError_t launch_b(const GemvParams& p, int n_vectors, int grid, int smem, cudaStream_t s) {
+cudaError_t launch_b(const GemvParams& p, int n_vectors, int ctas_per_sm, int sm_count, int smem, cudaStream_t s) {
   switch (n_vectors) {
-    case 1: return launch_v<BLOCK_BYTES, 1>(p, grid, smem, s);
-    case 2: return launch_v<BLOCK_BYTES, 2>(p, grid, smem, s);
-    case 3: return launch_v<BLOCK_BYTES, 3>(p, grid, smem, s);
-    case 4: return launch_v<BLOCK_BYTES, 4>(p, grid, smem, s);
-    case 5: return launch_v<BLOCK_BYTES, 5>(p, grid, smem, s);
-    case 6: return launch_v<BLOCK_BYTES, 6>(p, grid, smem, s);
-    case 7: return launch_v<BLOCK_BYTES, 7>(p, grid, smem, s);
-    default: return launch_v<BLOCK_BYTES, 8>(p, grid, smem, s);
+    case 1: return launch_v<BLOCK_BYTES, 1>(p, ctas_per_sm, sm_count, smem, s);
+    case 2: return launch_v<BLOCK_BYTES, 2>(p, ctas_per_sm, sm_count, smem, s);
+    case 3: return launch_v<BLOCK_BYTES, 3>(p, ctas_per_sm, sm_count, smem, s);
+    case 4: return launch_v<BLOCK_BYTES, 4>(p, ctas_per_sm, sm_count, smem, s);
+    case 5: return launch_v<BLOCK_BYTES, 5>(p, ctas_per_sm, sm_count, smem, s);
+    case 6: return launch_v<BLOCK_BYTES, 6>(p, ctas_per_sm, sm_count, smem, s);
+    case 7: return launch_v<BLOCK_BYTES, 7>(p, ctas_per_sm, sm_count, smem, s);
+    default: return launch_v<BLOCK_BYTES, 8>(p, ctas_per_sm, sm_count, smem, s);
   }
 }
 
 }  // namespace
 
 cudaError_t launch_gemv_gguf(GemvParams p, int block_bytes, int n_vectors, int sm_count, cudaStream_t s) {
-  const int rb = (p.cols / 32) * block_bytes;
-  p.rows_per_group = rb >= kGemvStageBytes ? 1 : kGemvStageBytes / rb;
-  if (p.rows_per_group > p.rows) p.rows_per_group = p.rows;
-  p.stage_bytes = (p.rows_per_group * rb + 15 + 16) & ~15;  // the copy starts up to 14 bytes early
-  const int smem = 2 * p.stage_bytes;
-  const int n_groups = (p.rows + p.rows_per_group - 1) / p.rows_per_group;
-  const int grid = n_groups < 2 * sm_count ? n_groups : 2 * sm_count;
-  return block_bytes == 18 ? launch_b<18>(p, n_vectors, grid, smem, s) : launch_b<34>(p, n_vectors, grid, smem, s);
+  const long long rb = (long long)(p.cols / 32) * block_bytes;
+  // R rows per group (the kernel's compile-time count, no per-row guards),
+  // fewer only when two stages of R rows would not fit one CTA; a stage holds
+  // the group widened to 16-byte boundaries at both ends
+  int rpg = gemv_rows(n_vectors);
+  while (rpg > 1 && 2 * ((rpg * rb + 45) & ~15ll) + kGemvStageOffset + 128 > 227 * 1024) --rpg;
+  if (rpg > p.rows) rpg = p.rows;
+  p.rows_per_group = rpg;
+  p.stage_bytes = (int)((rpg * rb + 30 + 15) & ~15ll);
+  // as many stages (2 to 4) as fit two CTAs per SM (2 x 112 KiB of the SM's
+  // 228, with the static word and the per-CTA reserve), else one CTA per SM
+  // with up to 227 KiB
+  const int per_two = (112 * 1024 - kGemvStageOffset) / p.stage_bytes;
+  int ctas_per_sm = 2;
+  int stages = per_two < kGemvMaxStages ? per_two : kGemvMaxStages;
+  if (stages < 2) {
+    ctas_per_sm = 1;
+    const int per_one = (227 * 1024 - 128 - kGemvStageOffset) / p.stage_bytes;
+    stages = per_one < kGemvMaxStages ? per_one : kGemvMaxStages;
+  }
+  p.stages = stages;
+  const int smem = kGemvStageOffset + stages * p.stage_bytes;
+  return block_bytes == 18 ? launch_b<18>(p, n_vectors, ctas_per_sm, sm_count, smem, s)
+                           : launch_b<34>(p, n_vectors, ctas_per_sm, sm_count, smem, s);
 }
 
 }  // namespace te

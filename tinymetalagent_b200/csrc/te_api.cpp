@@ -901,7 +901,7 @@ TE_API te_status te_matvec_gguf(te_attn_engine* e, uint32_t quant, const void* w
   }
   const int block_bytes = quant == TE_ATTN_QUANT_GGUF_Q4_0 ? 18 : 34;
   const size_t rb = cols / 32 * block_bytes;
-  if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX || 2 * (rb + 32) > 227 * 1024) {
+  if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX || 2 * (rb + 48) + 1280 > 227 * 1024) {  // two stages of one row
     return fail(e, TE_STATUS_UNSUPPORTED, "matrix rows too long to stage");
   }
   DeviceGuard dg(e->device);
@@ -912,6 +912,7 @@ TE_API te_status te_matvec_gguf(te_attn_engine* e, uint32_t quant, const void* w
   p.rows = (int32_t)rows;
   p.cols = (int32_t)cols;
   p.accumulate = (flags & TE_ATTN_ACCUMULATE) ? 1 : 0;
+  p.error = e->d_error;
   const cudaError_t err = launch_gemv_gguf(p, block_bytes, (int)n_vectors, e->sm_count, e->stream);
   if (err != cudaSuccess) return cuda_fail(e, err, "matvec kernel launch");
   e->launches++;
