@@ -7,10 +7,11 @@
 // quants -- Q4_0: 16 bytes, byte j holding weight j in its low nibble and
 // weight j+16 in its high nibble, both offset by 8; Q8_0: 32 int8 -- and
 // weight = quant * scale.  The Metal version is te_metal_matvec_f32
-// (c/src/metal/metal_kernels.metal.inc:75-1927).  Here the products are the
-// reference's ((q - 8) * scale) * x in fp32; the sums run in another order
-// (per-lane partial sums, a warp tree, then the 8 warps in order), so results
-// agree to fp32 rounding, not bit for bit.
+// (c/src/metal/metal_kernels.metal.inc:75-1927).  Here the weights are the
+// same exact values, but the scale multiplies partial sums of 8 weights
+// (scale * sum (q - 8) * x) and the sums run in another order (per lane, a
+// warp tree, then the 8 warps in order), so results agree to fp32 rounding,
+// not bit for bit.
 //
 // A persistent CTA walks groups of up to R whole rows (a contiguous byte range
 // of W).  One thread stages each group into shared memory with a single bulk
@@ -22,7 +23,7 @@
 // lane l taking block l / 4 and 8 of its weights (4 or 8 quant bytes), and
 // warp w takes steps w, w + 8, ... of every row of the group, so each input
 // value a lane loads serves all R rows.  Quant codes become exact floats
-// through the 2^23 bit pattern (one byte permute per weight), scales and
+// through the 2^23 bit pattern (one byte permute per weight), offsets and
 // products run two per f32x2 instruction, and each warp's per-row sums meet
 // in shared memory, where y[v][row] is formed.
 #include <cuda_fp16.h>
@@ -42,82 +43,101 @@ constexpr int kGemvPartialFloats = 2 * kGemvWarps * 16;  // [2 parities][warps][
 constexpr int kGemvStageOffset = kGemvHeader + kGemvPartialFloats * 4;
 static_assert(kGemvStageOffset % 16 == 0, "bulk copies land on 16-byte boundaries");
 
-// rows per group for V input vectors: R * V <= 16 accumulator pairs per lane
-__host__ __device__ constexpr int gemv_rows(int v) { return v <= 2 ? 8 : (v <= 4 ? 4 : 2); }
+// rows per group for V input vectors (R * V <= 16 accumulators per lane);
+// Q8_0 groups take half as many rows, so that two CTAs per SM hold three
+// stages of typical rows
+__host__ __device__ constexpr int gemv_rows(int block_bytes, int v) {
+  return (v <= 2 ? 8 : (v <= 4 ? 4 : 2)) / (block_bytes == 34 && v <= 2 ? 2 : 1);
+}
 
-// One group's dot products, accumulated per lane: a warp step covers 8
-// blocks (256 weights) and lane l takes block l / 4 of it and 8 of its
-// weights -- Q4_0: quant bytes 4 (l % 4) .. +3, i.e. weights 4 (l % 4) .. +3
-// (low nibbles) and 16 + 4 (l % 4) .. +3 (high nibbles); Q8_0: weights
-// 8 (l % 4) .. +7 -- for every row of the group (FULL: all R rows present, no
-// per-row guard).  A lane past the row's end (cols / 32 not a multiple of 8)
-// reads the row's last block with scale 0 and input 0.
-template <int BLOCK_BYTES, int V, int R, bool FULL>
-__device__ __forceinline__ void gemv_pass(const unsigned char* base, int rb, int nb, int nr, const float* x, int cols,
-                                          int warp, int lane, uint64_t (&acc)[R][V]) {
+// One warp step of a group's dot products: 8 blocks (256 weights), lane l
+// taking block l / 4 of it and 8 of its weights -- Q4_0: quant bytes
+// 4 (l % 4) .. +3, i.e. weights 4 (l % 4) .. +3 (low nibbles) and
+// 16 + 4 (l % 4) .. +3 (high nibbles); Q8_0: weights 8 (l % 4) .. +7 -- for
+// every row of the group (FULL: all R rows present, no per-row guard).  Per
+// row and vector the lane forms sum (q - offset) * x over its 8 weights
+// (exact weights, fp32 products and sums) and adds scale * that to acc.  In a
+// step that runs past the row's end (EDGE; cols / 32 not a multiple of 8) a
+// lane past it reads the row's last block with input 0 and adds 0.
+template <int BLOCK_BYTES, int V, int R, bool FULL, bool EDGE>
+__device__ __forceinline__ void gemv_step(const unsigned char* base, int rb, int nb, int nr, const float* x, int cols,
+                                          int b0, int lane, float (&acc)[R][V]) {
   constexpr float kOff = BLOCK_BYTES == 18 ? 8388616.0f : 8388736.0f;  // 2^23 + the quant offset (8 or 128)
   const uint64_t off2 = f2_pack(kOff, kOff);
   const int j = lane & 3;
-  const int xo0 = BLOCK_BYTES == 18 ? 4 * j : 8 * j;       // input offsets of the lane's two weight quads
+  const int xo0 = BLOCK_BYTES == 18 ? 4 * j : 8 * j;  // input offsets of the lane's two weight quads
   const int xo1 = BLOCK_BYTES == 18 ? 16 + 4 * j : 8 * j + 4;
   const int qo = BLOCK_BYTES == 18 ? 2 + 4 * j : 2 + 8 * j;  // the lane's quant bytes within a block
-  for (int b0 = 8 * warp; b0 < nb; b0 += 8 * kGemvWarps) {
-    const int b = b0 + (lane >> 2);
-    const bool in = b < nb;
-    const int bc = in ? b : nb - 1;
-    uint64_t xs[V][4];
+  const int b = b0 + (lane >> 2);
+  const bool in = !EDGE || b < nb;
+  const int bc = in ? b : nb - 1;
+  uint64_t xs[V][4];
 #pragma unroll
-    for (int v = 0; v < V; ++v) {
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
-      if (in) {
-        const float* xr = x + (size_t)v * cols + (size_t)b * 32;
-        a = __ldg(reinterpret_cast<const float4*>(xr + xo0));
-        c = __ldg(reinterpret_cast<const float4*>(xr + xo1));
-      }
-      xs[v][0] = f2_pack(a.x, a.y);
-      xs[v][1] = f2_pack(a.z, a.w);
-      xs[v][2] = f2_pack(c.x, c.y);
-      xs[v][3] = f2_pack(c.z, c.w);
+  for (int v = 0; v < V; ++v) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
+    if (in) {
+      const float* xr = x + (size_t)v * cols + (size_t)b * 32;
+      a = __ldg(reinterpret_cast<const float4*>(xr + xo0));
+      c = __ldg(reinterpret_cast<const float4*>(xr + xo1));
     }
+    xs[v][0] = f2_pack(a.x, a.y);
+    xs[v][1] = f2_pack(a.z, a.w);
+    xs[v][2] = f2_pack(c.x, c.y);
+    xs[v][3] = f2_pack(c.z, c.w);
+  }
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if (FULL || r < nr) {
-        const unsigned char* blk = base + r * rb + bc * BLOCK_BYTES;
-        float sc = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
-        sc = in ? sc : 0.f;
-        const uint16_t* qp = reinterpret_cast<const uint16_t*>(blk + qo);
-        uint32_t lo, hi;  // the lane's 8 codes, one per byte (Q8_0: int8 + 128)
-        if (BLOCK_BYTES == 18) {
-          const uint32_t q = prmt(qp[0], qp[1], 0x5410u);
-          lo = q & 0x0f0f0f0fu;
-          hi = (q >> 4) & 0x0f0f0f0fu;
-        } else {
-          lo = prmt(qp[0], qp[1], 0x5410u) ^ 0x80808080u;
-          hi = prmt(qp[2], qp[3], 0x5410u) ^ 0x80808080u;
-        }
-        // code byte i under the exponent bits of 2^23: the float 2^23 + code,
-        // exact; minus the offset, times the scale, both exact in fp32
-        const uint64_t s2 = f2_pack(sc, sc);
-        uint64_t wq[4];
-        wq[0] = f2_pack(__uint_as_float(prmt(lo, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(lo, 0x4B000000u, 0x7441u)));
-        wq[1] = f2_pack(__uint_as_float(prmt(lo, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(lo, 0x4B000000u, 0x7443u)));
-        wq[2] = f2_pack(__uint_as_float(prmt(hi, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(hi, 0x4B000000u, 0x7441u)));
-        wq[3] = f2_pack(__uint_as_float(prmt(hi, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(hi, 0x4B000000u, 0x7443u)));
+  for (int r = 0; r < R; ++r) {
+    if (FULL || r < nr) {
+      const unsigned char* blk = base + r * rb + bc * BLOCK_BYTES;
+      const float sc = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
+      const uint16_t* qp = reinterpret_cast<const uint16_t*>(blk + qo);
+      uint32_t lo, hi;  // the lane's 8 codes, one per byte (Q8_0: int8 + 128)
+      if (BLOCK_BYTES == 18) {
+        const uint32_t q = prmt(qp[0], qp[1], 0x5410u);
+        lo = q & 0x0f0f0f0fu;
+        hi = (q >> 4) & 0x0f0f0f0fu;
+      } else {
+        lo = prmt(qp[0], qp[1], 0x5410u) ^ 0x80808080u;
+        hi = prmt(qp[2], qp[3], 0x5410u) ^ 0x80808080u;
+      }
+      // code byte i under the exponent bits of 2^23: the float 2^23 + code,
+      // exact; minus the offset, exact
+      uint64_t wq[4];
+      wq[0] = f2_pack(__uint_as_float(prmt(lo, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(lo, 0x4B000000u, 0x7441u)));
+      wq[1] = f2_pack(__uint_as_float(prmt(lo, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(lo, 0x4B000000u, 0x7443u)));
+      wq[2] = f2_pack(__uint_as_float(prmt(hi, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(hi, 0x4B000000u, 0x7441u)));
+      wq[3] = f2_pack(__uint_as_float(prmt(hi, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(hi, 0x4B000000u, 0x7443u)));
 #pragma unroll
-        for (int k = 0; k < 4; ++k) wq[k] = f2_mul(f2_sub(wq[k], off2), s2);
+      for (int k = 0; k < 4; ++k) wq[k] = f2_sub(wq[k], off2);
 #pragma unroll
-        for (int v = 0; v < V; ++v) {
+      for (int v = 0; v < V; ++v) {
+        uint64_t d = f2_mul(wq[0], xs[v][0]);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) acc[r][v] = f2_fma(wq[k], xs[v][k], acc[r][v]);
-        }
+        for (int k = 1; k < 4; ++k) d = f2_fma(wq[k], xs[v][k], d);
+        float d0, d1;
+        f2_unpack(d, d0, d1);
+        float part = d0 + d1;
+        if (EDGE) part = in ? part : 0.f;
+        acc[r][v] = fmaf(sc, part, acc[r][v]);
       }
     }
   }
 }
 
+// A group's dot products, per lane: warp w takes steps w, w + 8, ... of the row.
+template <int BLOCK_BYTES, int V, int R, bool FULL>
+__device__ __forceinline__ void gemv_pass(const unsigned char* base, int rb, int nb, int nr, const float* x, int cols,
+                                          int warp, int lane, float (&acc)[R][V]) {
+  int b0 = 8 * warp;
+  for (; b0 + 8 <= nb; b0 += 8 * kGemvWarps) {
+    gemv_step<BLOCK_BYTES, V, R, FULL, false>(base, rb, nb, nr, x, cols, b0, lane, acc);
+  }
+  if (b0 < nb) gemv_step<BLOCK_BYTES, V, R, FULL, true>(base, rb, nb, nr, x, cols, b0, lane, acc);
+}
+
 template <int BLOCK_BYTES, int V>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_gguf_kernel(const GemvParams p) {
-  constexpr int R = gemv_rows(V);
+  constexpr int R = gemv_rows(BLOCK_BYTES, V);
   extern __shared__ __align__(128) unsigned char gsm[];
   uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
   float* partial = reinterpret_cast<float*>(gsm + kGemvHeader);
@@ -186,11 +206,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_gguf_kernel(const GemvPa
     const long long lo16 = ((long long)r0 * rb) & ~15ll;
     const unsigned char* base = stages + (size_t)stage * p.stage_bytes + (int)((long long)r0 * rb - lo16);
 
-    uint64_t acc[R][V];  // f32x2 partial sums
+    float acc[R][V];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
 #pragma unroll
-      for (int v = 0; v < V; ++v) acc[r][v] = 0ull;
+      for (int v = 0; v < V; ++v) acc[r][v] = 0.f;
     }
     if (nr == R) {
       gemv_pass<BLOCK_BYTES, V, R, true>(base, (int)rb, nb, nr, p.x, p.cols, warp, lane, acc);
@@ -203,9 +223,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_gguf_kernel(const GemvPa
       if (r < nr) {
 #pragma unroll
         for (int v = 0; v < V; ++v) {
-          float a0, a1;
-          f2_unpack(acc[r][v], a0, a1);
-          float s = a0 + a1;
+          float s = acc[r][v];
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
           if (lane == 0) part[(warp * R + r) * V + v] = s;
@@ -272,7 +290,7 @@ cudaError_t launch_gemv_gguf(GemvParams p, int block_bytes, int n_vectors, int s
   // R rows per group (the kernel's compile-time count, no per-row guards),
   // fewer only when two stages of R rows would not fit one CTA; a stage holds
   // the group widened to 16-byte boundaries at both ends
-  int rpg = gemv_rows(n_vectors);
+  int rpg = gemv_rows(block_bytes, n_vectors);
   while (rpg > 1 && 2 * ((rpg * rb + 45) & ~15ll) + kGemvStageOffset + 128 > 227 * 1024) --rpg;
   if (rpg > p.rows) rpg = p.rows;
   p.rows_per_group = rpg;
