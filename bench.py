@@ -228,6 +228,15 @@ def run_gpu(args) -> None:
     hbm_peak, tc_peak, peak_src = load_peaks()
     eng = AttnEngine(local, decode_chunk_tokens=args.chunk)
     stream = torch.cuda.ExternalStream(eng.stream)
+    if args.gemv_only:
+        # the matrix-vector measurement alone (e.g. under a profiler): one JSON line
+        res = run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank)
+        eng.close()
+        if rank == 0:
+            print(json.dumps(res))
+        if world > 1:
+            dist.destroy_process_group()
+        return
     cap = CTX0 + DECODE_STEPS
     cache = eng.kv_cache(layers=LAYERS, max_seqs=1, max_tokens_per_seq=cap, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
                          rope_theta=THETA)
@@ -809,6 +818,8 @@ def main() -> None:
     ap.add_argument("--prefill-steps", type=int, default=10)
     ap.add_argument("--no-configs", action="store_true", help="skip the config-4 / config-5 measurements")
     ap.add_argument("--no-gemv", action="store_true", help="skip the GGUF matrix-vector measurement")
+    ap.add_argument("--gemv-only", action="store_true",
+                    help="run only the GGUF matrix-vector measurement (Q4_0: launches 1-23, Q8_0: 24-46)")
     ap.add_argument("--cfg-steps", type=int, default=16, help="decode steps timed for config 4")
     ap.add_argument("--long-steps", type=int, default=128, help="decode steps timed for config 5")
     ap.add_argument("--long-exchange", choices=["nccl", "p2p"], default="nccl",
