@@ -43,6 +43,9 @@ constexpr int kGemvPartialFloats = 2 * kGemvWarps * 16;  // [2 parities][warps][
 constexpr int kGemvStageOffset = kGemvHeader + kGemvPartialFloats * 4;
 static_assert(kGemvStageOffset % 16 == 0, "bulk copies land on 16-byte boundaries");
 
+// CTAs per SM the kernel is compiled for (registers): 3 with 1-2 vectors
+__host__ __device__ constexpr int gemv_ctas(int v) { return v <= 2 ? 3 : 2; }
+
 // rows per group for V input vectors (R * V <= 16 accumulators per lane);
 // Q8_0 groups take half as many rows, so that two CTAs per SM hold three
 // stages of typical rows
@@ -136,7 +139,7 @@ __device__ __forceinline__ void gemv_pass(const unsigned char* base, int rb, int
 }
 
 template <int BLOCK_BYTES, int V>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_gguf_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, gemv_ctas(V)) gemv_gguf_kernel(const GemvParams p) {
   constexpr int R = gemv_rows(BLOCK_BYTES, V);
   extern __shared__ __align__(128) unsigned char gsm[];
   uint64_t* full = reinterpret_cast<uint64_t*>(gsm);
@@ -295,17 +298,17 @@ cudaError_t launch_gemv_gguf(GemvParams p, int block_bytes, int n_vectors, int s
   if (rpg > p.rows) rpg = p.rows;
   p.rows_per_group = rpg;
   p.stage_bytes = (int)((rpg * rb + 30 + 15) & ~15ll);
-  // as many stages (2 to 4) as fit two CTAs per SM (2 x 112 KiB of the SM's
-  // 228, with the static word and the per-CTA reserve), else one CTA per SM
-  // with up to 227 KiB
-  const int per_two = (112 * 1024 - kGemvStageOffset) / p.stage_bytes;
-  int ctas_per_sm = 2;
-  int stages = per_two < kGemvMaxStages ? per_two : kGemvMaxStages;
-  if (stages < 2) {
-    ctas_per_sm = 1;
-    const int per_one = (227 * 1024 - 128 - kGemvStageOffset) / p.stage_bytes;
-    stages = per_one < kGemvMaxStages ? per_one : kGemvMaxStages;
+  // the most CTAs per SM (up to gemv_ctas) whose shares of the SM's 228 KiB
+  // (less the static word and the per-CTA reserve) hold at least two stages;
+  // then as many stages as fit the share, up to 4
+  int ctas_per_sm = gemv_ctas(n_vectors);
+  int stages = 0;
+  for (; ctas_per_sm >= 1; --ctas_per_sm) {
+    const int share = ctas_per_sm == 1 ? 227 * 1024 - 128 : (228 * 1024) / ctas_per_sm - 1024 - 128;
+    stages = (share - kGemvStageOffset) / p.stage_bytes;
+    if (stages >= 2) break;
   }
+  if (stages > kGemvMaxStages) stages = kGemvMaxStages;
   p.stages = stages;
   const int smem = kGemvStageOffset + stages * p.stage_bytes;
   return block_bytes == 18 ? launch_b<18>(p, n_vectors, ctas_per_sm, sm_count, smem, s)
