@@ -8,7 +8,10 @@ import this module.  It loads two C builds through ctypes:
   ``c/src/qwen.c:810-824``);
 * ``_ref/libteref.so`` -- the reference's own ``c/src/ops.c`` compiled from its
   sources by ``oracle/Makefile`` (present where the reference was available at
-  build time; the built file travels with the repository snapshot).
+  build time; the built file travels with the repository snapshot);
+* ``_ref/libteqwen.so`` -- the reference's CPU forward pass (``c/src/qwen.c``
+  ``te_qwen_forward_token`` / ``te_qwen_project_next`` with its GGUF parser),
+  built the same way (``ref_qwen.c``), the checker of the layer step.
 
 ctypes releases the GIL during each foreign call, so the threaded CPU baseline
 runs the single-threaded C functions on several cores at once.
@@ -25,6 +28,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 PORT_LIB = HERE / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libteref.so"
+REF_QWEN_LIB = HERE / "_ref" / "libteqwen.so"
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _u16p = ctypes.POINTER(ctypes.c_uint16)
@@ -190,6 +194,48 @@ class Ref(_Lib):
         self.lib.ref_stub_register_tensor(0, 0, 0, None, 0)
         assert st == 0 and written.value == rows, st
         return out
+
+
+class RefQwen:
+    """The reference's per-token forward pass on a GGUF file (one model per process: the
+    harness keeps it in file-scope state).  forward(token, position) -> hidden [hidden] fp32;
+    project() -> (logits [vocab], greedy token)."""
+
+    def __init__(self, path, context_tokens: int):
+        if not REF_QWEN_LIB.is_file():
+            raise FileNotFoundError(f"oracle library missing: {REF_QWEN_LIB}")
+        self.lib = ctypes.CDLL(str(REF_QWEN_LIB))
+        self.lib.rq_open.argtypes = [ctypes.c_char_p, ctypes.c_uint32]
+        self.lib.rq_forward.argtypes = [ctypes.c_uint32, ctypes.c_size_t, _f32p]
+        self.lib.rq_project.argtypes = [_f32p, ctypes.POINTER(ctypes.c_uint32)]
+        self.lib.rq_dims.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
+        st = self.lib.rq_open(str(path).encode(), context_tokens)
+        if st != 0:
+            raise RuntimeError(f"reference model load failed: status {st}")
+        d = (ctypes.c_uint64 * 8)()
+        self.lib.rq_dims(d)
+        keys = ("hidden", "ffn", "layers", "heads", "kv_heads", "head_dim", "vocab", "context")
+        self.dims = {k: int(v) for k, v in zip(keys, d)}
+
+    def forward(self, token: int, position: int) -> np.ndarray:
+        h = np.zeros(self.dims["hidden"], np.float32)
+        st = self.lib.rq_forward(token, position, _ptr(h))
+        assert st == 0, st
+        return h
+
+    def project(self):
+        logits = np.zeros(self.dims["vocab"], np.float32)
+        tok = ctypes.c_uint32()
+        st = self.lib.rq_project(_ptr(logits), ctypes.byref(tok))
+        assert st == 0, st
+        return logits, int(tok.value)
+
+    def close(self) -> None:
+        self.lib.rq_close()
+
+
+def ref_qwen_available() -> bool:
+    return REF_QWEN_LIB.is_file()
 
 
 _port = None

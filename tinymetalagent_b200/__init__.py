@@ -2,7 +2,8 @@
 
 The product is ``libtinyengine.so`` (built from ``csrc/``) behind the C ABI in
 ``include/tinyengine.h`` and ``include/tinyengine_attn.h``; this package holds
-its ctypes binding and the multi-GPU host orchestration.
+its ctypes binding, the multi-GPU host orchestration, and the qwen2 decode
+step built on them (``qwen.QwenDecoder``, with the GGUF reader ``gguf``).
 """
 from .runtime import (  # noqa: F401
     TE_ATTN_ACCUMULATE,
