@@ -415,6 +415,11 @@ def run_gpu(args) -> None:
     if not args.no_gemv:
         gemv = run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank)
 
+    # ---- the qwen2 decode step (projections + attention + glue), one GPU ----
+    qwen = None
+    if not args.no_qwen and world == 1:
+        qwen = run_qwen(eng, stream, hbm_peak, peak_src, args)
+
     # ---- BASELINE configs 4 (sequence-sharded batch) and 5 (KV split + NCCL merge) ----
     ragged = long = None
     if not args.no_configs:
@@ -451,6 +456,7 @@ def run_gpu(args) -> None:
             "prefill": prefill,
             "decode3b_qkv_bias": qkv_bias,
             "gemv_gguf": gemv,
+            "qwen_decode_step": qwen,
             "ragged7b": ragged,
             "long7b": long,
         }
@@ -610,6 +616,107 @@ def run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank):
                                    "sample": f"{n} calls of te_model_matvec_f32 (Q4_0 {r_cpu}x{cols}, its pthread "
                                              f"row split) in {dt:.1f} s"}
     return res
+
+
+QWEN_SHAPE = dict(layers=24, hidden=896, heads=14, kv_heads=2, ffn=4864, vocab=151936, context=1024)
+
+
+def run_qwen(eng, stream, hbm_peak, peak_src, args):
+    """QwenDecoder (the te_qwen_forward_token-compatible decode step) on a synthetic model of
+    Qwen2.5-0.5B's shape -- 24 layers, hidden 896, 14 heads of 64 over 2 KV heads, FFN 4864, vocabulary
+    151 936; Q4_0 projections, Q8_0 embedding and lm_head -- written as a GGUF file at run time (no
+    model file is available offline).  A step is forward_token + project_next (greedy, its argmax read
+    back to the host) after a 16-token prompt; tokens/s over args.qwen_steps steps, device time on the
+    engine's stream.  Beside it, the reference's own CPU forward pass on the same file."""
+    import tempfile
+    import shutil
+    import torch
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    from gguf_synth import GGML_Q4_0, write_qwen2
+    from tinymetalagent_b200.qwen import QwenDecoder
+
+    tmp = Path(tempfile.mkdtemp(prefix="qwen_bench_"))
+    try:
+        path = tmp / "qwen2_0p5b_shape.gguf"
+        write_qwen2(path, quant_attn=GGML_Q4_0, quant_ffn=GGML_Q4_0, seed=3, **QWEN_SHAPE)
+        prompt, steps = 16, args.qwen_steps
+        ctx = prompt + steps + 8
+        dec = QwenDecoder(eng, path, ctx)
+        weight_bytes = sum(int(v.numel()) for lay in dec.layers for k, v in lay.items()
+                           if k in ("qkv", "o", "gu", "down")) + int(dec._head.numel())
+        rng = np.random.default_rng(9)
+        toks = [int(t) for t in rng.integers(0, QWEN_SHAPE["vocab"], prompt)]
+        for pos, t in enumerate(toks):
+            dec.forward_token(t, pos)
+        nxt = dec.project_next()
+        for _ in range(3):  # warm-up steps, then restart from the same position
+            dec.forward_token(nxt, prompt)
+            dec.project_next()
+        launches0 = eng.launch_count
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        t0 = time.perf_counter()
+        pos = prompt
+        for _ in range(steps):
+            dec.forward_token(nxt, pos)
+            nxt = dec.project_next()
+            pos += 1
+        e1.record(stream)
+        e1.synchronize()
+        wall_ms = (time.perf_counter() - t0) * 1e3
+        ms = max(e0.elapsed_time(e1), wall_ms)
+        launches = eng.launch_count - launches0
+        # the same window recorded as one CUDA graph (capture_greedy) and replayed
+        dec.cache.truncate(0, prompt)
+        first = nxt
+        dec.capture_greedy(prompt, steps)
+        dec.replay_greedy(first)  # warm
+        torch.cuda.synchronize()
+        e0.record(stream)
+        dec.replay_greedy(first)
+        e1.record(stream)
+        e1.synchronize()
+        graph_ms = e0.elapsed_time(e1)
+        dec.close()
+        tps = steps / (ms / 1e3)
+        graph_tps = steps / (graph_ms / 1e3)
+        gbs = weight_bytes * tps / 1e9
+        graph_gbs = weight_bytes * graph_tps / 1e9
+        res = {"metric": "qwen2 decode step (QwenDecoder: greedy steps recorded as one CUDA graph, replayed)",
+               "value": round(graph_tps, 1), "unit": "tokens/s", "ms_per_token": round(graph_ms / steps, 4),
+               "steps": steps,
+               "eager": {"value": round(tps, 1), "unit": "tokens/s", "ms_per_token": round(ms / steps, 4),
+                         "note": "forward_token + project_next from Python, argmax read back every step"},
+               "model": "synthetic Qwen2.5-0.5B shape: 24 layers, H14/Hkv2/hd64, hidden 896, FFN 4864, "
+                        "vocab 151936, Q4_0 projections, Q8_0 embedding/lm_head",
+               "weight_bytes_per_token": weight_bytes,
+               "roofline": {"bound": "hbm", "achieved": round(graph_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                            "frac": round(graph_gbs / hbm_peak, 4), "peak_source": f"{peak_src} (burst copy)",
+                            "eager_achieved": round(gbs, 1),
+                            "note": "weight bytes read once per token over the graph-replay time"},
+               "library_launches_per_token": round(launches / steps, 1)}
+        if not args.no_cpu:
+            from oracle import oracle as O
+            if O.ref_qwen_available():
+                ref = O.RefQwen(path, ctx)
+                for p_, t in enumerate(toks):
+                    ref.forward(t, p_)
+                _, rt = ref.project()
+                n, t0 = 0, time.perf_counter()
+                while time.perf_counter() - t0 < 3.0 and prompt + n < ctx:
+                    ref.forward(rt, prompt + n)
+                    _, rt = ref.project()
+                    n += 1
+                dt = time.perf_counter() - t0
+                ref.close()
+                res["cpu_baseline"] = {"value": round(n / dt, 2), "unit": "tokens/s", "kind": "reference",
+                                       "cores": O.host_cores(),
+                                       "sample": f"{n} tokens of te_qwen_forward_token + te_qwen_project_next "
+                                                 f"(its CPU path, pthread matvec row split) in {dt:.1f} s"}
+        return res
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
 
 
 def cpu_sample_7b(n: int, budget_s: float):
@@ -818,6 +925,8 @@ def main() -> None:
     ap.add_argument("--prefill-steps", type=int, default=10)
     ap.add_argument("--no-configs", action="store_true", help="skip the config-4 / config-5 measurements")
     ap.add_argument("--no-gemv", action="store_true", help="skip the GGUF matrix-vector measurement")
+    ap.add_argument("--no-qwen", action="store_true", help="skip the qwen2 decode-step measurement")
+    ap.add_argument("--qwen-steps", type=int, default=64, help="decode steps timed for the qwen2 decode step")
     ap.add_argument("--gemv-only", action="store_true",
                     help="run only the GGUF matrix-vector measurement (Q4_0: launches 1-23, Q8_0: 24-46)")
     ap.add_argument("--cfg-steps", type=int, default=16, help="decode steps timed for config 4")

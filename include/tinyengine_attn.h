@@ -58,6 +58,8 @@ extern "C" {
 #define TE_ATTN_QKV_BIAS      (1u << 5) /* add the cache's per-layer q/k/v biases (te_kv_cache_set_qkv_bias)
                                            to the raw inputs first, in fp32, before RoPE and rounding */
 #define TE_ATTN_ACCUMULATE    (1u << 6) /* te_matvec_gguf: y += W x (the residual add of a projection) */
+#define TE_ATTN_RMSNORM_INPUT (1u << 7) /* te_matvec_gguf_fused: the input is RMSNorm(x) * norm_weight */
+#define TE_ATTN_SWIGLU_INPUT  (1u << 8) /* te_matvec_gguf_fused: the input is SwiGLU of x = [gate | up] */
 
 typedef struct te_attn_engine te_attn_engine;
 typedef struct te_kv_cache te_kv_cache;
@@ -220,6 +222,25 @@ TE_API te_status te_attention_merge_partials(te_attn_engine *engine, const float
 #define TE_ATTN_QUANT_GGUF_Q8_0 8u
 TE_API te_status te_matvec_gguf(te_attn_engine *engine, uint32_t quant, const void *w, size_t rows,
                                 size_t cols, const float *x, size_t n_vectors, float *y, uint32_t flags);
+
+/* The same product for ONE input vector with the elementwise step that the
+ * reference runs just before it fused into the input reads:
+ *   TE_ATTN_RMSNORM_INPUT: the input is te_rmsnorm_f32(x, norm_weight, eps)
+ *     (c/src/ops.c:272-293: squares summed in double, scale =
+ *     1 / sqrtf((float)(sum / cols) + eps), (x[c] * scale) * norm_weight[c]),
+ *     which precedes the q/k/v, gate/up and lm_head projections
+ *     (c/src/qwen.c:965-971, :1082-1088, :1350-1356);
+ *   TE_ATTN_SWIGLU_INPUT: x holds [gate | up] (2 * cols values) and the input
+ *     is te_swiglu_f32(gate, up) (ops.c:397-406: gate / (1 + expf(-gate)) *
+ *     up), which precedes the down projection (qwen.c:1933-1941).
+ * Exactly one of the two, optionally with TE_ATTN_ACCUMULATE.  norm_weight
+ * [cols] fp32 (RMSNorm only, 16-byte aligned), eps > 0; other arguments and
+ * limits as te_matvec_gguf.  The norm's sum runs in another order than the
+ * reference's (in double), and expf is the device's, so results agree to
+ * fp32 rounding. */
+TE_API te_status te_matvec_gguf_fused(te_attn_engine *engine, uint32_t quant, const void *w, size_t rows,
+                                      size_t cols, const float *x, const float *norm_weight, float eps,
+                                      float *y, uint32_t flags);
 
 /* KV-split exchange over NVLink --------------------------------------------
  *

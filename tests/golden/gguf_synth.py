@@ -41,7 +41,7 @@ def quant_blocks(rng, ggml_type: int, rows: int, cols: int, sigma: float) -> np.
     w = np.zeros((rows, blocks, width), np.uint8)
     scales = (sigma / code_std * (1.0 + 0.25 * rng.standard_normal((rows, blocks)))).astype(np.float16)
     w[:, :, 0:2] = scales.view(np.uint8).reshape(rows, blocks, 2)
-    w[:, :, 2:] = rng.integers(0, 256, (rows, blocks, width - 2), dtype=np.uint8)
+    w[:, :, 2:] = np.frombuffer(rng.bytes(rows * blocks * (width - 2)), np.uint8).reshape(rows, blocks, width - 2)
     return w.reshape(-1)
 
 

@@ -141,3 +141,80 @@ def test_matvec_residual_accumulate(port, quant):
             assert (np.abs(got[v] - exp) <= bound).all()
     finally:
         eng.close()
+
+
+@pytest.mark.parametrize("quant", [Q4, Q8])
+@pytest.mark.parametrize("shape", [(896 + 256, 896), (4864 * 2, 896), (300, 2048), (7, 160)])
+def test_matvec_fused_rmsnorm_input(port, quant, shape):
+    """te_matvec_gguf_fused + TE_ATTN_RMSNORM_INPUT: y = W te_rmsnorm_f32(x, w_norm, eps) (c/src/ops.c:272-293:
+    double sum of squares, fp32 scale, (x * scale) * w)."""
+    import torch
+    from tinymetalagent_b200 import TE_ATTN_RMSNORM_INPUT, AttnEngine
+    rows, cols = shape
+    rng = np.random.default_rng(rows + cols + quant)
+    w = quant_matrix(rng, GGML[quant], rows, cols)
+    x = (rng.standard_normal(cols) * 3.0).astype(np.float32)
+    nw = (1.0 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    eps = np.float32(1e-6)
+    ss = np.sum(x.astype(np.float64) ** 2)
+    scale = np.float32(1.0) / np.sqrt(np.float32(ss / cols) + eps)
+    xn = ((x * scale) * nw).astype(np.float32)
+    eng = AttnEngine(0)
+    try:
+        y = torch.full((1, rows), float("nan"), dtype=torch.float32, device="cuda")
+        eng.matvec_gguf_fused(quant, dev(w), rows, cols, dev(x), y, TE_ATTN_RMSNORM_INPUT, dev(nw), float(eps))
+        eng.synchronize()
+        check(port, quant, w, rows, cols, xn[None], y.cpu().numpy())
+    finally:
+        eng.close()
+
+
+@pytest.mark.parametrize("quant", [Q4, Q8])
+@pytest.mark.parametrize("shape", [(896, 4864), (2048, 2048), (33, 96)])
+def test_matvec_fused_swiglu_input_accumulate(port, quant, shape):
+    """te_matvec_gguf_fused + TE_ATTN_SWIGLU_INPUT + TE_ATTN_ACCUMULATE: y += W te_swiglu_f32(gate, up)
+    (ops.c:397-406), x = [gate | up] -- the down projection and its residual add (qwen.c:1933-1941, :1105-1108)."""
+    import torch
+    from tinymetalagent_b200 import TE_ATTN_ACCUMULATE, TE_ATTN_SWIGLU_INPUT, AttnEngine
+    rows, cols = shape
+    rng = np.random.default_rng(3 * rows + cols + quant)
+    w = quant_matrix(rng, GGML[quant], rows, cols)
+    gu = (rng.standard_normal(2 * cols) * 2.0).astype(np.float32)
+    g, u = gu[:cols], gu[cols:]
+    s = ((g / (np.float32(1.0) + np.exp(-g))) * u).astype(np.float32)
+    res = rng.standard_normal(rows).astype(np.float32)
+    eng = AttnEngine(0)
+    try:
+        y = dev(res[None])
+        eng.matvec_gguf_fused(quant, dev(w), rows, cols, dev(gu), y, TE_ATTN_SWIGLU_INPUT | TE_ATTN_ACCUMULATE)
+        eng.synchronize()
+        ref_fn = port.matvec_q4_0_f32 if quant == Q4 else port.matvec_q8_0_f32
+        exp = (res + ref_fn(w, rows, cols, s)).astype(np.float32)
+        wd = np.abs(dequant(quant, w, rows, cols))
+        bound = 2e-5 * (wd @ np.abs(s)) + 1e-6 + 1e-7 * np.abs(exp)  # fp32 sums + device expf (a few ulp)
+        assert (np.abs(y.cpu().numpy()[0] - exp) <= bound).all()
+    finally:
+        eng.close()
+
+
+def test_matvec_fused_rejects_bad_arguments():
+    import torch
+    from tinymetalagent_b200 import (TE_ATTN_RMSNORM_INPUT, TE_ATTN_SWIGLU_INPUT, AttnEngine, TinyEngineError)
+    eng = AttnEngine(0)
+    try:
+        w = torch.zeros(18 * 4, dtype=torch.uint8, device="cuda")
+        x = torch.zeros(128, dtype=torch.float32, device="cuda")
+        y = torch.zeros(2, dtype=torch.float32, device="cuda")
+        nw = torch.ones(64, dtype=torch.float32, device="cuda")
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf_fused(Q4, w, 2, 64, x, y, 0)                                  # no prologue
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf_fused(Q4, w, 2, 64, x, y, TE_ATTN_RMSNORM_INPUT | TE_ATTN_SWIGLU_INPUT, nw, 1e-6)
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf_fused(Q4, w, 2, 64, x, y, TE_ATTN_RMSNORM_INPUT, None, 1e-6)  # no norm weight
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf_fused(Q4, w, 2, 64, x, y, TE_ATTN_RMSNORM_INPUT, nw, 0.0)     # eps must be > 0
+        with pytest.raises(TinyEngineError):
+            eng.matvec_gguf_fused(Q4, w, 2, 64, x, y, TE_ATTN_RMSNORM_INPUT, nw[1:], 1e-6)  # unaligned weight
+    finally:
+        eng.close()

@@ -107,3 +107,47 @@ def test_decoder_rejects_gaps_and_bad_tokens(tmp_path):
     finally:
         dec.close()
         eng.close()
+
+
+def test_graph_replay_matches_eager_steps(tmp_path):
+    """capture_greedy / replay_greedy: the same kernels as the eager steps, recorded once; the tokens and
+    the final hidden state equal the eager run's, replaying twice gives the same tokens, and eager steps
+    continue after a replay."""
+    import torch
+    from tinymetalagent_b200 import AttnEngine
+    from tinymetalagent_b200.qwen import QwenDecoder
+    path = tmp_path / "m.gguf"
+    write_qwen2(path, **MODELS["hd64"])
+    prompt = [int(t) for t in np.random.default_rng(8).integers(0, 512, 12)]
+    n = 16
+    eng = AttnEngine(0)
+    try:
+        eager = QwenDecoder(eng, path, 40)
+        for pos, t in enumerate(prompt):
+            eager.forward_token(t, pos)
+        first = eager.project_next()
+        toks, tok = [], first
+        for i in range(n):
+            eager.forward_token(tok, len(prompt) + i)
+            tok = eager.project_next()
+            toks.append(tok)
+        h_eager = eager.x.cpu().numpy()
+        after = eager.forward_token(tok, len(prompt) + n).cpu().numpy()
+        eager.close()
+
+        g = QwenDecoder(eng, path, 40)
+        for pos, t in enumerate(prompt):
+            g.forward_token(t, pos)
+        assert g.project_next() == first
+        g.capture_greedy(len(prompt), n)
+        for _ in range(2):
+            got = g.replay_greedy(first).cpu().numpy()
+            assert got[0] == first and got[1:].tolist() == toks
+            np.testing.assert_allclose(g.x.cpu().numpy(), h_eager, rtol=0, atol=1e-6)
+        np.testing.assert_allclose(g.forward_token(tok, len(prompt) + n).cpu().numpy(), after, rtol=0, atol=1e-6)
+        with pytest.raises(RuntimeError):
+            g.replay_greedy(first)  # the cache moved on since the capture
+        g.close()
+        torch.cuda.synchronize()
+    finally:
+        eng.close()

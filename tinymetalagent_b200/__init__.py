@@ -13,6 +13,8 @@ from .runtime import (  # noqa: F401
     TE_ATTN_NO_ROPE,
     TE_ATTN_PARTIAL,
     TE_ATTN_QKV_BIAS,
+    TE_ATTN_RMSNORM_INPUT,
+    TE_ATTN_SWIGLU_INPUT,
     AttnEngine,
     KVCache,
     TinyEngineError,

@@ -38,7 +38,8 @@ namespace {
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kGemvMaxStages = 4;
-constexpr int kGemvHeader = 64;                          // the stages' mbarriers
+constexpr int kGemvHeader = 64;                          // the stages' mbarriers, then the RMSNorm scale
+constexpr int kGemvScaleOffset = 8 * kGemvMaxStages;
 constexpr int kGemvPartialFloats = 2 * kGemvWarps * 16;  // [2 parities][warps][R * V <= 16]
 constexpr int kGemvStageOffset = kGemvHeader + kGemvPartialFloats * 4;
 static_assert(kGemvStageOffset % 16 == 0, "bulk copies land on 16-byte boundaries");
@@ -62,8 +63,35 @@ __host__ __device__ constexpr int gemv_rows(int block_bytes, int v) {
 // (exact weights, fp32 products and sums) and adds scale * that to acc.  In a
 // step that runs past the row's end (EDGE; cols / 32 not a multiple of 8) a
 // lane past it reads the row's last block with input 0 and adds 0.
-template <int BLOCK_BYTES, int V, int R, bool FULL, bool EDGE>
-__device__ __forceinline__ void gemv_step(const unsigned char* base, int rb, int nb, int nr, const float* x, int cols,
+// The matrix-vector input and its fused prologue: PRO 0 reads x as given;
+// PRO 1 (RMSNorm) reads (x[c] * scale) * nw[c], the scale computed once per
+// CTA; PRO 2 (SwiGLU) reads x as [gate | up] and forms
+// gate[c] / (1 + expf(-gate[c])) * up[c].
+struct GemvInput {
+  const float* x;
+  const float* nw;
+  float scale;
+  int cols;
+};
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+template <int PRO>
+__device__ __forceinline__ float4 gemv_load(const GemvInput& in, int v, int col) {
+  const float* xr = in.x + (size_t)v * (PRO == 2 ? 2 : 1) * in.cols + col;
+  float4 a = __ldg(reinterpret_cast<const float4*>(xr));
+  if (PRO == 1) {
+    const float4 w = __ldg(reinterpret_cast<const float4*>(in.nw + col));
+    a = make_float4((a.x * in.scale) * w.x, (a.y * in.scale) * w.y, (a.z * in.scale) * w.z, (a.w * in.scale) * w.w);
+  } else if (PRO == 2) {
+    const float4 u = __ldg(reinterpret_cast<const float4*>(xr + in.cols));
+    a = make_float4(silu(a.x) * u.x, silu(a.y) * u.y, silu(a.z) * u.z, silu(a.w) * u.w);
+  }
+  return a;
+}
+
+template <int BLOCK_BYTES, int V, int R, bool FULL, bool EDGE, int PRO>
+__device__ __forceinline__ void gemv_step(const unsigned char* base, int rb, int nb, int nr, const GemvInput& X,
                                           int b0, int lane, float (&acc)[R][V]) {
   constexpr float kOff = BLOCK_BYTES == 18 ? 8388616.0f : 8388736.0f;  // 2^23 + the quant offset (8 or 128)
   const uint64_t off2 = f2_pack(kOff, kOff);
@@ -79,9 +107,8 @@ __device__ __forceinline__ void gemv_step(const unsigned char* base, int rb, int
   for (int v = 0; v < V; ++v) {
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
     if (in) {
-      const float* xr = x + (size_t)v * cols + (size_t)b * 32;
-      a = __ldg(reinterpret_cast<const float4*>(xr + xo0));
-      c = __ldg(reinterpret_cast<const float4*>(xr + xo1));
+      a = gemv_load<PRO>(X, v, b * 32 + xo0);
+      c = gemv_load<PRO>(X, v, b * 32 + xo1);
     }
     xs[v][0] = f2_pack(a.x, a.y);
     xs[v][1] = f2_pack(a.z, a.w);
@@ -128,17 +155,17 @@ __device__ __forceinline__ void gemv_step(const unsigned char* base, int rb, int
 }
 
 // A group's dot products, per lane: warp w takes steps w, w + 8, ... of the row.
-template <int BLOCK_BYTES, int V, int R, bool FULL>
-__device__ __forceinline__ void gemv_pass(const unsigned char* base, int rb, int nb, int nr, const float* x, int cols,
+template <int BLOCK_BYTES, int V, int R, bool FULL, int PRO>
+__device__ __forceinline__ void gemv_pass(const unsigned char* base, int rb, int nb, int nr, const GemvInput& X,
                                           int warp, int lane, float (&acc)[R][V]) {
   int b0 = 8 * warp;
   for (; b0 + 8 <= nb; b0 += 8 * kGemvWarps) {
-    gemv_step<BLOCK_BYTES, V, R, FULL, false>(base, rb, nb, nr, x, cols, b0, lane, acc);
+    gemv_step<BLOCK_BYTES, V, R, FULL, false, PRO>(base, rb, nb, nr, X, b0, lane, acc);
   }
-  if (b0 < nb) gemv_step<BLOCK_BYTES, V, R, FULL, true>(base, rb, nb, nr, x, cols, b0, lane, acc);
+  if (b0 < nb) gemv_step<BLOCK_BYTES, V, R, FULL, true, PRO>(base, rb, nb, nr, X, b0, lane, acc);
 }
 
-template <int BLOCK_BYTES, int V>
+template <int BLOCK_BYTES, int V, int PRO>
 __global__ void __launch_bounds__(kGemvThreads, gemv_ctas(V)) gemv_gguf_kernel(const GemvParams p) {
   constexpr int R = gemv_rows(BLOCK_BYTES, V);
   extern __shared__ __align__(128) unsigned char gsm[];
@@ -162,7 +189,32 @@ __global__ void __launch_bounds__(kGemvThreads, gemv_ctas(V)) gemv_gguf_kernel(c
     fence_mbarrier_init();
     s_abort = 0;
   }
+  GemvInput X{p.x, p.norm_w, 1.0f, p.cols};
+  if (PRO == 1) {
+    // RMSNorm scale of the (single) input vector, as te_rmsnorm_f32 forms it
+    // (c/src/ops.c:283-288): the squares summed in double, then
+    // 1 / sqrtf((float)(sum / cols) + eps) in fp32; each CTA computes it for
+    // itself (the vector is a few KB), the partial-sum area holding the
+    // per-warp sums before the first group uses it
+    double ss = 0.0;
+    for (int c = threadIdx.x * 4; c < p.cols; c += kGemvThreads * 4) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(p.x + c));
+      ss += (double)t.x * (double)t.x + (double)t.y * (double)t.y + (double)t.z * (double)t.z +
+            (double)t.w * (double)t.w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    double* red = reinterpret_cast<double*>(partial);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double tot = 0.0;
+      for (int k = 0; k < kGemvWarps; ++k) tot += red[k];
+      *reinterpret_cast<float*>(gsm + kGemvScaleOffset) = 1.0f / sqrtf((float)(tot / (double)p.cols) + p.eps);
+    }
+  }
   __syncthreads();
+  if (PRO == 1) X.scale = *reinterpret_cast<const float*>(gsm + kGemvScaleOffset);
 
   // one thread: stage group g; the copy covers [lo rounded down to 16, hi
   // rounded up to 16) clipped to the matrix's last 16-byte boundary, and the
@@ -216,9 +268,9 @@ __global__ void __launch_bounds__(kGemvThreads, gemv_ctas(V)) gemv_gguf_kernel(c
       for (int v = 0; v < V; ++v) acc[r][v] = 0.f;
     }
     if (nr == R) {
-      gemv_pass<BLOCK_BYTES, V, R, true>(base, (int)rb, nb, nr, p.x, p.cols, warp, lane, acc);
+      gemv_pass<BLOCK_BYTES, V, R, true, PRO>(base, (int)rb, nb, nr, X, warp, lane, acc);
     } else {
-      gemv_pass<BLOCK_BYTES, V, R, false>(base, (int)rb, nb, nr, p.x, p.cols, warp, lane, acc);
+      gemv_pass<BLOCK_BYTES, V, R, false, PRO>(base, (int)rb, nb, nr, X, warp, lane, acc);
     }
     float* part = partial + (it & 1) * (kGemvWarps * 16);
 #pragma unroll
@@ -254,13 +306,13 @@ __global__ void __launch_bounds__(kGemvThreads, gemv_ctas(V)) gemv_gguf_kernel(c
   }
 }
 
-template <int BLOCK_BYTES, int V>
+template <int BLOCK_BYTES, int V, int PRO = 0>
 cudaError_t launch_v(const GemvParams& p, int ctas_per_sm, int sm_count, int smem, cudaStream_t s) {
   // the largest staging any accepted shape needs (the host rejects longer
   // rows); each launch still asks for its own size
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_gguf_kernel<BLOCK_BYTES, V>,
+    cudaError_t e = cudaFuncSetAttribute(gemv_gguf_kernel<BLOCK_BYTES, V, PRO>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 128);
     if (e != cudaSuccess) return e;
     configured = true;
@@ -268,12 +320,14 @@ cudaError_t launch_v(const GemvParams& p, int ctas_per_sm, int sm_count, int sme
   const int n_groups = (p.rows + p.rows_per_group - 1) / p.rows_per_group;
   const int slots = ctas_per_sm * sm_count;
   const int grid = n_groups < slots ? n_groups : slots;
-  gemv_gguf_kernel<BLOCK_BYTES, V><<<grid, kGemvThreads, smem, s>>>(p);
+  gemv_gguf_kernel<BLOCK_BYTES, V, PRO><<<grid, kGemvThreads, smem, s>>>(p);
   return cudaGetLastError();
 }
 
 template <int BLOCK_BYTES>
 cudaError_t launch_b(const GemvParams& p, int n_vectors, int ctas_per_sm, int sm_count, int smem, cudaStream_t s) {
+  if (p.prologue == 1) return launch_v<BLOCK_BYTES, 1, 1>(p, ctas_per_sm, sm_count, smem, s);
+  if (p.prologue == 2) return launch_v<BLOCK_BYTES, 1, 2>(p, ctas_per_sm, sm_count, smem, s);
   switch (n_vectors) {
     case 1: return launch_v<BLOCK_BYTES, 1>(p, ctas_per_sm, sm_count, smem, s);
     case 2: return launch_v<BLOCK_BYTES, 2>(p, ctas_per_sm, sm_count, smem, s);

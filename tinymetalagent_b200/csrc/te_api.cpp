@@ -919,6 +919,45 @@ TE_API te_status te_matvec_gguf(te_attn_engine* e, uint32_t quant, const void* w
   return TE_STATUS_OK;
 }
 
+TE_API te_status te_matvec_gguf_fused(te_attn_engine* e, uint32_t quant, const void* w, size_t rows, size_t cols,
+                                      const float* x, const float* norm_weight, float eps, float* y, uint32_t flags) {
+  const uint32_t pro = flags & (TE_ATTN_RMSNORM_INPUT | TE_ATTN_SWIGLU_INPUT);
+  if (!e || !w || !x || !y || rows == 0 || cols == 0 || cols % 32 != 0 ||
+      (quant != TE_ATTN_QUANT_GGUF_Q4_0 && quant != TE_ATTN_QUANT_GGUF_Q8_0) ||
+      (flags & ~(TE_ATTN_ACCUMULATE | TE_ATTN_RMSNORM_INPUT | TE_ATTN_SWIGLU_INPUT)) ||
+      (pro != TE_ATTN_RMSNORM_INPUT && pro != TE_ATTN_SWIGLU_INPUT)) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  if (pro == TE_ATTN_RMSNORM_INPUT && (!norm_weight || !(eps > 0.0f))) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "RMSNorm input needs its weight and eps > 0");
+  }
+  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) |
+       (pro == TE_ATTN_RMSNORM_INPUT ? reinterpret_cast<uintptr_t>(norm_weight) : 0u)) & 15u) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "w, x and norm_weight must be 16-byte aligned");
+  }
+  const int block_bytes = quant == TE_ATTN_QUANT_GGUF_Q4_0 ? 18 : 34;
+  const size_t rb = cols / 32 * block_bytes;
+  if (rows > (size_t)INT32_MAX || cols > (size_t)INT32_MAX / 2 || 2 * (rb + 48) + 1280 > 227 * 1024) {
+    return fail(e, TE_STATUS_UNSUPPORTED, "matrix rows too long to stage");
+  }
+  DeviceGuard dg(e->device);
+  GemvParams p{};
+  p.w = w;
+  p.x = x;
+  p.y = y;
+  p.rows = (int32_t)rows;
+  p.cols = (int32_t)cols;
+  p.accumulate = (flags & TE_ATTN_ACCUMULATE) ? 1 : 0;
+  p.error = e->d_error;
+  p.prologue = pro == TE_ATTN_RMSNORM_INPUT ? 1 : 2;
+  p.norm_w = norm_weight;
+  p.eps = eps;
+  const cudaError_t err = launch_gemv_gguf(p, block_bytes, 1, e->sm_count, e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "matvec kernel launch");
+  e->launches++;
+  return TE_STATUS_OK;
+}
+
 static_assert(sizeof(cudaIpcMemHandle_t) == TE_ATTN_IPC_HANDLE_BYTES, "IPC handle size");
 
 TE_API te_status te_attn_exchange_create(te_attn_engine* e, size_t world, size_t rank, size_t rows, size_t head_dim,

@@ -259,6 +259,9 @@ struct GemvParams {
   int32_t stages;           // set by the launcher (2..4)
   int32_t accumulate;       // 1: y += W x (fp32 add of each finished dot product)
   int* error;               // engine error word (a staging wait that ran out)
+  int32_t prologue;         // 0: x as given; 1: RMSNorm(x) * norm_w; 2: SwiGLU of x = [gate | up] (one vector)
+  const float* norm_w;      // RMSNorm weight [cols] (prologue 1)
+  float eps;                // RMSNorm epsilon (prologue 1)
 };
 // block_bytes 18 (Q4_0) or 34 (Q8_0); 1 <= n_vectors <= 8.
 cudaError_t launch_gemv_gguf(GemvParams p, int block_bytes, int n_vectors, int sm_count, cudaStream_t s);

@@ -2,29 +2,21 @@
 
 Mirrors the reference's per-token forward pass, te_qwen_forward_token
 (c/src/qwen.c:907-1112), and its greedy projection, te_qwen_project_next
-(:1303-1377), on a GGUF model, with this repository's kernels on the hot
-path:
+(:1303-1377), on a GGUF model, with five launches of this library per layer:
 
-  per layer   RMSNorm(x, attn_norm)                          glue (below)
-              q|k|v = W_qkv n            one te_matvec_gguf over the q, k and v
-                                         rows stacked (they share the input)
-              bias + RoPE + f16 append + GQA decode
-                                         one te_attention_decode launch
-                                         (TE_ATTN_QKV_BIAS: the biases are added
-                                         in fp32 inside it, :998-1011)
-              x += W_o attn              te_matvec_gguf + TE_ATTN_ACCUMULATE
-              RMSNorm(x, ffn_norm)                           glue
-              g|u = W_gate|up n          one te_matvec_gguf (rows stacked)
-              s = SwiGLU(g, u)                               glue
-              x += W_down s              te_matvec_gguf + TE_ATTN_ACCUMULATE
-  head        RMSNorm(x, output_norm); logits = W_out n (te_matvec_gguf); argmax
+  q|k|v = W_qkv RMSNorm(x)   te_matvec_gguf_fused (TE_ATTN_RMSNORM_INPUT) over
+                             the q, k and v rows stacked (they share the input)
+  bias + RoPE + f16 append + GQA decode
+                             one te_attention_decode launch (TE_ATTN_QKV_BIAS:
+                             the biases added in fp32 inside it, :998-1011)
+  x += W_o attn              te_matvec_gguf + TE_ATTN_ACCUMULATE
+  g|u = W_gate|up RMSNorm(x) te_matvec_gguf_fused (RMSNorm), rows stacked
+  x += W_down SwiGLU(g, u)   te_matvec_gguf_fused (TE_ATTN_SWIGLU_INPUT +
+                             TE_ATTN_ACCUMULATE)
 
-The glue -- the embedding row, RMSNorm, SwiGLU, argmax -- is elementwise work
-on a few thousand values per token, done with device tensor operations in the
-reference's arithmetic: RMSNorm sums squares in double, then
-scale = 1 / sqrt(float(mean) + eps) and out = (x * scale) * w (te_rmsnorm_f32,
-ops.c:272-293); SwiGLU is g / (1 + exp(-g)) * u (te_swiglu_f32, ops.c:397-406);
-argmax takes the first maximum (te_argmax_f32).
+and for the head logits = W_out RMSNorm(x) (one fused launch) and the argmax
+(first maximum, as te_argmax_f32).  The embedding table is dequantised once
+into fp32 in HBM (q * scale, exact), so a token's row is a copy.
 
 One difference from the reference's CPU pass is by design: the KV cache is
 the engine's f16 cache (the reference's Metal path's layout), where the CPU
@@ -38,7 +30,8 @@ from pathlib import Path
 import numpy as np
 
 from .gguf import GGML_F32, GGML_Q4_0, GGML_Q8_0, GGUFError, GGUFFile
-from .runtime import TE_ATTN_ACCUMULATE, TE_ATTN_ADVANCE, TE_ATTN_QKV_BIAS, AttnEngine
+from .runtime import (TE_ATTN_ACCUMULATE, TE_ATTN_ADVANCE, TE_ATTN_QKV_BIAS, TE_ATTN_RMSNORM_INPUT,
+                      TE_ATTN_SWIGLU_INPUT, AttnEngine)
 
 _QUANT = {GGML_Q4_0: 4, GGML_Q8_0: 8}  # ggml type -> TE_ATTN_QUANT_GGUF_*
 
@@ -51,6 +44,8 @@ class QwenDecoder:
     or restart below the current length, which truncates the cache there) and
     returns the hidden state (a device tensor [hidden]); project_next()
     returns the greedy next token and leaves the logits in `self.logits`.
+    Work runs on the engine's stream; before returning, both make the
+    caller's current stream wait for it, so the results can be used there.
     """
 
     def __init__(self, engine: AttnEngine, model: str | Path | GGUFFile, context_tokens: int):
@@ -125,8 +120,7 @@ class QwenDecoder:
         emb = t["token_embd.weight"]
         if emb.ggml_type not in (GGML_Q8_0, GGML_Q4_0, GGML_F32):
             raise GGUFError("token_embd.weight: unsupported type")
-        self._emb_type = emb.ggml_type
-        self._emb = raw("token_embd.weight")
+        self._emb = self._dequant_table(raw("token_embd.weight"), emb.ggml_type, d["vocab"], H)
         head = "output.weight" if "output.weight" in t else "token_embd.weight"
         self._head = raw(head)
         self._q_head = quant_of(head)
@@ -142,40 +136,50 @@ class QwenDecoder:
         self._gu = torch.empty(2 * F, dtype=torch.float32, device=dev)
         self.logits = torch.empty(d["vocab"], dtype=torch.float32, device=dev)
 
-    # ---- glue (reference arithmetic) ---------------------------------------
-    def _rmsnorm(self, x, w):
+    # ---- embedding table ----------------------------------------------------
+    @staticmethod
+    def _dequant_table(raw, ggml_type, rows, cols):
+        """[rows][cols] fp32 from GGUF bytes, as te_model_dequantize_row_f32:
+        q * scale (Q8_0), (q - 8) * scale (Q4_0; low nibbles are weights 0-15
+        of a block, high nibbles 16-31) -- exact products in fp32."""
         import torch
-        ss = torch.sum(x.double() * x.double())
-        scale = 1.0 / torch.sqrt((ss / x.numel()).float() + self.dims["eps"])
-        return (x * scale) * w
+        if ggml_type == GGML_F32:
+            return raw.view(torch.float32).view(rows, cols).clone()
+        width = 34 if ggml_type == GGML_Q8_0 else 18
+        blocks = raw.view(rows, cols // 32, width)
+        out = torch.empty((rows, cols), dtype=torch.float32, device=raw.device)
+        step = 8192
+        for r0 in range(0, rows, step):
+            b = blocks[r0:r0 + step]
+            scale = b[:, :, 0:2].contiguous().view(torch.float16).float()  # [n, blocks, 1]
+            if ggml_type == GGML_Q8_0:
+                q = b[:, :, 2:].contiguous().view(torch.int8).float()
+            else:
+                c = b[:, :, 2:].to(torch.int32)
+                q = torch.cat([c & 0x0F, c >> 4], dim=2).float() - 8.0
+            out[r0:r0 + step] = (q * scale).reshape(-1, cols)
+        return out
 
-    def _embed(self, token: int):
-        import torch
-        H = self.dims["hidden"]
-        if self._emb_type == GGML_F32:
-            return self._emb.view(torch.float32).view(-1, H)[token].clone()
-        width = 34 if self._emb_type == GGML_Q8_0 else 18
-        row = self._emb.view(-1, H // 32, width)[token]
-        scale = row[:, 0:2].contiguous().view(torch.float16).float()  # [blocks, 1]
-        if self._emb_type == GGML_Q8_0:
-            q = row[:, 2:].contiguous().view(torch.int8).float()
-        else:
-            b = row[:, 2:].to(torch.int32)
-            q = torch.cat([b & 0x0F, b >> 4], dim=1).float() - 8.0
-        return (q * scale).reshape(H)
+    def _embed(self, token):
+        """The token's fp32 row; token is an int or a one-element device tensor
+        (the graph-captured steps read it from device memory)."""
+        return self._emb[token] if isinstance(token, int) else self._emb.index_select(0, token)[0]
 
     # ---- the step ----------------------------------------------------------
     def forward_token(self, token: int, position: int):
         import torch
         with torch.cuda.stream(self._stream):
-            return self._forward(token, position)
+            x = self._forward(token, position)
+        # the caller's stream sees x only after the engine's stream wrote it
+        torch.cuda.current_stream(self._dev).wait_stream(self._stream)
+        return x
 
     def _forward(self, token: int, position: int):
         import torch
         d = self.dims
         H, F, L = d["hidden"], d["ffn"], d["layers"]
         heads, kvh, hd = d["heads"], d["kv_heads"], d["head_dim"]
-        if not 0 <= token < d["vocab"]:
+        if isinstance(token, int) and not 0 <= token < d["vocab"]:
             raise ValueError("token outside the vocabulary")
         if position >= self.context_tokens:
             raise ValueError("position beyond context_tokens")
@@ -185,10 +189,11 @@ class QwenDecoder:
         if position < n:
             self.cache.truncate(0, position)
         eng = self.engine
+        eps = d["eps"]
         self.x.copy_(self._embed(token))
         for layer, w in enumerate(self.layers):
-            nrm = self._rmsnorm(self.x, w["attn_norm"])
-            eng.matvec_gguf(w["q_qkv"], w["qkv"], H + 2 * self.kv, H, nrm, self._qkv)
+            eng.matvec_gguf_fused(w["q_qkv"], w["qkv"], H + 2 * self.kv, H, self.x, self._qkv, TE_ATTN_RMSNORM_INPUT,
+                                  w["attn_norm"], eps)
             q = self._qkv[:H].view(1, 1, heads, hd)
             k = self._qkv[H:H + self.kv].view(1, 1, kvh, hd)
             v = self._qkv[H + self.kv:].view(1, 1, kvh, hd)
@@ -196,23 +201,83 @@ class QwenDecoder:
             self.cache.decode(layer, 1, [0], q, self._attn.view(1, 1, heads, hd), heads, k_new=k, v_new=v,
                               flags=flags)
             eng.matvec_gguf(w["q_o"], w["o"], H, H, self._attn, self.x, flags=TE_ATTN_ACCUMULATE)
-            nrm = self._rmsnorm(self.x, w["ffn_norm"])
-            eng.matvec_gguf(w["q_gu"], w["gu"], 2 * F, H, nrm, self._gu)
-            g, u = self._gu[:F], self._gu[F:]
-            s = (g / (1.0 + torch.exp(-g))) * u
-            eng.matvec_gguf(w["q_down"], w["down"], H, F, s, self.x, flags=TE_ATTN_ACCUMULATE)
+            eng.matvec_gguf_fused(w["q_gu"], w["gu"], 2 * F, H, self.x, self._gu, TE_ATTN_RMSNORM_INPUT,
+                                  w["ffn_norm"], eps)
+            eng.matvec_gguf_fused(w["q_down"], w["down"], H, F, self._gu, self.x,
+                                  TE_ATTN_SWIGLU_INPUT | TE_ATTN_ACCUMULATE)
         return self.x
 
     def project_next(self) -> int:
         import torch
         d = self.dims
         with torch.cuda.stream(self._stream):
-            nrm = self._rmsnorm(self.x, self._out_norm)
-            self.engine.matvec_gguf(self._q_head, self._head, d["vocab"], d["hidden"], nrm, self.logits)
-            best = torch.argmax(self.logits)
-        return int(best.item())
+            self._head_logits()
+            best = int(torch.argmax(self.logits).item())  # read back in the engine stream's order
+        torch.cuda.current_stream(self._dev).wait_stream(self._stream)
+        return best
+
+    def _head_logits(self) -> None:
+        d = self.dims
+        self.engine.matvec_gguf_fused(self._q_head, self._head, d["vocab"], d["hidden"], self.x, self.logits,
+                                      TE_ATTN_RMSNORM_INPUT, self._out_norm, d["eps"])
+
+    # ---- many steps as one CUDA graph ----------------------------------------
+    def capture_greedy(self, start_position: int, n_steps: int) -> None:
+        """Record n_steps greedy decode steps as one CUDA graph.  Step i reads
+        its token from the device tensor self.tokens[i], runs every layer at
+        position start_position + i and writes the argmax of its logits to
+        self.tokens[i + 1]: no host work between steps.  The sequence must
+        already hold start_position tokens.  Every position of the window is
+        first run eagerly once (mapping its cache pages and sizing the
+        engine's scratch, so that nothing is allocated while recording); the
+        graph's kernel arguments fix the positions, so each replay restarts
+        at start_position.  Afterwards the cache's length counts the window."""
+        import torch
+        if n_steps < 1 or start_position + n_steps > self.context_tokens:
+            raise ValueError("window beyond context_tokens")
+        if self.cache.length(0) < start_position:
+            raise ValueError("the sequence does not hold start_position tokens yet")
+        self.cache.reserve(0, start_position + n_steps)
+        for i in range(n_steps):  # eager pass over the window
+            self.forward_token(0, start_position + i)
+        self.project_next()
+        with torch.cuda.stream(self._stream):
+            self.tokens = torch.zeros(n_steps + 1, dtype=torch.int64, device=self._dev)
+        self._stream.synchronize()
+        self.cache.truncate(0, start_position)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self._stream):
+            for i in range(n_steps):
+                self._forward(self.tokens[i:i + 1], start_position + i)
+                self._head_logits()
+                self.tokens[i + 1:i + 2].copy_(torch.argmax(self.logits).reshape(1))
+        self._graph = graph
+        self._graph_window = (start_position, n_steps)
+
+    def replay_greedy(self, first_token: int):
+        """Run the captured window from its start with first_token as the token
+        at start_position; returns self.tokens (device; tokens[1:] are the
+        greedy choices), ordered before the caller's stream.  The recording
+        already counted the window in the cache's length, and each replay
+        rewrites those positions, so eager steps may follow a replay at
+        start_position + n_steps; a cache changed since the recording (other
+        steps, a truncation) is refused."""
+        import torch
+        if getattr(self, "_graph", None) is None:
+            raise RuntimeError("capture_greedy first")
+        if not 0 <= first_token < self.dims["vocab"]:
+            raise ValueError("token outside the vocabulary")
+        start, n = self._graph_window
+        if self.cache.length(0) != start + n:
+            raise RuntimeError("the cache changed since the capture; capture again")
+        with torch.cuda.stream(self._stream):
+            self.tokens[0:1].fill_(first_token)
+            self._graph.replay()
+        torch.cuda.current_stream(self._dev).wait_stream(self._stream)
+        return self.tokens
 
     def close(self) -> None:
+        self._graph = None
         if getattr(self, "cache", None) is not None:
             self.cache.close()
             self.cache = None

@@ -34,6 +34,8 @@ TE_ATTN_INPUT_F16 = 1 << 3
 TE_ATTN_HOST_BUFFERS = 1 << 4
 TE_ATTN_QKV_BIAS = 1 << 5
 TE_ATTN_ACCUMULATE = 1 << 6
+TE_ATTN_RMSNORM_INPUT = 1 << 7
+TE_ATTN_SWIGLU_INPUT = 1 << 8
 TE_ATTN_QUANT_GGUF_Q4_0 = 4
 TE_ATTN_QUANT_GGUF_Q8_0 = 8
 
@@ -118,6 +120,8 @@ SIGNATURES: dict[str, tuple] = {
     "te_attention_decode": (_int, [_vp, _sz, _sz, _u32p, _sz, _i64p, _vp, _vp, _vp, _sz, _vp, ctypes.c_uint32]),
     "te_attention_merge_partials": (_int, [_vp, _vp, _sz, _sz, _sz, _vp, ctypes.c_uint32]),
     "te_matvec_gguf": (_int, [_vp, ctypes.c_uint32, _vp, _sz, _sz, _vp, _sz, _vp, ctypes.c_uint32]),
+    "te_matvec_gguf_fused": (_int, [_vp, ctypes.c_uint32, _vp, _sz, _sz, _vp, _vp, ctypes.c_float, _vp,
+                                    ctypes.c_uint32]),
     "te_attn_exchange_create": (_int, [_vp, _sz, _sz, _sz, _sz, ctypes.POINTER(_vp), _vp]),
     "te_attn_exchange_connect": (_int, [_vp, _vp]),
     "te_attn_exchange_merge": (_int, [_vp, _vp, _vp]),
@@ -264,6 +268,13 @@ class AttnEngine:
 
     def kv_cache(self, **kw) -> "KVCache":
         return KVCache(self, **kw)
+
+    def matvec_gguf_fused(self, quant: int, w, rows: int, cols: int, x, y, flags: int, norm_weight=None,
+                          eps: float = 0.0) -> None:
+        """One vector: y = W p(x) (or y += that, with TE_ATTN_ACCUMULATE), p the RMSNorm (TE_ATTN_RMSNORM_INPUT,
+        with norm_weight and eps) or the SwiGLU of x = [gate | up] (TE_ATTN_SWIGLU_INPUT)."""
+        self.check(self.lib.te_matvec_gguf_fused(self.handle, quant, _addr(w), rows, cols, _addr(x),
+                                                 _addr(norm_weight), eps, _addr(y), flags))
 
     def matvec_gguf(self, quant: int, w, rows: int, cols: int, x, y, n_vectors: int = 1, flags: int = 0) -> None:
         """y[v][r] = sum_c W[r][c] x[v][c] (or y += that, with TE_ATTN_ACCUMULATE) for a GGUF Q4_0 / Q8_0
