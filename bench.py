@@ -228,9 +228,10 @@ def run_gpu(args) -> None:
     hbm_peak, tc_peak, peak_src = load_peaks()
     eng = AttnEngine(local, decode_chunk_tokens=args.chunk)
     stream = torch.cuda.ExternalStream(eng.stream)
-    if args.gemv_only:
-        # the matrix-vector measurement alone (e.g. under a profiler): one JSON line
-        res = run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank)
+    if args.gemv_only or args.qwen_only:
+        # one measurement alone (e.g. under a profiler): one JSON line
+        res = (run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank) if args.gemv_only
+               else run_qwen(eng, stream, hbm_peak, peak_src, args))
         eng.close()
         if rank == 0:
             print(json.dumps(res))
@@ -927,6 +928,8 @@ def main() -> None:
     ap.add_argument("--no-gemv", action="store_true", help="skip the GGUF matrix-vector measurement")
     ap.add_argument("--no-qwen", action="store_true", help="skip the qwen2 decode-step measurement")
     ap.add_argument("--qwen-steps", type=int, default=64, help="decode steps timed for the qwen2 decode step")
+    ap.add_argument("--qwen-only", action="store_true",
+                    help="run only the qwen2 decode-step measurement (121 library launches per token)")
     ap.add_argument("--gemv-only", action="store_true",
                     help="run only the GGUF matrix-vector measurement (Q4_0: launches 1-23, Q8_0: 24-46)")
     ap.add_argument("--cfg-steps", type=int, default=16, help="decode steps timed for config 4")

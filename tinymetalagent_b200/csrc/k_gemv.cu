@@ -189,6 +189,51 @@ __global__ void __launch_bounds__(kGemvThreads, gemv_ctas(V)) gemv_gguf_kernel(c
     fence_mbarrier_init();
     s_abort = 0;
   }
+  // Launched as a programmatic dependent: until griddep_wait the previous
+  // kernel on the stream may still run, so before it this CTA only asks L2
+  // for the weight bytes of its first groups (no memory state it could race
+  // with); x, y and the staging copies come after.  The next kernel may be
+  // scheduled as soon as every CTA has started.
+  if (threadIdx.x == 0) {
+    for (int s = 0; s + 1 < n_stages; ++s) {
+      const int g = blockIdx.x + s * gridDim.x;
+      if (g >= n_groups) break;
+      const long long lo16 = ((long long)g * rows_per_group * rb) & ~15ll;
+      const long long hi16 = min(((long long)min(p.rows, (g + 1) * rows_per_group) * rb + 15) & ~15ll, total16);
+      if (hi16 > lo16) bulk_prefetch_l2(w + lo16, (uint32_t)(hi16 - lo16));
+    }
+  }
+  griddep_launch_dependents();
+  griddep_wait();
+  // one thread: stage group g; the copy covers [lo rounded down to 16, hi
+  // rounded up to 16) clipped to the matrix's last 16-byte boundary, and the
+  // bytes past that boundary (last group only) arrive by plain loads before
+  // the mbarrier arrival that publishes them
+  auto issue = [&](int g, int stage) {
+    const long long lo = (long long)g * rows_per_group * rb;
+    const long long hi = min((long long)p.rows, (long long)(g + 1) * rows_per_group) * rb;
+    const long long lo16 = lo & ~15ll;
+    const long long hi16 = min((hi + 15) & ~15ll, total16);
+    unsigned char* dst = stages + (size_t)stage * p.stage_bytes;
+    for (long long t = hi16 > lo16 ? hi16 : lo16; t < hi; t += 2) {
+      *reinterpret_cast<uint16_t*>(dst + (t - lo16)) = __ldg(reinterpret_cast<const uint16_t*>(w + t));
+    }
+    if (hi16 > lo16) {
+      mbar_arrive_expect_tx(&full[stage], (uint32_t)(hi16 - lo16));
+      bulk_load(dst, w + lo16, (uint32_t)(hi16 - lo16), &full[stage]);
+    } else {
+      mbar_arrive(&full[stage]);
+    }
+  };
+
+  // the first stages' copies start before the input's prologue runs
+  if (threadIdx.x == 0) {
+    for (int s = 0; s + 1 < n_stages; ++s) {
+      const int g = blockIdx.x + s * gridDim.x;
+      if (g < n_groups) issue(g, s);
+    }
+  }
+
   GemvInput X{p.x, p.norm_w, 1.0f, p.cols};
   if (PRO == 1) {
     // RMSNorm scale of the (single) input vector, as te_rmsnorm_f32 forms it
@@ -216,33 +261,6 @@ __global__ void __launch_bounds__(kGemvThreads, gemv_ctas(V)) gemv_gguf_kernel(c
   __syncthreads();
   if (PRO == 1) X.scale = *reinterpret_cast<const float*>(gsm + kGemvScaleOffset);
 
-  // one thread: stage group g; the copy covers [lo rounded down to 16, hi
-  // rounded up to 16) clipped to the matrix's last 16-byte boundary, and the
-  // bytes past that boundary (last group only) arrive by plain loads before
-  // the mbarrier arrival that publishes them
-  auto issue = [&](int g, int stage) {
-    const long long lo = (long long)g * rows_per_group * rb;
-    const long long hi = min((long long)p.rows, (long long)(g + 1) * rows_per_group) * rb;
-    const long long lo16 = lo & ~15ll;
-    const long long hi16 = min((hi + 15) & ~15ll, total16);
-    unsigned char* dst = stages + (size_t)stage * p.stage_bytes;
-    for (long long t = hi16 > lo16 ? hi16 : lo16; t < hi; t += 2) {
-      *reinterpret_cast<uint16_t*>(dst + (t - lo16)) = __ldg(reinterpret_cast<const uint16_t*>(w + t));
-    }
-    if (hi16 > lo16) {
-      mbar_arrive_expect_tx(&full[stage], (uint32_t)(hi16 - lo16));
-      bulk_load(dst, w + lo16, (uint32_t)(hi16 - lo16), &full[stage]);
-    } else {
-      mbar_arrive(&full[stage]);
-    }
-  };
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s + 1 < n_stages; ++s) {
-      const int g = blockIdx.x + s * gridDim.x;
-      if (g < n_groups) issue(g, s);
-    }
-  }
 
   int it = 0;
   for (int g = blockIdx.x; g < n_groups; g += gridDim.x, ++it) {
@@ -320,8 +338,19 @@ cudaError_t launch_v(const GemvParams& p, int ctas_per_sm, int sm_count, int sme
   const int n_groups = (p.rows + p.rows_per_group - 1) / p.rows_per_group;
   const int slots = ctas_per_sm * sm_count;
   const int grid = n_groups < slots ? n_groups : slots;
-  gemv_gguf_kernel<BLOCK_BYTES, V, PRO><<<grid, kGemvThreads, smem, s>>>(p);
-  return cudaGetLastError();
+  // programmatic dependent launch (the kernel waits before touching any
+  // memory the previous kernel may write)
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_gguf_kernel<BLOCK_BYTES, V, PRO>, p);
 }
 
 template <int BLOCK_BYTES>
