@@ -46,8 +46,9 @@ def quant_blocks(rng, ggml_type: int, rows: int, cols: int, sigma: float) -> np.
 
 
 def write_qwen2(path: Path, *, layers=2, hidden=256, heads=4, kv_heads=2, ffn=512, vocab=512, context=128,
-                quant_attn=GGML_Q8_0, quant_ffn=GGML_Q4_0, seed=1, rope_base=1e6, eps=1e-6) -> dict:
-    """Write the model; returns its dimensions."""
+                quant_attn=GGML_Q8_0, quant_ffn=GGML_Q4_0, seed=1, rope_base=1e6, eps=1e-6, tied=False) -> dict:
+    """Write the model; returns its dimensions.  tied: no output.weight, so the lm_head is
+    token_embd.weight (as in Qwen2.5-0.5B; the reference falls back to it, qwen.c:1305)."""
     rng = np.random.default_rng(seed)
     hd = hidden // heads
     kv = kv_heads * hd
@@ -75,7 +76,8 @@ def write_qwen2(path: Path, *, layers=2, hidden=256, heads=4, kv_heads=2, ffn=51
         mat(p + "ffn_up.weight", quant_ffn, ffn, hidden, 1.0 / np.sqrt(hidden))
         mat(p + "ffn_down.weight", quant_ffn, hidden, ffn, 0.5 / np.sqrt(ffn))
     vec("output_norm.weight", 1.0 + 0.1 * rng.standard_normal(hidden))
-    mat("output.weight", GGML_Q8_0, vocab, hidden, 4.0 / np.sqrt(hidden))  # logits O(4): clear greedy margins
+    if not tied:
+        mat("output.weight", GGML_Q8_0, vocab, hidden, 4.0 / np.sqrt(hidden))  # logits O(4): clear greedy margins
 
     kvs = [
         ("general.architecture", _T_STRING, "qwen2"),

@@ -30,6 +30,9 @@ MODELS = {
     # hidden 512, 4 heads of 128, 1 KV head (group 4); Q4_0 attention, Q8_0 MLP
     "hd128": dict(layers=3, hidden=512, heads=4, kv_heads=1, ffn=1024, vocab=640, quant_attn=GGML_Q4_0,
                   quant_ffn=GGML_Q8_0, seed=12),
+    # tied embeddings: no output.weight, the lm_head is token_embd.weight; 7 query heads per KV head
+    "tied": dict(layers=2, hidden=448, heads=7, kv_heads=1, ffn=640, vocab=384, quant_attn=GGML_Q8_0,
+                 quant_ffn=GGML_Q4_0, seed=13, tied=True),
 }
 
 
