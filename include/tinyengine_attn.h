@@ -223,14 +223,14 @@ TE_API te_status te_attention_merge_partials(te_attn_engine *engine, const float
 TE_API te_status te_matvec_gguf(te_attn_engine *engine, uint32_t quant, const void *w, size_t rows,
                                 size_t cols, const float *x, size_t n_vectors, float *y, uint32_t flags);
 
-/* The same product for ONE input vector with the elementwise step that the
- * reference runs just before it fused into the input reads:
+/* The same product (n_vectors 1..8) with the elementwise step that the
+ * reference runs just before it fused into the input reads, per vector:
  *   TE_ATTN_RMSNORM_INPUT: the input is te_rmsnorm_f32(x, norm_weight, eps)
  *     (c/src/ops.c:272-293: squares summed in double, scale =
  *     1 / sqrtf((float)(sum / cols) + eps), (x[c] * scale) * norm_weight[c]),
  *     which precedes the q/k/v, gate/up and lm_head projections
  *     (c/src/qwen.c:965-971, :1082-1088, :1350-1356);
- *   TE_ATTN_SWIGLU_INPUT: x holds [gate | up] (2 * cols values) and the input
+ *   TE_ATTN_SWIGLU_INPUT: x holds [gate | up] per vector (x [n_vectors][2 * cols]) and the input
  *     is te_swiglu_f32(gate, up) (ops.c:397-406: gate / (1 + expf(-gate)) *
  *     up), which precedes the down projection (qwen.c:1933-1941).
  * Exactly one of the two, optionally with TE_ATTN_ACCUMULATE.  norm_weight
@@ -239,8 +239,8 @@ TE_API te_status te_matvec_gguf(te_attn_engine *engine, uint32_t quant, const vo
  * reference's (in double), and expf is the device's, so results agree to
  * fp32 rounding. */
 TE_API te_status te_matvec_gguf_fused(te_attn_engine *engine, uint32_t quant, const void *w, size_t rows,
-                                      size_t cols, const float *x, const float *norm_weight, float eps,
-                                      float *y, uint32_t flags);
+                                      size_t cols, const float *x, size_t n_vectors, const float *norm_weight,
+                                      float eps, float *y, uint32_t flags);
 
 /* KV-split exchange over NVLink --------------------------------------------
  *

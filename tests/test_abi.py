@@ -80,7 +80,7 @@ def test_engine_api_null_guards(lib):
     assert lib.te_attn_exchange_connect(None, None) == R.TE_STATUS_INVALID_ARGUMENT
     assert lib.te_attn_exchange_merge(None, None, None) == R.TE_STATUS_INVALID_ARGUMENT
     assert lib.te_matvec_gguf(None, 4, None, 1, 32, None, 1, None, 0) == R.TE_STATUS_INVALID_ARGUMENT
-    assert lib.te_matvec_gguf_fused(None, 4, None, 1, 32, None, None, 1e-6, None, R.TE_ATTN_RMSNORM_INPUT) == \
+    assert lib.te_matvec_gguf_fused(None, 4, None, 1, 32, None, 1, None, 1e-6, None, R.TE_ATTN_RMSNORM_INPUT) == \
         R.TE_STATUS_INVALID_ARGUMENT
     lib.te_attn_exchange_free(None)
     lib.te_attn_engine_free(None)

@@ -144,55 +144,62 @@ def test_matvec_residual_accumulate(port, quant):
 
 
 @pytest.mark.parametrize("quant", [Q4, Q8])
-@pytest.mark.parametrize("shape", [(896 + 256, 896), (4864 * 2, 896), (300, 2048), (7, 160)])
+@pytest.mark.parametrize("shape", [(896 + 256, 896, 1), (4864 * 2, 896, 3), (300, 2048, 8), (7, 160, 2)])
 def test_matvec_fused_rmsnorm_input(port, quant, shape):
-    """te_matvec_gguf_fused + TE_ATTN_RMSNORM_INPUT: y = W te_rmsnorm_f32(x, w_norm, eps) (c/src/ops.c:272-293:
-    double sum of squares, fp32 scale, (x * scale) * w)."""
+    """te_matvec_gguf_fused + TE_ATTN_RMSNORM_INPUT: y[v] = W te_rmsnorm_f32(x[v], w_norm, eps) (c/src/ops.c:272-293:
+    double sum of squares, fp32 scale, (x * scale) * w), one scale per vector."""
     import torch
     from tinymetalagent_b200 import TE_ATTN_RMSNORM_INPUT, AttnEngine
-    rows, cols = shape
-    rng = np.random.default_rng(rows + cols + quant)
+    rows, cols, nv = shape
+    rng = np.random.default_rng(rows + cols + quant + nv)
     w = quant_matrix(rng, GGML[quant], rows, cols)
-    x = (rng.standard_normal(cols) * 3.0).astype(np.float32)
+    x = (rng.standard_normal((nv, cols)) * rng.uniform(0.5, 4.0, (nv, 1))).astype(np.float32)
     nw = (1.0 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
     eps = np.float32(1e-6)
-    ss = np.sum(x.astype(np.float64) ** 2)
-    scale = np.float32(1.0) / np.sqrt(np.float32(ss / cols) + eps)
-    xn = ((x * scale) * nw).astype(np.float32)
+    xn = np.empty_like(x)
+    for v in range(nv):
+        ss = np.sum(x[v].astype(np.float64) ** 2)
+        scale = np.float32(1.0) / np.sqrt(np.float32(ss / cols) + eps)
+        xn[v] = (x[v] * scale) * nw
     eng = AttnEngine(0)
     try:
-        y = torch.full((1, rows), float("nan"), dtype=torch.float32, device="cuda")
-        eng.matvec_gguf_fused(quant, dev(w), rows, cols, dev(x), y, TE_ATTN_RMSNORM_INPUT, dev(nw), float(eps))
+        y = torch.full((nv, rows), float("nan"), dtype=torch.float32, device="cuda")
+        eng.matvec_gguf_fused(quant, dev(w), rows, cols, dev(x), y, TE_ATTN_RMSNORM_INPUT, dev(nw), float(eps),
+                              n_vectors=nv)
         eng.synchronize()
-        check(port, quant, w, rows, cols, xn[None], y.cpu().numpy())
+        check(port, quant, w, rows, cols, xn, y.cpu().numpy())
     finally:
         eng.close()
 
 
 @pytest.mark.parametrize("quant", [Q4, Q8])
-@pytest.mark.parametrize("shape", [(896, 4864), (2048, 2048), (33, 96)])
+@pytest.mark.parametrize("shape", [(896, 4864, 1), (2048, 2048, 4), (33, 96, 8)])
 def test_matvec_fused_swiglu_input_accumulate(port, quant, shape):
-    """te_matvec_gguf_fused + TE_ATTN_SWIGLU_INPUT + TE_ATTN_ACCUMULATE: y += W te_swiglu_f32(gate, up)
-    (ops.c:397-406), x = [gate | up] -- the down projection and its residual add (qwen.c:1933-1941, :1105-1108)."""
+    """te_matvec_gguf_fused + TE_ATTN_SWIGLU_INPUT + TE_ATTN_ACCUMULATE: y[v] += W te_swiglu_f32(gate, up)
+    (ops.c:397-406), x[v] = [gate | up] -- the down projection and its residual add (qwen.c:1933-1941,
+    :1105-1108)."""
     import torch
     from tinymetalagent_b200 import TE_ATTN_ACCUMULATE, TE_ATTN_SWIGLU_INPUT, AttnEngine
-    rows, cols = shape
-    rng = np.random.default_rng(3 * rows + cols + quant)
+    rows, cols, nv = shape
+    rng = np.random.default_rng(3 * rows + cols + quant + nv)
     w = quant_matrix(rng, GGML[quant], rows, cols)
-    gu = (rng.standard_normal(2 * cols) * 2.0).astype(np.float32)
-    g, u = gu[:cols], gu[cols:]
-    s = ((g / (np.float32(1.0) + np.exp(-g))) * u).astype(np.float32)
-    res = rng.standard_normal(rows).astype(np.float32)
+    gu = (rng.standard_normal((nv, 2 * cols)) * 2.0).astype(np.float32)
+    res = rng.standard_normal((nv, rows)).astype(np.float32)
     eng = AttnEngine(0)
     try:
-        y = dev(res[None])
-        eng.matvec_gguf_fused(quant, dev(w), rows, cols, dev(gu), y, TE_ATTN_SWIGLU_INPUT | TE_ATTN_ACCUMULATE)
+        y = dev(res)
+        eng.matvec_gguf_fused(quant, dev(w), rows, cols, dev(gu), y, TE_ATTN_SWIGLU_INPUT | TE_ATTN_ACCUMULATE,
+                              n_vectors=nv)
         eng.synchronize()
+        got = y.cpu().numpy()
         ref_fn = port.matvec_q4_0_f32 if quant == Q4 else port.matvec_q8_0_f32
-        exp = (res + ref_fn(w, rows, cols, s)).astype(np.float32)
         wd = np.abs(dequant(quant, w, rows, cols))
-        bound = 2e-5 * (wd @ np.abs(s)) + 1e-6 + 1e-7 * np.abs(exp)  # fp32 sums + device expf (a few ulp)
-        assert (np.abs(y.cpu().numpy()[0] - exp) <= bound).all()
+        for v in range(nv):
+            g, u = gu[v, :cols], gu[v, cols:]
+            s = ((g / (np.float32(1.0) + np.exp(-g))) * u).astype(np.float32)
+            exp = (res[v] + ref_fn(w, rows, cols, s)).astype(np.float32)
+            bound = 2e-5 * (wd @ np.abs(s)) + 1e-6 + 1e-7 * np.abs(exp)  # fp32 sums + device expf (a few ulp)
+            assert (np.abs(got[v] - exp) <= bound).all(), v
     finally:
         eng.close()
 

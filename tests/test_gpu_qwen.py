@@ -154,3 +154,43 @@ def test_graph_replay_matches_eager_steps(tmp_path):
         torch.cuda.synchronize()
     finally:
         eng.close()
+
+
+def test_prefill_prompt_matches_reference(tmp_path):
+    """prefill_prompt (head_dim 128: batched projections + one te_attention_prefill launch per layer) against
+    the reference's token-by-token forward pass; then greedy steps continue from the prefilled cache, and a
+    prompt prefilled in two calls (the second over the first's cache) gives the same state."""
+    from oracle import oracle as O
+    if not O.ref_qwen_available():
+        pytest.skip("reference forward pass not built")
+    from tinymetalagent_b200 import AttnEngine
+    from tinymetalagent_b200.qwen import QwenDecoder
+    path = tmp_path / "m.gguf"
+    write_qwen2(path, **MODELS["hd128"])
+    prompt = [int(t) for t in np.random.default_rng(21).integers(0, 640, 21)]
+    ctx = 40
+    ref = O.RefQwen(path, ctx)
+    eng = AttnEngine(0)
+    try:
+        for pos, t in enumerate(prompt):
+            h_ref = ref.forward(t, pos)
+        dec = QwenDecoder(eng, path, ctx)
+        h = dec.prefill_prompt(prompt).cpu().numpy()
+        close(h, h_ref, 2e-2, 2e-2, "hidden after the prompt")
+        for pos in range(len(prompt), len(prompt) + 8):
+            logits_ref, tok_ref = ref.project()
+            tok = dec.project_next()
+            close(dec.logits.cpu().numpy(), logits_ref, 5e-2, 2e-2, f"logits after position {pos - 1}")
+            assert margin(logits_ref) > 0.1 and tok == tok_ref, f"greedy token at position {pos}"
+            h_ref = ref.forward(tok_ref, pos)
+            close(dec.forward_token(tok, pos).cpu().numpy(), h_ref, 2e-2, 2e-2, f"hidden at position {pos}")
+        dec.close()
+
+        two = QwenDecoder(eng, path, ctx)
+        two.prefill_prompt(prompt[:12])
+        h2 = two.prefill_prompt(prompt[12:], position=12).cpu().numpy()
+        np.testing.assert_allclose(h2, h, rtol=2e-3, atol=2e-3)
+        two.close()
+    finally:
+        eng.close()
+        ref.close()

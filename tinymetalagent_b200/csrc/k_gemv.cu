@@ -39,7 +39,7 @@ constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kGemvMaxStages = 4;
 constexpr int kGemvHeader = 64;                          // the stages' mbarriers, then the RMSNorm scale
-constexpr int kGemvScaleOffset = 8 * kGemvMaxStages;
+constexpr int kGemvScaleOffset = 8 * kGemvMaxStages;  // up to 8 scales (32 bytes)
 constexpr int kGemvPartialFloats = 2 * kGemvWarps * 16;  // [2 parities][warps][R * V <= 16]
 constexpr int kGemvStageOffset = kGemvHeader + kGemvPartialFloats * 4;
 static_assert(kGemvStageOffset % 16 == 0, "bulk copies land on 16-byte boundaries");
@@ -70,7 +70,7 @@ __host__ __device__ constexpr int gemv_rows(int block_bytes, int v) {
 struct GemvInput {
   const float* x;
   const float* nw;
-  float scale;
+  const float* scales;  // shared memory: the RMSNorm scale of each vector
   int cols;
 };
 
@@ -82,7 +82,8 @@ __device__ __forceinline__ float4 gemv_load(const GemvInput& in, int v, int col)
   float4 a = __ldg(reinterpret_cast<const float4*>(xr));
   if (PRO == 1) {
     const float4 w = __ldg(reinterpret_cast<const float4*>(in.nw + col));
-    a = make_float4((a.x * in.scale) * w.x, (a.y * in.scale) * w.y, (a.z * in.scale) * w.z, (a.w * in.scale) * w.w);
+    const float sc = in.scales[v];
+    a = make_float4((a.x * sc) * w.x, (a.y * sc) * w.y, (a.z * sc) * w.z, (a.w * sc) * w.w);
   } else if (PRO == 2) {
     const float4 u = __ldg(reinterpret_cast<const float4*>(xr + in.cols));
     a = make_float4(silu(a.x) * u.x, silu(a.y) * u.y, silu(a.z) * u.z, silu(a.w) * u.w);
@@ -234,32 +235,40 @@ __global__ void __launch_bounds__(kGemvThreads, gemv_ctas(V)) gemv_gguf_kernel(c
     }
   }
 
-  GemvInput X{p.x, p.norm_w, 1.0f, p.cols};
+  float* scales = reinterpret_cast<float*>(gsm + kGemvScaleOffset);
+  const GemvInput X{p.x, p.norm_w, scales, p.cols};
   if (PRO == 1) {
-    // RMSNorm scale of the (single) input vector, as te_rmsnorm_f32 forms it
+    // RMSNorm scale of each input vector, as te_rmsnorm_f32 forms it
     // (c/src/ops.c:283-288): the squares summed in double, then
-    // 1 / sqrtf((float)(sum / cols) + eps) in fp32; each CTA computes it for
-    // itself (the vector is a few KB), the partial-sum area holding the
+    // 1 / sqrtf((float)(sum / cols) + eps) in fp32; each CTA computes them
+    // for itself (the vectors are a few KB), the partial-sum area holding the
     // per-warp sums before the first group uses it
-    double ss = 0.0;
-    for (int c = threadIdx.x * 4; c < p.cols; c += kGemvThreads * 4) {
-      const float4 t = __ldg(reinterpret_cast<const float4*>(p.x + c));
-      ss += (double)t.x * (double)t.x + (double)t.y * (double)t.y + (double)t.z * (double)t.z +
-            (double)t.w * (double)t.w;
-    }
+    double ss[V];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    double* red = reinterpret_cast<double*>(partial);
-    if (lane == 0) red[warp] = ss;
+    for (int v = 0; v < V; ++v) ss[v] = 0.0;
+    for (int c = threadIdx.x * 4; c < p.cols; c += kGemvThreads * 4) {
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(p.x + (size_t)v * p.cols + c));
+        ss[v] += (double)t.x * (double)t.x + (double)t.y * (double)t.y + (double)t.z * (double)t.z +
+                 (double)t.w * (double)t.w;
+      }
+    }
+    double* red = reinterpret_cast<double*>(partial);  // [V][warps]
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss[v] += __shfl_xor_sync(0xffffffffu, ss[v], o);
+      if (lane == 0) red[v * kGemvWarps + warp] = ss[v];
+    }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < V) {
       double tot = 0.0;
-      for (int k = 0; k < kGemvWarps; ++k) tot += red[k];
-      *reinterpret_cast<float*>(gsm + kGemvScaleOffset) = 1.0f / sqrtf((float)(tot / (double)p.cols) + p.eps);
+      for (int k = 0; k < kGemvWarps; ++k) tot += red[threadIdx.x * kGemvWarps + k];
+      scales[threadIdx.x] = 1.0f / sqrtf((float)(tot / (double)p.cols) + p.eps);
     }
   }
   __syncthreads();
-  if (PRO == 1) X.scale = *reinterpret_cast<const float*>(gsm + kGemvScaleOffset);
 
 
   int it = 0;
@@ -353,20 +362,25 @@ cudaError_t launch_v(const GemvParams& p, int ctas_per_sm, int sm_count, int sme
   return cudaLaunchKernelEx(&cfg, gemv_gguf_kernel<BLOCK_BYTES, V, PRO>, p);
 }
 
+template <int BLOCK_BYTES, int PRO>
+cudaError_t launch_p(const GemvParams& p, int n_vectors, int ctas_per_sm, int sm_count, int smem, cudaStream_t s) {
+  switch (n_vectors) {
+    case 1: return launch_v<BLOCK_BYTES, 1, PRO>(p, ctas_per_sm, sm_count, smem, s);
+    case 2: return launch_v<BLOCK_BYTES, 2, PRO>(p, ctas_per_sm, sm_count, smem, s);
+    case 3: return launch_v<BLOCK_BYTES, 3, PRO>(p, ctas_per_sm, sm_count, smem, s);
+    case 4: return launch_v<BLOCK_BYTES, 4, PRO>(p, ctas_per_sm, sm_count, smem, s);
+    case 5: return launch_v<BLOCK_BYTES, 5, PRO>(p, ctas_per_sm, sm_count, smem, s);
+    case 6: return launch_v<BLOCK_BYTES, 6, PRO>(p, ctas_per_sm, sm_count, smem, s);
+    case 7: return launch_v<BLOCK_BYTES, 7, PRO>(p, ctas_per_sm, sm_count, smem, s);
+    default: return launch_v<BLOCK_BYTES, 8, PRO>(p, ctas_per_sm, sm_count, smem, s);
+  }
+}
+
 template <int BLOCK_BYTES>
 cudaError_t launch_b(const GemvParams& p, int n_vectors, int ctas_per_sm, int sm_count, int smem, cudaStream_t s) {
-  if (p.prologue == 1) return launch_v<BLOCK_BYTES, 1, 1>(p, ctas_per_sm, sm_count, smem, s);
-  if (p.prologue == 2) return launch_v<BLOCK_BYTES, 1, 2>(p, ctas_per_sm, sm_count, smem, s);
-  switch (n_vectors) {
-    case 1: return launch_v<BLOCK_BYTES, 1>(p, ctas_per_sm, sm_count, smem, s);
-    case 2: return launch_v<BLOCK_BYTES, 2>(p, ctas_per_sm, sm_count, smem, s);
-    case 3: return launch_v<BLOCK_BYTES, 3>(p, ctas_per_sm, sm_count, smem, s);
-    case 4: return launch_v<BLOCK_BYTES, 4>(p, ctas_per_sm, sm_count, smem, s);
-    case 5: return launch_v<BLOCK_BYTES, 5>(p, ctas_per_sm, sm_count, smem, s);
-    case 6: return launch_v<BLOCK_BYTES, 6>(p, ctas_per_sm, sm_count, smem, s);
-    case 7: return launch_v<BLOCK_BYTES, 7>(p, ctas_per_sm, sm_count, smem, s);
-    default: return launch_v<BLOCK_BYTES, 8>(p, ctas_per_sm, sm_count, smem, s);
-  }
+  if (p.prologue == 1) return launch_p<BLOCK_BYTES, 1>(p, n_vectors, ctas_per_sm, sm_count, smem, s);
+  if (p.prologue == 2) return launch_p<BLOCK_BYTES, 2>(p, n_vectors, ctas_per_sm, sm_count, smem, s);
+  return launch_p<BLOCK_BYTES, 0>(p, n_vectors, ctas_per_sm, sm_count, smem, s);
 }
 
 }  // namespace

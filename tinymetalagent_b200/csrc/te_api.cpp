@@ -920,9 +920,10 @@ TE_API te_status te_matvec_gguf(te_attn_engine* e, uint32_t quant, const void* w
 }
 
 TE_API te_status te_matvec_gguf_fused(te_attn_engine* e, uint32_t quant, const void* w, size_t rows, size_t cols,
-                                      const float* x, const float* norm_weight, float eps, float* y, uint32_t flags) {
+                                      const float* x, size_t n_vectors, const float* norm_weight, float eps, float* y,
+                                      uint32_t flags) {
   const uint32_t pro = flags & (TE_ATTN_RMSNORM_INPUT | TE_ATTN_SWIGLU_INPUT);
-  if (!e || !w || !x || !y || rows == 0 || cols == 0 || cols % 32 != 0 ||
+  if (!e || !w || !x || !y || rows == 0 || cols == 0 || cols % 32 != 0 || n_vectors == 0 || n_vectors > 8 ||
       (quant != TE_ATTN_QUANT_GGUF_Q4_0 && quant != TE_ATTN_QUANT_GGUF_Q8_0) ||
       (flags & ~(TE_ATTN_ACCUMULATE | TE_ATTN_RMSNORM_INPUT | TE_ATTN_SWIGLU_INPUT)) ||
       (pro != TE_ATTN_RMSNORM_INPUT && pro != TE_ATTN_SWIGLU_INPUT)) {
@@ -952,7 +953,7 @@ TE_API te_status te_matvec_gguf_fused(te_attn_engine* e, uint32_t quant, const v
   p.prologue = pro == TE_ATTN_RMSNORM_INPUT ? 1 : 2;
   p.norm_w = norm_weight;
   p.eps = eps;
-  const cudaError_t err = launch_gemv_gguf(p, block_bytes, 1, e->sm_count, e->stream);
+  const cudaError_t err = launch_gemv_gguf(p, block_bytes, (int)n_vectors, e->sm_count, e->stream);
   if (err != cudaSuccess) return cuda_fail(e, err, "matvec kernel launch");
   e->launches++;
   return TE_STATUS_OK;

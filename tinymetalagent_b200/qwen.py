@@ -207,6 +207,72 @@ class QwenDecoder:
                                   TE_ATTN_SWIGLU_INPUT | TE_ATTN_ACCUMULATE)
         return self.x
 
+    # ---- a whole prompt at once -----------------------------------------------
+    def prefill_prompt(self, tokens, position: int = 0):
+        """The prompt's tokens at positions position .. position + T - 1, every
+        layer once for all T (the reference's batched prompt pass,
+        te_qwen_prefill_prompt_batch, qwen.c:630-906): projections of up to 8
+        tokens per launch (te_matvec_gguf_fused / te_matvec_gguf with
+        n_vectors), one te_attention_prefill launch per layer (bias, RoPE, f16
+        append and causal attention over the cache).  The prefill kernel is
+        built for head_dim 128; other models take forward_token per token.
+        Returns the last token's hidden state, like forward_token."""
+        import torch
+        toks = [int(t) for t in tokens]
+        d = self.dims
+        if not toks:
+            raise ValueError("empty prompt")
+        if any(not 0 <= t < d["vocab"] for t in toks):
+            raise ValueError("token outside the vocabulary")
+        if position + len(toks) > self.context_tokens:
+            raise ValueError("prompt beyond context_tokens")
+        if d["head_dim"] != 128:
+            for i, t in enumerate(toks):
+                x = self.forward_token(t, position + i)
+            return x
+        n = self.cache.length(0)
+        if position > n:
+            raise ValueError("positions must follow one another")
+        if position < n:
+            self.cache.truncate(0, position)
+        with torch.cuda.stream(self._stream):
+            self._prefill(toks)
+        torch.cuda.current_stream(self._dev).wait_stream(self._stream)
+        return self.x
+
+    def _prefill(self, toks) -> None:
+        import torch
+        d = self.dims
+        H, F, L = d["hidden"], d["ffn"], d["layers"]
+        heads, kv, eps = d["heads"], self.kv, d["eps"]
+        T = len(toks)
+        eng = self.engine
+        idx = torch.tensor(toks, dtype=torch.int64).to(self._dev, non_blocking=True)
+        X = self._emb.index_select(0, idx)  # [T][H], the residual stream of every token
+        qkv = torch.empty((T, H + 2 * kv), dtype=torch.float32, device=self._dev)
+        attn = torch.empty((T, H), dtype=torch.float32, device=self._dev)
+        gu = torch.empty((T, 2 * F), dtype=torch.float32, device=self._dev)
+        chunks = [(c, min(8, T - c)) for c in range(0, T, 8)]
+        for layer, w in enumerate(self.layers):
+            for c, m in chunks:
+                eng.matvec_gguf_fused(w["q_qkv"], w["qkv"], H + 2 * kv, H, X[c:c + m], qkv[c:c + m],
+                                      TE_ATTN_RMSNORM_INPUT, w["attn_norm"], eps, n_vectors=m)
+            q = qkv[:, :H].contiguous()
+            k = qkv[:, H:H + kv].contiguous()
+            v = qkv[:, H + kv:].contiguous()
+            flags = TE_ATTN_QKV_BIAS | (TE_ATTN_ADVANCE if layer == L - 1 else 0)
+            self.cache.prefill(layer, 1, 0, q, k, v, T, heads, attn, flags)
+            for c, m in chunks:
+                eng.matvec_gguf(w["q_o"], w["o"], H, H, attn[c:c + m], X[c:c + m], n_vectors=m,
+                                flags=TE_ATTN_ACCUMULATE)
+            for c, m in chunks:
+                eng.matvec_gguf_fused(w["q_gu"], w["gu"], 2 * F, H, X[c:c + m], gu[c:c + m],
+                                      TE_ATTN_RMSNORM_INPUT, w["ffn_norm"], eps, n_vectors=m)
+            for c, m in chunks:
+                eng.matvec_gguf_fused(w["q_down"], w["down"], H, F, gu[c:c + m], X[c:c + m],
+                                      TE_ATTN_SWIGLU_INPUT | TE_ATTN_ACCUMULATE, n_vectors=m)
+        self.x.copy_(X[T - 1])
+
     def project_next(self) -> int:
         import torch
         d = self.dims

@@ -120,7 +120,7 @@ SIGNATURES: dict[str, tuple] = {
     "te_attention_decode": (_int, [_vp, _sz, _sz, _u32p, _sz, _i64p, _vp, _vp, _vp, _sz, _vp, ctypes.c_uint32]),
     "te_attention_merge_partials": (_int, [_vp, _vp, _sz, _sz, _sz, _vp, ctypes.c_uint32]),
     "te_matvec_gguf": (_int, [_vp, ctypes.c_uint32, _vp, _sz, _sz, _vp, _sz, _vp, ctypes.c_uint32]),
-    "te_matvec_gguf_fused": (_int, [_vp, ctypes.c_uint32, _vp, _sz, _sz, _vp, _vp, ctypes.c_float, _vp,
+    "te_matvec_gguf_fused": (_int, [_vp, ctypes.c_uint32, _vp, _sz, _sz, _vp, _sz, _vp, ctypes.c_float, _vp,
                                     ctypes.c_uint32]),
     "te_attn_exchange_create": (_int, [_vp, _sz, _sz, _sz, _sz, ctypes.POINTER(_vp), _vp]),
     "te_attn_exchange_connect": (_int, [_vp, _vp]),
@@ -270,10 +270,10 @@ class AttnEngine:
         return KVCache(self, **kw)
 
     def matvec_gguf_fused(self, quant: int, w, rows: int, cols: int, x, y, flags: int, norm_weight=None,
-                          eps: float = 0.0) -> None:
-        """One vector: y = W p(x) (or y += that, with TE_ATTN_ACCUMULATE), p the RMSNorm (TE_ATTN_RMSNORM_INPUT,
-        with norm_weight and eps) or the SwiGLU of x = [gate | up] (TE_ATTN_SWIGLU_INPUT)."""
-        self.check(self.lib.te_matvec_gguf_fused(self.handle, quant, _addr(w), rows, cols, _addr(x),
+                          eps: float = 0.0, n_vectors: int = 1) -> None:
+        """y[v] = W p(x[v]) (or y[v] += that, with TE_ATTN_ACCUMULATE), p the RMSNorm (TE_ATTN_RMSNORM_INPUT,
+        with norm_weight and eps) or the SwiGLU of x[v] = [gate | up] (TE_ATTN_SWIGLU_INPUT); 1..8 vectors."""
+        self.check(self.lib.te_matvec_gguf_fused(self.handle, quant, _addr(w), rows, cols, _addr(x), n_vectors,
                                                  _addr(norm_weight), eps, _addr(y), flags))
 
     def matvec_gguf(self, quant: int, w, rows: int, cols: int, x, y, n_vectors: int = 1, flags: int = 0) -> None:
