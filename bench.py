@@ -230,8 +230,11 @@ def run_gpu(args) -> None:
     stream = torch.cuda.ExternalStream(eng.stream)
     if args.gemv_only or args.qwen_only:
         # one measurement alone (e.g. under a profiler): one JSON line
-        res = (run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank) if args.gemv_only
-               else run_qwen(eng, stream, hbm_peak, peak_src, args))
+        if args.gemv_only:
+            res = run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank)
+        else:
+            res = run_qwen(eng, stream, hbm_peak, peak_src, args)
+            res["prompt_prefill"] = run_qwen_prefill(eng, stream, args)
         eng.close()
         if rank == 0:
             print(json.dumps(res))
@@ -417,9 +420,10 @@ def run_gpu(args) -> None:
         gemv = run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank)
 
     # ---- the qwen2 decode step (projections + attention + glue), one GPU ----
-    qwen = None
+    qwen = qwen_prefill = None
     if not args.no_qwen and world == 1:
         qwen = run_qwen(eng, stream, hbm_peak, peak_src, args)
+        qwen_prefill = run_qwen_prefill(eng, stream, args)
 
     # ---- BASELINE configs 4 (sequence-sharded batch) and 5 (KV split + NCCL merge) ----
     ragged = long = None
@@ -458,6 +462,7 @@ def run_gpu(args) -> None:
             "decode3b_qkv_bias": qkv_bias,
             "gemv_gguf": gemv,
             "qwen_decode_step": qwen,
+            "qwen_prompt_prefill": qwen_prefill,
             "ragged7b": ragged,
             "long7b": long,
         }
@@ -715,6 +720,69 @@ def run_qwen(eng, stream, hbm_peak, peak_src, args):
                                        "cores": O.host_cores(),
                                        "sample": f"{n} tokens of te_qwen_forward_token + te_qwen_project_next "
                                                  f"(its CPU path, pthread matvec row split) in {dt:.1f} s"}
+        return res
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
+QWEN_PREFILL_SHAPE = dict(layers=28, hidden=1536, heads=12, kv_heads=2, ffn=8960, vocab=151936, context=1024)
+
+
+def run_qwen_prefill(eng, stream, args):
+    """QwenDecoder.prefill_prompt on a synthetic model of Qwen2.5-1.5B's shape (28 layers, hidden 1536,
+    12 heads of 128 over 2 KV heads, FFN 8960, vocabulary 151 936; Q4_0 projections, Q8_0 embedding and
+    lm_head), a 512-token prompt: prompt tokens/s, device time on the engine's stream (the call's fused
+    projections of 8 tokens per launch and one attention prefill per layer).  Beside it, the reference's
+    CPU forward pass on the same file, token by token (a bounded sample)."""
+    import tempfile
+    import shutil
+    import torch
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    from gguf_synth import GGML_Q4_0, write_qwen2
+    from tinymetalagent_b200.qwen import QwenDecoder
+
+    tmp = Path(tempfile.mkdtemp(prefix="qwen_prefill_bench_"))
+    try:
+        path = tmp / "qwen2_1p5b_shape.gguf"
+        write_qwen2(path, quant_attn=GGML_Q4_0, quant_ffn=GGML_Q4_0, seed=4, **QWEN_PREFILL_SHAPE)
+        T = 512
+        dec = QwenDecoder(eng, path, T + 8)
+        prompt = [int(t) for t in np.random.default_rng(10).integers(0, QWEN_PREFILL_SHAPE["vocab"], T)]
+        dec.prefill_prompt(prompt)  # warm
+        dec.project_next()
+        times = []
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            dec.prefill_prompt(prompt, position=0)
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        launches0 = eng.launch_count
+        dec.prefill_prompt(prompt, position=0)
+        launches = eng.launch_count - launches0
+        dec.close()
+        ms = min(times)
+        res = {"metric": "qwen2 prompt prefill (QwenDecoder.prefill_prompt)", "value": round(T / (ms / 1e3), 1),
+               "unit": "prompt tokens/s", "ms_per_prompt": round(ms, 3), "prompt_tokens": T,
+               "model": "synthetic Qwen2.5-1.5B shape: 28 layers, H12/Hkv2/hd128, hidden 1536, FFN 8960, "
+                        "vocab 151936, Q4_0 projections, Q8_0 embedding/lm_head",
+               "library_launches": int(launches), "timing": "best of 3 calls, CUDA events"}
+        if not args.no_cpu:
+            from oracle import oracle as O
+            if O.ref_qwen_available():
+                ref = O.RefQwen(path, T + 8)
+                n, t0 = 0, time.perf_counter()
+                while time.perf_counter() - t0 < 3.0 and n < T:
+                    ref.forward(prompt[n], n)
+                    n += 1
+                dt = time.perf_counter() - t0
+                ref.close()
+                res["cpu_baseline"] = {"value": round(n / dt, 2), "unit": "prompt tokens/s", "kind": "reference",
+                                       "cores": O.host_cores(),
+                                       "sample": f"the first {n} prompt tokens through te_qwen_forward_token "
+                                                 f"(its CPU path) in {dt:.1f} s"}
         return res
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
