@@ -52,6 +52,7 @@ class QwenDecoder:
         import torch
 
         self.engine = engine
+        self._owns_gguf = not isinstance(model, GGUFFile)
         self.gguf = model if isinstance(model, GGUFFile) else GGUFFile(model)
         d = self.gguf.qwen2_dims()
         self.dims = d
@@ -343,7 +344,16 @@ class QwenDecoder:
         return self.tokens
 
     def close(self) -> None:
+        """Releases the cache, the device weights and (when this decoder opened
+        it) the GGUF mapping; pending work on the engine's stream completes first."""
+        if getattr(self, "_stream", None) is not None:
+            self._stream.synchronize()
         self._graph = None
         if getattr(self, "cache", None) is not None:
             self.cache.close()
             self.cache = None
+        self.layers = []
+        self._emb = self._head = self._out_norm = None
+        if getattr(self, "_owns_gguf", False) and self.gguf is not None:
+            self.gguf.close()
+            self.gguf = None
