@@ -76,12 +76,13 @@ struct GemvInput {
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
+// w: the RMSNorm weights of columns col .. col + 3 (PRO 1), loaded once per
+// step for all vectors
 template <int PRO>
-__device__ __forceinline__ float4 gemv_load(const GemvInput& in, int v, int col) {
+__device__ __forceinline__ float4 gemv_load(const GemvInput& in, int v, int col, const float4& w) {
   const float* xr = in.x + (size_t)v * (PRO == 2 ? 2 : 1) * in.cols + col;
   float4 a = __ldg(reinterpret_cast<const float4*>(xr));
   if (PRO == 1) {
-    const float4 w = __ldg(reinterpret_cast<const float4*>(in.nw + col));
     const float sc = in.scales[v];
     a = make_float4((a.x * sc) * w.x, (a.y * sc) * w.y, (a.z * sc) * w.z, (a.w * sc) * w.w);
   } else if (PRO == 2) {
@@ -104,12 +105,17 @@ __device__ __forceinline__ void gemv_step(const unsigned char* base, int rb, int
   const bool in = !EDGE || b < nb;
   const int bc = in ? b : nb - 1;
   uint64_t xs[V][4];
+  float4 wa = make_float4(0.f, 0.f, 0.f, 0.f), wc = wa;
+  if (PRO == 1 && in) {
+    wa = __ldg(reinterpret_cast<const float4*>(X.nw + b * 32 + xo0));
+    wc = __ldg(reinterpret_cast<const float4*>(X.nw + b * 32 + xo1));
+  }
 #pragma unroll
   for (int v = 0; v < V; ++v) {
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
     if (in) {
-      a = gemv_load<PRO>(X, v, b * 32 + xo0);
-      c = gemv_load<PRO>(X, v, b * 32 + xo1);
+      a = gemv_load<PRO>(X, v, b * 32 + xo0, wa);
+      c = gemv_load<PRO>(X, v, b * 32 + xo1, wc);
     }
     xs[v][0] = f2_pack(a.x, a.y);
     xs[v][1] = f2_pack(a.z, a.w);
