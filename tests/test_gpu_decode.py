@@ -455,3 +455,38 @@ def test_decode_growing_scores(port, chunk):
         close(out.cpu().numpy()[0, 0], exp.reshape(h, hd))
     finally:
         eng.close()
+
+
+@pytest.mark.parametrize("shape", [(16, 2, 128), (28, 4, 128), (16, 1, 128), (14, 2, 64), (16, 1, 64)])
+@pytest.mark.parametrize("chunk", [0, 128])
+def test_decode_growing_scores_fp32_rope(port, shape, chunk):
+    """Rotated fp32 queries against keys that grow 16x over 3000 tokens, so
+    |q.k| / sqrt(hd) reaches tens: a query rounded once to f16 moves the
+    attention weights beyond the bar here.  The kernel feeds the tensor cores
+    q = f16(q) + f16(q - f16(q)) (the low part in the padding rows of the
+    group's fragments for groups <= 8, a second fragment set for groups of
+    9-16), so the products keep the fp32 query.  RoPE on, the new token
+    appended by the same launch, cluster and stream-K splits."""
+    import torch
+    from tinymetalagent_b200 import AttnEngine, TE_ATTN_ADVANCE
+    h, hkv, hd = shape
+    n = 3000
+    rng = np.random.default_rng(93 + h + hd)
+    ramp = (1.0 + np.arange(n) / 200.0)[:, None, None]
+    kraw = (rng.standard_normal((n, hkv, hd)) * ramp).astype(np.float32)
+    vraw = rng.standard_normal((n, hkv, hd)).astype(np.float32)
+    qraw = rng.standard_normal((h, hd)).astype(np.float32)
+    expect, kb, vb = _oracle_decode(port, kraw, vraw, qraw, 0, hkv, hd, h)
+    eng = AttnEngine(0, decode_chunk_tokens=chunk)
+    try:
+        cache = eng.kv_cache(layers=1, max_seqs=1, max_tokens_per_seq=n, kv_heads=hkv, head_dim=hd)
+        cache.append_rope(0, 1, 0, torch_dev(kraw[:-1]), torch_dev(vraw[:-1]), n - 1, TE_ATTN_ADVANCE)
+        out = torch.zeros((h, hd), dtype=torch.float32, device="cuda")
+        cache.decode(0, 1, [0], torch_dev(qraw), out, h, k_new=torch_dev(kraw[-1:]), v_new=torch_dev(vraw[-1:]),
+                     flags=TE_ATTN_ADVANCE)
+        eng.synchronize()
+        close(out.cpu().numpy(), expect)
+        kg, vg = cache.read_f16(0, 0, 0, n)
+        assert np.array_equal(kg, kb) and np.array_equal(vg, vb)
+    finally:
+        eng.close()

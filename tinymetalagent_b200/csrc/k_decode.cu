@@ -53,12 +53,16 @@ struct DecodeCfg {
   static constexpr int kKSteps = HD / 16;                  // mma k-steps for q.k
   static constexpr int kChunksPerThread = HD / 32;         // 16-byte chunks of a K row per thread
   static constexpr int kNTiles = HD / 8;                   // mma n-tiles for P.V
-  static constexpr int kRing = HD == 128 ? (GP == 8 ? 5 : 4) : 8;  // K/V stages in flight
+  static constexpr int kRing = HD == 128 ? (GP == 8 ? 5 : 3) : 8;  // K/V stages in flight
   static constexpr int kRowF = HD + 4;                     // padded row stride (floats): rows 4 banks apart
   static constexpr int kMergeBytes = kConsumerWarps * GP * kRowF * 4;  // one buffer: per-warp O
   static constexpr int kQBytes = GP * kRowF * 4;           // one buffer: raw q rows of the group
   static constexpr int kCSBytes = HD * 4;                  // one buffer: cos row + sin row
-  static constexpr int kFragBytes = kKSteps * 4 * 4 * 32;  // one buffer: f16 query fragments of a warp
+  // One buffer: the f16 query fragments of a warp.  GP = 8 carries each head's
+  // low part in the padding rows 8-15 of the same fragments; GP = 16 needs a
+  // second set of fragments for the low parts.
+  static constexpr int kFragSet = kKSteps * 4 * 4 * 32;
+  static constexpr int kFragBytes = kFragSet * (GP == 16 ? 2 : 1);
   static constexpr int kMLFloats = 2 * kConsumerWarps * 16;  // one buffer: m[4][16], l[4][16]
   static constexpr int kNewBytes = 3 * HD * 4;             // one buffer: new token's raw k, v, and cos/sin row
   static constexpr int kResBytes = (16 + HD) * 4;          // one buffer: new token's scores[16], v[HD] (as cached)
@@ -88,6 +92,12 @@ __device__ __forceinline__ void add_bias8(float (&v)[8], const float* b) {
   v[0] = __fadd_rn(v[0], b0.x); v[1] = __fadd_rn(v[1], b0.y); v[2] = __fadd_rn(v[2], b0.z); v[3] = __fadd_rn(v[3], b0.w);
   v[4] = __fadd_rn(v[4], b1.x); v[5] = __fadd_rn(v[5], b1.y); v[6] = __fadd_rn(v[6], b1.z); v[7] = __fadd_rn(v[7], b1.w);
 }
+
+// Low part of x in a two-term f16 split: x = hi + lo with hi = f16(x) and lo
+// = x - hi (exact in fp32), itself rounded to f16 for the tensor core.  The
+// query enters the f16 MMA as hi and lo, so q.k keeps about 22 bits of the
+// fp32 query instead of 11.
+__device__ __forceinline__ float f16_residual(float x) { return x - __half2float(__float2half_rn(x)); }
 
 __device__ __forceinline__ float rope_lo(float a, float b, float c, float s) {
   return __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
@@ -430,6 +440,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
           const int row = g + 8 * r;
+          if (GP == 8 && r == 1) {
+            // padding rows 8-15 carry the low parts of rows 0-7
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[1][e] = f16_residual(v[0][e]);
+            continue;
+          }
           if (row >= G || row >= GP) {
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[r][e] = 0.f;
@@ -463,6 +479,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
           f.z = pack_half2(v[0][4 * h + 2], v[0][4 * h + 3]);
           f.w = pack_half2(v[1][4 * h + 2], v[1][4 * h + 3]);
           frag[(2 * j + h) * 32 + lane] = f;
+          if (GP == 16) {
+            // second fragment set: the low parts of all 16 rows
+            uint4 fl;
+            fl.x = pack_half2(f16_residual(v[0][4 * h + 0]), f16_residual(v[0][4 * h + 1]));
+            fl.y = pack_half2(f16_residual(v[1][4 * h + 0]), f16_residual(v[1][4 * h + 1]));
+            fl.z = pack_half2(f16_residual(v[0][4 * h + 2]), f16_residual(v[0][4 * h + 3]));
+            fl.w = pack_half2(f16_residual(v[1][4 * h + 2]), f16_residual(v[1][4 * h + 3]));
+            frag[C::kFragSet / 16 + (2 * j + h) * 32 + lane] = fl;
+          }
         }
       }
       __syncwarp();
@@ -772,8 +797,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         qa[ks][3] = f.w;
       }
     }
+    // GP = 16 reads the low-part fragments from shared memory at every stage,
+    // so it releases the buffer only after the segment's last stage.
+    const uint32_t frag_lo = smem_u32(smem + C::kOffFrag + fb * C::kFragBytes + C::kFragSet);
     __syncwarp();
-    if (lane == 0) mbar_arrive(&fempty[fb]);
+    if (GP == 8 && lane == 0) mbar_arrive(&fempty[fb]);
 
     // 2) stream the chunk's stages
     float acc[C::kNTiles][4];
@@ -791,23 +819,44 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         const uint32_t st = smem_u32(smem + slot * C::kStageBytes);
         float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const int r = 16 * warp + g + 8 * t;
+        for (int j = 0; j < C::kChunksPerThread; ++j) {
+          int box;
+          const int ch = k_chunk_of<HD>(c, j, &box);
+          uint4 l0, l1;
+          if (GP == 16) {
+            l0 = lds128(frag_lo + (uint32_t)((2 * j) * 32 + lane) * 16u);
+            l1 = lds128(frag_lo + (uint32_t)((2 * j + 1) * 32 + lane) * 16u);
+          }
 #pragma unroll
-          for (int j = 0; j < C::kChunksPerThread; ++j) {
-            int box;
-            const int ch = k_chunk_of<HD>(c, j, &box);
+          for (int t = 0; t < 2; ++t) {
+            const int r = 16 * warp + g + 8 * t;
             const uint4 kv = lds128(st + box * kBoxBytes + r * 128 + ((ch ^ (r & 7)) << 4));
             mma_16816(sacc[t], qa[2 * j], kv.x, kv.y);
             mma_16816(sacc[t], qa[2 * j + 1], kv.z, kv.w);
+            if (GP == 16) {
+              const uint32_t a0[4] = {l0.x, l0.y, l0.z, l0.w};
+              const uint32_t a1[4] = {l1.x, l1.y, l1.z, l1.w};
+              mma_16816(sacc[t], a0, kv.x, kv.y);
+              mma_16816(sacc[t], a1, kv.z, kv.w);
+            }
           }
         }
+        if (GP == 8) {
+          // rows g + 8 hold q_lo . k of row g: the score is the sum
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            sacc[t][0] += sacc[t][2];
+            sacc[t][1] += sacc[t][3];
+          }
+        }
+        // rows g + 8 are query heads only with GP = 16
+        constexpr int kE = GP == 16 ? 4 : 2;
         float sc[2][4];
         float mx_lo = -INFINITY, mx_hi = -INFINITY;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
+          for (int e = 0; e < kE; ++e) {
             const int tok = tok_base + 8 * t + 2 * c + (e & 1);
             const float v = tok < w.t1 ? sacc[t][e] * sl : -INFINITY;
             sc[t][e] = v;
@@ -816,28 +865,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         }
         mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
         mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
-        mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
-        mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
         const float nm_lo = fmaxf(m_lo, mx_lo);
-        const float nm_hi = fmaxf(m_hi, mx_hi);
         const float base_lo = nm_lo == -INFINITY ? 0.f : nm_lo;
-        const float base_hi = nm_hi == -INFINITY ? 0.f : nm_hi;
         const float al_lo = ex2(m_lo - base_lo);
-        const float al_hi = ex2(m_hi - base_hi);
         m_lo = nm_lo;
-        m_hi = nm_hi;
+        float al_hi = 1.f, base_hi = 0.f;
+        if (GP == 16) {
+          mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+          mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+          const float nm_hi = fmaxf(m_hi, mx_hi);
+          base_hi = nm_hi == -INFINITY ? 0.f : nm_hi;
+          al_hi = ex2(m_hi - base_hi);
+          m_hi = nm_hi;
+        }
         float ps_lo = 0.f, ps_hi = 0.f;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
+          for (int e = 0; e < kE; ++e) {
             const float pv = ex2(sc[t][e] - (e < 2 ? base_lo : base_hi));
             sc[t][e] = pv;
             if (e < 2) ps_lo += pv; else ps_hi += pv;
           }
         }
         l_lo = l_lo * al_lo + ps_lo;
-        l_hi = l_hi * al_hi + ps_hi;
+        if (GP == 16) l_hi = l_hi * al_hi + ps_hi;
         if (__any_sync(0xffffffffu, al_lo != 1.f || al_hi != 1.f)) {
 #pragma unroll
           for (int i = 0; i < C::kNTiles; ++i) {
@@ -849,9 +901,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
         }
         uint32_t pa[4];
         pa[0] = pack_half2(sc[0][0], sc[0][1]);
-        pa[1] = pack_half2(sc[0][2], sc[0][3]);
+        pa[1] = GP == 16 ? pack_half2(sc[0][2], sc[0][3]) : 0u;
         pa[2] = pack_half2(sc[1][0], sc[1][1]);
-        pa[3] = pack_half2(sc[1][2], sc[1][3]);
+        pa[3] = GP == 16 ? pack_half2(sc[1][2], sc[1][3]) : 0u;
         const int rv0 = 16 * warp + 2 * c;
 #pragma unroll
         for (int bx = 0; bx < C::kBoxes; ++bx) {
@@ -876,6 +928,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
+    if (GP == 16 && lane == 0) mbar_arrive(&fempty[fb]);  // the low-part fragments are no longer read
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
@@ -1204,13 +1257,9 @@ __global__ void merge_partials_kernel(const float* __restrict__ partials, int n_
 template <int HD, int GP>
 cudaError_t launch_decode_impl(const DecodeParams& p, cudaStream_t s) {
   using C = DecodeCfg<HD, GP>;
-  static bool configured = false;  // per process
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_f16_kernel<HD, GP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};  // one bit per device
+  const cudaError_t e = set_smem_limit_once(configured, (const void*)decode_f16_kernel<HD, GP>, C::kSmemBytes);
+  if (e != cudaSuccess) return e;
   // Programmatic dependent launch: the CTAs may become resident (on SMs the
   // previous kernel has left) and set up their barriers before it completes;
   // they wait for it (griddepcontrol.wait) before touching global memory.

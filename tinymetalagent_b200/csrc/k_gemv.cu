@@ -343,13 +343,10 @@ template <int BLOCK_BYTES, int V, int PRO = 0>
 cudaError_t launch_v(const GemvParams& p, int ctas_per_sm, int sm_count, int smem, cudaStream_t s) {
   // the largest staging any accepted shape needs (the host rejects longer
   // rows); each launch still asks for its own size
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_gguf_kernel<BLOCK_BYTES, V, PRO>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 128);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};  // one bit per device
+  const cudaError_t e =
+      set_smem_limit_once(configured, (const void*)gemv_gguf_kernel<BLOCK_BYTES, V, PRO>, 227 * 1024 - 128);
+  if (e != cudaSuccess) return e;
   const int n_groups = (p.rows + p.rows_per_group - 1) / p.rows_per_group;
   const int slots = ctas_per_sm * sm_count;
   const int grid = n_groups < slots ? n_groups : slots;

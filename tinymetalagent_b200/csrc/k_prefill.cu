@@ -489,12 +489,9 @@ int prefill_items(int n_layers, int heads, int kv_heads, int n_tokens_padded) {
 }
 
 cudaError_t launch_prefill_tc(const PrefillParams& p, int sm_count, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};  // one bit per device
+  const cudaError_t e = set_smem_limit_once(configured, (const void*)prefill_tc_kernel, kSmemBytes);
+  if (e != cudaSuccess) return e;
   const int grid = p.n_items < sm_count ? p.n_items : sm_count;
   prefill_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
   return cudaGetLastError();

@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <string>
@@ -28,6 +29,23 @@ struct SeqEntry {
 };
 
 constexpr int kMaxParamSeqs = 64;  // sequences per decode launch
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device.
+// The attribute applies to the current device only, so every device a
+// process launches on needs its own call; `done` holds one bit per device
+// ordinal (< 64) and may be shared by host threads (a repeated call is
+// harmless).
+inline cudaError_t set_smem_limit_once(std::atomic<uint64_t>& done, const void* kernel, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  const uint64_t bit = 1ull << dev;
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
 
 // Stream-K split: CTA b of `grid` owns stages [stage_start(b), stage_start(b+1)).
 // Quotient of non-negative a / b; on the device a 32-bit divide when both fit
