@@ -57,6 +57,20 @@ def step_bytes(n_attended: int, layers: int = LAYERS, heads: int = HEADS, kv_hea
     return layers * (kv_read + qo + new)
 
 
+def decode3b_lens(steps: int) -> list[int]:
+    """Tokens attended by each of `steps` config-2 decode steps: step i appends
+    one token and attends CTX0 + (i mod 256) + 1 (the cache is wound back to
+    CTX0 every 256 steps)."""
+    return [CTX0 + (i % DECODE_STEPS) + 1 for i in range(steps)]
+
+
+def decode3b_workload(steps: int) -> str:
+    lens = decode3b_lens(steps)
+    return (f"decode3b: BASELINE config 2 -- Qwen2.5-Coder-3B decode, 36 layers, H16/Hkv2/hd128, f16 KV, "
+            f"RoPE theta 1e6, 1 token appended per layer-step; {steps} steps attending {min(lens)}..{max(lens)} "
+            f"tokens (the config's full range 4097..{CTX0 + DECODE_STEPS} is {DECODE_STEPS} steps)")
+
+
 def prefill_flops(s: int = PREFILL_TOKENS, layers: int = LAYERS) -> int:
     """Causal-exact FLOPs: QK^T and PV over the lower triangle incl. diagonal."""
     return layers * 4 * HEADS * HEAD_DIM * s * (s + 1) // 2
@@ -79,10 +93,13 @@ class ClockSampler:
 
     def __init__(self, index: int):
         self.index = index
-        self.rows: list[list[str]] = []
+        self.rows: list[tuple[float, list[str]]] = []  # (host arrival time, fields)
         self.proc = None
+        self.window = None  # (t0, t1) of the timed region, host clock
 
     def __enter__(self):
+        # No idle sleep here: the caller keeps the GPU busy (warm replays)
+        # while nvidia-smi starts, then marks the timed window.
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
@@ -91,16 +108,19 @@ class ClockSampler:
             self.thread.start()
         except OSError:
             self.proc = None
-        time.sleep(0.25)
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+            self.rows.append((time.perf_counter(), [x.strip() for x in line.split(",")]))
+
+    def mark(self, t0: float, t1: float) -> None:
+        """The timed region's host-clock span: only samples inside it are summarised."""
+        self.window = (t0, t1)
 
     def __exit__(self, *exc):
         if self.proc:
-            time.sleep(0.15)
+            time.sleep(0.12)  # the sample that covers the region's last 100 ms
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -108,7 +128,8 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        rows = [r for r in self.rows if len(r) >= 9]
+        rows = [r for t, r in self.rows if len(r) >= 9
+                and (self.window is None or self.window[0] <= t <= self.window[1] + 0.1)]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
@@ -127,17 +148,22 @@ class CpuDecode:
     """The reference CPU attention (te_attention_decode_f32) on decode
     layer-steps (config 2 by default): each call rotates q (te_rope_f32) and
     attends one layer's fp32-widened f16 cache of n tokens; independent layers
-    run on `threads` host threads (ctypes releases the GIL during each C call)."""
+    run on `threads` host threads (ctypes releases the GIL during each C call).
+    With a position, a call first does the decode step's append as the
+    reference's CPU decode does (c/src/qwen.c:1013-1036): te_rope_f32 of the new
+    k row at that position, both rows rounded to the cache's f16 and stored at
+    that row, then attends tokens 0..position."""
 
     def __init__(self, kind: str, threads: int, n_layers: int = LAYERS, n: int = CTX0 + 1, heads: int = HEADS,
-                 kv_heads: int = KV_HEADS, scale: float = 0.5, shared_kv: bool = False):
+                 kv_heads: int = KV_HEADS, scale: float = 0.5, shared_kv: bool = False, capacity: int = 0):
         from oracle import oracle as O
         self.lib = O.ref() if kind == "reference" else O.port()
         self.threads = threads
         self.n, self.heads, self.kv_heads = n, heads, kv_heads
         self.n_layers = n_layers
+        rows = max(n, capacity)
         rng = np.random.default_rng(0)
-        shape = self.n * kv_heads * HEAD_DIM
+        shape = rows * kv_heads * HEAD_DIM
         def cache():
             return (rng.standard_normal(shape, dtype=np.float32) * scale).astype(np.float16).astype(np.float32)
         if shared_kv:  # one K and one V shared by the layer calls (large caches: bounded set-up time)
@@ -147,18 +173,28 @@ class CpuDecode:
             self.ks = [cache() for _ in range(n_layers)]
             self.vs = [cache() for _ in range(n_layers)]
         self.qs = [rng.standard_normal(heads * HEAD_DIM).astype(np.float32) for _ in range(n_layers)]
+        self.kn = [(rng.standard_normal(kv_heads * HEAD_DIM) * scale).astype(np.float32) for _ in range(n_layers)]
+        self.vn = [(rng.standard_normal(kv_heads * HEAD_DIM) * scale).astype(np.float32) for _ in range(n_layers)]
         from concurrent.futures import ThreadPoolExecutor
         self.pool = ThreadPoolExecutor(max_workers=threads)
 
-    def _one(self, i):
+    def _one(self, i, pos=None):
+        row = self.kv_heads * HEAD_DIM
+        if pos is not None:
+            k = self.kn[i].copy()
+            self.lib.rope_f32(k, self.kv_heads, HEAD_DIM, pos, THETA)
+            self.ks[i][pos * row:(pos + 1) * row] = k.astype(np.float16)
+            self.vs[i][pos * row:(pos + 1) * row] = self.vn[i].astype(np.float16)
+        last = self.n - 1 if pos is None else pos
         q = self.qs[i].copy()
-        self.lib.rope_f32(q, self.heads, HEAD_DIM, self.n - 1, THETA)
-        return self.lib.attention_decode_f32(q, self.ks[i], self.vs[i], self.n - 1, self.heads, self.kv_heads,
+        self.lib.rope_f32(q, self.heads, HEAD_DIM, last, THETA)
+        return self.lib.attention_decode_f32(q, self.ks[i], self.vs[i], last, self.heads, self.kv_heads,
                                              HEAD_DIM)
 
-    def step(self) -> int:
-        """One decode step: every layer once.  Returns the number of layer calls."""
-        list(self.pool.map(self._one, range(self.n_layers)))
+    def step(self, pos=None) -> int:
+        """One decode step: every layer once (appending at `pos` when given).
+        Returns the number of layer calls."""
+        list(self.pool.map(lambda i: self._one(i, pos), range(self.n_layers)))
         return self.n_layers
 
     def sample(self, budget_s: float):
@@ -183,25 +219,35 @@ def run_reference(args) -> None:
     from oracle import oracle as O
     kind = "reference" if O.ref_available() else "port"
     threads = O.host_cores()
-    # one step of the reference arm = one 36-layer decode step of config 2 on all host threads
-    cpu = CpuDecode(kind, threads)
-    for _ in range(max(args.warmup, 0)):
-        cpu.step()
+    # one step of the reference arm = one 36-layer decode step of config 2 on
+    # all host threads: per layer, RoPE + f16 append of the new k/v row, then
+    # attention over the tokens cached so far -- the same lengths as the GPU arm
+    cpu = CpuDecode(kind, threads, capacity=CTX0 + DECODE_STEPS)
+    lens = decode3b_lens(args.steps)
+    for i in range(max(args.warmup, 0)):
+        cpu.step(CTX0 + i % DECODE_STEPS)
     t0 = time.perf_counter()
     calls = 0
-    for _ in range(args.steps):
-        calls += cpu.step()
+    for n in lens:
+        calls += cpu.step(n - 1)
     dt = time.perf_counter() - t0
     cpu.close()
-    value = step_bytes(CTX0 + 1, 1, appended=False) * calls / dt / 1e9
+    value = sum(step_bytes(n) for n in lens) / dt / 1e9
+    # the same layer calls on one host thread, a bounded sample beside the all-thread figure
+    c1 = CpuDecode(kind, 1, n_layers=4)
+    gbs1, calls1, dt1 = c1.sample(3.0)
+    c1.close()
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "decode3b: Qwen2.5-Coder-3B decode, 36 layers, H16/Hkv2/hd128, ctx 4097",
-                   "parallelism": "cpu threads"},
+        "config": {"workload": decode3b_workload(args.steps), "parallelism": "cpu threads"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
-                         "sample": f"{LAYERS} layer calls per step at N={CTX0 + 1} (f16 cache widened to fp32)"},
+                         "sample": f"{args.steps} steps x {LAYERS} layer calls (te_rope_f32 + f16 append + "
+                                   f"te_attention_decode_f32 over {min(lens)}..{max(lens)} tokens, the f16 cache "
+                                   f"widened to fp32)",
+                         "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
+                                           "sample": f"{calls1} layer calls in {dt1:.1f} s on 1 thread"}},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -281,18 +327,40 @@ def run_gpu(args) -> None:
     cache.truncate(0, CTX0)
     cache.reserve(0, cap)
     # step i attends CTX0 + (i mod 256) + 1 tokens (the cache wraps back to CTX0 every 256 steps)
-    lens = [CTX0 + (i % DECODE_STEPS) + 1 for i in range(args.steps)]
+    lens = decode3b_lens(args.steps)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # eager timing (host launch loop), reported for reference
+
+    def time_region(fn):
+        """One timed region: barrier + synchronize, events around fn() on the engine's stream."""
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        fn()
+        ev1.record(stream)
+        ev1.synchronize()
+        return ev0.elapsed_time(ev1)
+
+    def eager_k():
+        cache.truncate(0, CTX0)
+        for _ in range(args.steps):
+            step()
+
+    def regions_for(ms_est):
+        """Timed regions (each exactly K steps) to cover args.min_timed_ms; the
+        same count on every rank, since each region starts with a barrier."""
+        r = max(5, int(np.ceil(args.min_timed_ms / max(ms_est, 1e-3))))
+        r = min(r, 100000)
+        if world > 1:
+            t = torch.tensor([float(r)], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            r = int(t.item())
+        return r
+
+    # eager timing (host launch loop), reported beside the graph timing
     cache.truncate(0, CTX0)
-    barrier()
-    torch.cuda.synchronize()
-    ev0.record(stream)
-    for _ in range(args.steps):
-        step()
-    ev1.record(stream)
-    ev1.synchronize()
-    eager_ms = ev0.elapsed_time(ev1)
+    est = time_region(eager_k)
+    eager_times = [time_region(eager_k) for _ in range(regions_for(est) // 4 + 1)]
+    eager_ms = float(np.median(eager_times))
     graph = None
     if not args.no_graph:
         cache.truncate(0, CTX0)
@@ -303,23 +371,32 @@ def run_gpu(args) -> None:
         with torch.cuda.stream(stream):
             graph.replay()  # warm
         stream.synchronize()
-    launches0 = eng.launch_count
-    barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        ev0.record(stream)
+
+    def run_k():
         if graph is not None:
             with torch.cuda.stream(stream):
                 graph.replay()
         else:
-            cache.truncate(0, CTX0)
-            for _ in range(args.steps):
-                step()
-        ev1.record(stream)
-        ev1.synchronize()
-    launches = args.steps if graph is not None else eng.launch_count - launches0
+            eager_k()
+
+    # Timed: R regions, each exactly K steps (one replay of the K-step graph)
+    # bracketed by a barrier and a synchronize on both sides and timed alone
+    # with CUDA events; the reported time is the median region (max over
+    # ranks).  The clock sampler starts first and the GPU stays busy with warm
+    # replays while nvidia-smi comes up, so the timed regions see loaded clocks.
+    with ClockSampler(local) as clocks:
+        t_end = time.perf_counter() + 0.4
+        while time.perf_counter() < t_end:
+            run_k()
+            stream.synchronize()
+        n_regions = regions_for(time_region(run_k))
+        t_start = time.perf_counter()
+        times = [time_region(run_k) for _ in range(n_regions)]
+        clocks.mark(t_start, time.perf_counter())
+    launches = args.steps  # one decode launch per step in each timed region
     eng.synchronize()
-    ms = ev0.elapsed_time(ev1)
+    ms = float(np.median(times))
+    spread = (float(np.percentile(times, 90)) - float(np.percentile(times, 10))) / ms
     if graph is not None:
         del graph
     cache.truncate(0, CTX0)
@@ -349,14 +426,11 @@ def run_gpu(args) -> None:
         with torch.cuda.stream(stream):
             graph.replay()  # warm
         stream.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        with torch.cuda.stream(stream):
-            graph.replay()
-        ev1.record(stream)
-        ev1.synchronize()
-        ms_b = ev0.elapsed_time(ev1)
+        def replay_b():
+            with torch.cuda.stream(stream):
+                graph.replay()
+
+        ms_b = float(np.median([time_region(replay_b) for _ in range(max(5, n_regions // 4))]))
         del graph
         cache.truncate(0, CTX0)
         if world > 1:
@@ -404,10 +478,16 @@ def run_gpu(args) -> None:
         kind = "reference" if O.ref_available() else "port"
         threads = O.host_cores()
         cd = CpuDecode(kind, threads)
-        gbs, calls, dt = cd.sample(args.cpu_seconds)
+        gbs, calls, dt = cd.sample(args.cpu_seconds * 2 / 3)
         cd.close()
+        # the same layer calls on one host thread (the reference's function is single-threaded)
+        c1 = CpuDecode(kind, 1, n_layers=4)
+        gbs1, calls1, dt1 = c1.sample(args.cpu_seconds / 3)
+        c1.close()
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
-               "sample": f"{calls} config-2 layer calls (N={CTX0 + 1}, 16 heads) in {dt:.1f} s on {threads} threads"}
+               "sample": f"{calls} config-2 layer calls (N={CTX0 + 1}, 16 heads) in {dt:.1f} s on {threads} threads",
+               "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
+                                 "sample": f"{calls1} config-2 layer calls in {dt1:.1f} s on 1 thread"}}
 
     # ---- prefill: 2048-token causal prefill over 36 layers ----
     prefill = None
@@ -433,25 +513,33 @@ def run_gpu(args) -> None:
         ragged = run_ragged7b(eng, stream, hbm_peak, peak_src, args, world, rank)
         long = run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank)
 
-    traffic = None
+    # DRAM traffic of one decode launch, as measured by ncu on this kernel
+    # version (config 2 at ctx 4097) and stored in the profiles folder; not a
+    # measurement of this run.
+    traffic = traffic_src = None
     tfile = ROOT / "profiles" / "traffic.json"
     if tfile.is_file():
-        traffic = json.loads(tfile.read_text()).get("decode_f16_kernel_decode3b_bytes_per_launch")
+        td = json.loads(tfile.read_text())
+        traffic = td.get("decode_f16_kernel_decode3b_bytes_per_launch")
+        traffic_src = td.get("source")
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16 KV, fp32 q/accumulate", "data": "synthetic",
-            "config": {"workload": "decode3b: BASELINE config 2 -- Qwen2.5-Coder-3B decode, 36 layers, H16/Hkv2/"
-                                   "hd128, f16 KV, 4097..4352 tokens over 256 steps, 1 token appended per layer-step",
+            "config": {"workload": decode3b_workload(args.steps),
                        "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
                        "l2": "per-step KV (151 MB) exceeds the 126 MB L2",
-                       "kernel": "decode_f16_kernel<128,8>: stream-K fused RoPE-append + flash decode + LSE combine",
-                       "timing": "K steps captured in one CUDA graph, replayed" if not args.no_graph else "eager",
+                       "kernel": "decode_f16_kernel<128,8>: stream-K or cluster split; fused RoPE-append + "
+                                 "flash decode (fp32 q as f16 hi + lo) + LSE combine",
+                       "timing": (f"median of {n_regions} timed regions, each one replay of the {args.steps}-step "
+                                  f"CUDA graph ({sum(times):.0f} ms in all)") if not args.no_graph
+                                 else f"median of {n_regions} timed regions of {args.steps} eager steps",
+                       "region_spread_p10_p90": round(spread, 4),
                        "eager_ms_per_step": round(eager_ms / args.steps, 5)},
             "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(kernel_gbs / hbm_peak, 4), "traffic": traffic,
+                         "frac": round(kernel_gbs / hbm_peak, 4), "traffic": traffic, "traffic_source": traffic_src,
                          "peak_source": f"{peak_src} (burst copy)"},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
@@ -985,6 +1073,8 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=DECODE_STEPS)
     ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--min-timed-ms", type=float, default=200.0,
+                    help="config 2: timed K-step regions are repeated until they span this much device time")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")

@@ -308,25 +308,37 @@ TE_API te_status te_attention_prefill(te_kv_cache *cache, size_t layer_begin, si
  *
  * The split-K scratch is a fixed 4 MiB + 1.25 KiB file-scope device array
  * that every GPU which loads this library holds until the process exits.
- * Limits: head_dim 64 or 128; heads / kv_heads <= 16; kv_heads <= 256;
- * kv_heads * (heads / kv_heads) * (head_dim + 2) * 4 bytes must fit the
- * 4 MiB scratch (chunking adapts to n_tokens); larger shapes return
- * TE_STATUS_UNSUPPORTED.  The call allocates nothing: no cudaMalloc or
- * cudaFree and no allocating library routine.
+ * Limits: head_dim 64 or 128; heads / kv_heads <= 16; kv_heads <= 256.
+ * The partial records take kv_heads * (heads / kv_heads) * (head_dim + 4) * 4
+ * bytes per CTA segment and the split shrinks its grid until they fit, so
+ * every shape within these limits fits the 4 MiB (at most 2.16 MB on a one-CTA
+ * grid); the TE_STATUS_UNSUPPORTED check behind it is defensive.  The call
+ * allocates nothing: no cudaMalloc or cudaFree and no allocating library
+ * routine.
  *
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress, with that device current), so make that first call
  * before any stream capture.  Every call shares the one array: calls whose
  * kernels overlap on the GPU (different streams, or different host threads)
- * race on it and must be serialised by the caller.  Counters are cleared at
- * the start of each call; a device-side wait that expires is not reported by
- * this asynchronous call.
+ * race on it and must be serialised by the caller.  Counters and the error
+ * word are cleared at the start of each call; a device-side wait that expires
+ * (2 s) is not reported by this asynchronous call but left in the error word,
+ * which te_attention_decode_paged_noalloc_status reads.
  */
 TE_API te_status te_attention_decode_paged_noalloc(
     const uint16_t *k_pool, const uint16_t *v_pool, const int32_t *page_table,
     size_t num_pages, size_t page_tokens, size_t n_tokens,
     const float *q, size_t heads, size_t kv_heads, size_t head_dim,
     float *out, void *stream);
+
+/* Synchronises `stream` (cudaStream_t, NULL = legacy default stream) and
+ * reads the current device's error word of te_attention_decode_paged_noalloc:
+ * *code = 0 and TE_STATUS_OK, or the code a bounded device-side wait of the
+ * last call left (then cleared) and TE_STATUS_RUNTIME_ERROR.  Allocates
+ * nothing.  The next te_attention_decode_paged_noalloc call on the device
+ * clears the word, so read it before that call.  No counterpart in the
+ * reference. */
+TE_API te_status te_attention_decode_paged_noalloc_status(void *stream, int *code);
 
 #ifdef __cplusplus
 }

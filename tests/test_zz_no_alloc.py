@@ -73,6 +73,54 @@ def test_noalloc_decode_matches_engine_decode_twice():
         assert excess.max() <= 0, (call, float(np.abs(got - expect).max()))
 
 
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("group", [7, 16])
+@pytest.mark.parametrize("n_tokens", [1, 63, 65, 3001])
+def test_noalloc_decode_matches_oracle(port, head_dim, group, n_tokens):
+    """The allocation-free path against the CPU oracle (the reference's
+    te_attention_decode_f32 over the same f16 K/V widened to fp32), so a fault
+    shared with the engine's decode would show: head_dim 64/128, groups of 7
+    (the padded-fragment layout) and 16 (two fragment sets), one partial stage
+    up to a long multi-CTA split; the page table maps two of its entries to one
+    page (tokens that repeat), as a caller may."""
+    import torch
+    from tinymetalagent_b200 import runtime as R
+    lib = R.load_library()
+    kv_heads, page_tokens = 2, 64
+    heads = group * kv_heads
+    n_pages_seq = (n_tokens + page_tokens - 1) // page_tokens
+    num_pages = n_pages_seq + 3
+    rng = np.random.default_rng(head_dim * 1000 + group * 10 + n_tokens)
+    pool_k = rng.standard_normal((num_pages, kv_heads, page_tokens, head_dim), dtype=np.float32).astype(np.float16)
+    pool_v = rng.standard_normal((num_pages, kv_heads, page_tokens, head_dim), dtype=np.float32).astype(np.float16)
+    table = rng.permutation(num_pages)[:n_pages_seq].astype(np.int32)
+    if n_pages_seq >= 3:
+        table[-1] = table[0]  # a repeated page: its tokens appear twice in the sequence
+    # the sequence as the oracle reads it: [n_tokens][kv_heads][head_dim]
+    k_seq = pool_k[table].transpose(0, 2, 1, 3).reshape(-1, kv_heads, head_dim)[:n_tokens]
+    v_seq = pool_v[table].transpose(0, 2, 1, 3).reshape(-1, kv_heads, head_dim)[:n_tokens]
+    q = rng.standard_normal((heads, head_dim), dtype=np.float32)
+    expect = port.attention_decode_f32(q.ravel(), k_seq.astype(np.float32).ravel(), v_seq.astype(np.float32).ravel(),
+                                       n_tokens - 1, heads, kv_heads, head_dim).reshape(heads, head_dim)
+    dk = torch.from_numpy(pool_k.view(np.uint16)).cuda()
+    dv = torch.from_numpy(pool_v.view(np.uint16)).cuda()
+    dt = torch.from_numpy(table).cuda()
+    dq = torch.from_numpy(q).cuda()
+    stream = torch.cuda.current_stream()
+    for call in range(2):  # twice in a row on the shared scratch
+        out = torch.full((heads, head_dim), float("nan"), dtype=torch.float32, device="cuda")
+        st = lib.te_attention_decode_paged_noalloc(dk.data_ptr(), dv.data_ptr(), dt.data_ptr(), num_pages,
+                                                   page_tokens, n_tokens, dq.data_ptr(), heads, kv_heads, head_dim,
+                                                   out.data_ptr(), stream.cuda_stream)
+        assert st == R.TE_STATUS_OK, lib.te_strerror(st)
+        code = ctypes.c_int(-1)
+        assert lib.te_attention_decode_paged_noalloc_status(stream.cuda_stream, ctypes.byref(code)) == R.TE_STATUS_OK
+        assert code.value == 0
+        got = out.cpu().numpy()
+        excess = np.abs(got - expect) - (ATOL + RTOL * np.abs(expect))
+        assert excess.max() <= 0, (call, float(np.abs(got - expect).max()))
+
+
 def test_noalloc_rejects_out_of_range_shapes():
     from tinymetalagent_b200 import runtime as R
     lib = R.load_library()

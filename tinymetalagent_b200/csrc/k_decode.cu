@@ -1415,6 +1415,29 @@ extern "C" __attribute__((visibility("default"))) te_status te_attention_decode_
     max_grid /= 2;
     plan_stream_k(p, max_grid);
   }
+  // Defensive: with kv_heads <= 256 and groups <= 16 a one-CTA grid needs at
+  // most 256 * 16 * 132 * 4 bytes (2.16 MB), so every accepted shape fits.
   if ((size_t)p.grid * p.max_segs * rec_bytes > kNoAllocPartialBytes) return TE_STATUS_UNSUPPORTED;
   return launch_decode_f16(p, (int)head_dim, s) == cudaSuccess ? TE_STATUS_OK : TE_STATUS_RUNTIME_ERROR;
+}
+
+extern "C" __attribute__((visibility("default"))) te_status te_attention_decode_paged_noalloc_status(void* stream,
+                                                                                                      int* code) {
+  if (!code) return TE_STATUS_INVALID_ARGUMENT;
+  *code = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return TE_STATUS_RUNTIME_ERROR;
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    base = g_noalloc_addr[dev];
+  }
+  if (!base) return TE_STATUS_OK;  // no call on this device yet
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return TE_STATUS_RUNTIME_ERROR;
+  int* word = reinterpret_cast<int*>(static_cast<unsigned char*>(base) + kNoAllocPartialBytes + kNoAllocCounterBytes);
+  if (cudaMemcpy(code, word, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return TE_STATUS_RUNTIME_ERROR;
+  if (*code == 0) return TE_STATUS_OK;
+  cudaMemset(word, 0, sizeof(int));
+  return TE_STATUS_RUNTIME_ERROR;
 }

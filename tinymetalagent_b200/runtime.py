@@ -128,6 +128,7 @@ SIGNATURES: dict[str, tuple] = {
     "te_attn_exchange_free": (None, [_vp]),
     "te_attention_prefill": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _vp, _sz, _sz, _vp, ctypes.c_uint32]),
     "te_attention_decode_paged_noalloc": (_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _sz, _sz, _sz, _vp, _vp]),
+    "te_attention_decode_paged_noalloc_status": (_int, [_vp, ctypes.POINTER(ctypes.c_int)]),
 }
 
 
