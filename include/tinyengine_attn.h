@@ -60,6 +60,9 @@ extern "C" {
 #define TE_ATTN_ACCUMULATE    (1u << 6) /* te_matvec_gguf: y += W x (the residual add of a projection) */
 #define TE_ATTN_RMSNORM_INPUT (1u << 7) /* te_matvec_gguf_fused: the input is RMSNorm(x) * norm_weight */
 #define TE_ATTN_SWIGLU_INPUT  (1u << 8) /* te_matvec_gguf_fused: the input is SwiGLU of x = [gate | up] */
+#define TE_ATTN_EXACT_Q       (1u << 9) /* te_attention_prefill with binary16 inputs: the rotated (or biased)
+                                           fp32 query enters the tensor cores as f16 hi + lo parts, as fp32
+                                           inputs always do (about half the speed of the single rounding) */
 
 typedef struct te_attn_engine te_attn_engine;
 typedef struct te_kv_cache te_kv_cache;
@@ -280,9 +283,15 @@ TE_API void te_attn_exchange_free(te_attn_exchange *exchange);
  * new token t attends to cached tokens 0 .. length+t (length = tokens cached
  * before the call).  Replaces the CPU prefill loop (c/src/qwen.c:774-824) and
  * te_metal_prefill_all_layers_f32's attention
- * (c/src/metal/metal_backend_layers.mm.inc:2406-2456).  Flags:
+ * (c/src/metal/metal_backend_layers.mm.inc:2406-2456) and, for head_dim 64,
+ * the Metal MMA prefill te_attention_flash_mma_t_f32_kernel
+ * (c/src/metal/metal_kernels.metal.inc:2693-2836).  head_dim 64 or 128.
+ * The tensor cores multiply f16: fp32 query inputs are fed as two f16 parts
+ * (hi = f16(q), lo = f16(q - hi)) into the same accumulator, keeping the
+ * fp32 query's precision; binary16 inputs whose query is rotated or biased
+ * round it once to f16 unless TE_ATTN_EXACT_Q is given.  Flags:
  * TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16, TE_ATTN_HOST_BUFFERS, TE_ATTN_NO_ROPE,
- * TE_ATTN_QKV_BIAS.
+ * TE_ATTN_QKV_BIAS, TE_ATTN_EXACT_Q.
  */
 TE_API te_status te_attention_prefill(te_kv_cache *cache, size_t layer_begin, size_t n_layers,
                                       size_t seq, const void *q, const void *k, const void *v,

@@ -241,3 +241,84 @@ def test_prefill_growing_scores(port, shape):
         assert np.array_equal(kg, k16.view(np.uint16)) and np.array_equal(vg, v16.view(np.uint16))
     finally:
         eng.close()
+
+
+@pytest.mark.parametrize("s", [1, 37, 128, 513])
+@pytest.mark.parametrize("f16_inputs", [False, True])
+def test_prefill_head_dim_64(port, s, f16_inputs):
+    """head_dim 64 at the Qwen2.5-0.5B shape (H14/Hkv2, the model of BASELINE
+    config 1 and of the reference's only MMA prefill,
+    c/src/metal/metal_kernels.metal.inc:2693-2836): fp32 inputs (query as hi +
+    lo f16 parts, one head per item) and f16 inputs (single rounding, head
+    pairs); cache bit-exact, every row against the oracle."""
+    import torch
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16, AttnEngine
+    h, hkv, hd = 14, 2, 64
+    rng = np.random.default_rng(640 + s)
+    q = rng.standard_normal((s, h, hd)).astype(np.float32)
+    k = rng.standard_normal((s, hkv, hd)).astype(np.float32)
+    v = rng.standard_normal((s, hkv, hd)).astype(np.float32)
+    flags = TE_ATTN_ADVANCE
+    if f16_inputs:
+        q, k, v = (a.astype(np.float16) for a in (q, k, v))
+        flags |= TE_ATTN_INPUT_F16
+    exp, kb, vb = oracle_prefill(port, q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), h, hkv, hd)
+    eng = AttnEngine(0)
+    try:
+        cache = eng.kv_cache(layers=1, max_seqs=1, max_tokens_per_seq=s, kv_heads=hkv, head_dim=hd)
+        out = torch.zeros((1, s, h, hd), dtype=torch.float32, device="cuda")
+        if f16_inputs:
+            t16 = lambda a: dev(a.view(np.uint16)).view(torch.float16)  # noqa: E731
+            cache.prefill(0, 1, 0, t16(q[None]), t16(k[None]), t16(v[None]), s, h, out, flags)
+        else:
+            cache.prefill(0, 1, 0, dev(q[None]), dev(k[None]), dev(v[None]), s, h, out, flags)
+        eng.synchronize()
+        got = out.cpu().numpy()[0]
+        for t in range(s):
+            close(got[t], exp[t])
+        kg, vg = cache.read_f16(0, 0, 0, s)
+        assert np.array_equal(kg, kb) and np.array_equal(vg, vb)
+    finally:
+        eng.close()
+
+
+@pytest.mark.parametrize("shape", [(16, 2, 128), (28, 4, 128), (14, 2, 64)])
+@pytest.mark.parametrize("mode", ["fp32", "f16_exact_q"])
+def test_prefill_growing_scores_rotated_query(port, shape, mode):
+    """Rotated queries against keys that grow 16x over 600 tokens (|q.k| /
+    sqrt(hd) of tens): a query rounded once to f16 moves the weights beyond
+    the bar here.  fp32 inputs, and f16 inputs with TE_ATTN_EXACT_Q, feed the
+    rotated query as f16 hi + lo parts into the same accumulator and must meet
+    1e-3 + 2e-3 |ref| on every checked row, with many O rescales per row."""
+    import torch
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_EXACT_Q, TE_ATTN_INPUT_F16, AttnEngine
+    h, hkv, hd = shape
+    s = 600
+    rng = np.random.default_rng(177 + h + hd)
+    q = rng.standard_normal((s, h, hd)).astype(np.float32)
+    k = (rng.standard_normal((s, hkv, hd)) * (1.0 + np.arange(s) / 40.0)[:, None, None]).astype(np.float32)
+    v = rng.standard_normal((s, hkv, hd)).astype(np.float32)
+    flags = TE_ATTN_ADVANCE
+    if mode == "f16_exact_q":
+        q, k, v = (a.astype(np.float16) for a in (q, k, v))
+        flags |= TE_ATTN_INPUT_F16 | TE_ATTN_EXACT_Q
+    rows = (0, 1, 63, 64, 127, 128, 129, 255, 256, 383, 384, 511, 512, 599)
+    exp, kb, vb = oracle_prefill(port, q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), h, hkv, hd,
+                                 positions=rows)
+    eng = AttnEngine(0)
+    try:
+        cache = eng.kv_cache(layers=1, max_seqs=1, max_tokens_per_seq=s, kv_heads=hkv, head_dim=hd)
+        out = torch.zeros((1, s, h, hd), dtype=torch.float32, device="cuda")
+        if mode == "f16_exact_q":
+            t16 = lambda a: dev(a.view(np.uint16)).view(torch.float16)  # noqa: E731
+            cache.prefill(0, 1, 0, t16(q[None]), t16(k[None]), t16(v[None]), s, h, out, flags)
+        else:
+            cache.prefill(0, 1, 0, dev(q[None]), dev(k[None]), dev(v[None]), s, h, out, flags)
+        eng.synchronize()
+        got = out.cpu().numpy()[0]
+        for t in rows:
+            close(got[t], exp[t])
+        kg, vg = cache.read_f16(0, 0, 0, s)
+        assert np.array_equal(kg, kb) and np.array_equal(vg, vb)
+    finally:
+        eng.close()

@@ -156,18 +156,20 @@ def test_graph_replay_matches_eager_steps(tmp_path):
         eng.close()
 
 
-def test_prefill_prompt_matches_reference(tmp_path):
-    """prefill_prompt (head_dim 128: batched projections + one te_attention_prefill launch per layer) against
-    the reference's token-by-token forward pass; then greedy steps continue from the prefilled cache, and a
-    prompt prefilled in two calls (the second over the first's cache) gives the same state."""
+@pytest.mark.parametrize("name", list(MODELS))
+def test_prefill_prompt_matches_reference(tmp_path, name):
+    """prefill_prompt (batched projections + one te_attention_prefill launch per layer; head_dim 64 and 128,
+    groups 2, 4 and 7) against the reference's token-by-token forward pass; then greedy steps continue from
+    the prefilled cache, and a prompt prefilled in two calls (the second over the first's cache) gives the
+    same state."""
     from oracle import oracle as O
     if not O.ref_qwen_available():
         pytest.skip("reference forward pass not built")
     from tinymetalagent_b200 import AttnEngine
     from tinymetalagent_b200.qwen import QwenDecoder
     path = tmp_path / "m.gguf"
-    write_qwen2(path, **MODELS["hd128"])
-    prompt = [int(t) for t in np.random.default_rng(21).integers(0, 640, 21)]
+    write_qwen2(path, **MODELS[name])
+    prompt = [int(t) for t in np.random.default_rng(21).integers(0, MODELS[name]["vocab"], 21)]
     ctx = 40
     ref = O.RefQwen(path, ctx)
     eng = AttnEngine(0)

@@ -15,6 +15,7 @@ from .runtime import (  # noqa: F401
     TE_ATTN_QKV_BIAS,
     TE_ATTN_RMSNORM_INPUT,
     TE_ATTN_SWIGLU_INPUT,
+    TE_ATTN_EXACT_Q,
     AttnEngine,
     KVCache,
     TinyEngineError,

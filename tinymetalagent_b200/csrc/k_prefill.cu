@@ -14,6 +14,13 @@
 // item).  Items are ordered by decreasing causal length and dealt round-robin
 // to a persistent grid of one CTA per SM.
 //
+// Template parameters: HD = 128 or 64 (the reference's only MMA prefill is the
+// head_dim-64 kernel above); SPLIT = the query enters the tensor cores as two
+// f16 tiles, hi = f16(q) and lo = f16(q - hi), both multiplied by the same K
+// tile into the same S accumulator, so q.k keeps about 22 bits of the fp32
+// query.  A SPLIT item is one head: its lo tile takes the second query slot
+// and the second softmax warpgroup idles.
+//
 // Warp roles (384 threads):
 //   warp 0      TMA producer: the Q tiles, then K and V tiles (128 keys) into
 //               two 2-stage rings (K released after its tile's last Q K^T, V
@@ -44,39 +51,52 @@ namespace {
 
 constexpr int BM = 128;                     // queries per tile
 constexpr int BN = 128;                     // keys per tile
-constexpr int HD = 128;                     // head dim
-constexpr int kTile = BM * HD * 2;          // 32 KiB: 128 rows x 128 f16, as two 64-column halves
-constexpr int kHalf = kTile / 2;            // 16 KiB: 128 rows x 128 B
+constexpr int kHalf = 128 * 128;            // 16 KiB: 128 rows x 128 B (one 64-column chunk of a tile)
 constexpr int kBox = 64 * 128;              // 8 KiB TMA box: 64 rows x 64 f16
 constexpr int kThreads = 384;               // three warpgroups
 constexpr int kRegsLow = 120;                // per thread, warpgroup 0 (producer, MMA issuer)
 constexpr int kRegsHigh = 184;              // per thread, the two softmax warpgroups
 static_assert(128 * (kRegsLow + 2 * kRegsHigh) <= 65536, "register split exceeds the launch's registers");
 
-constexpr int OFF_QA = 0;
-constexpr int OFF_QB = kTile;
-constexpr int OFF_KV = 2 * kTile;           // stage s: K at OFF_KV + s*2*kTile, V at + kTile
-constexpr int OFF_OST = OFF_KV + 4 * kTile; // output staging: 4 KiB (32 rows x 128 B) per softmax warp
-constexpr int OFF_BAR = OFF_OST + 8 * 4096;  // 229376
-constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
-static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
+// Shared-memory plan for head dim HD: query slots A and B, a 2-stage ring of K
+// and V tiles, output staging (4 KiB per softmax warp), barriers.
+template <int HD>
+struct Plan {
+  static constexpr int kChunks = HD / 64;    // 64-column chunks per tile row
+  static constexpr int kTile = BM * HD * 2;  // one Q, K or V tile (BM == BN)
+  static constexpr int OFF_QA = 0;
+  static constexpr int OFF_QB = kTile;
+  static constexpr int OFF_KV = 2 * kTile;   // stage s: K at OFF_KV + s*2*kTile, V at + kTile
+  static constexpr int OFF_OST = OFF_KV + 4 * kTile;
+  static constexpr int OFF_BAR = OFF_OST + 8 * 4096;
+  static constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
+};
 
 enum Bar {
   Q_FULL = 0, Q_EMPTY, K_FULL0, K_FULL1, V_FULL0, V_FULL1, K_EMPTY0, K_EMPTY1, V_EMPTY0, V_EMPTY1,
   S_FULL_A, S_FULL_B, P_FULL_A, P_FULL_B, O_FULL_A, O_FULL_B, O_EMPTY_A, O_EMPTY_B, DRAIN, kNumBars
 };
 
+// Tensor memory: S_A [0,128) S_B [128,256) O_A [256,256+HD) O_B [256+HD,256+2HD).
 constexpr uint32_t kTmemCols = 512;
 __device__ __forceinline__ uint32_t col_s(int t) { return t ? 128u : 0u; }
-__device__ __forceinline__ uint32_t col_o(int t) { return t ? 384u : 256u; }
+template <int HD>
+__device__ __forceinline__ uint32_t col_o(int t) { return 256u + (uint32_t)(t * HD); }
 
 struct Item {
   int layer_local, kvh, head_a, has_b, qt, n_kv;
 };
 
+// Items of one (layer, kv head, 128-query tile): pairs of heads, or single
+// heads when SPLIT (the second query slot holds the low part).
+template <bool SPLIT>
+__device__ __forceinline__ int units_per_group(int G) { return SPLIT ? G : (G + 1) / 2; }
+
+template <bool SPLIT>
 __device__ __forceinline__ Item item_of(const PrefillParams& p, int it) {
   const int G = p.heads / p.kv_heads;
-  const int pairs = (G + 1) / 2;
+  const int pairs = units_per_group<SPLIT>(G);
   const int per_qt = p.n_layers * p.kv_heads * pairs;
   const int n_qt = p.n_tokens_padded / BM;
   Item I;
@@ -86,8 +106,8 @@ __device__ __forceinline__ Item item_of(const PrefillParams& p, int it) {
   r /= pairs;
   I.kvh = r % p.kv_heads;
   I.layer_local = r / p.kv_heads;
-  I.head_a = I.kvh * G + 2 * pr;
-  I.has_b = 2 * pr + 1 < G;
+  I.head_a = I.kvh * G + (SPLIT ? pr : 2 * pr);
+  I.has_b = SPLIT ? 0 : (2 * pr + 1 < G);
   const int total = p.q_offset + p.n_tokens;
   const int last_key = min(p.q_offset + (I.qt + 1) * BM, total);  // keys [0, last_key)
   I.n_kv = (last_key + BN - 1) / BN;
@@ -117,7 +137,12 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+template <int HD, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ PrefillParams p) {
+  using PL = Plan<HD>;
+  constexpr int kTile = PL::kTile;
+  constexpr int OFF_QA = PL::OFF_QA, OFF_QB = PL::OFF_QB, OFF_KV = PL::OFF_KV, OFF_OST = PL::OFF_OST;
+  constexpr int OFF_BAR = PL::OFF_BAR;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -175,20 +200,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     bool ok = true;
     for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x, ++ic) {
       if (__shfl_sync(0xffffffffu, lane == 0 && aborted(abort_flag) ? 1 : 0, 0)) break;
-      const Item I = item_of(p, it);
+      const Item I = item_of<SPLIT>(p, it);
       if (lane == 0) {
         if (!mbar_wait(&bar[Q_EMPTY], (ic & 1) ^ 1)) {
           set_error(p.error, 11);
           ok = false;
         } else {
-          mbar_arrive_expect_tx(&bar[Q_FULL], I.has_b ? 2 * kTile : kTile);
-          for (int t = 0; t < 1 + I.has_b; ++t) {
+          // query tiles: heads A (and B), or head A's hi and lo parts (query
+          // rows 2h and 2h + 1 of the split layout)
+          const int n_q = SPLIT ? 2 : 1 + I.has_b;
+          mbar_arrive_expect_tx(&bar[Q_FULL], (uint32_t)(n_q * kTile));
+          for (int t = 0; t < n_q; ++t) {
+            const int qrow = SPLIT ? 2 * I.head_a + t : I.head_a + t;
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
-              for (int c = 0; c < 2; ++c)
+              for (int c = 0; c < PL::kChunks; ++c)
                 tma_load_4d_hint(smem + (t ? OFF_QB : OFF_QA) + c * kHalf + h * kBox, &p.tmap_q, &bar[Q_FULL],
-                                 c * 64, I.head_a + t, I.qt * BM + h * 64, I.layer_local, stream_once);
+                                 c * 64, qrow, I.qt * BM + h * 64, I.layer_local, stream_once);
           }
         }
       }
@@ -231,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
-              for (int c = 0; c < 2; ++c)
+              for (int c = 0; c < PL::kChunks; ++c)
                 tma_load_2d_hint(ks + c * kHalf + h * kBox, &p.tmap_k, &bar[K_FULL0 + s], c * 64, rows[h], keep);
           }
           if (ok && !mbar_wait(&bar[V_EMPTY0 + s], ((kc >> 1) & 1) ^ 1)) {
@@ -242,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
-              for (int c = 0; c < 2; ++c)
+              for (int c = 0; c < PL::kChunks; ++c)
                 tma_load_2d_hint(vs + c * kHalf + h * kBox, &p.tmap_v, &bar[V_FULL0 + s], c * 64, rows[h], keep);
           }
         }
@@ -282,6 +311,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           const uint64_t b = smem_desc_sw128(sk + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
           umma_f16(tmem + col_s(t), a, b, idesc_qk, k > 0 ? 1u : 0u);
         }
+        if (SPLIT) {
+          // the query's low part (slot B) times the same K tile, into the same S
+#pragma unroll
+          for (int k = 0; k < HD / 16; ++k) {
+            const uint64_t a = smem_desc_sw128(sq[1] + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
+            const uint64_t b = smem_desc_sw128(sk + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
+            umma_f16(tmem + col_s(t), a, b, idesc_qk, 1u);
+          }
+        }
         umma_commit(&bar[S_FULL_A + t]);
       };
       auto pv = [&](int t, uint32_t k_idx, int j) {
@@ -289,11 +327,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k) {
           const uint64_t b = smem_desc_sw128(sv + k * 2048, kHalf, 1024);
-          umma_f16_ts(tmem + col_o(t), tmem + col_s(t) + k * 8, b, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + col_o<HD>(t), tmem + col_s(t) + k * 8, b, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
         }
       };
       for (int it = blockIdx.x; it < p.n_items && ok && !aborted(abort_flag); it += gridDim.x, ++ic) {
-        const Item I = item_of(p, it);
+        const Item I = item_of<SPLIT>(p, it);
         const int nt = 1 + I.has_b;
         const uint32_t kc0 = kc;
         if (!wait(Q_FULL, ic & 1) || !wait(K_FULL0 + (kc0 & 1), (kc0 >> 1) & 1)) { ok = false; break; }
@@ -342,13 +380,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const int row = quad * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
     const uint32_t s_addr = tmem + lane_addr + col_s(t);
-    const uint32_t o_addr = tmem + lane_addr + col_o(t);
+    const uint32_t o_addr = tmem + lane_addr + col_o<HD>(t);
     const float sl = p.scale_log2;
     uint32_t sc = 0, oc = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < p.n_items && ok; it += gridDim.x) {
       if (__any_sync(0xffffffffu, aborted(abort_flag))) break;
-      const Item I = item_of(p, it);
+      const Item I = item_of<SPLIT>(p, it);
       if (t == 1 && !I.has_b) continue;
       const int q_pos = p.q_offset + I.qt * BM + row;
       const int key_limit = min(q_pos, total - 1);
@@ -481,20 +519,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+template <int HD, bool SPLIT>
+cudaError_t launch_prefill_impl(const PrefillParams& p, int sm_count, cudaStream_t s) {
+  static std::atomic<uint64_t> configured{0};  // one bit per device
+  const cudaError_t e = set_smem_limit_once(configured, (const void*)prefill_tc_kernel<HD, SPLIT>, Plan<HD>::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int grid = p.n_items < sm_count ? p.n_items : sm_count;
+  prefill_tc_kernel<HD, SPLIT><<<grid, kThreads, Plan<HD>::kSmemBytes, s>>>(p);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
-int prefill_items(int n_layers, int heads, int kv_heads, int n_tokens_padded) {
+int prefill_items(int n_layers, int heads, int kv_heads, int n_tokens_padded, bool split) {
   const int G = heads / kv_heads;
-  return n_layers * kv_heads * ((G + 1) / 2) * (n_tokens_padded / BM);
+  return n_layers * kv_heads * (split ? G : (G + 1) / 2) * (n_tokens_padded / BM);
 }
 
 cudaError_t launch_prefill_tc(const PrefillParams& p, int sm_count, cudaStream_t s) {
-  static std::atomic<uint64_t> configured{0};  // one bit per device
-  const cudaError_t e = set_smem_limit_once(configured, (const void*)prefill_tc_kernel, kSmemBytes);
-  if (e != cudaSuccess) return e;
-  const int grid = p.n_items < sm_count ? p.n_items : sm_count;
-  prefill_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
-  return cudaGetLastError();
+  if (p.head_dim == 128) {
+    return p.split ? launch_prefill_impl<128, true>(p, sm_count, s) : launch_prefill_impl<128, false>(p, sm_count, s);
+  }
+  if (p.head_dim == 64) {
+    return p.split ? launch_prefill_impl<64, true>(p, sm_count, s) : launch_prefill_impl<64, false>(p, sm_count, s);
+  }
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace te

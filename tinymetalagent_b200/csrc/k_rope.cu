@@ -133,6 +133,34 @@ __global__ void append_rope_kernel(const AppendParams p) {
   *reinterpret_cast<uint4*>(vd + d + half) = pack8(vhi);
 }
 
+// Low parts of a two-term f16 split: lo = f16(x - f16(x)), x - f16(x) exact in fp32.
+__device__ __forceinline__ void f16_residual8(const float (&x)[8], float (&r)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) r[e] = x[e] - __half2float(__float2half_rn(x[e]));
+}
+
+// Stores dims [d, d+8) and [d+half, d+half+8) of the query row whose unsplit
+// offset is `row` (elements, [..][heads][hd] layout): as f16 there, or with
+// p.split as the hi row 2r and the lo row 2r + 1 of [..][heads][2][hd].
+template <int HD>
+__device__ __forceinline__ void store_q8(const QPrepParams& p, size_t row, int d, const float (&lo)[8],
+                                         const float (&hi)[8]) {
+  constexpr int half = HD / 2;
+  if (!p.split) {
+    *reinterpret_cast<uint4*>(p.qh + row + d) = pack8(lo);
+    *reinterpret_cast<uint4*>(p.qh + row + d + half) = pack8(hi);
+    return;
+  }
+  float rl[8], rh[8];
+  f16_residual8(lo, rl);
+  f16_residual8(hi, rh);
+  __half* hrow = p.qh + 2 * row;
+  *reinterpret_cast<uint4*>(hrow + d) = pack8(lo);
+  *reinterpret_cast<uint4*>(hrow + d + half) = pack8(hi);
+  *reinterpret_cast<uint4*>(hrow + HD + d) = pack8(rl);
+  *reinterpret_cast<uint4*>(hrow + HD + d + half) = pack8(rh);
+}
+
 // Query rows of one token and head: f16 in the same layout, rotated unless
 // RoPE is off.
 template <int HD>
@@ -149,8 +177,7 @@ __device__ __forceinline__ void q_prep_row(const QPrepParams& p, size_t row, int
     const int pos = p.first_pos + t;
     rope8(lo, hi, p.rope_cos + (size_t)pos * half, p.rope_sin + (size_t)pos * half, d);
   }
-  *reinterpret_cast<uint4*>(p.qh + row + d) = pack8(lo);
-  *reinterpret_cast<uint4*>(p.qh + row + d + half) = pack8(hi);
+  store_q8<HD>(p, row, d, lo, hi);
 }
 
 // q[n_layers][n_tokens][heads][hd] -> f16 qh (same layout).  One thread per
@@ -304,8 +331,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) prefill_prep_kernel(const App
                 hi[k][e] = rope_hi(x, y, cv[e], sn[e]);
               }
             }
-            *reinterpret_cast<uint4*>(q.qh + qbase + (size_t)r * HD + d) = pack8(lo[k]);
-            *reinterpret_cast<uint4*>(q.qh + qbase + (size_t)r * HD + d + half) = pack8(hi[k]);
+            store_q8<HD>(q, qbase + (size_t)r * HD, d, lo[k], hi[k]);
           }
         }
       }

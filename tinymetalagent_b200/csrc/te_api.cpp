@@ -1061,7 +1061,8 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
     return TE_STATUS_INVALID_ARGUMENT;
   }
   te_attn_engine* e = c->eng;
-  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | TE_ATTN_HOST_BUFFERS | TE_ATTN_NO_ROPE | TE_ATTN_QKV_BIAS)) {
+  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | TE_ATTN_HOST_BUFFERS | TE_ATTN_NO_ROPE | TE_ATTN_QKV_BIAS |
+                TE_ATTN_EXACT_Q)) {
     return fail(e, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for te_attention_prefill");
   }
   const size_t hkv = c->d.kv_heads, hd = c->d.head_dim;
@@ -1070,7 +1071,6 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   if (bias && (!c->d_qb || c->bias_heads != heads)) {
     return fail(e, TE_STATUS_INVALID_ARGUMENT, "TE_ATTN_QKV_BIAS needs te_kv_cache_set_qkv_bias with these heads");
   }
-  if (hd != 128) return fail(e, TE_STATUS_UNSUPPORTED, "prefill kernel is built for head_dim 128");
   if (!(flags & TE_ATTN_HOST_BUFFERS) &&
       ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
         reinterpret_cast<uintptr_t>(out)) & 15u)) {
@@ -1082,9 +1082,17 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   if ((uint64_t)(c->offset[seq] + total) > c->d.max_position) {
     return fail(e, TE_STATUS_INVALID_ARGUMENT, "RoPE position beyond max_position");
   }
+  // The kernel multiplies f16 queries.  f16 inputs without RoPE or bias are
+  // read as they are (exact); otherwise the prepared query is fp32 and enters
+  // the tensor cores as hi + lo f16 parts (split) -- always for fp32 inputs,
+  // for f16 inputs when TE_ATTN_EXACT_Q asks -- or rounded once to f16.
+  const bool input_f16 = (flags & TE_ATTN_INPUT_F16) != 0;
+  const bool with_q = !(input_f16 && (flags & TE_ATTN_NO_ROPE) && !bias);
+  const bool split = with_q && (!input_f16 || (flags & TE_ATTN_EXACT_Q));
+  const size_t q_rows_per_token = heads * (split ? 2 : 1);
   const size_t n_pad = (n_tokens + 127) / 128 * 128;
-  const size_t items = (size_t)prefill_items((int)n_layers, (int)heads, (int)hkv, (int)n_pad);
-  const size_t qh_rows = n_layers * heads * n_pad;
+  const size_t items = (size_t)prefill_items((int)n_layers, (int)heads, (int)hkv, (int)n_pad, split);
+  const size_t qh_rows = n_layers * q_rows_per_token * n_pad;
   if (items > (size_t)INT32_MAX || qh_rows >= (1ull << 31)) return fail(e, TE_STATUS_UNSUPPORTED, "prefill too large");
   DeviceGuard dg(e->device);
   te_status st = ensure_pages(c, seq, total);
@@ -1143,11 +1151,10 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   // 2) f16 queries for the kernel: f16 inputs without RoPE or bias are read
   // as they are; otherwise they are biased, rotated and converted into
   // scratch in the same layout, in one pass with the append.
-  const bool with_q = !(a.input_f16 && !a.rope && !bias);
   const void* qf16 = dq;
   QPrepParams qp{};
   if (with_q) {
-    err = grow(e, &e->qh, &e->qh_bytes, n_layers * n_tokens * heads * hd * sizeof(__half), false);
+    err = grow(e, &e->qh, &e->qh_bytes, n_layers * n_tokens * q_rows_per_token * hd * sizeof(__half), false);
     if (err != cudaSuccess) return cuda_fail(e, err, "prefill query scratch allocation");
     qp.q = dq;
     qp.qh = reinterpret_cast<__half*>(e->qh);
@@ -1162,6 +1169,7 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
     qp.heads = (int32_t)heads;
     qp.head_dim = (int32_t)hd;
     qp.first_pos = a.first_pos;
+    qp.split = split ? 1 : 0;
     qf16 = e->qh;
   }
   a.error = e->d_error;
@@ -1172,7 +1180,7 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   // 3) causal flash attention on tcgen05
   PrefillParams p;
   std::memset(&p, 0, sizeof(p));
-  if (!make_tmap_q_f16(&p.tmap_q, qf16, hd, heads, n_tokens, n_layers)) {
+  if (!make_tmap_q_f16(&p.tmap_q, qf16, hd, q_rows_per_token, n_tokens, n_layers)) {
     return fail(e, TE_STATUS_RUNTIME_ERROR, "query tensor map");
   }
   p.tmap_k = c->tmap_k;
@@ -1191,6 +1199,8 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   p.page_tokens = (int32_t)c->d.page_tokens;
   p.n_pages_mapped = (int32_t)((total + c->d.page_tokens - 1) / c->d.page_tokens);
   p.n_items = (int32_t)items;
+  p.head_dim = (int32_t)hd;
+  p.split = split ? 1 : 0;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hd));
   if (e->time_kernels) cudaEventRecord(e->ev_k0, e->stream);
   err = launch_prefill_tc(p, e->sm_count, e->stream);

@@ -218,6 +218,8 @@ struct QPrepParams {
   int32_t heads;
   int32_t head_dim;
   int32_t first_pos;
+  int32_t split;            // 1: write each query row as two f16 rows, hi = f16(q) and lo = f16(q - hi):
+                            // qh [n_layers][n_tokens][heads][2][hd]
 };
 cudaError_t launch_q_prep(const QPrepParams& p, cudaStream_t s);
 // One pass over a prefill call's inputs: the K/V append of `a` and, when
@@ -243,12 +245,15 @@ struct PrefillParams {
   int32_t num_pages;    // pages per layer in the pool
   int32_t page_tokens;
   int32_t n_pages_mapped;  // mapped pages of the sequence (covers q_offset + n_tokens)
-  int32_t n_items;      // work items: n_layers * heads * (n_tokens_padded / 128)
+  int32_t n_items;      // work items (prefill_items)
+  int32_t head_dim;     // 64 or 128
+  int32_t split;        // 1: queries as hi/lo f16 rows (tmap_q over 2 * heads rows per token), one head per item
   float scale_log2;
 };
 cudaError_t launch_prefill_tc(const PrefillParams& p, int sm_count, cudaStream_t s);
-// Work items of the prefill kernel: (layer, kv head, query-head pair, 128-query tile).
-int prefill_items(int n_layers, int heads, int kv_heads, int n_tokens_padded);
+// Work items of the prefill kernel: (layer, kv head, query-head pair -- or one
+// head when split --, 128-query tile).
+int prefill_items(int n_layers, int heads, int kv_heads, int n_tokens_padded, bool split);
 
 // KV-split exchange over NVLink (k_exchange.cu): one kernel per decode step
 // pushes this rank's partial records into every rank's exchange area and

@@ -215,8 +215,7 @@ class QwenDecoder:
         te_qwen_prefill_prompt_batch, qwen.c:630-906): projections of up to 8
         tokens per launch (te_matvec_gguf_fused / te_matvec_gguf with
         n_vectors), one te_attention_prefill launch per layer (bias, RoPE, f16
-        append and causal attention over the cache).  The prefill kernel is
-        built for head_dim 128; other models take forward_token per token.
+        append and causal attention over the cache; head_dim 64 or 128).
         Returns the last token's hidden state, like forward_token."""
         import torch
         toks = [int(t) for t in tokens]
@@ -227,10 +226,6 @@ class QwenDecoder:
             raise ValueError("token outside the vocabulary")
         if position + len(toks) > self.context_tokens:
             raise ValueError("prompt beyond context_tokens")
-        if d["head_dim"] != 128:
-            for i, t in enumerate(toks):
-                x = self.forward_token(t, position + i)
-            return x
         n = self.cache.length(0)
         if position > n:
             raise ValueError("positions must follow one another")

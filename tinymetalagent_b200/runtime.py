@@ -36,6 +36,7 @@ TE_ATTN_QKV_BIAS = 1 << 5
 TE_ATTN_ACCUMULATE = 1 << 6
 TE_ATTN_RMSNORM_INPUT = 1 << 7
 TE_ATTN_SWIGLU_INPUT = 1 << 8
+TE_ATTN_EXACT_Q = 1 << 9
 TE_ATTN_QUANT_GGUF_Q4_0 = 4
 TE_ATTN_QUANT_GGUF_Q8_0 = 8
 
