@@ -287,6 +287,16 @@ def run_gpu(args) -> None:
         if world > 1:
             dist.destroy_process_group()
         return
+    if args.only_configs:
+        # BASELINE configs 4 and 5 alone (e.g. a scaling sweep): one JSON line
+        res = {"ragged7b": run_ragged7b(eng, stream, hbm_peak, peak_src, args, world, rank),
+               "long7b": run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank), "n_gpus": world}
+        eng.close()
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     cap = CTX0 + DECODE_STEPS
     cache = eng.kv_cache(layers=LAYERS, max_seqs=1, max_tokens_per_seq=cap, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
                          rope_theta=THETA)
@@ -562,50 +572,39 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
 
 
-def run_prefill(eng, stream, tc_peak, peak_src, args, world, rank, local):
-    """Config 3: f16 Q/K/V for 2048 tokens x 36 layers; one te_attention_prefill call
-    (RoPE + f16 append, query prep, tcgen05 flash prefill) per step, device-timed."""
+def _measure_prefill(eng, stream, args, world, rank, layers, heads, kv_heads, hd, s, extra_flags=0):
+    """One te_attention_prefill call per step over `layers` layers of an
+    s-token prompt (f16 Q/K/V N(0,1), RoPE theta 1e6): device time per call
+    (CUDA events over the steps, max over ranks), the tcgen05 kernel's own time
+    (events the library records around it), and launches per call."""
     import torch
     import torch.distributed as dist
 
     from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16
-    s = PREFILL_TOKENS
-    cache = eng.kv_cache(layers=LAYERS, max_seqs=1, max_tokens_per_seq=s, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
+    cache = eng.kv_cache(layers=layers, max_seqs=1, max_tokens_per_seq=s, kv_heads=kv_heads, head_dim=hd,
                          rope_theta=THETA)
     g = torch.Generator(device="cuda").manual_seed(99 + rank)
     with torch.cuda.stream(stream):
-        q = torch.randn((LAYERS, s, HEADS, HEAD_DIM), generator=g, device="cuda").half()
-        k = torch.randn((LAYERS, s, KV_HEADS, HEAD_DIM), generator=g, device="cuda").half()
-        v = torch.randn((LAYERS, s, KV_HEADS, HEAD_DIM), generator=g, device="cuda").half()
-        out = torch.empty((LAYERS, s, HEADS, HEAD_DIM), device="cuda")
+        q = torch.randn((layers, s, heads, hd), generator=g, device="cuda").half()
+        k = torch.randn((layers, s, kv_heads, hd), generator=g, device="cuda").half()
+        v = torch.randn((layers, s, kv_heads, hd), generator=g, device="cuda").half()
+        out = torch.empty((layers, s, heads, hd), device="cuda")
     stream.synchronize()
 
     def step():
         cache.truncate(0, 0)
-        cache.prefill(0, LAYERS, 0, q, k, v, s, HEADS, out, TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16)
+        cache.prefill(0, layers, 0, q, k, v, s, heads, out, TE_ATTN_ADVANCE | TE_ATTN_INPUT_F16 | extra_flags)
 
     for _ in range(3):
         step()
     eng.synchronize()
     steps = max(3, min(args.prefill_steps, 50))
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = eng.launch_count
-    ev0.record(stream)
-    for _ in range(steps):
-        step()
-    ev1.record(stream)
-    ev1.synchronize()
+    ms = _time_steps(stream, step, steps, world, dist) / steps
     eng.synchronize()
-    ms = ev0.elapsed_time(ev1) / steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    flops = prefill_flops(s, LAYERS)
-    tflops = flops / (ms / 1e3) / 1e12
     launches = int(eng.launch_count - launches0)
     # the tensor-core kernel alone: CUDA events the library records around it
-    # on its stream (same calls, timed separately from the headline loop)
+    # on its stream (same calls, timed separately from the loop above)
     eng.time_kernels(True)
     kms = []
     for _ in range(steps):
@@ -617,18 +616,53 @@ def run_prefill(eng, stream, tc_peak, peak_src, args, world, rank, local):
         t = torch.tensor([kernel_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         kernel_ms = float(t.item())
-    kernel_tflops = flops / (kernel_ms / 1e3) / 1e12
     cache.close()
-    return {"metric": "causal prefill attention TFLOP/s (BASELINE config 3)", "value": round(tflops * world, 2),
-            "unit": "TFLOP/s", "ms_per_step": round(ms, 4), "steps": steps,
-            "workload": "S=2048, H16/Hkv2/hd128, 36 layers, f16 Q/K/V; one te_attention_prefill call per step "
-                        "(RoPE + K/V append + query preparation pass, then the tcgen05 attention kernel)",
-            "flops_per_step": flops, "gpu_launches": launches,
-            "kernel_ms_per_step": round(kernel_ms, 4),
-            "roofline": {"bound": "tensor", "achieved": round(kernel_tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
-                         "frac": round(kernel_tflops / tc_peak, 4), "kernel": "prefill_tc_kernel (CUDA events)",
-                         "whole_call_frac": round(tflops / tc_peak, 4),
-                         "peak_source": f"{peak_src} (bf16 dense burst)"}}
+    del q, k, v, out
+    return ms, kernel_ms, launches // steps, steps
+
+
+def run_prefill(eng, stream, tc_peak, peak_src, args, world, rank, local):
+    """Config 3: f16 Q/K/V for 2048 tokens x 36 layers; one te_attention_prefill call
+    (RoPE + f16 append, query prep, tcgen05 flash prefill) per step, device-timed.
+    Beside it: the same call with TE_ATTN_EXACT_Q (the rotated query as f16 hi + lo
+    parts, one head per item), and head_dim 64 at the Qwen2.5-0.5B shape."""
+    from tinymetalagent_b200 import TE_ATTN_EXACT_Q
+    s = PREFILL_TOKENS
+    ms, kernel_ms, launches, steps = _measure_prefill(eng, stream, args, world, rank, LAYERS, HEADS, KV_HEADS,
+                                                      HEAD_DIM, s)
+    flops = prefill_flops(s, LAYERS)
+    tflops = flops / (ms / 1e3) / 1e12
+    kernel_tflops = flops / (kernel_ms / 1e3) / 1e12
+    res = {"metric": "causal prefill attention TFLOP/s (BASELINE config 3)", "value": round(tflops * world, 2),
+           "unit": "TFLOP/s", "ms_per_step": round(ms, 4), "steps": steps,
+           "workload": "S=2048, H16/Hkv2/hd128, 36 layers, f16 Q/K/V; one te_attention_prefill call per step "
+                       "(RoPE + K/V append + query preparation pass, then the tcgen05 attention kernel)",
+           "flops_per_step": flops, "gpu_launches": launches * steps,
+           "kernel_ms_per_step": round(kernel_ms, 4),
+           "roofline": {"bound": "tensor", "achieved": round(kernel_tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                        "frac": round(kernel_tflops / tc_peak, 4), "kernel": "prefill_tc_kernel<128> (CUDA events)",
+                        "whole_call_frac": round(tflops / tc_peak, 4),
+                        "peak_source": f"{peak_src} (bf16 dense burst)"}}
+    if not args.no_prefill_variants:
+        ms_x, kms_x, _, _ = _measure_prefill(eng, stream, args, world, rank, LAYERS, HEADS, KV_HEADS, HEAD_DIM, s,
+                                             TE_ATTN_EXACT_Q)
+        res["exact_q"] = {"metric": "config 3 with TE_ATTN_EXACT_Q (rotated query as f16 hi + lo, one head per item)",
+                          "value": round(flops / (ms_x / 1e3) / 1e12 * world, 2), "unit": "TFLOP/s",
+                          "ms_per_step": round(ms_x, 4), "kernel_ms_per_step": round(kms_x, 4),
+                          "kernel_frac": round(flops / (kms_x / 1e3) / 1e12 / tc_peak, 4),
+                          "relative_to_single_rounding": round(ms / ms_x, 4)}
+        L5, H5, K5, D5 = 24, 14, 2, 64  # Qwen2.5-0.5B attention shape
+        f5 = L5 * 4 * H5 * D5 * s * (s + 1) // 2
+        ms_5, kms_5, _, _ = _measure_prefill(eng, stream, args, world, rank, L5, H5, K5, D5, s)
+        res["hd64"] = {"metric": "causal prefill TFLOP/s, head_dim 64 (Qwen2.5-0.5B shape)",
+                       "workload": "S=2048, H14/Hkv2/hd64, 24 layers, f16 Q/K/V N(0,1), RoPE theta 1e6",
+                       "value": round(f5 / (ms_5 / 1e3) / 1e12 * world, 2), "unit": "TFLOP/s",
+                       "flops_per_step": f5, "ms_per_step": round(ms_5, 4), "kernel_ms_per_step": round(kms_5, 4),
+                       "roofline": {"bound": "tensor", "achieved": round(f5 / (kms_5 / 1e3) / 1e12, 1),
+                                    "peak": tc_peak, "unit": "TFLOP/s",
+                                    "frac": round(f5 / (kms_5 / 1e3) / 1e12 / tc_peak, 4),
+                                    "kernel": "prefill_tc_kernel<64> (CUDA events)"}}
+    return res
 
 
 # Config 4 / 5 shapes (Qwen2.5-7B: 28 layers, 28 query heads, 4 KV heads).
@@ -1082,7 +1116,10 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
     ap.add_argument("--no-graph", action="store_true", help="time the decode steps as eager launches")
     ap.add_argument("--prefill-steps", type=int, default=10)
+    ap.add_argument("--no-prefill-variants", action="store_true",
+                    help="skip the exact-query and head_dim-64 prefill measurements")
     ap.add_argument("--no-configs", action="store_true", help="skip the config-4 / config-5 measurements")
+    ap.add_argument("--only-configs", action="store_true", help="run only the config-4 / config-5 measurements")
     ap.add_argument("--no-gemv", action="store_true", help="skip the GGUF matrix-vector measurement")
     ap.add_argument("--no-qwen", action="store_true", help="skip the qwen2 decode-step measurement")
     ap.add_argument("--qwen-steps", type=int, default=64, help="decode steps timed for the qwen2 decode step")
