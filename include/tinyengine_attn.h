@@ -110,6 +110,27 @@ TE_API uint64_t te_attn_engine_launch_count(const te_attn_engine *engine);
  * nothing was recorded). */
 TE_API te_status te_attn_engine_time_kernels(te_attn_engine *engine, int enable);
 TE_API te_status te_attn_engine_last_kernel_ms(te_attn_engine *engine, float *ms);
+/* Bound (1 ms .. 60 s; default 2 s) of the waits in which this engine's
+ * kernels wait for other GPUs (te_attn_exchange_merge's wait for the peers'
+ * pushes).  A wait that runs out sets the engine's error word, which the next
+ * te_attn_engine_synchronize reports as TE_STATUS_RUNTIME_ERROR; the device
+ * context stays usable.  The reference's counterpart is the status check of
+ * each Metal command buffer (c/src/metal/metal_backend_layers.mm.inc:2318,
+ * 2581): a failed GPU step becomes TE_STATUS_RUNTIME_ERROR. */
+TE_API te_status te_attn_engine_set_wait_limit(te_attn_engine *engine, uint32_t milliseconds);
+/* Per-kernel device-time profile: while enabled, every launch of this
+ * library's kernels on the engine's stream is bracketed by a CUDA event pair
+ * (launches captured into a CUDA graph are not timed).  Also enabled at
+ * engine creation by the environment variable TINYENGINE_PROFILE (any value
+ * but "0"), the reference's switch (c/src/qwen.c:47-73, 2216-2304); then the
+ * engine prints its totals to stderr when freed.  The report is one line,
+ * "tinyengine_profile: device_ms=T decode=ms/calls append=... merge=...
+ * prefill_prep=... prefill_attn=... matvec=... exchange=...", the reference's
+ * "name=ms/calls" format.  te_attn_engine_profile_report synchronises the
+ * engine's stream and writes that line to buf (TE_STATUS_INVALID_ARGUMENT if
+ * it does not fit). */
+TE_API te_status te_attn_engine_profile(te_attn_engine *engine, int enable);
+TE_API te_status te_attn_engine_profile_report(te_attn_engine *engine, char *buf, size_t len);
 
 /* KV cache ---------------------------------------------------------------- */
 

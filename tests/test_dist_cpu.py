@@ -110,3 +110,77 @@ def test_kv_split_protocol_gloo(world):
     got = sorted(results.get(timeout=5) for _ in range(world))
     assert [r for r, _ in got] == list(range(world))
     assert all(w <= 0 for _, w in got), got
+
+
+def _fault_worker(rank, world, port_no, store_port, use_store, results):
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port_no)
+    os.environ["TE_FAULT_INJECT"] = "rank:1:step:1"
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=4))
+    outcome = (rank, "no error", -1, -1)
+    try:
+        from tinymetalagent_b200 import TinyEngineError
+        store = dist.TCPStore("127.0.0.1", store_port, world, rank == 0, timeout=timedelta(seconds=20)) \
+            if use_store else None
+        spec = ShardSpec.plan(rank, world, N)
+        rows = H
+
+        def partial_fn(q, k_new, v_new, q_pos):  # a well-formed record: m = 0, l = 1, acc = rank
+            rec = torch.zeros((rows, HD + 2))
+            rec[:, :HD] = float(rank)
+            rec[:, HD + 1] = 1.0
+            return rec
+
+        dec = KVSplitDecoder(spec, 1, H, HD, partial_fn=partial_fn,
+                             merge_fn=lambda g: torch.from_numpy(merge_partials_numpy(g.numpy())), device="cpu",
+                             store=store)
+        q = torch.zeros((1, 1, H, HD))
+        kv = torch.zeros((1, 1, HKV, HD))
+        import time
+        for s in range(3):
+            t0 = time.monotonic()
+            try:
+                out = dec.step(q, kv, kv)
+            except TinyEngineError as e:
+                outcome = (rank, str(e), s, e.status, time.monotonic() - t0)
+                break
+            assert np.allclose(out.numpy(), (world - 1) / 2.0)  # the mean of the ranks' records
+    finally:
+        results.put(outcome)
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+@pytest.mark.parametrize("use_store", [False, True])
+def test_kv_split_rank_failure_ends_every_rank_with_an_error(use_store):
+    """Host-side fault injection (TE_FAULT_INJECT=rank:1:step:1) on three gloo
+    ranks: rank 1 fails its second step before any launch; the other ranks end
+    that step with TinyEngineError / TE_STATUS_RUNTIME_ERROR -- from the shared
+    store's fault record, or from the process group's 4 s timeout that ends
+    their all-gather -- and no process hangs."""
+    from tinymetalagent_b200.runtime import TE_STATUS_RUNTIME_ERROR
+    world = 3
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    ports = (_free_port(), _free_port())
+    procs = [ctx.Process(target=_fault_worker, args=(r, world, ports[0], ports[1], use_store, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    stuck = [p for p in procs if p.is_alive()]
+    for p in stuck:  # our own children only
+        p.kill()
+    assert not stuck, "a rank hung"
+    got = sorted(results.get(timeout=5) for _ in range(world))
+    assert [g[0] for g in got] == list(range(world))
+    for rank, msg, step, status, *_ in got:
+        assert step == 1 and status == TE_STATUS_RUNTIME_ERROR, (rank, msg)
+        if rank == 1:
+            assert "injected fault" in msg
+        else:
+            assert "reported a failure" in msg or "all-gather" in msg, msg

@@ -22,8 +22,9 @@
 // ahead of any peer (its step s+1 waits for the peers' step s+1 pushes, which
 // each peer makes after its step s merge), so the two parities never overlap.
 // The step count lives in device memory, so replaying a captured CUDA graph
-// continues the sequence.  The wait is bounded (2 s); it sets the engine's
-// error word and gives up.
+// continues the sequence.  The wait is bounded (the engine's wait limit, 2 s
+// unless te_attn_engine_set_wait_limit changed it); when it runs out the CTA
+// sets the engine's error word and leaves without merging.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -79,7 +80,7 @@ __global__ void __launch_bounds__(256) exchange_merge_kernel(const __grid_consta
       const uint64_t start = globaltimer_ns();
       while (ld_acquire_sys(mine) < target) {
         __nanosleep(64);
-        if (globaltimer_ns() - start > kWaitLimitNs) {
+        if (globaltimer_ns() - start > p.wait_ns) {
           set_error(p.error, 40);
           ok = 0;
           break;

@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -43,6 +44,19 @@ struct te_attn_engine {
   bool time_kernels = false;  // te_attn_engine_time_kernels
   bool kernel_timed = false;
   cudaEvent_t ev_k0 = nullptr, ev_k1 = nullptr;
+  uint64_t wait_ns = 2000000000ull;  // bound of the exchange kernel's waits for other GPUs
+  // Per-kernel device-time profile (te_attn_engine_profile, TINYENGINE_PROFILE=1):
+  // an event pair around every launch, resolved when the engine synchronises.
+  bool profile = false;
+  bool profile_env = false;  // enabled by TINYENGINE_PROFILE: printed to stderr when the engine is freed
+  struct ProfPair {
+    int kind;
+    cudaEvent_t a, b;
+  };
+  std::vector<ProfPair> prof_pending;
+  std::vector<ProfPair> prof_free;
+  double prof_ms[8] = {};
+  uint64_t prof_calls[8] = {};
 };
 
 struct te_kv_cache {
@@ -103,6 +117,69 @@ te_status cuda_fail(te_attn_engine* e, cudaError_t err, const char* what) {
 bool cuda_device_available() {
   int n = 0;
   return cudaGetDeviceCount(&n) == cudaSuccess && n > 0;
+}
+
+// Kernel families of the profile, in report order.
+enum ProfKind { PK_DECODE = 0, PK_APPEND, PK_MERGE, PK_PREFILL_PREP, PK_PREFILL_ATTN, PK_MATVEC, PK_EXCHANGE, PK_COUNT };
+const char* const kProfNames[PK_COUNT] = {"decode",       "append", "merge",   "prefill_prep",
+                                          "prefill_attn", "matvec", "exchange"};
+
+// Opens a profiled launch: records the first event of a pair on the engine's
+// stream and returns its slot, or -1 when profiling is off or the stream is
+// being captured into a graph (event timing does not apply to replays).
+int prof_begin(te_attn_engine* e, int kind) {
+  if (!e->profile) return -1;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(e->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return -1;
+  te_attn_engine::ProfPair pp;
+  if (!e->prof_free.empty()) {
+    pp = e->prof_free.back();
+    e->prof_free.pop_back();
+  } else if (cudaEventCreate(&pp.a) != cudaSuccess || cudaEventCreate(&pp.b) != cudaSuccess) {
+    return -1;
+  }
+  pp.kind = kind;
+  cudaEventRecord(pp.a, e->stream);
+  e->prof_pending.push_back(pp);
+  return (int)e->prof_pending.size() - 1;
+}
+
+void prof_end(te_attn_engine* e, int slot) {
+  if (slot >= 0) cudaEventRecord(e->prof_pending[(size_t)slot].b, e->stream);
+}
+
+// Folds every completed pair into the per-kind totals (waits for none).
+void prof_collect(te_attn_engine* e) {
+  std::vector<te_attn_engine::ProfPair> keep;
+  for (const auto& pp : e->prof_pending) {
+    if (cudaEventQuery(pp.b) != cudaSuccess) {
+      keep.push_back(pp);
+      continue;
+    }
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, pp.a, pp.b) == cudaSuccess) {
+      e->prof_ms[pp.kind] += ms;
+      e->prof_calls[pp.kind] += 1;
+    }
+    e->prof_free.push_back(pp);
+  }
+  e->prof_pending.swap(keep);
+  (void)cudaGetLastError();  // a query of a not-yet-complete event is not an error
+}
+
+std::string prof_line(const te_attn_engine* e) {
+  double total = 0.0;
+  for (int k = 0; k < PK_COUNT; ++k) total += e->prof_ms[k];
+  std::string out;
+  char buf[96];
+  std::snprintf(buf, sizeof(buf), "tinyengine_profile: device_ms=%.3f", total);
+  out += buf;
+  for (int k = 0; k < PK_COUNT; ++k) {
+    std::snprintf(buf, sizeof(buf), " %s=%.3f/%llu", kProfNames[k], e->prof_ms[k],
+                  (unsigned long long)e->prof_calls[k]);
+    out += buf;
+  }
+  return out;
 }
 
 // Grows a device buffer; the stream is drained first so no queued kernel uses the old one.
@@ -372,6 +449,8 @@ TE_API te_status te_attn_engine_create(const te_attn_options* options, te_attn_e
     return TE_STATUS_OUT_OF_MEMORY;
   }
   e->tile_counter = reinterpret_cast<uint32_t*>(e->d_error + 4);
+  const char* prof = std::getenv("TINYENGINE_PROFILE");
+  if (prof && prof[0] && std::strcmp(prof, "0") != 0) e->profile = e->profile_env = true;
   *out_engine = e;
   return TE_STATUS_OK;
 }
@@ -388,6 +467,16 @@ TE_API void te_attn_engine_free(te_attn_engine* e) {
     cudaFree(e->qh);
     if (e->ev_k0) cudaEventDestroy(e->ev_k0);
     if (e->ev_k1) cudaEventDestroy(e->ev_k1);
+    prof_collect(e);
+    if (e->profile_env) std::fprintf(stderr, "%s\n", prof_line(e).c_str());
+    for (const auto& pp : e->prof_pending) {
+      cudaEventDestroy(pp.a);
+      cudaEventDestroy(pp.b);
+    }
+    for (const auto& pp : e->prof_free) {
+      cudaEventDestroy(pp.a);
+      cudaEventDestroy(pp.b);
+    }
     if (e->own_stream && e->stream) cudaStreamDestroy(e->stream);
   }
   delete e;
@@ -414,6 +503,7 @@ TE_API te_status te_attn_engine_synchronize(te_attn_engine* e) {
   DeviceGuard dg(e->device);
   cudaError_t err = cudaStreamSynchronize(e->stream);
   if (err != cudaSuccess) return cuda_fail(e, err, "stream synchronize");
+  if (e->profile) prof_collect(e);
   int code = 0;
   err = cudaMemcpy(&code, e->d_error, sizeof(int), cudaMemcpyDeviceToHost);
   if (err != cudaSuccess) return cuda_fail(e, err, "error word read");
@@ -443,6 +533,29 @@ TE_API te_status te_attn_engine_time_kernels(te_attn_engine* e, int enable) {
   e->time_kernels = enable != 0;
   e->kernel_timed = false;
   return TE_STATUS_OK;
+}
+
+TE_API te_status te_attn_engine_set_wait_limit(te_attn_engine* e, uint32_t milliseconds) {
+  if (!e || milliseconds == 0 || milliseconds > 60000) return TE_STATUS_INVALID_ARGUMENT;
+  e->wait_ns = (uint64_t)milliseconds * 1000000ull;
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_attn_engine_profile(te_attn_engine* e, int enable) {
+  if (!e) return TE_STATUS_INVALID_ARGUMENT;
+  e->profile = enable != 0;
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_attn_engine_profile_report(te_attn_engine* e, char* buf, size_t len) {
+  if (!e || !buf || len == 0) return TE_STATUS_INVALID_ARGUMENT;
+  DeviceGuard dg(e->device);
+  cudaError_t err = cudaStreamSynchronize(e->stream);
+  if (err != cudaSuccess) return cuda_fail(e, err, "stream synchronize");
+  prof_collect(e);
+  const std::string line = prof_line(e);
+  std::snprintf(buf, len, "%s", line.c_str());
+  return line.size() < len ? TE_STATUS_OK : TE_STATUS_INVALID_ARGUMENT;
 }
 
 TE_API te_status te_attn_engine_last_kernel_ms(te_attn_engine* e, float* ms) {
@@ -700,7 +813,9 @@ TE_API te_status te_kv_append_rope(te_kv_cache* c, size_t layer_begin, size_t n_
   p.head_dim = (int32_t)c->d.head_dim;
   p.num_pages = (int32_t)c->d.total_pages;
   p.page_tokens = (int32_t)c->d.page_tokens;
+  const int prof = prof_begin(e, PK_APPEND);
   cudaError_t err = launch_append_rope(p, e->stream);
+  prof_end(e, prof);
   if (err != cudaSuccess) return cuda_fail(e, err, "append kernel launch");
   e->launches++;
   if (flags & TE_ATTN_ADVANCE) c->len[seq] = first + (int64_t)n_tokens;
@@ -849,7 +964,9 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
       if (err != cudaSuccess) return cuda_fail(e, err, "decode scratch allocation");
       p.partials = e->partials;
       p.counters = e->counters;
+      const int prof = prof_begin(e, PK_DECODE);
       err = launch_decode_f16(p, (int)hd, e->stream);
+      prof_end(e, prof);
       if (err != cudaSuccess) return cuda_fail(e, err, "decode kernel launch");
       return TE_STATUS_OK;
     };
@@ -883,8 +1000,10 @@ TE_API te_status te_attention_merge_partials(te_attn_engine* e, const float* par
   if (flags & ~TE_ATTN_PARTIAL) return fail(e, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for merge");
   if (rows > (size_t)INT32_MAX) return TE_STATUS_UNSUPPORTED;
   DeviceGuard dg(e->device);
+  const int prof = prof_begin(e, PK_MERGE);
   cudaError_t err = launch_merge_partials(partials, (int)n_parts, (int)rows, (int)head_dim, out,
                                           (flags & TE_ATTN_PARTIAL) ? 1 : 0, e->stream);
+  prof_end(e, prof);
   if (err != cudaSuccess) return cuda_fail(e, err, "merge kernel launch");
   e->launches++;
   return TE_STATUS_OK;
@@ -913,7 +1032,9 @@ TE_API te_status te_matvec_gguf(te_attn_engine* e, uint32_t quant, const void* w
   p.cols = (int32_t)cols;
   p.accumulate = (flags & TE_ATTN_ACCUMULATE) ? 1 : 0;
   p.error = e->d_error;
+  const int prof = prof_begin(e, PK_MATVEC);
   const cudaError_t err = launch_gemv_gguf(p, block_bytes, (int)n_vectors, e->sm_count, e->stream);
+  prof_end(e, prof);
   if (err != cudaSuccess) return cuda_fail(e, err, "matvec kernel launch");
   e->launches++;
   return TE_STATUS_OK;
@@ -953,7 +1074,9 @@ TE_API te_status te_matvec_gguf_fused(te_attn_engine* e, uint32_t quant, const v
   p.prologue = pro == TE_ATTN_RMSNORM_INPUT ? 1 : 2;
   p.norm_w = norm_weight;
   p.eps = eps;
+  const int prof = prof_begin(e, PK_MATVEC);
   const cudaError_t err = launch_gemv_gguf(p, block_bytes, (int)n_vectors, e->sm_count, e->stream);
+  prof_end(e, prof);
   if (err != cudaSuccess) return cuda_fail(e, err, "matvec kernel launch");
   e->launches++;
   return TE_STATUS_OK;
@@ -1034,7 +1157,10 @@ TE_API te_status te_attn_exchange_merge(te_attn_exchange* x, const float* partia
   p.head_dim = x->hd;
   p.grid = x->grid;
   p.rows_per_cta = (x->rows + x->grid - 1) / x->grid;
+  p.wait_ns = e->wait_ns;
+  const int prof = prof_begin(e, PK_EXCHANGE);
   const cudaError_t err = launch_exchange_merge(p, e->stream);
+  prof_end(e, prof);
   if (err != cudaSuccess) return cuda_fail(e, err, "exchange kernel launch");
   e->launches++;
   return TE_STATUS_OK;
@@ -1173,7 +1299,9 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
     qf16 = e->qh;
   }
   a.error = e->d_error;
+  int prof = prof_begin(e, PK_PREFILL_PREP);
   err = launch_prefill_prep(a, qp, with_q, e->sm_count, e->stream);
+  prof_end(e, prof);
   if (err != cudaSuccess) return cuda_fail(e, err, "append / query preparation launch");
   e->launches++;
 
@@ -1203,7 +1331,9 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
   p.split = split ? 1 : 0;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hd));
   if (e->time_kernels) cudaEventRecord(e->ev_k0, e->stream);
+  prof = prof_begin(e, PK_PREFILL_ATTN);
   err = launch_prefill_tc(p, e->sm_count, e->stream);
+  prof_end(e, prof);
   if (err != cudaSuccess) return cuda_fail(e, err, "prefill kernel launch");
   if (e->time_kernels) {
     cudaEventRecord(e->ev_k1, e->stream);

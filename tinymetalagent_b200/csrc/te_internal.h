@@ -266,6 +266,7 @@ struct ExchangeParams {
   uint32_t* steps;                      // this rank's per-CTA step counts
   int* error;
   int32_t world, rank, rows, head_dim, rows_per_cta, grid;
+  uint64_t wait_ns;                     // bound of the wait for the peers' pushes
 };
 size_t exchange_area_bytes(int world, int rows, int head_dim, int grid);
 int exchange_grid(int rows);

@@ -14,13 +14,38 @@ on a single device; there is no counterpart):
 
 The per-rank compute of ``KVSplitDecoder`` is the engine; tests replace it with
 a CPU stand-in to check the partition/gather/merge protocol on gloo ranks.
+
+Failures surface as ``TinyEngineError`` with TE_STATUS_RUNTIME_ERROR, the
+reference's status for a failed GPU step (a Metal command buffer that did not
+complete, c/src/metal/metal_backend_layers.mm.inc:2318,2581).  A rank that
+fails records it in an optional host store before raising; the other ranks
+check the store before each step's launches, and a rank already inside the
+exchange ends it through the process group's timeout (NCCL, gloo) or the
+engine's bounded wait (the NVLink exchange, ``AttnEngine.set_wait_limit``).
+``TE_FAULT_INJECT="rank:k"`` (or ``"rank:k:step:s"``) makes rank k fail its
+step s (default 0) on the host, before any launch of that step, to test this.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Callable, Optional, Sequence
 
 import numpy as np
+
+FAULT_KEY = "te_kv_split_fault"
+
+
+def injected_fault(rank: int, step: int, spec: Optional[str] = None) -> bool:
+    """True when TE_FAULT_INJECT (or `spec`) names this rank and step:
+    "rank:k" fails step 0 of rank k, "rank:k:step:s" its step s."""
+    spec = os.environ.get("TE_FAULT_INJECT", "") if spec is None else spec
+    if not spec:
+        return False
+    parts = spec.split(":")
+    if len(parts) not in (2, 4) or parts[0] != "rank" or (len(parts) == 4 and parts[2] != "step"):
+        raise ValueError(f"TE_FAULT_INJECT must be 'rank:k' or 'rank:k:step:s', not {spec!r}")
+    return int(parts[1]) == rank and (int(parts[3]) if len(parts) == 4 else 0) == step
 
 
 def shard_sequences(lengths: Sequence[int], world: int) -> list[list[int]]:
@@ -83,12 +108,17 @@ class KVSplitDecoder:
                te_attention_merge_partials; "p2p": one kernel pushes them into
                the peers' memory over NVLink and merges what arrived
                (te_attn_exchange_*; needs one GPU per rank, world <= 8)
+    store      optional torch.distributed Store shared by the ranks: a rank that
+               fails writes FAULT_KEY there, and every rank checks it before
+               each step's launches (one host round trip per step)
     """
 
     def __init__(self, spec: ShardSpec, n_layers: int, heads: int, head_dim: int, cache=None, engine=None,
                  group=None, partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None,
-                 device=None, exchange: str = "nccl"):
+                 device=None, exchange: str = "nccl", store=None):
         self.spec = spec
+        self.store = store
+        self.steps_done = 0
         self.n_layers, self.heads, self.head_dim = n_layers, heads, head_dim
         self.cache, self.engine, self.group = cache, engine, group
         self.partial_fn = partial_fn
@@ -144,16 +174,34 @@ class KVSplitDecoder:
             self.cache.decode(0, self.n_layers, [0], q, self._part, self.heads, q_positions=[q_pos],
                               flags=TE_ATTN_PARTIAL)
 
+    def _fail(self, why: str, cause: Optional[BaseException] = None):
+        from .runtime import TE_STATUS_RUNTIME_ERROR, TinyEngineError
+        if self.store is not None:
+            try:
+                self.store.set(FAULT_KEY, str(self.spec.rank))
+            except Exception:  # the store itself may be gone; the error below still stands
+                pass
+        raise TinyEngineError(f"KV-split rank {self.spec.rank}, step {self.steps_done}: {why}",
+                              TE_STATUS_RUNTIME_ERROR) from cause
+
     def step(self, q, k_new, v_new):
         """One decode step: q [n_layers][1][heads][hd] raw fp32 (every rank gets the
         same q), k_new/v_new [n_layers][1][kv_heads][hd] (used by the tail rank).
         Returns the merged attention output [n_layers][1][heads][hd] on every rank
-        (ready in stream order on the engine's stream)."""
+        (ready in stream order on the engine's stream).  Raises TinyEngineError
+        (TE_STATUS_RUNTIME_ERROR) when this rank fails or learns that a peer has."""
+        if self.store is not None and self.store.check([FAULT_KEY]):
+            self._fail(f"rank {self.store.get(FAULT_KEY).decode()} reported a failure; no launch made")
+        if injected_fault(self.spec.rank, self.steps_done):
+            self._fail("injected fault (TE_FAULT_INJECT)")
         if self._stream is None:
-            return self._step(q, k_new, v_new)
-        import torch
-        with torch.cuda.stream(self._stream):
-            return self._step(q, k_new, v_new)
+            out = self._step(q, k_new, v_new)
+        else:
+            import torch
+            with torch.cuda.stream(self._stream):
+                out = self._step(q, k_new, v_new)
+        self.steps_done += 1
+        return out
 
     def _step(self, q, k_new, v_new):
         import torch.distributed as dist
@@ -164,7 +212,10 @@ class KVSplitDecoder:
             self.length += 1
             return self._out
         if self.spec.world > 1:
-            dist.all_gather_into_tensor(self._gather_flat, self._part, group=self.group)
+            try:
+                dist.all_gather_into_tensor(self._gather_flat, self._part, group=self.group)
+            except Exception as e:  # a peer failed or left: the group's timeout ended the collective
+                self._fail(f"all-gather of the partial records failed ({type(e).__name__})", e)
         else:
             self._gather[0].copy_(self._part)
         if self.merge_fn is not None:

@@ -106,6 +106,9 @@ SIGNATURES: dict[str, tuple] = {
     "te_attn_engine_last_error": (ctypes.c_char_p, [_vp]),
     "te_attn_engine_launch_count": (ctypes.c_uint64, [_vp]),
     "te_attn_engine_time_kernels": (_int, [_vp, _int]),
+    "te_attn_engine_set_wait_limit": (_int, [_vp, ctypes.c_uint32]),
+    "te_attn_engine_profile": (_int, [_vp, _int]),
+    "te_attn_engine_profile_report": (_int, [_vp, ctypes.c_char_p, _sz]),
     "te_attn_engine_last_kernel_ms": (_int, [_vp, ctypes.POINTER(ctypes.c_float)]),
     "te_kv_cache_default_desc": (KVCacheDesc, []),
     "te_kv_cache_create": (_int, [_vp, ctypes.POINTER(KVCacheDesc), ctypes.POINTER(_vp)]),
@@ -262,6 +265,20 @@ class AttnEngine:
         ms = ctypes.c_float(0.0)
         self.check(self.lib.te_attn_engine_last_kernel_ms(self.handle, ctypes.byref(ms)))
         return float(ms.value)
+
+    def set_wait_limit(self, milliseconds: int) -> None:
+        """Bound of the waits for other GPUs (the NVLink exchange); see te_attn_engine_set_wait_limit."""
+        self.check(self.lib.te_attn_engine_set_wait_limit(self.handle, int(milliseconds)))
+
+    def profile(self, enable: bool = True) -> None:
+        """Per-kernel device-time profile of this engine's launches (TINYENGINE_PROFILE)."""
+        self.check(self.lib.te_attn_engine_profile(self.handle, 1 if enable else 0))
+
+    def profile_report(self) -> str:
+        """The profile's 'tinyengine_profile: device_ms=... decode=ms/calls ...' line (synchronises)."""
+        buf = ctypes.create_string_buffer(512)
+        self.check(self.lib.te_attn_engine_profile_report(self.handle, buf, len(buf)))
+        return buf.value.decode()
 
     def merge_partials(self, partials, n_parts: int, rows: int, head_dim: int, out, partial_out: bool = False):
         self.check(self.lib.te_attention_merge_partials(
