@@ -1092,8 +1092,10 @@ def run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank):
             "unit": "tokens/s", "scaling": "strong", "steps": steps, "ms_per_step": round(ms / steps, 4),
             "workload": "long7b: one sequence of 32768 cached tokens, 28 layers, H28/Hkv4/hd128, f16 KV N(0,1), "
                         f"KV split over {world} rank(s), "
-                        + ("NVLink push of (acc, m, l) into the peers + LSE merge in one kernel per step; "
-                           if exchange == "p2p" else "NCCL all-gather of (acc, m, l) + LSE merge per step; ")
+                        + {"p2p": "NVLink push of (acc, m, l) into the peers + LSE merge in one kernel per step; ",
+                           "fused": "exchange fused into the decode launch (the last rank to finish a (layer, kv "
+                                    "head) group merges it over NVLink into every rank's output); ",
+                           "nccl": "NCCL all-gather of (acc, m, l) + LSE merge per step; "}[exchange]
                         + "steps captured in one CUDA graph",
             "exchange": exchange,
             "tokens_per_rank": n_local, "kv_gbs": round(gbs, 1),
@@ -1129,8 +1131,9 @@ def main() -> None:
                     help="run only the GGUF matrix-vector measurement (Q4_0: launches 1-23, Q8_0: 24-46)")
     ap.add_argument("--cfg-steps", type=int, default=16, help="decode steps timed for config 4")
     ap.add_argument("--long-steps", type=int, default=128, help="decode steps timed for config 5")
-    ap.add_argument("--long-exchange", choices=["nccl", "p2p"], default="nccl",
-                    help="config 5 at N>1: NCCL all-gather + merge, or the NVLink exchange kernel")
+    ap.add_argument("--long-exchange", choices=["nccl", "p2p", "fused"], default="nccl",
+                    help="config 5 at N>1: NCCL all-gather + merge, the NVLink exchange kernel, or the exchange "
+                         "fused into the decode launch")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -1,5 +1,5 @@
-"""KV-sequence split on two GPUs (BASELINE config 5's partitioning): each rank
-holds half of one sequence's cache, computes partial (acc, m, l) records, the
+"""KV-sequence split on two or four GPUs (BASELINE config 5's partitioning): each rank
+holds a contiguous part of one sequence's cache, computes partial (acc, m, l) records, the
 records are exchanged -- all-gathered over NCCL, or pushed into the peer's
 memory over NVLink by the p2p exchange kernel -- and merged by log-sum-exp;
 the tail rank appends the new token.  Checked against the CPU oracle over the whole
@@ -77,17 +77,22 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
-def test_kv_split_two_gpus_matches_oracle(port, tmp_path, exchange):
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("exchange", ["nccl", "p2p", "fused"])
+def test_kv_split_two_gpus_matches_oracle(port, tmp_path, exchange, world):
+    """world ranks (2, or 4 where the box has them), each on its own GPU;
+    exchange: NCCL all-gather + merge kernel, the NVLink push kernel, or the
+    exchange fused into the decode launch (te_attention_decode_kv_split)."""
     import torch
     import torch.multiprocessing as mp
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path), exchange), nprocs=2, join=True,
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), exchange), nprocs=world, join=True,
                        start_method="spawn")
     kraw, vraw, qraw = _data()
-    outs = [np.load(tmp_path / f"out{r}.npy") for r in range(2)]
-    assert np.array_equal(outs[0], outs[1])  # every rank holds the same merged output
+    outs = [np.load(tmp_path / f"out{r}.npy") for r in range(world)]
+    for r in range(1, world):
+        assert np.array_equal(outs[0], outs[r])  # every rank holds the same merged output
     for layer in range(L):
         kb, vb = port.append_rope_f16(kraw[layer], vraw[layer], 0, HKV, HD, THETA)
         kf = port.f16_bits_to_f32(kb)

@@ -75,7 +75,8 @@ struct DecodeCfg {
   static constexpr int kOffRes = kOffNew + 2 * kNewBytes;
   static constexpr int kOffBar = kOffRes + 2 * kResBytes;
   static constexpr int kNumBars = 2 * kRing + 15;  // full, empty, [2] each: qfull qempty fready fempty mready mfree nready; cbar
-  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 1024;
+  static constexpr int kOffFlag = kOffBar + kNumBars * 8;  // two flag words of the fused KV-split exchange
+  static constexpr int kSmemBytes = kOffFlag + 16 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
 };
 
@@ -173,12 +174,109 @@ __device__ __forceinline__ void store_result(const DecodeParams& p, size_t orow,
   if (!p.partial_out) {
     const float inv = 1.f / L;
     *reinterpret_cast<float4*>(p.out + orow * HD + d) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+  } else if (p.partial_out == 2) {
+    float* r = p.out + orow * (HD + 4);  // the fused exchange's 16-byte aligned records
+    *reinterpret_cast<float4*>(r + d) = O;
+    if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
   } else {
     float* r = p.out + orow * (HD + 2);
     *reinterpret_cast<float2*>(r + d) = make_float2(O.x, O.y);
     *reinterpret_cast<float2*>(r + d + 2) = make_float2(O.z, O.w);
     if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
   }
+}
+
+// Fused KV-split exchange: the NT threads that stored group gidx's records
+// (rows orow0 .. orow0 + group - 1 of this rank's record region) call this
+// together; `sync` is a barrier of exactly those threads and `flag` a shared
+// word of theirs.  They arrive on the group's counter at its home rank; the
+// arrival that completes the world (counts are taken modulo world, one
+// arrival per rank and step) merges the group: it reads every rank's records
+// over NVLink (the arrivals' release / acquire order them), combines them by
+// log-sum-exp as te_attention_merge_partials does, writes the merged rows into
+// every rank's output region and counts the group as merged at every rank.
+// Nobody waits here.
+template <int HD, int NT, typename Sync>
+__device__ __noinline__ void xch_group_finished(const DecodeParams& p, int gidx, size_t orow0, int t, Sync sync,
+                                                volatile uint32_t* flag) {
+  constexpr int REC = HD + 4;
+  constexpr int kC = HD / 4;
+  __threadfence_system();  // this thread's record stores are visible to every GPU before the arrival
+  sync();
+  if (t == 0) {
+    const uint32_t old = atom_add_acq_rel_sys(p.xch_cnt[gidx % p.xch_world] + gidx, 1u);
+    *flag = (old + 1u) % (uint32_t)p.xch_world == 0u ? 1u : 0u;
+  }
+  sync();
+  const uint32_t last = *flag;
+  sync();  // the flag is read before its next use
+  if (!last) return;
+  for (int i = t; i < p.group * kC; i += NT) {
+    const size_t orow = orow0 + i / kC;
+    const int c = (i % kC) * 4;
+    float m[kMaxExchangeRanks], l[kMaxExchangeRanks];
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kMaxExchangeRanks; ++w) {
+      if (w >= p.xch_world) break;
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.xch_rec[w] + orow * REC + HD));
+      m[w] = ml.x;
+      l[w] = ml.y;
+      if (ml.y > 0.f) M = fmaxf(M, ml.x);
+    }
+    float L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kMaxExchangeRanks; ++w) {
+      if (w >= p.xch_world) break;
+      if (!(l[w] > 0.f)) continue;
+      const float sw = ex2(m[w] - M);
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(p.xch_rec[w] + orow * REC + c));
+      L += l[w] * sw;
+      O.x += a.x * sw;
+      O.y += a.y * sw;
+      O.z += a.z * sw;
+      O.w += a.w * sw;
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    O = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+#pragma unroll
+    for (int w = 0; w < kMaxExchangeRanks; ++w) {
+      if (w >= p.xch_world) break;
+      *reinterpret_cast<float4*>(p.xch_out[w] + orow * HD + c) = O;
+    }
+  }
+  __threadfence_system();  // merged rows visible everywhere before they are counted
+  sync();
+  if (t == 0) {
+    for (int w = 0; w < p.xch_world; ++w) red_add_release_sys(p.xch_done[w], 1u);
+  }
+}
+
+// End of the fused exchange on this rank: the CTA whose consumer warps finish
+// last waits (bounded) until every group of the call has been merged into
+// this rank's output, so that the kernel's completion orders the merged rows
+// before later work on the stream.  done = {merged groups (cumulative), CTA
+// ticket, completed steps}.
+__device__ __noinline__ void xch_finish(const DecodeParams& p) {
+  uint32_t* done = p.xch_done[p.xch_rank];
+  __threadfence();
+  const uint32_t ticket = atomicAdd(done + 1, 1u);
+  if (ticket != (uint32_t)p.grid - 1u) return;
+  const uint32_t groups = (uint32_t)(p.n_layers * p.kv_heads * p.n_seqs);
+  const uint32_t target = (done[2] + 1u) * groups;
+  if ((int32_t)(ld_acquire_sys_u32(done) - target) < 0) {
+    const uint64_t start = globaltimer_ns();
+    while ((int32_t)(ld_acquire_sys_u32(done) - target) < 0) {
+      __nanosleep(100);
+      if (globaltimer_ns() - start > p.xch_wait_ns) {
+        set_error(p.error, 41);
+        break;
+      }
+    }
+  }
+  done[1] = 0u;
+  done[2] += 1u;
 }
 
 // CTA owning stage s: the b with start(b) <= s < start(b + 1).
@@ -603,6 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
           if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
         }
       }
+      int finished = single ? 1 : 0;  // this warp stored the group's final rows
       if (!single) {
         // The last CTA of the group to finish folds all the parts' records, in
         // part order (so the result does not depend on which CTA came last).
@@ -673,7 +772,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
             const int row = r0 + u * kRowStep;
             if (row < G) store_result<HD>(p, qrow0 + row, d, O[u], M[u], L[u]);
           }
+          finished = 1;
         }
+      }
+      if (p.xch_world > 1 && finished) {
+        xch_group_finished<HD, 32>(p, w.gidx, qrow0, lane, [] { __syncwarp(); },
+                                   reinterpret_cast<volatile uint32_t*>(smem + C::kOffFlag));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&mfree[b]);
@@ -770,6 +874,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
   }
 
   // ---- consumer warps 0-3 ------------------------------------------------
+  volatile uint32_t* cflag = reinterpret_cast<volatile uint32_t*>(smem + C::kOffFlag + 4);
   const int g = lane >> 2;  // mma group id: head rows g and g+8, token rows
   const int c = lane & 3;   // thread in group
   const float sl = p.scale_log2;
@@ -1062,6 +1167,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
 #pragma unroll
         for (int f = 0; f < kF; ++f) store_result<HD>(p, qrow0 + row, 4 * (cl + f * kTPR), O2[f], M2, L2);
       }
+      if (p.xch_world > 1) xch_group_finished<HD, 128>(p, w.gidx, qrow0, t, [] { consumer_bar_sync(); }, cflag);
       continue;
     }
     const int b_first = cta_of(p, w.gs0);
@@ -1071,6 +1177,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
 #pragma unroll
         for (int f = 0; f < kF; ++f) store_result<HD>(p, qrow0 + row, 4 * (cl + f * kTPR), O[f], M, L);
       }
+      if (p.xch_world > 1) xch_group_finished<HD, 128>(p, w.gidx, qrow0, t, [] { consumer_bar_sync(); }, cflag);
       continue;
     }
     // Split group: publish this part's record, take a ticket; the last part
@@ -1152,6 +1259,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
 #pragma unroll
       for (int f = 0; f < kF; ++f) store_result<HD>(p, qrow0 + row, 4 * (cl + f * kTPR), O2[f], M2, L2);
     }
+    if (p.xch_world > 1) xch_group_finished<HD, 128>(p, w.gidx, qrow0, t, [] { consumer_bar_sync(); }, cflag);
+  }
+  if (p.xch_world > 1) {
+    consumer_bar_sync();
+    if (tid == 0) xch_finish(p);
   }
 }
 

@@ -822,9 +822,12 @@ TE_API te_status te_kv_append_rope(te_kv_cache* c, size_t layer_begin, size_t n_
   return TE_STATUS_OK;
 }
 
-TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t n_layers, const uint32_t* seq_ids,
-                                     size_t n_seqs, const int64_t* q_positions, const float* q, const float* k_new,
-                                     const float* v_new, size_t heads, float* out, uint32_t flags) {
+// The decode call; with an exchange x (one sequence, no host buffers or
+// public partial records) the records go to x's area and the kernel runs the
+// fused KV-split exchange.
+static te_status decode_call(te_kv_cache* c, size_t layer_begin, size_t n_layers, const uint32_t* seq_ids,
+                             size_t n_seqs, const int64_t* q_positions, const float* q, const float* k_new,
+                             const float* v_new, size_t heads, float* out, uint32_t flags, te_attn_exchange* x) {
   if (!c || !seq_ids || !q || !out || n_layers == 0 || n_seqs == 0 || heads == 0 ||
       layer_begin + n_layers > c->d.layers || (k_new == NULL) != (v_new == NULL)) {
     return TE_STATUS_INVALID_ARGUMENT;
@@ -936,6 +939,22 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
   p.rope = (flags & TE_ATTN_NO_ROPE) ? 0 : 1;
   p.partial_out = (flags & TE_ATTN_PARTIAL) ? 1 : 0;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hd));
+  if (x) {
+    const size_t push = exchange_area_bytes(x->world, x->rows, x->hd, x->grid);
+    const FusedLayout f = fused_layout(push, x->rows, x->hd);
+    p.partial_out = 2;
+    p.out = reinterpret_cast<float*>(reinterpret_cast<char*>(x->local) + f.rec);
+    p.xch_world = x->world;
+    p.xch_rank = x->rank;
+    p.xch_wait_ns = e->wait_ns;
+    for (int w = 0; w < x->world; ++w) {
+      char* b = reinterpret_cast<char*>(x->base[w]);
+      p.xch_rec[w] = reinterpret_cast<float*>(b + f.rec);
+      p.xch_out[w] = reinterpret_cast<float*>(b + f.out);
+      p.xch_cnt[w] = reinterpret_cast<uint32_t*>(b + f.cnt);
+      p.xch_done[w] = reinterpret_cast<uint32_t*>(b + f.done);
+    }
+  }
 
   // Stream-K split over at most one CTA per SM, or over ranges of about
   // decode_chunk_tokens tokens when the engine was given that hint.
@@ -991,6 +1010,41 @@ TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t 
   if (append && (flags & TE_ATTN_ADVANCE)) {
     for (size_t i = 0; i < n_seqs; ++i) c->len[seq_ids[i]] += 1;
   }
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_attention_decode(te_kv_cache* c, size_t layer_begin, size_t n_layers, const uint32_t* seq_ids,
+                                     size_t n_seqs, const int64_t* q_positions, const float* q, const float* k_new,
+                                     const float* v_new, size_t heads, float* out, uint32_t flags) {
+  return decode_call(c, layer_begin, n_layers, seq_ids, n_seqs, q_positions, q, k_new, v_new, heads, out, flags,
+                     nullptr);
+}
+
+TE_API te_status te_attention_decode_kv_split(te_attn_exchange* x, te_kv_cache* c, size_t layer_begin,
+                                              size_t n_layers, size_t seq, int64_t q_position, const float* q,
+                                              const float* k_new, const float* v_new, size_t heads,
+                                              uint32_t flags) {
+  if (!x || !c || c->eng != x->eng || !q) return TE_STATUS_INVALID_ARGUMENT;
+  te_attn_engine* e = x->eng;
+  if (!x->connected) return fail(e, TE_STATUS_INVALID_ARGUMENT, "exchange not connected");
+  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_NO_ROPE | TE_ATTN_QKV_BIAS)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for te_attention_decode_kv_split");
+  }
+  if (n_layers * heads != (size_t)x->rows || c->d.head_dim != (uint32_t)x->hd) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "the exchange was created for other rows or head_dim");
+  }
+  if (seq > UINT32_MAX) return TE_STATUS_INVALID_ARGUMENT;
+  const uint32_t sid = (uint32_t)seq;
+  const int64_t qp = q_position;
+  float* rec = reinterpret_cast<float*>(x->local);  // placeholder: decode_call writes to the exchange's records
+  return decode_call(c, layer_begin, n_layers, &sid, 1, q_position >= 0 ? &qp : nullptr, q, k_new, v_new, heads,
+                     rec, flags, x);
+}
+
+TE_API te_status te_attn_exchange_output(te_attn_exchange* x, float** out) {
+  if (!x || !out) return TE_STATUS_INVALID_ARGUMENT;
+  const size_t push = exchange_area_bytes(x->world, x->rows, x->hd, x->grid);
+  *out = reinterpret_cast<float*>(reinterpret_cast<char*>(x->local) + fused_layout(push, x->rows, x->hd).out);
   return TE_STATUS_OK;
 }
 
@@ -1098,7 +1152,7 @@ TE_API te_status te_attn_exchange_create(te_attn_engine* e, size_t world, size_t
   x->rows = (int)rows;
   x->hd = (int)head_dim;
   x->grid = exchange_grid((int)rows);
-  const size_t bytes = exchange_area_bytes(x->world, x->rows, x->hd, x->grid);
+  const size_t bytes = fused_layout(exchange_area_bytes(x->world, x->rows, x->hd, x->grid), x->rows, x->hd).end;
   cudaError_t err = cudaMalloc(&x->local, bytes);
   if (err == cudaSuccess) err = cudaMemset(x->local, 0, bytes);
   cudaIpcMemHandle_t h;

@@ -29,6 +29,7 @@ struct SeqEntry {
 };
 
 constexpr int kMaxParamSeqs = 64;  // sequences per decode launch
+constexpr int kMaxExchangeRanks = 8;  // ranks of a KV-split exchange
 
 // Raises a kernel's dynamic shared-memory limit to `bytes` once per device.
 // The attribute applies to the current device only, so every device a
@@ -99,10 +100,26 @@ struct DecodeParams {
   int32_t page_tokens;
   int32_t max_pages_per_seq;
   int32_t rope;               // 1: rotate q (and appended k)
-  int32_t partial_out;        // 1: write partial records
+  int32_t partial_out;        // 1: write partial records {acc, m, l} (stride hd + 2); 2: the same with stride
+                              // hd + 4 (16-byte aligned rows), the fused KV-split exchange's records
   float scale_log2;           // log2(e) / sqrt(hd)
+  // Fused KV-split exchange (xch_world > 1; one sequence): this rank's records
+  // go to xch_rec[xch_rank] (partial_out = 2).  A CTA that finishes a (layer,
+  // kv head) group arrives on the group's counter at its home rank (group %
+  // world); the last of the world arrivals merges the group's records from
+  // every rank and writes the merged rows into every rank's xch_out, then
+  // counts one merged group in every rank's xch_done[.][0].  The CTA whose
+  // consumers finish last on this rank waits (bounded, xch_wait_ns) until all
+  // of this rank's groups are merged before the kernel ends.
+  int32_t xch_world, xch_rank;
+  uint64_t xch_wait_ns;
+  float* xch_rec[kMaxExchangeRanks];      // every rank's records [rows][hd + 4] (this process's mapping)
+  float* xch_out[kMaxExchangeRanks];      // every rank's merged output [rows][hd]
+  uint32_t* xch_cnt[kMaxExchangeRanks];   // every rank's per-group arrival counters
+  uint32_t* xch_done[kMaxExchangeRanks];  // every rank's {merged groups, CTA finish ticket}
   SeqEntry seqs[kMaxParamSeqs];
 };
+static_assert(sizeof(DecodeParams) <= 4096, "decode parameters exceed the kernel parameter space");
 
 // 2-D f16 tensor map over [rows][cols] (box box_rows x 64, 128B swizzle); false on failure.
 bool encode_tmap_f16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
@@ -258,7 +275,6 @@ int prefill_items(int n_layers, int heads, int kv_heads, int n_tokens_padded, bo
 // KV-split exchange over NVLink (k_exchange.cu): one kernel per decode step
 // pushes this rank's partial records into every rank's exchange area and
 // merges the rows once the peers' pushes have arrived.
-constexpr int kMaxExchangeRanks = 8;
 struct ExchangeParams {
   const float* partial;                 // this rank's records [rows][head_dim + 2]
   float* out;                           // merged [rows][head_dim]
@@ -269,6 +285,25 @@ struct ExchangeParams {
   uint64_t wait_ns;                     // bound of the wait for the peers' pushes
 };
 size_t exchange_area_bytes(int world, int rows, int head_dim, int grid);
+// Regions of the fused KV-split exchange (te_attention_decode_kv_split) in
+// the same area, after the push exchange's: byte offsets, 256-byte aligned.
+struct FusedLayout {
+  size_t rec;   // this rank's records [rows][head_dim + 4] fp32 (written by its decode)
+  size_t out;   // merged output [rows][head_dim] fp32 (written by whichever rank merges a group)
+  size_t cnt;   // per-group arrival counters [rows] u32 (groups <= rows)
+  size_t done;  // {merged groups, CTA ticket, completed steps, pad} u32
+  size_t end;
+};
+inline FusedLayout fused_layout(size_t push_bytes, int rows, int head_dim) {
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  FusedLayout f;
+  f.rec = up(push_bytes);
+  f.out = up(f.rec + (size_t)rows * (head_dim + 4) * sizeof(float));
+  f.cnt = up(f.out + (size_t)rows * head_dim * sizeof(float));
+  f.done = up(f.cnt + (size_t)rows * sizeof(uint32_t));
+  f.end = up(f.done + 4 * sizeof(uint32_t));
+  return f;
+}
 int exchange_grid(int rows);
 cudaError_t launch_exchange_merge(const ExchangeParams& p, cudaStream_t s);
 

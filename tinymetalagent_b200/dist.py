@@ -107,7 +107,11 @@ class KVSplitDecoder:
     exchange   "nccl": all-gather the records over the process group, then
                te_attention_merge_partials; "p2p": one kernel pushes them into
                the peers' memory over NVLink and merges what arrived
-               (te_attn_exchange_*; needs one GPU per rank, world <= 8)
+               (te_attn_exchange_*; needs one GPU per rank, world <= 8);
+               "fused": the decode launch itself exchanges and merges
+               (te_attention_decode_kv_split: the rank whose arrival completes
+               a group merges it into every rank's output; one launch per step,
+               no collective; one GPU per rank, world <= 8)
     store      optional torch.distributed Store shared by the ranks: a rank that
                fails writes FAULT_KEY there, and every rank checks it before
                each step's launches (one host round trip per step)
@@ -135,10 +139,13 @@ class KVSplitDecoder:
         # the engine's kernels and the collective run on one stream (the engine's)
         self._stream = torch.cuda.ExternalStream(engine.stream) if engine is not None else None
         self._exchange = None
-        if exchange not in ("nccl", "p2p"):
-            raise ValueError("exchange is 'nccl' or 'p2p'")
-        if exchange == "p2p" and spec.world > 1:
+        if exchange not in ("nccl", "p2p", "fused"):
+            raise ValueError("exchange is 'nccl', 'p2p' or 'fused'")
+        self.fused = exchange == "fused" and spec.world > 1
+        if exchange in ("p2p", "fused") and spec.world > 1:
             self._exchange = self._connect_p2p(engine, group, rows, head_dim)
+        if self.fused:
+            self._out = self._exchange.output((n_layers, 1, heads, head_dim))
 
     def _connect_p2p(self, engine, group, rows: int, head_dim: int):
         import torch
@@ -206,6 +213,15 @@ class KVSplitDecoder:
     def _step(self, q, k_new, v_new):
         import torch.distributed as dist
         q_pos = self.length  # global position of the new token
+        if self.fused:
+            from .runtime import TE_ATTN_ADVANCE
+            if self.spec.is_tail:
+                self._exchange.decode_kv_split(self.cache, 0, self.n_layers, 0, -1, q, k_new, v_new, self.heads,
+                                               TE_ATTN_ADVANCE)
+            else:
+                self._exchange.decode_kv_split(self.cache, 0, self.n_layers, 0, q_pos, q, None, None, self.heads)
+            self.length += 1
+            return self._out
         self._local_partial(q, k_new, v_new, q_pos)
         if self._exchange is not None:
             self._exchange.merge(self._part, self._out)

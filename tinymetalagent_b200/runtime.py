@@ -130,6 +130,8 @@ SIGNATURES: dict[str, tuple] = {
     "te_attn_exchange_connect": (_int, [_vp, _vp]),
     "te_attn_exchange_merge": (_int, [_vp, _vp, _vp]),
     "te_attn_exchange_free": (None, [_vp]),
+    "te_attention_decode_kv_split": (_int, [_vp, _vp, _sz, _sz, _sz, ctypes.c_int64, _vp, _vp, _vp, _sz, ctypes.c_uint32]),
+    "te_attn_exchange_output": (_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
     "te_attention_prefill": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _vp, _sz, _sz, _vp, ctypes.c_uint32]),
     "te_attention_decode_paged_noalloc": (_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _sz, _sz, _sz, _vp, _vp]),
     "te_attention_decode_paged_noalloc_status": (_int, [_vp, ctypes.POINTER(ctypes.c_int)]),
@@ -330,6 +332,24 @@ class Exchange:
 
     def merge(self, partial, out) -> None:
         self.engine.check(self.lib.te_attn_exchange_merge(self.handle, _addr(partial), _addr(out)))
+
+    def decode_kv_split(self, cache: "KVCache", layer_begin: int, n_layers: int, seq: int, q_position: int, q,
+                        k_new, v_new, heads: int, flags: int = 0) -> None:
+        """te_attention_decode_kv_split: this rank's share of one fused KV-split decode step."""
+        self.engine.check(self.lib.te_attention_decode_kv_split(
+            self.handle, cache.handle, layer_begin, n_layers, seq, int(q_position), _addr(q), _addr(k_new),
+            _addr(v_new), heads, flags))
+
+    def output(self, shape):
+        """The merged output region as a float32 CUDA tensor of `shape` (a view, not a copy)."""
+        import torch
+        ptr = ctypes.c_void_p()
+        self.engine.check(self.lib.te_attn_exchange_output(self.handle, ctypes.byref(ptr)))
+
+        class _View:  # __cuda_array_interface__ lets torch wrap the library's memory without a copy
+            __cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr.value, False),
+                                        "version": 2, "strides": None}
+        return torch.as_tensor(_View(), device=f"cuda:{self.engine.device}")
 
     def close(self) -> None:
         if getattr(self, "handle", None):
