@@ -175,7 +175,10 @@ __device__ __forceinline__ void store_result(const DecodeParams& p, size_t orow,
     const float inv = 1.f / L;
     *reinterpret_cast<float4*>(p.out + orow * HD + d) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
   } else if (p.partial_out == 2) {
-    float* r = p.out + orow * (HD + 4);  // the fused exchange's 16-byte aligned records
+    // fused exchange: straight into this rank's slot of the group's home rank
+    // (group = orow / group size for one sequence), 16-byte aligned rows
+    const int gidx = (int)(orow / (size_t)p.group);
+    float* r = p.xch_rec[gidx % p.xch_world] + ((size_t)p.xch_rank * p.xch_rows + orow) * (HD + 4);
     *reinterpret_cast<float4*>(r + d) = O;
     if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
   } else {
@@ -186,89 +189,115 @@ __device__ __forceinline__ void store_result(const DecodeParams& p, size_t orow,
   }
 }
 
-// Fused KV-split exchange: the NT threads that stored group gidx's records
-// (rows orow0 .. orow0 + group - 1 of this rank's record region) call this
-// together; `sync` is a barrier of exactly those threads and `flag` a shared
-// word of theirs.  They arrive on the group's counter at its home rank; the
-// arrival that completes the world (counts are taken modulo world, one
-// arrival per rank and step) merges the group: it reads every rank's records
-// over NVLink (the arrivals' release / acquire order them), combines them by
-// log-sum-exp as te_attention_merge_partials does, writes the merged rows into
-// every rank's output region and counts the group as merged at every rank.
-// Nobody waits here.
-template <int HD, int NT, typename Sync>
-__device__ __noinline__ void xch_group_finished(const DecodeParams& p, int gidx, size_t orow0, int t, Sync sync,
-                                                volatile uint32_t* flag) {
-  constexpr int REC = HD + 4;
-  constexpr int kC = HD / 4;
-  __threadfence_system();  // this thread's record stores are visible to every GPU before the arrival
+// Named barrier of the four consumer warps (barrier 0 is __syncthreads).
+__device__ __forceinline__ void consumer_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Fused KV-split exchange, arrival: the NT threads that stored group gidx's
+// records into its home rank's gather area (sync = a barrier of exactly
+// them) count the group as delivered there.  Thread 0's reduction is a
+// release at system scope, cumulative over the stores the barrier ordered
+// before it; nothing waits.
+template <typename Sync>
+__device__ __forceinline__ void xch_group_finished(const DecodeParams& p, int gidx, int t, Sync sync) {
   sync();
-  if (t == 0) {
-    const uint32_t old = atom_add_acq_rel_sys(p.xch_cnt[gidx % p.xch_world] + gidx, 1u);
-    *flag = (old + 1u) % (uint32_t)p.xch_world == 0u ? 1u : 0u;
-  }
-  sync();
-  const uint32_t last = *flag;
-  sync();  // the flag is read before its next use
-  if (!last) return;
-  for (int i = t; i < p.group * kC; i += NT) {
-    const size_t orow = orow0 + i / kC;
-    const int c = (i % kC) * 4;
-    float m[kMaxExchangeRanks], l[kMaxExchangeRanks];
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kMaxExchangeRanks; ++w) {
-      if (w >= p.xch_world) break;
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.xch_rec[w] + orow * REC + HD));
-      m[w] = ml.x;
-      l[w] = ml.y;
-      if (ml.y > 0.f) M = fmaxf(M, ml.x);
-    }
-    float L = 0.f;
-    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int w = 0; w < kMaxExchangeRanks; ++w) {
-      if (w >= p.xch_world) break;
-      if (!(l[w] > 0.f)) continue;
-      const float sw = ex2(m[w] - M);
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(p.xch_rec[w] + orow * REC + c));
-      L += l[w] * sw;
-      O.x += a.x * sw;
-      O.y += a.y * sw;
-      O.z += a.z * sw;
-      O.w += a.w * sw;
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    O = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
-#pragma unroll
-    for (int w = 0; w < kMaxExchangeRanks; ++w) {
-      if (w >= p.xch_world) break;
-      *reinterpret_cast<float4*>(p.xch_out[w] + orow * HD + c) = O;
-    }
-  }
-  __threadfence_system();  // merged rows visible everywhere before they are counted
-  sync();
-  if (t == 0) {
-    for (int w = 0; w < p.xch_world; ++w) red_add_release_sys(p.xch_done[w], 1u);
-  }
+  if (t == 0) red_add_release_sys(p.xch_cnt[gidx % p.xch_world] + gidx, 1u);
 }
 
-// End of the fused exchange on this rank: the CTA whose consumer warps finish
-// last waits (bounded) until every group of the call has been merged into
-// this rank's output, so that the kernel's completion orders the merged rows
-// before later work on the stream.  done = {merged groups (cumulative), CTA
-// ticket, completed steps}.
-__device__ __noinline__ void xch_finish(const DecodeParams& p) {
+// Fused KV-split exchange, end of the kernel on this rank (the 128 consumer
+// threads of every CTA, after their last segment).  CTA b merges the home
+// groups g = rank + j * world with j = b, b + grid, ...: it waits (bounded)
+// until every rank's record of g has arrived in the local gather area,
+// combines them by log-sum-exp (te_attention_merge_partials' rescale) from
+// local memory, writes the merged rows into every rank's output region and
+// counts the group there.  Then the CTA whose consumers finish last waits
+// (bounded) until this rank's output holds every group, so the kernel's
+// completion orders the merged rows before later work on the stream.
+// Counters are cumulative: done = {merged groups, CTA ticket, steps}.
+template <int HD>
+__device__ __noinline__ void xch_finish(const DecodeParams& p, int t, volatile uint32_t* flag) {
+  constexpr int REC = HD + 4;
+  constexpr int kC = HD / 4;
+  const int world = p.xch_world;
+  const int G = p.group;
+  const uint32_t groups = (uint32_t)(p.n_layers * p.kv_heads * p.n_seqs);
   uint32_t* done = p.xch_done[p.xch_rank];
+  const uint32_t step = *reinterpret_cast<volatile uint32_t*>(done + 2);  // advanced only after every ticket
+  const float* area = p.xch_rec[p.xch_rank];
+  const uint32_t* cnt = p.xch_cnt[p.xch_rank];
+  for (uint32_t j = blockIdx.x;; j += (uint32_t)p.grid) {
+    const uint32_t g = (uint32_t)p.xch_rank + j * (uint32_t)world;
+    if (g >= groups) break;
+    if (t == 0) {
+      const uint32_t target = (step + 1u) * (uint32_t)world;
+      uint32_t ok = 1u;
+      if ((int32_t)(ld_acquire_sys_u32(cnt + g) - target) < 0) {
+        const uint64_t start = globaltimer_ns();
+        while ((int32_t)(ld_acquire_sys_u32(cnt + g) - target) < 0) {
+          if (globaltimer_ns() - start > p.xch_wait_ns) {
+            set_error(p.error, 42);
+            ok = 0u;
+            break;
+          }
+        }
+      }
+      *flag = ok;
+    }
+    consumer_bar_sync();
+    const uint32_t ok = *flag;
+    consumer_bar_sync();
+    if (!ok) continue;
+    const size_t orow0 = (size_t)g * G;
+    for (int i = t; i < G * kC; i += 128) {
+      const size_t orow = orow0 + i / kC;
+      const int c = (i % kC) * 4;
+      float2 ml[kMaxExchangeRanks];
+      float4 a[kMaxExchangeRanks];
+#pragma unroll
+      for (int w = 0; w < kMaxExchangeRanks; ++w) {
+        if (w < world) {
+          const float* r = area + ((size_t)w * p.xch_rows + orow) * REC;
+          ml[w] = __ldcg(reinterpret_cast<const float2*>(r + HD));
+          a[w] = __ldcg(reinterpret_cast<const float4*>(r + c));
+        }
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kMaxExchangeRanks; ++w) {
+        if (w < world && ml[w].y > 0.f) M = fmaxf(M, ml[w].x);
+      }
+      float L = 0.f;
+      float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int w = 0; w < kMaxExchangeRanks; ++w) {
+        if (w >= world || !(ml[w].y > 0.f)) continue;
+        const float sw = ex2(ml[w].x - M);
+        L += ml[w].y * sw;
+        O.x += a[w].x * sw;
+        O.y += a[w].y * sw;
+        O.z += a[w].z * sw;
+        O.w += a[w].w * sw;
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      O = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+#pragma unroll
+      for (int w = 0; w < kMaxExchangeRanks; ++w) {
+        if (w < world) *reinterpret_cast<float4*>(p.xch_out[w] + orow * HD + c) = O;
+      }
+    }
+    consumer_bar_sync();  // the merged rows before thread 0's counts (releases at system scope)
+    if (t == 0) {
+      for (int w = 0; w < world; ++w) red_add_release_sys(p.xch_done[w], 1u);
+    }
+  }
+  consumer_bar_sync();
+  if (t != 0) return;
   __threadfence();
   const uint32_t ticket = atomicAdd(done + 1, 1u);
   if (ticket != (uint32_t)p.grid - 1u) return;
-  const uint32_t groups = (uint32_t)(p.n_layers * p.kv_heads * p.n_seqs);
-  const uint32_t target = (done[2] + 1u) * groups;
+  const uint32_t target = (step + 1u) * groups;
   if ((int32_t)(ld_acquire_sys_u32(done) - target) < 0) {
     const uint64_t start = globaltimer_ns();
     while ((int32_t)(ld_acquire_sys_u32(done) - target) < 0) {
-      __nanosleep(100);
       if (globaltimer_ns() - start > p.xch_wait_ns) {
         set_error(p.error, 41);
         break;
@@ -276,7 +305,7 @@ __device__ __noinline__ void xch_finish(const DecodeParams& p) {
     }
   }
   done[1] = 0u;
-  done[2] += 1u;
+  done[2] = step + 1u;
 }
 
 // CTA owning stage s: the b with start(b) <= s < start(b + 1).
@@ -301,8 +330,6 @@ __device__ __forceinline__ void fold_part(float& M, float& L, float4& O, float m
   M = mn;
 }
 
-// Named barrier of the four consumer warps (barrier 0 is __syncthreads).
-__device__ __forceinline__ void consumer_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 // Scratch offset (floats) of the split-K record CTA bp wrote for group gidx:
 // its segment jp = gidx - (group of bp's first stage).
@@ -775,10 +802,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
           finished = 1;
         }
       }
-      if (p.xch_world > 1 && finished) {
-        xch_group_finished<HD, 32>(p, w.gidx, qrow0, lane, [] { __syncwarp(); },
-                                   reinterpret_cast<volatile uint32_t*>(smem + C::kOffFlag));
-      }
+      if (p.xch_world > 1 && finished) xch_group_finished(p, w.gidx, lane, [] { __syncwarp(); });
       __syncwarp();
       if (lane == 0) mbar_arrive(&mfree[b]);
     }
@@ -1167,7 +1191,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
 #pragma unroll
         for (int f = 0; f < kF; ++f) store_result<HD>(p, qrow0 + row, 4 * (cl + f * kTPR), O2[f], M2, L2);
       }
-      if (p.xch_world > 1) xch_group_finished<HD, 128>(p, w.gidx, qrow0, t, [] { consumer_bar_sync(); }, cflag);
+      if (p.xch_world > 1) xch_group_finished(p, w.gidx, t, [] { consumer_bar_sync(); });
       continue;
     }
     const int b_first = cta_of(p, w.gs0);
@@ -1177,7 +1201,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
 #pragma unroll
         for (int f = 0; f < kF; ++f) store_result<HD>(p, qrow0 + row, 4 * (cl + f * kTPR), O[f], M, L);
       }
-      if (p.xch_world > 1) xch_group_finished<HD, 128>(p, w.gidx, qrow0, t, [] { consumer_bar_sync(); }, cflag);
+      if (p.xch_world > 1) xch_group_finished(p, w.gidx, t, [] { consumer_bar_sync(); });
       continue;
     }
     // Split group: publish this part's record, take a ticket; the last part
@@ -1259,11 +1283,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
 #pragma unroll
       for (int f = 0; f < kF; ++f) store_result<HD>(p, qrow0 + row, 4 * (cl + f * kTPR), O2[f], M2, L2);
     }
-    if (p.xch_world > 1) xch_group_finished<HD, 128>(p, w.gidx, qrow0, t, [] { consumer_bar_sync(); }, cflag);
+    if (p.xch_world > 1) xch_group_finished(p, w.gidx, t, [] { consumer_bar_sync(); });
   }
   if (p.xch_world > 1) {
     consumer_bar_sync();
-    if (tid == 0) xch_finish(p);
+    xch_finish<HD>(p, tid, cflag);
   }
 }
 

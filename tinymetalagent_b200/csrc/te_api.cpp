@@ -941,11 +941,12 @@ static te_status decode_call(te_kv_cache* c, size_t layer_begin, size_t n_layers
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hd));
   if (x) {
     const size_t push = exchange_area_bytes(x->world, x->rows, x->hd, x->grid);
-    const FusedLayout f = fused_layout(push, x->rows, x->hd);
+    const FusedLayout f = fused_layout(push, x->world, x->rows, x->hd);
     p.partial_out = 2;
     p.out = reinterpret_cast<float*>(reinterpret_cast<char*>(x->local) + f.rec);
     p.xch_world = x->world;
     p.xch_rank = x->rank;
+    p.xch_rows = x->rows;
     p.xch_wait_ns = e->wait_ns;
     for (int w = 0; w < x->world; ++w) {
       char* b = reinterpret_cast<char*>(x->base[w]);
@@ -1044,7 +1045,7 @@ TE_API te_status te_attention_decode_kv_split(te_attn_exchange* x, te_kv_cache* 
 TE_API te_status te_attn_exchange_output(te_attn_exchange* x, float** out) {
   if (!x || !out) return TE_STATUS_INVALID_ARGUMENT;
   const size_t push = exchange_area_bytes(x->world, x->rows, x->hd, x->grid);
-  *out = reinterpret_cast<float*>(reinterpret_cast<char*>(x->local) + fused_layout(push, x->rows, x->hd).out);
+  *out = reinterpret_cast<float*>(reinterpret_cast<char*>(x->local) + fused_layout(push, x->world, x->rows, x->hd).out);
   return TE_STATUS_OK;
 }
 
@@ -1152,7 +1153,7 @@ TE_API te_status te_attn_exchange_create(te_attn_engine* e, size_t world, size_t
   x->rows = (int)rows;
   x->hd = (int)head_dim;
   x->grid = exchange_grid((int)rows);
-  const size_t bytes = fused_layout(exchange_area_bytes(x->world, x->rows, x->hd, x->grid), x->rows, x->hd).end;
+  const size_t bytes = fused_layout(exchange_area_bytes(x->world, x->rows, x->hd, x->grid), x->world, x->rows, x->hd).end;
   cudaError_t err = cudaMalloc(&x->local, bytes);
   if (err == cudaSuccess) err = cudaMemset(x->local, 0, bytes);
   cudaIpcMemHandle_t h;

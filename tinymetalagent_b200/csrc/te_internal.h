@@ -103,20 +103,20 @@ struct DecodeParams {
   int32_t partial_out;        // 1: write partial records {acc, m, l} (stride hd + 2); 2: the same with stride
                               // hd + 4 (16-byte aligned rows), the fused KV-split exchange's records
   float scale_log2;           // log2(e) / sqrt(hd)
-  // Fused KV-split exchange (xch_world > 1; one sequence): this rank's records
-  // go to xch_rec[xch_rank] (partial_out = 2).  A CTA that finishes a (layer,
-  // kv head) group arrives on the group's counter at its home rank (group %
-  // world); the last of the world arrivals merges the group's records from
-  // every rank and writes the merged rows into every rank's xch_out, then
-  // counts one merged group in every rank's xch_done[.][0].  The CTA whose
-  // consumers finish last on this rank waits (bounded, xch_wait_ns) until all
-  // of this rank's groups are merged before the kernel ends.
-  int32_t xch_world, xch_rank;
+  // Fused KV-split exchange (xch_world > 1; one sequence; partial_out = 2):
+  // each (layer, kv head) group g has a home rank, g % world.  Every rank
+  // stores its record rows of g into its slot of the home's gather area and
+  // counts them on the home's counter of g; at the end of the kernel the
+  // home's CTAs merge their home groups from local memory, write the merged
+  // rows into every rank's output region and count them there; the CTA whose
+  // consumers finish last on a rank waits (bounded, xch_wait_ns) until that
+  // rank's output holds every group.
+  int32_t xch_world, xch_rank, xch_rows;
   uint64_t xch_wait_ns;
-  float* xch_rec[kMaxExchangeRanks];      // every rank's records [rows][hd + 4] (this process's mapping)
+  float* xch_rec[kMaxExchangeRanks];      // every rank's gather area [world][rows][hd + 4] (this process's mapping)
   float* xch_out[kMaxExchangeRanks];      // every rank's merged output [rows][hd]
-  uint32_t* xch_cnt[kMaxExchangeRanks];   // every rank's per-group arrival counters
-  uint32_t* xch_done[kMaxExchangeRanks];  // every rank's {merged groups, CTA finish ticket}
+  uint32_t* xch_cnt[kMaxExchangeRanks];   // every rank's per-group arrival counts (cumulative)
+  uint32_t* xch_done[kMaxExchangeRanks];  // every rank's {merged groups (cumulative), CTA ticket, steps}
   SeqEntry seqs[kMaxParamSeqs];
 };
 static_assert(sizeof(DecodeParams) <= 4096, "decode parameters exceed the kernel parameter space");
@@ -288,17 +288,17 @@ size_t exchange_area_bytes(int world, int rows, int head_dim, int grid);
 // Regions of the fused KV-split exchange (te_attention_decode_kv_split) in
 // the same area, after the push exchange's: byte offsets, 256-byte aligned.
 struct FusedLayout {
-  size_t rec;   // this rank's records [rows][head_dim + 4] fp32 (written by its decode)
-  size_t out;   // merged output [rows][head_dim] fp32 (written by whichever rank merges a group)
+  size_t rec;   // gather area [world][rows][head_dim + 4] fp32: every rank's records of this rank's home groups
+  size_t out;   // merged output [rows][head_dim] fp32 (written by each group's home rank)
   size_t cnt;   // per-group arrival counters [rows] u32 (groups <= rows)
   size_t done;  // {merged groups, CTA ticket, completed steps, pad} u32
   size_t end;
 };
-inline FusedLayout fused_layout(size_t push_bytes, int rows, int head_dim) {
+inline FusedLayout fused_layout(size_t push_bytes, int world, int rows, int head_dim) {
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
   FusedLayout f;
   f.rec = up(push_bytes);
-  f.out = up(f.rec + (size_t)rows * (head_dim + 4) * sizeof(float));
+  f.out = up(f.rec + (size_t)world * rows * (head_dim + 4) * sizeof(float));
   f.cnt = up(f.out + (size_t)rows * head_dim * sizeof(float));
   f.done = up(f.cnt + (size_t)rows * sizeof(uint32_t));
   f.end = up(f.done + 4 * sizeof(uint32_t));
