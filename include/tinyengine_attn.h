@@ -302,24 +302,24 @@ TE_API void te_attn_exchange_free(te_attn_exchange *exchange);
  * rank decodes its token range of sequence `seq` of `cache` (layers
  * [layer_begin, +n_layers), heads query heads; the exchange's rows must be
  * n_layers * heads and its head_dim the cache's) like te_attention_decode
- * with TE_ATTN_PARTIAL, but each (layer, kv head) group's record goes to
- * this rank's exchange area, and the kernel arrives on the group's counter at
- * a home rank over NVLink.  Whichever rank's arrival completes the world
- * merges that group: it reads every rank's records, combines them by
- * log-sum-exp (te_attention_merge_partials' rescale) and writes the merged
- * rows into every rank's output region (te_attn_exchange_output: [n_layers]
- * [heads][head_dim] fp32 in this rank's HBM), so no rank waits for a group.
- * The kernel ends after this rank's output is complete (one bounded wait,
- * the engine's wait limit; on expiry te_attn_engine_synchronize reports
- * TE_STATUS_RUNTIME_ERROR and the exchange must be recreated).
- * q_position < 0: the query's position is the sequence's last (the rank that
- * owns the tail appends k_new/v_new, one token per layer); otherwise the
- * global position given (ranks without the tail pass NULL k_new/v_new).
- * Every rank calls this once per step, in the same order; the output of a
- * step is valid in stream order after the call and until the next step's call
- * on this rank.  Flags: TE_ATTN_ADVANCE, TE_ATTN_NO_ROPE, TE_ATTN_QKV_BIAS.
- * Asynchronous on the engine's stream; capturable in a CUDA graph.  No
- * reference counterpart (the reference runs on one device). */
+ * with TE_ATTN_PARTIAL, but as each (layer, kv head) group's record is
+ * finished the kernel stores it into every rank's exchange area over NVLink
+ * and counts it there (one system-scope release; nothing waits).  At its end
+ * the kernel merges every group for this rank's own output from its local
+ * area by log-sum-exp (te_attention_merge_partials' rescale), each CTA
+ * waiting (bounded: the engine's wait limit) only for the records of the
+ * groups it merges.  Output: te_attn_exchange_output, [n_layers][heads]
+ * [head_dim] fp32 in this rank's HBM.  On an expired wait
+ * te_attn_engine_synchronize reports TE_STATUS_RUNTIME_ERROR and the
+ * exchange must be recreated.  q_position < 0: the query's position is the
+ * sequence's last (the rank that owns the tail appends k_new/v_new, one token
+ * per layer); otherwise the global position given (ranks without the tail
+ * pass NULL k_new/v_new).  Every rank calls this once per step, in the same
+ * order; a step's output is valid in stream order after the call and until
+ * the next step's call on this rank.  Flags: TE_ATTN_ADVANCE,
+ * TE_ATTN_NO_ROPE, TE_ATTN_QKV_BIAS.  Asynchronous on the engine's stream;
+ * capturable in a CUDA graph.  No reference counterpart (the reference runs
+ * on one device). */
 TE_API te_status te_attention_decode_kv_split(te_attn_exchange *exchange, te_kv_cache *cache,
                                               size_t layer_begin, size_t n_layers, size_t seq,
                                               int64_t q_position, const float *q, const float *k_new,

@@ -175,12 +175,16 @@ __device__ __forceinline__ void store_result(const DecodeParams& p, size_t orow,
     const float inv = 1.f / L;
     *reinterpret_cast<float4*>(p.out + orow * HD + d) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
   } else if (p.partial_out == 2) {
-    // fused exchange: straight into this rank's slot of the group's home rank
-    // (group = orow / group size for one sequence), 16-byte aligned rows
-    const int gidx = (int)(orow / (size_t)p.group);
-    float* r = p.xch_rec[gidx % p.xch_world] + ((size_t)p.xch_rank * p.xch_rows + orow) * (HD + 4);
-    *reinterpret_cast<float4*>(r + d) = O;
-    if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
+    // fused exchange: into this rank's slot of every rank's gather area, the
+    // half of the step's parity (16-byte aligned rows)
+    const uint32_t par = *reinterpret_cast<volatile const uint32_t*>(p.xch_done[p.xch_rank] + 2) & 1u;
+    const size_t off = (((size_t)par * p.xch_world + p.xch_rank) * p.xch_rows + orow) * (HD + 4);
+#pragma unroll 1
+    for (int w = 0; w < p.xch_world; ++w) {
+      float* r = p.xch_rec[w] + off;
+      *reinterpret_cast<float4*>(r + d) = O;
+      if (d == 0) *reinterpret_cast<float2*>(r + HD) = make_float2(M, L);
+    }
   } else {
     float* r = p.out + orow * (HD + 2);
     *reinterpret_cast<float2*>(r + d) = make_float2(O.x, O.y);
@@ -193,26 +197,29 @@ __device__ __forceinline__ void store_result(const DecodeParams& p, size_t orow,
 __device__ __forceinline__ void consumer_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 // Fused KV-split exchange, arrival: the NT threads that stored group gidx's
-// records into its home rank's gather area (sync = a barrier of exactly
-// them) count the group as delivered there.  Thread 0's reduction is a
-// release at system scope, cumulative over the stores the barrier ordered
-// before it; nothing waits.
+// records into every rank's gather area (sync = a barrier of exactly them)
+// count the group there.  One system-scope release fence by thread 0
+// (cumulative over the stores the barrier ordered before it), then relaxed
+// counts; nothing waits.
 template <typename Sync>
 __device__ __forceinline__ void xch_group_finished(const DecodeParams& p, int gidx, int t, Sync sync) {
   sync();
-  if (t == 0) red_add_release_sys(p.xch_cnt[gidx % p.xch_world] + gidx, 1u);
+  if (t == 0) {
+    fence_acq_rel_sys();
+    for (int w = 0; w < p.xch_world; ++w) red_add_relaxed_sys(p.xch_cnt[w] + gidx, 1u);
+  }
 }
 
 // Fused KV-split exchange, end of the kernel on this rank (the 128 consumer
-// threads of every CTA, after their last segment).  CTA b merges the home
-// groups g = rank + j * world with j = b, b + grid, ...: it waits (bounded)
-// until every rank's record of g has arrived in the local gather area,
-// combines them by log-sum-exp (te_attention_merge_partials' rescale) from
-// local memory, writes the merged rows into every rank's output region and
-// counts the group there.  Then the CTA whose consumers finish last waits
-// (bounded) until this rank's output holds every group, so the kernel's
-// completion orders the merged rows before later work on the stream.
-// Counters are cumulative: done = {merged groups, CTA ticket, steps}.
+// threads of every CTA, after their last segment).  CTA b merges groups
+// g = b, b + grid, ... for this rank's own output: it waits (bounded) until
+// every rank's record of g has arrived in the local gather area, combines
+// them by log-sum-exp (te_attention_merge_partials' rescale) from local
+// memory and writes the merged rows.  The kernel's completion then orders the
+// whole output before later work on the stream.  Counts are cumulative; the
+// gather area has two halves (step parity): a rank can be at most one step
+// ahead of another, since its step s + 1 merges need every rank's step s + 1
+// records.  done = {unused, CTA ticket, steps}.
 template <int HD>
 __device__ __noinline__ void xch_finish(const DecodeParams& p, int t, volatile uint32_t* flag) {
   constexpr int REC = HD + 4;
@@ -222,11 +229,10 @@ __device__ __noinline__ void xch_finish(const DecodeParams& p, int t, volatile u
   const uint32_t groups = (uint32_t)(p.n_layers * p.kv_heads * p.n_seqs);
   uint32_t* done = p.xch_done[p.xch_rank];
   const uint32_t step = *reinterpret_cast<volatile uint32_t*>(done + 2);  // advanced only after every ticket
-  const float* area = p.xch_rec[p.xch_rank];
+  const float* area = p.xch_rec[p.xch_rank] + (size_t)(step & 1u) * world * p.xch_rows * REC;
   const uint32_t* cnt = p.xch_cnt[p.xch_rank];
-  for (uint32_t j = blockIdx.x;; j += (uint32_t)p.grid) {
-    const uint32_t g = (uint32_t)p.xch_rank + j * (uint32_t)world;
-    if (g >= groups) break;
+  float* out = p.xch_out[p.xch_rank];
+  for (uint32_t g = blockIdx.x; g < groups; g += (uint32_t)p.grid) {
     if (t == 0) {
       const uint32_t target = (step + 1u) * (uint32_t)world;
       uint32_t ok = 1u;
@@ -278,15 +284,7 @@ __device__ __noinline__ void xch_finish(const DecodeParams& p, int t, volatile u
         O.w += a[w].w * sw;
       }
       const float inv = L > 0.f ? 1.f / L : 0.f;
-      O = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
-#pragma unroll
-      for (int w = 0; w < kMaxExchangeRanks; ++w) {
-        if (w < world) *reinterpret_cast<float4*>(p.xch_out[w] + orow * HD + c) = O;
-      }
-    }
-    consumer_bar_sync();  // the merged rows before thread 0's counts (releases at system scope)
-    if (t == 0) {
-      for (int w = 0; w < world; ++w) red_add_release_sys(p.xch_done[w], 1u);
+      *reinterpret_cast<float4*>(out + orow * HD + c) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
     }
   }
   consumer_bar_sync();
@@ -294,18 +292,8 @@ __device__ __noinline__ void xch_finish(const DecodeParams& p, int t, volatile u
   __threadfence();
   const uint32_t ticket = atomicAdd(done + 1, 1u);
   if (ticket != (uint32_t)p.grid - 1u) return;
-  const uint32_t target = (step + 1u) * groups;
-  if ((int32_t)(ld_acquire_sys_u32(done) - target) < 0) {
-    const uint64_t start = globaltimer_ns();
-    while ((int32_t)(ld_acquire_sys_u32(done) - target) < 0) {
-      if (globaltimer_ns() - start > p.xch_wait_ns) {
-        set_error(p.error, 41);
-        break;
-      }
-    }
-  }
   done[1] = 0u;
-  done[2] = step + 1u;
+  done[2] = step + 1u;  // every CTA has read the step (before its ticket)
 }
 
 // CTA owning stage s: the b with start(b) <= s < start(b + 1).

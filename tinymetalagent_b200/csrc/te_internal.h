@@ -104,19 +104,17 @@ struct DecodeParams {
                               // hd + 4 (16-byte aligned rows), the fused KV-split exchange's records
   float scale_log2;           // log2(e) / sqrt(hd)
   // Fused KV-split exchange (xch_world > 1; one sequence; partial_out = 2):
-  // each (layer, kv head) group g has a home rank, g % world.  Every rank
-  // stores its record rows of g into its slot of the home's gather area and
-  // counts them on the home's counter of g; at the end of the kernel the
-  // home's CTAs merge their home groups from local memory, write the merged
-  // rows into every rank's output region and count them there; the CTA whose
-  // consumers finish last on a rank waits (bounded, xch_wait_ns) until that
-  // rank's output holds every group.
+  // every rank stores its record rows of each finished (layer, kv head) group
+  // into its slot of every rank's gather area and counts the group there; at
+  // the end of the kernel each rank's CTAs merge every group for the rank's
+  // own output from local memory, once all world records have arrived
+  // (bounded waits, xch_wait_ns).
   int32_t xch_world, xch_rank, xch_rows;
   uint64_t xch_wait_ns;
-  float* xch_rec[kMaxExchangeRanks];      // every rank's gather area [world][rows][hd + 4] (this process's mapping)
-  float* xch_out[kMaxExchangeRanks];      // every rank's merged output [rows][hd]
+  float* xch_rec[kMaxExchangeRanks];      // every rank's gather area [2 parities][world][rows][hd + 4] (mapped)
+  float* xch_out[kMaxExchangeRanks];      // every rank's merged output [rows][hd]; this rank's is written
   uint32_t* xch_cnt[kMaxExchangeRanks];   // every rank's per-group arrival counts (cumulative)
-  uint32_t* xch_done[kMaxExchangeRanks];  // every rank's {merged groups (cumulative), CTA ticket, steps}
+  uint32_t* xch_done[kMaxExchangeRanks];  // every rank's {unused, CTA ticket, steps}
   SeqEntry seqs[kMaxParamSeqs];
 };
 static_assert(sizeof(DecodeParams) <= 4096, "decode parameters exceed the kernel parameter space");
@@ -288,8 +286,8 @@ size_t exchange_area_bytes(int world, int rows, int head_dim, int grid);
 // Regions of the fused KV-split exchange (te_attention_decode_kv_split) in
 // the same area, after the push exchange's: byte offsets, 256-byte aligned.
 struct FusedLayout {
-  size_t rec;   // gather area [world][rows][head_dim + 4] fp32: every rank's records of this rank's home groups
-  size_t out;   // merged output [rows][head_dim] fp32 (written by each group's home rank)
+  size_t rec;   // gather area [2 parities][world][rows][head_dim + 4] fp32: every rank's records
+  size_t out;   // merged output [rows][head_dim] fp32 (written by this rank's decode)
   size_t cnt;   // per-group arrival counters [rows] u32 (groups <= rows)
   size_t done;  // {merged groups, CTA ticket, completed steps, pad} u32
   size_t end;
@@ -298,7 +296,7 @@ inline FusedLayout fused_layout(size_t push_bytes, int world, int rows, int head
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
   FusedLayout f;
   f.rec = up(push_bytes);
-  f.out = up(f.rec + (size_t)world * rows * (head_dim + 4) * sizeof(float));
+  f.out = up(f.rec + 2 * (size_t)world * rows * (head_dim + 4) * sizeof(float));
   f.cnt = up(f.out + (size_t)rows * head_dim * sizeof(float));
   f.done = up(f.cnt + (size_t)rows * sizeof(uint32_t));
   f.end = up(f.done + 4 * sizeof(uint32_t));

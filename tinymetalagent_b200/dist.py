@@ -109,9 +109,10 @@ class KVSplitDecoder:
                the peers' memory over NVLink and merges what arrived
                (te_attn_exchange_*; needs one GPU per rank, world <= 8);
                "fused": the decode launch itself exchanges and merges
-               (te_attention_decode_kv_split: the rank whose arrival completes
-               a group merges it into every rank's output; one launch per step,
-               no collective; one GPU per rank, world <= 8)
+               (te_attention_decode_kv_split: each finished group's record is
+               stored into every rank's memory over NVLink and every rank merges
+               its own output at the end of its launch; one launch per step, no
+               collective; one GPU per rank, world <= 8)
     store      optional torch.distributed Store shared by the ranks: a rank that
                fails writes FAULT_KEY there, and every rank checks it before
                each step's launches (one host round trip per step)
