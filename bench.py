@@ -366,11 +366,6 @@ def run_gpu(args) -> None:
             r = int(t.item())
         return r
 
-    # eager timing (host launch loop), reported beside the graph timing
-    cache.truncate(0, CTX0)
-    est = time_region(eager_k)
-    eager_times = [time_region(eager_k) for _ in range(regions_for(est) // 4 + 1)]
-    eager_ms = float(np.median(eager_times))
     graph = None
     if not args.no_graph:
         cache.truncate(0, CTX0)
@@ -403,6 +398,8 @@ def run_gpu(args) -> None:
         t_start = time.perf_counter()
         times = [time_region(run_k) for _ in range(n_regions)]
         clocks.mark(t_start, time.perf_counter())
+        # eager launches (host loop) in the same sustained window, for comparison
+        eager_ms = float(np.median([time_region(eager_k) for _ in range(max(5, n_regions // 4))]))
     launches = args.steps  # one decode launch per step in each timed region
     eng.synchronize()
     ms = float(np.median(times))

@@ -338,11 +338,16 @@ def test_kv_split_partials_and_merge(port):
     eng.close()
 
 
-def test_decode_host_buffers(port):
-    """The same step through host buffers (the e2e path): copies in, compute, copy out, synchronous."""
+@pytest.mark.parametrize("L", [2, 12])
+@pytest.mark.parametrize("pinned", [False, True])
+def test_decode_host_buffers(port, L, pinned):
+    """The same step through host buffers (the e2e path): copies in, compute,
+    output back, synchronous.  A pinned `out` is written by the kernel
+    directly (no copy back), a pageable one through a copy; both must equal
+    the device-pointer call's results bit for bit."""
     from tinymetalagent_b200 import AttnEngine, TE_ATTN_ADVANCE, TE_ATTN_HOST_BUFFERS
     import torch
-    h, hkv, hd, n, L = 16, 2, 128, 700, 2
+    h, hkv, hd, n = 16, 2, 128, 700
     rng = np.random.default_rng(10)
     kraw = rng.standard_normal((L, n, hkv, hd)).astype(np.float32)
     vraw = rng.standard_normal((L, n, hkv, hd)).astype(np.float32)
@@ -353,10 +358,26 @@ def test_decode_host_buffers(port):
     out = np.zeros((L, 1, h, hd), np.float32)
     kn = np.ascontiguousarray(kraw[:, -1:])
     vn = np.ascontiguousarray(vraw[:, -1:])
-    cache.decode(0, L, [0], qraw, out, h, k_new=kn, v_new=vn, flags=TE_ATTN_ADVANCE | TE_ATTN_HOST_BUFFERS)
+    if pinned:
+        ins = [torch.from_numpy(a).pin_memory() for a in (qraw, kn, vn)]
+        out_p = torch.zeros((L, 1, h, hd), dtype=torch.float32).pin_memory()
+        cache.decode(0, L, [0], ins[0], out_p, h, k_new=ins[1], v_new=ins[2],
+                     flags=TE_ATTN_ADVANCE | TE_ATTN_HOST_BUFFERS)
+        out = out_p.numpy()
+    else:
+        cache.decode(0, L, [0], qraw, out, h, k_new=kn, v_new=vn, flags=TE_ATTN_ADVANCE | TE_ATTN_HOST_BUFFERS)
+    assert cache.length(0) == n
     for layer in range(L):
-        exp, _, _ = _oracle_decode(port, kraw[layer], vraw[layer], qraw[layer, 0], 0, hkv, hd, h)
+        exp, kb, vb = _oracle_decode(port, kraw[layer], vraw[layer], qraw[layer, 0], 0, hkv, hd, h)
         close(out[layer, 0], exp)
+        kg, vg = cache.read_f16(layer, 0, 0, n)
+        assert np.array_equal(kg, kb) and np.array_equal(vg, vb)
+    # the device-pointer call on the same state gives the same bits
+    cache.truncate(0, n - 1)
+    dout = torch.zeros((L, 1, h, hd), dtype=torch.float32, device="cuda")
+    cache.decode(0, L, [0], torch_dev(qraw), dout, h, k_new=torch_dev(kn), v_new=torch_dev(vn), flags=TE_ATTN_ADVANCE)
+    eng.synchronize()
+    assert np.array_equal(dout.cpu().numpy(), out)
     cache.close()
     eng.close()
 

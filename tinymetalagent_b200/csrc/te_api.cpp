@@ -45,6 +45,7 @@ struct te_attn_engine {
   bool kernel_timed = false;
   cudaEvent_t ev_k0 = nullptr, ev_k1 = nullptr;
   uint64_t wait_ns = 2000000000ull;  // bound of the exchange kernel's waits for other GPUs
+
   // Per-kernel device-time profile (te_attn_engine_profile, TINYENGINE_PROFILE=1):
   // an event pair around every launch, resolved when the engine synchronises.
   bool profile = false;
@@ -891,7 +892,17 @@ static te_status decode_call(te_kv_cache* c, size_t layer_begin, size_t n_layers
   const float* dk = k_new;
   const float* dv = v_new;
   float* dout = out;
+  // With host buffers, an `out` in pinned host memory that the device can
+  // address (cudaHostAlloc / cudaMallocHost memory, under unified addressing)
+  // is written by the kernel directly: no device-to-host copy afterwards.
+  bool out_mapped = false;
   if (flags & TE_ATTN_HOST_BUFFERS) {
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, out) == cudaSuccess && pa.type == cudaMemoryTypeHost && pa.devicePointer &&
+        (reinterpret_cast<uintptr_t>(pa.devicePointer) & 15u) == 0) {
+      out_mapped = true;
+    }
+    (void)cudaGetLastError();  // an unregistered (pageable) pointer is not an error here
     const size_t need = (q_elems + 2 * kv_elems + out_elems) * sizeof(float);
     cudaError_t err = grow(e, &e->io, &e->io_bytes, need, false);
     if (err != cudaSuccess) return cuda_fail(e, err, "staging allocation");
@@ -907,6 +918,11 @@ static te_status decode_call(te_kv_cache* c, size_t layer_begin, size_t n_layers
     dq = sq;
     dk = append ? sk : nullptr;
     dv = append ? sv : nullptr;
+    if (out_mapped) {
+      cudaPointerAttributes pa{};
+      cudaPointerGetAttributes(&pa, out);
+      dout = static_cast<float*>(pa.devicePointer);
+    }
   }
 
   DecodeParams p;
@@ -1004,7 +1020,9 @@ static te_status decode_call(te_kv_cache* c, size_t layer_begin, size_t n_layers
   }
 
   if (flags & TE_ATTN_HOST_BUFFERS) {
-    cudaError_t err = cudaMemcpyAsync(out, dout, out_elems * sizeof(float), cudaMemcpyDeviceToHost, e->stream);
+    cudaError_t err = out_mapped ? cudaSuccess
+                                 : cudaMemcpyAsync(out, dout, out_elems * sizeof(float), cudaMemcpyDeviceToHost,
+                                                   e->stream);
     if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "output download");
   }
