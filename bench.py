@@ -1009,9 +1009,12 @@ def run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank):
     """one 32768-token sequence, 28 layers, H28/Hkv4/hd128,
     f16 KV N(0,1), RoPE theta 1e6.  The KV sequence is split across ranks
     (contiguous token ranges); per step every rank computes partial (acc, m, l)
-    records over its range (the tail rank also appends the new token), the
-    records are all-gathered over NCCL and merged by log-sum-exp
-    (te_attention_merge_partials).  Strong scaling: one sequence in total."""
+    records over its range (the tail rank also appends the new token) and the
+    records are merged by log-sum-exp: by default inside the same decode launch
+    (--long-exchange fused: each finished group's record is stored into every
+    rank's memory over NVLink, every rank merges its own output), or by an NCCL
+    all-gather plus te_attention_merge_partials (nccl), or by the push kernel
+    (p2p).  Strong scaling: one sequence in total."""
     import torch
     import torch.distributed as dist
 
@@ -1042,8 +1045,9 @@ def run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank):
         kn = torch.randn((L7, 1, KV7, HEAD_DIM), generator=g, device="cuda")
         vn = torch.randn((L7, 1, KV7, HEAD_DIM), generator=g, device="cuda")
     stream.synchronize()
-    exchange = args.long_exchange if world > 1 else "nccl"
-    dec = KVSplitDecoder(spec, L7, H7, HEAD_DIM, cache=cache, engine=eng, device="cuda", exchange=exchange)
+    exchange = args.long_exchange if world > 1 else "local"
+    dec = KVSplitDecoder(spec, L7, H7, HEAD_DIM, cache=cache, engine=eng, device="cuda",
+                         exchange="nccl" if exchange == "local" else exchange)
 
     def step():
         with torch.cuda.stream(stream):  # NCCL and the engine share the engine's stream
@@ -1089,9 +1093,11 @@ def run_long7b(eng, stream, hbm_peak, peak_src, args, world, rank):
             "unit": "tokens/s", "scaling": "strong", "steps": steps, "ms_per_step": round(ms / steps, 4),
             "workload": "long7b: one sequence of 32768 cached tokens, 28 layers, H28/Hkv4/hd128, f16 KV N(0,1), "
                         f"KV split over {world} rank(s), "
-                        + {"p2p": "NVLink push of (acc, m, l) into the peers + LSE merge in one kernel per step; ",
-                           "fused": "exchange fused into the decode launch (the last rank to finish a (layer, kv "
-                                    "head) group merges it over NVLink into every rank's output); ",
+                        + {"local": "one rank: partial records merged by te_attention_merge_partials; ",
+                           "p2p": "NVLink push of (acc, m, l) into the peers + LSE merge in one kernel per step; ",
+                           "fused": "exchange fused into the decode launch (each finished (layer, kv head) group's "
+                                    "record stored into every rank's memory over NVLink; every rank merges its own "
+                                    "output); ",
                            "nccl": "NCCL all-gather of (acc, m, l) + LSE merge per step; "}[exchange]
                         + "steps captured in one CUDA graph",
             "exchange": exchange,
@@ -1128,7 +1134,7 @@ def main() -> None:
                     help="run only the GGUF matrix-vector measurement (Q4_0: launches 1-23, Q8_0: 24-46)")
     ap.add_argument("--cfg-steps", type=int, default=16, help="decode steps timed for config 4")
     ap.add_argument("--long-steps", type=int, default=128, help="decode steps timed for config 5")
-    ap.add_argument("--long-exchange", choices=["nccl", "p2p", "fused"], default="nccl",
+    ap.add_argument("--long-exchange", choices=["nccl", "p2p", "fused"], default="fused",
                     help="config 5 at N>1: NCCL all-gather + merge, the NVLink exchange kernel, or the exchange "
                          "fused into the decode launch")
     args = ap.parse_args()
