@@ -116,3 +116,42 @@ def test_profile_counts_and_times_each_launch():
         cache.close()
     finally:
         eng.close()
+
+
+def test_second_device_after_the_first(port):
+    """The kernels' dynamic shared-memory limits are raised once per device:
+    a decode and a prefill on device 1 after device 0 in the same process both
+    run and match the oracle (a once-per-process flag left device 1 at the
+    default 48 KiB and every launch there failed)."""
+    import torch
+    from tinymetalagent_b200 import TE_ATTN_ADVANCE, AttnEngine
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    h, hkv, hd, n = 16, 2, 128, 300
+    rng = np.random.default_rng(12)
+    k = rng.standard_normal((n, hkv, hd)).astype(np.float32)
+    v = rng.standard_normal((n, hkv, hd)).astype(np.float32)
+    q = rng.standard_normal((n, h, hd)).astype(np.float32)
+    kb, vb = port.append_rope_f16(k, v, 0, hkv, hd, 1e6)
+    kf = port.f16_bits_to_f32(kb).ravel()
+    vf = port.f16_bits_to_f32(vb).ravel()
+    for dev in (0, 1):
+        eng = AttnEngine(dev)
+        try:
+            cache = eng.kv_cache(layers=1, max_seqs=2, max_tokens_per_seq=n, kv_heads=hkv, head_dim=hd)
+            td = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(f"cuda:{dev}")  # noqa: E731
+            out = torch.zeros((1, n, h, hd), device=f"cuda:{dev}")
+            cache.prefill(0, 1, 0, td(q[None]), td(k[None]), td(v[None]), n, h, out, TE_ATTN_ADVANCE)
+            cache.append_rope(0, 1, 1, td(k[:-1]), td(v[:-1]), n - 1, TE_ATTN_ADVANCE)
+            dout = torch.zeros((h, hd), device=f"cuda:{dev}")
+            cache.decode(0, 1, [1], td(q[-1]), dout, h, k_new=td(k[-1:]), v_new=td(v[-1:]), flags=TE_ATTN_ADVANCE)
+            eng.synchronize()
+            qr = q[-1].copy().ravel()
+            port.rope_f32(qr, h, hd, n - 1, 1e6)
+            exp = port.attention_decode_f32(qr, kf, vf, n - 1, h, hkv, hd).reshape(h, hd)
+            for got in (out.cpu().numpy()[0, -1], dout.cpu().numpy()):
+                err = np.abs(got - exp) - (1e-3 + 2e-3 * np.abs(exp))
+                assert err.max() <= 0, (dev, float(np.abs(got - exp).max()))
+            cache.close()
+        finally:
+            eng.close()
