@@ -184,3 +184,45 @@ def test_kv_split_rank_failure_ends_every_rank_with_an_error(use_store):
             assert "injected fault" in msg
         else:
             assert "reported a failure" in msg or "all-gather" in msg, msg
+
+
+def test_kv_split_polls_and_aborts_the_communicator():
+    """With an NCCL group the decoder polls the communicator's asynchronous error
+    before each step and aborts the communicator when a step fails.  A stand-in
+    backend with ProcessGroupNCCL's get_error/abort interface checks the logic on
+    the CPU: an error reported between steps ends the next step before any
+    launch, with TE_STATUS_RUNTIME_ERROR, and the communicator is aborted."""
+    from tinymetalagent_b200.runtime import TE_STATUS_RUNTIME_ERROR, TinyEngineError
+
+    class FakeBackend:
+        def __init__(self):
+            self.error, self.aborted = "ErrorType.SUCCESS", False
+
+        def get_error(self):
+            return self.error
+
+        def abort(self):
+            self.aborted = True
+
+    spec = ShardSpec.plan(0, 2, N)
+    calls = []
+
+    def partial_fn(q, k_new, v_new, q_pos):
+        calls.append(q_pos)
+        rec = torch.zeros((H, HD + 2))
+        rec[:, HD + 1] = 1.0
+        return rec
+
+    dec = KVSplitDecoder(spec, 1, H, HD, partial_fn=partial_fn, merge_fn=lambda g: g[0, :, :HD], device="cpu")
+    be = FakeBackend()
+    dec._nccl_backend = lambda: be  # the stand-in for the group's NCCL backend
+    dec.spec = ShardSpec(0, 1, spec.begin, spec.end, spec.global_len)  # one rank: no real collective
+    q = torch.zeros((1, 1, H, HD))
+    kv = torch.zeros((1, 1, HKV, HD))
+    dec.step(q, kv, kv)
+    assert calls == [N] and not be.aborted
+    be.error = "ErrorType.REMOTE_ERROR"
+    with pytest.raises(TinyEngineError) as err:
+        dec.step(q, kv, kv)
+    assert err.value.status == TE_STATUS_RUNTIME_ERROR and "REMOTE_ERROR" in str(err.value)
+    assert be.aborted and calls == [N]  # no launch was made for the failed step

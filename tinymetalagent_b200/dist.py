@@ -22,6 +22,9 @@ fails records it in an optional host store before raising; the other ranks
 check the store before each step's launches, and a rank already inside the
 exchange ends it through the process group's timeout (NCCL, gloo) or the
 engine's bounded wait (the NVLink exchange, ``AttnEngine.set_wait_limit``).
+With NCCL, each step first polls the communicator's asynchronous error
+(``ProcessGroupNCCL.get_error``, i.e. ncclCommGetAsyncError) and a failure
+aborts the communicator (``abort``, i.e. ncclCommAbort) before raising.
 ``TE_FAULT_INJECT="rank:k"`` (or ``"rank:k:step:s"``) makes rank k fail its
 step s (default 0) on the host, before any launch of that step, to test this.
 """
@@ -182,8 +185,36 @@ class KVSplitDecoder:
             self.cache.decode(0, self.n_layers, [0], q, self._part, self.heads, q_positions=[q_pos],
                               flags=TE_ATTN_PARTIAL)
 
+    def _nccl_backend(self):
+        """The NCCL backend of the exchange's process group, or None (gloo, CPU stand-ins, one rank)."""
+        if self.spec.world <= 1 or self.partial_fn is not None or self._exchange is not None:
+            return None
+        import torch.distributed as dist
+        try:
+            pg = self.group if self.group is not None else dist.distributed_c10d._get_default_group()
+            import torch
+            be = pg._get_backend(torch.device("cuda"))
+        except Exception:
+            return None
+        return be if hasattr(be, "get_error") and hasattr(be, "abort") else None
+
+    def _collective_error(self) -> Optional[str]:
+        """The communicator's asynchronous error (NCCL's ncclCommGetAsyncError, as
+        ProcessGroupNCCL.get_error reports it), or None when there is none."""
+        be = self._nccl_backend()
+        if be is None:
+            return None
+        err = be.get_error()
+        return None if str(err).rsplit(".", 1)[-1] == "SUCCESS" else str(err)
+
     def _fail(self, why: str, cause: Optional[BaseException] = None):
         from .runtime import TE_STATUS_RUNTIME_ERROR, TinyEngineError
+        be = self._nccl_backend()
+        if be is not None:
+            try:  # abort the communicator: no later collective of this group waits on a failed peer
+                be.abort()
+            except Exception:
+                pass
         if self.store is not None:
             try:
                 self.store.set(FAULT_KEY, str(self.spec.rank))
@@ -200,6 +231,9 @@ class KVSplitDecoder:
         (TE_STATUS_RUNTIME_ERROR) when this rank fails or learns that a peer has."""
         if self.store is not None and self.store.check([FAULT_KEY]):
             self._fail(f"rank {self.store.get(FAULT_KEY).decode()} reported a failure; no launch made")
+        async_err = self._collective_error()
+        if async_err is not None:
+            self._fail(f"the communicator reported {async_err}; no launch made")
         if injected_fault(self.spec.rank, self.steps_done):
             self._fail("injected fault (TE_FAULT_INJECT)")
         if self._stream is None:
