@@ -24,7 +24,7 @@ def _data():
     return k, v, q
 
 
-def _worker(rank, world, port_no, out_dir, exchange):
+def _worker(rank, world, port_no, out_dir, exchange, graph=False):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -49,15 +49,32 @@ def _worker(rank, world, port_no, out_dir, exchange):
             v = torch.from_numpy(np.ascontiguousarray(vraw[layer, spec.begin:spec.end])).cuda()
             cache.append_rope(layer, 1, 0, k, v, n_local, TE_ATTN_ADVANCE if layer == L - 1 else 0)
         eng.synchronize()
+        if spec.is_tail:
+            cache.reserve(0, n_local + STEPS + 4)  # no page-table upload inside a graph capture
         dec = KVSplitDecoder(spec, L, H, HD, cache=cache, engine=eng, device="cuda", exchange=exchange)
+        ins = [(torch.from_numpy(np.ascontiguousarray(qraw[s])).cuda(),
+                torch.from_numpy(np.ascontiguousarray(kraw[:, N + s:N + s + 1])).cuda(),
+                torch.from_numpy(np.ascontiguousarray(vraw[:, N + s:N + s + 1])).cuda()) for s in range(STEPS)]
+        eager = 2 if graph else STEPS
         outs = []
-        for s in range(STEPS):
-            q = torch.from_numpy(np.ascontiguousarray(qraw[s])).cuda()
-            kn = torch.from_numpy(np.ascontiguousarray(kraw[:, N + s:N + s + 1])).cuda()
-            vn = torch.from_numpy(np.ascontiguousarray(vraw[:, N + s:N + s + 1])).cuda()
-            o = dec.step(q, kn, vn)
+        for s in range(eager):
+            o = dec.step(*ins[s])
             eng.synchronize()
             outs.append(o.cpu().numpy().copy())
+        if graph:
+            # the remaining steps recorded as one CUDA graph on the engine's stream, then replayed once
+            st = torch.cuda.ExternalStream(eng.stream)
+            res = [torch.empty((L, 1, H, HD), device="cuda") for _ in range(STEPS - eager)]
+            dist.barrier()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                for i in range(STEPS - eager):
+                    res[i].copy_(dec.step(*ins[eager + i]))
+            with torch.cuda.stream(st):
+                g.replay()
+            eng.synchronize()
+            outs += [r.cpu().numpy() for r in res]
+            del g
         np.save(os.path.join(out_dir, f"out{rank}.npy"), np.stack(outs))
         dist.barrier()  # every rank's last step is done before the exchange areas go away
         dec.close()
@@ -78,17 +95,20 @@ def _free_port():
 
 
 @pytest.mark.parametrize("world", [2, 4])
-@pytest.mark.parametrize("exchange", ["nccl", "p2p", "fused"])
+@pytest.mark.parametrize("exchange", ["nccl", "p2p", "fused", "fused_graph"])
 def test_kv_split_two_gpus_matches_oracle(port, tmp_path, exchange, world):
     """world ranks (2, or 4 where the box has them), each on its own GPU;
     exchange: NCCL all-gather + merge kernel, the NVLink push kernel, or the
-    exchange fused into the decode launch (te_attention_decode_kv_split)."""
+    exchange fused into the decode launch (te_attention_decode_kv_split) --
+    also with its last three steps recorded in a CUDA graph and replayed (the
+    step count that picks the gather area's half lives on the device)."""
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), exchange), nprocs=world, join=True,
-                       start_method="spawn")
+    graph = exchange.endswith("_graph")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), exchange.replace("_graph", ""), graph),
+                       nprocs=world, join=True, start_method="spawn")
     kraw, vraw, qraw = _data()
     outs = [np.load(tmp_path / f"out{r}.npy") for r in range(world)]
     for r in range(1, world):

@@ -75,7 +75,7 @@ struct DecodeCfg {
   static constexpr int kOffRes = kOffNew + 2 * kNewBytes;
   static constexpr int kOffBar = kOffRes + 2 * kResBytes;
   static constexpr int kNumBars = 2 * kRing + 15;  // full, empty, [2] each: qfull qempty fready fempty mready mfree nready; cbar
-  static constexpr int kOffFlag = kOffBar + kNumBars * 8;  // two flag words of the fused KV-split exchange
+  static constexpr int kOffFlag = kOffBar + kNumBars * 8;  // a flag word of the fused KV-split exchange
   static constexpr int kSmemBytes = kOffFlag + 16 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
 };
@@ -177,7 +177,7 @@ __device__ __forceinline__ void store_result(const DecodeParams& p, size_t orow,
   } else if (p.partial_out == 2) {
     // fused exchange: into this rank's slot of every rank's gather area, the
     // half of the step's parity (16-byte aligned rows)
-    const uint32_t par = *reinterpret_cast<volatile const uint32_t*>(p.xch_done[p.xch_rank] + 2) & 1u;
+    const uint32_t par = *reinterpret_cast<volatile const uint32_t*>(p.xch_done + 2) & 1u;
     const size_t off = (((size_t)par * p.xch_world + p.xch_rank) * p.xch_rows + orow) * (HD + 4);
 #pragma unroll 1
     for (int w = 0; w < p.xch_world; ++w) {
@@ -227,11 +227,11 @@ __device__ __noinline__ void xch_finish(const DecodeParams& p, int t, volatile u
   const int world = p.xch_world;
   const int G = p.group;
   const uint32_t groups = (uint32_t)(p.n_layers * p.kv_heads * p.n_seqs);
-  uint32_t* done = p.xch_done[p.xch_rank];
+  uint32_t* done = p.xch_done;
   const uint32_t step = *reinterpret_cast<volatile uint32_t*>(done + 2);  // advanced only after every ticket
   const float* area = p.xch_rec[p.xch_rank] + (size_t)(step & 1u) * world * p.xch_rows * REC;
   const uint32_t* cnt = p.xch_cnt[p.xch_rank];
-  float* out = p.xch_out[p.xch_rank];
+  float* out = p.xch_out;
   for (uint32_t g = blockIdx.x; g < groups; g += (uint32_t)p.grid) {
     if (t == 0) {
       const uint32_t target = (step + 1u) * (uint32_t)world;
@@ -886,7 +886,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_f16_kernel(const __grid_co
   }
 
   // ---- consumer warps 0-3 ------------------------------------------------
-  volatile uint32_t* cflag = reinterpret_cast<volatile uint32_t*>(smem + C::kOffFlag + 4);
+  volatile uint32_t* cflag = reinterpret_cast<volatile uint32_t*>(smem + C::kOffFlag);
   const int g = lane >> 2;  // mma group id: head rows g and g+8, token rows
   const int c = lane & 3;   // thread in group
   const float sl = p.scale_log2;

@@ -967,10 +967,10 @@ static te_status decode_call(te_kv_cache* c, size_t layer_begin, size_t n_layers
     for (int w = 0; w < x->world; ++w) {
       char* b = reinterpret_cast<char*>(x->base[w]);
       p.xch_rec[w] = reinterpret_cast<float*>(b + f.rec);
-      p.xch_out[w] = reinterpret_cast<float*>(b + f.out);
       p.xch_cnt[w] = reinterpret_cast<uint32_t*>(b + f.cnt);
-      p.xch_done[w] = reinterpret_cast<uint32_t*>(b + f.done);
     }
+    p.xch_out = reinterpret_cast<float*>(reinterpret_cast<char*>(x->local) + f.out);
+    p.xch_done = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(x->local) + f.done);
   }
 
   // Stream-K split over at most one CTA per SM, or over ranges of about

@@ -112,9 +112,9 @@ struct DecodeParams {
   int32_t xch_world, xch_rank, xch_rows;
   uint64_t xch_wait_ns;
   float* xch_rec[kMaxExchangeRanks];      // every rank's gather area [2 parities][world][rows][hd + 4] (mapped)
-  float* xch_out[kMaxExchangeRanks];      // every rank's merged output [rows][hd]; this rank's is written
+  float* xch_out;                         // this rank's merged output [rows][hd]
   uint32_t* xch_cnt[kMaxExchangeRanks];   // every rank's per-group arrival counts (cumulative)
-  uint32_t* xch_done[kMaxExchangeRanks];  // every rank's {unused, CTA ticket, steps}
+  uint32_t* xch_done;                     // this rank's {unused, CTA ticket, steps}
   SeqEntry seqs[kMaxParamSeqs];
 };
 static_assert(sizeof(DecodeParams) <= 4096, "decode parameters exceed the kernel parameter space");
