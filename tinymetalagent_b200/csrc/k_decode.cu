@@ -1421,6 +1421,31 @@ cudaError_t launch_decode_f32_generic(const float* q, const float* k, const floa
   return cudaGetLastError();
 }
 
+// Copies up to three buffers of host-visible (pinned, device-mapped) memory
+// into device staging with plain 16-byte loads over PCIe: one launch in place
+// of one copy operation per buffer.  The next kernel on the stream (a
+// programmatic dependent) may be scheduled as soon as every CTA has started.
+__global__ void __launch_bounds__(256) gather_host_kernel(const __grid_constant__ GatherParams p) {
+  griddep_launch_dependents();
+  size_t total = 0;
+  for (int i = 0; i < p.n; ++i) total += p.chunks[i];
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    size_t k = e;
+    int i = 0;
+    while (k >= p.chunks[i]) k -= p.chunks[i++];
+    reinterpret_cast<uint4*>(p.dst[i])[k] = reinterpret_cast<const uint4*>(p.src[i])[k];
+  }
+}
+
+cudaError_t launch_gather_host(const GatherParams& p, cudaStream_t s) {
+  size_t total = 0;
+  for (int i = 0; i < p.n; ++i) total += p.chunks[i];
+  const int grid = (int)std::min<size_t>((total + 255) / 256, 148);
+  if (grid == 0) return cudaSuccess;
+  gather_host_kernel<<<grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_merge_partials(const float* partials, int n_parts, int rows, int head_dim, float* out,
                                   int partial_out, cudaStream_t s) {
   merge_partials_kernel<<<rows, 128, 0, s>>>(partials, n_parts, rows, head_dim, out, partial_out);

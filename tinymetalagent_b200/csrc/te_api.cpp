@@ -911,9 +911,34 @@ static te_status decode_call(te_kv_cache* c, size_t layer_begin, size_t n_layers
     float* sk = sq + q_elems;
     float* sv = sk + kv_elems;
     dout = sv + kv_elems;
-    err = cudaMemcpyAsync(sq, q, q_elems * sizeof(float), cudaMemcpyHostToDevice, e->stream);
-    if (err == cudaSuccess && append) err = cudaMemcpyAsync(sk, k_new, kv_elems * sizeof(float), cudaMemcpyHostToDevice, e->stream);
-    if (err == cudaSuccess && append) err = cudaMemcpyAsync(sv, v_new, kv_elems * sizeof(float), cudaMemcpyHostToDevice, e->stream);
+    // Inputs in pinned host memory the device can address, 16-byte aligned and
+    // sized: one gather kernel reads them over PCIe (instead of one copy
+    // operation per buffer); otherwise ordinary copies.
+    GatherParams gp{};
+    const void* srcs[3] = {q, k_new, v_new};
+    float* dsts[3] = {sq, sk, sv};
+    const size_t bytes[3] = {q_elems * sizeof(float), kv_elems * sizeof(float), kv_elems * sizeof(float)};
+    bool mapped = true;
+    for (int i = 0; i < (append ? 3 : 1) && mapped; ++i) {
+      cudaPointerAttributes pa{};
+      mapped = cudaPointerGetAttributes(&pa, srcs[i]) == cudaSuccess && pa.type == cudaMemoryTypeHost &&
+               pa.devicePointer && ((reinterpret_cast<uintptr_t>(pa.devicePointer) | bytes[i]) & 15u) == 0;
+      if (mapped) {
+        gp.src[gp.n] = pa.devicePointer;
+        gp.dst[gp.n] = dsts[i];
+        gp.chunks[gp.n] = bytes[i] / 16;
+        ++gp.n;
+      }
+    }
+    (void)cudaGetLastError();  // an unregistered (pageable) pointer is not an error here
+    if (mapped) {
+      err = launch_gather_host(gp, e->stream);
+      if (err == cudaSuccess) e->launches++;
+    } else {
+      err = cudaMemcpyAsync(sq, q, q_elems * sizeof(float), cudaMemcpyHostToDevice, e->stream);
+      if (err == cudaSuccess && append) err = cudaMemcpyAsync(sk, k_new, kv_elems * sizeof(float), cudaMemcpyHostToDevice, e->stream);
+      if (err == cudaSuccess && append) err = cudaMemcpyAsync(sv, v_new, kv_elems * sizeof(float), cudaMemcpyHostToDevice, e->stream);
+    }
     if (err != cudaSuccess) return cuda_fail(e, err, "input upload");
     dq = sq;
     dk = append ? sk : nullptr;

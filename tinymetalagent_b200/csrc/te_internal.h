@@ -191,6 +191,15 @@ cudaError_t launch_rope_rows(float* values, const float* cos_row, const float* s
                              cudaStream_t s);
 cudaError_t launch_merge_partials(const float* partials, int n_parts, int rows, int head_dim, float* out,
                                   int partial_out, cudaStream_t s);
+// Host-visible (pinned, device-mapped) buffers copied to device memory by one
+// kernel: chunks[i] 16-byte units from src[i] to dst[i], both 16-byte aligned.
+struct GatherParams {
+  const void* src[3];
+  void* dst[3];
+  size_t chunks[3];
+  int32_t n;
+};
+cudaError_t launch_gather_host(const GatherParams& p, cudaStream_t s);
 
 struct AppendParams {
   const void* k;            // [n_layers][n_tokens][kv_heads][hd], fp32 or f16
