@@ -138,14 +138,14 @@ def test_config5_long_context_whole_and_four_way_split(port):
         eng.close()
 
 
-def test_config3_prefill_two_full_layers(port):
+def test_config3_prefill_three_full_layers(port):
     """Config 3: the 2048-token causal prefill (H16/Hkv2/hd128, f16 Q/K/V
-    N(0,1), RoPE theta 1e6 at positions 0..2047) on two whole layers in one
-    call; every 16th row and the last 16 rows of both layers against the
-    oracle's per-token loop, and both layers' caches bit-exact."""
+    N(0,1), RoPE theta 1e6 at positions 0..2047) on three whole layers in one
+    call; every 16th row and the last 16 rows of every layer against the
+    oracle's per-token loop, and every layer's cache bit-exact."""
     import torch
     from tinymetalagent_b200 import TE_ATTN_ADVANCE, TE_ATTN_INPUT_F16, AttnEngine
-    h, hkv, hd, s, L = 16, 2, 128, 2048, 2
+    h, hkv, hd, s, L = 16, 2, 128, 2048, 3
     rng = np.random.default_rng(33)
     q16 = rng.standard_normal((L, s, h, hd), dtype=np.float32).astype(np.float16)
     k16 = rng.standard_normal((L, s, hkv, hd), dtype=np.float32).astype(np.float16)

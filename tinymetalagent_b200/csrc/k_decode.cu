@@ -34,6 +34,7 @@
 
 #include "te_internal.h"
 #include "te_ptx.cuh"
+#include "te_rope.cuh"
 
 namespace te {
 namespace {
@@ -84,28 +85,6 @@ struct DecodeCfg {
 // record starts on a 16-byte boundary.
 template <int HD>
 constexpr int kScratchRec = HD + 4;
-
-// v[i] += b[i] for 8 consecutive fp32 bias values (c/src/ops.c:408-416: one
-// fp32 addition per element, rounded to nearest).
-__device__ __forceinline__ void add_bias8(float (&v)[8], const float* b) {
-  const float4 b0 = *reinterpret_cast<const float4*>(b);
-  const float4 b1 = *reinterpret_cast<const float4*>(b + 4);
-  v[0] = __fadd_rn(v[0], b0.x); v[1] = __fadd_rn(v[1], b0.y); v[2] = __fadd_rn(v[2], b0.z); v[3] = __fadd_rn(v[3], b0.w);
-  v[4] = __fadd_rn(v[4], b1.x); v[5] = __fadd_rn(v[5], b1.y); v[6] = __fadd_rn(v[6], b1.z); v[7] = __fadd_rn(v[7], b1.w);
-}
-
-// Low part of x in a two-term f16 split: x = hi + lo with hi = f16(x) and lo
-// = x - hi (exact in fp32), itself rounded to f16 for the tensor core.  The
-// query enters the f16 MMA as hi and lo, so q.k keeps about 22 bits of the
-// fp32 query instead of 11.
-__device__ __forceinline__ float f16_residual(float x) { return x - __half2float(__float2half_rn(x)); }
-
-__device__ __forceinline__ float rope_lo(float a, float b, float c, float s) {
-  return __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-}
-__device__ __forceinline__ float rope_hi(float a, float b, float c, float s) {
-  return __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
-}
 
 // Physical head-dim offset (in 16-byte chunks within a 64-column box) that a
 // thread with quad index c reads for k-step pair j, and the box it lies in.

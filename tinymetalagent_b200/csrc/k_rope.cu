@@ -1,13 +1,7 @@
 // RoPE kernels: the drop-in te_rope_f32, the fused RoPE(k) + f16 append into
-// the paged cache, and the prefill query preparation.
-//
-// All rotations use the reference's exact fp32 expression shapes
-//   lo = a*cos - b*sin,  hi = b*cos + a*sin     (c/src/ops.c:313-318,
-//                                               c/src/qwen.c:2152-2157)
-// with separately rounded products (no FMA contraction), on the host-built
-// cos/sin table (c/src/qwen.c:531-539), so results are bit-identical to the
-// CPU reference; the f16 store is round-to-nearest-even like Metal's half()
-// (c/src/metal/metal_kernels.metal.inc:2422-2427).
+// the paged cache, and the prefill query preparation.  Rotation, bias and f16
+// conversion arithmetic (bit-identical to the CPU reference) is in
+// te_rope.cuh.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -15,16 +9,10 @@
 
 #include "te_internal.h"
 #include "te_ptx.cuh"
+#include "te_rope.cuh"
 
 namespace te {
 namespace {
-
-__device__ __forceinline__ float rope_lo(float a, float b, float c, float s) {
-  return __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-}
-__device__ __forceinline__ float rope_hi(float a, float b, float c, float s) {
-  return __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
-}
 
 __global__ void rope_rows_kernel(float* values, const float* cos_row, const float* sin_row, int heads,
                                  int head_dim) {
@@ -37,58 +25,6 @@ __global__ void rope_rows_kernel(float* values, const float* cos_row, const floa
   const float c = cos_row[d], s = sin_row[d];
   row[d] = rope_lo(a, b, c, s);
   row[d + half] = rope_hi(a, b, c, s);
-}
-
-// 8 consecutive values of an fp32 or f16 row as fp32.
-__device__ __forceinline__ void load8(const void* base, size_t idx, int f16, float (&v)[8]) {
-  if (f16) {
-    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(base) + idx);
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __half22float2(h[i]);
-      v[2 * i] = f.x;
-      v[2 * i + 1] = f.y;
-    }
-  } else {
-    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
-    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx + 4);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  }
-}
-
-// v[i] += b[i] for 8 consecutive fp32 bias values (the reference's te_add_f32,
-// c/src/ops.c:408-416: one fp32 addition per element, rounded to nearest).
-__device__ __forceinline__ void add_bias8(float (&v)[8], const float* b) {
-  const float4 b0 = *reinterpret_cast<const float4*>(b);
-  const float4 b1 = *reinterpret_cast<const float4*>(b + 4);
-  v[0] = __fadd_rn(v[0], b0.x); v[1] = __fadd_rn(v[1], b0.y); v[2] = __fadd_rn(v[2], b0.z); v[3] = __fadd_rn(v[3], b0.w);
-  v[4] = __fadd_rn(v[4], b1.x); v[5] = __fadd_rn(v[5], b1.y); v[6] = __fadd_rn(v[6], b1.z); v[7] = __fadd_rn(v[7], b1.w);
-}
-
-__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
-  uint4 u;
-  __half2* h = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-  return u;
-}
-
-// Rotates 8 pairs (d..d+7, d+half..d+half+7) in place with the reference expressions.
-__device__ __forceinline__ void rope8(float (&lo)[8], float (&hi)[8], const float* cos_row, const float* sin_row, int d) {
-  const float4 c0 = *reinterpret_cast<const float4*>(cos_row + d);
-  const float4 c1 = *reinterpret_cast<const float4*>(cos_row + d + 4);
-  const float4 s0 = *reinterpret_cast<const float4*>(sin_row + d);
-  const float4 s1 = *reinterpret_cast<const float4*>(sin_row + d + 4);
-  const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-  const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float a = lo[i], b = hi[i];
-    lo[i] = rope_lo(a, b, c[i], s[i]);
-    hi[i] = rope_hi(a, b, c[i], s[i]);
-  }
 }
 
 // One thread per (token, kv head, group of 8 rotation pairs); grid.y = layer.
@@ -134,33 +70,6 @@ __global__ void append_rope_kernel(const AppendParams p) {
 }
 
 // Low parts of a two-term f16 split: lo = f16(x - f16(x)), x - f16(x) exact in fp32.
-__device__ __forceinline__ void f16_residual8(const float (&x)[8], float (&r)[8]) {
-#pragma unroll
-  for (int e = 0; e < 8; ++e) r[e] = x[e] - __half2float(__float2half_rn(x[e]));
-}
-
-// Stores dims [d, d+8) and [d+half, d+half+8) of the query row whose unsplit
-// offset is `row` (elements, [..][heads][hd] layout): as f16 there, or with
-// p.split as the hi row 2r and the lo row 2r + 1 of [..][heads][2][hd].
-template <int HD>
-__device__ __forceinline__ void store_q8(const QPrepParams& p, size_t row, int d, const float (&lo)[8],
-                                         const float (&hi)[8]) {
-  constexpr int half = HD / 2;
-  if (!p.split) {
-    *reinterpret_cast<uint4*>(p.qh + row + d) = pack8(lo);
-    *reinterpret_cast<uint4*>(p.qh + row + d + half) = pack8(hi);
-    return;
-  }
-  float rl[8], rh[8];
-  f16_residual8(lo, rl);
-  f16_residual8(hi, rh);
-  __half* hrow = p.qh + 2 * row;
-  *reinterpret_cast<uint4*>(hrow + d) = pack8(lo);
-  *reinterpret_cast<uint4*>(hrow + d + half) = pack8(hi);
-  *reinterpret_cast<uint4*>(hrow + HD + d) = pack8(rl);
-  *reinterpret_cast<uint4*>(hrow + HD + d + half) = pack8(rh);
-}
-
 // Query rows of one token and head: f16 in the same layout, rotated unless
 // RoPE is off.
 template <int HD>
