@@ -748,16 +748,59 @@ def run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank):
 QWEN_SHAPE = dict(layers=24, hidden=896, heads=14, kv_heads=2, ffn=4864, vocab=151936, context=1024)
 
 
+def _qwen_decode_times(eng, stream, dec, toks, steps):
+    """Eager steps (forward_token + project_next, argmax read back each step) and the same window recorded
+    as one CUDA graph (capture_greedy) and replayed: (eager ms, graph ms as the median of 5 replays,
+    library launches per eager step)."""
+    import torch
+    prompt = len(toks)
+    for pos, t in enumerate(toks):
+        dec.forward_token(t, pos)
+    nxt = dec.project_next()
+    for _ in range(3):  # warm-up steps, then restart from the same position
+        dec.forward_token(nxt, prompt)
+        dec.project_next()
+    launches0 = eng.launch_count
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    t0 = time.perf_counter()
+    pos = prompt
+    first = nxt
+    for _ in range(steps):
+        dec.forward_token(nxt, pos)
+        nxt = dec.project_next()
+        pos += 1
+    e1.record(stream)
+    e1.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1e3
+    ms = max(e0.elapsed_time(e1), wall_ms)
+    launches = eng.launch_count - launches0
+    dec.cache.truncate(0, prompt)
+    dec.capture_greedy(prompt, steps)
+    dec.replay_greedy(first)  # warm
+    torch.cuda.synchronize()
+    reps = []
+    for _ in range(5):
+        e0.record(stream)
+        dec.replay_greedy(first)
+        e1.record(stream)
+        e1.synchronize()
+        reps.append(e0.elapsed_time(e1))
+    return ms, float(np.median(reps)), launches / steps
+
+
 def run_qwen(eng, stream, hbm_peak, peak_src, args):
     """QwenDecoder (the te_qwen_forward_token-compatible decode step) on a synthetic model of
     Qwen2.5-0.5B's shape -- 24 layers, hidden 896, 14 heads of 64 over 2 KV heads, FFN 4864, vocabulary
     151 936; Q4_0 projections, Q8_0 embedding and lm_head -- written as a GGUF file at run time (no
-    model file is available offline).  A step is forward_token + project_next (greedy, its argmax read
-    back to the host) after a 16-token prompt; tokens/s over args.qwen_steps steps, device time on the
-    engine's stream.  Beside it, the reference's own CPU forward pass on the same file."""
+    model file is available offline).  A step is one greedy token after a 16-token prompt: the value is
+    the whole-token step kernel (one launch per token: every layer, the head and the argmax) recorded
+    as one CUDA graph and replayed; beside it the same window on the per-op path (five launches per
+    layer), and eager steps of both.  Device time on the engine's stream.  Beside them, the
+    reference's own CPU forward pass on the same file."""
     import tempfile
     import shutil
-    import torch
     sys.path.insert(0, str(ROOT / "tests" / "golden"))
     from gguf_synth import GGML_Q4_0, write_qwen2
     from tinymetalagent_b200.qwen import QwenDecoder
@@ -768,61 +811,41 @@ def run_qwen(eng, stream, hbm_peak, peak_src, args):
         write_qwen2(path, quant_attn=GGML_Q4_0, quant_ffn=GGML_Q4_0, seed=3, **QWEN_SHAPE)
         prompt, steps = 16, args.qwen_steps
         ctx = prompt + steps + 8
-        dec = QwenDecoder(eng, path, ctx)
-        weight_bytes = sum(int(v.numel()) for lay in dec.layers for k, v in lay.items()
-                           if k in ("qkv", "o", "gu", "down")) + int(dec._head.numel())
         rng = np.random.default_rng(9)
         toks = [int(t) for t in rng.integers(0, QWEN_SHAPE["vocab"], prompt)]
-        for pos, t in enumerate(toks):
-            dec.forward_token(t, pos)
-        nxt = dec.project_next()
-        for _ in range(3):  # warm-up steps, then restart from the same position
-            dec.forward_token(nxt, prompt)
-            dec.project_next()
-        launches0 = eng.launch_count
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        e0.record(stream)
-        t0 = time.perf_counter()
-        pos = prompt
-        for _ in range(steps):
-            dec.forward_token(nxt, pos)
-            nxt = dec.project_next()
-            pos += 1
-        e1.record(stream)
-        e1.synchronize()
-        wall_ms = (time.perf_counter() - t0) * 1e3
-        ms = max(e0.elapsed_time(e1), wall_ms)
-        launches = eng.launch_count - launches0
-        # the same window recorded as one CUDA graph (capture_greedy) and replayed
-        dec.cache.truncate(0, prompt)
-        first = nxt
-        dec.capture_greedy(prompt, steps)
-        dec.replay_greedy(first)  # warm
-        torch.cuda.synchronize()
-        e0.record(stream)
-        dec.replay_greedy(first)
-        e1.record(stream)
-        e1.synchronize()
-        graph_ms = e0.elapsed_time(e1)
-        dec.close()
-        tps = steps / (ms / 1e3)
-        graph_tps = steps / (graph_ms / 1e3)
-        gbs = weight_bytes * tps / 1e9
+        out = {}
+        for fused in (True, False):
+            dec = QwenDecoder(eng, path, ctx, fused_step=fused)
+            weight_bytes = sum(int(v.numel()) for lay in dec.layers for k, v in lay.items()
+                               if k in ("qkv", "o", "gu", "down")) + int(dec._head.numel())
+            out[fused] = _qwen_decode_times(eng, stream, dec, toks, steps)
+            dec.close()
+        ms, graph_ms, lpt = out[True]
+        ms2, graph_ms2, lpt2 = out[False]
+        tps, graph_tps = steps / (ms / 1e3), steps / (graph_ms / 1e3)
         graph_gbs = weight_bytes * graph_tps / 1e9
-        res = {"metric": "qwen2 decode step (QwenDecoder: greedy steps recorded as one CUDA graph, replayed)",
+        res = {"metric": "qwen2 decode step (QwenDecoder, whole-token step kernel: greedy steps recorded as one "
+                         "CUDA graph, replayed)",
                "value": round(graph_tps, 1), "unit": "tokens/s", "ms_per_token": round(graph_ms / steps, 4),
-               "steps": steps,
+               "steps": steps, "context_tokens": f"{prompt + 1}..{prompt + steps}",
                "eager": {"value": round(tps, 1), "unit": "tokens/s", "ms_per_token": round(ms / steps, 4),
-                         "note": "forward_token + project_next from Python, argmax read back every step"},
+                         "library_launches_per_token": round(lpt, 1),
+                         "note": "forward_token (one step launch) + project_next (per-op head, torch argmax) "
+                                 "from Python, argmax read back every step"},
+               "per_op": {"value": round(steps / (graph_ms2 / 1e3), 1), "unit": "tokens/s",
+                          "ms_per_token": round(graph_ms2 / steps, 4),
+                          "library_launches_per_token": round(lpt2, 1),
+                          "eager_value": round(steps / (ms2 / 1e3), 1),
+                          "note": "te_matvec_gguf_fused + te_attention_decode + te_matvec_gguf, five launches "
+                                  "per layer, recorded as one CUDA graph"},
                "model": "synthetic Qwen2.5-0.5B shape: 24 layers, H14/Hkv2/hd64, hidden 896, FFN 4864, "
                         "vocab 151936, Q4_0 projections, Q8_0 embedding/lm_head",
                "weight_bytes_per_token": weight_bytes,
                "roofline": {"bound": "hbm", "achieved": round(graph_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                             "frac": round(graph_gbs / hbm_peak, 4), "peak_source": f"{peak_src} (burst copy)",
-                            "eager_achieved": round(gbs, 1),
+                            "per_op_achieved": round(weight_bytes * steps / (graph_ms2 / 1e3) / 1e9, 1),
                             "note": "weight bytes read once per token over the graph-replay time"},
-               "library_launches_per_token": round(launches / steps, 1)}
+               "library_launches_per_token": 1.0}
         if not args.no_cpu:
             from oracle import oracle as O
             if O.ref_qwen_available():
@@ -867,7 +890,7 @@ def run_qwen_prefill(eng, stream, args):
         path = tmp / "qwen2_1p5b_shape.gguf"
         write_qwen2(path, quant_attn=GGML_Q4_0, quant_ffn=GGML_Q4_0, seed=4, **QWEN_PREFILL_SHAPE)
         T = 512
-        dec = QwenDecoder(eng, path, T + 8)
+        dec = QwenDecoder(eng, path, T + 8, fused_step=False)
         prompt = [int(t) for t in np.random.default_rng(10).integers(0, QWEN_PREFILL_SHAPE["vocab"], T)]
         dec.prefill_prompt(prompt)  # warm
         dec.project_next()

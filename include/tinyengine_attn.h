@@ -125,7 +125,7 @@ TE_API te_status te_attn_engine_set_wait_limit(te_attn_engine *engine, uint32_t 
  * but "0"), the reference's switch (c/src/qwen.c:47-73, 2216-2304); then the
  * engine prints its totals to stderr when freed.  The report is one line,
  * "tinyengine_profile: device_ms=T decode=ms/calls append=... merge=...
- * prefill_prep=... prefill_attn=... matvec=... exchange=...", the reference's
+ * prefill_prep=... prefill_attn=... matvec=... exchange=... step=...", the reference's
  * "name=ms/calls" format.  te_attn_engine_profile_report synchronises the
  * engine's stream and writes that line to buf (TE_STATUS_INVALID_ARGUMENT if
  * it does not fit). */
@@ -346,6 +346,76 @@ TE_API te_status te_attn_exchange_output(te_attn_exchange *exchange, float **out
 TE_API te_status te_attention_prefill(te_kv_cache *cache, size_t layer_begin, size_t n_layers,
                                       size_t seq, const void *q, const void *k, const void *v,
                                       size_t n_tokens, size_t heads, float *out, uint32_t flags);
+
+/* Whole-token qwen2 decode step in one launch ------------------------------
+ *
+ * te_qwen_forward_token (c/src/qwen.c:907-1112) for every layer of one token
+ * -- RMSNorm, the q/k/v projections and their biases, RoPE, the f16 KV append,
+ * GQA attention, the output projection and its residual add, RMSNorm, the
+ * gate/up projections, SwiGLU, the down projection and its residual add --
+ * and optionally te_qwen_project_next (:1303-1377: output RMSNorm, lm_head,
+ * first-maximum argmax), as ONE cooperative kernel launch with one CTA per
+ * SM, where the per-op path (te_matvec_gguf_fused + te_attention_decode +
+ * te_matvec_gguf) takes five launches per layer.  The replaced reference
+ * boundary is the same pair of functions; the Metal path's counterpart is
+ * te_metal_decode_all_layers_f32 (c/src/metal_backend.h:206-343), which
+ * batches a token's layers into one command buffer.
+ *
+ * te_qwen_step_create packs, once, each CTA's row slice of every projection
+ * (q|k|v rows stacked, output, gate|up rows stacked, down, lm_head) into one
+ * contiguous device stream, a second copy of the weights (about the size of
+ * the projections); the caller's weight buffers are only read during the
+ * call.  All pointers in the descriptor are device pointers except the four
+ * arrays of per-layer matrix pointers, which are host arrays of `layers`
+ * device pointers (read during the call only).  Matrices are row-major GGUF
+ * Q4_0 / Q8_0 (TE_ATTN_QUANT_GGUF_*), 2-byte aligned:
+ *   w_qkv[l]  [(heads + 2 * kv_heads) * head_dim][hidden]  q rows, k rows, v rows
+ *   w_o[l]    [hidden][hidden]        w_gu[l] [2 * ffn][hidden]  gate rows, up rows
+ *   w_down[l] [hidden][ffn]           w_head  [vocab][hidden]
+ * attn_norm / ffn_norm [layers][hidden], out_norm [hidden] and the
+ * dequantised embedding table [vocab][hidden] are fp32, 16-byte aligned.
+ * kv_heads and head_dim are the cache's (head_dim 64 or 128, heads * head_dim
+ * == hidden, heads / kv_heads <= 16, hidden and ffn multiples of 32); the
+ * cache's layers must equal `layers`; the q/k/v biases are the cache's
+ * (te_kv_cache_set_qkv_bias with `heads`, applied with TE_ATTN_QKV_BIAS).
+ *
+ * te_qwen_step_run appends one token to sequence `seq` at index length (RoPE
+ * position offset + length) and runs every layer: *token (device int64) is
+ * the token, `hidden` (device fp32 [hidden], 16-byte aligned) receives the
+ * hidden state after the last layer (its previous contents are not read).
+ * With TE_ATTN_STEP_HEAD it also writes logits [vocab] and the greedy next
+ * token to *next_token (device int64).  Flags: TE_ATTN_ADVANCE,
+ * TE_ATTN_QKV_BIAS, TE_ATTN_STEP_HEAD.  Asynchronous on the engine's stream;
+ * within reserved pages (te_kv_cache_reserve) it issues only the kernel launch
+ * and can be captured in a CUDA graph.  Results agree with the per-op path
+ * to fp32 rounding (the same exact weight decoding, other summation orders).
+ * A token outside the vocabulary, or a device-side wait that runs out (2 s),
+ * sets the engine's error word (te_attn_engine_synchronize reports
+ * TE_STATUS_RUNTIME_ERROR).  Free every step before its cache.
+ */
+#define TE_ATTN_STEP_HEAD     (1u << 10) /* te_qwen_step_run: output RMSNorm + lm_head + argmax too */
+
+typedef struct te_qwen_step te_qwen_step;
+typedef struct te_qwen_step_desc {
+    uint32_t abi_version;      /* TE_ATTN_ABI_VERSION */
+    uint32_t layers, hidden, heads, ffn, vocab;
+    float eps;                 /* RMSNorm epsilon, > 0 */
+    uint32_t quant_qkv, quant_o, quant_gu, quant_down, quant_head;
+    const void *const *w_qkv;  /* host array [layers] of device pointers */
+    const void *const *w_o;
+    const void *const *w_gu;
+    const void *const *w_down;
+    const void *w_head;
+    const float *attn_norm;
+    const float *ffn_norm;
+    const float *out_norm;
+    const float *embedding;
+} te_qwen_step_desc;
+
+TE_API te_status te_qwen_step_create(te_kv_cache *cache, const te_qwen_step_desc *desc, te_qwen_step **out_step);
+TE_API te_status te_qwen_step_run(te_qwen_step *step, size_t seq, const int64_t *token, float *hidden,
+                                  float *logits, int64_t *next_token, uint32_t flags);
+TE_API void te_qwen_step_free(te_qwen_step *step);
 
 /*
  * Allocation-free decode for callers that cannot allocate device memory:

@@ -46,8 +46,9 @@ def margin(logits):
     return float(top[1] - top[0])
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["step", "per_op"])
 @pytest.mark.parametrize("name", list(MODELS))
-def test_decode_steps_match_reference(tmp_path, name):
+def test_decode_steps_match_reference(tmp_path, name, fused):
     from oracle import oracle as O
     if not O.ref_qwen_available():
         pytest.skip("reference forward pass not built")
@@ -58,7 +59,8 @@ def test_decode_steps_match_reference(tmp_path, name):
     ctx = 48
     ref = O.RefQwen(path, ctx)
     eng = AttnEngine(0)
-    dec = QwenDecoder(eng, path, ctx)
+    dec = QwenDecoder(eng, path, ctx, fused_step=fused)
+    assert dec.fused_step == fused
     try:
         vocab = ref.dims["vocab"]
         rng = np.random.default_rng(5)
@@ -112,7 +114,8 @@ def test_decoder_rejects_gaps_and_bad_tokens(tmp_path):
         eng.close()
 
 
-def test_graph_replay_matches_eager_steps(tmp_path):
+@pytest.mark.parametrize("fused", [True, False], ids=["step", "per_op"])
+def test_graph_replay_matches_eager_steps(tmp_path, fused):
     """capture_greedy / replay_greedy: the same kernels as the eager steps, recorded once; the tokens and
     the final hidden state equal the eager run's, replaying twice gives the same tokens, and eager steps
     continue after a replay."""
@@ -125,7 +128,7 @@ def test_graph_replay_matches_eager_steps(tmp_path):
     n = 16
     eng = AttnEngine(0)
     try:
-        eager = QwenDecoder(eng, path, 40)
+        eager = QwenDecoder(eng, path, 40, fused_step=fused)
         for pos, t in enumerate(prompt):
             eager.forward_token(t, pos)
         first = eager.project_next()
@@ -138,7 +141,7 @@ def test_graph_replay_matches_eager_steps(tmp_path):
         after = eager.forward_token(tok, len(prompt) + n).cpu().numpy()
         eager.close()
 
-        g = QwenDecoder(eng, path, 40)
+        g = QwenDecoder(eng, path, 40, fused_step=fused)
         for pos, t in enumerate(prompt):
             g.forward_token(t, pos)
         assert g.project_next() == first

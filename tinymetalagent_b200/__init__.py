@@ -16,8 +16,10 @@ from .runtime import (  # noqa: F401
     TE_ATTN_RMSNORM_INPUT,
     TE_ATTN_SWIGLU_INPUT,
     TE_ATTN_EXACT_Q,
+    TE_ATTN_STEP_HEAD,
     AttnEngine,
     KVCache,
+    QwenStep,
     TinyEngineError,
     attention_decode_f32,
     load_library,

@@ -20,7 +20,7 @@ BUILD = PKG / "_build"
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["k_decode.cu", "k_rope.cu", "k_prefill.cu", "k_exchange.cu", "k_gemv.cu"]
+CU_SOURCES = ["k_decode.cu", "k_rope.cu", "k_prefill.cu", "k_exchange.cu", "k_gemv.cu", "k_step.cu"]
 CXX_SOURCES = ["te_api.cpp"]
 C_SOURCES = ["rope_table.c"]
 

@@ -56,7 +56,7 @@ struct te_attn_engine {
   };
   std::vector<ProfPair> prof_pending;
   std::vector<ProfPair> prof_free;
-  double prof_ms[8] = {};
+  double prof_ms[8] = {};  // per ProfKind
   uint64_t prof_calls[8] = {};
 };
 
@@ -121,9 +121,11 @@ bool cuda_device_available() {
 }
 
 // Kernel families of the profile, in report order.
-enum ProfKind { PK_DECODE = 0, PK_APPEND, PK_MERGE, PK_PREFILL_PREP, PK_PREFILL_ATTN, PK_MATVEC, PK_EXCHANGE, PK_COUNT };
+enum ProfKind {
+  PK_DECODE = 0, PK_APPEND, PK_MERGE, PK_PREFILL_PREP, PK_PREFILL_ATTN, PK_MATVEC, PK_EXCHANGE, PK_STEP, PK_COUNT
+};
 const char* const kProfNames[PK_COUNT] = {"decode",       "append", "merge",   "prefill_prep",
-                                          "prefill_attn", "matvec", "exchange"};
+                                          "prefill_attn", "matvec", "exchange", "step"};
 
 // Opens a profiled launch: records the first event of a pair on the engine's
 // stream and returns its slot, or -1 when profiling is off or the stream is
@@ -1445,6 +1447,246 @@ TE_API te_status te_attention_prefill(te_kv_cache* c, size_t layer_begin, size_t
     if (err != cudaSuccess) return cuda_fail(e, err, "output download");
   }
   if (flags & TE_ATTN_ADVANCE) c->len[seq] = (int64_t)total;
+  return TE_STATUS_OK;
+}
+
+
+// ===========================================================================
+// Whole-token qwen2 decode step (k_step.cu)
+// ===========================================================================
+
+struct te_qwen_step {
+  te_kv_cache* cache = nullptr;
+  te_attn_engine* eng = nullptr;
+  StepParams p{};           // everything but the per-call fields
+  unsigned char* wpack = nullptr;
+  long long* d_off = nullptr;
+  float* scratch = nullptr;
+  uint32_t* sync = nullptr;
+  int grid = 0, smem = 0;
+  uint32_t heads = 0;
+};
+
+TE_API void te_qwen_step_free(te_qwen_step* st) {
+  if (!st) return;
+  if (st->eng) {
+    DeviceGuard dg(st->eng->device);
+    cudaStreamSynchronize(st->eng->stream);
+    cudaFree(st->wpack);
+    cudaFree(st->d_off);
+    cudaFree(st->scratch);
+    cudaFree(st->sync);
+  }
+  delete st;
+}
+
+TE_API te_status te_qwen_step_create(te_kv_cache* c, const te_qwen_step_desc* d, te_qwen_step** out) {
+  if (!c || !d || !out) return TE_STATUS_INVALID_ARGUMENT;
+  *out = nullptr;
+  te_attn_engine* e = c->eng;
+  if (d->abi_version != TE_ATTN_ABI_VERSION) return fail(e, TE_STATUS_INVALID_ARGUMENT, "abi_version mismatch");
+  const uint32_t L = d->layers, H = d->hidden, NH = d->heads, F = d->ffn, V = d->vocab;
+  const uint32_t kvh = c->d.kv_heads, hd = c->d.head_dim;
+  if (L == 0 || L != c->d.layers || NH == 0 || NH % kvh != 0 || NH * hd != H || H % 32 != 0 || F == 0 ||
+      F % 32 != 0 || V == 0 || !(d->eps > 0.0f)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "model shape does not match the cache (heads * head_dim == hidden, "
+                                               "hidden and ffn multiples of 32)");
+  }
+  if (NH / kvh > 16) return fail(e, TE_STATUS_UNSUPPORTED, "more than 16 query heads per kv head");
+  if (H > (1u << 24) || F > (1u << 24) || V > (uint32_t)INT32_MAX) return TE_STATUS_INVALID_ARGUMENT;
+  const uint32_t quants[kStepKinds] = {d->quant_qkv, d->quant_o, d->quant_gu, d->quant_down, d->quant_head};
+  for (uint32_t q : quants) {
+    if (q != TE_ATTN_QUANT_GGUF_Q4_0 && q != TE_ATTN_QUANT_GGUF_Q8_0) return TE_STATUS_INVALID_ARGUMENT;
+  }
+  if (!d->w_qkv || !d->w_o || !d->w_gu || !d->w_down || !d->w_head || !d->attn_norm || !d->ffn_norm ||
+      !d->out_norm || !d->embedding) {
+    return TE_STATUS_INVALID_ARGUMENT;
+  }
+  const void* const* per_layer[4] = {d->w_qkv, d->w_o, d->w_gu, d->w_down};
+  for (int k = 0; k < 4; ++k) {
+    for (uint32_t l = 0; l < L; ++l) {
+      if (!per_layer[k][l] || (reinterpret_cast<uintptr_t>(per_layer[k][l]) & 1u)) {
+        return fail(e, TE_STATUS_INVALID_ARGUMENT, "projection pointers must be non-null and 2-byte aligned");
+      }
+    }
+  }
+  if ((reinterpret_cast<uintptr_t>(d->w_head) & 1u) ||
+      ((reinterpret_cast<uintptr_t>(d->attn_norm) | reinterpret_cast<uintptr_t>(d->ffn_norm) |
+        reinterpret_cast<uintptr_t>(d->out_norm) | reinterpret_cast<uintptr_t>(d->embedding)) & 15u)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "norm weights and the embedding table must be 16-byte aligned");
+  }
+  if ((uint64_t)c->d.layers * c->d.total_pages * kvh * c->d.page_tokens >= (1ull << 31)) {
+    return fail(e, TE_STATUS_UNSUPPORTED, "KV pool too large for the step kernel's 32-bit row ids");
+  }
+  DeviceGuard dg(e->device);
+  const int G = e->sm_count;
+  const uint32_t kv = kvh * hd;
+  const uint32_t rows[kStepKinds] = {H + 2 * kv, H, 2 * F, H, V};
+  const uint32_t cols[kStepKinds] = {H, H, H, F, H};
+  int max_row = 0;
+  for (int k = 0; k < kStepKinds; ++k) {
+    const int bb = quants[k] == TE_ATTN_QUANT_GGUF_Q4_0 ? 18 : 34;
+    max_row = std::max(max_row, (int)(cols[k] / 32 * bb));
+  }
+  const int slot = std::max(8192, (max_row + 15) & ~15);
+  const int attn_bytes = 4 * (16 * (int)hd + 16 * 256 + 32 + 256);
+  const int union_bytes = (std::max((int)std::max(H, F) * 4, attn_bytes) + 127) & ~127;
+  const int budget = 227 * 1024 - step_fixed_smem() - union_bytes;
+  const int n_slots = std::min(kStepMaxSlots, budget > 0 ? budget / slot : 0);
+  if (n_slots < 3) return fail(e, TE_STATUS_UNSUPPORTED, "rows or vectors too long for the step kernel's ring");
+  const int smem = step_smem_bytes(slot, n_slots, union_bytes);
+  cudaError_t err = step_configure();
+  if (err != cudaSuccess) return cuda_fail(e, err, "step kernel shared-memory limit");
+  if (step_max_ctas_per_sm(smem) < 1) return fail(e, TE_STATUS_UNSUPPORTED, "step kernel does not fit an SM");
+
+  StepParams p{};
+  for (int k = 0; k < kStepKinds; ++k) {
+    plan_step_mat(p.mat[k], (int)rows[k], (int)cols[k], quants[k] == TE_ATTN_QUANT_GGUF_Q4_0 ? 18 : 34, G, slot);
+  }
+  // each CTA's stream: its stages of every layer's four projections, then the head's
+  std::vector<long long> off((size_t)G + 1);
+  std::vector<StepPackSeg> segs;
+  long long pos = 0;
+  auto add = [&](int k, const void* w, int b) {
+    const StepMat& m = p.mat[k];
+    int r0;
+    const int n = step_cta_rows(m, b, r0);
+    const int ns = step_n_stages(n, m.rps);
+    for (int s = 0; s < ns; ++s) {
+      const int lo = step_stage_lo(s, n, ns), hi = step_stage_lo(s + 1, n, ns);
+      StepPackSeg sg;
+      sg.src = static_cast<const unsigned char*>(w) + (size_t)(r0 + lo) * m.row_bytes;
+      sg.dst_off = pos;
+      sg.bytes = (long long)(hi - lo) * m.row_bytes;
+      segs.push_back(sg);
+      pos += step_stage_bytes(hi - lo, m.row_bytes);
+    }
+  };
+  for (int b = 0; b < G; ++b) {
+    off[(size_t)b] = pos;
+    for (uint32_t l = 0; l < L; ++l) {
+      for (int k = 0; k < 4; ++k) add(k, per_layer[k][l], b);
+    }
+    add(kStepHead, d->w_head, b);
+  }
+  off[(size_t)G] = pos;
+  if (segs.size() > (size_t)INT32_MAX) return TE_STATUS_UNSUPPORTED;
+
+  auto* st = new te_qwen_step();
+  st->cache = c;
+  st->eng = e;
+  st->grid = G;
+  st->smem = smem;
+  st->heads = NH;
+  const int max_chunks = (int)((c->d.max_tokens_per_seq + 255) / 256);
+  const size_t group = NH / kvh;
+  auto up4 = [](size_t n) { return (n + 3) & ~size_t(3); };  // 16-byte aligned sub-buffers
+  const size_t n_qkv = up4(H + 2 * kv), n_attn = up4(H), n_gu = up4(2 * (size_t)F);
+  const size_t n_rec = up4((size_t)kvh * max_chunks * group * (hd + 2)), n_cand = up4(2 * (size_t)G);
+  StepPackSeg* d_segs = nullptr;
+  err = cudaMalloc(&st->wpack, (size_t)std::max(pos, 16ll));
+  if (err == cudaSuccess) err = cudaMalloc(&st->d_off, off.size() * sizeof(long long));
+  if (err == cudaSuccess) err = cudaMalloc(&st->scratch, (n_qkv + n_attn + n_gu + n_rec + n_cand) * sizeof(float));
+  if (err == cudaSuccess) err = cudaMalloc(&st->sync, (4 + kvh) * sizeof(uint32_t));
+  if (err == cudaSuccess) err = cudaMalloc(&d_segs, std::max<size_t>(segs.size(), 1) * sizeof(StepPackSeg));
+  if (err == cudaSuccess) err = cudaMemsetAsync(st->wpack, 0, (size_t)std::max(pos, 16ll), e->stream);
+  if (err == cudaSuccess) err = cudaMemsetAsync(st->sync, 0, (4 + kvh) * sizeof(uint32_t), e->stream);
+  if (err == cudaSuccess) {
+    err = cudaMemcpyAsync(st->d_off, off.data(), off.size() * sizeof(long long), cudaMemcpyHostToDevice, e->stream);
+  }
+  if (err == cudaSuccess && !segs.empty()) {
+    err = cudaMemcpyAsync(d_segs, segs.data(), segs.size() * sizeof(StepPackSeg), cudaMemcpyHostToDevice, e->stream);
+  }
+  if (err == cudaSuccess) err = launch_step_pack(d_segs, (int)segs.size(), st->wpack, e->stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+  if (d_segs) cudaFree(d_segs);
+  if (err != cudaSuccess) {
+    te_qwen_step_free(st);
+    return cuda_fail(e, err, "step set-up");
+  }
+  p.wpack = st->wpack;
+  p.cta_off = st->d_off;
+  p.layers = (int32_t)L;
+  p.hidden = (int32_t)H;
+  p.heads = (int32_t)NH;
+  p.kv_heads = (int32_t)kvh;
+  p.head_dim = (int32_t)hd;
+  p.ffn = (int32_t)F;
+  p.vocab = (int32_t)V;
+  p.group = (int32_t)group;
+  p.eps = d->eps;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)hd));
+  p.k_pool = c->k_pool;
+  p.v_pool = c->v_pool;
+  p.num_pages = (int32_t)c->d.total_pages;
+  p.page_tokens = (int32_t)c->d.page_tokens;
+  p.rope_cos = c->d_cos;
+  p.rope_sin = c->d_sin;
+  p.attn_norm = d->attn_norm;
+  p.ffn_norm = d->ffn_norm;
+  p.out_norm = d->out_norm;
+  p.emb = d->embedding;
+  p.qkv = st->scratch;
+  p.attn = p.qkv + n_qkv;
+  p.gu = p.attn + n_attn;
+  p.rec = p.gu + n_gu;
+  p.cand = p.rec + n_rec;
+  p.sync = st->sync;
+  p.error = e->d_error;
+  p.slot_bytes = slot;
+  p.n_slots = n_slots;
+  p.union_bytes = union_bytes;
+  st->p = p;
+  *out = st;
+  return TE_STATUS_OK;
+}
+
+TE_API te_status te_qwen_step_run(te_qwen_step* st, size_t seq, const int64_t* token, float* hidden, float* logits,
+                                  int64_t* next_token, uint32_t flags) {
+  if (!st || !token || !hidden) return TE_STATUS_INVALID_ARGUMENT;
+  te_kv_cache* c = st->cache;
+  te_attn_engine* e = st->eng;
+  if (flags & ~(TE_ATTN_ADVANCE | TE_ATTN_QKV_BIAS | TE_ATTN_STEP_HEAD)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "unsupported flags for te_qwen_step_run");
+  }
+  const bool head = (flags & TE_ATTN_STEP_HEAD) != 0;
+  if (head && (!logits || !next_token)) return fail(e, TE_STATUS_INVALID_ARGUMENT, "the head needs logits and next_token");
+  if ((reinterpret_cast<uintptr_t>(hidden) & 15u) || (reinterpret_cast<uintptr_t>(token) & 7u) ||
+      (head && ((reinterpret_cast<uintptr_t>(logits) & 3u) || (reinterpret_cast<uintptr_t>(next_token) & 7u)))) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "hidden must be 16-byte aligned, token and next_token 8-byte aligned");
+  }
+  if (seq >= c->d.max_seqs) return TE_STATUS_INVALID_ARGUMENT;
+  if ((flags & TE_ATTN_QKV_BIAS) && (!c->d_qb || c->bias_heads != st->heads)) {
+    return fail(e, TE_STATUS_INVALID_ARGUMENT, "TE_ATTN_QKV_BIAS needs te_kv_cache_set_qkv_bias with these heads");
+  }
+  const int64_t len = c->len[seq] + 1;
+  if ((uint64_t)len > c->d.max_tokens_per_seq) return fail(e, TE_STATUS_INVALID_ARGUMENT, "sequence full");
+  const int64_t pos = c->offset[seq] + len - 1;
+  if ((uint64_t)pos >= c->d.max_position) return fail(e, TE_STATUS_INVALID_ARGUMENT, "RoPE position beyond max_position");
+  DeviceGuard dg(e->device);
+  te_status sts = ensure_pages(c, seq, (size_t)len);
+  if (sts != TE_STATUS_OK) return sts;
+  StepParams p = st->p;
+  p.page_row = c->d_page_table + seq * c->pages_per_seq;
+  p.page_base = contiguous_base(c, seq, (size_t)len);
+  p.n_tokens = (int32_t)len;
+  p.rope_pos = (int32_t)pos;
+  if (flags & TE_ATTN_QKV_BIAS) {
+    p.q_bias = c->d_qb;
+    p.k_bias = c->d_kb;
+    p.v_bias = c->d_vb;
+  }
+  p.token_in = token;
+  p.x = hidden;
+  p.logits = logits;
+  p.token_out = next_token;
+  p.head = head ? 1 : 0;
+  const int prof = prof_begin(e, PK_STEP);
+  const cudaError_t err = launch_step(p, st->grid, st->smem, e->stream);
+  prof_end(e, prof);
+  if (err != cudaSuccess) return cuda_fail(e, err, "step kernel launch");
+  e->launches++;
+  if (flags & TE_ATTN_ADVANCE) c->len[seq] = len;
   return TE_STATUS_OK;
 }
 

@@ -332,4 +332,89 @@ struct GemvParams {
 // block_bytes 18 (Q4_0) or 34 (Q8_0); 1 <= n_vectors <= 8.
 cudaError_t launch_gemv_gguf(GemvParams p, int block_bytes, int n_vectors, int sm_count, cudaStream_t s);
 
+// ---- whole-token qwen2 decode step (k_step.cu) -----------------------------
+// One cooperative launch runs every layer of one token: CTA b owns a fixed
+// slice of rows of every projection, and its share of all weights is packed
+// into one contiguous, 16-byte aligned byte stream (stages of whole rows, in
+// the order the kernel consumes them), which a producer warp copies into a
+// shared-memory ring ahead of the consumer warps, across phase boundaries.
+enum StepKind { kStepQKV = 0, kStepO = 1, kStepGU = 2, kStepDown = 3, kStepHead = 4, kStepKinds = 5 };
+constexpr int kStepMaxStageRows = 64;  // rows per stage (per-stage partial-sum area)
+constexpr int kStepMaxSlots = 32;      // ring slots
+
+struct StepMat {
+  int32_t rows, cols;
+  int32_t block_bytes;  // 18 (Q4_0) or 34 (Q8_0)
+  int32_t row_bytes;    // cols / 32 * block_bytes
+  int32_t rpc;          // rows per CTA (CTA b: rows [b * rpc, min(rows, (b + 1) * rpc)))
+  int32_t rps;          // most rows per stage
+};
+
+// Rows of matrix m owned by CTA b (first row in r0).
+__host__ __device__ inline int step_cta_rows(const StepMat& m, int b, int& r0) {
+  r0 = b * m.rpc;
+  const int r1 = r0 + m.rpc < m.rows ? r0 + m.rpc : m.rows;
+  return r1 > r0 ? r1 - r0 : 0;
+}
+__host__ __device__ inline int step_n_stages(int n, int rps) { return n > 0 ? (n + rps - 1) / rps : 0; }
+// Stage s of n rows split into ns stages covers rows [lo(s), lo(s + 1)).
+__host__ __device__ inline int step_stage_lo(int s, int n, int ns) { return (int)((long long)s * n / ns); }
+__host__ __device__ inline uint32_t step_stage_bytes(int rows, int row_bytes) {
+  return ((uint32_t)rows * (uint32_t)row_bytes + 15u) & ~15u;
+}
+
+struct StepParams {
+  const unsigned char* wpack;  // packed weight streams
+  const long long* cta_off;    // [grid + 1] byte offset of each CTA's stream
+  StepMat mat[kStepKinds];
+  int32_t layers, hidden, heads, kv_heads, head_dim, ffn, vocab, group;
+  float eps;
+  float scale_log2;            // log2(e) / sqrt(head_dim)
+  // KV cache (one sequence)
+  uint16_t* k_pool;
+  uint16_t* v_pool;
+  const int32_t* page_row;     // the sequence's page-table row
+  int32_t page_base;           // >= 0: pages are page_base, page_base + 1, ... (no table read)
+  int32_t num_pages, page_tokens;
+  int32_t n_tokens;            // tokens attended, the new one included (its cache index is n_tokens - 1)
+  int32_t rope_pos;            // RoPE position of the new token (= of the query)
+  const float* rope_cos;       // [max_position][head_dim / 2]
+  const float* rope_sin;
+  const float* q_bias;         // null, or [layers][heads * head_dim]
+  const float* k_bias;         // null, or [layers][kv_heads * head_dim]
+  const float* v_bias;
+  const float* attn_norm;      // [layers][hidden]
+  const float* ffn_norm;       // [layers][hidden]
+  const float* out_norm;       // [hidden]
+  const float* emb;            // [vocab][hidden] fp32
+  const int64_t* token_in;     // device: this step's token
+  int64_t* token_out;          // device: the greedy next token (head only)
+  float* x;                    // [hidden] residual stream (out: the hidden state after the last layer)
+  float* qkv;                  // [heads * hd + 2 * kv_heads * hd]
+  float* attn;                 // [heads * hd]
+  float* gu;                   // [2 * ffn]
+  float* logits;               // [vocab] (head only)
+  float* rec;                  // attention partial records [kv_heads][chunks][group][hd + 2]
+  float* cand;                 // [grid][2] per-CTA argmax candidates
+  uint32_t* sync;              // [0] grid count, [1] exit count, [2] argmax ticket, [4 + g] merge count of kv head g
+  int* error;
+  int32_t head;                // 1: output RMSNorm + lm_head + argmax after the layers
+  int32_t slot_bytes, n_slots, union_bytes;
+};
+// Plans matrix m's split over `grid` CTAs with stages of at most slot_bytes.
+void plan_step_mat(StepMat& m, int rows, int cols, int block_bytes, int grid, int slot_bytes);
+// Shared memory of the step kernel for these sizes.
+int step_smem_bytes(int slot_bytes, int n_slots, int union_bytes);
+int step_fixed_smem();
+cudaError_t step_configure();  // raises the kernel's shared-memory limit on the current device
+int step_max_ctas_per_sm(int smem);
+cudaError_t launch_step(const StepParams& p, int grid, int smem, cudaStream_t s);
+// Packing: n segments, each `bytes` from src[i] (2-byte aligned) to dst + dst_off[i] (16-byte aligned).
+struct StepPackSeg {
+  const void* src;
+  long long dst_off;
+  long long bytes;
+};
+cudaError_t launch_step_pack(const StepPackSeg* segs, int n, unsigned char* dst, cudaStream_t s);
+
 }  // namespace te

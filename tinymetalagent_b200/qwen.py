@@ -31,7 +31,7 @@ import numpy as np
 
 from .gguf import GGML_F32, GGML_Q4_0, GGML_Q8_0, GGUFError, GGUFFile
 from .runtime import (TE_ATTN_ACCUMULATE, TE_ATTN_ADVANCE, TE_ATTN_QKV_BIAS, TE_ATTN_RMSNORM_INPUT,
-                      TE_ATTN_SWIGLU_INPUT, AttnEngine)
+                      TE_ATTN_STEP_HEAD, TE_ATTN_SWIGLU_INPUT, AttnEngine, QwenStep)
 
 _QUANT = {GGML_Q4_0: 4, GGML_Q8_0: 8}  # ggml type -> TE_ATTN_QUANT_GGUF_*
 
@@ -46,11 +46,20 @@ class QwenDecoder:
     returns the greedy next token and leaves the logits in `self.logits`.
     Work runs on the engine's stream; before returning, both make the
     caller's current stream wait for it, so the results can be used there.
+
+    With fused_step (the default) a decode token runs as ONE launch of the
+    library's whole-token step kernel (te_qwen_step_run: every layer, and in
+    recorded greedy steps the head and argmax too) instead of five launches
+    per layer; the per-op path (fused_step=False) stays available and is what
+    prefill_prompt uses.  The fused step needs the same quantisation for a
+    projection in every layer; otherwise the decoder takes the per-op path.
     """
 
-    def __init__(self, engine: AttnEngine, model: str | Path | GGUFFile, context_tokens: int):
+    def __init__(self, engine: AttnEngine, model: str | Path | GGUFFile, context_tokens: int,
+                 fused_step: bool = True):
         import torch
 
+        self._want_step = fused_step
         self.engine = engine
         self._owns_gguf = not isinstance(model, GGUFFile)
         self.gguf = model if isinstance(model, GGUFFile) else GGUFFile(model)
@@ -131,6 +140,18 @@ class QwenDecoder:
                                           kv_heads=kvh, head_dim=hd, max_position=self.context_tokens,
                                           rope_theta=d["rope_base"])
         self.cache.set_qkv_bias(0, heads, qb, kb, vb)
+        self._step = None
+        quants = {k: {w["q_" + k] for w in self.layers} for k in ("qkv", "o", "gu", "down")}
+        if self._want_step and all(len(v) == 1 for v in quants.values()):
+            self._norms = (torch.stack([w["attn_norm"] for w in self.layers]).contiguous(),
+                           torch.stack([w["ffn_norm"] for w in self.layers]).contiguous())
+            self._step = QwenStep(
+                self.cache, layers=L, hidden=H, heads=heads, ffn=F, vocab=d["vocab"], eps=d["eps"],
+                quants={**{k: next(iter(v)) for k, v in quants.items()}, "head": self._q_head},
+                w_qkv=[w["qkv"] for w in self.layers], w_o=[w["o"] for w in self.layers],
+                w_gu=[w["gu"] for w in self.layers], w_down=[w["down"] for w in self.layers], w_head=self._head,
+                attn_norm=self._norms[0], ffn_norm=self._norms[1], out_norm=self._out_norm, embedding=self._emb)
+        self._tok = torch.zeros(1, dtype=torch.int64, device=dev)
         self.x = torch.zeros(H, dtype=torch.float32, device=dev)
         self._qkv = torch.empty(H + 2 * self.kv, dtype=torch.float32, device=dev)
         self._attn = torch.empty(H, dtype=torch.float32, device=dev)
@@ -166,6 +187,11 @@ class QwenDecoder:
         (the graph-captured steps read it from device memory)."""
         return self._emb[token] if isinstance(token, int) else self._emb.index_select(0, token)[0]
 
+    @property
+    def fused_step(self) -> bool:
+        """True when decode tokens run as one te_qwen_step_run launch."""
+        return self._step is not None
+
     # ---- the step ----------------------------------------------------------
     def forward_token(self, token: int, position: int):
         import torch
@@ -175,7 +201,10 @@ class QwenDecoder:
         torch.cuda.current_stream(self._dev).wait_stream(self._stream)
         return x
 
-    def _forward(self, token: int, position: int):
+    def _forward(self, token: int, position: int, next_token=None):
+        """Every layer for one token; with next_token (a one-element int64
+        device tensor, fused step only) also the head, the logits in
+        self.logits and the greedy choice in next_token."""
         import torch
         d = self.dims
         H, F, L = d["hidden"], d["ffn"], d["layers"]
@@ -191,6 +220,16 @@ class QwenDecoder:
             self.cache.truncate(0, position)
         eng = self.engine
         eps = d["eps"]
+        if self._step is not None:
+            if isinstance(token, int):
+                self._tok.fill_(token)
+                token = self._tok
+            flags = TE_ATTN_QKV_BIAS | TE_ATTN_ADVANCE
+            if next_token is not None:
+                self._step.run(0, token, self.x, self.logits, next_token, flags | TE_ATTN_STEP_HEAD)
+            else:
+                self._step.run(0, token, self.x, flags=flags)
+            return self.x
         self.x.copy_(self._embed(token))
         for layer, w in enumerate(self.layers):
             eng.matvec_gguf_fused(w["q_qkv"], w["qkv"], H + 2 * self.kv, H, self.x, self._qkv, TE_ATTN_RMSNORM_INPUT,
@@ -310,6 +349,9 @@ class QwenDecoder:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=self._stream):
             for i in range(n_steps):
+                if self._step is not None:  # one launch per token: layers, head and argmax
+                    self._forward(self.tokens[i:i + 1], start_position + i, next_token=self.tokens[i + 1:i + 2])
+                    continue
                 self._forward(self.tokens[i:i + 1], start_position + i)
                 self._head_logits()
                 self.tokens[i + 1:i + 2].copy_(torch.argmax(self.logits).reshape(1))
@@ -344,6 +386,9 @@ class QwenDecoder:
         if getattr(self, "_stream", None) is not None:
             self._stream.synchronize()
         self._graph = None
+        if getattr(self, "_step", None) is not None:
+            self._step.close()
+            self._step = None
         if getattr(self, "cache", None) is not None:
             self.cache.close()
             self.cache = None

@@ -37,6 +37,7 @@ TE_ATTN_ACCUMULATE = 1 << 6
 TE_ATTN_RMSNORM_INPUT = 1 << 7
 TE_ATTN_SWIGLU_INPUT = 1 << 8
 TE_ATTN_EXACT_Q = 1 << 9
+TE_ATTN_STEP_HEAD = 1 << 10
 TE_ATTN_QUANT_GGUF_Q4_0 = 4
 TE_ATTN_QUANT_GGUF_Q8_0 = 8
 
@@ -69,6 +70,32 @@ class KVCacheDesc(ctypes.Structure):
         ("total_pages", ctypes.c_uint32),
         ("max_position", ctypes.c_uint32),
         ("rope_theta", ctypes.c_float),
+    ]
+
+
+class QwenStepDesc(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", ctypes.c_uint32),
+        ("layers", ctypes.c_uint32),
+        ("hidden", ctypes.c_uint32),
+        ("heads", ctypes.c_uint32),
+        ("ffn", ctypes.c_uint32),
+        ("vocab", ctypes.c_uint32),
+        ("eps", ctypes.c_float),
+        ("quant_qkv", ctypes.c_uint32),
+        ("quant_o", ctypes.c_uint32),
+        ("quant_gu", ctypes.c_uint32),
+        ("quant_down", ctypes.c_uint32),
+        ("quant_head", ctypes.c_uint32),
+        ("w_qkv", ctypes.POINTER(ctypes.c_void_p)),
+        ("w_o", ctypes.POINTER(ctypes.c_void_p)),
+        ("w_gu", ctypes.POINTER(ctypes.c_void_p)),
+        ("w_down", ctypes.POINTER(ctypes.c_void_p)),
+        ("w_head", ctypes.c_void_p),
+        ("attn_norm", ctypes.c_void_p),
+        ("ffn_norm", ctypes.c_void_p),
+        ("out_norm", ctypes.c_void_p),
+        ("embedding", ctypes.c_void_p),
     ]
 
 
@@ -133,6 +160,9 @@ SIGNATURES: dict[str, tuple] = {
     "te_attention_decode_kv_split": (_int, [_vp, _vp, _sz, _sz, _sz, ctypes.c_int64, _vp, _vp, _vp, _sz, ctypes.c_uint32]),
     "te_attn_exchange_output": (_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
     "te_attention_prefill": (_int, [_vp, _sz, _sz, _sz, _vp, _vp, _vp, _sz, _sz, _vp, ctypes.c_uint32]),
+    "te_qwen_step_create": (_int, [_vp, ctypes.POINTER(QwenStepDesc), ctypes.POINTER(_vp)]),
+    "te_qwen_step_run": (_int, [_vp, _sz, _vp, _vp, _vp, _vp, ctypes.c_uint32]),
+    "te_qwen_step_free": (None, [_vp]),
     "te_attention_decode_paged_noalloc": (_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp, _sz, _sz, _sz, _vp, _vp]),
     "te_attention_decode_paged_noalloc_status": (_int, [_vp, ctypes.POINTER(ctypes.c_int)]),
 }
@@ -377,9 +407,13 @@ class KVCache:
         self.page_tokens = page_tokens
         self.max_tokens_per_seq = max_tokens_per_seq
         self.rope_theta = rope_theta
+        self._steps = weakref.WeakSet()
 
     def close(self) -> None:
-        # An engine that is already gone has freed this cache with itself.
+        # Steps built on this cache go first; an engine that is already gone
+        # has freed this cache with itself.
+        for step in list(getattr(self, "_steps", ())):
+            step.close()
         if getattr(self, "handle", None) and getattr(self.engine, "handle", None):
             self.lib.te_kv_cache_free(self.handle)
         self.handle = None
@@ -464,3 +498,54 @@ class KVCache:
                 flags: int = 0) -> None:
         self._c(self.lib.te_attention_prefill(self.handle, layer_begin, n_layers, seq, _addr(q), _addr(k), _addr(v),
                                               n_tokens, heads, _addr(out), flags))
+
+
+class QwenStep:
+    """te_qwen_step_*: every layer of one qwen2 decode token (and optionally the
+    output norm, lm_head and argmax) in one cooperative launch over `cache`.
+
+    Weights are device tensors (or addresses): per-layer lists w_qkv, w_o,
+    w_gu, w_down of GGUF Q4_0/Q8_0 rows, w_head, and the fp32 norms and
+    embedding table; quants maps "qkv", "o", "gu", "down", "head" to
+    TE_ATTN_QUANT_GGUF_*.  The library packs its own copy of the weights at
+    creation."""
+
+    def __init__(self, cache: KVCache, *, layers: int, hidden: int, heads: int, ffn: int, vocab: int, eps: float,
+                 quants: dict, w_qkv, w_o, w_gu, w_down, w_head, attn_norm, ffn_norm, out_norm, embedding):
+        self.cache = cache
+        self.engine = cache.engine
+        self.lib = cache.lib
+        d = QwenStepDesc()
+        d.abi_version = TE_ATTN_ABI_VERSION
+        d.layers, d.hidden, d.heads, d.ffn, d.vocab, d.eps = layers, hidden, heads, ffn, vocab, eps
+        d.quant_qkv, d.quant_o, d.quant_gu = quants["qkv"], quants["o"], quants["gu"]
+        d.quant_down, d.quant_head = quants["down"], quants["head"]
+        arrays = []
+        for name, ws in (("w_qkv", w_qkv), ("w_o", w_o), ("w_gu", w_gu), ("w_down", w_down)):
+            if len(ws) != layers:
+                raise ValueError(f"{name}: one matrix per layer")
+            arr = (ctypes.c_void_p * layers)(*[_addr(w) for w in ws])
+            arrays.append(arr)
+            setattr(d, name, ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)))
+        d.w_head, d.attn_norm, d.ffn_norm = _addr(w_head), _addr(attn_norm), _addr(ffn_norm)
+        d.out_norm, d.embedding = _addr(out_norm), _addr(embedding)
+        handle = _vp()
+        self.engine.check(self.lib.te_qwen_step_create(cache.handle, ctypes.byref(d), ctypes.byref(handle)))
+        self.handle = handle
+        cache._steps.add(self)
+
+    def run(self, seq: int, token, hidden, logits=None, next_token=None, flags: int = 0) -> None:
+        """token / next_token: one-element int64 device tensors (or addresses); hidden [hidden] fp32."""
+        self.engine.check(self.lib.te_qwen_step_run(self.handle, seq, _addr(token), _addr(hidden), _addr(logits),
+                                                    _addr(next_token), flags))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) and getattr(self.engine, "handle", None):
+            self.lib.te_qwen_step_free(self.handle)
+        self.handle = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
