@@ -21,15 +21,16 @@
 //
 // Phases per layer (every CTA; a CTA with no rows or items only arrives):
 //   A  q|k|v = W_qkv RMSNorm(x)       rows of the stacked q, k, v matrices
-//   B  attention                       work items (kv head, 256-token chunk):
+//   B  attention                       work items (kv head, 128-token chunk):
 //                                      bias + RoPE of the group's queries, the
 //                                      new k/v (bias, RoPE on k, f16 RNE) into
 //                                      the paged cache, scores, softmax, P.V;
 //                                      chunks of one kv head merge by
 //                                      log-sum-exp in the last arriving CTA
 //   C  x = x + W_o attn
-//   D  g|u = W_gu RMSNorm(x)
-//   E  x = x + W_down SwiGLU(g, u)
+//   D  h = SwiGLU(W_gate RMSNorm(x), W_up RMSNorm(x))   (gate and up rows of
+//                                      a stage side by side, SwiGLU in the epilogue)
+//   E  x = x + W_down h
 // then, optionally, logits = W_head RMSNorm(x) and the first-maximum argmax
 // (per-CTA candidates, reduced by the last arriving CTA).
 //
@@ -51,11 +52,11 @@
 namespace te {
 namespace {
 
-constexpr int kCWarps = 8;                    // consumer warps
+constexpr int kCWarps = 12;                   // consumer warps (three per SM sub-partition)
 constexpr int kCThreads = kCWarps * 32;
 constexpr int kStepThreads = kCThreads + 32;  // + one producer warp
-constexpr int kChunk = 256;                   // attention tokens per work item
-constexpr int kMaxGroup = 16;                 // query heads per kv head
+constexpr int kChunk = kStepChunk;            // attention tokens per work item
+constexpr int kMaxGroup = kStepMaxGroup;      // query heads per kv head
 
 // Shared memory: mbarriers, scalars, per-stage partial sums (two parities),
 // the phase work area (input vector, or the attention item's buffers), ring.
@@ -69,10 +70,24 @@ constexpr int kOffUnion = kOffRed + 2 * kRedFloats * 4;
 // misc words
 constexpr int kMiscAbort = 0;    // int: the consumers gave up (the producer stops)
 constexpr int kMiscLast = 4;     // int: this CTA merges (attention) / reduces (argmax)
-constexpr int kMiscDred = 64;    // double[8]: RMSNorm partial sums per warp
-constexpr int kMiscBest = 128;   // {float, int}[8]: argmax per warp
+constexpr int kMiscDred = 64;    // double[kCWarps]: RMSNorm partial sums per warp
+constexpr int kMiscBest = 160;   // {float, int}[kCWarps]: argmax per warp
+constexpr int kMiscRing = 256;   // u32[2][kStepMaxSlots]: the producer's in-flight stage ranges
+constexpr uint32_t kNQ = kStepMaxSlots;  // stage descriptors (full/empty mbarrier pairs), a power of two
+static_assert((kNQ & (kNQ - 1)) == 0 && kMiscRing + 8 * kStepMaxSlots <= kMiscBytes, "ring descriptors");
+static_assert(kMiscDred + 8 * kCWarps <= kMiscBest && kMiscBest + 8 * kCWarps <= kMiscRing, "misc layout");
 
-__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// The weight ring is a byte ring: stage i takes [off, off + bytes) at the
+// running head, or at 0 when it would pass the end.  Producer and consumers
+// apply the same rule to the same sequence of stage sizes, so only the
+// mbarriers of stage descriptor i % kNQ pass between them.
+__device__ __forceinline__ uint32_t ring_place(uint32_t& head, uint32_t bytes, uint32_t cap) {
+  const uint32_t off = head + bytes <= cap ? head : 0u;
+  head = off + bytes;
+  return off;
+}
+
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory"); }
 
 // Consumer barrier that also ORs a per-thread flag: every consumer thread
 // gets the same answer, so a failure seen by any thread stops all of them at
@@ -82,10 +97,10 @@ __device__ __forceinline__ bool cbar_or(bool pred) {
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 256, p;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"((uint32_t)pred)
+      : "r"((uint32_t)pred), "n"(kCThreads)
       : "memory");
   return r != 0;
 }
@@ -107,7 +122,6 @@ __device__ __forceinline__ void red_add_relaxed_gpu(uint32_t* p, uint32_t v) {
 // Activations written by other CTAs in this launch are read through L2
 // (ld.global.cg), never through the non-coherent or L1 paths.
 __device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
-__device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
@@ -121,6 +135,7 @@ struct Ctx {
   unsigned char* ring;
   int b, G, tid, warp, lane;
   uint32_t stage;      // stages consumed
+  uint32_t head;       // ring head after the stages consumed
   uint32_t phase;      // phases this CTA has arrived at
 };
 
@@ -166,14 +181,24 @@ __device__ __forceinline__ void grid_arrive(Ctx& c) {
 
 // ---- phase prologues: the input vector of a projection into U -------------
 
+// The prologues read vectors that other CTAs wrote in this launch: copied
+// into U by cp.async through L2 (.cg), every thread's 16-byte copies in
+// flight together, so a prologue costs about one L2 round trip and no
+// registers.
+__device__ __forceinline__ void stage_async(Ctx& c, const float* src, int n) {
+  for (int i = c.tid * 4; i < n; i += kCThreads * 4) cp_async_cg16(smem_u32(c.U + i), src + i);
+  cp_async_wait_all();
+  cbar();
+}
+
 // te_rmsnorm_f32 (c/src/ops.c:272-293): squares summed in double, scale =
 // 1 / sqrtf((float)(sum / n) + eps), out = (x * scale) * w.
 __device__ void prologue_rmsnorm(Ctx& c, const float* src, const float* w) {
   const int H = c.p->hidden;
+  stage_async(c, src, H);
   double ss = 0.0;
   for (int i = c.tid * 4; i < H; i += kCThreads * 4) {
-    const float4 v = ldcg4(src + i);
-    *reinterpret_cast<float4*>(c.U + i) = v;
+    const float4 v = *reinterpret_cast<const float4*>(c.U + i);
     ss += (double)v.x * (double)v.x + (double)v.y * (double)v.y + (double)v.z * (double)v.z +
           (double)v.w * (double)v.w;
   }
@@ -195,112 +220,83 @@ __device__ void prologue_rmsnorm(Ctx& c, const float* src, const float* w) {
   cbar();
 }
 
-__device__ void prologue_copy(Ctx& c, const float* src, int n) {
-  for (int i = c.tid * 4; i < n; i += kCThreads * 4) *reinterpret_cast<float4*>(c.U + i) = ldcg4(src + i);
-  cbar();
-}
-
-// te_swiglu_f32 (c/src/ops.c:397-406): gate / (1 + expf(-gate)) * up.
-__device__ void prologue_swiglu(Ctx& c) {
-  const int F = c.p->ffn;
-  for (int i = c.tid; i < F; i += kCThreads) c.U[i] = silu(ldcg(c.p->gu + i)) * ldcg(c.p->gu + F + i);
-  cbar();
-}
-
 // ---- projections ----------------------------------------------------------
 
-// Lane's 8 weights of one block (Q4_0: quant bytes 4j..4j+3 = weights 4j..
-// 4j+3 (low nibbles) and 16+4j.. (high); Q8_0: weights 8j..8j+7) dotted with
-// its 8 inputs: sum (q - offset) * x with exact weights, then * the block's
-// f16 scale (the reference's te_q4_0_dot_row / te_q8_0_dot_row products,
-// c/src/ops.c:584-620).
+// Block b of physical row r of a stage (transposed layout, see
+// step_stage_bytes): sum (q - offset) * x over its 32 weights with exact
+// weights (the code under the exponent of 2^23, minus 2^23 + offset), fp32
+// products and sums in two chains, times the block's f16 scale (the
+// reference's te_q4_0_dot_row / te_q8_0_dot_row products,
+// c/src/ops.c:584-620).  Q4_0: quant byte j holds weight j (low nibble) and
+// weight j + 16 (high nibble); Q8_0: 32 int8.  x: the block's 32 inputs
+// (shared memory, 16-byte aligned).
 template <int BB>
-__device__ __forceinline__ float block_dot(const unsigned char* blk, int j, const uint64_t (&xs)[4]) {
+__device__ __forceinline__ float block_dot(const unsigned char* stage, uint32_t scale_bytes, int RS, int r, int b,
+                                           const float* x) {
   constexpr float kOff = BB == 18 ? 8388616.0f : 8388736.0f;  // 2^23 + the quant offset (8 or 128)
   const uint64_t off2 = f2_pack(kOff, kOff);
-  const float sc = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
-  const uint16_t* qp = reinterpret_cast<const uint16_t*>(blk + (BB == 18 ? 2 + 4 * j : 2 + 8 * j));
-  uint32_t lo, hi;
+  const float sc = __half2float(__ushort_as_half(reinterpret_cast<const uint16_t*>(stage)[b * RS + r]));
+  const uint4* quants = reinterpret_cast<const uint4*>(stage + scale_bytes);
+  uint64_t da = 0, db = 0;  // two chains of two fp32 partial sums, all +0.0f
+  auto quad = [&](uint64_t& d, uint32_t codes, const float* xq) {  // 4 codes, one per byte, with x[0..3]
+    const float4 xv = *reinterpret_cast<const float4*>(xq);
+    const uint64_t w01 = f2_sub(f2_pack(__uint_as_float(prmt(codes, 0x4B000000u, 0x7440u)),
+                                        __uint_as_float(prmt(codes, 0x4B000000u, 0x7441u))), off2);
+    const uint64_t w23 = f2_sub(f2_pack(__uint_as_float(prmt(codes, 0x4B000000u, 0x7442u)),
+                                        __uint_as_float(prmt(codes, 0x4B000000u, 0x7443u))), off2);
+    d = f2_fma(w01, f2_pack(xv.x, xv.y), d);
+    d = f2_fma(w23, f2_pack(xv.z, xv.w), d);
+  };
   if (BB == 18) {
-    const uint32_t q = prmt(qp[0], qp[1], 0x5410u);
-    lo = q & 0x0f0f0f0fu;
-    hi = (q >> 4) & 0x0f0f0f0fu;
+    const uint4 q = quants[b * RS + r];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // quant bytes 4k .. 4k + 3
+      quad(da, w[k] & 0x0f0f0f0fu, x + 4 * k);
+      quad(db, (w[k] >> 4) & 0x0f0f0f0fu, x + 16 + 4 * k);
+    }
   } else {
-    lo = prmt(qp[0], qp[1], 0x5410u) ^ 0x80808080u;
-    hi = prmt(qp[2], qp[3], 0x5410u) ^ 0x80808080u;
+    const uint4 q0 = quants[(2 * b) * RS + r], q1 = quants[(2 * b + 1) * RS + r];
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) quad(k & 1 ? db : da, w[k] ^ 0x80808080u, x + 4 * k);
   }
-  uint64_t wq[4];
-  wq[0] = f2_pack(__uint_as_float(prmt(lo, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(lo, 0x4B000000u, 0x7441u)));
-  wq[1] = f2_pack(__uint_as_float(prmt(lo, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(lo, 0x4B000000u, 0x7443u)));
-  wq[2] = f2_pack(__uint_as_float(prmt(hi, 0x4B000000u, 0x7440u)), __uint_as_float(prmt(hi, 0x4B000000u, 0x7441u)));
-  wq[3] = f2_pack(__uint_as_float(prmt(hi, 0x4B000000u, 0x7442u)), __uint_as_float(prmt(hi, 0x4B000000u, 0x7443u)));
-#pragma unroll
-  for (int k = 0; k < 4; ++k) wq[k] = f2_sub(wq[k], off2);
-  uint64_t d = f2_mul(wq[0], xs[0]);
-#pragma unroll
-  for (int k = 1; k < 4; ++k) d = f2_fma(wq[k], xs[k], d);
   float d0, d1;
-  f2_unpack(d, d0, d1);
+  f2_unpack(f2_add(da, db), d0, d1);
   return sc * (d0 + d1);
 }
 
-// Warps per row for a stage of R rows and S column steps (a step is 8
-// blocks, one per four lanes): the split with the least work per warp.
-__device__ __forceinline__ int stage_wpr(int R, int S) {
-  int best = 1, cost = ((R + kCWarps - 1) / kCWarps) * S;
-#pragma unroll
-  for (int w = 2; w <= kCWarps; w *= 2) {
-    const int rg = kCWarps / w;
-    const int cw = ((R + rg - 1) / rg) * ((S + w - 1) / w);
-    if (cw < cost) {
-      cost = cw;
-      best = w;
-    }
-  }
-  return best;
-}
-
-// Partial dot products of a stage's R rows into red[row][part]: warp w takes
-// rows w / wpr, + 8 / wpr, ... and column steps w % wpr, + wpr, ...; the
-// input values a lane loads serve up to four rows.
+// Partial dot products of a stage's R (<= 32) rows into red[row][warp]:
+// rows go across lanes (RT = R rounded up to a power of two lanes per group
+// of K = 32 / RT lanes), and a row's blocks are dealt to its kCWarps * K
+// (warp, lane group) units, so each lane sums whole blocks of one row,
+// independent of each other, and a row's K lanes meet by shuffles.  With the
+// transposed stage layout the lanes of a warp read consecutive 16-byte
+// chunks (no bank conflicts) and share each input load (a broadcast).
 template <int BB>
-__device__ void stage_rows(const unsigned char* base, int row_bytes, int R, int nb, int S, int wpr, const float* xin,
-                           float* red, int warp, int lane) {
-  const int rg = kCWarps / wpr, rgi = warp / wpr, cp = warp % wpr;
-  const int j = lane & 3;
-  const int xo0 = BB == 18 ? 4 * j : 8 * j;
-  const int xo1 = BB == 18 ? 16 + 4 * j : 8 * j + 4;
-  for (int rb = rgi; rb < R; rb += 4 * rg) {
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int st = cp; st < S; st += wpr) {
-      const int blk = st * 8 + (lane >> 2);
-      if (blk < nb) {
-        const float4 a = *reinterpret_cast<const float4*>(xin + blk * 32 + xo0);
-        const float4 e = *reinterpret_cast<const float4*>(xin + blk * 32 + xo1);
-        const uint64_t xs[4] = {f2_pack(a.x, a.y), f2_pack(a.z, a.w), f2_pack(e.x, e.y), f2_pack(e.z, e.w)};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = rb + i * rg;
-          if (r < R) acc[i] += block_dot<BB>(base + (size_t)r * row_bytes + blk * BB, j, xs);
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = rb + i * rg;
-      if (r < R) {  // the same for the whole warp
-        float s = acc[i];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) red[r * kCWarps + cp] = s;
-      }
-    }
+__device__ void stage_rows(const unsigned char* stage, int R, int nb, const float* xin, float* red, int warp,
+                           int lane) {
+  int RT = 1;
+  while (RT < R) RT <<= 1;
+  const int K = 32 / RT;
+  const int r = lane & (RT - 1), k = lane / RT;
+  const int units = kCWarps * K;
+  const uint32_t scale_bytes = step_scale_bytes(R, nb);
+  float acc = 0.f;
+  if (r < R) {
+#pragma unroll 2
+    for (int b = warp * K + k; b < nb; b += units) acc += block_dot<BB>(stage, scale_bytes, R, r, b, xin + b * 32);
   }
+  for (int o = RT; o < 32; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (k == 0 && r < R) red[r * kCWarps + warp] = acc;
 }
 
 // One projection phase over this CTA's rows: y[row] = dot, or resid[row] +
 // dot (fp32 add: the residual add after the output and down projections);
 // with `best` also the running first-maximum (value, row) of the outputs.
+// For the gate/up matrix (m.pair) a stage holds R gate rows then the same R
+// up rows, and y[row] = SwiGLU(gate, up) = gate / (1 + expf(-gate)) * up
+// (te_swiglu_f32, c/src/ops.c:397-406): the down projection's input.
 __device__ bool gemv_phase(Ctx& c, int kind, float* y, const float* resid, float* best_v, int* best_i) {
   const StepParams& p = *c.p;
   const StepMat& m = p.mat[kind];
@@ -308,20 +304,20 @@ __device__ bool gemv_phase(Ctx& c, int kind, float* y, const float* resid, float
   const int n = step_cta_rows(m, c.b, r0);
   const int ns = step_n_stages(n, m.rps);
   const int nb = m.cols / 32;
-  const int S = (nb + 7) / 8;
   for (int s = 0; s < ns; ++s) {
     const int lo = step_stage_lo(s, n, ns);
     const int R = step_stage_lo(s + 1, n, ns) - lo;
-    const int wpr = stage_wpr(R, S);
-    const uint32_t slot = c.stage % (uint32_t)p.n_slots;
-    const bool ok = mbar_wait_warp(&c.full[slot], (c.stage / (uint32_t)p.n_slots) & 1u);
+    const int RS = m.pair ? 2 * R : R;  // rows in the stage
+    const uint32_t slot = c.stage & (kNQ - 1u);
+    const uint32_t off = ring_place(c.head, step_stage_bytes(RS, nb, m.block_bytes), (uint32_t)p.ring_bytes);
+    const bool ok = mbar_wait_warp(&c.full[slot], (c.stage / kNQ) & 1u);
     float* red = c.red + (c.stage & 1u) * kRedFloats;
     if (ok) {
-      const unsigned char* base = c.ring + (size_t)slot * p.slot_bytes;
+      const unsigned char* base = c.ring + off;
       if (m.block_bytes == 18) {
-        stage_rows<18>(base, m.row_bytes, R, nb, S, wpr, c.U, red, c.warp, c.lane);
+        stage_rows<18>(base, RS, nb, c.U, red, c.warp, c.lane);
       } else {
-        stage_rows<34>(base, m.row_bytes, R, nb, S, wpr, c.U, red, c.warp, c.lane);
+        stage_rows<34>(base, RS, nb, c.U, red, c.warp, c.lane);
       }
     }
     __syncwarp();
@@ -331,8 +327,15 @@ __device__ bool gemv_phase(Ctx& c, int kind, float* y, const float* resid, float
     if (stop_all(c, !ok)) return false;  // also: the stage's partial sums are complete
     if (c.tid < R) {
       float sum = red[c.tid * kCWarps];
-      for (int k = 1; k < wpr; ++k) sum += red[c.tid * kCWarps + k];
+#pragma unroll
+      for (int k = 1; k < kCWarps; ++k) sum += red[c.tid * kCWarps + k];
       const int row = r0 + lo + c.tid;
+      if (m.pair) {
+        float up = red[(R + c.tid) * kCWarps];
+#pragma unroll
+        for (int k = 1; k < kCWarps; ++k) up += red[(R + c.tid) * kCWarps + k];
+        sum = silu(sum) * up;
+      }
       if (resid) sum = __fadd_rn(ldcg(resid + row), sum);
       y[row] = sum;
       if (best_v && sum > *best_v) {  // rows ascend per thread: the first maximum
@@ -367,75 +370,78 @@ __device__ void attention_item(Ctx& c, int layer, int g, int ch, int nch) {
   float* sc = qs + kMaxGroup * HD;                   // [kMaxGroup][kChunk]
   float* ml = sc + kMaxGroup * kChunk;               // [kMaxGroup][2]
   int* rowid = reinterpret_cast<int*>(ml + 2 * kMaxGroup);  // [kChunk]
+  uint16_t* vs = reinterpret_cast<uint16_t*>(rowid + kChunk);  // [kChunk][HD] f16: the chunk's V rows
   const float* cosr = p.rope_cos + (size_t)p.rope_pos * half;
   const float* sinr = p.rope_sin + (size_t)p.rope_pos * half;
   const int QH = p.heads * HD;
   const int KV = p.kv_heads * HD;
 
-  for (int e = c.tid; e < Gq * half; e += kCThreads) {
-    const int h = e / half, d = e - h * half;
-    const int qh = g * Gq + h;
-    float a = ldcg(p.qkv + qh * HD + d), bb = ldcg(p.qkv + qh * HD + d + half);
-    if (p.q_bias) {
-      const float* qb = p.q_bias + ((size_t)layer * p.heads + qh) * HD;
-      a = __fadd_rn(a, __ldg(qb + d));
-      bb = __fadd_rn(bb, __ldg(qb + d + half));
-    }
-    const float cs = __ldg(cosr + d), sn = __ldg(sinr + d);
-    qs[h * HD + d] = rope_lo(a, bb, cs, sn);
-    qs[h * HD + d + half] = rope_hi(a, bb, cs, sn);
-  }
   const int t0 = ch * kChunk;
   const int t1 = min(p.n_tokens, t0 + kChunk);
   const int nt = t1 - t0;
+  const bool with_new = t1 == p.n_tokens;  // this chunk holds the new token
+  const size_t new_row = cache_row(p, layer, g, p.n_tokens - 1);
+  const size_t kvb = ((size_t)layer * p.kv_heads + g) * HD;
   for (int t = c.tid; t < nt; t += kCThreads) rowid[t] = (int)cache_row(p, layer, g, t0 + t);
-  if (t1 == p.n_tokens) {
-    const size_t row = cache_row(p, layer, g, p.n_tokens - 1);
-    const size_t kvb = ((size_t)layer * p.kv_heads + g) * HD;
-    for (int d = c.tid; d < half; d += kCThreads) {
-      float a = ldcg(p.qkv + QH + g * HD + d), bb = ldcg(p.qkv + QH + g * HD + d + half);
-      if (p.k_bias) {
-        a = __fadd_rn(a, __ldg(p.k_bias + kvb + d));
-        bb = __fadd_rn(bb, __ldg(p.k_bias + kvb + d + half));
+  // one pass over the item's inputs, all loads of an element issued together:
+  // e < Gq * half: query pair (h, d); then, with the new token, its k pairs and v values
+  const int n_in = Gq * half + (with_new ? half + HD : 0);
+  for (int e = c.tid; e < n_in; e += kCThreads) {
+    if (e < Gq * half + half) {
+      const bool isq = e < Gq * half;
+      const int h = isq ? e / half : 0;
+      const int d = isq ? e - h * half : e - Gq * half;
+      const float* src = isq ? p.qkv + (g * Gq + h) * HD : p.qkv + QH + g * HD;
+      const float* bias = isq ? (p.q_bias ? p.q_bias + ((size_t)layer * p.heads + g * Gq + h) * HD : nullptr)
+                              : (p.k_bias ? p.k_bias + kvb : nullptr);
+      float a = ldcg(src + d), bb = ldcg(src + d + half);
+      if (bias) {
+        a = __fadd_rn(a, __ldg(bias + d));
+        bb = __fadd_rn(bb, __ldg(bias + d + half));
       }
       const float cs = __ldg(cosr + d), sn = __ldg(sinr + d);
-      p.k_pool[row * HD + d] = __half_as_ushort(__float2half_rn(rope_lo(a, bb, cs, sn)));
-      p.k_pool[row * HD + d + half] = __half_as_ushort(__float2half_rn(rope_hi(a, bb, cs, sn)));
-    }
-    for (int d = c.tid; d < HD; d += kCThreads) {
+      const float lo = rope_lo(a, bb, cs, sn), hi = rope_hi(a, bb, cs, sn);
+      if (isq) {
+        qs[h * HD + d] = lo;
+        qs[h * HD + d + half] = hi;
+      } else {  // the new k, rotated and rounded to f16 (RNE) into the cache
+        p.k_pool[new_row * HD + d] = __half_as_ushort(__float2half_rn(lo));
+        p.k_pool[new_row * HD + d + half] = __half_as_ushort(__float2half_rn(hi));
+      }
+    } else {
+      const int d = e - Gq * half - half;
       float v = ldcg(p.qkv + QH + KV + g * HD + d);
       if (p.v_bias) v = __fadd_rn(v, __ldg(p.v_bias + kvb + d));
-      p.v_pool[row * HD + d] = __half_as_ushort(__float2half_rn(v));
+      p.v_pool[new_row * HD + d] = __half_as_ushort(__float2half_rn(v));
     }
   }
   cbar();  // queries, row ids and the new cache row are in place
 
-  if (c.tid < nt) {  // scores: one token per thread, every head of the group
-    const uint4* kr = reinterpret_cast<const uint4*>(p.k_pool + (size_t)rowid[c.tid] * HD);
-    float dot[kMaxGroup];
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) dot[h] = 0.f;
-#pragma unroll 2
+  // the chunk's V rows into shared memory by cp.async (16 bytes a copy), in
+  // flight while the scores are formed
+  for (int e = c.tid; e < nt * (HD / 8); e += kCThreads) {
+    const int t = e / (HD / 8), d8 = e - t * (HD / 8);
+    cp_async_cg16(smem_u32(vs + t * HD + d8 * 8), p.v_pool + (size_t)rowid[t] * HD + d8 * 8);
+  }
+  // scores: one (head, token) pair per thread, consecutive threads on consecutive tokens
+  for (int e = c.tid; e < Gq * nt; e += kCThreads) {
+    const int h = e / nt, t = e - h * nt;
+    const uint4* kr = reinterpret_cast<const uint4*>(p.k_pool + (size_t)rowid[t] * HD);
+    const float* qh = qs + h * HD;
+    float dot = 0.f;
+#pragma unroll 4
     for (int d8 = 0; d8 < HD / 8; ++d8) {
       float kv[8];
       unpack8(__ldcg(kr + d8), kv);
-#pragma unroll
-      for (int h = 0; h < kMaxGroup; ++h) {
-        if (h < Gq) {
-          const float4 q0 = *reinterpret_cast<const float4*>(qs + h * HD + d8 * 8);
-          const float4 q1 = *reinterpret_cast<const float4*>(qs + h * HD + d8 * 8 + 4);
-          float s = dot[h];
-          s = fmaf(q0.x, kv[0], s); s = fmaf(q0.y, kv[1], s); s = fmaf(q0.z, kv[2], s); s = fmaf(q0.w, kv[3], s);
-          s = fmaf(q1.x, kv[4], s); s = fmaf(q1.y, kv[5], s); s = fmaf(q1.z, kv[6], s); s = fmaf(q1.w, kv[7], s);
-          dot[h] = s;
-        }
-      }
+      const float4 q0 = *reinterpret_cast<const float4*>(qh + d8 * 8);
+      const float4 q1 = *reinterpret_cast<const float4*>(qh + d8 * 8 + 4);
+      dot = fmaf(q0.x, kv[0], dot); dot = fmaf(q0.y, kv[1], dot); dot = fmaf(q0.z, kv[2], dot);
+      dot = fmaf(q0.w, kv[3], dot); dot = fmaf(q1.x, kv[4], dot); dot = fmaf(q1.y, kv[5], dot);
+      dot = fmaf(q1.z, kv[6], dot); dot = fmaf(q1.w, kv[7], dot);
     }
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) {
-      if (h < Gq) sc[h * kChunk + c.tid] = dot[h] * p.scale_log2;
-    }
+    sc[h * kChunk + t] = dot * p.scale_log2;
   }
+  cp_async_wait_all();
   cbar();
 
   for (int h = c.warp; h < Gq; h += kCWarps) {  // softmax of head h: one warp
@@ -456,16 +462,15 @@ __device__ void attention_item(Ctx& c, int layer, int g, int ch, int nch) {
 #pragma unroll
     for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
 #pragma unroll 4
-    for (int t = 0; t < nt; ++t) {  // P.V: lane -> DPL dims, coalesced rows
+    for (int t = 0; t < nt; ++t) {  // P.V from shared memory: lane -> DPL dims of the row
       const float pw = sc[h * kChunk + t];
-      const uint16_t* vr = p.v_pool + (size_t)rowid[t] * HD + c.lane * DPL;
+      const uint16_t* vr = vs + t * HD + c.lane * DPL;
       if constexpr (DPL == 2) {
-        const unsigned int u = __ldcg(reinterpret_cast<const unsigned int*>(vr));
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u));
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vr));
         acc[0] = fmaf(pw, f.x, acc[0]);
         acc[1] = fmaf(pw, f.y, acc[1]);
       } else {
-        const uint2 u = __ldcg(reinterpret_cast<const uint2*>(vr));
+        const uint2 u = *reinterpret_cast<const uint2*>(vr);
         const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
         const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
         acc[0] = fmaf(pw, f0.x, acc[0]);
@@ -611,15 +616,15 @@ __device__ void consumer(Ctx& c) {
     }
     grid_arrive(c);
     if (!grid_wait(c)) return;  // C
-    prologue_copy(c, p.attn, p.hidden);
+    stage_async(c, p.attn, p.hidden);
     if (!gemv_phase(c, kStepO, p.x, l == 0 ? emb_row : p.x, nullptr, nullptr)) return;
     grid_arrive(c);
     if (!grid_wait(c)) return;  // D
     prologue_rmsnorm(c, p.x, p.ffn_norm + l * H);
-    if (!gemv_phase(c, kStepGU, p.gu, nullptr, nullptr, nullptr)) return;
+    if (!gemv_phase(c, kStepGU, p.h, nullptr, nullptr, nullptr)) return;
     grid_arrive(c);
     if (!grid_wait(c)) return;  // E
-    prologue_swiglu(c);
+    stage_async(c, p.h, p.ffn);
     if (!gemv_phase(c, kStepDown, p.x, p.x, nullptr, nullptr)) return;
     grid_arrive(c);
   }
@@ -632,23 +637,32 @@ __device__ void consumer(Ctx& c) {
   argmax_finish(c, bv, bi);
 }
 
-// One lane: streams this CTA's packed weights through the ring in
-// consumption order, each slot refilled once all consumer warps released it.
+// One lane: streams this CTA's packed weights through the byte ring in
+// consumption order.  A stage is issued once its descriptor's previous stage
+// and every in-flight stage its bytes overlap have been released by all
+// consumer warps (they release in order).
 __device__ void producer(const StepParams& p, unsigned char* ring, uint64_t* full, uint64_t* empty,
-                         volatile int* s_abort) {
+                         uint32_t* offs, uint32_t* ends, volatile int* s_abort) {
   const int b = blockIdx.x;
   const unsigned char* src = p.wpack + p.cta_off[b];
-  const uint32_t NS = (uint32_t)p.n_slots;
-  uint32_t i = 0;
+  const uint32_t cap = (uint32_t)p.ring_bytes;
+  uint32_t i = 0, tail = 0, head = 0;
   bool ok = true;
+  auto clash = [&](uint32_t off, uint32_t bytes) {
+    for (uint32_t j = tail; j < i; ++j) {
+      const uint32_t q = j & (kNQ - 1u);
+      if (offs[q] < off + bytes && off < ends[q]) return true;
+    }
+    return false;
+  };
   auto put = [&](uint32_t bytes) {
-    const uint32_t slot = i % NS;
-    if (i >= NS) {
-      const uint32_t par = ((i / NS) - 1u) & 1u;
-      if (!mbar_try_wait(&empty[slot], par)) {
+    const uint32_t off = ring_place(head, bytes, cap);
+    while (tail < i && (i - tail >= kNQ || clash(off, bytes))) {
+      const uint32_t q = tail & (kNQ - 1u), par = (tail / kNQ) & 1u;
+      if (!mbar_try_wait(&empty[q], par)) {
         const uint64_t t0 = globaltimer_ns();
         uint32_t n = 0;
-        while (!mbar_try_wait(&empty[slot], par)) {
+        while (!mbar_try_wait(&empty[q], par)) {
           if ((++n & 15u) == 0 && (*s_abort != 0 || globaltimer_ns() - t0 > kWaitLimitNs)) {
             ok = false;
             break;
@@ -659,9 +673,13 @@ __device__ void producer(const StepParams& p, unsigned char* ring, uint64_t* ful
           return;
         }
       }
+      ++tail;
     }
-    mbar_arrive_expect_tx(&full[slot], bytes);
-    bulk_load(ring + (size_t)slot * p.slot_bytes, src, bytes, &full[slot]);
+    const uint32_t q = i & (kNQ - 1u);
+    offs[q] = off;
+    ends[q] = off + bytes;
+    mbar_arrive_expect_tx(&full[q], bytes);
+    bulk_load(ring + off, src, bytes, &full[q]);
     src += bytes;
     ++i;
   };
@@ -671,7 +689,8 @@ __device__ void producer(const StepParams& p, unsigned char* ring, uint64_t* ful
     const int n = step_cta_rows(m, b, r0);
     const int ns = step_n_stages(n, m.rps);
     for (int s = 0; s < ns && ok; ++s) {
-      put(step_stage_bytes(step_stage_lo(s + 1, n, ns) - step_stage_lo(s, n, ns), m.row_bytes));
+      const int rows = step_stage_lo(s + 1, n, ns) - step_stage_lo(s, n, ns);
+      put(step_stage_bytes(m.pair ? 2 * rows : rows, m.cols / 32, m.block_bytes));
     }
   };
   for (int l = 0; l < p.layers && ok; ++l) {
@@ -680,8 +699,8 @@ __device__ void producer(const StepParams& p, unsigned char* ring, uint64_t* ful
   if (p.head && ok) stream(kStepHead);
   // No copy may still be landing when the CTA exits (the consumers may have
   // given up before using the last stages): wait for the newest use of every
-  // slot (already complete in a normal run).
-  for (uint32_t j = i > NS ? i - NS : 0; j < i; ++j) mbar_wait(&full[j % NS], (j / NS) & 1u);
+  // descriptor (already complete in a normal run).
+  for (uint32_t j = i > kNQ ? i - kNQ : 0; j < i; ++j) mbar_wait(&full[j & (kNQ - 1u)], (j / kNQ) & 1u);
 }
 
 __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_constant__ StepParams p) {
@@ -692,16 +711,17 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
   unsigned char* ring = smem + kOffUnion + p.union_bytes;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int s = 0; s < p.n_slots; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kCWarps);
+    for (uint32_t q = 0; q < kNQ; ++q) {
+      mbar_init(&full[q], 1);
+      mbar_init(&empty[q], kCWarps);
     }
     fence_mbarrier_init();
     *s_abort = 0;
   }
   __syncthreads();
   if (warp == kCWarps) {
-    if (lane == 0) producer(p, ring, full, empty, s_abort);
+    uint32_t* rr = reinterpret_cast<uint32_t*>(smem + kOffMisc + kMiscRing);
+    if (lane == 0) producer(p, ring, full, empty, rr, rr + kNQ, s_abort);
   } else {
     Ctx c;
     c.p = &p;
@@ -717,6 +737,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     c.warp = warp;
     c.lane = lane;
     c.stage = 0;
+    c.head = 0;
     c.phase = 0;
     consumer(c);
     if (tid == 0) *s_abort = 1;  // done (or gave up): a producer still waiting for a slot stops
@@ -735,33 +756,55 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
   }
 }
 
+// One CTA per stage: every (block, row) of the stage's physical rows into the
+// transposed layout (scale plane, then the 16-byte quant chunks).
 __global__ void step_pack_kernel(const StepPackSeg* segs, int n, unsigned char* dst) {
   for (int s = blockIdx.x; s < n; s += gridDim.x) {
     const StepPackSeg sg = segs[s];
-    const uint16_t* src = reinterpret_cast<const uint16_t*>(sg.src);
-    uint16_t* d = reinterpret_cast<uint16_t*>(dst + sg.dst_off);
-    for (long long i = threadIdx.x; i < sg.bytes / 2; i += blockDim.x) d[i] = src[i];
+    const int R = sg.rows, nb = sg.nb, BB = sg.block_bytes;
+    const int row_bytes = nb * BB;
+    unsigned char* out = dst + sg.dst_off;
+    const uint32_t scale_bytes = step_scale_bytes(R, nb);
+    for (int e = threadIdx.x; e < R * nb; e += blockDim.x) {
+      const int b = e / R, r = e - b * R;
+      const unsigned char* src = r < sg.split ? static_cast<const unsigned char*>(sg.src0) + (size_t)r * row_bytes
+                                              : static_cast<const unsigned char*>(sg.src1) +
+                                                    (size_t)(r - sg.split) * row_bytes;
+      const uint16_t* blk = reinterpret_cast<const uint16_t*>(src + (size_t)b * BB);
+      reinterpret_cast<uint16_t*>(out)[b * R + r] = blk[0];
+      if (BB == 18) {
+        uint16_t* q = reinterpret_cast<uint16_t*>(out + scale_bytes + (size_t)(b * R + r) * 16);
+        for (int i = 0; i < 8; ++i) q[i] = blk[1 + i];
+      } else {
+        uint16_t* q0 = reinterpret_cast<uint16_t*>(out + scale_bytes + (size_t)((2 * b) * R + r) * 16);
+        uint16_t* q1 = reinterpret_cast<uint16_t*>(out + scale_bytes + (size_t)((2 * b + 1) * R + r) * 16);
+        for (int i = 0; i < 8; ++i) {
+          q0[i] = blk[1 + i];
+          q1[i] = blk[9 + i];
+        }
+      }
+    }
   }
 }
 
 }  // namespace
 
-void plan_step_mat(StepMat& m, int rows, int cols, int block_bytes, int grid, int slot_bytes) {
+void plan_step_mat(StepMat& m, int rows, int cols, int block_bytes, int grid, int stage_max, int pair) {
   m.rows = rows;
   m.cols = cols;
   m.block_bytes = block_bytes;
   m.row_bytes = cols / 32 * block_bytes;
+  m.pair = pair;
   m.rpc = (rows + grid - 1) / grid;
-  int rps = slot_bytes / m.row_bytes;
-  if (rps > kStepMaxStageRows) rps = kStepMaxStageRows;
+  const int per = pair ? 2 : 1;  // physical rows per row
+  int rps = stage_max / (per * m.row_bytes);
+  if (rps > kStepMaxStageRows / per) rps = kStepMaxStageRows / per;
   m.rps = rps < 1 ? 1 : rps;
 }
 
 int step_fixed_smem() { return kOffUnion; }
 
-int step_smem_bytes(int slot_bytes, int n_slots, int union_bytes) {
-  return kOffUnion + union_bytes + slot_bytes * n_slots;
-}
+int step_smem_bytes(int ring_bytes, int union_bytes) { return kOffUnion + union_bytes + ring_bytes; }
 
 cudaError_t step_configure() {
   static std::atomic<uint64_t> configured{0};  // one bit per device

@@ -1521,27 +1521,28 @@ TE_API te_status te_qwen_step_create(te_kv_cache* c, const te_qwen_step_desc* d,
   DeviceGuard dg(e->device);
   const int G = e->sm_count;
   const uint32_t kv = kvh * hd;
-  const uint32_t rows[kStepKinds] = {H + 2 * kv, H, 2 * F, H, V};
+  const uint32_t rows[kStepKinds] = {H + 2 * kv, H, F, H, V};  // gate/up: F rows of (gate row, up row)
   const uint32_t cols[kStepKinds] = {H, H, H, F, H};
   int max_row = 0;
   for (int k = 0; k < kStepKinds; ++k) {
     const int bb = quants[k] == TE_ATTN_QUANT_GGUF_Q4_0 ? 18 : 34;
-    max_row = std::max(max_row, (int)(cols[k] / 32 * bb));
+    max_row = std::max(max_row, (int)(cols[k] / 32 * bb) * (k == kStepGU ? 2 : 1));  // a gate/up stage: two rows
   }
-  const int slot = std::max(8192, (max_row + 15) & ~15);
-  const int attn_bytes = 4 * (16 * (int)hd + 16 * 256 + 32 + 256);
+  // stages of up to 32 KiB (or one row, or one gate/up pair) in a byte ring of the rest of shared memory
+  const int stage_max = std::max(32768, (max_row + 15) & ~15);
+  const int attn_bytes = step_attn_bytes((int)hd);
   const int union_bytes = (std::max((int)std::max(H, F) * 4, attn_bytes) + 127) & ~127;
-  const int budget = 227 * 1024 - step_fixed_smem() - union_bytes;
-  const int n_slots = std::min(kStepMaxSlots, budget > 0 ? budget / slot : 0);
-  if (n_slots < 3) return fail(e, TE_STATUS_UNSUPPORTED, "rows or vectors too long for the step kernel's ring");
-  const int smem = step_smem_bytes(slot, n_slots, union_bytes);
+  const int ring_bytes = (227 * 1024 - step_fixed_smem() - union_bytes) & ~15;
+  if (ring_bytes < 2 * stage_max) return fail(e, TE_STATUS_UNSUPPORTED, "rows or vectors too long for the step kernel's ring");
+  const int smem = step_smem_bytes(ring_bytes, union_bytes);
   cudaError_t err = step_configure();
   if (err != cudaSuccess) return cuda_fail(e, err, "step kernel shared-memory limit");
   if (step_max_ctas_per_sm(smem) < 1) return fail(e, TE_STATUS_UNSUPPORTED, "step kernel does not fit an SM");
 
   StepParams p{};
   for (int k = 0; k < kStepKinds; ++k) {
-    plan_step_mat(p.mat[k], (int)rows[k], (int)cols[k], quants[k] == TE_ATTN_QUANT_GGUF_Q4_0 ? 18 : 34, G, slot);
+    plan_step_mat(p.mat[k], (int)rows[k], (int)cols[k], quants[k] == TE_ATTN_QUANT_GGUF_Q4_0 ? 18 : 34, G,
+                  stage_max, k == kStepGU ? 1 : 0);
   }
   // each CTA's stream: its stages of every layer's four projections, then the head's
   std::vector<long long> off((size_t)G + 1);
@@ -1555,11 +1556,16 @@ TE_API te_status te_qwen_step_create(te_kv_cache* c, const te_qwen_step_desc* d,
     for (int s = 0; s < ns; ++s) {
       const int lo = step_stage_lo(s, n, ns), hi = step_stage_lo(s + 1, n, ns);
       StepPackSeg sg;
-      sg.src = static_cast<const unsigned char*>(w) + (size_t)(r0 + lo) * m.row_bytes;
+      sg.src0 = static_cast<const unsigned char*>(w) + (size_t)(r0 + lo) * m.row_bytes;
+      // gate/up: the same rows of the second half (up rows follow the F gate rows)
+      sg.src1 = m.pair ? static_cast<const unsigned char*>(w) + (size_t)(m.rows + r0 + lo) * m.row_bytes : sg.src0;
       sg.dst_off = pos;
-      sg.bytes = (long long)(hi - lo) * m.row_bytes;
+      sg.rows = (m.pair ? 2 : 1) * (hi - lo);
+      sg.split = hi - lo;
+      sg.nb = m.cols / 32;
+      sg.block_bytes = m.block_bytes;
       segs.push_back(sg);
-      pos += step_stage_bytes(hi - lo, m.row_bytes);
+      pos += step_stage_bytes(sg.rows, sg.nb, m.block_bytes);
     }
   };
   for (int b = 0; b < G; ++b) {
@@ -1578,10 +1584,10 @@ TE_API te_status te_qwen_step_create(te_kv_cache* c, const te_qwen_step_desc* d,
   st->grid = G;
   st->smem = smem;
   st->heads = NH;
-  const int max_chunks = (int)((c->d.max_tokens_per_seq + 255) / 256);
+  const int max_chunks = (int)((c->d.max_tokens_per_seq + kStepChunk - 1) / kStepChunk);
   const size_t group = NH / kvh;
   auto up4 = [](size_t n) { return (n + 3) & ~size_t(3); };  // 16-byte aligned sub-buffers
-  const size_t n_qkv = up4(H + 2 * kv), n_attn = up4(H), n_gu = up4(2 * (size_t)F);
+  const size_t n_qkv = up4(H + 2 * kv), n_attn = up4(H), n_gu = up4(F);
   const size_t n_rec = up4((size_t)kvh * max_chunks * group * (hd + 2)), n_cand = up4(2 * (size_t)G);
   StepPackSeg* d_segs = nullptr;
   err = cudaMalloc(&st->wpack, (size_t)std::max(pos, 16ll));
@@ -1628,13 +1634,12 @@ TE_API te_status te_qwen_step_create(te_kv_cache* c, const te_qwen_step_desc* d,
   p.emb = d->embedding;
   p.qkv = st->scratch;
   p.attn = p.qkv + n_qkv;
-  p.gu = p.attn + n_attn;
-  p.rec = p.gu + n_gu;
+  p.h = p.attn + n_attn;
+  p.rec = p.h + n_gu;
   p.cand = p.rec + n_rec;
   p.sync = st->sync;
   p.error = e->d_error;
-  p.slot_bytes = slot;
-  p.n_slots = n_slots;
+  p.ring_bytes = ring_bytes;
   p.union_bytes = union_bytes;
   st->p = p;
   *out = st;

@@ -339,8 +339,16 @@ cudaError_t launch_gemv_gguf(GemvParams p, int block_bytes, int n_vectors, int s
 // the order the kernel consumes them), which a producer warp copies into a
 // shared-memory ring ahead of the consumer warps, across phase boundaries.
 enum StepKind { kStepQKV = 0, kStepO = 1, kStepGU = 2, kStepDown = 3, kStepHead = 4, kStepKinds = 5 };
-constexpr int kStepMaxStageRows = 64;  // rows per stage (per-stage partial-sum area)
-constexpr int kStepMaxSlots = 32;      // ring slots
+constexpr int kStepMaxStageRows = 32;  // rows per stage: one per lane (gate/up: 16 pairs)
+constexpr int kStepMaxSlots = 32;      // stages in flight (mbarrier pairs)
+constexpr int kStepChunk = 128;        // attention tokens per work item
+constexpr int kStepMaxGroup = 16;      // query heads per kv head
+// Attention work area of the step kernel (queries, scores, row maxima and
+// sums, pool row ids, the chunk's V rows in f16).
+constexpr int step_attn_bytes(int head_dim) {
+  return 4 * (kStepMaxGroup * head_dim + kStepMaxGroup * kStepChunk + 2 * kStepMaxGroup + kStepChunk) +
+         2 * kStepChunk * head_dim;
+}
 
 struct StepMat {
   int32_t rows, cols;
@@ -348,6 +356,8 @@ struct StepMat {
   int32_t row_bytes;    // cols / 32 * block_bytes
   int32_t rpc;          // rows per CTA (CTA b: rows [b * rpc, min(rows, (b + 1) * rpc)))
   int32_t rps;          // most rows per stage
+  int32_t pair;         // 1: gate/up -- row r is gate row r and up row r (rows = ffn); a stage of R
+                        // rows holds the R gate rows, then the R up rows
 };
 
 // Rows of matrix m owned by CTA b (first row in r0).
@@ -358,9 +368,23 @@ __host__ __device__ inline int step_cta_rows(const StepMat& m, int b, int& r0) {
 }
 __host__ __device__ inline int step_n_stages(int n, int rps) { return n > 0 ? (n + rps - 1) / rps : 0; }
 // Stage s of n rows split into ns stages covers rows [lo(s), lo(s + 1)).
-__host__ __device__ inline int step_stage_lo(int s, int n, int ns) { return (int)((long long)s * n / ns); }
-__host__ __device__ inline uint32_t step_stage_bytes(int rows, int row_bytes) {
-  return ((uint32_t)rows * (uint32_t)row_bytes + 15u) & ~15u;
+__host__ __device__ inline int step_stage_lo(int s, int n, int ns) {
+  const long long a = (long long)s * n;
+#ifdef __CUDA_ARCH__
+  if (a < (1ll << 31)) return (int)((unsigned)a / (unsigned)ns);  // the 64-bit divide is a long sequence
+#endif
+  return (int)(a / ns);
+}
+// A stage of `rows` physical rows of nb blocks is stored transposed, so that
+// each block's parts are aligned and consecutive rows of one block are
+// consecutive in shared memory: first the f16 scales [nb][rows], padded to 16
+// bytes, then the quants in 16-byte chunks -- Q4_0 [nb][rows] x 16 bytes,
+// Q8_0 [nb][2][rows] x 16 bytes (first and second half of the 32 int8).
+__host__ __device__ inline uint32_t step_scale_bytes(int rows, int nb) {
+  return ((uint32_t)rows * (uint32_t)nb * 2u + 15u) & ~15u;
+}
+__host__ __device__ inline uint32_t step_stage_bytes(int rows, int nb, int block_bytes) {
+  return step_scale_bytes(rows, nb) + (uint32_t)rows * (uint32_t)nb * (uint32_t)(block_bytes - 2);
 }
 
 struct StepParams {
@@ -392,28 +416,32 @@ struct StepParams {
   float* x;                    // [hidden] residual stream (out: the hidden state after the last layer)
   float* qkv;                  // [heads * hd + 2 * kv_heads * hd]
   float* attn;                 // [heads * hd]
-  float* gu;                   // [2 * ffn]
+  float* h;                    // [ffn] SwiGLU(gate, up): the down projection's input
   float* logits;               // [vocab] (head only)
   float* rec;                  // attention partial records [kv_heads][chunks][group][hd + 2]
   float* cand;                 // [grid][2] per-CTA argmax candidates
   uint32_t* sync;              // [0] grid count, [1] exit count, [2] argmax ticket, [4 + g] merge count of kv head g
   int* error;
   int32_t head;                // 1: output RMSNorm + lm_head + argmax after the layers
-  int32_t slot_bytes, n_slots, union_bytes;
+  int32_t ring_bytes;          // weight ring (shared memory after the work area)
+  int32_t union_bytes;         // phase work area
 };
-// Plans matrix m's split over `grid` CTAs with stages of at most slot_bytes.
-void plan_step_mat(StepMat& m, int rows, int cols, int block_bytes, int grid, int slot_bytes);
+// Plans matrix m's split over `grid` CTAs with stages of at most stage_max bytes.
+void plan_step_mat(StepMat& m, int rows, int cols, int block_bytes, int grid, int stage_max, int pair);
 // Shared memory of the step kernel for these sizes.
-int step_smem_bytes(int slot_bytes, int n_slots, int union_bytes);
+int step_smem_bytes(int ring_bytes, int union_bytes);
 int step_fixed_smem();
 cudaError_t step_configure();  // raises the kernel's shared-memory limit on the current device
 int step_max_ctas_per_sm(int smem);
 cudaError_t launch_step(const StepParams& p, int grid, int smem, cudaStream_t s);
-// Packing: n segments, each `bytes` from src[i] (2-byte aligned) to dst + dst_off[i] (16-byte aligned).
+// Packing: one segment per stage.  Physical row r of the stage is source row
+// src0 + r * row_bytes for r < split, else src1 + (r - split) * row_bytes (the
+// gate/up pairs' second half); written transposed at dst + dst_off.
 struct StepPackSeg {
-  const void* src;
+  const void* src0;
+  const void* src1;
   long long dst_off;
-  long long bytes;
+  int32_t rows, split, nb, block_bytes;
 };
 cudaError_t launch_step_pack(const StepPackSeg* segs, int n, unsigned char* dst, cudaStream_t s);
 
