@@ -6,8 +6,14 @@
 // SwiGLU -> down projection + residual; te_qwen_project_next (:1303-1377)
 // then applies the output RMSNorm, the lm_head and the argmax.  The per-op
 // path of this library runs that as five launches per layer; here one
-// persistent grid (one CTA per SM) runs all of it, with a grid-wide
-// arrival count between dependent phases instead of kernel boundaries.
+// persistent grid (one CTA per SM) runs all of it.  Between dependent phases
+// there is no grid-wide barrier: every vector a phase produces for other CTAs
+// (q|k|v, attention output, x, SwiGLU output) is written as 64-bit words
+// {value, tag}, the tag naming the launch, layer and phase, and a reader
+// takes each word as soon as its tag is the one it expects -- the data and
+// its readiness arrive in one load (the low-latency protocol of NCCL's LL
+// transport).  A CTA with no rows in a phase skips it and waits only where
+// it has work.
 //
 // Weights do not depend on activations, so they are streamed without regard
 // to phases: CTA b owns a fixed row slice of every projection, its share of
@@ -19,7 +25,7 @@
 // producer keeps fetching the next phases' (and layers') rows, so a phase
 // starts with its weights already on chip.
 //
-// Phases per layer (every CTA; a CTA with no rows or items only arrives):
+// Phases per layer (a CTA with no rows or items in a phase skips it):
 //   A  q|k|v = W_qkv RMSNorm(x)       rows of the stacked q, k, v matrices
 //   B  attention                       work items (kv head, 128-token chunk):
 //                                      bias + RoPE of the group's queries, the
@@ -63,7 +69,7 @@ constexpr int kMaxGroup = kStepMaxGroup;      // query heads per kv head
 constexpr int kOffFull = 0;
 constexpr int kOffEmpty = kOffFull + 8 * kStepMaxSlots;
 constexpr int kOffMisc = kOffEmpty + 8 * kStepMaxSlots;
-constexpr int kMiscBytes = 512;
+constexpr int kMiscBytes = 768;
 constexpr int kOffRed = kOffMisc + kMiscBytes;
 constexpr int kRedFloats = kStepMaxStageRows * kCWarps;
 constexpr int kOffUnion = kOffRed + 2 * kRedFloats * 4;
@@ -73,9 +79,11 @@ constexpr int kMiscLast = 4;     // int: this CTA merges (attention) / reduces (
 constexpr int kMiscDred = 64;    // double[kCWarps]: RMSNorm partial sums per warp
 constexpr int kMiscBest = 160;   // {float, int}[kCWarps]: argmax per warp
 constexpr int kMiscRing = 256;   // u32[2][kStepMaxSlots]: the producer's in-flight stage ranges
+constexpr int kMiscXown = 512;   // float[kStepMaxOwnRows]: this CTA's rows of the residual stream x
 constexpr uint32_t kNQ = kStepMaxSlots;  // stage descriptors (full/empty mbarrier pairs), a power of two
 static_assert((kNQ & (kNQ - 1)) == 0 && kMiscRing + 8 * kStepMaxSlots <= kMiscBytes, "ring descriptors");
 static_assert(kMiscDred + 8 * kCWarps <= kMiscBest && kMiscBest + 8 * kCWarps <= kMiscRing, "misc layout");
+static_assert(kMiscXown + 4 * kStepMaxOwnRows <= kMiscBytes, "misc layout");
 
 // The weight ring is a byte ring: stage i takes [off, off + bytes) at the
 // running head, or at 0 when it would pass the end.  Producer and consumers
@@ -115,9 +123,6 @@ __device__ __forceinline__ int ld_relaxed_gpu_s32(const int* p) {
   asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void red_add_relaxed_gpu(uint32_t* p, uint32_t v) {
-  asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 // Activations written by other CTAs in this launch are read through L2
 // (ld.global.cg), never through the non-coherent or L1 paths.
@@ -136,7 +141,7 @@ struct Ctx {
   int b, G, tid, warp, lane;
   uint32_t stage;      // stages consumed
   uint32_t head;       // ring head after the stages consumed
-  uint32_t phase;      // phases this CTA has arrived at
+  uint32_t epoch;      // this launch's tag field (advanced by the last CTA of each launch)
 };
 
 __device__ __forceinline__ bool stop_all(Ctx& c, bool fail) {
@@ -145,57 +150,112 @@ __device__ __forceinline__ bool stop_all(Ctx& c, bool fail) {
   return any;
 }
 
-// Start of a phase: every CTA has arrived at the previous one (count >=
-// phase * grid).  Thread 0 polls; the barrier hands the outcome to all.
-__device__ bool grid_wait(Ctx& c) {
-  bool fail = false;
-  if (c.tid == 0 && c.phase > 0) {
-    const uint32_t target = c.phase * (uint32_t)c.G;
-    uint32_t* cnt = &c.p->sync[0];
-    if (ld_relaxed_gpu(cnt) < target) {
-      const uint64_t t0 = globaltimer_ns();
-      uint32_t n = 0;
-      while (ld_relaxed_gpu(cnt) < target) {
-        if ((++n & 63u) == 0 && (ld_relaxed_gpu_s32(c.p->error) != 0 || globaltimer_ns() - t0 > kWaitLimitNs)) {
-          fail = true;
-          break;
-        }
+// ---- tagged words -----------------------------------------------------------
+// Tag of the vector phase `ph` (0 q|k|v, 1 attention, 2 x after the output
+// projection, 3 SwiGLU, 4 x after the down projection) of layer l.
+__device__ __forceinline__ uint32_t tag_of(const Ctx& c, int l, int ph) {
+  return ((c.epoch + 1u) << 10) | ((uint32_t)l << 3) | (uint32_t)ph;
+}
+// One 64-bit store: a reader that sees the tag sees the value (single-copy
+// atomic 8-byte accesses).
+__device__ __forceinline__ void st_ll(unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_ll(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+// Bounded polling with a short backoff: words that are not there yet are
+// re-read after 32, 64, ... 256 ns, so that the CTAs waiting for a vector do
+// not crowd the L2 lines its writers are storing to.  Gives up after 2 s or
+// when another CTA reported an error.
+struct Poll {
+  uint64_t t0 = 0;
+  uint32_t tries = 0;
+  __device__ __forceinline__ bool again(const StepParams& p) {
+    if (tries == 0) t0 = globaltimer_ns();
+    __nanosleep(32u << (tries < 3 ? tries : 3));
+    ++tries;
+    if ((tries & 15u) == 0 && (ld_relaxed_gpu_s32(p.error) != 0 || globaltimer_ns() - t0 > kWaitLimitNs)) {
+      set_error(p.error, 60);
+      return false;
+    }
+    return true;
+  }
+};
+// Two words loaded together, then completed.
+__device__ __forceinline__ bool ll_get2(const StepParams& p, const unsigned long long* a, const unsigned long long* b,
+                                        uint32_t tag, float& va, float& vb) {
+  unsigned long long wa = ld_ll(a), wb = ld_ll(b);
+  Poll poll;
+  while ((uint32_t)(wa >> 32) != tag || (uint32_t)(wb >> 32) != tag) {
+    if (!poll.again(p)) return false;
+    if ((uint32_t)(wa >> 32) != tag) wa = ld_ll(a);
+    if ((uint32_t)(wb >> 32) != tag) wb = ld_ll(b);
+  }
+  va = __uint_as_float((uint32_t)wa);
+  vb = __uint_as_float((uint32_t)wb);
+  return true;
+}
+// n tagged words into U, up to kLL loads in flight per thread (the stale
+// ones re-read together); ends with a consumer barrier (false: some word
+// never arrived, the CTA stops).
+__device__ bool ll_stage(Ctx& c, const unsigned long long* src, int n, uint32_t tag) {
+  constexpr int kLL = 8;
+  bool ok = true;
+  for (int base = c.tid; base < n && ok; base += kCThreads * kLL) {
+    unsigned long long w[kLL];
+    uint32_t stale = 0;
+#pragma unroll
+    for (int k = 0; k < kLL; ++k) {
+      const int i = base + k * kCThreads;
+      if (i < n) w[k] = ld_ll(src + i);
+    }
+#pragma unroll
+    for (int k = 0; k < kLL; ++k) {
+      if (base + k * kCThreads < n && (uint32_t)(w[k] >> 32) != tag) stale |= 1u << k;
+    }
+    Poll poll;
+    while (stale) {
+      if (!poll.again(*c.p)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int k = 0; k < kLL; ++k) {
+        if (stale & (1u << k)) w[k] = ld_ll(src + base + k * kCThreads);
+      }
+#pragma unroll
+      for (int k = 0; k < kLL; ++k) {
+        if ((stale & (1u << k)) && (uint32_t)(w[k] >> 32) == tag) stale &= ~(1u << k);
       }
     }
-    fence_acq_rel_gpu();
-    if (fail) set_error(c.p->error, 60);
+#pragma unroll
+    for (int k = 0; k < kLL; ++k) {
+      const int i = base + k * kCThreads;
+      if (i < n) c.U[i] = __uint_as_float((uint32_t)w[k]);
+    }
   }
-  return !stop_all(c, fail);
-}
-
-// End of a phase: all consumer threads' writes of it are published by one
-// release from thread 0.
-__device__ __forceinline__ void grid_arrive(Ctx& c) {
-  cbar();
-  if (c.tid == 0) {
-    fence_acq_rel_gpu();
-    red_add_relaxed_gpu(&c.p->sync[0], 1u);
-  }
-  ++c.phase;
+  return !stop_all(c, !ok);
 }
 
 // ---- phase prologues: the input vector of a projection into U -------------
 
-// The prologues read vectors that other CTAs wrote in this launch: copied
-// into U by cp.async through L2 (.cg), every thread's 16-byte copies in
-// flight together, so a prologue costs about one L2 round trip and no
-// registers.
+// The embedding row (written before the launch) into U by cp.async, every
+// thread's 16-byte copies in flight together.
 __device__ __forceinline__ void stage_async(Ctx& c, const float* src, int n) {
   for (int i = c.tid * 4; i < n; i += kCThreads * 4) cp_async_cg16(smem_u32(c.U + i), src + i);
   cp_async_wait_all();
   cbar();
 }
 
-// te_rmsnorm_f32 (c/src/ops.c:272-293): squares summed in double, scale =
-// 1 / sqrtf((float)(sum / n) + eps), out = (x * scale) * w.
-__device__ void prologue_rmsnorm(Ctx& c, const float* src, const float* w) {
+// te_rmsnorm_f32 (c/src/ops.c:272-293) of the vector in U, in place: squares
+// summed in double, scale = 1 / sqrtf((float)(sum / n) + eps), out = (x *
+// scale) * w.
+__device__ void rmsnorm_u(Ctx& c, const float* w) {
   const int H = c.p->hidden;
-  stage_async(c, src, H);
   double ss = 0.0;
   for (int i = c.tid * 4; i < H; i += kCThreads * 4) {
     const float4 v = *reinterpret_cast<const float4*>(c.U + i);
@@ -291,13 +351,24 @@ __device__ void stage_rows(const unsigned char* stage, int R, int nb, const floa
   if (k == 0 && r < R) red[r * kCWarps + warp] = acc;
 }
 
-// One projection phase over this CTA's rows: y[row] = dot, or resid[row] +
-// dot (fp32 add: the residual add after the output and down projections);
+// One projection phase over this CTA's rows: dot, or own[row] + dot (fp32
+// add: the residual add after the output and down projections);
 // with `best` also the running first-maximum (value, row) of the outputs.
 // For the gate/up matrix (m.pair) a stage holds R gate rows then the same R
 // up rows, and y[row] = SwiGLU(gate, up) = gate / (1 + expf(-gate)) * up
 // (te_swiglu_f32, c/src/ops.c:397-406): the down projection's input.
-__device__ bool gemv_phase(Ctx& c, int kind, float* y, const float* resid, float* best_v, int* best_i) {
+// Where a projection's rows go: tagged words for other CTAs (ll, tag), plain
+// floats (plain), and/or this CTA's residual rows (own: x[row] = own + dot,
+// kept in shared memory by the CTA that owns the row in both residual
+// projections).
+struct Out {
+  unsigned long long* ll;
+  uint32_t tag;
+  float* plain;
+  float* own;
+};
+
+__device__ bool gemv_phase(Ctx& c, int kind, const Out& o, float* best_v, int* best_i) {
   const StepParams& p = *c.p;
   const StepMat& m = p.mat[kind];
   int r0;
@@ -336,8 +407,12 @@ __device__ bool gemv_phase(Ctx& c, int kind, float* y, const float* resid, float
         for (int k = 1; k < kCWarps; ++k) up += red[(R + c.tid) * kCWarps + k];
         sum = silu(sum) * up;
       }
-      if (resid) sum = __fadd_rn(ldcg(resid + row), sum);
-      y[row] = sum;
+      if (o.own) {
+        sum = __fadd_rn(o.own[lo + c.tid], sum);
+        o.own[lo + c.tid] = sum;
+      }
+      if (o.ll) st_ll(o.ll + row, sum, o.tag);
+      if (o.plain) o.plain[row] = sum;
       if (best_v && sum > *best_v) {  // rows ascend per thread: the first maximum
         *best_v = sum;
         *best_i = row;
@@ -361,7 +436,7 @@ __device__ __forceinline__ size_t cache_row(const StepParams& p, int layer, int 
 // softmax); the new token's k (bias, RoPE) and v (bias) go into the cache
 // rounded to f16 (RNE) first, as the per-op decode's appender does.
 template <int HD>
-__device__ void attention_item(Ctx& c, int layer, int g, int ch, int nch) {
+__device__ bool attention_item(Ctx& c, int layer, int g, int ch, int nch) {
   const StepParams& p = *c.p;
   constexpr int half = HD / 2;
   constexpr int DPL = HD / 32;  // dims per lane in P.V
@@ -385,16 +460,19 @@ __device__ void attention_item(Ctx& c, int layer, int g, int ch, int nch) {
   for (int t = c.tid; t < nt; t += kCThreads) rowid[t] = (int)cache_row(p, layer, g, t0 + t);
   // one pass over the item's inputs, all loads of an element issued together:
   // e < Gq * half: query pair (h, d); then, with the new token, its k pairs and v values
+  const uint32_t tq = tag_of(c, layer, 0);
   const int n_in = Gq * half + (with_new ? half + HD : 0);
+  bool ok = true;
   for (int e = c.tid; e < n_in; e += kCThreads) {
     if (e < Gq * half + half) {
       const bool isq = e < Gq * half;
       const int h = isq ? e / half : 0;
       const int d = isq ? e - h * half : e - Gq * half;
-      const float* src = isq ? p.qkv + (g * Gq + h) * HD : p.qkv + QH + g * HD;
+      const unsigned long long* src = isq ? p.ll_qkv + (g * Gq + h) * HD : p.ll_qkv + QH + g * HD;
       const float* bias = isq ? (p.q_bias ? p.q_bias + ((size_t)layer * p.heads + g * Gq + h) * HD : nullptr)
                               : (p.k_bias ? p.k_bias + kvb : nullptr);
-      float a = ldcg(src + d), bb = ldcg(src + d + half);
+      float a, bb;
+      ok = ll_get2(p, src + d, src + d + half, tq, a, bb) && ok;
       if (bias) {
         a = __fadd_rn(a, __ldg(bias + d));
         bb = __fadd_rn(bb, __ldg(bias + d + half));
@@ -410,12 +488,13 @@ __device__ void attention_item(Ctx& c, int layer, int g, int ch, int nch) {
       }
     } else {
       const int d = e - Gq * half - half;
-      float v = ldcg(p.qkv + QH + KV + g * HD + d);
+      float v, unused;
+      ok = ll_get2(p, p.ll_qkv + QH + KV + g * HD + d, p.ll_qkv + QH + KV + g * HD + d, tq, v, unused) && ok;
       if (p.v_bias) v = __fadd_rn(v, __ldg(p.v_bias + kvb + d));
       p.v_pool[new_row * HD + d] = __half_as_ushort(__float2half_rn(v));
     }
   }
-  cbar();  // queries, row ids and the new cache row are in place
+  if (stop_all(c, !ok)) return false;  // queries, row ids and the new cache row are in place
 
   // the chunk's V rows into shared memory by cp.async (16 bytes a copy), in
   // flight while the scores are formed
@@ -481,9 +560,9 @@ __device__ void attention_item(Ctx& c, int layer, int g, int ch, int nch) {
     }
     if (nch == 1) {
       const float inv = 1.0f / l;
-      float* o = p.attn + (size_t)(g * Gq + h) * HD + c.lane * DPL;
+      unsigned long long* o = p.ll_attn + (size_t)(g * Gq + h) * HD + c.lane * DPL;
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) o[i] = acc[i] * inv;
+      for (int i = 0; i < DPL; ++i) st_ll(o + i, acc[i] * inv, tag_of(c, layer, 1));
     } else {
       float* r = p.rec + ((size_t)(g * nch + ch) * Gq + h) * (HD + 2);
 #pragma unroll
@@ -496,7 +575,7 @@ __device__ void attention_item(Ctx& c, int layer, int g, int ch, int nch) {
   }
   if (nch == 1) {
     cbar();  // the work area is reused by the next item
-    return;
+    return true;
   }
   // several chunks: the last CTA to finish one of this kv head's chunks merges them
   int* s_last = reinterpret_cast<int*>(c.smem + kOffMisc + kMiscLast);
@@ -523,21 +602,25 @@ __device__ void attention_item(Ctx& c, int layer, int g, int ch, int nch) {
         for (int i = 0; i < DPL; ++i) acc[i] = fmaf(ldcg(r + c.lane * DPL + i), w, acc[i]);
       }
       const float inv = 1.0f / L;
-      float* o = p.attn + (size_t)(g * Gq + h) * HD + c.lane * DPL;
+      unsigned long long* o = p.ll_attn + (size_t)(g * Gq + h) * HD + c.lane * DPL;
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) o[i] = acc[i] * inv;
+      for (int i = 0; i < DPL; ++i) st_ll(o + i, acc[i] * inv, tag_of(c, layer, 1));
     }
     if (c.tid == 0) atomicExch(&p.sync[4 + g], 0u);
   }
   cbar();
+  return true;
 }
 
 template <int HD>
-__device__ void attention_phase(Ctx& c, int layer) {
+__device__ bool attention_phase(Ctx& c, int layer) {
   const StepParams& p = *c.p;
   const int nch = (p.n_tokens + kChunk - 1) / kChunk;
   const int items = p.kv_heads * nch;
-  for (int it = c.b; it < items; it += c.G) attention_item<HD>(c, layer, it / nch, it % nch, nch);
+  for (int it = c.b; it < items; it += c.G) {
+    if (!attention_item<HD>(c, layer, it / nch, it % nch, nch)) return false;
+  }
+  return true;
 }
 
 // ---- argmax ---------------------------------------------------------------
@@ -602,39 +685,53 @@ __device__ void consumer(Ctx& c) {
     token = 0;
   }
   const float* emb_row = p.emb + (size_t)token * p.hidden;
-  const size_t H = (size_t)p.hidden;
+  const int H = p.hidden;
+  int r0;
+  // this CTA's rows of x (the same rows in the output and down projections):
+  // the residual stream's rows it updates, starting from the embedding
+  float* xown = reinterpret_cast<float*>(c.smem + kOffMisc + kMiscXown);
+  const int nx = step_cta_rows(p.mat[kStepO], c.b, r0);
+  for (int i = c.tid; i < nx; i += kCThreads) xown[i] = ldcg(emb_row + r0 + i);
+  cbar();
+  const bool a_rows = step_cta_rows(p.mat[kStepQKV], c.b, r0) > 0;
+  const bool gu_rows = step_cta_rows(p.mat[kStepGU], c.b, r0) > 0;
   for (int l = 0; l < p.layers; ++l) {
-    if (!grid_wait(c)) return;  // A
-    prologue_rmsnorm(c, l == 0 ? emb_row : p.x, p.attn_norm + l * H);
-    if (!gemv_phase(c, kStepQKV, p.qkv, nullptr, nullptr, nullptr)) return;
-    grid_arrive(c);
-    if (!grid_wait(c)) return;  // B
-    if (p.head_dim == 64) {
-      attention_phase<64>(c, l);
-    } else {
-      attention_phase<128>(c, l);
+    if (a_rows) {  // A: q|k|v = W_qkv RMSNorm(x)
+      if (l == 0) {
+        stage_async(c, emb_row, H);
+      } else if (!ll_stage(c, p.ll_x[1], H, tag_of(c, l - 1, 4))) {
+        return;
+      }
+      rmsnorm_u(c, p.attn_norm + (size_t)l * H);
+      if (!gemv_phase(c, kStepQKV, Out{p.ll_qkv, tag_of(c, l, 0), nullptr, nullptr}, nullptr, nullptr)) return;
     }
-    grid_arrive(c);
-    if (!grid_wait(c)) return;  // C
-    stage_async(c, p.attn, p.hidden);
-    if (!gemv_phase(c, kStepO, p.x, l == 0 ? emb_row : p.x, nullptr, nullptr)) return;
-    grid_arrive(c);
-    if (!grid_wait(c)) return;  // D
-    prologue_rmsnorm(c, p.x, p.ffn_norm + l * H);
-    if (!gemv_phase(c, kStepGU, p.h, nullptr, nullptr, nullptr)) return;
-    grid_arrive(c);
-    if (!grid_wait(c)) return;  // E
-    stage_async(c, p.h, p.ffn);
-    if (!gemv_phase(c, kStepDown, p.x, p.x, nullptr, nullptr)) return;
-    grid_arrive(c);
+    if (p.head_dim == 64 ? !attention_phase<64>(c, l) : !attention_phase<128>(c, l)) return;  // B
+    if (nx > 0) {  // C: x += W_o attn
+      if (!ll_stage(c, p.ll_attn, H, tag_of(c, l, 1))) return;
+      if (!gemv_phase(c, kStepO, Out{p.ll_x[0], tag_of(c, l, 2), nullptr, xown}, nullptr, nullptr)) return;
+    }
+    if (gu_rows) {  // D: h = SwiGLU(W_gate RMSNorm(x), W_up RMSNorm(x))
+      if (!ll_stage(c, p.ll_x[0], H, tag_of(c, l, 2))) return;
+      rmsnorm_u(c, p.ffn_norm + (size_t)l * H);
+      if (!gemv_phase(c, kStepGU, Out{p.ll_h, tag_of(c, l, 3), nullptr, nullptr}, nullptr, nullptr)) return;
+    }
+    if (nx > 0) {  // E: x += W_down h (the last layer's x also as plain floats: the hidden state)
+      if (!ll_stage(c, p.ll_h, p.ffn, tag_of(c, l, 3))) return;
+      if (!gemv_phase(c, kStepDown, Out{p.ll_x[1], tag_of(c, l, 4), l == p.layers - 1 ? p.x : nullptr, xown},
+                      nullptr, nullptr)) {
+        return;
+      }
+    }
   }
   if (!p.head) return;
-  if (!grid_wait(c)) return;
-  prologue_rmsnorm(c, p.x, p.out_norm);
   float bv = -INFINITY;
   int bi = INT_MAX;
-  if (!gemv_phase(c, kStepHead, p.logits, nullptr, &bv, &bi)) return;
-  argmax_finish(c, bv, bi);
+  if (step_cta_rows(p.mat[kStepHead], c.b, r0) > 0) {
+    if (!ll_stage(c, p.ll_x[1], H, tag_of(c, p.layers - 1, 4))) return;
+    rmsnorm_u(c, p.out_norm);
+    if (!gemv_phase(c, kStepHead, Out{nullptr, 0u, p.logits, nullptr}, &bv, &bi)) return;
+  }
+  argmax_finish(c, bv, bi);  // every CTA hands in a candidate
 }
 
 // One lane: streams this CTA's packed weights through the byte ring in
@@ -738,17 +835,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     c.lane = lane;
     c.stage = 0;
     c.head = 0;
-    c.phase = 0;
+    c.epoch = ld_relaxed_gpu(&p.sync[3]);
     consumer(c);
     if (tid == 0) *s_abort = 1;  // done (or gave up): a producer still waiting for a slot stops
   }
   __syncthreads();
   if (tid == 0) {
-    // the last CTA out clears the launch's counters for the next step
+    // the last CTA out clears the launch's counters and advances the epoch
     __threadfence();
     const uint32_t old = atomicAdd(&p.sync[1], 1u);
     if (old == gridDim.x - 1) {
-      atomicExch(&p.sync[0], 0u);
+      // every CTA read this launch's epoch before doing anything else
+      atomicAdd(&p.sync[3], 1u);
       atomicExch(&p.sync[2], 0u);
       for (int g = 0; g < p.kv_heads; ++g) atomicExch(&p.sync[4 + g], 0u);
       atomicExch(&p.sync[1], 0u);

@@ -1493,6 +1493,9 @@ TE_API te_status te_qwen_step_create(te_kv_cache* c, const te_qwen_step_desc* d,
                                                "hidden and ffn multiples of 32)");
   }
   if (NH / kvh > 16) return fail(e, TE_STATUS_UNSUPPORTED, "more than 16 query heads per kv head");
+  if (L > (uint32_t)kStepMaxLayers || (H + e->sm_count - 1) / e->sm_count > (uint32_t)kStepMaxOwnRows) {
+    return fail(e, TE_STATUS_UNSUPPORTED, "more layers or hidden rows per SM than the step kernel takes");
+  }
   if (H > (1u << 24) || F > (1u << 24) || V > (uint32_t)INT32_MAX) return TE_STATUS_INVALID_ARGUMENT;
   const uint32_t quants[kStepKinds] = {d->quant_qkv, d->quant_o, d->quant_gu, d->quant_down, d->quant_head};
   for (uint32_t q : quants) {
@@ -1587,12 +1590,14 @@ TE_API te_status te_qwen_step_create(te_kv_cache* c, const te_qwen_step_desc* d,
   const int max_chunks = (int)((c->d.max_tokens_per_seq + kStepChunk - 1) / kStepChunk);
   const size_t group = NH / kvh;
   auto up4 = [](size_t n) { return (n + 3) & ~size_t(3); };  // 16-byte aligned sub-buffers
-  const size_t n_qkv = up4(H + 2 * kv), n_attn = up4(H), n_gu = up4(F);
+  // tagged words (8 bytes each): q|k|v, attention, SwiGLU output, two x vectors
+  const size_t n_ll = up4(H + 2 * kv) + up4(H) + up4(F) + 2 * up4(H);
   const size_t n_rec = up4((size_t)kvh * max_chunks * group * (hd + 2)), n_cand = up4(2 * (size_t)G);
   StepPackSeg* d_segs = nullptr;
   err = cudaMalloc(&st->wpack, (size_t)std::max(pos, 16ll));
   if (err == cudaSuccess) err = cudaMalloc(&st->d_off, off.size() * sizeof(long long));
-  if (err == cudaSuccess) err = cudaMalloc(&st->scratch, (n_qkv + n_attn + n_gu + n_rec + n_cand) * sizeof(float));
+  if (err == cudaSuccess) err = cudaMalloc(&st->scratch, 2 * n_ll * sizeof(float) + (n_rec + n_cand) * sizeof(float));
+  if (err == cudaSuccess) err = cudaMemsetAsync(st->scratch, 0, 2 * n_ll * sizeof(float), e->stream);
   if (err == cudaSuccess) err = cudaMalloc(&st->sync, (4 + kvh) * sizeof(uint32_t));
   if (err == cudaSuccess) err = cudaMalloc(&d_segs, std::max<size_t>(segs.size(), 1) * sizeof(StepPackSeg));
   if (err == cudaSuccess) err = cudaMemsetAsync(st->wpack, 0, (size_t)std::max(pos, 16ll), e->stream);
@@ -1632,10 +1637,13 @@ TE_API te_status te_qwen_step_create(te_kv_cache* c, const te_qwen_step_desc* d,
   p.ffn_norm = d->ffn_norm;
   p.out_norm = d->out_norm;
   p.emb = d->embedding;
-  p.qkv = st->scratch;
-  p.attn = p.qkv + n_qkv;
-  p.h = p.attn + n_attn;
-  p.rec = p.h + n_gu;
+  auto* ll = reinterpret_cast<unsigned long long*>(st->scratch);
+  p.ll_qkv = ll;
+  p.ll_attn = p.ll_qkv + up4(H + 2 * kv);
+  p.ll_h = p.ll_attn + up4(H);
+  p.ll_x[0] = p.ll_h + up4(F);
+  p.ll_x[1] = p.ll_x[0] + up4(H);
+  p.rec = st->scratch + 2 * n_ll;
   p.cand = p.rec + n_rec;
   p.sync = st->sync;
   p.error = e->d_error;

@@ -343,6 +343,8 @@ constexpr int kStepMaxStageRows = 32;  // rows per stage: one per lane (gate/up:
 constexpr int kStepMaxSlots = 32;      // stages in flight (mbarrier pairs)
 constexpr int kStepChunk = 128;        // attention tokens per work item
 constexpr int kStepMaxGroup = 16;      // query heads per kv head
+constexpr int kStepMaxOwnRows = 64;    // rows of x one CTA owns (hidden <= 64 * grid)
+constexpr int kStepMaxLayers = 127;    // layers a tag can name
 // Attention work area of the step kernel (queries, scores, row maxima and
 // sums, pool row ids, the chunk's V rows in f16).
 constexpr int step_attn_bytes(int head_dim) {
@@ -413,14 +415,16 @@ struct StepParams {
   const float* emb;            // [vocab][hidden] fp32
   const int64_t* token_in;     // device: this step's token
   int64_t* token_out;          // device: the greedy next token (head only)
-  float* x;                    // [hidden] residual stream (out: the hidden state after the last layer)
-  float* qkv;                  // [heads * hd + 2 * kv_heads * hd]
-  float* attn;                 // [heads * hd]
-  float* h;                    // [ffn] SwiGLU(gate, up): the down projection's input
+  float* x;                    // [hidden] out: the hidden state after the last layer
+  // Vectors passed between CTAs as 64-bit words {value bits, tag}:
+  unsigned long long* ll_qkv;  // [heads * hd + 2 * kv_heads * hd]
+  unsigned long long* ll_attn; // [heads * hd]
+  unsigned long long* ll_h;    // [ffn] SwiGLU(gate, up): the down projection's input
+  unsigned long long* ll_x[2]; // [hidden] x after the output projection / after the down projection
   float* logits;               // [vocab] (head only)
   float* rec;                  // attention partial records [kv_heads][chunks][group][hd + 2]
   float* cand;                 // [grid][2] per-CTA argmax candidates
-  uint32_t* sync;              // [0] grid count, [1] exit count, [2] argmax ticket, [4 + g] merge count of kv head g
+  uint32_t* sync;              // [1] exit count, [2] argmax ticket, [3] launch epoch, [4 + g] merge count of kv head g
   int* error;
   int32_t head;                // 1: output RMSNorm + lm_head + argmax after the layers
   int32_t ring_bytes;          // weight ring (shared memory after the work area)
