@@ -201,8 +201,12 @@ __device__ __forceinline__ bool ll_get2(const StepParams& p, const unsigned long
 }
 // n tagged words into U, up to kLL loads in flight per thread (the stale
 // ones re-read together); ends with a consumer barrier (false: some word
-// never arrived, the CTA stops).
-__device__ bool ll_stage(Ctx& c, const unsigned long long* src, int n, uint32_t tag) {
+// never arrived, the CTA stops).  With norm_w, U becomes te_rmsnorm_f32 of
+// the vector (c/src/ops.c:272-293: squares summed in double, scale =
+// 1 / sqrtf((float)(sum / n) + eps), out = (x * scale) * w), the squares
+// summed as the words arrive.
+__device__ bool ll_stage(Ctx& c, const unsigned long long* src, int n, uint32_t tag, const float* norm_w = nullptr) {
+  double ss = 0.0;
   constexpr int kLL = 8;
   bool ok = true;
   for (int base = c.tid; base < n && ok; base += kCThreads * kLL) {
@@ -235,10 +239,26 @@ __device__ bool ll_stage(Ctx& c, const unsigned long long* src, int n, uint32_t 
 #pragma unroll
     for (int k = 0; k < kLL; ++k) {
       const int i = base + k * kCThreads;
-      if (i < n) c.U[i] = __uint_as_float((uint32_t)w[k]);
+      if (i < n) {
+        const float v = __uint_as_float((uint32_t)w[k]);
+        c.U[i] = v;
+        ss += (double)v * (double)v;
+      }
     }
   }
-  return !stop_all(c, !ok);
+  if (norm_w == nullptr) return !stop_all(c, !ok);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  double* dred = reinterpret_cast<double*>(c.smem + kOffMisc + kMiscDred);
+  if (c.lane == 0) dred[c.warp] = ss;
+  if (stop_all(c, !ok)) return false;
+  double tot = 0.0;
+#pragma unroll
+  for (int k = 0; k < kCWarps; ++k) tot += dred[k];
+  const float scale = 1.0f / sqrtf((float)(tot / (double)n) + c.p->eps);
+  for (int i = c.tid; i < n; i += kCThreads) c.U[i] = (c.U[i] * scale) * __ldg(norm_w + i);  // this thread's words
+  cbar();
+  return true;
 }
 
 // ---- phase prologues: the input vector of a projection into U -------------
@@ -370,17 +390,19 @@ struct Out {
 
 __device__ bool gemv_phase(Ctx& c, int kind, const Out& o, float* best_v, int* best_i) {
   const StepParams& p = *c.p;
-  const StepMat& m = p.mat[kind];
+  const StepMat m = p.mat[kind];  // read once per phase
   int r0;
   const int n = step_cta_rows(m, c.b, r0);
   const int ns = step_n_stages(n, m.rps);
   const int nb = m.cols / 32;
-  for (int s = 0; s < ns; ++s) {
-    const int lo = step_stage_lo(s, n, ns);
-    const int R = step_stage_lo(s + 1, n, ns) - lo;
+  const int q = ns > 0 ? n / ns : 0, rem = n - q * ns;  // step_stage_lo, incrementally
+  const uint32_t cap = (uint32_t)p.ring_bytes;
+  int lo = 0;
+  for (int s = 0; s < ns; lo += q + (s < rem ? 1 : 0), ++s) {
+    const int R = q + (s < rem ? 1 : 0);
     const int RS = m.pair ? 2 * R : R;  // rows in the stage
     const uint32_t slot = c.stage & (kNQ - 1u);
-    const uint32_t off = ring_place(c.head, step_stage_bytes(RS, nb, m.block_bytes), (uint32_t)p.ring_bytes);
+    const uint32_t off = ring_place(c.head, step_stage_bytes(RS, nb, m.block_bytes), cap);
     const bool ok = mbar_wait_warp(&c.full[slot], (c.stage / kNQ) & 1u);
     float* red = c.red + (c.stage & 1u) * kRedFloats;
     if (ok) {
@@ -446,6 +468,8 @@ __device__ bool attention_item(Ctx& c, int layer, int g, int ch, int nch) {
   float* ml = sc + kMaxGroup * kChunk;               // [kMaxGroup][2]
   int* rowid = reinterpret_cast<int*>(ml + 2 * kMaxGroup);  // [kChunk]
   uint16_t* vs = reinterpret_cast<uint16_t*>(rowid + kChunk);  // [kChunk][HD] f16: the chunk's V rows
+  // [kChunk][HD] f16: the chunk's K rows, 16-byte chunk j of token t at j ^ (t & 7)
+  uint16_t* ks = vs + kChunk * HD;
   const float* cosr = p.rope_cos + (size_t)p.rope_pos * half;
   const float* sinr = p.rope_sin + (size_t)p.rope_pos * half;
   const int QH = p.heads * HD;
@@ -457,7 +481,17 @@ __device__ bool attention_item(Ctx& c, int layer, int g, int ch, int nch) {
   const bool with_new = t1 == p.n_tokens;  // this chunk holds the new token
   const size_t new_row = cache_row(p, layer, g, p.n_tokens - 1);
   const size_t kvb = ((size_t)layer * p.kv_heads + g) * HD;
-  for (int t = c.tid; t < nt; t += kCThreads) rowid[t] = (int)cache_row(p, layer, g, t0 + t);
+  // the chunk's cached K and V rows into shared memory by cp.async (16 bytes a
+  // copy), in flight while this CTA waits for the step's q, k and v
+  const int n_old = with_new ? nt - 1 : nt;
+  for (int e = c.tid; e < n_old * (HD / 8); e += kCThreads) {
+    const int t = e / (HD / 8), d8 = e - t * (HD / 8);
+    const size_t row = cache_row(p, layer, g, t0 + t);
+    cp_async_cg16(smem_u32(vs + t * HD + d8 * 8), p.v_pool + row * HD + d8 * 8);
+    cp_async_cg16(smem_u32(ks + t * HD + ((d8 ^ (t & 7)) * 8)), p.k_pool + row * HD + d8 * 8);
+  }
+  const int t_new = nt - 1;  // the new token's index in the chunk (with_new)
+  auto ks_at = [&](int t, int d) { return ks + t * HD + (((d >> 3) ^ (t & 7)) << 3) + (d & 7); };
   // one pass over the item's inputs, all loads of an element issued together:
   // e < Gq * half: query pair (h, d); then, with the new token, its k pairs and v values
   const uint32_t tq = tag_of(c, layer, 0);
@@ -482,36 +516,36 @@ __device__ bool attention_item(Ctx& c, int layer, int g, int ch, int nch) {
       if (isq) {
         qs[h * HD + d] = lo;
         qs[h * HD + d + half] = hi;
-      } else {  // the new k, rotated and rounded to f16 (RNE) into the cache
-        p.k_pool[new_row * HD + d] = __half_as_ushort(__float2half_rn(lo));
-        p.k_pool[new_row * HD + d + half] = __half_as_ushort(__float2half_rn(hi));
+      } else {  // the new k, rotated and rounded to f16 (RNE), into the cache and the staged rows
+        const uint16_t klo = __half_as_ushort(__float2half_rn(lo)), khi = __half_as_ushort(__float2half_rn(hi));
+        p.k_pool[new_row * HD + d] = klo;
+        p.k_pool[new_row * HD + d + half] = khi;
+        *ks_at(t_new, d) = klo;
+        *ks_at(t_new, d + half) = khi;
       }
     } else {
       const int d = e - Gq * half - half;
       float v, unused;
       ok = ll_get2(p, p.ll_qkv + QH + KV + g * HD + d, p.ll_qkv + QH + KV + g * HD + d, tq, v, unused) && ok;
       if (p.v_bias) v = __fadd_rn(v, __ldg(p.v_bias + kvb + d));
-      p.v_pool[new_row * HD + d] = __half_as_ushort(__float2half_rn(v));
+      const uint16_t vh = __half_as_ushort(__float2half_rn(v));
+      p.v_pool[new_row * HD + d] = vh;
+      vs[t_new * HD + d] = vh;
     }
   }
-  if (stop_all(c, !ok)) return false;  // queries, row ids and the new cache row are in place
+  cp_async_wait_all();
+  if (stop_all(c, !ok)) return false;  // queries and the chunk's K and V rows are in place
 
-  // the chunk's V rows into shared memory by cp.async (16 bytes a copy), in
-  // flight while the scores are formed
-  for (int e = c.tid; e < nt * (HD / 8); e += kCThreads) {
-    const int t = e / (HD / 8), d8 = e - t * (HD / 8);
-    cp_async_cg16(smem_u32(vs + t * HD + d8 * 8), p.v_pool + (size_t)rowid[t] * HD + d8 * 8);
-  }
   // scores: one (head, token) pair per thread, consecutive threads on consecutive tokens
   for (int e = c.tid; e < Gq * nt; e += kCThreads) {
     const int h = e / nt, t = e - h * nt;
-    const uint4* kr = reinterpret_cast<const uint4*>(p.k_pool + (size_t)rowid[t] * HD);
+    const uint16_t* kr = ks + t * HD;
     const float* qh = qs + h * HD;
     float dot = 0.f;
 #pragma unroll 4
     for (int d8 = 0; d8 < HD / 8; ++d8) {
       float kv[8];
-      unpack8(__ldcg(kr + d8), kv);
+      unpack8(*reinterpret_cast<const uint4*>(kr + ((d8 ^ (t & 7)) << 3)), kv);
       const float4 q0 = *reinterpret_cast<const float4*>(qh + d8 * 8);
       const float4 q1 = *reinterpret_cast<const float4*>(qh + d8 * 8 + 4);
       dot = fmaf(q0.x, kv[0], dot); dot = fmaf(q0.y, kv[1], dot); dot = fmaf(q0.z, kv[2], dot);
@@ -520,7 +554,6 @@ __device__ bool attention_item(Ctx& c, int layer, int g, int ch, int nch) {
     }
     sc[h * kChunk + t] = dot * p.scale_log2;
   }
-  cp_async_wait_all();
   cbar();
 
   for (int h = c.warp; h < Gq; h += kCWarps) {  // softmax of head h: one warp
@@ -699,10 +732,10 @@ __device__ void consumer(Ctx& c) {
     if (a_rows) {  // A: q|k|v = W_qkv RMSNorm(x)
       if (l == 0) {
         stage_async(c, emb_row, H);
-      } else if (!ll_stage(c, p.ll_x[1], H, tag_of(c, l - 1, 4))) {
+        rmsnorm_u(c, p.attn_norm);
+      } else if (!ll_stage(c, p.ll_x[1], H, tag_of(c, l - 1, 4), p.attn_norm + (size_t)l * H)) {
         return;
       }
-      rmsnorm_u(c, p.attn_norm + (size_t)l * H);
       if (!gemv_phase(c, kStepQKV, Out{p.ll_qkv, tag_of(c, l, 0), nullptr, nullptr}, nullptr, nullptr)) return;
     }
     if (p.head_dim == 64 ? !attention_phase<64>(c, l) : !attention_phase<128>(c, l)) return;  // B
@@ -711,8 +744,7 @@ __device__ void consumer(Ctx& c) {
       if (!gemv_phase(c, kStepO, Out{p.ll_x[0], tag_of(c, l, 2), nullptr, xown}, nullptr, nullptr)) return;
     }
     if (gu_rows) {  // D: h = SwiGLU(W_gate RMSNorm(x), W_up RMSNorm(x))
-      if (!ll_stage(c, p.ll_x[0], H, tag_of(c, l, 2))) return;
-      rmsnorm_u(c, p.ffn_norm + (size_t)l * H);
+      if (!ll_stage(c, p.ll_x[0], H, tag_of(c, l, 2), p.ffn_norm + (size_t)l * H)) return;
       if (!gemv_phase(c, kStepGU, Out{p.ll_h, tag_of(c, l, 3), nullptr, nullptr}, nullptr, nullptr)) return;
     }
     if (nx > 0) {  // E: x += W_down h (the last layer's x also as plain floats: the hidden state)
@@ -727,8 +759,7 @@ __device__ void consumer(Ctx& c) {
   float bv = -INFINITY;
   int bi = INT_MAX;
   if (step_cta_rows(p.mat[kStepHead], c.b, r0) > 0) {
-    if (!ll_stage(c, p.ll_x[1], H, tag_of(c, p.layers - 1, 4))) return;
-    rmsnorm_u(c, p.out_norm);
+    if (!ll_stage(c, p.ll_x[1], H, tag_of(c, p.layers - 1, 4), p.out_norm)) return;
     if (!gemv_phase(c, kStepHead, Out{nullptr, 0u, p.logits, nullptr}, &bv, &bi)) return;
   }
   argmax_finish(c, bv, bi);  // every CTA hands in a candidate

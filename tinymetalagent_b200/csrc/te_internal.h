@@ -346,10 +346,10 @@ constexpr int kStepMaxGroup = 16;      // query heads per kv head
 constexpr int kStepMaxOwnRows = 64;    // rows of x one CTA owns (hidden <= 64 * grid)
 constexpr int kStepMaxLayers = 127;    // layers a tag can name
 // Attention work area of the step kernel (queries, scores, row maxima and
-// sums, pool row ids, the chunk's V rows in f16).
+// sums, pool row ids, the chunk's V and K rows in f16).
 constexpr int step_attn_bytes(int head_dim) {
   return 4 * (kStepMaxGroup * head_dim + kStepMaxGroup * kStepChunk + 2 * kStepMaxGroup + kStepChunk) +
-         2 * kStepChunk * head_dim;
+         2 * 2 * kStepChunk * head_dim;
 }
 
 struct StepMat {
@@ -369,13 +369,11 @@ __host__ __device__ inline int step_cta_rows(const StepMat& m, int b, int& r0) {
   return r1 > r0 ? r1 - r0 : 0;
 }
 __host__ __device__ inline int step_n_stages(int n, int rps) { return n > 0 ? (n + rps - 1) / rps : 0; }
-// Stage s of n rows split into ns stages covers rows [lo(s), lo(s + 1)).
+// Stage s of n rows split into ns stages covers rows [lo(s), lo(s + 1)):
+// n / ns rows each, the first n % ns stages one more.
 __host__ __device__ inline int step_stage_lo(int s, int n, int ns) {
-  const long long a = (long long)s * n;
-#ifdef __CUDA_ARCH__
-  if (a < (1ll << 31)) return (int)((unsigned)a / (unsigned)ns);  // the 64-bit divide is a long sequence
-#endif
-  return (int)(a / ns);
+  const int q = n / ns, rem = n - q * ns;
+  return s * q + (s < rem ? s : rem);
 }
 // A stage of `rows` physical rows of nb blocks is stored transposed, so that
 // each block's parts are aligned and consecutive rows of one block are
