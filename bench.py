@@ -280,7 +280,8 @@ def run_gpu(args) -> None:
             res = run_gemv(eng, stream, hbm_peak, peak_src, args, world, rank)
         else:
             res = run_qwen(eng, stream, hbm_peak, peak_src, args)
-            res["prompt_prefill"] = run_qwen_prefill(eng, stream, args)
+            if not args.no_qwen_prefill:
+                res["prompt_prefill"] = run_qwen_prefill(eng, stream, args)
         eng.close()
         if rank == 0:
             print(json.dumps(res))
@@ -1153,8 +1154,10 @@ def main() -> None:
     ap.add_argument("--no-gemv", action="store_true", help="skip the GGUF matrix-vector measurement")
     ap.add_argument("--no-qwen", action="store_true", help="skip the qwen2 decode-step measurement")
     ap.add_argument("--qwen-steps", type=int, default=64, help="decode steps timed for the qwen2 decode step")
+    ap.add_argument("--no-qwen-prefill", action="store_true",
+                    help="with --qwen-only: skip the prompt-prefill measurement")
     ap.add_argument("--qwen-only", action="store_true",
-                    help="run only the qwen2 decode-step measurement (121 library launches per token)")
+                    help="run only the qwen2 decode-step measurements (whole-token step kernel and per-op path)")
     ap.add_argument("--gemv-only", action="store_true",
                     help="run only the GGUF matrix-vector measurement (Q4_0: launches 1-23, Q8_0: 24-46)")
     ap.add_argument("--cfg-steps", type=int, default=16, help="decode steps timed for config 4")

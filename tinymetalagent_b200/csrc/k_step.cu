@@ -418,20 +418,22 @@ __device__ bool gemv_phase(Ctx& c, int kind, const Out& o, float* best_v, int* b
     ++c.stage;
     if (!ok) set_error(p.error, 61);
     if (stop_all(c, !ok)) return false;  // also: the stage's partial sums are complete
-    if (c.tid < R) {
-      float sum = red[c.tid * kCWarps];
+    // the epilogue runs on the last warp, which has the fewest blocks (blocks go to the low warps first)
+    const int et = c.tid - (kCThreads - 32);
+    if (et >= 0 && et < R) {
+      float sum = red[et * kCWarps];
 #pragma unroll
-      for (int k = 1; k < kCWarps; ++k) sum += red[c.tid * kCWarps + k];
-      const int row = r0 + lo + c.tid;
+      for (int k = 1; k < kCWarps; ++k) sum += red[et * kCWarps + k];
+      const int row = r0 + lo + et;
       if (m.pair) {
-        float up = red[(R + c.tid) * kCWarps];
+        float up = red[(R + et) * kCWarps];
 #pragma unroll
-        for (int k = 1; k < kCWarps; ++k) up += red[(R + c.tid) * kCWarps + k];
+        for (int k = 1; k < kCWarps; ++k) up += red[(R + et) * kCWarps + k];
         sum = silu(sum) * up;
       }
       if (o.own) {
-        sum = __fadd_rn(o.own[lo + c.tid], sum);
-        o.own[lo + c.tid] = sum;
+        sum = __fadd_rn(o.own[lo + et], sum);
+        o.own[lo + et] = sum;
       }
       if (o.ll) st_ll(o.ll + row, sum, o.tag);
       if (o.plain) o.plain[row] = sum;
