@@ -346,7 +346,60 @@ __device__ __forceinline__ float block_dot(const unsigned char* stage, uint32_t 
   return sc * (d0 + d1);
 }
 
-// Partial dot products of a stage's R (<= 32) rows into red[row][warp]:
+// Blocks b of physical rows r0 and r1 of a stage together (as block_dot,
+// each input quad loaded once for both rows).
+template <int BB>
+__device__ __forceinline__ void block_dot2(const unsigned char* stage, uint32_t scale_bytes, int RS, int r0, int r1,
+                                           int b, const float* x, float& out0, float& out1) {
+  constexpr float kOff = BB == 18 ? 8388616.0f : 8388736.0f;  // 2^23 + the quant offset (8 or 128)
+  const uint64_t off2 = f2_pack(kOff, kOff);
+  const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage);
+  const float sc0 = __half2float(__ushort_as_half(scales[b * RS + r0]));
+  const float sc1 = __half2float(__ushort_as_half(scales[b * RS + r1]));
+  const uint4* quants = reinterpret_cast<const uint4*>(stage + scale_bytes);
+  uint64_t a0 = 0, b0 = 0, a1 = 0, b1 = 0;  // two chains per row, all +0.0f
+  auto quad2 = [&](uint64_t& d0, uint64_t& d1, uint32_t c0, uint32_t c1, const float* xq) {
+    const float4 xv = *reinterpret_cast<const float4*>(xq);
+    const uint64_t x01 = f2_pack(xv.x, xv.y), x23 = f2_pack(xv.z, xv.w);
+    d0 = f2_fma(f2_sub(f2_pack(__uint_as_float(prmt(c0, 0x4B000000u, 0x7440u)),
+                               __uint_as_float(prmt(c0, 0x4B000000u, 0x7441u))), off2), x01, d0);
+    d0 = f2_fma(f2_sub(f2_pack(__uint_as_float(prmt(c0, 0x4B000000u, 0x7442u)),
+                               __uint_as_float(prmt(c0, 0x4B000000u, 0x7443u))), off2), x23, d0);
+    d1 = f2_fma(f2_sub(f2_pack(__uint_as_float(prmt(c1, 0x4B000000u, 0x7440u)),
+                               __uint_as_float(prmt(c1, 0x4B000000u, 0x7441u))), off2), x01, d1);
+    d1 = f2_fma(f2_sub(f2_pack(__uint_as_float(prmt(c1, 0x4B000000u, 0x7442u)),
+                               __uint_as_float(prmt(c1, 0x4B000000u, 0x7443u))), off2), x23, d1);
+  };
+  if (BB == 18) {
+    const uint4 q0 = quants[b * RS + r0], q1 = quants[b * RS + r1];
+    const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w}, w1[4] = {q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      quad2(a0, a1, w0[k] & 0x0f0f0f0fu, w1[k] & 0x0f0f0f0fu, x + 4 * k);
+      quad2(b0, b1, (w0[k] >> 4) & 0x0f0f0f0fu, (w1[k] >> 4) & 0x0f0f0f0fu, x + 16 + 4 * k);
+    }
+  } else {
+    const uint4 q00 = quants[(2 * b) * RS + r0], q01 = quants[(2 * b + 1) * RS + r0];
+    const uint4 q10 = quants[(2 * b) * RS + r1], q11 = quants[(2 * b + 1) * RS + r1];
+    const uint32_t w0[8] = {q00.x, q00.y, q00.z, q00.w, q01.x, q01.y, q01.z, q01.w};
+    const uint32_t w1[8] = {q10.x, q10.y, q10.z, q10.w, q11.x, q11.y, q11.z, q11.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k & 1) {
+        quad2(b0, b1, w0[k] ^ 0x80808080u, w1[k] ^ 0x80808080u, x + 4 * k);
+      } else {
+        quad2(a0, a1, w0[k] ^ 0x80808080u, w1[k] ^ 0x80808080u, x + 4 * k);
+      }
+    }
+  }
+  float d0, d1, e0, e1;
+  f2_unpack(f2_add(a0, b0), d0, d1);
+  f2_unpack(f2_add(a1, b1), e0, e1);
+  out0 = sc0 * (d0 + d1);
+  out1 = sc1 * (e0 + e1);
+}
+
+// Partial dot products of a stage's R (<= 64) rows into red[row][warp]:
 // rows go across lanes (RT = R rounded up to a power of two lanes per group
 // of K = 32 / RT lanes), and a row's blocks are dealt to its kCWarps * K
 // (warp, lane group) units, so each lane sums whole blocks of one row,
@@ -356,12 +409,30 @@ __device__ __forceinline__ float block_dot(const unsigned char* stage, uint32_t 
 template <int BB>
 __device__ void stage_rows(const unsigned char* stage, int R, int nb, const float* xin, float* red, int warp,
                            int lane) {
+  const uint32_t scale_bytes = step_scale_bytes(R, nb);
+  if (R > 32) {  // two rows per lane, r and r + half, sharing each input load
+    const int half = (R + 1) >> 1;
+    const int r1 = lane + half;
+    const bool v1 = r1 < R;
+    float acc0 = 0.f, acc1 = 0.f;
+    if (lane < half) {
+#pragma unroll 1
+      for (int b = warp; b < nb; b += kCWarps) {
+        float o0, o1;
+        block_dot2<BB>(stage, scale_bytes, R, lane, v1 ? r1 : lane, b, xin + b * 32, o0, o1);
+        acc0 += o0;
+        acc1 += o1;
+      }
+      red[lane * kCWarps + warp] = acc0;
+      if (v1) red[r1 * kCWarps + warp] = acc1;
+    }
+    return;
+  }
   int RT = 1;
   while (RT < R) RT <<= 1;
   const int K = 32 / RT;
   const int r = lane & (RT - 1), k = lane / RT;
   const int units = kCWarps * K;
-  const uint32_t scale_bytes = step_scale_bytes(R, nb);
   float acc = 0.f;
   if (r < R) {
 #pragma unroll 2
@@ -419,8 +490,7 @@ __device__ bool gemv_phase(Ctx& c, int kind, const Out& o, float* best_v, int* b
     if (!ok) set_error(p.error, 61);
     if (stop_all(c, !ok)) return false;  // also: the stage's partial sums are complete
     // the epilogue runs on the last warp, which has the fewest blocks (blocks go to the low warps first)
-    const int et = c.tid - (kCThreads - 32);
-    if (et >= 0 && et < R) {
+    for (int et = c.tid - (kCThreads - 32); et >= 0 && et < R; et += 32) {
       float sum = red[et * kCWarps];
 #pragma unroll
       for (int k = 1; k < kCWarps; ++k) sum += red[et * kCWarps + k];

@@ -1531,11 +1531,13 @@ TE_API te_status te_qwen_step_create(te_kv_cache* c, const te_qwen_step_desc* d,
     const int bb = quants[k] == TE_ATTN_QUANT_GGUF_Q4_0 ? 18 : 34;
     max_row = std::max(max_row, (int)(cols[k] / 32 * bb) * (k == kStepGU ? 2 : 1));  // a gate/up stage: two rows
   }
-  // stages of up to 32 KiB (or one row, or one gate/up pair) in a byte ring of the rest of shared memory
-  const int stage_max = std::max(32768, (max_row + 15) & ~15);
+  // stages of up to 64 KiB (at least 32 KiB, or one row, or one gate/up pair), in a byte ring of the rest
+  // of shared memory that holds at least two of them
   const int attn_bytes = step_attn_bytes((int)hd);
   const int union_bytes = (std::max((int)std::max(H, F) * 4, attn_bytes) + 127) & ~127;
   const int ring_bytes = (227 * 1024 - step_fixed_smem() - union_bytes) & ~15;
+  const int stage_min = std::max(32768, (max_row + 15) & ~15);
+  const int stage_max = std::max(stage_min, std::min(65536, (ring_bytes / 2) & ~15));
   if (ring_bytes < 2 * stage_max) return fail(e, TE_STATUS_UNSUPPORTED, "rows or vectors too long for the step kernel's ring");
   const int smem = step_smem_bytes(ring_bytes, union_bytes);
   cudaError_t err = step_configure();

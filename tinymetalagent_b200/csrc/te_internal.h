@@ -339,7 +339,7 @@ cudaError_t launch_gemv_gguf(GemvParams p, int block_bytes, int n_vectors, int s
 // the order the kernel consumes them), which a producer warp copies into a
 // shared-memory ring ahead of the consumer warps, across phase boundaries.
 enum StepKind { kStepQKV = 0, kStepO = 1, kStepGU = 2, kStepDown = 3, kStepHead = 4, kStepKinds = 5 };
-constexpr int kStepMaxStageRows = 32;  // rows per stage: one per lane (gate/up: 16 pairs)
+constexpr int kStepMaxStageRows = 64;  // rows per stage: one or two per lane (gate/up: 32 pairs)
 constexpr int kStepMaxSlots = 32;      // stages in flight (mbarrier pairs)
 constexpr int kStepChunk = 128;        // attention tokens per work item
 constexpr int kStepMaxGroup = 16;      // query heads per kv head
