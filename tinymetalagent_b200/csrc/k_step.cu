@@ -208,6 +208,11 @@ __device__ __forceinline__ bool ll_get2(const StepParams& p, const unsigned long
 __device__ bool ll_stage(Ctx& c, const unsigned long long* src, int n, uint32_t tag, const float* norm_w = nullptr) {
   double ss = 0.0;
   constexpr int kLL = 8;
+  // the norm weights go to shared memory past the vector (cp.async), in flight while the words are awaited
+  float* wn = c.U + ((n + 3) & ~3);
+  if (norm_w) {
+    for (int i = c.tid * 4; i < n; i += kCThreads * 4) cp_async_cg16(smem_u32(wn + i), norm_w + i);
+  }
   bool ok = true;
   for (int base = c.tid; base < n && ok; base += kCThreads * kLL) {
     unsigned long long w[kLL];
@@ -251,12 +256,13 @@ __device__ bool ll_stage(Ctx& c, const unsigned long long* src, int n, uint32_t 
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   double* dred = reinterpret_cast<double*>(c.smem + kOffMisc + kMiscDred);
   if (c.lane == 0) dred[c.warp] = ss;
+  cp_async_wait_all();
   if (stop_all(c, !ok)) return false;
   double tot = 0.0;
 #pragma unroll
   for (int k = 0; k < kCWarps; ++k) tot += dred[k];
   const float scale = 1.0f / sqrtf((float)(tot / (double)n) + c.p->eps);
-  for (int i = c.tid; i < n; i += kCThreads) c.U[i] = (c.U[i] * scale) * __ldg(norm_w + i);  // this thread's words
+  for (int i = c.tid; i < n; i += kCThreads) c.U[i] = (c.U[i] * scale) * wn[i];  // this thread's words
   cbar();
   return true;
 }

@@ -1534,7 +1534,8 @@ TE_API te_status te_qwen_step_create(te_kv_cache* c, const te_qwen_step_desc* d,
   // stages of up to 64 KiB (at least 32 KiB, or one row, or one gate/up pair), in a byte ring of the rest
   // of shared memory that holds at least two of them
   const int attn_bytes = step_attn_bytes((int)hd);
-  const int union_bytes = (std::max((int)std::max(H, F) * 4, attn_bytes) + 127) & ~127;
+  // work area: the ffn-sized input vector, the attention buffers, or x with its RMSNorm weights
+  const int union_bytes = (std::max(std::max((int)std::max(H, F) * 4, attn_bytes), (int)H * 8) + 127) & ~127;
   const int ring_bytes = (227 * 1024 - step_fixed_smem() - union_bytes) & ~15;
   const int stage_min = std::max(32768, (max_row + 15) & ~15);
   const int stage_max = std::max(stage_min, std::min(65536, (ring_bytes / 2) & ~15));
