@@ -82,10 +82,33 @@ def test_engine_api_null_guards(lib):
     assert lib.te_matvec_gguf(None, 4, None, 1, 32, None, 1, None, 0) == R.TE_STATUS_INVALID_ARGUMENT
     assert lib.te_matvec_gguf_fused(None, 4, None, 1, 32, None, 1, None, 1e-6, None, R.TE_ATTN_RMSNORM_INPUT) == \
         R.TE_STATUS_INVALID_ARGUMENT
+    assert lib.te_qwen_step_create(None, None, None) == R.TE_STATUS_INVALID_ARGUMENT
+    assert lib.te_qwen_step_run(None, 0, None, None, None, None, 0) == R.TE_STATUS_INVALID_ARGUMENT
+    lib.te_qwen_step_free(None)
     lib.te_attn_exchange_free(None)
     lib.te_attn_engine_free(None)
     lib.te_kv_cache_free(None)
     assert lib.te_attn_engine_launch_count(None) == 0
+
+
+def test_qwen_step_desc_layout():
+    # te_qwen_step_desc (include/tinyengine_attn.h): six uint32, a float, five
+    # uint32 quant kinds, then nine pointers
+    d = R.QwenStepDesc
+    assert ctypes.sizeof(d) == 120
+    assert d.eps.offset == 24 and d.quant_qkv.offset == 28 and d.quant_head.offset == 44
+    assert d.w_qkv.offset == 48 and d.embedding.offset == 112
+
+
+def test_qwen_step_checks_layer_lists_before_the_library():
+    # one matrix per layer for each projection, checked by the binding before any C call
+    class Fake:
+        engine = None
+        lib = None
+    with pytest.raises(ValueError):
+        R.QwenStep(Fake(), layers=2, hidden=64, heads=1, ffn=64, vocab=8, eps=1e-6,
+                   quants={"qkv": 4, "o": 4, "gu": 4, "down": 4, "head": 8}, w_qkv=[0], w_o=[0, 0],
+                   w_gu=[0, 0], w_down=[0, 0], w_head=0, attn_norm=0, ffn_norm=0, out_norm=0, embedding=0)
 
 
 def _has_gpu():
