@@ -18,12 +18,12 @@
 // Weights do not depend on activations, so they are streamed without regard
 // to phases: CTA b owns a fixed row slice of every projection, its share of
 // all weights is packed host-side into one contiguous byte stream in the
-// order it consumes them (stages of whole rows, 16-byte aligned), and a
-// producer warp copies that stream through a ring of shared-memory slots
-// (cp.async.bulk, completion on the slot's mbarrier) as fast as the slots
-// free up.  While the eight consumer warps wait at a phase boundary, the
-// producer keeps fetching the next phases' (and layers') rows, so a phase
-// starts with its weights already on chip.
+// order it consumes them (stages of up to 64 whole rows, stored transposed
+// and 16-byte aligned), and a producer warp copies that stream through a byte
+// ring in shared memory (cp.async.bulk, completion on the stage's mbarrier)
+// as fast as the consumers release space.  While the twelve consumer warps
+// wait for a phase's input, the producer keeps fetching the next phases' (and
+// layers') rows, so a phase starts with its weights already on chip.
 //
 // Phases per layer (a CTA with no rows or items in a phase skips it):
 //   A  q|k|v = W_qkv RMSNorm(x)       rows of the stacked q, k, v matrices
