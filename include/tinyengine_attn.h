@@ -376,7 +376,8 @@ TE_API te_status te_attention_prefill(te_kv_cache *cache, size_t layer_begin, si
  * dequantised embedding table [vocab][hidden] are fp32, 16-byte aligned.
  * kv_heads and head_dim are the cache's (head_dim 64 or 128, heads * head_dim
  * == hidden, heads / kv_heads <= 16, hidden and ffn multiples of 32); the
- * cache's layers must equal `layers`; the q/k/v biases are the cache's
+ * cache's layers must equal `layers` (at most 127), and hidden may not exceed
+ * 64 rows per SM of the device (TE_STATUS_UNSUPPORTED otherwise); the q/k/v biases are the cache's
  * (te_kv_cache_set_qkv_bias with `heads`, applied with TE_ATTN_QKV_BIAS).
  *
  * te_qwen_step_run appends one token to sequence `seq` at index length (RoPE
